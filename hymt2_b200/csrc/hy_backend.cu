@@ -1,0 +1,1229 @@
+// hy_backend.cu — the hymt2 device backend for B200 (sm_100a).
+//
+// Implements the host's hy_device_ops vtable (reference src/device.h:70-79)
+// and the additive decode API of include/hymt2_cuda.h.  Everything the host
+// hands over is resident in HBM after upload/fused_prepare; a decode step is
+// one CUDA graph of programmatic-dependent launches:
+//   embed -> L x [qkv GEMV | attention | o_proj GEMV (+residual) |
+//                 gate/up GEMV | down GEMV (SiLU*up prologue, +residual)]
+//         -> LM-head GEMV with fused argmax -> token feedback
+// and never synchronises with the host.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "../../include/hymt2_cuda.h"
+#include "hy_attn.cuh"
+#include "hy_gemv.cuh"
+#include "hy_misc.cuh"
+
+using namespace hyk;
+
+// Provided by the host's device layer (reference src/device.c:25) when this
+// backend is linked into the host library; absent in the standalone .so.
+extern "C" hy_device *hy_device_wrap(hy_dev_kind kind, const char *name, void *impl, const hy_device_ops *ops,
+                                     bool software) __attribute__((weak));
+
+namespace {
+
+constexpr int kMaxChunk = 256;     // tokens per device prefill / forward chunk
+constexpr int kSplitLen = 256;     // keys per decode attention split
+constexpr size_t kMaxDynSmem = 200 * 1024;
+
+struct HyCtx;
+
+struct HyWeight {
+    int gtype, fmt, n, k, nb, shift, off;
+    uint8_t *w;
+    float *s;
+    long long stride;
+    float *d_out;   // matmul op output [MAX_BATCH][n] (lazy)
+    float *h_out;   // pinned alias returned by weight_out (lazy)
+    HyCtx *c;
+};
+
+struct Layer {
+    HyWeight *q, *k, *v, *o, *g, *u, *d;
+    float *attn_norm, *ffn_norm, *q_norm, *k_norm;  // device
+};
+
+struct Graph {
+    cudaGraphExec_t exec = nullptr;
+    long long kernels = 0;
+};
+
+struct HyCtx {
+    int dev = 0;
+    cudaStream_t st = nullptr;
+    int nsm = 148;
+    bool broken = false;
+    char err[256] = {0};
+    long long launches = 0;
+    long long capture_kernels = 0;
+    // matmul-op staging
+    q8k_block *d_xq = nullptr;
+    size_t xq_cap = 0;
+    float *d_x32 = nullptr;
+    size_t x32_cap = 0;
+    int32_t *d_ints = nullptr;
+    size_t ints_cap = 0;
+    // fused model state
+    bool fused = false;
+    int L = 0, H = 0, F = 0, heads = 0, kvh = 0, hd = 0, qd = 0, kvd = 0, ctx = 0, half = 0;
+    float eps = 0.f;
+    std::vector<Layer> layers;
+    float *d_norms = nullptr;
+    HyWeight *outw = nullptr, *embd = nullptr;
+    float *d_out_norm = nullptr, *d_cos = nullptr, *d_sin = nullptr;
+    uint16_t *d_kv = nullptr;
+    float *d_h = nullptr, *d_qkv = nullptr, *d_ao = nullptr, *d_g = nullptr, *d_u = nullptr, *d_logits = nullptr;
+    float *d_part = nullptr;
+    int *d_tickets = nullptr;
+    int max_splits = 0;
+    DecodeState *d_state = nullptr;
+    int *d_out_ids = nullptr, *d_tokens = nullptr, *d_chunk_pos = nullptr;
+    float *d_tmp_h() { return d_h + (size_t)(kMaxChunk - 1) * H; }  // scratch row for timing runs
+    int *h_pinned_int = nullptr;  // small pinned staging: [0] forward position, [2..1001] rewind ring
+    unsigned rewind_slot = 0;
+    int vocab_out = 0;
+    Graph g_fwd1, g_fwd1_logits, g_dec;
+    int g_dec_vocab = -1;
+};
+
+bool fail(HyCtx *c, const char *what, cudaError_t e) {
+    c->broken = true;
+    snprintf(c->err, sizeof c->err, "%s: %s", what, e == cudaSuccess ? "invalid request" : cudaGetErrorString(e));
+    return false;
+}
+#define CK(c, call)                                          \
+    do {                                                     \
+        cudaError_t _e = (call);                             \
+        if (_e != cudaSuccess) return fail((c), #call, _e); \
+    } while (0)
+#define REQ(c, cond, msg)                                             \
+    do {                                                              \
+        if (!(cond)) {                                                \
+            snprintf((c)->err, sizeof (c)->err, "%s", (msg));          \
+            return false;                                             \
+        }                                                             \
+    } while (0)
+
+template <typename... KArgs, typename... Args>
+bool launch(HyCtx *c, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, bool pdl, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = c->st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+    if (e != cudaSuccess) return fail(c, "kernel launch", e);
+    c->launches++;
+    c->capture_kernels++;
+    return true;
+}
+
+WDesc desc(const HyWeight *w, float *out, int ld) {
+    WDesc d;
+    d.w = w->w;
+    d.s = w->s;
+    d.out = out;
+    d.stride = w->stride;
+    d.fmt = w->fmt;
+    d.n = w->n;
+    d.k = w->k;
+    d.shift = w->shift;
+    d.off = w->off;
+    d.ld = ld;
+    return d;
+}
+
+bool is_q8_fmt(int fmt) { return fmt == FMT_PANEL || fmt == FMT_Q4K || fmt == FMT_Q6K; }
+
+// ---------------------------------------------------------------- GEMV dispatch
+
+template <typename K>
+void set_smem(K kern) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxDynSmem);
+}
+
+void init_kernel_attrs() {
+    static bool done = false;
+    if (done) return;
+    done = true;
+    set_smem(gemv_panel_nt1<1>);
+    set_smem(gemv_panel_nt1<2>);
+    set_smem(gemv_panel_nt1<3>);
+    set_smem(gemv_panel_nt1<4>);
+    set_smem(gemv_panel_nt<4>);
+    set_smem(gemv_panel_nt<16>);
+    set_smem(gemv_q6k<1>);
+    set_smem(gemv_q6k<4>);
+    set_smem(gemv_q6k<16>);
+    set_smem(gemv_q4k<1>);
+    set_smem(gemv_q4k<4>);
+    set_smem(gemv_q4k<16>);
+    set_smem(gemv_fp<FMT_Q80, 1>);
+    set_smem(gemv_fp<FMT_Q80, 4>);
+    set_smem(gemv_fp<FMT_F16, 1>);
+    set_smem(gemv_fp<FMT_F16, 4>);
+    set_smem(gemv_fp<FMT_F32, 1>);
+    set_smem(gemv_fp<FMT_F32, 4>);
+}
+
+// One launch for nt <= NT tokens.
+bool gemv_launch(HyCtx *c, const GemvArgs &a, bool pdl, int ctas_per_sm) {
+    const int fmt = a.w[0].fmt;
+    int grid = (a.rows_total + kGemvWarps - 1) / kGemvWarps;
+    if (grid > c->nsm * ctas_per_sm) grid = c->nsm * ctas_per_sm;
+    const dim3 blk(kGemvThreads);
+    if (is_q8_fmt(fmt)) {
+        const int NT = a.nt == 1 ? 1 : (a.nt <= 4 ? 4 : 16);
+        const size_t smem = q8_smem_bytes(NT, a.k);
+        if (fmt == FMT_PANEL) {
+            const int cpl = (a.k + 2047) / 2048;
+            if (NT == 1 && cpl <= 4) {
+                switch (cpl) {
+                case 1: return launch(c, gemv_panel_nt1<1>, grid, blk, smem, pdl, a);
+                case 2: return launch(c, gemv_panel_nt1<2>, grid, blk, smem, pdl, a);
+                case 3: return launch(c, gemv_panel_nt1<3>, grid, blk, smem, pdl, a);
+                default: return launch(c, gemv_panel_nt1<4>, grid, blk, smem, pdl, a);
+                }
+            }
+            if (NT <= 4) return launch(c, gemv_panel_nt<4>, grid, blk, q8_smem_bytes(4, a.k), pdl, a);
+            return launch(c, gemv_panel_nt<16>, grid, blk, smem, pdl, a);
+        }
+        if (fmt == FMT_Q6K) {
+            if (NT == 1) return launch(c, gemv_q6k<1>, grid, blk, smem, pdl, a);
+            if (NT == 4) return launch(c, gemv_q6k<4>, grid, blk, smem, pdl, a);
+            return launch(c, gemv_q6k<16>, grid, blk, smem, pdl, a);
+        }
+        if (NT == 1) return launch(c, gemv_q4k<1>, grid, blk, smem, pdl, a);
+        if (NT == 4) return launch(c, gemv_q4k<4>, grid, blk, smem, pdl, a);
+        return launch(c, gemv_q4k<16>, grid, blk, smem, pdl, a);
+    }
+    const int NT = a.nt == 1 ? 1 : 4;
+    const size_t smem = fp_smem_bytes(NT, a.k);
+    if (fmt == FMT_Q80) return NT == 1 ? launch(c, gemv_fp<FMT_Q80, 1>, grid, blk, smem, pdl, a)
+                                       : launch(c, gemv_fp<FMT_Q80, 4>, grid, blk, smem, pdl, a);
+    if (fmt == FMT_F16) return NT == 1 ? launch(c, gemv_fp<FMT_F16, 1>, grid, blk, smem, pdl, a)
+                                       : launch(c, gemv_fp<FMT_F16, 4>, grid, blk, smem, pdl, a);
+    return NT == 1 ? launch(c, gemv_fp<FMT_F32, 1>, grid, blk, smem, pdl, a)
+                   : launch(c, gemv_fp<FMT_F32, 4>, grid, blk, smem, pdl, a);
+}
+
+// Any nt: split into token groups the kernels take (16 for Q8_K formats,
+// 4 for fp32-activation formats).
+bool run_gemv(HyCtx *c, GemvArgs a, bool pdl, int ctas_per_sm = 1) {
+    const int group = is_q8_fmt(a.w[0].fmt) ? 16 : 4;
+    const int nt = a.nt;
+    if (nt <= group) return gemv_launch(c, a, pdl, ctas_per_sm);
+    REQ(c, a.epi != EPI_ARGMAX && a.ints == nullptr, "token groups need a plain epilogue");
+    for (int t0 = 0; t0 < nt; t0 += group) {
+        GemvArgs b = a;
+        b.nt = nt - t0 < group ? nt - t0 : group;
+        if (b.xq) b.xq += (size_t)t0 * (a.k / 256);
+        if (b.x) b.x += (size_t)t0 * a.ldx;
+        if (b.x2) b.x2 += (size_t)t0 * a.ldx;
+        for (int i = 0; i < a.nw; i++) b.w[i].out += (size_t)t0 * a.w[i].ld;
+        if (!gemv_launch(c, b, pdl, ctas_per_sm)) return false;
+    }
+    return true;
+}
+
+GemvArgs gemv_args(int nt, int k) {
+    GemvArgs a;
+    memset(&a, 0, sizeof a);
+    a.nt = nt;
+    a.k = k;
+    return a;
+}
+
+// Launch GEMVs for up to three weights sharing one activation, merging the
+// ones with the same device format into a single launch.
+bool run_multi(HyCtx *c, HyWeight *const *ws, float *const *outs, const int *lds, int cnt, const GemvArgs &tmpl,
+               bool pdl) {
+    bool done[3] = {false, false, false};
+    for (int i = 0; i < cnt; i++) {
+        if (done[i]) continue;
+        GemvArgs a = tmpl;
+        a.nw = 0;
+        a.rows_total = 0;
+        for (int j = i; j < cnt; j++) {
+            if (done[j] || ws[j]->fmt != ws[i]->fmt || ws[j]->k != ws[i]->k) continue;
+            a.w[a.nw++] = desc(ws[j], outs[j], lds[j]);
+            a.rows_total += ws[j]->n;
+            done[j] = true;
+        }
+        if (!run_gemv(c, a, pdl)) return false;
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------- fused layer loop
+
+template <int HD, int G>
+bool attn_launch(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
+    if (nt == 1) return launch(c, attn_decode<HD, G>, dim3(c->kvh, c->max_splits), dim3(G * 32), 0, pdl, aa);
+    int warps = c->heads + c->kvh;
+    if (warps > 32) warps = 32;
+    if (!launch(c, rope_norm_store<HD>, dim3(nt), dim3(warps * 32), 0, pdl, aa)) return false;
+    return launch(c, attn_prefill<HD, G>, dim3(c->kvh, nt), dim3(G * 32), 0, pdl, aa);
+}
+
+bool attention(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
+    const int G = c->heads / c->kvh;
+#define HY_ATT(HD_, G_) \
+    if (c->hd == HD_ && G == G_) return attn_launch<HD_, G_>(c, aa, nt, pdl);
+    HY_ATT(128, 4) HY_ATT(128, 1) HY_ATT(128, 2) HY_ATT(128, 8)
+    HY_ATT(64, 4) HY_ATT(64, 1) HY_ATT(64, 2) HY_ATT(64, 8)
+#undef HY_ATT
+    REQ(c, false, "unsupported head geometry");
+}
+
+bool layer_forward(HyCtx *c, int li, int nt, const int *pos_ptr, bool pdl) {
+    const Layer &L = c->layers[li];
+    const int qkv_ld = c->qd + 2 * c->kvd;
+    {
+        HyWeight *ws[3] = {L.q, L.k, L.v};
+        float *outs[3] = {c->d_qkv, c->d_qkv + c->qd, c->d_qkv + c->qd + c->kvd};
+        const int lds[3] = {qkv_ld, qkv_ld, qkv_ld};
+        GemvArgs a = gemv_args(nt, c->H);
+        a.act = ACT_NORM;
+        a.x = c->d_h;
+        a.ldx = c->H;
+        a.norm_w = L.attn_norm;
+        a.eps = c->eps;
+        a.epi = EPI_STORE;
+        if (!run_multi(c, ws, outs, lds, 3, a, pdl)) return false;
+    }
+    {
+        AttnArgs aa;
+        memset(&aa, 0, sizeof aa);
+        aa.qkv = c->d_qkv;
+        aa.qkv_ld = qkv_ld;
+        aa.kc = c->d_kv + (size_t)li * 2 * c->ctx * c->kvd;
+        aa.vc = aa.kc + (size_t)c->ctx * c->kvd;
+        aa.q_norm = L.q_norm;
+        aa.k_norm = L.k_norm;
+        aa.rope_cos = c->d_cos;
+        aa.rope_sin = c->d_sin;
+        aa.pos_ptr = pos_ptr;
+        aa.nt = nt;
+        aa.heads = c->heads;
+        aa.kv_heads = c->kvh;
+        aa.kvdim = c->kvd;
+        aa.qdim = c->qd;
+        aa.ctx = c->ctx;
+        aa.half = c->half;
+        aa.eps = c->eps;
+        aa.scale = 1.0f / sqrtf((float)c->hd);
+        aa.ao = c->d_ao;
+        aa.part = c->d_part;
+        aa.tickets = c->d_tickets;
+        aa.split_len = kSplitLen;
+        aa.max_splits = c->max_splits;
+        if (!attention(c, aa, nt, pdl)) return false;
+    }
+    {
+        GemvArgs a = gemv_args(nt, c->qd);
+        a.act = ACT_VEC;
+        a.x = c->d_ao;
+        a.ldx = c->qd;
+        a.epi = EPI_ADD;
+        a.nw = 1;
+        a.rows_total = L.o->n;
+        a.w[0] = desc(L.o, c->d_h, c->H);
+        if (!run_gemv(c, a, pdl)) return false;
+    }
+    {
+        HyWeight *ws[2] = {L.g, L.u};
+        float *outs[2] = {c->d_g, c->d_u};
+        const int lds[2] = {c->F, c->F};
+        GemvArgs a = gemv_args(nt, c->H);
+        a.act = ACT_NORM;
+        a.x = c->d_h;
+        a.ldx = c->H;
+        a.norm_w = L.ffn_norm;
+        a.eps = c->eps;
+        a.epi = EPI_STORE;
+        if (!run_multi(c, ws, outs, lds, 2, a, pdl)) return false;
+    }
+    {
+        GemvArgs a = gemv_args(nt, c->F);
+        a.act = ACT_SILU;
+        a.x = c->d_g;
+        a.x2 = c->d_u;
+        a.ldx = c->F;
+        a.epi = EPI_ADD;
+        a.nw = 1;
+        a.rows_total = L.d->n;
+        a.w[0] = desc(L.d, c->d_h, c->H);
+        if (!run_gemv(c, a, pdl)) return false;
+    }
+    return true;
+}
+
+// LM head on one token's residual x (RMSNorm with out_norm first).
+bool head_forward(HyCtx *c, const float *x, bool store_logits, bool argmax, bool pdl) {
+    REQ(c, c->outw != nullptr, "no LM head uploaded");
+    GemvArgs a = gemv_args(1, c->H);
+    a.act = ACT_NORM;
+    a.x = x;
+    a.ldx = c->H;
+    a.norm_w = c->d_out_norm;
+    a.eps = c->eps;
+    a.nw = 1;
+    a.rows_total = c->outw->n;
+    a.w[0] = desc(c->outw, store_logits ? c->d_logits : nullptr, c->outw->n);
+    if (argmax) {
+        a.epi = EPI_ARGMAX;
+        a.amax = &c->d_state->amax;
+        a.amax_rows = c->vocab_out > 0 ? c->vocab_out : c->outw->n;
+    } else {
+        a.epi = EPI_STORE;
+    }
+    return run_gemv(c, a, pdl, 2);
+}
+
+bool layers_forward(HyCtx *c, int nt, const int *pos_ptr, bool pdl) {
+    for (int li = 0; li < c->L; li++)
+        if (!layer_forward(c, li, nt, pos_ptr, pdl)) return false;
+    return true;
+}
+
+// ---------------------------------------------------------------- graphs
+
+void graph_reset(Graph &g) {
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+    g.exec = nullptr;
+    g.kernels = 0;
+}
+
+template <typename F>
+bool capture(HyCtx *c, Graph &g, F body) {
+    graph_reset(g);
+    CK(c, cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
+    c->capture_kernels = 0;
+    const long long before = c->launches;
+    const bool ok = body();
+    cudaGraph_t graph = nullptr;
+    cudaError_t e = cudaStreamEndCapture(c->st, &graph);
+    c->launches = before;
+    if (!ok) {
+        if (graph) cudaGraphDestroy(graph);
+        return false;
+    }
+    if (e != cudaSuccess) return fail(c, "cudaStreamEndCapture", e);
+    e = cudaGraphInstantiate(&g.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (e != cudaSuccess) return fail(c, "cudaGraphInstantiate", e);
+    g.kernels = c->capture_kernels;
+    return true;
+}
+
+bool graph_launch(HyCtx *c, Graph &g) {
+    CK(c, cudaGraphLaunch(g.exec, c->st));
+    c->launches += g.kernels;
+    return true;
+}
+
+bool build_decode_graph(HyCtx *c) {
+    if (c->g_dec.exec && c->g_dec_vocab == c->vocab_out) return true;
+    REQ(c, c->embd != nullptr, "no embedding weight set (hyc_set_embedding)");
+    const bool ok = capture(c, c->g_dec, [&]() {
+        if (!launch(c, embed_rows, dim3(1), dim3(256), 0, true, desc(c->embd, nullptr, 0),
+                    (const int *)&c->d_state->tok, c->d_h))
+            return false;
+        if (!layers_forward(c, 1, &c->d_state->pos, true)) return false;
+        if (!head_forward(c, c->d_h, false, true, true)) return false;
+        return launch(c, decode_finalize, dim3(1), dim3(32), 0, true, c->d_state, c->d_out_ids);
+    });
+    if (ok) c->g_dec_vocab = c->vocab_out;
+    return ok;
+}
+
+// ---------------------------------------------------------------- test hooks
+
+// Runs the GEMV prologue's quantiser (stage_q8k) and writes full host-layout
+// blocks: natural qs, lane-major qp, d, sum, bsums.
+__global__ void __launch_bounds__(kGemvThreads) quantize_export(const __grid_constant__ GemvArgs a, q8k_block *y) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int K = a.k, nb = K / 256;
+    Q8Smem s = q8_smem(smem, 16, K);
+    stage_q8k(a, s, K);
+    for (int t = 0; t < a.nt; t++) {
+        for (int i = threadIdx.x; i < nb * 256; i += blockDim.x) {
+            const int b = i >> 8, e = i & 255, ch = e >> 6, l = (e >> 4) & 3, j = e & 15;
+            const int8_t v = s.qp[(size_t)t * K + (size_t)l * (K / 4) + (b * 4 + piece_of_chunk(ch)) * 16 + j];
+            q8k_block &blk = y[(size_t)t * nb + b];
+            blk.qs[e] = v;
+            // qp[l*64 + p*16 + j] holds natural chunk kPieceOrder[p], plane l
+            blk.qp[l * 64 + piece_of_chunk(ch) * 16 + j] = v;
+        }
+        for (int i = threadIdx.x; i < nb; i += blockDim.x) {
+            q8k_block &blk = y[(size_t)t * nb + i];
+            blk.d = s.d[t * nb + i];
+            blk.sum = s.sum[t * nb + i];
+            for (int j = 0; j < 16; j++) blk.bsums[j] = s.bs[(size_t)t * nb * 16 + i * 16 + j];
+            for (int j = 0; j < (int)sizeof(blk._pad); j++) blk._pad[j] = 0;
+        }
+    }
+}
+
+// ---------------------------------------------------------------- vtable ops
+
+void free_fused(HyCtx *c) {
+    graph_reset(c->g_fwd1);
+    graph_reset(c->g_fwd1_logits);
+    graph_reset(c->g_dec);
+    c->g_dec_vocab = -1;
+    void *ptrs[] = {c->d_norms, c->d_out_norm, c->d_cos, c->d_sin, c->d_kv, c->d_h, c->d_qkv, c->d_ao,
+                    c->d_g, c->d_u, c->d_logits, c->d_part, c->d_tickets, c->d_state, c->d_out_ids,
+                    c->d_tokens, c->d_chunk_pos};
+    for (void *p : ptrs)
+        if (p) cudaFree(p);
+    c->d_norms = c->d_out_norm = c->d_cos = c->d_sin = nullptr;
+    c->d_kv = nullptr;
+    c->d_h = c->d_qkv = c->d_ao = c->d_g = c->d_u = c->d_logits = c->d_part = nullptr;
+    c->d_tickets = nullptr;
+    c->d_state = nullptr;
+    c->d_out_ids = c->d_tokens = c->d_chunk_pos = nullptr;
+    c->layers.clear();
+    c->fused = false;
+}
+
+void destroy_impl(void *impl) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c) return;
+    cudaSetDevice(c->dev);
+    free_fused(c);
+    if (c->d_xq) cudaFree(c->d_xq);
+    if (c->d_x32) cudaFree(c->d_x32);
+    if (c->d_ints) cudaFree(c->d_ints);
+    if (c->h_pinned_int) cudaFreeHost(c->h_pinned_int);
+    if (c->st) cudaStreamDestroy(c->st);
+    delete c;
+}
+
+void release(hy_dweight *hw) {
+    HyWeight *w = (HyWeight *)hw;
+    if (!w) return;
+    if (w->w) cudaFree(w->w);
+    if (w->s) cudaFree(w->s);
+    if (w->d_out) cudaFree(w->d_out);
+    if (w->h_out) cudaFreeHost(w->h_out);
+    delete w;
+}
+
+// Device copy of one host weight (reference contract src/device.h:32,
+// src/model.c:384-406).  STQ1_0 / Q2_0C arrive with the host-built panel
+// (pk/ps); when they do not, the panel is built here on the device.
+hy_dweight *upload(void *impl, const weight_t *w) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !w || w->n <= 0 || w->k <= 0) return nullptr;
+    if (cudaSetDevice(c->dev) != cudaSuccess) return nullptr;
+    HyWeight *d = new HyWeight();
+    memset(d, 0, sizeof *d);
+    d->c = c;
+    d->gtype = w->type;
+    d->n = w->n;
+    d->k = w->k;
+    d->nb = w->k / 256;
+    bool ok = true;
+    auto bail = [&](const char *why) {
+        snprintf(c->err, sizeof c->err, "upload: %s", why);
+        release((hy_dweight *)d);
+        return (hy_dweight *)nullptr;
+    };
+    switch (w->type) {
+    case GT_STQ1_0:
+    case GT_Q2_0C: {
+        if (w->k % (w->type == GT_Q2_0C ? 512 : 256)) return bail("inner dimension not a block multiple");
+        d->fmt = FMT_PANEL;
+        d->shift = w->type == GT_Q2_0C ? 1 : 0;
+        d->off = w->type == GT_Q2_0C ? 3 : 1;
+        if (w->pk) {
+            d->shift = w->pshift;
+            d->off = w->poff;
+        }
+        d->stride = (long long)d->nb * 64;
+        const size_t pk_bytes = (size_t)d->n * d->nb * 64, ps_bytes = (size_t)d->n * d->nb * 4;
+        ok = cudaMalloc(&d->w, pk_bytes) == cudaSuccess && cudaMalloc(&d->s, ps_bytes) == cudaSuccess;
+        if (!ok) return bail("out of device memory");
+        if (w->pk) {
+            ok = cudaMemcpy(d->w, w->pk, pk_bytes, cudaMemcpyHostToDevice) == cudaSuccess &&
+                 cudaMemcpy(d->s, w->ps, ps_bytes, cudaMemcpyHostToDevice) == cudaSuccess;
+        } else {
+            uint8_t *raw = nullptr;
+            const size_t rb = (size_t)d->n * w->row_bytes;
+            ok = cudaMalloc(&raw, rb) == cudaSuccess && cudaMemcpy(raw, w->data, rb, cudaMemcpyHostToDevice) == cudaSuccess;
+            if (ok) {
+                const long long tot = (long long)d->n * d->nb;
+                panel_from_native<<<(unsigned)((tot + 255) / 256), 256, 0, c->st>>>(raw, (long long)w->row_bytes, w->type,
+                                                                                  d->n, d->nb, d->w, d->s);
+                ok = cudaStreamSynchronize(c->st) == cudaSuccess && cudaGetLastError() == cudaSuccess;
+            }
+            if (raw) cudaFree(raw);
+        }
+        break;
+    }
+    case GT_Q4_K:
+        if (w->k % 256) return bail("inner dimension not a block multiple");
+        d->fmt = FMT_Q4K;
+        d->stride = (long long)d->nb * 144;
+        ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess &&
+             cudaMemcpy(d->w, w->data, (size_t)d->n * d->stride, cudaMemcpyHostToDevice) == cudaSuccess;
+        break;
+    case GT_Q6_K: {
+        if (w->k % 256) return bail("inner dimension not a block multiple");
+        d->fmt = FMT_Q6K;
+        d->stride = (long long)align16((size_t)d->nb * 208 + (size_t)d->nb * 2);
+        uint8_t *raw = nullptr;
+        const size_t rb = (size_t)d->n * d->nb * 210;
+        ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess && cudaMalloc(&raw, rb) == cudaSuccess &&
+             cudaMemcpy(raw, w->data, rb, cudaMemcpyHostToDevice) == cudaSuccess;
+        if (ok) {
+            const long long tot = (long long)d->n * d->nb;
+            q6k_relayout<<<(unsigned)((tot + 255) / 256), 256, 0, c->st>>>(raw, d->n, d->nb, d->w, d->stride);
+            ok = cudaStreamSynchronize(c->st) == cudaSuccess && cudaGetLastError() == cudaSuccess;
+        }
+        if (raw) cudaFree(raw);
+        break;
+    }
+    case GT_Q8_0: {
+        if (w->k % 32) return bail("inner dimension not a block multiple");
+        d->fmt = FMT_Q80;
+        const int nblk = w->k / 32;
+        d->stride = (long long)align16((size_t)w->k + (size_t)nblk * 2);
+        uint8_t *raw = nullptr;
+        const size_t rb = (size_t)d->n * nblk * 34;
+        ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess && cudaMalloc(&raw, rb) == cudaSuccess &&
+             cudaMemcpy(raw, w->data, rb, cudaMemcpyHostToDevice) == cudaSuccess;
+        if (ok) {
+            const long long tot = (long long)d->n * nblk;
+            q80_relayout<<<(unsigned)((tot + 255) / 256), 256, 0, c->st>>>(raw, d->n, nblk, d->w, d->stride);
+            ok = cudaStreamSynchronize(c->st) == cudaSuccess && cudaGetLastError() == cudaSuccess;
+        }
+        if (raw) cudaFree(raw);
+        break;
+    }
+    case GT_F16:
+    case GT_F32: {
+        const int es = w->type == GT_F16 ? 2 : 4;
+        if ((w->k * es) % 16) return bail("row length not a multiple of 16 bytes");
+        d->fmt = w->type == GT_F16 ? FMT_F16 : FMT_F32;
+        d->stride = (long long)w->k * es;
+        ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess &&
+             cudaMemcpy(d->w, w->data, (size_t)d->n * d->stride, cudaMemcpyHostToDevice) == cudaSuccess;
+        break;
+    }
+    default:
+        return bail("unsupported weight type");
+    }
+    if (!ok) {
+        c->broken = true;
+        return bail("device copy failed");
+    }
+    return (hy_dweight *)d;
+}
+
+bool ensure_out(HyWeight *w) {
+    if (w->d_out) return true;
+    const size_t bytes = (size_t)MAX_BATCH * w->n * sizeof(float);
+    if (cudaMalloc(&w->d_out, bytes) != cudaSuccess) return false;
+    if (cudaHostAlloc((void **)&w->h_out, bytes, cudaHostAllocDefault) != cudaSuccess) return false;
+    return true;
+}
+
+float *weight_out(hy_dweight *hw) {
+    HyWeight *w = (HyWeight *)hw;
+    if (!w || !ensure_out(w)) return nullptr;
+    return w->h_out;
+}
+
+bool is_software(const void *) { return false; }
+
+bool ensure_buf(HyCtx *c, void **p, size_t *cap, size_t need) {
+    if (need <= *cap) return true;
+    if (*p) cudaFree(*p);
+    *p = nullptr;
+    *cap = 0;
+    CK(c, cudaMalloc(p, need));
+    *cap = need;
+    return true;
+}
+
+// Synchronous batched GEMV over host Q8_K activations (reference contract:
+// src/device.h:35-38, host blocks xq[nt][nb], outputs out[t*n + r]).
+bool matmul(void *impl, hy_dweight *const *ws, float *const *outs, int cnt, const q8k_block *xq, int nt) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || cnt < 1 || nt < 1 || nt > MAX_BATCH || !xq) return false;
+    if (cudaSetDevice(c->dev) != cudaSuccess) return false;
+    const int nb = ((HyWeight *)ws[0])->nb;
+    for (int i = 0; i < cnt; i++) {
+        HyWeight *w = (HyWeight *)ws[i];
+        if (!w || w->nb != nb || !is_q8_fmt(w->fmt)) return false;  // fp32 formats need fp32 activations
+        if (!ensure_out(w)) return fail(c, "matmul output", cudaErrorMemoryAllocation);
+    }
+    const size_t bytes = (size_t)nt * nb * sizeof(q8k_block);
+    if (!ensure_buf(c, (void **)&c->d_xq, &c->xq_cap, bytes)) return false;
+    CK(c, cudaMemcpyAsync(c->d_xq, xq, bytes, cudaMemcpyHostToDevice, c->st));
+    for (int i = 0; i < cnt; i++) {
+        HyWeight *w = (HyWeight *)ws[i];
+        GemvArgs a = gemv_args(nt, w->k);
+        a.act = ACT_Q8K;
+        a.xq = c->d_xq;
+        a.epi = EPI_STORE;
+        a.nw = 1;
+        a.rows_total = w->n;
+        a.w[0] = desc(w, w->d_out, w->n);
+        if (!run_gemv(c, a, false)) return false;
+    }
+    for (int i = 0; i < cnt; i++) {
+        HyWeight *w = (HyWeight *)ws[i];
+        float *dst = outs[i] ? outs[i] : w->h_out;
+        CK(c, cudaMemcpyAsync(dst, w->d_out, (size_t)nt * w->n * sizeof(float), cudaMemcpyDeviceToHost, c->st));
+    }
+    CK(c, cudaStreamSynchronize(c->st));
+    return true;
+}
+
+// Allocate KV cache, scratch and constants for the model shape (reference
+// contract src/device.h:61-64, src/cuda.c:282-337; idempotent per shape).
+bool fused_prepare(void *impl, const hy_fused_args *sh) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !sh || !sh->layers) return false;
+    if (cudaSetDevice(c->dev) != cudaSuccess) return false;
+    REQ(c, sh->heads > 0 && sh->kv_heads > 0 && sh->heads % sh->kv_heads == 0, "bad head counts");
+    const int G = sh->heads / sh->kv_heads;
+    REQ(c, (sh->hdim == 64 || sh->hdim == 128) && (G == 1 || G == 2 || G == 4 || G == 8), "unsupported head geometry");
+    REQ(c, sh->rope_half * 2 == sh->hdim, "partial rotary dimension not supported");
+    REQ(c, sh->hidden % 256 == 0 && sh->ffn % 256 == 0 && sh->qdim % 256 == 0, "dims must be multiples of 256");
+    REQ(c, sh->qdim == sh->heads * sh->hdim && sh->kvdim == sh->kv_heads * sh->hdim, "inconsistent dims");
+    REQ(c, sh->ctx > 0, "ctx must be positive");
+    const bool same = c->fused && c->L == sh->n_layer && c->H == sh->hidden && c->F == sh->ffn &&
+                      c->heads == sh->heads && c->kvh == sh->kv_heads && c->hd == sh->hdim && c->ctx == sh->ctx;
+    if (!same) {
+        free_fused(c);
+        c->L = sh->n_layer;
+        c->H = sh->hidden;
+        c->F = sh->ffn;
+        c->heads = sh->heads;
+        c->kvh = sh->kv_heads;
+        c->hd = sh->hdim;
+        c->qd = sh->qdim;
+        c->kvd = sh->kvdim;
+        c->ctx = sh->ctx;
+        c->half = sh->rope_half;
+        c->eps = sh->eps;
+        c->max_splits = (c->ctx + kSplitLen - 1) / kSplitLen;
+        const size_t T = kMaxChunk;
+        const size_t vocab = sh->outw ? (size_t)((HyWeight *)sh->outw)->n : 1;
+        CK(c, cudaMalloc(&c->d_kv, (size_t)c->L * 2 * c->ctx * c->kvd * sizeof(uint16_t)));
+        CK(c, cudaMemsetAsync(c->d_kv, 0, (size_t)c->L * 2 * c->ctx * c->kvd * sizeof(uint16_t), c->st));
+        CK(c, cudaMalloc(&c->d_h, T * c->H * 4));
+        CK(c, cudaMalloc(&c->d_qkv, T * (c->qd + 2 * c->kvd) * 4));
+        CK(c, cudaMalloc(&c->d_ao, T * c->qd * 4));
+        CK(c, cudaMalloc(&c->d_g, T * c->F * 4));
+        CK(c, cudaMalloc(&c->d_u, T * c->F * 4));
+        CK(c, cudaMalloc(&c->d_logits, vocab * 4));
+        CK(c, cudaMalloc(&c->d_part, (size_t)c->kvh * c->max_splits * G * (c->hd + 2) * 4));
+        CK(c, cudaMalloc(&c->d_tickets, (size_t)c->kvh * 4));
+        CK(c, cudaMemsetAsync(c->d_tickets, 0, (size_t)c->kvh * 4, c->st));
+        CK(c, cudaMalloc(&c->d_state, sizeof(DecodeState)));
+        CK(c, cudaMemsetAsync(c->d_state, 0, sizeof(DecodeState), c->st));
+        CK(c, cudaMalloc(&c->d_out_ids, (size_t)(c->ctx + 1) * 4));
+        CK(c, cudaMalloc(&c->d_tokens, (size_t)(c->ctx + 1) * 4));
+        CK(c, cudaMalloc(&c->d_chunk_pos, (size_t)(c->ctx / kMaxChunk + 2) * 4));
+        const size_t half_tab = (size_t)c->ctx * c->half * 4;
+        CK(c, cudaMalloc(&c->d_cos, half_tab));
+        CK(c, cudaMalloc(&c->d_sin, half_tab));
+        CK(c, cudaMalloc(&c->d_out_norm, (size_t)c->H * 4));
+        CK(c, cudaMalloc(&c->d_norms, (size_t)c->L * (2 * c->H + 2 * c->hd) * 4));
+    }
+    const size_t half_tab = (size_t)c->ctx * c->half * 4;
+    CK(c, cudaMemcpy(c->d_cos, sh->rope_cos, half_tab, cudaMemcpyHostToDevice));
+    CK(c, cudaMemcpy(c->d_sin, sh->rope_sin, half_tab, cudaMemcpyHostToDevice));
+    if (sh->out_norm) CK(c, cudaMemcpy(c->d_out_norm, sh->out_norm, (size_t)c->H * 4, cudaMemcpyHostToDevice));
+    c->layers.assign(c->L, Layer());
+    for (int i = 0; i < c->L; i++) {
+        const hy_fused_layer &fl = sh->layers[i];
+        Layer &L = c->layers[i];
+        L.q = (HyWeight *)fl.wq; L.k = (HyWeight *)fl.wk; L.v = (HyWeight *)fl.wv; L.o = (HyWeight *)fl.wo;
+        L.g = (HyWeight *)fl.wg; L.u = (HyWeight *)fl.wu; L.d = (HyWeight *)fl.wd;
+        REQ(c, L.q && L.k && L.v && L.o && L.g && L.u && L.d, "missing layer weight");
+        REQ(c, L.q->k == c->H && L.k->k == c->H && L.v->k == c->H && L.o->k == c->qd && L.g->k == c->H &&
+                   L.u->k == c->H && L.d->k == c->F,
+            "layer weight shapes do not match the model");
+        float *base = c->d_norms + (size_t)i * (2 * c->H + 2 * c->hd);
+        L.attn_norm = base;
+        L.ffn_norm = base + c->H;
+        L.q_norm = base + 2 * c->H;
+        L.k_norm = base + 2 * c->H + c->hd;
+        CK(c, cudaMemcpy(L.attn_norm, fl.attn_norm, (size_t)c->H * 4, cudaMemcpyHostToDevice));
+        CK(c, cudaMemcpy(L.ffn_norm, fl.ffn_norm, (size_t)c->H * 4, cudaMemcpyHostToDevice));
+        CK(c, cudaMemcpy(L.q_norm, fl.q_norm, (size_t)c->hd * 4, cudaMemcpyHostToDevice));
+        CK(c, cudaMemcpy(L.k_norm, fl.k_norm, (size_t)c->hd * 4, cudaMemcpyHostToDevice));
+    }
+    c->outw = (HyWeight *)sh->outw;
+    if (c->outw) REQ(c, c->outw->k == c->H, "LM head shape does not match the model");
+    graph_reset(c->g_fwd1);
+    graph_reset(c->g_fwd1_logits);
+    graph_reset(c->g_dec);
+    c->g_dec_vocab = -1;
+    CK(c, cudaStreamSynchronize(c->st));
+    c->fused = true;
+    return true;
+}
+
+// Whole-network forward for nt tokens at pos0.. with host h in/out and host
+// logits of the last token (reference contract src/device.h:65,
+// src/cuda.c:339-421): one H2D, device-resident layers, one D2H, one sync.
+bool fused_forward(void *impl, hy_fused_args *a) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->fused || !a || !a->h || a->nt < 1 || a->nt > kMaxChunk) return false;
+    if (a->pos0 < 0 || a->pos0 + a->nt > c->ctx) return false;
+    if (a->want_logits && (!c->outw || !a->logits)) return false;
+    if (cudaSetDevice(c->dev) != cudaSuccess) return false;
+    const int nt = a->nt;
+    for (int i = 0; i < c->L; i++) {  // the host may pass a fresh layer array; handles must match
+        const hy_fused_layer &fl = a->layers[i];
+        if ((HyWeight *)fl.wq != c->layers[i].q || (HyWeight *)fl.wd != c->layers[i].d) return false;
+    }
+    CK(c, cudaMemcpyAsync(c->d_h, a->h, (size_t)nt * c->H * 4, cudaMemcpyHostToDevice, c->st));
+    *c->h_pinned_int = a->pos0;
+    CK(c, cudaMemcpyAsync(&c->d_state->pos_fwd, c->h_pinned_int, 4, cudaMemcpyHostToDevice, c->st));
+    const int *pos_ptr = &c->d_state->pos_fwd;
+    if (nt == 1) {
+        Graph &g = a->want_logits ? c->g_fwd1_logits : c->g_fwd1;
+        if (!g.exec) {
+            const bool logits = a->want_logits != 0;
+            if (!capture(c, g, [&]() {
+                    if (!layers_forward(c, 1, pos_ptr, true)) return false;
+                    return !logits || head_forward(c, c->d_h, true, false, true);
+                }))
+                return false;
+        }
+        if (!graph_launch(c, g)) return false;
+    } else {
+        if (!layers_forward(c, nt, pos_ptr, false)) return false;
+        if (a->want_logits && !head_forward(c, c->d_h + (size_t)(nt - 1) * c->H, true, false, false)) return false;
+    }
+    CK(c, cudaMemcpyAsync(a->h, c->d_h, (size_t)nt * c->H * 4, cudaMemcpyDeviceToHost, c->st));
+    if (a->want_logits)
+        CK(c, cudaMemcpyAsync(a->logits, c->d_logits, (size_t)c->outw->n * 4, cudaMemcpyDeviceToHost, c->st));
+    CK(c, cudaStreamSynchronize(c->st));
+    return true;
+}
+
+const hy_device_ops kOps = {destroy_impl, upload, release, matmul, is_software, weight_out, fused_prepare,
+                            fused_forward};
+
+}  // namespace
+
+// ==================================================================== C ABI
+
+extern "C" {
+
+HYC_API int hy_cuda_probe(char *out, int cap) {
+    int n = 0;
+    const int ok = cudaGetDeviceCount(&n) == cudaSuccess && n > 0;
+    if (!ok) cudaGetLastError();
+    if (out && cap > 0) snprintf(out, (size_t)cap, "%d", ok);
+    return ok;
+}
+
+HYC_API void *hyc_create(int device, char *info, size_t cap) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n < 1) {
+        cudaGetLastError();
+        if (info && cap) snprintf(info, cap, "no CUDA device");
+        return nullptr;
+    }
+    if (device < 0 || device >= n) {
+        if (info && cap) snprintf(info, cap, "CUDA device %d out of range (%d present)", device, n);
+        return nullptr;
+    }
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, device) != cudaSuccess || p.major != 10) {
+        if (info && cap) snprintf(info, cap, "device %d is not sm_100 (this build targets B200 / sm_100a)", device);
+        return nullptr;
+    }
+    if (cudaSetDevice(device) != cudaSuccess) {
+        if (info && cap) snprintf(info, cap, "cudaSetDevice(%d) failed", device);
+        return nullptr;
+    }
+    HyCtx *c = new HyCtx();
+    c->dev = device;
+    c->nsm = p.multiProcessorCount;
+    init_kernel_attrs();
+    if (cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaHostAlloc((void **)&c->h_pinned_int, 4096, cudaHostAllocDefault) != cudaSuccess) {
+        if (info && cap) snprintf(info, cap, "stream / pinned allocation failed");
+        destroy_impl(c);
+        return nullptr;
+    }
+    if (info && cap) snprintf(info, cap, "%s (sm_%d%d, %d SMs, %.0f GB)", p.name, p.major, p.minor, p.multiProcessorCount,
+                              (double)p.totalGlobalMem / 1e9);
+    return c;
+}
+
+HYC_API const hy_device_ops *hyc_device_ops(void) { return &kOps; }
+
+HYC_API hy_device *hy_cuda_create(const char *pref, char *info, size_t cap) {
+    int dev = 0;
+    if (pref && pref[0] >= '0' && pref[0] <= '9') dev = atoi(pref);
+    if (!hy_device_wrap) {
+        if (info && cap) snprintf(info, cap, "host device layer not linked (standalone library: use hyc_create)");
+        return nullptr;
+    }
+    void *impl = hyc_create(dev, info, cap);
+    if (!impl) return nullptr;
+    hy_device *d = hy_device_wrap(HY_DEV_CUDA, "cuda", impl, &kOps, false);
+    if (!d) destroy_impl(impl);
+    return d;
+}
+
+HYC_API int hyc_last_error(void *impl, char *out, int cap) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!out || cap <= 0) return 0;
+    snprintf(out, (size_t)cap, "%s", c ? c->err : "null handle");
+    return (int)strlen(out);
+}
+
+HYC_API void *hyc_stream(void *impl) { return impl ? (void *)((HyCtx *)impl)->st : nullptr; }
+
+HYC_API int hyc_sync(void *impl) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c) return -1;
+    cudaError_t e = cudaStreamSynchronize(c->st);
+    if (e != cudaSuccess) {
+        fail(c, "cudaStreamSynchronize", e);
+        return -1;
+    }
+    return 0;
+}
+
+HYC_API int hyc_set_embedding(void *impl, hy_dweight *embd) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || !embd) return -1;
+    c->embd = (HyWeight *)embd;
+    graph_reset(c->g_dec);
+    c->g_dec_vocab = -1;
+    return 0;
+}
+
+HYC_API long long hyc_launch_count(void *impl) { return impl ? ((HyCtx *)impl)->launches : 0; }
+
+HYC_API void *hyc_host_alloc(size_t bytes) {
+    void *p = nullptr;
+    return cudaHostAlloc(&p, bytes, cudaHostAllocDefault) == cudaSuccess ? p : nullptr;
+}
+HYC_API void hyc_host_free(void *p) {
+    if (p) cudaFreeHost(p);
+}
+
+HYC_API int hyc_decode_begin(void *impl, const int *prompt, int n, int keep, int max_new, const int *stop_ids,
+                             int n_stop, int vocab_out) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->fused || !c->embd || !c->outw || !prompt) return -1;
+    if (n < 1 || keep < 0 || keep >= n || max_new < 1 || n + max_new > c->ctx || n_stop < 0 || n_stop > 16) return -1;
+    if (cudaSetDevice(c->dev) != cudaSuccess) return -1;
+    c->vocab_out = (vocab_out > 0 && vocab_out <= c->outw->n) ? vocab_out : c->outw->n;
+    DecodeState s;
+    memset(&s, 0, sizeof s);
+    s.pos = n - 1;
+    s.cap = max_new;
+    s.n_stop = n_stop;
+    for (int i = 0; i < n_stop; i++) s.stop_ids[i] = stop_ids[i];
+    std::vector<int> cp;
+    for (int p0 = keep; p0 < n; p0 += kMaxChunk) cp.push_back(p0);
+    if (cudaMemcpyAsync(c->d_state, &s, sizeof s, cudaMemcpyHostToDevice, c->st) != cudaSuccess ||
+        cudaMemcpyAsync(c->d_tokens, prompt + keep, (size_t)(n - keep) * 4, cudaMemcpyHostToDevice, c->st) != cudaSuccess ||
+        cudaMemcpyAsync(c->d_chunk_pos, cp.data(), cp.size() * 4, cudaMemcpyHostToDevice, c->st) != cudaSuccess) {
+        fail(c, "decode_begin copies", cudaErrorUnknown);
+        return -1;
+    }
+    for (size_t i = 0; i < cp.size(); i++) {
+        const int p0 = cp[i], nt = (n - p0) < kMaxChunk ? (n - p0) : kMaxChunk;
+        if (!launch(c, embed_rows, dim3(nt), dim3(256), 0, false, desc(c->embd, nullptr, 0),
+                    (const int *)(c->d_tokens + (p0 - keep)), c->d_h))
+            return -1;
+        if (!layers_forward(c, nt, c->d_chunk_pos + i, false)) return -1;
+        if (i + 1 == cp.size()) {
+            if (!head_forward(c, c->d_h + (size_t)(nt - 1) * c->H, false, true, false)) return -1;
+            if (!launch(c, decode_finalize, dim3(1), dim3(32), 0, false, c->d_state, c->d_out_ids)) return -1;
+        }
+    }
+    // the synchronous copies above were ordered before the launches; the graph
+    // for single-token steps is built once per vocab_out
+    if (!build_decode_graph(c)) return -1;
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        fail(c, "decode_begin", e);
+        return -1;
+    }
+    return 0;
+}
+
+HYC_API int hyc_decode_steps(void *impl, int steps) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->g_dec.exec) return -1;
+    for (int i = 0; i < steps; i++)
+        if (!graph_launch(c, c->g_dec)) return -1;
+    return 0;
+}
+
+HYC_API int hyc_decode_steps_host(void *impl, int steps, int *tok_io) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->g_dec.exec || !tok_io) return -1;
+    if (cudaMemcpyAsync(&tok_io[0], &c->d_state->tok, 4, cudaMemcpyDeviceToHost, c->st) != cudaSuccess) return -1;
+    for (int i = 0; i < steps; i++) {
+        if (cudaMemcpyAsync(&c->d_state->tok, &tok_io[i], 4, cudaMemcpyHostToDevice, c->st) != cudaSuccess) return -1;
+        if (!graph_launch(c, c->g_dec)) return -1;
+        if (cudaMemcpyAsync(&tok_io[i + 1], &c->d_state->tok, 4, cudaMemcpyDeviceToHost, c->st) != cudaSuccess) return -1;
+    }
+    return 0;
+}
+
+HYC_API int hyc_decode_read(void *impl, int *out_ids, int cap) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->fused) return -1;
+    DecodeState s;
+    if (cudaMemcpyAsync(&s, c->d_state, sizeof s, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
+        cudaStreamSynchronize(c->st) != cudaSuccess) {
+        fail(c, "decode_read", cudaErrorUnknown);
+        return -1;
+    }
+    int n = s.step < s.cap ? s.step : s.cap;
+    if (n > cap) n = cap;
+    if (n > 0 && out_ids) {
+        if (cudaMemcpy(out_ids, c->d_out_ids, (size_t)n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+        // truncate after the first stop id, as the host loop breaks there
+        for (int i = 0; i < n; i++)
+            for (int j = 0; j < s.n_stop; j++)
+                if (out_ids[i] == s.stop_ids[j]) return i;
+    }
+    return n;
+}
+
+HYC_API int hyc_decode_rewind(void *impl, int pos, int tok) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->fused || pos < 0 || pos >= c->ctx) return -1;
+    // tok and pos are adjacent ints in DecodeState; the values go through a
+    // ring of pinned slots so the copy can stay asynchronous
+    int *slot = c->h_pinned_int + 2 + 2 * (c->rewind_slot++ % 500);
+    slot[0] = tok;
+    slot[1] = pos;
+    if (cudaMemcpyAsync(&c->d_state->tok, slot, 8, cudaMemcpyHostToDevice, c->st) != cudaSuccess) return -1;
+    return 0;
+}
+
+HYC_API int hyc_generate(void *impl, const int *prompt, int n, int keep, int max_new, const int *stop_ids, int n_stop,
+                         int vocab_out, int *out_ids) {
+    if (hyc_decode_begin(impl, prompt, n, keep, max_new, stop_ids, n_stop, vocab_out) != 0) return -1;
+    if (max_new > 1 && hyc_decode_steps(impl, max_new - 1) != 0) return -1;
+    return hyc_decode_read(impl, out_ids, max_new);
+}
+
+HYC_API int hyc_quantize_q8k(void *impl, const float *x, int k, int nt, q8k_block *y) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !x || !y || k <= 0 || k % 256 || nt < 1 || nt > 16) return -1;
+    if (cudaSetDevice(c->dev) != cudaSuccess) return -1;
+    const size_t xb = (size_t)nt * k * 4, yb = (size_t)nt * (k / 256) * sizeof(q8k_block);
+    if (!ensure_buf(c, (void **)&c->d_x32, &c->x32_cap, xb) || !ensure_buf(c, (void **)&c->d_xq, &c->xq_cap, yb)) return -1;
+    if (cudaMemcpyAsync(c->d_x32, x, xb, cudaMemcpyHostToDevice, c->st) != cudaSuccess) return -1;
+    GemvArgs a = gemv_args(nt, k);
+    a.act = ACT_VEC;
+    a.x = c->d_x32;
+    a.ldx = k;
+    if (!launch(c, quantize_export, dim3(1), dim3(kGemvThreads), q8_smem_bytes(16, k), false, a, c->d_xq)) return -1;
+    if (cudaMemcpyAsync(y, c->d_xq, yb, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
+        cudaStreamSynchronize(c->st) != cudaSuccess)
+        return fail(c, "quantize", cudaErrorUnknown) ? 0 : -1;
+    return 0;
+}
+
+HYC_API int hyc_block_ints(void *impl, hy_dweight *hw, const q8k_block *xq, int nt, int32_t *out) {
+    HyCtx *c = (HyCtx *)impl;
+    HyWeight *w = (HyWeight *)hw;
+    if (!c || c->broken || !w || !xq || !out || nt < 1 || nt > 16 || !is_q8_fmt(w->fmt)) return -1;
+    if (cudaSetDevice(c->dev) != cudaSuccess || !ensure_out(w)) return -1;
+    const int per = w->fmt == FMT_Q4K ? 2 * w->nb : w->nb;
+    const size_t xb = (size_t)nt * w->nb * sizeof(q8k_block), ib = (size_t)nt * w->n * per * 4;
+    if (!ensure_buf(c, (void **)&c->d_xq, &c->xq_cap, xb) || !ensure_buf(c, (void **)&c->d_ints, &c->ints_cap, ib))
+        return -1;
+    if (cudaMemcpyAsync(c->d_xq, xq, xb, cudaMemcpyHostToDevice, c->st) != cudaSuccess) return -1;
+    GemvArgs a = gemv_args(nt, w->k);
+    a.act = ACT_Q8K;
+    a.xq = c->d_xq;
+    a.epi = EPI_STORE;
+    a.nw = 1;
+    a.rows_total = w->n;
+    a.w[0] = desc(w, w->d_out, w->n);
+    a.ints = c->d_ints;
+    if (!gemv_launch(c, a, false, 1)) return -1;
+    if (cudaMemcpyAsync(out, c->d_ints, ib, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
+        cudaStreamSynchronize(c->st) != cudaSuccess)
+        return -1;
+    return per;
+}
+
+HYC_API int hyc_matmul_f32(void *impl, hy_dweight *hw, const float *x, int nt, float *out) {
+    HyCtx *c = (HyCtx *)impl;
+    HyWeight *w = (HyWeight *)hw;
+    if (!c || c->broken || !w || !x || !out || nt < 1 || nt > MAX_BATCH) return -1;
+    if (cudaSetDevice(c->dev) != cudaSuccess || !ensure_out(w)) return -1;
+    const size_t xb = (size_t)nt * w->k * 4;
+    if (!ensure_buf(c, (void **)&c->d_x32, &c->x32_cap, xb)) return -1;
+    if (cudaMemcpyAsync(c->d_x32, x, xb, cudaMemcpyHostToDevice, c->st) != cudaSuccess) return -1;
+    GemvArgs a = gemv_args(nt, w->k);
+    a.act = ACT_VEC;  // Q8_K formats quantise on the device, fp32 formats use x as is
+    a.x = c->d_x32;
+    a.ldx = w->k;
+    a.epi = EPI_STORE;
+    a.nw = 1;
+    a.rows_total = w->n;
+    a.w[0] = desc(w, w->d_out, w->n);
+    if (!run_gemv(c, a, false)) return -1;
+    if (cudaMemcpyAsync(out, w->d_out, (size_t)nt * w->n * 4, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
+        cudaStreamSynchronize(c->st) != cudaSuccess)
+        return -1;
+    return 0;
+}
+
+HYC_API int hyc_dequant_row(void *impl, hy_dweight *hw, int row, float *dst) {
+    HyCtx *c = (HyCtx *)impl;
+    HyWeight *w = (HyWeight *)hw;
+    if (!c || c->broken || !w || !dst || row < 0 || row >= w->n) return -1;
+    if (cudaSetDevice(c->dev) != cudaSuccess) return -1;
+    if (!ensure_buf(c, (void **)&c->d_x32, &c->x32_cap, (size_t)w->k * 4)) return -1;
+    if (!launch(c, dequant_row_kernel, dim3(1), dim3(256), 0, false, desc(w, nullptr, 0), row, c->d_x32)) return -1;
+    if (cudaMemcpyAsync(dst, c->d_x32, (size_t)w->k * 4, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
+        cudaStreamSynchronize(c->st) != cudaSuccess)
+        return -1;
+    return 0;
+}
+
+HYC_API int hyc_kv_read(void *impl, int layer, int npos, uint16_t *k, uint16_t *v) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->fused || layer < 0 || layer >= c->L || npos < 0 || npos > c->ctx) return -1;
+    const uint16_t *kc = c->d_kv + (size_t)layer * 2 * c->ctx * c->kvd, *vc = kc + (size_t)c->ctx * c->kvd;
+    if (cudaMemcpyAsync(k, kc, (size_t)npos * c->kvd * 2, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
+        cudaMemcpyAsync(v, vc, (size_t)npos * c->kvd * 2, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
+        cudaStreamSynchronize(c->st) != cudaSuccess)
+        return -1;
+    return 0;
+}
+
+// Enqueue `iters` launches of one hot operation of the fused decode step
+// (no synchronisation) so a caller can time it with events on hyc_stream:
+//   0 LM-head GEMV + argmax    1 q|k|v GEMV     2 gate|up GEMV
+//   3 down GEMV (+SiLU prologue, +residual)     4 o_proj GEMV (+residual)
+//   5 decode attention at the current decode position
+// Layer weights rotate over all layers so they stream from HBM, not L2.
+HYC_API int hyc_bench_op(void *impl, int op, int iters) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->fused || iters < 1) return -1;
+    if (op == 0 && c->d_state && c->outw) {
+        for (int i = 0; i < iters; i++)
+            if (!head_forward(c, c->d_h, false, true, true)) return -1;
+        return 0;
+    }
+    for (int i = 0; i < iters; i++) {
+        const Layer &L = c->layers[i % c->L];
+        const int qkv_ld = c->qd + 2 * c->kvd;
+        bool ok = true;
+        if (op == 1 || op == 2) {
+            HyWeight *ws[3] = {L.q, L.k, L.v};
+            float *outs[3] = {c->d_qkv, c->d_qkv + c->qd, c->d_qkv + c->qd + c->kvd};
+            int lds[3] = {qkv_ld, qkv_ld, qkv_ld};
+            if (op == 2) {
+                ws[0] = L.g; ws[1] = L.u;
+                outs[0] = c->d_g; outs[1] = c->d_u;
+                lds[0] = lds[1] = c->F;
+            }
+            GemvArgs a = gemv_args(1, c->H);
+            a.act = ACT_NORM;
+            a.x = c->d_h;
+            a.ldx = c->H;
+            a.norm_w = op == 1 ? L.attn_norm : L.ffn_norm;
+            a.eps = c->eps;
+            a.epi = EPI_STORE;
+            ok = run_multi(c, ws, outs, lds, op == 1 ? 3 : 2, a, true);
+        } else if (op == 3 || op == 4) {
+            HyWeight *w = op == 3 ? L.d : L.o;
+            GemvArgs a = gemv_args(1, w->k);
+            a.act = op == 3 ? ACT_SILU : ACT_VEC;
+            a.x = op == 3 ? c->d_g : c->d_ao;
+            a.x2 = c->d_u;
+            a.ldx = w->k;
+            a.epi = EPI_ADD;
+            a.nw = 1;
+            a.rows_total = w->n;
+            a.w[0] = desc(w, c->d_tmp_h(), c->H);
+            ok = run_gemv(c, a, true);
+        } else if (op == 5) {
+            AttnArgs aa;
+            memset(&aa, 0, sizeof aa);
+            aa.qkv = c->d_qkv;
+            aa.qkv_ld = qkv_ld;
+            aa.kc = c->d_kv + (size_t)(i % c->L) * 2 * c->ctx * c->kvd;
+            aa.vc = aa.kc + (size_t)c->ctx * c->kvd;
+            aa.q_norm = L.q_norm;
+            aa.k_norm = L.k_norm;
+            aa.rope_cos = c->d_cos;
+            aa.rope_sin = c->d_sin;
+            aa.pos_ptr = &c->d_state->pos;
+            aa.nt = 1;
+            aa.heads = c->heads;
+            aa.kv_heads = c->kvh;
+            aa.kvdim = c->kvd;
+            aa.qdim = c->qd;
+            aa.ctx = c->ctx;
+            aa.half = c->half;
+            aa.eps = c->eps;
+            aa.scale = 1.0f / sqrtf((float)c->hd);
+            aa.ao = c->d_ao;
+            aa.part = c->d_part;
+            aa.tickets = c->d_tickets;
+            aa.split_len = kSplitLen;
+            aa.max_splits = c->max_splits;
+            ok = attention(c, aa, 1, true);
+        } else {
+            return -1;
+        }
+        if (!ok) return -1;
+    }
+    return 0;
+}
+
+// The host loader's RoPE tables (reference src/model.c:537 and :576-586),
+// evaluated with the same single-precision libm calls.
+HYC_API int hyc_rope_tables(float freq_base, float alpha, int hdim, int rope_dim, int ctx, float *cos_out,
+                            float *sin_out) {
+    if (hdim <= 0 || rope_dim <= 0 || (rope_dim & 1) || ctx <= 0 || !cos_out || !sin_out) return -1;
+    float base = freq_base;
+    if (alpha > 0 && hdim > 2) base *= powf(alpha, (float)hdim / (float)(hdim - 2));
+    const int half = rope_dim / 2;
+    for (int i = 0; i < half; i++) {
+        const float freq = 1.0f / powf(base, (float)i / (float)half);
+        for (int p = 0; p < ctx; p++) {
+            const float ang = (float)p * freq;
+            cos_out[(size_t)p * half + i] = cosf(ang);
+            sin_out[(size_t)p * half + i] = sinf(ang);
+        }
+    }
+    return 0;
+}
+
+}  // extern "C"

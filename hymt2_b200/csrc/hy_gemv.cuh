@@ -1,0 +1,712 @@
+// hy_gemv.cuh — quantised GEMV / small-batch GEMM on CUDA cores (sm_100a).
+//
+// One launch computes out[t][row] = dot(W[row], act[t]) for up to three
+// weights that share one activation (q/k/v, gate/up), t < nt <= NT.
+//
+// Prologue: every CTA builds the activation in shared memory itself —
+// RMSNorm / SiLU*up / plain copy, then the Q8_K quantiser (bit-identical to
+// reference src/kernels.c:128-165) — so no separate norm or quantise kernel
+// and no grid-wide barrier sits between producer and GEMV.  Weights of the
+// warp's first row are requested from HBM before griddepcontrol.wait, so the
+// fetch overlaps the previous kernel's tail.
+//
+// Main loop: one warp per row; each lane streams 16-byte weight chunks,
+// computes exact int32 per-256 block sums with dp4a, reduces each block
+// across the lanes that share it (exact), applies the block's scales in the
+// host's float order, then sums blocks across the warp.
+#pragma once
+#include "hy_common.cuh"
+
+namespace hyk {
+
+constexpr int kGemvWarps = 8;
+constexpr int kGemvThreads = kGemvWarps * 32;
+
+struct GemvArgs {
+    WDesc w[3];
+    int nw;
+    int rows_total;
+    int nt;
+    int k;
+    // activation source
+    int act;
+    const q8k_block *xq;
+    const float *x;
+    const float *x2;
+    int ldx;
+    const float *norm_w;
+    float eps;
+    // epilogue
+    int epi;
+    unsigned long long *amax;
+    int amax_rows;
+    int32_t *ints;  // optional exact per-block integers [nt][rows][nblk]
+};
+
+// ---------------------------------------------------------------- activation staging
+
+// Shared-memory plan for the Q8_K activation of NT tokens and K inputs.
+struct Q8Smem {
+    float *x;        // [K] fp32 staging of one token
+    int8_t *qp;      // [NT][4][K/4] plane-major codes
+    float *d;        // [NT][nb]
+    int *sum;        // [NT][nb]
+    int16_t *bs;     // [NT][nb*16]
+    float *red;      // [64]
+};
+
+__host__ __device__ inline size_t align16(size_t v) { return (v + 15) & ~(size_t)15; }
+
+__host__ __device__ inline size_t q8_smem_bytes(int NT, int K) {
+    const int nb = K / 256;
+    return align16((size_t)K * 4) + align16((size_t)NT * K) + align16((size_t)NT * nb * 4) * 2 +
+           align16((size_t)NT * nb * 32) + 64 * 4;
+}
+
+__device__ inline Q8Smem q8_smem(uint8_t *base, int NT, int K) {
+    const int nb = K / 256;
+    Q8Smem s;
+    size_t o = 0;
+    s.x = (float *)(base + o); o += align16((size_t)K * 4);
+    s.qp = (int8_t *)(base + o); o += align16((size_t)NT * K);
+    s.d = (float *)(base + o); o += align16((size_t)NT * nb * 4);
+    s.sum = (int *)(base + o); o += align16((size_t)NT * nb * 4);
+    s.bs = (int16_t *)(base + o); o += align16((size_t)NT * nb * 32);
+    s.red = (float *)(base + o);
+    return s;
+}
+
+// Block-wide sum over kGemvThreads threads.
+__device__ inline float block_sum(float v, float *red) {
+    v = warp_sum(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) red[w] = v;
+    __syncthreads();
+    float t = l < (int)(blockDim.x >> 5) ? red[l] : 0.f;
+    return warp_sum(t);
+}
+
+// Fill s.x with token t's fp32 activation according to a.act.
+__device__ inline void stage_fp32(const GemvArgs &a, int t, float *dst, float *red, int K) {
+    const float *x = a.x + (size_t)t * a.ldx;
+    if (a.act == ACT_NORM) {
+        float ss = 0.f;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) {
+            const float v = x[i];
+            ss = __fadd_rn(ss, __fmul_rn(v, v));
+        }
+        ss = block_sum(ss, red);
+        const float scale = 1.0f / sqrtf(ss / (float)K + a.eps);
+        for (int i = threadIdx.x; i < K; i += blockDim.x) dst[i] = __fmul_rn(__fmul_rn(x[i], scale), a.norm_w[i]);
+    } else if (a.act == ACT_SILU) {
+        const float *u = a.x2 + (size_t)t * a.ldx;
+        for (int i = threadIdx.x; i < K; i += blockDim.x) {
+            const float g = x[i];
+            dst[i] = __fmul_rn(g / (1.0f + expf(-g)), u[i]);
+        }
+    } else {
+        for (int i = threadIdx.x; i < K; i += blockDim.x) dst[i] = x[i];
+    }
+}
+
+// Q8_K quantisation of one 256 block held in smem `src`, by one warp; writes
+// plane-major codes and block constants for token t.  Bit-identical to the
+// host quantiser: first index of the largest |x|, iscale = -127/max,
+// d = 1/iscale, round-half-even, clip +-127, non-finite products -> 0.
+__device__ inline void quantize_block_warp(const float *src, Q8Smem &s, int t, int b, int nb, int K) {
+    const int lane = threadIdx.x & 31;
+    const float *p = src + b * 256 + lane * 8;
+    const float4 v0 = *(const float4 *)&p[0], v1 = *(const float4 *)&p[4];
+    const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    float ba = 0.f, bv = 0.f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float av = fabsf(v[j]);
+        if (av > ba) { ba = av; bv = v[j]; bi = lane * 8 + j; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, ba, o);
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oa > ba || (oa == ba && oi < bi)) { ba = oa; bv = ov; bi = oi; }
+    }
+    int q[8];
+    float d = 0.f;
+    if (ba == 0.f) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) q[j] = 0;
+    } else {
+        const float iscale = -127.f / bv;
+        d = 1.f / iscale;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float f = __fmul_rn(iscale, v[j]);
+            int r = isfinite(f) ? __float2int_rn(f) : 0;
+            r = r > 127 ? 127 : (r < -127 ? -127 : r);
+            q[j] = r;
+        }
+    }
+    int part = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) part += q[j];
+    const int pair = part + __shfl_xor_sync(0xffffffffu, part, 1);
+    const int total = warp_sum_i(part);
+    // natural element e = lane*8 + j -> chunk ch = lane/8, plane l = (lane%8)/2, byte (lane&1)*8 + j
+    const int ch = lane >> 3, l = (lane & 7) >> 1;
+    const int pos = (b * 4 + piece_of_chunk(ch)) * 16 + (lane & 1) * 8;
+    int8_t *dst = s.qp + (size_t)t * K + (size_t)l * (K / 4) + pos;
+    uint32_t lo = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
+    uint32_t hi = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
+    *(uint2 *)dst = make_uint2(lo, hi);
+    if ((lane & 1) == 0) s.bs[(size_t)t * nb * 16 + b * 16 + (lane >> 1)] = (int16_t)pair;
+    if (lane == 0) {
+        s.d[t * nb + b] = d;
+        s.sum[t * nb + b] = total;
+    }
+}
+
+// Build the Q8_K activation of all nt tokens in shared memory.
+__device__ inline void stage_q8k(const GemvArgs &a, Q8Smem &s, int K) {
+    const int nb = K / 256;
+    const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    for (int t = 0; t < a.nt; t++) {
+        if (a.act == ACT_Q8K) {
+            // host-made blocks: qp is already lane-major per block
+            const q8k_block *src = a.xq + (size_t)t * nb;
+            for (int i = threadIdx.x; i < nb * 16; i += blockDim.x) {
+                const int b = i >> 4, part = i & 15, l = part >> 2, piece = part & 3;
+                const uint4 v = *(const uint4 *)&src[b].qp[l * 64 + piece * 16];
+                *(uint4 *)&s.qp[(size_t)t * K + (size_t)l * (K / 4) + b * 64 + piece * 16] = v;
+            }
+            for (int i = threadIdx.x; i < nb * 16; i += blockDim.x)
+                s.bs[(size_t)t * nb * 16 + i] = src[i >> 4].bsums[i & 15];
+            for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+                s.d[t * nb + b] = src[b].d;
+                s.sum[t * nb + b] = src[b].sum;
+            }
+        } else {
+            stage_fp32(a, t, s.x, s.red, K);
+            __syncthreads();
+            for (int b = warp; b < nb; b += nwarps) quantize_block_warp(s.x, s, t, b, nb, K);
+        }
+        __syncthreads();
+    }
+}
+
+// ---------------------------------------------------------------- row bookkeeping
+
+__device__ __forceinline__ void map_row(const GemvArgs &a, int r, int &wi, int &lr) {
+    wi = 0;
+    lr = r;
+    if (a.nw > 1 && lr >= a.w[0].n) {
+        lr -= a.w[0].n;
+        wi = 1;
+        if (a.nw > 2 && lr >= a.w[1].n) {
+            lr -= a.w[1].n;
+            wi = 2;
+        }
+    }
+}
+
+__device__ __forceinline__ const WDesc &wsel(const GemvArgs &a, int wi) {
+    return wi == 0 ? a.w[0] : (wi == 1 ? a.w[1] : a.w[2]);
+}
+
+// Lane 0 applies the row epilogue; `best` tracks the warp's argmax candidate.
+template <int NT>
+__device__ __forceinline__ void row_epilogue(const GemvArgs &a, const WDesc &w, int lr, int row, const float *res,
+                                             unsigned long long &best) {
+    if ((threadIdx.x & 31) != 0) return;
+    if (a.epi == EPI_ARGMAX) {
+        if (w.out) w.out[lr] = res[0];
+        if (row < a.amax_rows) {
+            const unsigned long long key = argmax_key(res[0], (uint32_t)row);
+            if (key > best) best = key;
+        }
+        return;
+    }
+#pragma unroll
+    for (int t = 0; t < NT; t++) {
+        if (t >= a.nt) break;
+        float *o = w.out + (size_t)t * w.ld + lr;
+        if (a.epi == EPI_ADD) *o += res[t];
+        else *o = res[t];
+    }
+}
+
+__device__ inline void argmax_commit(const GemvArgs &a, unsigned long long best, float *red_area) {
+    if (a.epi != EPI_ARGMAX) return;
+    unsigned long long *sk = (unsigned long long *)red_area;
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    __syncthreads();
+    if (l == 0) sk[w] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned long long m = 0;
+        for (int i = 0; i < (int)(blockDim.x >> 5); i++) m = sk[i] > m ? sk[i] : m;
+        if (m) atomicMax(a.amax, m);
+    }
+}
+
+// ---------------------------------------------------------------- PANEL (STQ1_0 / Q2_0C)
+
+// Exact block integer of one 16-byte panel chunk against 64 activation bytes
+// (4 planes x 16): sum_l sum_i code_l(w[i]) * a_l[i].
+__device__ __forceinline__ int panel_chunk_dot(const uint4 wv, const int4 *act4) {
+    const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+    int e = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const int a0 = ((const int *)&act4[0])[j], a1 = ((const int *)&act4[1])[j];
+        const int a2 = ((const int *)&act4[2])[j], a3 = ((const int *)&act4[3])[j];
+        e = dp4a((int)(wd[j] & 0x03030303u), a0, e);
+        e = dp4a((int)((wd[j] >> 2) & 0x03030303u), a1, e);
+        e = dp4a((int)((wd[j] >> 4) & 0x03030303u), a2, e);
+        e = dp4a((int)((wd[j] >> 6) & 0x03030303u), a3, e);
+    }
+    return e;
+}
+
+// Decode (nt == 1): the lane's activation chunks live in registers for the
+// whole launch.  CPL = 16-byte chunks per lane per row (K <= 2048*CPL).
+template <int CPL>
+__global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt1(const __grid_constant__ GemvArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int K = a.k, nb = K / 256, nchunk = nb * 4;
+    const int lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * kGemvWarps + (threadIdx.x >> 5), nw = gridDim.x * kGemvWarps;
+
+    // prefetch the first row's weights before waiting on the producer
+    uint4 wcur[CPL];
+    float scur[CPL];
+    int r = gw, wi = 0, lr = 0;
+    if (r < a.rows_total) {
+        map_row(a, r, wi, lr);
+        const WDesc &w = wsel(a, wi);
+#pragma unroll
+        for (int i = 0; i < CPL; i++) {
+            const int c = lane + 32 * i;
+            if (c < nchunk) {
+                wcur[i] = ldg_stream(w.w + (size_t)lr * w.stride + (size_t)c * 16);
+                scur[i] = __ldg(w.s + (size_t)lr * nb + (c >> 2));
+            }
+        }
+    }
+    pdl_wait();
+    Q8Smem s = q8_smem(smem, 1, K);
+    stage_q8k(a, s, K);
+    pdl_trigger();
+
+    int4 act[CPL][4];
+    float dblk[CPL];
+    int sblk[CPL];
+#pragma unroll
+    for (int i = 0; i < CPL; i++) {
+        const int c = lane + 32 * i;
+        if (c < nchunk) {
+#pragma unroll
+            for (int l = 0; l < 4; l++) act[i][l] = *(const int4 *)&s.qp[(size_t)l * (K / 4) + c * 16];
+            dblk[i] = s.d[c >> 2];
+            sblk[i] = s.sum[c >> 2];
+        } else {
+#pragma unroll
+            for (int l = 0; l < 4; l++) act[i][l] = make_int4(0, 0, 0, 0);
+            dblk[i] = 0.f;
+            sblk[i] = 0;
+        }
+    }
+
+    unsigned long long best = 0;
+    for (; r < a.rows_total; r += nw) {
+        // issue the next row's loads before computing this one
+        const int rn = r + nw;
+        int wn = 0, ln = 0;
+        uint4 wnext[CPL];
+        float snext[CPL];
+        if (rn < a.rows_total) {
+            map_row(a, rn, wn, ln);
+            const WDesc &w2 = wsel(a, wn);
+#pragma unroll
+            for (int i = 0; i < CPL; i++) {
+                const int c = lane + 32 * i;
+                if (c < nchunk) {
+                    wnext[i] = ldg_stream(w2.w + (size_t)ln * w2.stride + (size_t)c * 16);
+                    snext[i] = __ldg(w2.s + (size_t)ln * nb + (c >> 2));
+                }
+            }
+        }
+        const WDesc &w = wsel(a, wi);
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < CPL; i++) {
+            const int c = lane + 32 * i;
+            int e = c < nchunk ? panel_chunk_dot(wcur[i], act[i]) : 0;
+            e += __shfl_xor_sync(0xffffffffu, e, 1);
+            e += __shfl_xor_sync(0xffffffffu, e, 2);
+            if (c < nchunk && (lane & 3) == 0) {
+                const int v = e * (1 << w.shift) - w.off * sblk[i];
+                if (a.ints) a.ints[(size_t)r * nb + (c >> 2)] = v;
+                acc += scur[i] * dblk[i] * (float)v;
+            }
+        }
+        acc = warp_sum(acc);
+        row_epilogue<1>(a, w, lr, r, &acc, best);
+#pragma unroll
+        for (int i = 0; i < CPL; i++) {
+            wcur[i] = wnext[i];
+            scur[i] = snext[i];
+        }
+        wi = wn;
+        lr = ln;
+    }
+    argmax_commit(a, best, s.red);
+}
+
+// Small batches (1 < nt <= NT): activations read from plane-major smem.
+template <int NT>
+__global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt(const __grid_constant__ GemvArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int K = a.k, nb = K / 256, nchunk = nb * 4;
+    const int lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * kGemvWarps + (threadIdx.x >> 5), nw = gridDim.x * kGemvWarps;
+    pdl_wait();
+    Q8Smem s = q8_smem(smem, NT, K);
+    stage_q8k(a, s, K);
+    pdl_trigger();
+    unsigned long long best = 0;
+    for (int r = gw; r < a.rows_total; r += nw) {
+        int wi, lr;
+        map_row(a, r, wi, lr);
+        const WDesc &w = wsel(a, wi);
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = 0.f;
+        for (int c0 = 0; c0 < nchunk; c0 += 32) {
+            const int c = c0 + lane;
+            const bool ok = c < nchunk;
+            uint4 wv = make_uint4(0, 0, 0, 0);
+            float sc = 0.f;
+            if (ok) {
+                wv = ldg_stream(w.w + (size_t)lr * w.stride + (size_t)c * 16);
+                sc = __ldg(w.s + (size_t)lr * nb + (c >> 2));
+            }
+            const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+            uint32_t code[4][4];
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int l = 0; l < 4; l++) code[l][j] = (wd[j] >> (2 * l)) & 0x03030303u;
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                if (t >= a.nt) break;
+                int e = 0;
+                if (ok) {
+#pragma unroll
+                    for (int l = 0; l < 4; l++) {
+                        const int4 av = *(const int4 *)&s.qp[(size_t)t * K + (size_t)l * (K / 4) + c * 16];
+                        e = dp4a((int)code[l][0], av.x, e);
+                        e = dp4a((int)code[l][1], av.y, e);
+                        e = dp4a((int)code[l][2], av.z, e);
+                        e = dp4a((int)code[l][3], av.w, e);
+                    }
+                }
+                e += __shfl_xor_sync(0xffffffffu, e, 1);
+                e += __shfl_xor_sync(0xffffffffu, e, 2);
+                if (ok && (lane & 3) == 0) {
+                    const int b = c >> 2;
+                    const int v = e * (1 << w.shift) - w.off * s.sum[t * nb + b];
+                    if (a.ints) a.ints[((size_t)t * a.rows_total + r) * nb + b] = v;
+                    acc[t] += sc * s.d[t * nb + b] * (float)v;
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = warp_sum(acc[t]);
+        row_epilogue<NT>(a, w, lr, r, acc, best);
+    }
+    argmax_commit(a, best, s.red);
+}
+
+// ---------------------------------------------------------------- Q6_K
+
+// Unit = (block b, half hf, 16-group s): ql[hf*64+s*16..+16], ql[..+32],
+// qh[hf*32+s*16..+16] -> 64 codes in 4 quarters of 16; quarter q covers
+// natural elements hf*128 + q*32 + s*16 + [0,16) with sub-scale index
+// hf*8 + 2q + s (layout of reference src/kernels.c:786-806).
+template <int NT>
+__global__ void __launch_bounds__(kGemvThreads) gemv_q6k(const __grid_constant__ GemvArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int K = a.k, nb = K / 256, nunit = nb * 4;
+    const int lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * kGemvWarps + (threadIdx.x >> 5), nw = gridDim.x * kGemvWarps;
+    pdl_wait();
+    Q8Smem s = q8_smem(smem, NT, K);
+    stage_q8k(a, s, K);
+    pdl_trigger();
+    unsigned long long best = 0;
+    for (int r = gw; r < a.rows_total; r += nw) {
+        int wi, lr;
+        map_row(a, r, wi, lr);
+        const WDesc &w = wsel(a, wi);
+        const uint8_t *row = w.w + (size_t)lr * w.stride;
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = 0.f;
+        for (int u0 = 0; u0 < nunit; u0 += 32) {
+            const int u = u0 + lane;
+            const bool ok = u < nunit;
+            const int b = u >> 2, hf = (u >> 1) & 1, sg = u & 1;
+            uint4 qa = make_uint4(0, 0, 0, 0), qb = qa, qh = qa, scv = qa;
+            float dw = 0.f;
+            if (ok) {
+                qa = ldg_stream(row + (size_t)b * 128 + hf * 64 + sg * 16);
+                qb = ldg_stream(row + (size_t)b * 128 + hf * 64 + 32 + sg * 16);
+                qh = ldg_stream(row + (size_t)nb * 128 + (size_t)b * 64 + hf * 32 + sg * 16);
+                scv = __ldg((const uint4 *)(row + (size_t)nb * 192 + (size_t)b * 16));
+                dw = h2f(__ldg((const unsigned short *)(row + (size_t)nb * 208) + b));
+            }
+            const int8_t *sc = (const int8_t *)&scv;
+            const uint32_t A[4] = {qa.x, qa.y, qa.z, qa.w}, B[4] = {qb.x, qb.y, qb.z, qb.w};
+            const uint32_t Hh[4] = {qh.x, qh.y, qh.z, qh.w};
+            uint32_t code[4][4];
+#pragma unroll
+            for (int q = 0; q < 4; q++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const uint32_t src = (q & 1) ? B[j] : A[j];
+                    const uint32_t lo = (src >> (4 * (q >> 1))) & 0x0f0f0f0fu;
+                    const uint32_t hi = (Hh[j] >> (2 * q)) & 0x03030303u;
+                    code[q][j] = lo | (hi << 4);
+                }
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                if (t >= a.nt) break;
+                int acc_i = 0;
+                if (ok) {
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        // natural element base hf*128 + q*32 + sg*16 -> chunk hf*2 + q/2, plane (2q+sg)&3
+                        const int ch = hf * 2 + (q >> 1), l = (2 * q + sg) & 3;
+                        const int4 av = *(const int4 *)&s.qp[(size_t)t * K + (size_t)l * (K / 4) +
+                                                            (b * 4 + piece_of_chunk(ch)) * 16];
+                        int tq = dp4a((int)code[q][0], av.x, 0);
+                        tq = dp4a((int)code[q][1], av.y, tq);
+                        tq = dp4a((int)code[q][2], av.z, tq);
+                        tq = dp4a((int)code[q][3], av.w, tq);
+                        const int sub = hf * 8 + 2 * q + sg;
+                        tq -= 32 * (int)s.bs[(size_t)t * nb * 16 + b * 16 + sub];
+                        acc_i += (int)sc[sub] * tq;
+                    }
+                }
+                acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 1);
+                acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 2);
+                if (ok && (lane & 3) == 0) {
+                    if (a.ints) a.ints[((size_t)t * a.rows_total + r) * nb + b] = acc_i;
+                    acc[t] += dw * s.d[t * nb + b] * (float)acc_i;
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = warp_sum(acc[t]);
+        row_epilogue<NT>(a, w, lr, r, acc, best);
+    }
+    argmax_commit(a, best, s.red);
+}
+
+// ---------------------------------------------------------------- Q4_K
+
+__device__ __forceinline__ void k4_scale_min(const uint8_t *q, int j, int &sc, int &mn) {
+    if (j < 4) {
+        sc = q[j] & 63;
+        mn = q[j + 4] & 63;
+    } else {
+        sc = (q[j + 4] & 0x0f) | ((q[j - 4] >> 6) << 4);
+        mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+// Unit = (block b, pair g, 16-half s): qs[32g + 16s .. +16]; low nibbles are
+// elements 64g+16s+i (sub-block 2g), high nibbles 64g+32+16s+i (sub-block
+// 2g+1) — reference src/kernels.c:861-877.
+template <int NT>
+__global__ void __launch_bounds__(kGemvThreads) gemv_q4k(const __grid_constant__ GemvArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int K = a.k, nb = K / 256, nunit = nb * 8;
+    const int lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * kGemvWarps + (threadIdx.x >> 5), nw = gridDim.x * kGemvWarps;
+    pdl_wait();
+    Q8Smem s = q8_smem(smem, NT, K);
+    stage_q8k(a, s, K);
+    pdl_trigger();
+    unsigned long long best = 0;
+    for (int r = gw; r < a.rows_total; r += nw) {
+        int wi, lr;
+        map_row(a, r, wi, lr);
+        const WDesc &w = wsel(a, wi);
+        const uint8_t *row = w.w + (size_t)lr * w.stride;
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = 0.f;
+        for (int u0 = 0; u0 < nunit; u0 += 32) {
+            const int u = u0 + lane;
+            const bool ok = u < nunit;
+            const int b = u >> 3, g = (u >> 1) & 3, sg = u & 1;
+            uint4 qv = make_uint4(0, 0, 0, 0), hdr = qv;
+            if (ok) {
+                qv = ldg_stream(row + (size_t)b * 144 + 16 + g * 32 + sg * 16);
+                hdr = __ldg((const uint4 *)(row + (size_t)b * 144));
+            }
+            const uint8_t *hb = (const uint8_t *)&hdr;
+            int sc0, mn0, sc1, mn1;
+            k4_scale_min(hb + 4, 2 * g, sc0, mn0);
+            k4_scale_min(hb + 4, 2 * g + 1, sc1, mn1);
+            const float dd = h2f(*(const unsigned short *)hb), dm = h2f(*(const unsigned short *)(hb + 2));
+            const uint32_t Q[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                if (t >= a.nt) break;
+                int si = 0, sm = 0;
+                if (ok) {
+                    const int4 alo = *(const int4 *)&s.qp[(size_t)t * K + (size_t)sg * (K / 4) + (b * 4 + piece_of_chunk(g)) * 16];
+                    const int4 ahi = *(const int4 *)&s.qp[(size_t)t * K + (size_t)(2 + sg) * (K / 4) + (b * 4 + piece_of_chunk(g)) * 16];
+                    int s0 = dp4a((int)(Q[0] & 0x0f0f0f0fu), alo.x, 0);
+                    s0 = dp4a((int)(Q[1] & 0x0f0f0f0fu), alo.y, s0);
+                    s0 = dp4a((int)(Q[2] & 0x0f0f0f0fu), alo.z, s0);
+                    s0 = dp4a((int)(Q[3] & 0x0f0f0f0fu), alo.w, s0);
+                    int s1 = dp4a((int)((Q[0] >> 4) & 0x0f0f0f0fu), ahi.x, 0);
+                    s1 = dp4a((int)((Q[1] >> 4) & 0x0f0f0f0fu), ahi.y, s1);
+                    s1 = dp4a((int)((Q[2] >> 4) & 0x0f0f0f0fu), ahi.z, s1);
+                    s1 = dp4a((int)((Q[3] >> 4) & 0x0f0f0f0fu), ahi.w, s1);
+                    si = sc0 * s0 + sc1 * s1;
+                    if (sg == 0) {
+                        const int16_t *bs = s.bs + (size_t)t * nb * 16 + b * 16;
+                        sm = mn0 * ((int)bs[4 * g] + (int)bs[4 * g + 1]) + mn1 * ((int)bs[4 * g + 2] + (int)bs[4 * g + 3]);
+                    }
+                }
+#pragma unroll
+                for (int o = 1; o < 8; o <<= 1) {
+                    si += __shfl_xor_sync(0xffffffffu, si, o);
+                    sm += __shfl_xor_sync(0xffffffffu, sm, o);
+                }
+                if (ok && (lane & 7) == 0) {
+                    if (a.ints) {
+                        a.ints[(((size_t)t * a.rows_total + r) * nb + b) * 2] = si;
+                        a.ints[(((size_t)t * a.rows_total + r) * nb + b) * 2 + 1] = sm;
+                    }
+                    acc[t] += s.d[t * nb + b] * (dd * (float)si - dm * (float)sm);
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = warp_sum(acc[t]);
+        row_epilogue<NT>(a, w, lr, r, acc, best);
+    }
+    argmax_commit(a, best, s.red);
+}
+
+// ---------------------------------------------------------------- fp32-activation formats
+
+// Q8_0 / F16 / F32 use the fp32 activation itself (reference
+// src/kernels.c:1272-1300), staged in shared memory as [t][quad][unit][4] so
+// each lane's 16-byte reads are bank-conflict free.
+template <int FMT>
+struct FpFmt;
+template <>
+struct FpFmt<FMT_Q80> { static constexpr int kElems = 16; };  // 16 int8 per 16-byte unit
+template <>
+struct FpFmt<FMT_F16> { static constexpr int kElems = 8; };
+template <>
+struct FpFmt<FMT_F32> { static constexpr int kElems = 4; };
+
+// [NT][K] permuted activations, then a [K] staging row and 64 floats of reduction space.
+__host__ __device__ inline size_t fp_smem_bytes(int NT, int K) { return align16((size_t)NT * K * 4) + (size_t)K * 4 + 64 * 4; }
+
+template <int FMT, int NT>
+__global__ void __launch_bounds__(kGemvThreads) gemv_fp(const __grid_constant__ GemvArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    constexpr int E = FpFmt<FMT>::kElems, QPU = E / 4;
+    const int K = a.k, nunit = K / E;
+    const int lane = threadIdx.x & 31;
+    const int gw = blockIdx.x * kGemvWarps + (threadIdx.x >> 5), nw = gridDim.x * kGemvWarps;
+    float *sx = (float *)smem;                                   // [NT][QPU][nunit][4]
+    float *stg = (float *)(smem + align16((size_t)NT * K * 4));  // [K] staging
+    float *red = stg + K;
+    pdl_wait();
+    for (int t = 0; t < a.nt; t++) {
+        stage_fp32(a, t, stg, red, K);
+        __syncthreads();
+        for (int e = threadIdx.x; e < K; e += blockDim.x) {
+            const int u = e / E, q = (e % E) >> 2, j = e & 3;
+            sx[(((size_t)t * QPU + q) * nunit + u) * 4 + j] = stg[e];
+        }
+        __syncthreads();
+    }
+    pdl_trigger();
+    unsigned long long best = 0;
+    for (int r = gw; r < a.rows_total; r += nw) {
+        int wi, lr;
+        map_row(a, r, wi, lr);
+        const WDesc &w = wsel(a, wi);
+        const uint8_t *row = w.w + (size_t)lr * w.stride;
+        float acc[NT];
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = 0.f;
+        for (int u0 = 0; u0 < nunit; u0 += 32) {
+            const int u = u0 + lane;
+            const bool ok = u < nunit;
+            float wf[E];
+            float scale = 1.f;
+            if (ok) {
+                const uint4 v = ldg_stream(row + (size_t)u * 16);
+                if (FMT == FMT_Q80) {
+                    const int8_t *q = (const int8_t *)&v;
+#pragma unroll
+                    for (int j = 0; j < E; j++) wf[j] = (float)q[j];
+                    scale = h2f(__ldg((const unsigned short *)(row + K) + (u >> 1)));
+                } else if (FMT == FMT_F16) {
+                    const __half *h = (const __half *)&v;
+#pragma unroll
+                    for (int j = 0; j < E; j++) wf[j] = __half2float(h[j]);
+                } else {
+                    const float *f = (const float *)&v;
+#pragma unroll
+                    for (int j = 0; j < E; j++) wf[j] = f[j];
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < E; j++) wf[j] = 0.f;
+            }
+#pragma unroll
+            for (int t = 0; t < NT; t++) {
+                if (t >= a.nt) break;
+                float p = 0.f;
+                if (ok) {
+#pragma unroll
+                    for (int q = 0; q < QPU; q++) {
+                        const float4 xv = *(const float4 *)&sx[(((size_t)t * QPU + q) * nunit + u) * 4];
+                        p = fmaf(wf[4 * q + 0], xv.x, p);
+                        p = fmaf(wf[4 * q + 1], xv.y, p);
+                        p = fmaf(wf[4 * q + 2], xv.z, p);
+                        p = fmaf(wf[4 * q + 3], xv.w, p);
+                    }
+                }
+                if (FMT == FMT_Q80) {
+                    // two 16-wide halves form one 32-block: sum, then scale
+                    p += __shfl_xor_sync(0xffffffffu, p, 1);
+                    if ((lane & 1) == 0) acc[t] += scale * p;
+                } else {
+                    acc[t] += p;
+                }
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < NT; t++) acc[t] = warp_sum(acc[t]);
+        row_epilogue<NT>(a, w, lr, r, acc, best);
+    }
+    argmax_commit(a, best, red);
+}
+
+}  // namespace hyk

@@ -1,0 +1,124 @@
+/* hymt2_cuda.h — C ABI of the B200 (sm_100a) device backend for hymt2.
+ *
+ * Drop-in entry points (what the hymt2 host binds):
+ *   hy_cuda_create / hy_cuda_probe replace reference src/cuda.c:151-183 and
+ *   src/cuda.c:18-34 (declared by the host in src/device.c:8-9).  The created
+ *   device fills the host's `hy_device_ops` vtable (reference
+ *   src/device.h:70-79) with the semantics listed there: upload / release /
+ *   matmul / fused_prepare / fused_forward.
+ *
+ * Standalone entry points (hyc_*): the same implementation without the
+ * host's device wrapper, plus the additive operations the host vtable cannot
+ * express — on-device embedding, argmax and token feedback so a decode step
+ * runs as one CUDA graph with no host synchronisation.
+ *
+ * Conventions follow the host's: bool/NULL (or int 0 / negative) for
+ * success/failure, `info` strings on create, one host thread per handle.
+ * After any CUDA error a handle is "broken" and refuses further work; the
+ * host then falls back to its CPU path as it does today.
+ */
+#ifndef HYMT2_CUDA_H
+#define HYMT2_CUDA_H
+
+#include "hy_device_abi.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(_WIN32)
+#define HYC_API __declspec(dllexport)
+#else
+#define HYC_API __attribute__((visibility("default")))
+#endif
+
+/* ---- drop-in (replaces reference src/cuda.c) -------------------------- */
+
+/* Replaces src/cuda.c:151 hy_cuda_create.  `pref` "auto" or a device
+ * ordinal ("0", "1", ...).  Wraps the implementation with the host's
+ * hy_device_wrap (src/device.c:25); returns NULL with a reason in `info` when
+ * no sm_100 GPU is usable or when the host device layer is not linked in
+ * (standalone shared-library use: call hyc_create instead). */
+HYC_API hy_device *hy_cuda_create(const char *pref, char *info, size_t cap);
+/* Replaces src/cuda.c:18 hy_cuda_probe: writes "1" when a CUDA driver and
+ * device are present, else "0"; returns the same as int. */
+HYC_API int hy_cuda_probe(char *out, int cap);
+
+/* ---- standalone handle ------------------------------------------------ */
+
+/* Create the backend on `device` (ordinal).  NULL + reason in `info` on failure. */
+HYC_API void *hyc_create(int device, char *info, size_t cap);
+/* The vtable hy_cuda_create registers with the host (reference
+ * src/device.h:70-79 layout). */
+HYC_API const hy_device_ops *hyc_device_ops(void);
+/* Last error text of a handle ("" when none). */
+HYC_API int hyc_last_error(void *impl, char *out, int cap);
+/* cudaStream_t the handle launches on (for timing with external events). */
+HYC_API void *hyc_stream(void *impl);
+HYC_API int hyc_sync(void *impl);
+
+/* ---- additive operations (no counterpart in the reference vtable) ----- */
+
+/* Weight the device embedding lookup reads (the token embedding; may be the
+ * same handle as the LM head when they are tied). */
+HYC_API int hyc_set_embedding(void *impl, hy_dweight *embd);
+
+/* Greedy generation entirely on the device: prefill prompt[keep..n) in
+ * chunks (positions keep..n-1; positions < keep are reused from the device KV
+ * cache, the longest-common-prefix contract of reference src/model.c:931-936),
+ * then `max_new` argmax steps (first maximum over rows [0, vocab_out) wins,
+ * src/model.c:945-948) with token feedback, stopping after a token in
+ * stop_ids.  Writes the generated ids to out_ids and returns their count, or
+ * a negative value on error.  Requires fused_prepare and hyc_set_embedding. */
+HYC_API int hyc_generate(void *impl, const int *prompt, int n, int keep, int max_new, const int *stop_ids,
+                         int n_stop, int vocab_out, int *out_ids);
+
+/* Lower-level decode control used by hyc_generate and the benchmark:
+ *  hyc_decode_begin: prefill like hyc_generate and leave the first generated
+ *    token on the device (no synchronisation);
+ *  hyc_decode_steps: enqueue `steps` single-token decode graphs;
+ *  hyc_decode_steps_host: the same, but every step's input token is copied
+ *    from pinned host memory tok_io[s] and its result written back to
+ *    tok_io[s+1] (tok_io must hold steps+1 ints, allocated with
+ *    hyc_host_alloc);
+ *  hyc_decode_read: synchronise and copy the emitted ids (returns count);
+ *  hyc_decode_rewind: enqueue (asynchronously) a new next-token / next
+ *    position; KV rows >= pos are overwritten by later steps.  Up to 500
+ *    rewinds may be in flight before the stream is synchronised. */
+HYC_API int hyc_decode_begin(void *impl, const int *prompt, int n, int keep, int max_new, const int *stop_ids,
+                             int n_stop, int vocab_out);
+HYC_API int hyc_decode_steps(void *impl, int steps);
+HYC_API int hyc_decode_steps_host(void *impl, int steps, int *tok_io);
+HYC_API int hyc_decode_read(void *impl, int *out_ids, int cap);
+HYC_API int hyc_decode_rewind(void *impl, int pos, int tok);
+HYC_API void *hyc_host_alloc(size_t bytes);
+HYC_API void hyc_host_free(void *p);
+
+/* ---- kernel-level hooks for parity tests (host buffers, synchronous) -- */
+
+/* Device Q8_K quantiser on x[nt][k]; writes full host blocks. */
+HYC_API int hyc_quantize_q8k(void *impl, const float *x, int k, int nt, q8k_block *y);
+/* Exact per-block int32 accumulators of the GEMV for host blocks xq[nt][k/256]:
+ * out[t][row][b] (Q4_K: pairs sumi, summ).  Returns ints per (t, row). */
+HYC_API int hyc_block_ints(void *impl, hy_dweight *w, const q8k_block *xq, int nt, int32_t *out);
+/* One row of a device weight as fp32. */
+HYC_API int hyc_dequant_row(void *impl, hy_dweight *w, int row, float *dst);
+/* fp32-activation GEMV (Q8_0 / F16 / F32 weights): out[t*n + r]. */
+HYC_API int hyc_matmul_f32(void *impl, hy_dweight *w, const float *x, int nt, float *out);
+/* bf16 KV rows [0, npos) of one layer of the fused cache. */
+HYC_API int hyc_kv_read(void *impl, int layer, int npos, uint16_t *k, uint16_t *v);
+/* RoPE tables exactly as the host loader computes them (src/model.c:537,576-586). */
+HYC_API int hyc_rope_tables(float freq_base, float alpha, int hdim, int rope_dim, int ctx, float *cos_out,
+                            float *sin_out);
+/* Number of kernels this handle has enqueued so far (graph replays count
+ * every kernel node of the graph). */
+HYC_API long long hyc_launch_count(void *impl);
+/* Enqueue `iters` launches of one hot operation of the decode step for
+ * timing: 0 LM head + argmax, 1 q|k|v GEMV, 2 gate|up GEMV, 3 down GEMV,
+ * 4 o_proj GEMV, 5 decode attention; layer weights rotate over all layers. */
+HYC_API int hyc_bench_op(void *impl, int op, int iters);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
