@@ -85,6 +85,10 @@ SIGNATURES = {
     "hyc_rope_tables": (I, [F, F, I, I, I, P, P]),
     "hyc_launch_count": (C.c_longlong, [P]),
     "hyc_bench_op": (I, [P, I, I]),
+    "hyc_gemv_test": (I, [P, P, I, P, P, P, F, I, I, P]),
+    "hyc_debug_buffer": (I, [P, I, P, Z]),
+    "hyc_gemv_multi_test": (I, [P, P, I, I, P, P, F, I, P]),
+    "hyc_attention_test": (I, [P, I, I, I, I, I, I, F, P, P, P, P, P, P, P, P]),
 }
 
 

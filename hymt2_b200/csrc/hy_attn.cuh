@@ -19,7 +19,7 @@ struct AttnArgs {
     const float *q_norm, *k_norm;
     const float *rope_cos, *rope_sin;  // [ctx][half]
     const int *pos_ptr;     // position of token 0
-    int nt, heads, kv_heads, kvdim, qdim, ctx, half;
+    int nt, heads, kv_heads, hd, kvdim, qdim, ctx, half;
     float eps, scale;
     float *ao;              // [nt][qdim]
     float *part;            // decode split partials [kv_heads][max_splits][G][HD+2]

@@ -112,6 +112,17 @@ bool fail(HyCtx *c, const char *what, cudaError_t e) {
         }                                                             \
     } while (0)
 
+// All host<->device copies go through the handle's stream: a plain cudaMemcpy
+// from pageable memory may return before its DMA lands, and the stream is
+// non-blocking, so only stream order makes the data visible to our kernels.
+cudaError_t h2d(HyCtx *c, void *dst, const void *src, size_t bytes) {
+    return cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, c->st);
+}
+cudaError_t d2h(HyCtx *c, void *dst, const void *src, size_t bytes) {
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, c->st);
+    return e == cudaSuccess ? cudaStreamSynchronize(c->st) : e;
+}
+
 template <typename... KArgs, typename... Args>
 bool launch(HyCtx *c, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, bool pdl, Args &&...args) {
     cudaLaunchConfig_t cfg = {};
@@ -272,17 +283,17 @@ bool run_multi(HyCtx *c, HyWeight *const *ws, float *const *outs, const int *lds
 
 template <int HD, int G>
 bool attn_launch(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
-    if (nt == 1) return launch(c, attn_decode<HD, G>, dim3(c->kvh, c->max_splits), dim3(G * 32), 0, pdl, aa);
-    int warps = c->heads + c->kvh;
+    if (nt == 1) return launch(c, attn_decode<HD, G>, dim3(aa.kv_heads, aa.max_splits), dim3(G * 32), 0, pdl, aa);
+    int warps = aa.heads + aa.kv_heads;
     if (warps > 32) warps = 32;
     if (!launch(c, rope_norm_store<HD>, dim3(nt), dim3(warps * 32), 0, pdl, aa)) return false;
-    return launch(c, attn_prefill<HD, G>, dim3(c->kvh, nt), dim3(G * 32), 0, pdl, aa);
+    return launch(c, attn_prefill<HD, G>, dim3(aa.kv_heads, nt), dim3(G * 32), 0, pdl, aa);
 }
 
 bool attention(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
-    const int G = c->heads / c->kvh;
+    const int G = aa.heads / aa.kv_heads;
 #define HY_ATT(HD_, G_) \
-    if (c->hd == HD_ && G == G_) return attn_launch<HD_, G_>(c, aa, nt, pdl);
+    if (aa.hd == HD_ && G == G_) return attn_launch<HD_, G_>(c, aa, nt, pdl);
     HY_ATT(128, 4) HY_ATT(128, 1) HY_ATT(128, 2) HY_ATT(128, 8)
     HY_ATT(64, 4) HY_ATT(64, 1) HY_ATT(64, 2) HY_ATT(64, 8)
 #undef HY_ATT
@@ -320,6 +331,7 @@ bool layer_forward(HyCtx *c, int li, int nt, const int *pos_ptr, bool pdl) {
         aa.nt = nt;
         aa.heads = c->heads;
         aa.kv_heads = c->kvh;
+        aa.hd = c->hd;
         aa.kvdim = c->kvd;
         aa.qdim = c->qd;
         aa.ctx = c->ctx;
@@ -560,12 +572,12 @@ hy_dweight *upload(void *impl, const weight_t *w) {
         ok = cudaMalloc(&d->w, pk_bytes) == cudaSuccess && cudaMalloc(&d->s, ps_bytes) == cudaSuccess;
         if (!ok) return bail("out of device memory");
         if (w->pk) {
-            ok = cudaMemcpy(d->w, w->pk, pk_bytes, cudaMemcpyHostToDevice) == cudaSuccess &&
-                 cudaMemcpy(d->s, w->ps, ps_bytes, cudaMemcpyHostToDevice) == cudaSuccess;
+            ok = h2d(c, d->w, w->pk, pk_bytes) == cudaSuccess &&
+                 h2d(c, d->s, w->ps, ps_bytes) == cudaSuccess;
         } else {
             uint8_t *raw = nullptr;
             const size_t rb = (size_t)d->n * w->row_bytes;
-            ok = cudaMalloc(&raw, rb) == cudaSuccess && cudaMemcpy(raw, w->data, rb, cudaMemcpyHostToDevice) == cudaSuccess;
+            ok = cudaMalloc(&raw, rb) == cudaSuccess && h2d(c, raw, w->data, rb) == cudaSuccess;
             if (ok) {
                 const long long tot = (long long)d->n * d->nb;
                 panel_from_native<<<(unsigned)((tot + 255) / 256), 256, 0, c->st>>>(raw, (long long)w->row_bytes, w->type,
@@ -581,7 +593,7 @@ hy_dweight *upload(void *impl, const weight_t *w) {
         d->fmt = FMT_Q4K;
         d->stride = (long long)d->nb * 144;
         ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess &&
-             cudaMemcpy(d->w, w->data, (size_t)d->n * d->stride, cudaMemcpyHostToDevice) == cudaSuccess;
+             h2d(c, d->w, w->data, (size_t)d->n * d->stride) == cudaSuccess;
         break;
     case GT_Q6_K: {
         if (w->k % 256) return bail("inner dimension not a block multiple");
@@ -590,7 +602,7 @@ hy_dweight *upload(void *impl, const weight_t *w) {
         uint8_t *raw = nullptr;
         const size_t rb = (size_t)d->n * d->nb * 210;
         ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess && cudaMalloc(&raw, rb) == cudaSuccess &&
-             cudaMemcpy(raw, w->data, rb, cudaMemcpyHostToDevice) == cudaSuccess;
+             h2d(c, raw, w->data, rb) == cudaSuccess;
         if (ok) {
             const long long tot = (long long)d->n * d->nb;
             q6k_relayout<<<(unsigned)((tot + 255) / 256), 256, 0, c->st>>>(raw, d->n, d->nb, d->w, d->stride);
@@ -607,7 +619,7 @@ hy_dweight *upload(void *impl, const weight_t *w) {
         uint8_t *raw = nullptr;
         const size_t rb = (size_t)d->n * nblk * 34;
         ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess && cudaMalloc(&raw, rb) == cudaSuccess &&
-             cudaMemcpy(raw, w->data, rb, cudaMemcpyHostToDevice) == cudaSuccess;
+             h2d(c, raw, w->data, rb) == cudaSuccess;
         if (ok) {
             const long long tot = (long long)d->n * nblk;
             q80_relayout<<<(unsigned)((tot + 255) / 256), 256, 0, c->st>>>(raw, d->n, nblk, d->w, d->stride);
@@ -623,12 +635,13 @@ hy_dweight *upload(void *impl, const weight_t *w) {
         d->fmt = w->type == GT_F16 ? FMT_F16 : FMT_F32;
         d->stride = (long long)w->k * es;
         ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess &&
-             cudaMemcpy(d->w, w->data, (size_t)d->n * d->stride, cudaMemcpyHostToDevice) == cudaSuccess;
+             h2d(c, d->w, w->data, (size_t)d->n * d->stride) == cudaSuccess;
         break;
     }
     default:
         return bail("unsupported weight type");
     }
+    if (ok) ok = cudaStreamSynchronize(c->st) == cudaSuccess;
     if (!ok) {
         c->broken = true;
         return bail("device copy failed");
@@ -751,9 +764,9 @@ bool fused_prepare(void *impl, const hy_fused_args *sh) {
         CK(c, cudaMalloc(&c->d_norms, (size_t)c->L * (2 * c->H + 2 * c->hd) * 4));
     }
     const size_t half_tab = (size_t)c->ctx * c->half * 4;
-    CK(c, cudaMemcpy(c->d_cos, sh->rope_cos, half_tab, cudaMemcpyHostToDevice));
-    CK(c, cudaMemcpy(c->d_sin, sh->rope_sin, half_tab, cudaMemcpyHostToDevice));
-    if (sh->out_norm) CK(c, cudaMemcpy(c->d_out_norm, sh->out_norm, (size_t)c->H * 4, cudaMemcpyHostToDevice));
+    CK(c, h2d(c, c->d_cos, sh->rope_cos, half_tab));
+    CK(c, h2d(c, c->d_sin, sh->rope_sin, half_tab));
+    if (sh->out_norm) CK(c, h2d(c, c->d_out_norm, sh->out_norm, (size_t)c->H * 4));
     c->layers.assign(c->L, Layer());
     for (int i = 0; i < c->L; i++) {
         const hy_fused_layer &fl = sh->layers[i];
@@ -769,10 +782,10 @@ bool fused_prepare(void *impl, const hy_fused_args *sh) {
         L.ffn_norm = base + c->H;
         L.q_norm = base + 2 * c->H;
         L.k_norm = base + 2 * c->H + c->hd;
-        CK(c, cudaMemcpy(L.attn_norm, fl.attn_norm, (size_t)c->H * 4, cudaMemcpyHostToDevice));
-        CK(c, cudaMemcpy(L.ffn_norm, fl.ffn_norm, (size_t)c->H * 4, cudaMemcpyHostToDevice));
-        CK(c, cudaMemcpy(L.q_norm, fl.q_norm, (size_t)c->hd * 4, cudaMemcpyHostToDevice));
-        CK(c, cudaMemcpy(L.k_norm, fl.k_norm, (size_t)c->hd * 4, cudaMemcpyHostToDevice));
+        CK(c, h2d(c, L.attn_norm, fl.attn_norm, (size_t)c->H * 4));
+        CK(c, h2d(c, L.ffn_norm, fl.ffn_norm, (size_t)c->H * 4));
+        CK(c, h2d(c, L.q_norm, fl.q_norm, (size_t)c->hd * 4));
+        CK(c, h2d(c, L.k_norm, fl.k_norm, (size_t)c->hd * 4));
     }
     c->outw = (HyWeight *)sh->outw;
     if (c->outw) REQ(c, c->outw->k == c->H, "LM head shape does not match the model");
@@ -866,6 +879,7 @@ HYC_API void *hyc_create(int device, char *info, size_t cap) {
     c->dev = device;
     c->nsm = p.multiProcessorCount;
     init_kernel_attrs();
+    set_smem(quantize_export);
     if (cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking) != cudaSuccess ||
         cudaHostAlloc((void **)&c->h_pinned_int, 4096, cudaHostAllocDefault) != cudaSuccess) {
         if (info && cap) snprintf(info, cap, "stream / pinned allocation failed");
@@ -1007,7 +1021,7 @@ HYC_API int hyc_decode_read(void *impl, int *out_ids, int cap) {
     int n = s.step < s.cap ? s.step : s.cap;
     if (n > cap) n = cap;
     if (n > 0 && out_ids) {
-        if (cudaMemcpy(out_ids, c->d_out_ids, (size_t)n * 4, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+        if (d2h(c, out_ids, c->d_out_ids, (size_t)n * 4) != cudaSuccess) return -1;
         // truncate after the first stop id, as the host loop breaks there
         for (int i = 0; i < n; i++)
             for (int j = 0; j < s.n_stop; j++)
@@ -1187,6 +1201,7 @@ HYC_API int hyc_bench_op(void *impl, int op, int iters) {
             aa.nt = 1;
             aa.heads = c->heads;
             aa.kv_heads = c->kvh;
+            aa.hd = c->hd;
             aa.kvdim = c->kvd;
             aa.qdim = c->qd;
             aa.ctx = c->ctx;
@@ -1204,6 +1219,171 @@ HYC_API int hyc_bench_op(void *impl, int op, int iters) {
         }
         if (!ok) return -1;
     }
+    return 0;
+}
+
+// One GEMV with a fused prologue on host inputs (act 1 copy, 2 RMSNorm*w,
+// 3 SiLU(x)*x2); epi_add != 0 adds into the host `out` it is given.
+HYC_API int hyc_gemv_test(void *impl, hy_dweight *hw, int act, const float *x, const float *x2, const float *norm_w,
+                          float eps, int nt, int epi_add, float *out) {
+    HyCtx *c = (HyCtx *)impl;
+    HyWeight *w = (HyWeight *)hw;
+    if (!c || c->broken || !w || !x || !out || nt < 1 || nt > MAX_BATCH || act < 1 || act > 3) return -1;
+    if ((act == 2 && !norm_w) || (act == 3 && !x2)) return -1;
+    if (cudaSetDevice(c->dev) != cudaSuccess || !ensure_out(w)) return -1;
+    const size_t xb = (size_t)nt * w->k * 4;
+    float *dx = nullptr, *dx2 = nullptr, *dn = nullptr;
+    bool ok = cudaMalloc(&dx, xb) == cudaSuccess && cudaMalloc(&dx2, xb) == cudaSuccess &&
+              cudaMalloc(&dn, (size_t)w->k * 4) == cudaSuccess &&
+              h2d(c, dx, x, xb) == cudaSuccess &&
+              (!x2 || h2d(c, dx2, x2, xb) == cudaSuccess) &&
+              (!norm_w || h2d(c, dn, norm_w, (size_t)w->k * 4) == cudaSuccess) &&
+              (!epi_add || h2d(c, w->d_out, out, (size_t)nt * w->n * 4) == cudaSuccess);
+    if (ok) {
+        GemvArgs a = gemv_args(nt, w->k);
+        a.act = act;
+        a.x = dx;
+        a.x2 = dx2;
+        a.ldx = w->k;
+        a.norm_w = dn;
+        a.eps = eps;
+        a.epi = epi_add ? EPI_ADD : EPI_STORE;
+        a.nw = 1;
+        a.rows_total = w->n;
+        a.w[0] = desc(w, w->d_out, w->n);
+        ok = run_gemv(c, a, false) &&
+             cudaMemcpyAsync(out, w->d_out, (size_t)nt * w->n * 4, cudaMemcpyDeviceToHost, c->st) == cudaSuccess &&
+             cudaStreamSynchronize(c->st) == cudaSuccess;
+    }
+    cudaFree(dx);
+    cudaFree(dx2);
+    cudaFree(dn);
+    return ok ? 0 : -1;
+}
+
+// Up to three weights sharing one activation, merged into launches the way
+// the fused layer merges q|k|v and gate|up; outs[i] receive [nt][n_i].
+HYC_API int hyc_gemv_multi_test(void *impl, hy_dweight *const *hws, int cnt, int act, const float *x,
+                                const float *norm_w, float eps, int nt, float *const *outs) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !hws || cnt < 1 || cnt > 3 || !x || nt < 1 || nt > MAX_BATCH || act < 1 || act > 2) return -1;
+    if (act == 2 && !norm_w) return -1;
+    HyWeight *ws[3];
+    float *douts[3] = {nullptr, nullptr, nullptr};
+    int lds[3];
+    for (int i = 0; i < cnt; i++) {
+        ws[i] = (HyWeight *)hws[i];
+        if (!ws[i] || ws[i]->k != ws[0]->k || !ensure_out(ws[i])) return -1;
+        douts[i] = ws[i]->d_out;
+        lds[i] = ws[i]->n;
+    }
+    const int K = ws[0]->k;
+    float *dx = nullptr, *dn = nullptr;
+    bool ok = cudaMalloc(&dx, (size_t)nt * K * 4) == cudaSuccess && cudaMalloc(&dn, (size_t)K * 4) == cudaSuccess &&
+              h2d(c, dx, x, (size_t)nt * K * 4) == cudaSuccess &&
+              (!norm_w || h2d(c, dn, norm_w, (size_t)K * 4) == cudaSuccess);
+    if (ok) {
+        GemvArgs a = gemv_args(nt, K);
+        a.act = act;
+        a.x = dx;
+        a.ldx = K;
+        a.norm_w = dn;
+        a.eps = eps;
+        a.epi = EPI_STORE;
+        ok = run_multi(c, ws, douts, lds, cnt, a, false);
+        for (int i = 0; ok && i < cnt; i++)
+            ok = cudaMemcpyAsync(outs[i], douts[i], (size_t)nt * ws[i]->n * 4, cudaMemcpyDeviceToHost, c->st) ==
+                 cudaSuccess;
+        ok = ok && cudaStreamSynchronize(c->st) == cudaSuccess;
+    }
+    cudaFree(dx);
+    cudaFree(dn);
+    return ok ? 0 : -1;
+}
+
+// Attention with its fused rope / q-k norm / bf16 KV-store prologue on host
+// buffers: qkv [nt][q|k|v] pre-rope, kc/vc [ctx][kvdim] in/out, ao [nt][qdim].
+// nt == 1 runs the decode kernel (split-KV), nt > 1 the prefill pair.
+HYC_API int hyc_attention_test(void *impl, int heads, int kv_heads, int hdim, int ctx, int nt, int pos0, float eps,
+                               const float *qkv, uint16_t *kc, uint16_t *vc, const float *q_norm,
+                               const float *k_norm, const float *rope_cos, const float *rope_sin, float *ao) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || heads < 1 || kv_heads < 1 || heads % kv_heads || nt < 1 || nt > kMaxChunk || pos0 < 0 ||
+        pos0 + nt > ctx)
+        return -1;
+    if (cudaSetDevice(c->dev) != cudaSuccess) return -1;
+    const int G = heads / kv_heads, qd = heads * hdim, kvd = kv_heads * hdim, half = hdim / 2;
+    const int splits = (ctx + kSplitLen - 1) / kSplitLen;
+    const size_t qkv_b = (size_t)nt * (qd + 2 * kvd) * 4, kv_b = (size_t)ctx * kvd * 2, tab_b = (size_t)ctx * half * 4;
+    float *dqkv = nullptr, *dqn = nullptr, *dkn = nullptr, *dcos = nullptr, *dsin = nullptr, *dao = nullptr,
+          *dpart = nullptr;
+    uint16_t *dkc = nullptr, *dvc = nullptr;
+    int *dtick = nullptr, *dpos = nullptr;
+    bool ok = cudaMalloc(&dqkv, qkv_b) == cudaSuccess && cudaMalloc(&dkc, kv_b) == cudaSuccess &&
+              cudaMalloc(&dvc, kv_b) == cudaSuccess && cudaMalloc(&dqn, hdim * 4) == cudaSuccess &&
+              cudaMalloc(&dkn, hdim * 4) == cudaSuccess && cudaMalloc(&dcos, tab_b) == cudaSuccess &&
+              cudaMalloc(&dsin, tab_b) == cudaSuccess && cudaMalloc(&dao, (size_t)nt * qd * 4) == cudaSuccess &&
+              cudaMalloc(&dpart, (size_t)kv_heads * splits * G * (hdim + 2) * 4) == cudaSuccess &&
+              cudaMalloc(&dtick, kv_heads * 4) == cudaSuccess && cudaMalloc(&dpos, 4) == cudaSuccess &&
+              cudaMemsetAsync(dtick, 0, kv_heads * 4, c->st) == cudaSuccess &&
+              h2d(c, dpos, &pos0, 4) == cudaSuccess &&
+              h2d(c, dqkv, qkv, qkv_b) == cudaSuccess &&
+              h2d(c, dkc, kc, kv_b) == cudaSuccess &&
+              h2d(c, dvc, vc, kv_b) == cudaSuccess &&
+              h2d(c, dqn, q_norm, hdim * 4) == cudaSuccess &&
+              h2d(c, dkn, k_norm, hdim * 4) == cudaSuccess &&
+              h2d(c, dcos, rope_cos, tab_b) == cudaSuccess &&
+              h2d(c, dsin, rope_sin, tab_b) == cudaSuccess;
+    if (ok) {
+        AttnArgs aa;
+        memset(&aa, 0, sizeof aa);
+        aa.qkv = dqkv;
+        aa.qkv_ld = qd + 2 * kvd;
+        aa.kc = dkc;
+        aa.vc = dvc;
+        aa.q_norm = dqn;
+        aa.k_norm = dkn;
+        aa.rope_cos = dcos;
+        aa.rope_sin = dsin;
+        aa.pos_ptr = dpos;
+        aa.nt = nt;
+        aa.heads = heads;
+        aa.kv_heads = kv_heads;
+        aa.hd = hdim;
+        aa.kvdim = kvd;
+        aa.qdim = qd;
+        aa.ctx = ctx;
+        aa.half = half;
+        aa.eps = eps;
+        aa.scale = 1.0f / sqrtf((float)hdim);
+        aa.ao = dao;
+        aa.part = dpart;
+        aa.tickets = dtick;
+        aa.split_len = kSplitLen;
+        aa.max_splits = splits;
+        ok = attention(c, aa, nt, false) &&
+             cudaMemcpyAsync(ao, dao, (size_t)nt * qd * 4, cudaMemcpyDeviceToHost, c->st) == cudaSuccess &&
+             cudaMemcpyAsync(kc, dkc, kv_b, cudaMemcpyDeviceToHost, c->st) == cudaSuccess &&
+             cudaMemcpyAsync(vc, dvc, kv_b, cudaMemcpyDeviceToHost, c->st) == cudaSuccess &&
+             cudaStreamSynchronize(c->st) == cudaSuccess;
+    }
+    void *ptrs[] = {dqkv, dqn, dkn, dcos, dsin, dao, dpart, dkc, dvc, dtick, dpos};
+    for (void *p : ptrs) cudaFree(p);
+    return ok ? 0 : -1;
+}
+
+// Copy one internal activation buffer of the fused state to the host:
+// 0 h [256][hidden], 1 qkv [256][q|k|v], 2 ao [256][qdim], 3 gate, 4 up [256][ffn].
+HYC_API int hyc_debug_buffer(void *impl, int which, float *out, size_t count) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || !c->fused || !out) return -1;
+    const float *src[5] = {c->d_h, c->d_qkv, c->d_ao, c->d_g, c->d_u};
+    const size_t cap[5] = {(size_t)kMaxChunk * c->H, (size_t)kMaxChunk * (c->qd + 2 * c->kvd), (size_t)kMaxChunk * c->qd,
+                           (size_t)kMaxChunk * c->F, (size_t)kMaxChunk * c->F};
+    if (which < 0 || which > 4 || count > cap[which]) return -1;
+    if (cudaStreamSynchronize(c->st) != cudaSuccess ||
+        d2h(c, out, src[which], count * 4) != cudaSuccess)
+        return -1;
     return 0;
 }
 

@@ -120,6 +120,31 @@ class Backend:
             raise BackendError("matmul_f32: " + self.error())
         return out
 
+    def gemv_test(self, h: int, act: int, x, rows: int, x2=None, norm_w=None, eps: float = 1e-5,
+                  add_to: np.ndarray | None = None) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        nt = x.shape[0]
+        out = np.zeros((nt, rows), dtype=np.float32) if add_to is None else np.ascontiguousarray(add_to).copy()
+        x2p = None if x2 is None else np.ascontiguousarray(x2, dtype=np.float32)
+        nwp = None if norm_w is None else np.ascontiguousarray(norm_w, dtype=np.float32)
+        rc = self.lib.hyc_gemv_test(self.impl, h, act, x.ctypes.data, None if x2p is None else x2p.ctypes.data,
+                                    None if nwp is None else nwp.ctypes.data, eps, nt, int(add_to is not None),
+                                    out.ctypes.data)
+        if rc != 0:
+            raise BackendError("gemv_test: " + self.error())
+        return out
+
+    def attention_test(self, heads, kv_heads, hd, ctx, qkv, pos0, kc, vc, q_norm, k_norm, cos, sin, eps=1e-5):
+        qkv = np.ascontiguousarray(qkv, dtype=np.float32)
+        nt = qkv.shape[0]
+        ao = np.zeros((nt, heads * hd), dtype=np.float32)
+        rc = self.lib.hyc_attention_test(self.impl, heads, kv_heads, hd, ctx, nt, pos0, eps, qkv.ctypes.data,
+                                         kc.ctypes.data, vc.ctypes.data, q_norm.ctypes.data, k_norm.ctypes.data,
+                                         cos.ctypes.data, sin.ctypes.data, ao.ctypes.data)
+        if rc != 0:
+            raise BackendError("attention_test: " + self.error())
+        return ao
+
     def dequant_row(self, h: int, row: int, k: int) -> np.ndarray:
         out = np.zeros(k, dtype=np.float32)
         if self.lib.hyc_dequant_row(self.impl, h, row, out.ctypes.data) != 0:

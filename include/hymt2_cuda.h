@@ -105,6 +105,26 @@ HYC_API int hyc_block_ints(void *impl, hy_dweight *w, const q8k_block *xq, int n
 HYC_API int hyc_dequant_row(void *impl, hy_dweight *w, int row, float *dst);
 /* fp32-activation GEMV (Q8_0 / F16 / F32 weights): out[t*n + r]. */
 HYC_API int hyc_matmul_f32(void *impl, hy_dweight *w, const float *x, int nt, float *out);
+/* One GEMV with a fused activation prologue on host inputs: act 1 = x as is,
+ * 2 = RMSNorm(x[t]) * norm_w, 3 = SiLU(x) * x2; the Q8_K formats then
+ * quantise on the device.  epi_add != 0 adds into the given `out`. */
+HYC_API int hyc_gemv_test(void *impl, hy_dweight *w, int act, const float *x, const float *x2, const float *norm_w,
+                          float eps, int nt, int epi_add, float *out);
+/* Up to three weights of equal k sharing one activation (act 1 plain, 2
+ * RMSNorm*w), merged into launches as the fused layer merges q|k|v and
+ * gate|up; outs[i] receives [nt][rows_i]. */
+HYC_API int hyc_gemv_multi_test(void *impl, hy_dweight *const *ws, int cnt, int act, const float *x,
+                                const float *norm_w, float eps, int nt, float *const *outs);
+/* Attention with its fused rope -> q/k RMSNorm -> bf16 KV-store prologue on
+ * host buffers (qkv [nt][q|k|v] pre-rope; kc/vc [ctx][kvdim] in/out;
+ * ao [nt][qdim]).  nt == 1 runs the split-KV decode kernel. */
+HYC_API int hyc_attention_test(void *impl, int heads, int kv_heads, int hdim, int ctx, int nt, int pos0, float eps,
+                               const float *qkv, uint16_t *kc, uint16_t *vc, const float *q_norm,
+                               const float *k_norm, const float *rope_cos, const float *rope_sin, float *ao);
+/* Copy an internal activation buffer of the fused state to the host (after
+ * synchronising): 0 residual h, 1 q|k|v, 2 attention output, 3 gate, 4 up;
+ * `count` floats from the start of the buffer. */
+HYC_API int hyc_debug_buffer(void *impl, int which, float *out, size_t count);
 /* bf16 KV rows [0, npos) of one layer of the fused cache. */
 HYC_API int hyc_kv_read(void *impl, int layer, int npos, uint16_t *k, uint16_t *v);
 /* RoPE tables exactly as the host loader computes them (src/model.c:537,576-586). */

@@ -370,8 +370,20 @@ typedef struct {
     float *out;
 } mm_ctx;
 
+/* Accumulation precision of orc_matmul: 0 = float (the host's order), 1 =
+ * double (the float64 reference the reference's own model test compares
+ * against to measure its rounding spread, tests/test_model.py:353-364). */
+static int g_f64 = 0;
+void orc_set_f64(int on) { g_f64 = on; }
+
+static void matmul_range_f64(const mm_ctx *x, int r0, int r1);
+
 static void matmul_range(void *c, int r0, int r1) {
     const mm_ctx *x = (const mm_ctx *)c;
+    if (g_f64) {
+        matmul_range_f64(x, r0, r1);
+        return;
+    }
     const weight_t *w = x->w;
     const float *xf = x->xf;
     const q8k_block *xq = x->xq;
@@ -457,6 +469,56 @@ static void matmul_range(void *c, int r0, int r1) {
                 }
             }
             out[(size_t)t * w->n + r] = acc;
+        }
+    }
+}
+
+
+/* The same rows with every product and sum in double; weights and Q8_K
+ * activations enter exactly as in the float path. */
+static void matmul_range_f64(const mm_ctx *x, int r0, int r1) {
+    const weight_t *w = x->w;
+    const int nt = x->nt, nb = w->k / QK_K;
+    for (int r = r0; r < r1; r++) {
+        const uint8_t *row = w->data ? w->data + (size_t)r * w->row_bytes : NULL;
+        for (int t = 0; t < nt; t++) {
+            double acc = 0.0;
+            const q8k_block *y = x->xq + (size_t)t * nb;
+            const float *xf = x->xf + (size_t)t * w->k;
+            if (w->pk) {
+                for (int b = 0; b < nb; b++)
+                    acc += (double)w->ps[(size_t)r * nb + b] * (double)y[b].d *
+                           (double)panel_block_int(w->pk + ((size_t)r * nb + b) * 64, y + b, w->pshift, w->poff);
+            } else if (w->type == GT_Q4_K) {
+                for (int b = 0; b < nb; b++) {
+                    int32_t si, sm;
+                    q4k_block_ints(row + (size_t)b * 144, y + b, &si, &sm);
+                    acc += (double)y[b].d * ((double)orc_f16_to_f32(rd16(row + (size_t)b * 144)) * si -
+                                             (double)orc_f16_to_f32(rd16(row + (size_t)b * 144 + 2)) * sm);
+                }
+            } else if (w->type == GT_Q6_K) {
+                for (int b = 0; b < nb; b++)
+                    acc += (double)orc_f16_to_f32(rd16(row + (size_t)b * 210 + 208)) * (double)y[b].d *
+                           (double)q6k_block_int(row + (size_t)b * 210, y + b);
+            } else if (w->type == GT_Q2_0C) {
+                for (int b = 0; b < nb / 2; b++) {
+                    const uint8_t *blk = row + (size_t)b * 130;
+                    double part = 0.0;
+                    for (int h = 0; h < 2; h++) part += (double)q2c_half_int(blk, h, y + 2 * b + h) * (double)y[2 * b + h].d;
+                    acc += (double)orc_f16_to_f32(rd16(blk)) * part;
+                }
+            } else {
+                float *deq = (float *)malloc(sizeof(float) * (size_t)w->k);
+                orc_dequant_row(w, r, deq);
+                if (w->type == GT_STQ1_0) {
+                    for (int j = 0; j < w->k; j++)
+                        acc += (double)deq[j] * (double)y[j / QK_K].qs[j % QK_K] * (double)y[j / QK_K].d;
+                } else {
+                    for (int j = 0; j < w->k; j++) acc += (double)deq[j] * (double)xf[j];
+                }
+                free(deq);
+            }
+            x->out[(size_t)t * w->n + r] = (float)acc;
         }
     }
 }
@@ -613,20 +675,6 @@ static void rmsnorm(const float *x, const float *w, float *y, int dim, float eps
     for (int i = 0; i < dim; i++) y[i] = x[i] * scale * w[i];
 }
 
-/* NeoX rotation of each head's halves (src/model.c:754-765). */
-static void rope(const orc_model *m, float *x, int heads, int pos) {
-    const int half = m->d.rope_half;
-    const float *c = m->rope_cos + (size_t)pos * half, *s = m->rope_sin + (size_t)pos * half;
-    for (int h = 0; h < heads; h++) {
-        float *row = x + (size_t)h * m->d.hdim;
-        for (int i = 0; i < half; i++) {
-            const float a = row[i], b = row[i + half];
-            row[i] = a * c[i] - b * s[i];
-            row[i + half] = a * s[i] + b * c[i];
-        }
-    }
-}
-
 /* bf16 dot with four interleaved partial sums (src/kernels.c:1111-1121). */
 static float dot_bf16(const float *q, const uint16_t *k, int n) {
     float a[4] = {0, 0, 0, 0};
@@ -639,47 +687,108 @@ static float dot_bf16(const float *q, const uint16_t *k, int n) {
 }
 
 typedef struct {
-    orc_model *m;
-    int li, pos0;
+    int heads, kv_heads, hd, pos0;
+    const float *q;
+    const uint16_t *kc, *vc;
+    float *ao;
 } attn_ctx;
 
 static void attn_range(void *c, int i0, int i1) {
     const attn_ctx *a = (const attn_ctx *)c;
-    orc_model *m = a->m;
-    const orc_model_desc *D = &m->d;
-    const int li = a->li, pos0 = a->pos0, QD = m->qdim, KD = m->kvdim, HD = D->hdim;
-    const int group = D->heads / D->kv_heads;
+    const int QD = a->heads * a->hd, KD = a->kv_heads * a->hd, HD = a->hd;
+    const int group = a->heads / a->kv_heads;
     const float scale = 1.0f / sqrtf((float)HD);
     for (int item = i0; item < i1; item++) {
-            const int t = item / D->heads, h = item % D->heads, n = pos0 + t + 1, kvh = h / group;
-            const float *qh = m->q + (size_t)t * QD + (size_t)h * HD;
-            const uint16_t *K = m->kc[li] + (size_t)kvh * HD, *V = m->vc[li] + (size_t)kvh * HD;
-            float *sc = (float *)malloc(sizeof(float) * (size_t)n);
-            float mx = -INFINITY;
-            for (int j = 0; j < n; j++) {
-                sc[j] = dot_bf16(qh, K + (size_t)j * KD, HD) * scale;
-                if (sc[j] > mx) mx = sc[j];
-            }
-            float sum = 0.f;
-            for (int j = 0; j < n; j++) {
-                sc[j] = expf(sc[j] - mx);
-                sum += sc[j];
-            }
-            const float inv = 1.0f / sum;
-            float *o = m->ao + (size_t)t * QD + (size_t)h * HD;
-            for (int d = 0; d < HD; d++) o[d] = 0.f;
-            for (int j = 0; j < n; j++) {
-                const float p = sc[j] * inv;
-                const uint16_t *vr = V + (size_t)j * KD;
-                for (int d = 0; d < HD; d++) o[d] += p * orc_bf16_to_f32(vr[d]);
-            }
-            free(sc);
+        const int t = item / a->heads, h = item % a->heads, n = a->pos0 + t + 1, kvh = h / group;
+        const float *qh = a->q + (size_t)t * QD + (size_t)h * HD;
+        const uint16_t *K = a->kc + (size_t)kvh * HD, *V = a->vc + (size_t)kvh * HD;
+        float *sc = (float *)malloc(sizeof(float) * (size_t)n);
+        float mx = -INFINITY;
+        for (int j = 0; j < n; j++) {
+            sc[j] = dot_bf16(qh, K + (size_t)j * KD, HD) * scale;
+            if (sc[j] > mx) mx = sc[j];
         }
+        float sum = 0.f;
+        for (int j = 0; j < n; j++) {
+            sc[j] = expf(sc[j] - mx);
+            sum += sc[j];
+        }
+        const float inv = 1.0f / sum;
+        float *o = a->ao + (size_t)t * QD + (size_t)h * HD;
+        for (int d = 0; d < HD; d++) o[d] = 0.f;
+        for (int j = 0; j < n; j++) {
+            const float p = sc[j] * inv;
+            const uint16_t *vr = V + (size_t)j * KD;
+            for (int d = 0; d < HD; d++) o[d] += p * orc_bf16_to_f32(vr[d]);
+        }
+        free(sc);
+    }
+}
+
+/* Rope (NeoX halves, src/model.c:754-765) + per-head q/k RMSNorm + bf16 KV
+ * store for tokens pos0.., then causal
+ * GQA softmax attention (src/model.c:836-851 and :768-795).  q, k are
+ * modified in place; kc/vc are one layer's [ctx][kvdim] caches. */
+void orc_attention(int heads, int kv_heads, int hd, int rope_half, float *q, float *k, const float *v, int nt,
+                   int pos0, uint16_t *kc, uint16_t *vc, const float *q_norm, const float *k_norm,
+                   const float *rope_cos, const float *rope_sin, float eps, float *ao) {
+    const int QD = heads * hd, KD = kv_heads * hd;
+    for (int t = 0; t < nt; t++) {
+        float *qt = q + (size_t)t * QD, *kt = k + (size_t)t * KD;
+        const float *vt = v + (size_t)t * KD;
+        const int pos = pos0 + t;
+        const float *cs = rope_cos + (size_t)pos * rope_half, *sn = rope_sin + (size_t)pos * rope_half;
+        for (int pass = 0; pass < 2; pass++) {
+            float *x = pass ? kt : qt;
+            const int nh = pass ? kv_heads : heads;
+            for (int h = 0; h < nh; h++) {
+                float *row = x + (size_t)h * hd;
+                for (int i = 0; i < rope_half; i++) {
+                    const float a = row[i], b = row[i + rope_half];
+                    row[i] = a * cs[i] - b * sn[i];
+                    row[i + rope_half] = a * sn[i] + b * cs[i];
+                }
+            }
+        }
+        for (int h = 0; h < heads; h++) rmsnorm(qt + h * hd, q_norm, qt + h * hd, hd, eps);
+        for (int h = 0; h < kv_heads; h++) rmsnorm(kt + h * hd, k_norm, kt + h * hd, hd, eps);
+        uint16_t *kd = kc + (size_t)pos * KD, *vd = vc + (size_t)pos * KD;
+        for (int i = 0; i < KD; i++) {
+            kd[i] = orc_f32_to_bf16(kt[i]);
+            vd[i] = orc_f32_to_bf16(vt[i]);
+        }
+    }
+    attn_ctx ac = {heads, kv_heads, hd, pos0, q, kc, vc, ao};
+    par_for(nt * heads, attn_range, &ac);
+}
+
+/* The GEMV prologues: rmsnorm(x)*w (mode 2) or silu(x)*x2 (mode 3) per token,
+ * then the matmul as the host runs it (src/model.c:824-881). */
+void orc_prologue_matmul(const weight_t *w, int mode, const float *x, const float *x2, const float *norm_w, float eps,
+                         int nt, float *out) {
+    const int K = w->k;
+    float *act = (float *)malloc(sizeof(float) * (size_t)nt * K);
+    for (int t = 0; t < nt; t++) {
+        const float *xt = x + (size_t)t * K;
+        float *at = act + (size_t)t * K;
+        if (mode == 2) rmsnorm(xt, norm_w, at, K, eps);
+        else if (mode == 3)
+            for (int i = 0; i < K; i++) {
+                const float g = xt[i];
+                at[i] = g / (1.0f + expf(-g)) * x2[(size_t)t * K + i];
+            }
+        else memcpy(at, xt, sizeof(float) * (size_t)K);
+    }
+    q8k_block *xq = (q8k_block *)aligned_alloc(64, sizeof(q8k_block) * (size_t)nt * (K / QK_K + 1));
+    if (K % QK_K == 0) orc_quantize_rows(act, nt, K, xq);
+    orc_matmul(w, act, xq, nt, out);
+    free(xq);
+    free(act);
 }
 
 void orc_forward(orc_model *m, const int *toks, int nt, int pos0, float *logits, float *h_out) {
     const orc_model_desc *D = &m->d;
-    const int H = D->hidden, QD = m->qdim, KD = m->kvdim, F = D->ffn, HD = D->hdim;
+    const int H = D->hidden, QD = m->qdim, F = D->ffn, HD = D->hdim;
     /* embedding (src/model.c:802) */
     for (int t = 0; t < nt; t++) orc_dequant_row(&D->embd, toks[t], m->h + (size_t)t * H);
     for (int li = 0; li < D->n_layer; li++) {
@@ -689,21 +798,8 @@ void orc_forward(orc_model *m, const int *toks, int nt, int pos0, float *logits,
         orc_matmul(&D->wq[li], m->xn, m->xq, nt, m->q);
         orc_matmul(&D->wk[li], m->xn, m->xq, nt, m->k);
         orc_matmul(&D->wv[li], m->xn, m->xq, nt, m->v);
-        for (int t = 0; t < nt; t++) {
-            float *q = m->q + (size_t)t * QD, *k = m->k + (size_t)t * KD, *v = m->v + (size_t)t * KD;
-            rope(m, q, D->heads, pos0 + t);
-            rope(m, k, D->kv_heads, pos0 + t);
-            for (int h = 0; h < D->heads; h++) rmsnorm(q + h * HD, D->q_norm[li], q + h * HD, HD, D->eps);
-            for (int h = 0; h < D->kv_heads; h++) rmsnorm(k + h * HD, D->k_norm[li], k + h * HD, HD, D->eps);
-            uint16_t *kd = m->kc[li] + (size_t)(pos0 + t) * KD, *vd = m->vc[li] + (size_t)(pos0 + t) * KD;
-            for (int i = 0; i < KD; i++) {
-                kd[i] = orc_f32_to_bf16(k[i]);
-                vd[i] = orc_f32_to_bf16(v[i]);
-            }
-        }
-        /* causal GQA softmax attention over the bf16 cache (src/model.c:768-795) */
-        attn_ctx ac = {m, li, pos0};
-        par_for(nt * D->heads, attn_range, &ac);
+        orc_attention(D->heads, D->kv_heads, HD, D->rope_half, m->q, m->k, m->v, nt, pos0, m->kc[li], m->vc[li],
+                      D->q_norm[li], D->k_norm[li], m->rope_cos, m->rope_sin, D->eps, m->ao);
         orc_quantize_rows(m->ao, nt, QD, m->xq);
         orc_matmul(&D->wo[li], m->ao, m->xq, nt, m->tmp);
         for (size_t i = 0; i < (size_t)nt * H; i++) m->h[i] += m->tmp[i];

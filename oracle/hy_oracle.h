@@ -61,7 +61,16 @@ int orc_vocab_out(const orc_model *m);
 const uint16_t *orc_kcache(const orc_model *m, int layer);
 const uint16_t *orc_vcache(const orc_model *m, int layer);
 
+void orc_attention(int heads, int kv_heads, int hd, int rope_half, float *q, float *k, const float *v, int nt,
+                   int pos0, uint16_t *kc, uint16_t *vc, const float *q_norm, const float *k_norm,
+                   const float *rope_cos, const float *rope_sin, float eps, float *ao);
+void orc_prologue_matmul(const weight_t *w, int mode, const float *x, const float *x2, const float *norm_w, float eps,
+                         int nt, float *out);
+
 void orc_set_threads(int n);
+/* 1: orc_matmul accumulates in double (float64 reference for the rounding
+ * spread); 0: the host's float order (default). */
+void orc_set_f64(int on);
 
 #ifdef __cplusplus
 }

@@ -60,6 +60,35 @@ class Oracle:
         L.orc_vcache.argtypes = [P, I]
         L.orc_vcache.restype = P
         L.orc_set_threads.argtypes = [I]
+        L.orc_set_f64.argtypes = [I]
+        L.orc_attention.argtypes = [I, I, I, I, P, P, P, I, I, P, P, P, P, P, P, F, P]
+        L.orc_prologue_matmul.argtypes = [W, I, P, P, P, F, I, P]
+
+    def prologue_matmul(self, w, mode: int, x, x2=None, norm_w=None, eps: float = 1e-5) -> np.ndarray:
+        """rmsnorm(x)*w (mode 2) / silu(x)*x2 (mode 3) / x (mode 1), then matmul."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        nt = x.shape[0]
+        out = np.zeros((nt, w.n), dtype=np.float32)
+        x2p = None if x2 is None else np.ascontiguousarray(x2, dtype=np.float32)
+        nwp = None if norm_w is None else np.ascontiguousarray(norm_w, dtype=np.float32)
+        self.lib.orc_prologue_matmul(C.byref(w), mode, x.ctypes.data, None if x2p is None else x2p.ctypes.data,
+                                     None if nwp is None else nwp.ctypes.data, eps, nt, out.ctypes.data)
+        return out
+
+    def attention(self, heads, kv_heads, hd, qkv, pos0, kc, vc, q_norm, k_norm, cos, sin, eps=1e-5):
+        """Rope + q/k norm + bf16 KV store + causal attention for qkv [nt][q|k|v];
+        kc/vc [ctx][kvdim] updated in place.  Returns ao [nt][qdim]."""
+        qkv = np.ascontiguousarray(qkv, dtype=np.float32)
+        nt = qkv.shape[0]
+        qd, kvd = heads * hd, kv_heads * hd
+        q = np.ascontiguousarray(qkv[:, :qd])
+        k = np.ascontiguousarray(qkv[:, qd:qd + kvd])
+        v = np.ascontiguousarray(qkv[:, qd + kvd:])
+        ao = np.zeros((nt, qd), dtype=np.float32)
+        self.lib.orc_attention(heads, kv_heads, hd, hd // 2, q.ctypes.data, k.ctypes.data, v.ctypes.data, nt, pos0,
+                               kc.ctypes.data, vc.ctypes.data, q_norm.ctypes.data, k_norm.ctypes.data,
+                               cos.ctypes.data, sin.ctypes.data, eps, ao.ctypes.data)
+        return ao
 
     def quantize(self, x: np.ndarray) -> np.ndarray:
         x = np.ascontiguousarray(x, dtype=np.float32)
@@ -176,6 +205,28 @@ class OracleModel:
         self.orc.lib.orc_forward(self.m, t.ctypes.data, len(t), pos0, lg.ctypes.data if logits else None,
                                  h.ctypes.data)
         return h, lg
+
+    def logits_spread(self, ids, chunk: int = 16):
+        """(float32 logits, spread, tol) after the prompt: spread is the
+        reference's own fp32-vs-fp64 deviation max|l64-l32|/max|l64|
+        (tests/test_model.py:353-364), tol = max(1e-5, 3*spread)."""
+        ids = list(ids)
+        self.reset()
+        self.orc.lib.orc_set_f64(1)
+        try:
+            l64 = self._prefill_logits(ids, chunk)
+        finally:
+            self.orc.lib.orc_set_f64(0)
+        self.reset()
+        l32 = self._prefill_logits(ids, chunk)
+        spread = float(np.abs(l64 - l32).max() / np.abs(l64).max())
+        return l32, spread, max(1e-5, 3 * spread)
+
+    def _prefill_logits(self, ids, chunk):
+        lg = None
+        for i in range(0, len(ids), chunk):
+            _, lg = self.forward(ids[i:i + chunk], i, logits=i + chunk >= len(ids))
+        return lg
 
     def greedy(self, ids, ngen: int, chunk: int = 16, step_logits: bool = False):
         t = np.asarray(ids, dtype=np.int32)

@@ -47,12 +47,19 @@ def synth():
     return S
 
 
-@pytest.fixture(scope="session")
+_BACKEND = []
+
+
+@pytest.fixture
 def backend():
+    """One backend handle per session, replaced if a test left it broken
+    (a failed launch marks a handle unusable, as the host contract requires)."""
     from hymt2_b200.device import Backend
-    be = Backend(0)
-    yield be
-    be.close()
+    if _BACKEND and _BACKEND[0].error():
+        _BACKEND.pop().close()
+    if not _BACKEND:
+        _BACKEND.append(Backend(0))
+    return _BACKEND[0]
 
 
 def rand_blocks(rng, gtype: int, rows: int, k: int) -> np.ndarray:

@@ -126,8 +126,11 @@ def test_decode_host_io_path_same_ids(backend, tiny_models):
 
 @pytest.mark.slow
 def test_bench_model_greedy_full_size(backend, oracle, synth, model_dir):
-    """Config 0 (reference bench GGUF, 32 layers): 48-token prompt, greedy
-    ids vs the oracle; identical up to the first near-tie step."""
+    """Config 0 (reference bench GGUF, 32 layers): 48-token prompt.  Logits
+    within tol = max(1e-5, 3*spread), spread = the oracle's fp64-vs-fp32
+    deviation on the same prompt (the reference's rule, measured with the C
+    oracle because the numpy model does not fit a 1.8B model in the test
+    budget); greedy ids identical up to the first near-tie step."""
     import oracle as O
     from hymt2_b200.device import DeviceModel
     path = synth.ensure("c0_stq", model_dir)
@@ -140,13 +143,15 @@ def test_bench_model_greedy_full_size(backend, oracle, synth, model_dir):
         dm.close()
     om = O.OracleModel(oracle, path, ctx=1024)
     try:
+        l32, spread, tol = om.logits_spread(ids)
         want, steps = om.greedy(ids, 16, chunk=16, step_logits=True)
     finally:
         om.close()
-    rel = _rel(lg_d, steps[0])
-    assert rel < 1e-3, rel
+    rel = _rel(lg_d, l32)
+    print(f"full-size logits rel {rel:.3e}, oracle spread {spread:.3e}, tol {tol:.3e}")
+    assert rel <= tol, (rel, spread, tol)
     d = _first_divergence(got, want)
-    assert d is None or _near_tie(steps[d], 1e-3), (got, want)
+    assert d is None or _near_tie(steps[d], tol), (got, want)
 
 
 @pytest.mark.skipif(not os.path.exists(os.path.join(os.path.dirname(__file__), "..", "oracle", "_ref",
