@@ -88,6 +88,8 @@ SIGNATURES = {
     "hyc_gemv_test": (I, [P, P, I, P, P, P, F, I, I, P]),
     "hyc_debug_buffer": (I, [P, I, P, Z]),
     "hyc_gemv_multi_test": (I, [P, P, I, I, P, P, F, I, P]),
+    "hyc_trace": (I, [P, I]),
+    "hyc_trace_read": (I, [P, P, I]),
     "hyc_attention_test": (I, [P, I, I, I, I, I, I, F, P, P, P, P, P, P, P, P]),
 }
 

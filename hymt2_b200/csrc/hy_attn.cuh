@@ -25,6 +25,7 @@ struct AttnArgs {
     float *part;            // decode split partials [kv_heads][max_splits][G][HD+2]
     int *tickets;           // [kv_heads], zero between launches
     int split_len, max_splits;
+    int trace;              // timeline slot (< 0: off)
 };
 
 // NeoX rotation + per-head RMSNorm of one head held as v[i] = x[lane + 32 i].
@@ -55,6 +56,7 @@ __device__ __forceinline__ void rope_norm_warp(float (&v)[HD / 32], const float 
 // store every k head, bf16 store every v head.  grid (nt), one warp per head.
 template <int HD>
 __global__ void rope_norm_store(const __grid_constant__ AttnArgs a) {
+    pdl_trigger();
     pdl_wait();
     const int t = blockIdx.x, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = *a.pos_ptr + t;
@@ -81,7 +83,6 @@ __global__ void rope_norm_store(const __grid_constant__ AttnArgs a) {
             }
         }
     }
-    pdl_trigger();
 }
 
 // Core loop shared by decode and prefill: keys [j0, j1) for the G heads of
@@ -195,46 +196,91 @@ __device__ __forceinline__ void merge_warps(AttnSmem<HD, G> &S, float &M, float 
     }
 }
 
-// Decode: one query token at *pos_ptr.  grid (kv_heads, max_splits), G warps.
-// Prologue (each CTA): rope+norm of its G q heads and of k, bf16 k/v; split 0
-// stores k/v into the cache.  Splits beyond the live context exit at once.
+// Decode v2: one query token at *pos_ptr; grid (kv_heads, splits of kDecSplit
+// keys), G warps, warp w = query head kvh*G + w.  The split's cached K/V rows
+// (positions < pos, written by earlier decode steps, i.e. at least two
+// kernels back) are copied to shared memory with cp.async BEFORE
+// griddepcontrol.wait; the current position comes from this kernel's own
+// rope/norm prologue.  K rows are stored with their 16-byte chunks rotated by
+// the row index so lanes reading 32 different rows hit different banks.
+constexpr int kDecSplit = 128;
+
+template <int HD>
+__host__ __device__ inline size_t attn_dec_smem() { return (size_t)2 * kDecSplit * HD * 2; }
+
 template <int HD, int G>
-__global__ void __launch_bounds__(G * 32) attn_decode(const __grid_constant__ AttnArgs a) {
-    __shared__ AttnSmem<HD, G> S;
+__global__ void __launch_bounds__((G + 1) * 32) attn_decode2(const __grid_constant__ AttnArgs a) {
+    extern __shared__ __align__(16) uint8_t dsm[];
+    uint16_t *sK = (uint16_t *)dsm;                       // [kDecSplit][HD] rotated chunks
+    uint16_t *sV = sK + (size_t)kDecSplit * HD;           // [kDecSplit][HD]
+    __shared__ __align__(16) float sq[G][HD];
+    __shared__ __align__(16) float skc[HD], svc[HD];
+    __shared__ int last;
+    constexpr int CH = HD / 8;                            // 16-byte chunks per row
+    constexpr int DPL = HD / 32;                          // output dims per lane (contiguous)
+    trace_mark(a.trace, 0);
+    pdl_trigger();
     const int kvh = blockIdx.x, split = blockIdx.y;
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    pdl_wait();
-    const int pos = *a.pos_ptr, n = pos + 1;
-    const int j0 = split * a.split_len;
-    // a position outside the cache (decode driven past ctx) writes nothing
-    if (j0 >= n || pos < 0 || pos >= a.ctx) {
-        pdl_trigger();
-        return;
+    const int pos = *a.pos_ptr;  // written before this graph / >= 2 kernels back
+    const int j0 = split * kDecSplit;
+    if (pos < 0 || pos >= a.ctx || j0 > pos) return;
+    const int j1 = min(pos + 1, j0 + kDecSplit);
+    const int ncache = min(j1, pos) - j0;  // rows already in the cache
+    const uint16_t *Kg = a.kc + kvh * HD, *Vg = a.vc + kvh * HD;
+    for (int idx = threadIdx.x; idx < ncache * CH; idx += blockDim.x) {
+        const int j = idx / CH, c = idx - j * CH;
+        const size_t g = (size_t)(j0 + j) * a.kvdim + c * 8;
+        const unsigned dk = (unsigned)__cvta_generic_to_shared(sK + (size_t)j * HD + ((c + j) % CH) * 8);
+        const unsigned dv = (unsigned)__cvta_generic_to_shared(sV + (size_t)j * HD + c * 8);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk), "l"(Kg + g) : "memory");
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dv), "l"(Vg + g) : "memory");
     }
-    const int j1 = min(n, j0 + a.split_len);
-    const int nsplit = (n + a.split_len - 1) / a.split_len;
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    // constants of this position: rope row and the per-head norm weights
     const float *cs = a.rope_cos + (size_t)pos * a.half, *sn = a.rope_sin + (size_t)pos * a.half;
+    float rc[HD / 64], rs[HD / 64], nq[HD / 32];
+#pragma unroll
+    for (int i = 0; i < HD / 64; i++) {
+        rc[i] = __ldg(cs + lane + 32 * i);
+        rs[i] = __ldg(sn + lane + 32 * i);
+    }
+    const float *nrm = w < G ? a.q_norm : a.k_norm;
+#pragma unroll
+    for (int i = 0; i < HD / 32; i++) nq[i] = __ldg(nrm + lane + 32 * i);
+    pdl_wait();
+    trace_mark(a.trace, 1);
     {
-        const int h = kvh * G + w;
+        // warps 0..G-1: the G query heads; warp G: this KV head's k and v
         float v[HD / 32];
+        const float *src = w < G ? a.qkv + (kvh * G + w) * HD : a.qkv + a.qdim + kvh * HD;
 #pragma unroll
-        for (int i = 0; i < HD / 32; i++) v[i] = a.qkv[h * HD + lane + 32 * i];
-        rope_norm_warp<HD>(v, cs, sn, a.q_norm, a.eps);
+        for (int i = 0; i < HD / 32; i++) v[i] = src[lane + 32 * i];
 #pragma unroll
-        for (int i = 0; i < HD / 32; i++) S.sq[w][lane + 32 * i] = v[i];
-        if (w == 0) {
-            float kv[HD / 32];
-            const float *kr = a.qkv + a.qdim + kvh * HD, *vr = a.qkv + a.qdim + a.kvdim + kvh * HD;
+        for (int i = 0; i < HD / 64; i++) {
+            const float x0 = v[i], x1 = v[i + HD / 64];
+            v[i] = __fsub_rn(__fmul_rn(x0, rc[i]), __fmul_rn(x1, rs[i]));
+            v[i + HD / 64] = __fadd_rn(__fmul_rn(x0, rs[i]), __fmul_rn(x1, rc[i]));
+        }
+        float ssq = 0.f;
 #pragma unroll
-            for (int i = 0; i < HD / 32; i++) kv[i] = kr[lane + 32 * i];
-            rope_norm_warp<HD>(kv, cs, sn, a.k_norm, a.eps);
+        for (int i = 0; i < HD / 32; i++) ssq = __fadd_rn(ssq, __fmul_rn(v[i], v[i]));
+        ssq = warp_sum(ssq);
+        const float scale = 1.0f / sqrtf(ssq / (float)HD + a.eps);
+#pragma unroll
+        for (int i = 0; i < HD / 32; i++) v[i] = __fmul_rn(__fmul_rn(v[i], scale), nq[i]);
+        if (w < G) {
+#pragma unroll
+            for (int i = 0; i < HD / 32; i++) sq[w][lane + 32 * i] = v[i];
+        } else {
+            const float *vr = a.qkv + a.qdim + a.kvdim + kvh * HD;
             uint16_t *kd = a.kc + (size_t)pos * a.kvdim + kvh * HD, *vd = a.vc + (size_t)pos * a.kvdim + kvh * HD;
 #pragma unroll
             for (int i = 0; i < HD / 32; i++) {
                 const int e = lane + 32 * i;
-                const uint16_t kb = f32_to_bf16_bits(kv[i]), vb = f32_to_bf16_bits(vr[e]);
-                S.sk[e] = bf16_bits_to_f32(kb);
-                S.sv[e] = bf16_bits_to_f32(vb);
+                const uint16_t kb = f32_to_bf16_bits(v[i]), vb = f32_to_bf16_bits(vr[e]);
+                skc[e] = bf16_bits_to_f32(kb);
+                svc[e] = bf16_bits_to_f32(vb);
                 if (split == 0) {
                     kd[e] = kb;
                     vd[e] = vb;
@@ -242,58 +288,153 @@ __global__ void __launch_bounds__(G * 32) attn_decode(const __grid_constant__ At
             }
         }
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
-    pdl_trigger();
-    float m[G], l[G], o[G][HD / 32];
-    attend_range<HD, G>(a, kvh, j0, j1, pos, S.sq, S.sk, S.sv, m, l, o);
-#pragma unroll
-    for (int h = 0; h < G; h++) {
-        if (lane == 0) {
-            S.pm[w][h] = m[h];
-            S.pl[w][h] = l[h];
-        }
-#pragma unroll
-        for (int i = 0; i < HD / 32; i++) S.po[w][h][lane + 32 * i] = o[h][i];
+    trace_mark(a.trace, 2);
+    if (w == G) {  // the k/v warp has no head of its own
+        trace_mark(a.trace, 3);
+        return;
     }
-    __syncthreads();
-    float M, L, O[HD / 32];
-    merge_warps<HD, G>(S, M, L, O);
-    const int h = kvh * G + w;
-    if (nsplit == 1) {
-        const float inv = 1.0f / L;
+    // scores: warp w = head, lane handles keys j0 + lane + 32 i; each 8-dim q
+    // chunk is read once and applied to all of the lane's keys
+    constexpr int KPL = kDecSplit / 32;
+    float acc[KPL];
 #pragma unroll
-        for (int i = 0; i < HD / 32; i++) a.ao[h * HD + lane + 32 * i] = O[i] * inv;
+    for (int i = 0; i < KPL; i++) acc[i] = 0.f;
+    const int nk = j1 - j0;
+#pragma unroll 2
+    for (int c = 0; c < CH; c++) {
+        const float4 qa = *(const float4 *)&sq[w][c * 8], qb = *(const float4 *)&sq[w][c * 8 + 4];
+        const float qf[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
+#pragma unroll
+        for (int i = 0; i < KPL; i++) {
+            const int j = lane + 32 * i;
+            if (32 * i >= nk) break;
+            if (j < nk && j0 + j != pos) {
+                const uint4 kk = *(const uint4 *)(sK + (size_t)j * HD + ((c + j) % CH) * 8);
+                const uint32_t kw[4] = {kk.x, kk.y, kk.z, kk.w};
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    acc[i] = fmaf(qf[2 * q], bf16_bits_to_f32(kw[q] & 0xffffu), acc[i]);
+                    acc[i] = fmaf(qf[2 * q + 1], bf16_bits_to_f32(kw[q] >> 16), acc[i]);
+                }
+            }
+        }
+    }
+    float sc[KPL];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < KPL; i++) {
+        const int j = lane + 32 * i;
+        float s = -INFINITY;
+        if (j < nk) {
+            float dot = acc[i];
+            if (j0 + j == pos) {
+                dot = 0.f;
+#pragma unroll 8
+                for (int d = 0; d < HD; d++) dot = fmaf(sq[w][d], skc[d], dot);
+            }
+            s = dot * a.scale;
+        }
+        sc[i] = s;
+        mx = fmaxf(mx, s);
+    }
+    mx = warp_max(mx);
+    float l = 0.f;
+#pragma unroll
+    for (int i = 0; i < KPL; i++) {
+        sc[i] = (lane + 32 * i < nk) ? expf(sc[i] - mx) : 0.f;
+        l += sc[i];
+    }
+    l = warp_sum(l);
+    // o[d], d = lane*DPL + q: sum_j p_j v_j, four keys per step
+    float o[DPL];
+#pragma unroll
+    for (int q = 0; q < DPL; q++) o[q] = 0.f;
+#pragma unroll
+    for (int i = 0; i < KPL; i++) {
+        const int base = 32 * i;
+        if (base >= nk) break;
+        const int lim = min(32, nk - base);
+        int jj = 0;
+        for (; jj + 4 <= lim; jj += 4) {
+            float p[4], vv[4][DPL];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                p[u] = __shfl_sync(0xffffffffu, sc[i], jj + u);
+                const int jg = j0 + base + jj + u;
+                if (jg == pos) {
+#pragma unroll
+                    for (int q = 0; q < DPL; q++) vv[u][q] = svc[lane * DPL + q];
+                } else {
+                    const uint16_t *vr = sV + (size_t)(base + jj + u) * HD + lane * DPL;
+                    if (DPL == 4) {
+                        const uint2 x = *(const uint2 *)vr;
+                        vv[u][0] = bf16_bits_to_f32(x.x & 0xffffu);
+                        vv[u][1] = bf16_bits_to_f32(x.x >> 16);
+                        vv[u][2] = bf16_bits_to_f32(x.y & 0xffffu);
+                        vv[u][3] = bf16_bits_to_f32(x.y >> 16);
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < DPL; q++) vv[u][q] = bf16_bits_to_f32(vr[q]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+#pragma unroll
+                for (int q = 0; q < DPL; q++) o[q] = fmaf(p[u], vv[u][q], o[q]);
+        }
+        for (; jj < lim; jj++) {
+            const float p = __shfl_sync(0xffffffffu, sc[i], jj);
+            const int jg = j0 + base + jj;
+#pragma unroll
+            for (int q = 0; q < DPL; q++) {
+                const float vq = jg == pos ? svc[lane * DPL + q] : bf16_bits_to_f32(sV[(size_t)(base + jj) * HD + lane * DPL + q]);
+                o[q] = fmaf(p, vq, o[q]);
+            }
+        }
+    }
+    const int h = kvh * G + w;
+    const int nsplit = (pos + kDecSplit) / kDecSplit;
+    if (nsplit == 1) {
+        const float inv = 1.0f / l;
+#pragma unroll
+        for (int q = 0; q < DPL; q++) a.ao[h * HD + lane * DPL + q] = o[q] * inv;
+        trace_mark(a.trace, 3);
         return;
     }
     float *pp = a.part + (((size_t)kvh * a.max_splits + split) * G + w) * (HD + 2);
 #pragma unroll
-    for (int i = 0; i < HD / 32; i++) pp[2 + lane + 32 * i] = O[i];
+    for (int q = 0; q < DPL; q++) pp[2 + lane * DPL + q] = o[q];
     if (lane == 0) {
-        pp[0] = M;
-        pp[1] = L;
+        pp[0] = mx;
+        pp[1] = l;
     }
     __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) S.last = atomicAdd(&a.tickets[kvh], 1) == nsplit - 1;
-    __syncthreads();
-    if (!S.last) return;
+    // the k/v warp has exited: synchronise the G head warps only (named barrier 1)
+    asm volatile("bar.sync 1, %0;" ::"r"(G * 32) : "memory");
+    if (threadIdx.x == 0) last = atomicAdd(&a.tickets[kvh], 1) == nsplit - 1;
+    asm volatile("bar.sync 1, %0;" ::"r"(G * 32) : "memory");
+    trace_mark(a.trace, 3);
+    if (!last) return;
     __threadfence();
     float MM = -INFINITY;
     for (int sp = 0; sp < nsplit; sp++)
         MM = fmaxf(MM, __ldcg(a.part + (((size_t)kvh * a.max_splits + sp) * G + w) * (HD + 2)));
-    float LL = 0.f, OO[HD / 32];
+    float LL = 0.f, OO[DPL];
 #pragma unroll
-    for (int i = 0; i < HD / 32; i++) OO[i] = 0.f;
+    for (int q = 0; q < DPL; q++) OO[q] = 0.f;
     for (int sp = 0; sp < nsplit; sp++) {
-        const float *q = a.part + (((size_t)kvh * a.max_splits + sp) * G + w) * (HD + 2);
-        const float f = expf(__ldcg(q) - MM);
-        LL = fmaf(__ldcg(q + 1), f, LL);
+        const float *pq = a.part + (((size_t)kvh * a.max_splits + sp) * G + w) * (HD + 2);
+        const float f = expf(__ldcg(pq) - MM);
+        LL = fmaf(__ldcg(pq + 1), f, LL);
 #pragma unroll
-        for (int i = 0; i < HD / 32; i++) OO[i] = fmaf(__ldcg(q + 2 + lane + 32 * i), f, OO[i]);
+        for (int q = 0; q < DPL; q++) OO[q] = fmaf(__ldcg(pq + 2 + lane * DPL + q), f, OO[q]);
     }
     const float inv = 1.0f / LL;
 #pragma unroll
-    for (int i = 0; i < HD / 32; i++) a.ao[h * HD + lane + 32 * i] = OO[i] * inv;
+    for (int q = 0; q < DPL; q++) a.ao[h * HD + lane * DPL + q] = OO[q] * inv;
     if (threadIdx.x == 0) a.tickets[kvh] = 0;
 }
 
@@ -302,6 +443,7 @@ __global__ void __launch_bounds__(G * 32) attn_decode(const __grid_constant__ At
 // grid (kv_heads, nt), G warps.
 template <int HD, int G>
 __global__ void __launch_bounds__(G * 32) attn_prefill(const __grid_constant__ AttnArgs a) {
+    pdl_trigger();
     __shared__ AttnSmem<HD, G> S;
     const int kvh = blockIdx.x, t = blockIdx.y;
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -311,7 +453,6 @@ __global__ void __launch_bounds__(G * 32) attn_prefill(const __grid_constant__ A
 #pragma unroll
     for (int i = 0; i < HD / 32; i++) S.sq[w][lane + 32 * i] = qr[lane + 32 * i];
     __syncthreads();
-    pdl_trigger();
     float m[G], l[G], o[G][HD / 32];
     attend_range<HD, G>(a, kvh, 0, pos + 1, -1, S.sq, S.sk, S.sv, m, l, o);
 #pragma unroll

@@ -31,7 +31,7 @@ extern "C" hy_device *hy_device_wrap(hy_dev_kind kind, const char *name, void *i
 namespace {
 
 constexpr int kMaxChunk = 256;     // tokens per device prefill / forward chunk
-constexpr int kSplitLen = 256;     // keys per decode attention split
+constexpr int kSplitLen = kDecSplit;  // keys per decode attention split
 constexpr size_t kMaxDynSmem = 200 * 1024;
 
 struct HyCtx;
@@ -92,7 +92,11 @@ struct HyCtx {
     int vocab_out = 0;
     Graph g_fwd1, g_fwd1_logits, g_dec;
     int g_dec_vocab = -1;
+    bool trace_on = false;  // assign timeline slots to launches (debug)
+    int trace_next = 0;
 };
+
+int trace_slot(HyCtx *c) { return c->trace_on && c->trace_next < kTraceSlots ? c->trace_next++ : -1; }
 
 bool fail(HyCtx *c, const char *what, cudaError_t e) {
     c->broken = true;
@@ -188,10 +192,24 @@ void init_kernel_attrs() {
     set_smem(gemv_fp<FMT_F16, 4>);
     set_smem(gemv_fp<FMT_F32, 1>);
     set_smem(gemv_fp<FMT_F32, 4>);
+    set_smem(gemv_panel_dec<1>);
+    set_smem(gemv_panel_dec<2>);
+    set_smem(gemv_panel_dec<3>);
+    set_smem(gemv_panel_dec<4>);
+    set_smem(attn_decode2<128, 1>);
+    set_smem(attn_decode2<128, 2>);
+    set_smem(attn_decode2<128, 4>);
+    set_smem(attn_decode2<128, 8>);
+    set_smem(attn_decode2<64, 1>);
+    set_smem(attn_decode2<64, 2>);
+    set_smem(attn_decode2<64, 4>);
+    set_smem(attn_decode2<64, 8>);
 }
 
 // One launch for nt <= NT tokens.
-bool gemv_launch(HyCtx *c, const GemvArgs &a, bool pdl, int ctas_per_sm) {
+bool gemv_launch(HyCtx *c, const GemvArgs &a_in, bool pdl, int ctas_per_sm) {
+    GemvArgs a = a_in;
+    a.trace = trace_slot(c);
     const int fmt = a.w[0].fmt;
     int grid = (a.rows_total + kGemvWarps - 1) / kGemvWarps;
     if (grid > c->nsm * ctas_per_sm) grid = c->nsm * ctas_per_sm;
@@ -201,6 +219,21 @@ bool gemv_launch(HyCtx *c, const GemvArgs &a, bool pdl, int ctas_per_sm) {
         const size_t smem = q8_smem_bytes(NT, a.k);
         if (fmt == FMT_PANEL) {
             const int cpl = (a.k + 2047) / 2048;
+            if (NT == 1 && cpl <= 4 && a.epi != EPI_ARGMAX) {
+                // whole weight slice of each CTA staged in shared memory
+                // row slices in multiples of 4 (the kernel's row groups; keeps
+                // interleaved gate/up pairs inside one warp)
+                const int rpc = ((a.rows_total + grid - 1) / grid + 3) & ~3;
+                const size_t sm = panel_dec_smem(rpc, a.k);
+                if (sm <= kMaxDynSmem) {
+                    switch (cpl) {
+                    case 1: return launch(c, gemv_panel_dec<1>, grid, blk, sm, pdl, a, rpc);
+                    case 2: return launch(c, gemv_panel_dec<2>, grid, blk, sm, pdl, a, rpc);
+                    case 3: return launch(c, gemv_panel_dec<3>, grid, blk, sm, pdl, a, rpc);
+                    default: return launch(c, gemv_panel_dec<4>, grid, blk, sm, pdl, a, rpc);
+                    }
+                }
+            }
             if (NT == 1 && cpl <= 4) {
                 switch (cpl) {
                 case 1: return launch(c, gemv_panel_nt1<1>, grid, blk, smem, pdl, a);
@@ -255,6 +288,7 @@ GemvArgs gemv_args(int nt, int k) {
     memset(&a, 0, sizeof a);
     a.nt = nt;
     a.k = k;
+    a.trace = -1;
     return a;
 }
 
@@ -283,14 +317,18 @@ bool run_multi(HyCtx *c, HyWeight *const *ws, float *const *outs, const int *lds
 
 template <int HD, int G>
 bool attn_launch(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
-    if (nt == 1) return launch(c, attn_decode<HD, G>, dim3(aa.kv_heads, aa.max_splits), dim3(G * 32), 0, pdl, aa);
+    if (nt == 1)
+        return launch(c, attn_decode2<HD, G>, dim3(aa.kv_heads, aa.max_splits), dim3((G + 1) * 32), attn_dec_smem<HD>(),
+                      pdl, aa);
     int warps = aa.heads + aa.kv_heads;
     if (warps > 32) warps = 32;
     if (!launch(c, rope_norm_store<HD>, dim3(nt), dim3(warps * 32), 0, pdl, aa)) return false;
     return launch(c, attn_prefill<HD, G>, dim3(aa.kv_heads, nt), dim3(G * 32), 0, pdl, aa);
 }
 
-bool attention(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
+bool attention(HyCtx *c, const AttnArgs &aa_in, int nt, bool pdl) {
+    AttnArgs aa = aa_in;
+    aa.trace = trace_slot(c);
     const int G = aa.heads / aa.kv_heads;
 #define HY_ATT(HD_, G_) \
     if (aa.hd == HD_ && G == G_) return attn_launch<HD_, G_>(c, aa, nt, pdl);
@@ -298,6 +336,61 @@ bool attention(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
     HY_ATT(64, 4) HY_ATT(64, 1) HY_ATT(64, 2) HY_ATT(64, 8)
 #undef HY_ATT
     REQ(c, false, "unsupported head geometry");
+}
+
+// gate|up then down.  Single-token steps with two panel weights of the same
+// shape use one interleaved launch whose warps own (gate_r, up_r) pairs and
+// write silu(gate)*up once (reference src/model.c:873-876); down then only
+// quantises that vector.  Otherwise gate and up land in separate buffers and
+// down applies SiLU*up in its prologue.
+bool ffn_pair_ok(const Layer &L, int nt) {
+    return nt == 1 && L.g->fmt == FMT_PANEL && L.u->fmt == FMT_PANEL && L.g->n == L.u->n && L.g->k == L.u->k &&
+           L.g->shift == L.u->shift && L.g->off == L.u->off;
+}
+
+bool gateup_forward(HyCtx *c, const Layer &L, int nt, bool pdl) {
+    GemvArgs a = gemv_args(nt, c->H);
+    a.act = ACT_NORM;
+    a.x = c->d_h;
+    a.ldx = c->H;
+    a.norm_w = L.ffn_norm;
+    a.eps = c->eps;
+    if (ffn_pair_ok(L, nt)) {
+        a.epi = EPI_SILU;
+        a.nw = 2;
+        a.interleave = 1;
+        a.rows_total = 2 * L.g->n;
+        a.w[0] = desc(L.g, c->d_g, c->F);
+        a.w[1] = desc(L.u, nullptr, c->F);
+        return run_gemv(c, a, pdl);
+    }
+    HyWeight *ws[2] = {L.g, L.u};
+    float *outs[2] = {c->d_g, c->d_u};
+    const int lds[2] = {c->F, c->F};
+    a.epi = EPI_STORE;
+    return run_multi(c, ws, outs, lds, 2, a, pdl);
+}
+
+bool down_forward(HyCtx *c, const Layer &L, int nt, bool pdl, float *dst) {
+    GemvArgs a = gemv_args(nt, c->F);
+    if (ffn_pair_ok(L, nt)) {
+        a.act = ACT_VEC;  // d_g already holds silu(gate)*up
+        a.x = c->d_g;
+    } else {
+        a.act = ACT_SILU;
+        a.x = c->d_g;
+        a.x2 = c->d_u;
+    }
+    a.ldx = c->F;
+    a.epi = EPI_ADD;
+    a.nw = 1;
+    a.rows_total = L.d->n;
+    a.w[0] = desc(L.d, dst, c->H);
+    return run_gemv(c, a, pdl);
+}
+
+bool ffn_forward(HyCtx *c, const Layer &L, int nt, bool pdl) {
+    return gateup_forward(c, L, nt, pdl) && down_forward(c, L, nt, pdl, c->d_h);
 }
 
 bool layer_forward(HyCtx *c, int li, int nt, const int *pos_ptr, bool pdl) {
@@ -356,32 +449,7 @@ bool layer_forward(HyCtx *c, int li, int nt, const int *pos_ptr, bool pdl) {
         a.w[0] = desc(L.o, c->d_h, c->H);
         if (!run_gemv(c, a, pdl)) return false;
     }
-    {
-        HyWeight *ws[2] = {L.g, L.u};
-        float *outs[2] = {c->d_g, c->d_u};
-        const int lds[2] = {c->F, c->F};
-        GemvArgs a = gemv_args(nt, c->H);
-        a.act = ACT_NORM;
-        a.x = c->d_h;
-        a.ldx = c->H;
-        a.norm_w = L.ffn_norm;
-        a.eps = c->eps;
-        a.epi = EPI_STORE;
-        if (!run_multi(c, ws, outs, lds, 2, a, pdl)) return false;
-    }
-    {
-        GemvArgs a = gemv_args(nt, c->F);
-        a.act = ACT_SILU;
-        a.x = c->d_g;
-        a.x2 = c->d_u;
-        a.ldx = c->F;
-        a.epi = EPI_ADD;
-        a.nw = 1;
-        a.rows_total = L.d->n;
-        a.w[0] = desc(L.d, c->d_h, c->H);
-        if (!run_gemv(c, a, pdl)) return false;
-    }
-    return true;
+    return ffn_forward(c, L, nt, pdl);
 }
 
 // LM head on one token's residual x (RMSNorm with out_norm first).
@@ -453,11 +521,11 @@ bool build_decode_graph(HyCtx *c) {
     REQ(c, c->embd != nullptr, "no embedding weight set (hyc_set_embedding)");
     const bool ok = capture(c, c->g_dec, [&]() {
         if (!launch(c, embed_rows, dim3(1), dim3(256), 0, true, desc(c->embd, nullptr, 0),
-                    (const int *)&c->d_state->tok, c->d_h))
+                    (const int *)&c->d_state->tok, c->d_h, trace_slot(c)))
             return false;
         if (!layers_forward(c, 1, &c->d_state->pos, true)) return false;
         if (!head_forward(c, c->d_h, false, true, true)) return false;
-        return launch(c, decode_finalize, dim3(1), dim3(32), 0, true, c->d_state, c->d_out_ids);
+        return launch(c, decode_finalize, dim3(1), dim3(32), 0, true, c->d_state, c->d_out_ids, trace_slot(c));
     });
     if (ok) c->g_dec_vocab = c->vocab_out;
     return ok;
@@ -970,12 +1038,12 @@ HYC_API int hyc_decode_begin(void *impl, const int *prompt, int n, int keep, int
     for (size_t i = 0; i < cp.size(); i++) {
         const int p0 = cp[i], nt = (n - p0) < kMaxChunk ? (n - p0) : kMaxChunk;
         if (!launch(c, embed_rows, dim3(nt), dim3(256), 0, false, desc(c->embd, nullptr, 0),
-                    (const int *)(c->d_tokens + (p0 - keep)), c->d_h))
+                    (const int *)(c->d_tokens + (p0 - keep)), c->d_h, -1))
             return -1;
         if (!layers_forward(c, nt, c->d_chunk_pos + i, false)) return -1;
         if (i + 1 == cp.size()) {
             if (!head_forward(c, c->d_h + (size_t)(nt - 1) * c->H, false, true, false)) return -1;
-            if (!launch(c, decode_finalize, dim3(1), dim3(32), 0, false, c->d_state, c->d_out_ids)) return -1;
+            if (!launch(c, decode_finalize, dim3(1), dim3(32), 0, false, c->d_state, c->d_out_ids, -1)) return -1;
         }
     }
     // the synchronous copies above were ordered before the launches; the graph
@@ -991,7 +1059,7 @@ HYC_API int hyc_decode_begin(void *impl, const int *prompt, int n, int keep, int
 
 HYC_API int hyc_decode_steps(void *impl, int steps) {
     HyCtx *c = (HyCtx *)impl;
-    if (!c || c->broken || !c->g_dec.exec) return -1;
+    if (!c || c->broken || !c->fused || !build_decode_graph(c)) return -1;
     for (int i = 0; i < steps; i++)
         if (!graph_launch(c, c->g_dec)) return -1;
     return 0;
@@ -999,7 +1067,7 @@ HYC_API int hyc_decode_steps(void *impl, int steps) {
 
 HYC_API int hyc_decode_steps_host(void *impl, int steps, int *tok_io) {
     HyCtx *c = (HyCtx *)impl;
-    if (!c || c->broken || !c->g_dec.exec || !tok_io) return -1;
+    if (!c || c->broken || !c->fused || !tok_io || !build_decode_graph(c)) return -1;
     if (cudaMemcpyAsync(&tok_io[0], &c->d_state->tok, 4, cudaMemcpyDeviceToHost, c->st) != cudaSuccess) return -1;
     for (int i = 0; i < steps; i++) {
         if (cudaMemcpyAsync(&c->d_state->tok, &tok_io[i], 4, cudaMemcpyHostToDevice, c->st) != cudaSuccess) return -1;
@@ -1157,34 +1225,31 @@ HYC_API int hyc_bench_op(void *impl, int op, int iters) {
         const Layer &L = c->layers[i % c->L];
         const int qkv_ld = c->qd + 2 * c->kvd;
         bool ok = true;
-        if (op == 1 || op == 2) {
+        if (op == 1) {
             HyWeight *ws[3] = {L.q, L.k, L.v};
             float *outs[3] = {c->d_qkv, c->d_qkv + c->qd, c->d_qkv + c->qd + c->kvd};
             int lds[3] = {qkv_ld, qkv_ld, qkv_ld};
-            if (op == 2) {
-                ws[0] = L.g; ws[1] = L.u;
-                outs[0] = c->d_g; outs[1] = c->d_u;
-                lds[0] = lds[1] = c->F;
-            }
             GemvArgs a = gemv_args(1, c->H);
             a.act = ACT_NORM;
             a.x = c->d_h;
             a.ldx = c->H;
-            a.norm_w = op == 1 ? L.attn_norm : L.ffn_norm;
+            a.norm_w = L.attn_norm;
             a.eps = c->eps;
             a.epi = EPI_STORE;
-            ok = run_multi(c, ws, outs, lds, op == 1 ? 3 : 2, a, true);
-        } else if (op == 3 || op == 4) {
-            HyWeight *w = op == 3 ? L.d : L.o;
-            GemvArgs a = gemv_args(1, w->k);
-            a.act = op == 3 ? ACT_SILU : ACT_VEC;
-            a.x = op == 3 ? c->d_g : c->d_ao;
-            a.x2 = c->d_u;
-            a.ldx = w->k;
+            ok = run_multi(c, ws, outs, lds, 3, a, true);
+        } else if (op == 2) {
+            ok = gateup_forward(c, L, 1, true);
+        } else if (op == 3) {
+            ok = down_forward(c, L, 1, true, c->d_tmp_h());
+        } else if (op == 4) {
+            GemvArgs a = gemv_args(1, L.o->k);
+            a.act = ACT_VEC;
+            a.x = c->d_ao;
+            a.ldx = L.o->k;
             a.epi = EPI_ADD;
             a.nw = 1;
-            a.rows_total = w->n;
-            a.w[0] = desc(w, c->d_tmp_h(), c->H);
+            a.rows_total = L.o->n;
+            a.w[0] = desc(L.o, c->d_tmp_h(), c->H);
             ok = run_gemv(c, a, true);
         } else if (op == 5) {
             AttnArgs aa;
@@ -1385,6 +1450,44 @@ HYC_API int hyc_debug_buffer(void *impl, int which, float *out, size_t count) {
         d2h(c, out, src[which], count * 4) != cudaSuccess)
         return -1;
     return 0;
+}
+
+// Debug timeline: on != 0 rebuilds the graphs with one slot per kernel launch
+// (launch / past-wait / past-prologue / end in %globaltimer ns).
+HYC_API int hyc_trace(void *impl, int on) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c) return -1;
+    c->trace_on = on != 0;
+    c->trace_next = 0;
+    graph_reset(c->g_fwd1);
+    graph_reset(c->g_fwd1_logits);
+    graph_reset(c->g_dec);
+    c->g_dec_vocab = -1;
+    static unsigned long long zeros[kTraceSlots][4];
+    return cudaMemcpyToSymbolAsync(g_trace, zeros, sizeof zeros, 0, cudaMemcpyHostToDevice, c->st) == cudaSuccess &&
+                   cudaMemcpyToSymbolAsync(g_trace2, zeros, sizeof zeros, 0, cudaMemcpyHostToDevice, c->st) ==
+                       cudaSuccess &&
+                   cudaMemcpyToSymbolAsync(g_trace3, zeros, sizeof zeros, 0, cudaMemcpyHostToDevice, c->st) ==
+                       cudaSuccess &&
+                   cudaStreamSynchronize(c->st) == cudaSuccess
+               ? 0
+               : -1;
+}
+
+// Copy the timeline (slots * 4 values) and return the number of slots in use.
+HYC_API int hyc_trace_read(void *impl, unsigned long long *out, int max_slots) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || !out) return -1;
+    const int n = c->trace_next < max_slots ? c->trace_next : max_slots;
+    // out holds [max_slots][4] main stamps followed by [max_slots][4] sub-phase stamps
+    if (cudaStreamSynchronize(c->st) != cudaSuccess ||
+        cudaMemcpyFromSymbol(out, g_trace, (size_t)n * 4 * sizeof(unsigned long long)) != cudaSuccess ||
+        cudaMemcpyFromSymbol(out + (size_t)max_slots * 4, g_trace2, (size_t)n * 4 * sizeof(unsigned long long)) !=
+            cudaSuccess ||
+        cudaMemcpyFromSymbol(out + (size_t)max_slots * 8, g_trace3, (size_t)n * 4 * sizeof(unsigned long long)) !=
+            cudaSuccess)
+        return -1;
+    return n;
 }
 
 // The host loader's RoPE tables (reference src/model.c:537 and :576-586),

@@ -25,7 +25,8 @@ enum ActMode {
 };
 
 // What happens to each output row.
-enum Epi { EPI_STORE = 0, EPI_ADD = 1, EPI_ARGMAX = 2 };
+// EPI_SILU: interleaved gate|up pair -> w[0].out[row] = silu(gate) * up.
+enum Epi { EPI_STORE = 0, EPI_ADD = 1, EPI_ARGMAX = 2, EPI_SILU = 3 };
 
 constexpr int kPieceOrder[4] = {0, 2, 1, 3};
 
@@ -73,6 +74,36 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p) {
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                  : "l"(p));
     return r;
+}
+
+// Optional per-kernel timeline (debug): slot s holds [launch of CTA 0,
+// CTA 0 past griddepcontrol.wait, CTA 0 past its prologue, last CTA end] in
+// %globaltimer nanoseconds.  Slot < 0 disables recording.
+constexpr int kTraceSlots = 1024;
+__device__ unsigned long long g_trace[kTraceSlots][4];
+__device__ unsigned long long g_trace2[kTraceSlots][4];  // sub-phases of CTA 0
+__device__ unsigned long long g_trace3[kTraceSlots][4];  // CTA 0: clock64 and globaltimer at wait / end
+
+__device__ __forceinline__ unsigned long long gtimer() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ void trace_mark(int slot, int which) {
+    if (slot >= 0 && slot < kTraceSlots && threadIdx.x == 0) {
+        const unsigned long long t = gtimer();
+        if (which == 3) atomicMax(&g_trace[slot][3], t);
+        else if (blockIdx.x == 0 && blockIdx.y == 0) g_trace[slot][which] = t;
+        if (blockIdx.x == 0 && blockIdx.y == 0 && (which == 1 || which == 3)) {
+            g_trace3[slot][which == 1 ? 0 : 2] = clock64();
+            g_trace3[slot][which == 1 ? 1 : 3] = t;
+        }
+    }
+}
+
+__device__ __forceinline__ void trace_sub(int slot, int which) {
+    if (slot >= 0 && slot < kTraceSlots && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0)
+        g_trace2[slot][which] = gtimer();
 }
 
 // Monotone 64-bit argmax key: larger value wins, equal values -> smaller index

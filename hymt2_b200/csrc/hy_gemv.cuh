@@ -41,6 +41,8 @@ struct GemvArgs {
     unsigned long long *amax;
     int amax_rows;
     int32_t *ints;  // optional exact per-block integers [nt][rows][nblk]
+    int trace;      // timeline slot (< 0: off)
+    int interleave; // 2 weights of equal n: merged row m -> weight m & 1, row m >> 1
 };
 
 // ---------------------------------------------------------------- activation staging
@@ -87,26 +89,81 @@ __device__ inline float block_sum(float v, float *red) {
     return warp_sum(t);
 }
 
-// Fill s.x with token t's fp32 activation according to a.act.
-__device__ inline void stage_fp32(const GemvArgs &a, int t, float *dst, float *red, int K) {
-    const float *x = a.x + (size_t)t * a.ldx;
+// Fill dst[K] with token t's fp32 activation according to a.act.  Every
+// thread issues all of its 16-byte loads (x, and norm weight or up) before
+// using any of them, so the staging costs one L2 round trip, not K/blockDim.
+// Needs K % 4 == 0 and K <= 4 * kStageVec * blockDim.x.
+constexpr int kStageVec = 8;
+
+// The RMSNorm weight is a constant: load it before griddepcontrol.wait.
+template <int SV = kStageVec>
+__device__ inline void preload_norm(const GemvArgs &a, float4 (&nv)[SV], int K) {
+    if (a.act != ACT_NORM) return;
+    const float4 *y4 = (const float4 *)a.norm_w;
+#pragma unroll
+    for (int j = 0; j < SV; j++) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < (K >> 2)) nv[j] = __ldg(y4 + i);
+    }
+}
+
+template <int SV = kStageVec>
+__device__ inline void stage_fp32(const GemvArgs &a, int t, float *dst, float *red, int K,
+                                  const float4 (*pre)[SV] = nullptr) {
+    const float4 *x4 = (const float4 *)(a.x + (size_t)t * a.ldx);
+    const float4 *y4 = a.act == ACT_NORM ? (const float4 *)a.norm_w
+                                         : (a.act == ACT_SILU ? (const float4 *)(a.x2 + (size_t)t * a.ldx) : nullptr);
+    const int n4 = K >> 2;
+    float4 xv[SV], yv[SV];
+#pragma unroll
+    for (int j = 0; j < SV; j++) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < n4) {
+            xv[j] = x4[i];
+            if (pre && a.act == ACT_NORM) yv[j] = (*pre)[j];
+            else if (y4) yv[j] = __ldg(y4 + i);
+        }
+    }
+    float4 *d4 = (float4 *)dst;
     if (a.act == ACT_NORM) {
         float ss = 0.f;
-        for (int i = threadIdx.x; i < K; i += blockDim.x) {
-            const float v = x[i];
-            ss = __fadd_rn(ss, __fmul_rn(v, v));
+#pragma unroll
+        for (int j = 0; j < SV; j++) {
+            const int i = threadIdx.x + j * blockDim.x;
+            if (i < n4) {
+                ss = __fadd_rn(ss, __fmul_rn(xv[j].x, xv[j].x));
+                ss = __fadd_rn(ss, __fmul_rn(xv[j].y, xv[j].y));
+                ss = __fadd_rn(ss, __fmul_rn(xv[j].z, xv[j].z));
+                ss = __fadd_rn(ss, __fmul_rn(xv[j].w, xv[j].w));
+            }
         }
         ss = block_sum(ss, red);
         const float scale = 1.0f / sqrtf(ss / (float)K + a.eps);
-        for (int i = threadIdx.x; i < K; i += blockDim.x) dst[i] = __fmul_rn(__fmul_rn(x[i], scale), a.norm_w[i]);
+#pragma unroll
+        for (int j = 0; j < SV; j++) {
+            const int i = threadIdx.x + j * blockDim.x;
+            if (i < n4)
+                d4[i] = make_float4(__fmul_rn(__fmul_rn(xv[j].x, scale), yv[j].x),
+                                    __fmul_rn(__fmul_rn(xv[j].y, scale), yv[j].y),
+                                    __fmul_rn(__fmul_rn(xv[j].z, scale), yv[j].z),
+                                    __fmul_rn(__fmul_rn(xv[j].w, scale), yv[j].w));
+        }
     } else if (a.act == ACT_SILU) {
-        const float *u = a.x2 + (size_t)t * a.ldx;
-        for (int i = threadIdx.x; i < K; i += blockDim.x) {
-            const float g = x[i];
-            dst[i] = __fmul_rn(g / (1.0f + expf(-g)), u[i]);
+#pragma unroll
+        for (int j = 0; j < SV; j++) {
+            const int i = threadIdx.x + j * blockDim.x;
+            if (i < n4) {
+                const float4 g = xv[j], u = yv[j];
+                d4[i] = make_float4(__fmul_rn(g.x / (1.0f + expf(-g.x)), u.x), __fmul_rn(g.y / (1.0f + expf(-g.y)), u.y),
+                                    __fmul_rn(g.z / (1.0f + expf(-g.z)), u.z), __fmul_rn(g.w / (1.0f + expf(-g.w)), u.w));
+            }
         }
     } else {
-        for (int i = threadIdx.x; i < K; i += blockDim.x) dst[i] = x[i];
+#pragma unroll
+        for (int j = 0; j < SV; j++) {
+            const int i = threadIdx.x + j * blockDim.x;
+            if (i < n4) d4[i] = xv[j];
+        }
     }
 }
 
@@ -119,20 +176,21 @@ __device__ inline void quantize_block_warp(const float *src, Q8Smem &s, int t, i
     const float *p = src + b * 256 + lane * 8;
     const float4 v0 = *(const float4 *)&p[0], v1 = *(const float4 *)&p[4];
     const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-    float ba = 0.f, bv = 0.f;
-    int bi = 0x7fffffff;
+    // lane-local first maximum of |x|, then one redux for the max and one
+    // for the smallest index holding it (finite |x| bit patterns order like
+    // the values; NaN never qualifies, as in the host's strict '>')
+    float ba = 0.f, lv = 0.f;
+    int li = 0x7fffffff;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
         const float av = fabsf(v[j]);
-        if (av > ba) { ba = av; bv = v[j]; bi = lane * 8 + j; }
+        if (av > ba) { ba = av; lv = v[j]; li = lane * 8 + j; }
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float oa = __shfl_xor_sync(0xffffffffu, ba, o);
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (oa > ba || (oa == ba && oi < bi)) { ba = oa; bv = ov; bi = oi; }
-    }
+    const unsigned mbits = __reduce_max_sync(0xffffffffu, __float_as_uint(ba));
+    const unsigned cand = (__float_as_uint(ba) == mbits) ? (unsigned)li : 0x7fffffffu;
+    const int bi = (int)__reduce_min_sync(0xffffffffu, cand);
+    ba = __uint_as_float(mbits);
+    const float bv = __shfl_sync(0xffffffffu, lv, (bi >> 3) & 31);
     int q[8];
     float d = 0.f;
     if (ba == 0.f) {
@@ -153,7 +211,7 @@ __device__ inline void quantize_block_warp(const float *src, Q8Smem &s, int t, i
 #pragma unroll
     for (int j = 0; j < 8; j++) part += q[j];
     const int pair = part + __shfl_xor_sync(0xffffffffu, part, 1);
-    const int total = warp_sum_i(part);
+    const int total = __reduce_add_sync(0xffffffffu, part);
     // natural element e = lane*8 + j -> chunk ch = lane/8, plane l = (lane%8)/2, byte (lane&1)*8 + j
     const int ch = lane >> 3, l = (lane & 7) >> 1;
     const int pos = (b * 4 + piece_of_chunk(ch)) * 16 + (lane & 1) * 8;
@@ -169,7 +227,8 @@ __device__ inline void quantize_block_warp(const float *src, Q8Smem &s, int t, i
 }
 
 // Build the Q8_K activation of all nt tokens in shared memory.
-__device__ inline void stage_q8k(const GemvArgs &a, Q8Smem &s, int K) {
+template <int SV = kStageVec>
+__device__ inline void stage_q8k(const GemvArgs &a, Q8Smem &s, int K, const float4 (*pre)[SV] = nullptr) {
     const int nb = K / 256;
     const int warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     for (int t = 0; t < a.nt; t++) {
@@ -188,17 +247,24 @@ __device__ inline void stage_q8k(const GemvArgs &a, Q8Smem &s, int K) {
                 s.sum[t * nb + b] = src[b].sum;
             }
         } else {
-            stage_fp32(a, t, s.x, s.red, K);
+            stage_fp32<SV>(a, t, s.x, s.red, K, t == 0 ? pre : nullptr);
             __syncthreads();
+            if (t == 0) trace_sub(a.trace, 0);
             for (int b = warp; b < nb; b += nwarps) quantize_block_warp(s.x, s, t, b, nb, K);
         }
         __syncthreads();
+        if (t == 0) trace_sub(a.trace, 1);
     }
 }
 
 // ---------------------------------------------------------------- row bookkeeping
 
 __device__ __forceinline__ void map_row(const GemvArgs &a, int r, int &wi, int &lr) {
+    if (a.interleave) {
+        wi = r & 1;
+        lr = r >> 1;
+        return;
+    }
     wi = 0;
     lr = r;
     if (a.nw > 1 && lr >= a.w[0].n) {
@@ -238,6 +304,7 @@ __device__ __forceinline__ void row_epilogue(const GemvArgs &a, const WDesc &w, 
 }
 
 __device__ inline void argmax_commit(const GemvArgs &a, unsigned long long best, float *red_area) {
+    trace_mark(a.trace, 3);
     if (a.epi != EPI_ARGMAX) return;
     unsigned long long *sk = (unsigned long long *)red_area;
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -274,6 +341,8 @@ __device__ __forceinline__ int panel_chunk_dot(const uint4 wv, const int4 *act4)
 // whole launch.  CPL = 16-byte chunks per lane per row (K <= 2048*CPL).
 template <int CPL>
 __global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt1(const __grid_constant__ GemvArgs a) {
+    trace_mark(a.trace, 0);
+    pdl_trigger();
     extern __shared__ __align__(16) uint8_t smem[];
     const int K = a.k, nb = K / 256, nchunk = nb * 4;
     const int lane = threadIdx.x & 31;
@@ -296,9 +365,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt1(const __grid_cons
         }
     }
     pdl_wait();
+    trace_mark(a.trace, 1);
     Q8Smem s = q8_smem(smem, 1, K);
     stage_q8k(a, s, K);
-    pdl_trigger();
+    trace_mark(a.trace, 2);
 
     int4 act[CPL][4];
     float dblk[CPL];
@@ -365,17 +435,171 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt1(const __grid_cons
     argmax_commit(a, best, s.red);
 }
 
+// Decode (nt == 1) with the CTA's whole weight slice staged in shared memory.
+// CTA c owns rows [c*rows_per_cta, ...) of the merged row space; before
+// griddepcontrol.wait it issues cp.async copies of those rows' 64-byte panel
+// blocks and scales (weights never depend on the previous kernel), so the
+// HBM stream overlaps the producer kernel; after the wait it only builds the
+// activation and computes from shared memory.
+__host__ __device__ inline size_t panel_dec_smem(int rows_per_cta, int K) {
+    const int nb = K / 256;
+    return align16((size_t)rows_per_cta * nb * 64) + align16((size_t)rows_per_cta * nb * 4) + q8_smem_bytes(1, K);
+}
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
+}
+
+// Exact block integer of one 16-byte panel chunk with four independent
+// dp4a chains (one per 2-bit plane) so the adds overlap.
+__device__ __forceinline__ int panel_chunk_dot4(const uint4 wv, const int4 *act4) {
+    const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
+    int e0 = 0, e1 = 0, e2 = 0, e3 = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        e0 = dp4a((int)(wd[j] & 0x03030303u), ((const int *)&act4[0])[j], e0);
+        e1 = dp4a((int)((wd[j] >> 2) & 0x03030303u), ((const int *)&act4[1])[j], e1);
+        e2 = dp4a((int)((wd[j] >> 4) & 0x03030303u), ((const int *)&act4[2])[j], e2);
+        e3 = dp4a((int)((wd[j] >> 6) & 0x03030303u), ((const int *)&act4[3])[j], e3);
+    }
+    return (e0 + e1) + (e2 + e3);
+}
+
+template <int CPL>
+__global__ void __launch_bounds__(kGemvThreads) gemv_panel_dec(const __grid_constant__ GemvArgs a, int rows_per_cta) {
+    constexpr int RG = CPL == 1 ? 4 : 2;  // rows per warp iteration (independent chains)
+    extern __shared__ __align__(16) uint8_t smem[];
+    trace_mark(a.trace, 0);
+    pdl_trigger();
+    const int K = a.k, nb = K / 256, nchunk = nb * 4, row_b = nb * 64;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int r0 = blockIdx.x * rows_per_cta;
+    const int r1 = min(r0 + rows_per_cta, a.rows_total);
+    uint8_t *sw = smem;
+    float *ss = (float *)(smem + align16((size_t)rows_per_cta * row_b));
+    uint8_t *sact = smem + align16((size_t)rows_per_cta * row_b) + align16((size_t)rows_per_cta * nb * 4);
+    // stage the weight slice (16-byte chunks) and scales (4-byte) asynchronously
+    for (int idx = threadIdx.x; idx < (r1 - r0) * nchunk; idx += blockDim.x) {
+        const int rr = idx / nchunk, c = idx - rr * nchunk;
+        int wi, lr;
+        map_row(a, r0 + rr, wi, lr);
+        const WDesc &w = wsel(a, wi);
+        cp_async16(sw + (size_t)rr * row_b + c * 16, w.w + (size_t)lr * w.stride + (size_t)c * 16);
+    }
+    for (int idx = threadIdx.x; idx < (r1 - r0) * nb; idx += blockDim.x) {
+        const int rr = idx / nb, b = idx - rr * nb;
+        int wi, lr;
+        map_row(a, r0 + rr, wi, lr);
+        const WDesc &w = wsel(a, wi);
+        cp_async4(ss + (size_t)rr * nb + b, w.s + (size_t)lr * nb + b);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    constexpr int SV = 2 * CPL;  // K <= 2048*CPL: 2*CPL float4 per thread at 256 threads
+    float4 nv[SV];
+    preload_norm<SV>(a, nv, K);
+    pdl_wait();
+    trace_mark(a.trace, 1);
+    Q8Smem s = q8_smem(sact, 1, K);
+    stage_q8k<SV>(a, s, K, &nv);
+    trace_mark(a.trace, 2);
+    int4 act[CPL][4];
+    float dblk[CPL];
+    int sblk[CPL];
+#pragma unroll
+    for (int i = 0; i < CPL; i++) {
+        const int c = lane + 32 * i;
+        if (c < nchunk) {
+#pragma unroll
+            for (int l = 0; l < 4; l++) act[i][l] = *(const int4 *)&s.qp[(size_t)l * (K / 4) + c * 16];
+            dblk[i] = s.d[c >> 2];
+            sblk[i] = s.sum[c >> 2];
+        } else {
+#pragma unroll
+            for (int l = 0; l < 4; l++) act[i][l] = make_int4(0, 0, 0, 0);
+            dblk[i] = 0.f;
+            sblk[i] = 0;
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    trace_sub(a.trace, 2);
+    const int shift = a.w[0].shift, off = a.w[0].off;  // merged weights share the format
+    unsigned long long best = 0;
+    for (int rb = r0 + warp * RG; rb < r1; rb += kGemvWarps * RG) {
+        float acc[RG];
+#pragma unroll
+        for (int g = 0; g < RG; g++) acc[g] = 0.f;
+#pragma unroll
+        for (int i = 0; i < CPL; i++) {
+            const int c = lane + 32 * i;
+            int e[RG];
+#pragma unroll
+            for (int g = 0; g < RG; g++) {
+                e[g] = 0;
+                if (c < nchunk && rb + g < r1)
+                    e[g] = panel_chunk_dot4(*(const uint4 *)(sw + (size_t)(rb + g - r0) * row_b + c * 16), act[i]);
+            }
+#pragma unroll
+            for (int g = 0; g < RG; g++) e[g] += __shfl_xor_sync(0xffffffffu, e[g], 1);
+#pragma unroll
+            for (int g = 0; g < RG; g++) e[g] += __shfl_xor_sync(0xffffffffu, e[g], 2);
+            if (c < nchunk && (lane & 3) == 0) {
+#pragma unroll
+                for (int g = 0; g < RG; g++) {
+                    if (rb + g >= r1) break;
+                    const int v = e[g] * (1 << shift) - off * sblk[i];
+                    if (a.ints) a.ints[(size_t)(rb + g) * nb + (c >> 2)] = v;
+                    acc[g] += ss[(size_t)(rb + g - r0) * nb + (c >> 2)] * dblk[i] * (float)v;
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int g = 0; g < RG; g++) acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], o);
+        if (a.epi == EPI_SILU) {
+            // rows come in (gate, up) pairs of the same output index
+            if (lane == 0) {
+#pragma unroll
+                for (int g = 0; g + 1 < RG; g += 2) {
+                    if (rb + g + 1 >= r1) break;
+                    const float gt = acc[g], up = acc[g + 1];
+                    a.w[0].out[(rb + g) >> 1] = __fmul_rn(gt / (1.0f + expf(-gt)), up);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int g = 0; g < RG; g++) {
+                if (rb + g >= r1) break;
+                int wi, lr;
+                map_row(a, rb + g, wi, lr);
+                row_epilogue<1>(a, wsel(a, wi), lr, rb + g, &acc[g], best);
+            }
+        }
+    }
+    trace_sub(a.trace, 3);
+    argmax_commit(a, best, s.red);
+}
+
 // Small batches (1 < nt <= NT): activations read from plane-major smem.
 template <int NT>
 __global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt(const __grid_constant__ GemvArgs a) {
+    trace_mark(a.trace, 0);
+    pdl_trigger();
     extern __shared__ __align__(16) uint8_t smem[];
     const int K = a.k, nb = K / 256, nchunk = nb * 4;
     const int lane = threadIdx.x & 31;
     const int gw = blockIdx.x * kGemvWarps + (threadIdx.x >> 5), nw = gridDim.x * kGemvWarps;
     pdl_wait();
+    trace_mark(a.trace, 1);
     Q8Smem s = q8_smem(smem, NT, K);
     stage_q8k(a, s, K);
-    pdl_trigger();
+    trace_mark(a.trace, 2);
     unsigned long long best = 0;
     for (int r = gw; r < a.rows_total; r += nw) {
         int wi, lr;
@@ -438,14 +662,17 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt(const __grid_const
 // hf*8 + 2q + s (layout of reference src/kernels.c:786-806).
 template <int NT>
 __global__ void __launch_bounds__(kGemvThreads) gemv_q6k(const __grid_constant__ GemvArgs a) {
+    trace_mark(a.trace, 0);
+    pdl_trigger();
     extern __shared__ __align__(16) uint8_t smem[];
     const int K = a.k, nb = K / 256, nunit = nb * 4;
     const int lane = threadIdx.x & 31;
     const int gw = blockIdx.x * kGemvWarps + (threadIdx.x >> 5), nw = gridDim.x * kGemvWarps;
     pdl_wait();
+    trace_mark(a.trace, 1);
     Q8Smem s = q8_smem(smem, NT, K);
     stage_q8k(a, s, K);
-    pdl_trigger();
+    trace_mark(a.trace, 2);
     unsigned long long best = 0;
     for (int r = gw; r < a.rows_total; r += nw) {
         int wi, lr;
@@ -533,14 +760,17 @@ __device__ __forceinline__ void k4_scale_min(const uint8_t *q, int j, int &sc, i
 // 2g+1) — reference src/kernels.c:861-877.
 template <int NT>
 __global__ void __launch_bounds__(kGemvThreads) gemv_q4k(const __grid_constant__ GemvArgs a) {
+    trace_mark(a.trace, 0);
+    pdl_trigger();
     extern __shared__ __align__(16) uint8_t smem[];
     const int K = a.k, nb = K / 256, nunit = nb * 8;
     const int lane = threadIdx.x & 31;
     const int gw = blockIdx.x * kGemvWarps + (threadIdx.x >> 5), nw = gridDim.x * kGemvWarps;
     pdl_wait();
+    trace_mark(a.trace, 1);
     Q8Smem s = q8_smem(smem, NT, K);
     stage_q8k(a, s, K);
-    pdl_trigger();
+    trace_mark(a.trace, 2);
     unsigned long long best = 0;
     for (int r = gw; r < a.rows_total; r += nw) {
         int wi, lr;
@@ -626,6 +856,8 @@ __host__ __device__ inline size_t fp_smem_bytes(int NT, int K) { return align16(
 
 template <int FMT, int NT>
 __global__ void __launch_bounds__(kGemvThreads) gemv_fp(const __grid_constant__ GemvArgs a) {
+    trace_mark(a.trace, 0);
+    pdl_trigger();
     extern __shared__ __align__(16) uint8_t smem[];
     constexpr int E = FpFmt<FMT>::kElems, QPU = E / 4;
     const int K = a.k, nunit = K / E;
@@ -635,6 +867,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_fp(const __grid_constant__ 
     float *stg = (float *)(smem + align16((size_t)NT * K * 4));  // [K] staging
     float *red = stg + K;
     pdl_wait();
+    trace_mark(a.trace, 1);
     for (int t = 0; t < a.nt; t++) {
         stage_fp32(a, t, stg, red, K);
         __syncthreads();
@@ -644,7 +877,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_fp(const __grid_constant__ 
         }
         __syncthreads();
     }
-    pdl_trigger();
+    trace_mark(a.trace, 2);
     unsigned long long best = 0;
     for (int r = gw; r < a.rows_total; r += nw) {
         int wi, lr;

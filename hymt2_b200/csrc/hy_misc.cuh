@@ -124,12 +124,15 @@ __device__ inline float dequant_elem(const WDesc &w, int r, int e) {
 }
 
 // h[t][:] = embedding row of tokens[t]; out-of-range ids read row 0.
-__global__ void embed_rows(const __grid_constant__ WDesc w, const int *tokens, float *h) {
+__global__ void embed_rows(const __grid_constant__ WDesc w, const int *tokens, float *h, int trace) {
+    trace_mark(trace, 0);
+    pdl_trigger();
     pdl_wait();
+    trace_mark(trace, 1);
     int tok = tokens[blockIdx.x];
     if (tok < 0 || tok >= w.n) tok = 0;
     for (int e = threadIdx.x; e < w.k; e += blockDim.x) h[(size_t)blockIdx.x * w.k + e] = dequant_elem(w, tok, e);
-    pdl_trigger();
+    trace_mark(trace, 3);
 }
 
 __global__ void dequant_row_kernel(const __grid_constant__ WDesc w, int r, float *dst) {
@@ -152,8 +155,11 @@ struct DecodeState {
 };
 
 // Consume the argmax: emit the token, advance the position, reset the key.
-__global__ void decode_finalize(DecodeState *st, int *out_ids) {
+__global__ void decode_finalize(DecodeState *st, int *out_ids, int trace) {
+    trace_mark(trace, 0);
+    pdl_trigger();
     pdl_wait();
+    trace_mark(trace, 1);
     if (threadIdx.x == 0) {
         const unsigned long long key = st->amax;
         const int idx = key ? (int)argmax_index(key) : 0;
@@ -167,7 +173,7 @@ __global__ void decode_finalize(DecodeState *st, int *out_ids) {
         st->pos = st->pos + 1;
         st->amax = 0ull;
     }
-    pdl_trigger();
+    trace_mark(trace, 3);
 }
 
 }  // namespace hyk

@@ -125,6 +125,13 @@ HYC_API int hyc_attention_test(void *impl, int heads, int kv_heads, int hdim, in
  * synchronising): 0 residual h, 1 q|k|v, 2 attention output, 3 gate, 4 up;
  * `count` floats from the start of the buffer. */
 HYC_API int hyc_debug_buffer(void *impl, int which, float *out, size_t count);
+/* Debug timeline of the captured graphs: hyc_trace(impl, 1) rebuilds them
+ * with one slot per kernel; hyc_trace_read copies [max_slots][4] %globaltimer
+ * stamps (launch, past wait, past prologue, end), then [max_slots][4]
+ * sub-phase stamps of CTA 0, then [max_slots][4] (clock64, globaltimer) of
+ * CTA 0 at its wait and its end; returns the number of slots in use. */
+HYC_API int hyc_trace(void *impl, int on);
+HYC_API int hyc_trace_read(void *impl, unsigned long long *out, int max_slots);
 /* bf16 KV rows [0, npos) of one layer of the fused cache. */
 HYC_API int hyc_kv_read(void *impl, int layer, int npos, uint16_t *k, uint16_t *v);
 /* RoPE tables exactly as the host loader computes them (src/model.c:537,576-586). */
