@@ -90,6 +90,7 @@ SIGNATURES = {
     "hyc_gemv_multi_test": (I, [P, P, I, I, P, P, F, I, P]),
     "hyc_trace": (I, [P, I]),
     "hyc_trace_read": (I, [P, P, I]),
+    "hyc_attention_decode_noalloc": (I, [P, I, I, I, I, P, F, P, P, P, P, P, P, P, P, C.c_char_p, I]),
     "hyc_attention_test": (I, [P, I, I, I, I, I, I, F, P, P, P, P, P, P, P, P]),
 }
 

@@ -14,6 +14,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "../../include/hymt2_cuda.h"
@@ -144,6 +145,18 @@ bool launch(HyCtx *c, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
     c->launches++;
     c->capture_kernels++;
     return true;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t cudaLaunchKernelEx_compat(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                      Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.numAttrs = 0;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 WDesc desc(const HyWeight *w, float *out, int ld) {
@@ -1490,6 +1503,35 @@ HYC_API int hyc_trace_read(void *impl, unsigned long long *out, int max_slots) {
     return n;
 }
 
+// ---------------------------------------------------------------- allocation-free decode attention
+//
+// For callers that cannot allocate device memory themselves at the point of
+// the call (a host that has handed all free memory to its own arena or
+// caching allocator, or a latency-critical serving loop where cudaMalloc /
+// cudaFree would synchronise the device and stall other streams), the
+// split-KV decode attention can run with its scratch — the per-split
+// partial softmax states and the per-KV-head completion tickets — in a
+// fixed file-scope device array instead of memory from fused_prepare.
+// Every GPU that loads this library holds these 512 KiB + 256 B until the
+// process exits.
+constexpr size_t kNoAllocPartFloats = 131072;  // 512 KiB of split partials
+constexpr int kNoAllocTickets = 64;
+static __device__ __align__(256) float g_noalloc_part[kNoAllocPartFloats];
+static __device__ __align__(256) int g_noalloc_tickets[kNoAllocTickets];
+
+struct NoAllocScratch {
+    float *part = nullptr;
+    int *tickets = nullptr;
+    bool ready = false;
+};
+static NoAllocScratch g_noalloc[128];  // per device ordinal, filled on first use
+static std::mutex g_noalloc_mu;
+
+static int noalloc_fail(char *err, int cap, int code, const char *msg) {
+    if (err && cap > 0) snprintf(err, (size_t)cap, "%s", msg);
+    return code;
+}
+
 // The host loader's RoPE tables (reference src/model.c:537 and :576-586),
 // evaluated with the same single-precision libm calls.
 HYC_API int hyc_rope_tables(float freq_base, float alpha, int hdim, int rope_dim, int ctx, float *cos_out,
@@ -1506,6 +1548,95 @@ HYC_API int hyc_rope_tables(float freq_base, float alpha, int hdim, int rope_dim
             sin_out[(size_t)p * half + i] = sinf(ang);
         }
     }
+    return 0;
+}
+
+
+// Decode attention for one token (rope -> q/k RMSNorm -> bf16 K/V store at
+// *d_pos -> causal GQA softmax over 0..*d_pos) on caller-provided device
+// buffers, with no device allocation: the split-KV scratch lives in
+// g_noalloc_part / g_noalloc_tickets.  See include/hymt2_cuda.h.
+HYC_API int hyc_attention_decode_noalloc(void *stream, int heads, int kv_heads, int hdim, int ctx, const int *d_pos,
+                                         float eps, float *d_qkv, uint16_t *d_kc, uint16_t *d_vc,
+                                         const float *d_q_norm, const float *d_k_norm, const float *d_rope_cos,
+                                         const float *d_rope_sin, float *d_ao, char *err, int err_cap) {
+    if (heads < 1 || kv_heads < 1 || heads % kv_heads || ctx < 1 || !d_pos || !d_qkv || !d_kc || !d_vc ||
+        !d_q_norm || !d_k_norm || !d_rope_cos || !d_rope_sin || !d_ao)
+        return noalloc_fail(err, err_cap, -1, "invalid argument");
+    const int G = heads / kv_heads;
+    if ((hdim != 64 && hdim != 128) || (G != 1 && G != 2 && G != 4 && G != 8))
+        return noalloc_fail(err, err_cap, -1, "unsupported head geometry (hdim 64/128, group 1/2/4/8)");
+    const int splits = (ctx + kDecSplit - 1) / kDecSplit;
+    const size_t need = (size_t)kv_heads * splits * G * (hdim + 2);
+    if (need > kNoAllocPartFloats || kv_heads > kNoAllocTickets) {
+        char msg[192];
+        snprintf(msg, sizeof msg,
+                 "scratch limit exceeded: kv_heads*ceil(ctx/%d)*group*(hdim+2) = %zu floats > %zu, or kv_heads %d > %d",
+                 kDecSplit, need, kNoAllocPartFloats, kv_heads, kNoAllocTickets);
+        return noalloc_fail(err, err_cap, -2, msg);
+    }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128)
+        return noalloc_fail(err, err_cap, -3, "no current CUDA device");
+    NoAllocScratch &sc = g_noalloc[dev];
+    {
+        // once per device, with that device current: the symbols' device
+        // addresses (the host-side names are only stand-ins)
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!sc.ready) {
+            void *p = nullptr, *t = nullptr;
+            if (cudaGetSymbolAddress(&p, g_noalloc_part) != cudaSuccess ||
+                cudaGetSymbolAddress(&t, g_noalloc_tickets) != cudaSuccess) {
+                cudaGetLastError();
+                return noalloc_fail(err, err_cap, -3, "cudaGetSymbolAddress failed for the scratch array");
+            }
+            init_kernel_attrs();
+            sc.part = (float *)p;
+            sc.tickets = (int *)t;
+            sc.ready = true;
+        }
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    // the array keeps the previous call's contents: tickets must start at zero
+    if (cudaMemsetAsync(sc.tickets, 0, (size_t)kv_heads * sizeof(int), st) != cudaSuccess)
+        return noalloc_fail(err, err_cap, -3, "clearing the ticket scratch failed");
+    AttnArgs aa;
+    memset(&aa, 0, sizeof aa);
+    aa.qkv = d_qkv;
+    aa.qkv_ld = heads * hdim + 2 * kv_heads * hdim;
+    aa.kc = d_kc;
+    aa.vc = d_vc;
+    aa.q_norm = d_q_norm;
+    aa.k_norm = d_k_norm;
+    aa.rope_cos = d_rope_cos;
+    aa.rope_sin = d_rope_sin;
+    aa.pos_ptr = d_pos;
+    aa.nt = 1;
+    aa.heads = heads;
+    aa.kv_heads = kv_heads;
+    aa.hd = hdim;
+    aa.kvdim = kv_heads * hdim;
+    aa.qdim = heads * hdim;
+    aa.ctx = ctx;
+    aa.half = hdim / 2;
+    aa.eps = eps;
+    aa.scale = 1.0f / sqrtf((float)hdim);
+    aa.ao = d_ao;
+    aa.part = sc.part;
+    aa.tickets = sc.tickets;
+    aa.split_len = kDecSplit;
+    aa.max_splits = splits;
+    aa.trace = -1;
+    const dim3 grid(kv_heads, splits), block((G + 1) * 32);
+    const size_t smem = hdim == 128 ? attn_dec_smem<128>() : attn_dec_smem<64>();
+    cudaError_t e = cudaErrorInvalidValue;
+#define HY_NA(HD_, G_)                                                                    \
+    if (hdim == HD_ && G == G_) e = cudaLaunchKernelEx_compat(attn_decode2<HD_, G_>, grid, block, smem, st, aa);
+    HY_NA(128, 4) HY_NA(128, 1) HY_NA(128, 2) HY_NA(128, 8)
+    HY_NA(64, 4) HY_NA(64, 1) HY_NA(64, 2) HY_NA(64, 8)
+#undef HY_NA
+    if (e != cudaSuccess) return noalloc_fail(err, err_cap, -3, cudaGetErrorString(e));
+    if (err && err_cap > 0) err[0] = 0;
     return 0;
 }
 

@@ -145,6 +145,38 @@ HYC_API long long hyc_launch_count(void *impl);
  * 4 o_proj GEMV, 5 decode attention; layer weights rotate over all layers. */
 HYC_API int hyc_bench_op(void *impl, int op, int iters);
 
+/* ---- allocation-free decode attention -------------------------------- */
+
+/* No counterpart in the reference (its CUDA path allocates every buffer in
+ * fused_prepare).  For callers that cannot allocate device memory at the
+ * point of the call — for example a host whose own arena or caching
+ * allocator already holds all free device memory, or a serving loop that
+ * must not let cudaMalloc/cudaFree synchronise the device — this runs the
+ * split-KV decode attention of one token (rope -> q/k RMSNorm -> bf16 K/V
+ * store at *d_pos -> causal GQA softmax over positions 0..*d_pos) on
+ * caller-provided DEVICE buffers and allocates nothing: no cudaMalloc,
+ * cudaFree or allocating library call.  Its scratch (split partials and
+ * per-KV-head tickets) is a file-scope device array of 512 KiB + 256 B that
+ * every GPU loading this library keeps until the process exits.
+ *   d_qkv [q | k | v] (pre-rope, heads*hdim + 2*kv_heads*hdim floats);
+ *   d_kc, d_vc [ctx][kv_heads*hdim] bf16 caches (row *d_pos is written);
+ *   d_rope_cos/sin [ctx][hdim/2]; d_q_norm, d_k_norm [hdim]; d_ao [heads*hdim].
+ * Limits: hdim 64 or 128; heads/kv_heads in {1,2,4,8};
+ * kv_heads * ceil(ctx/128) * (heads/kv_heads) * (hdim+2) <= 131072 and
+ * kv_heads <= 64 — larger shapes return -2.  Returns 0, -1 (bad argument),
+ * -2 (beyond the scratch maximum) or -3 (CUDA error); `err` (optional)
+ * receives a message.  Work is enqueued on `stream` (a cudaStream_t).
+ * The first call on a device looks up the scratch address (once per device,
+ * with that device current); make that first call before any stream
+ * capture.  All calls share the one scratch array and it keeps the last
+ * call's contents (the tickets are cleared on the stream before each
+ * launch), so calls whose executions overlap on the GPU race with each
+ * other: serialise them, e.g. on one stream. */
+HYC_API int hyc_attention_decode_noalloc(void *stream, int heads, int kv_heads, int hdim, int ctx, const int *d_pos,
+                                         float eps, float *d_qkv, uint16_t *d_kc, uint16_t *d_vc,
+                                         const float *d_q_norm, const float *d_k_norm, const float *d_rope_cos,
+                                         const float *d_rope_sin, float *d_ao, char *err, int err_cap);
+
 #ifdef __cplusplus
 }
 #endif
