@@ -77,6 +77,9 @@ SIGNATURES = {
     "hyc_decode_rewind": (I, [P, I, I]),
     "hyc_host_alloc": (P, [Z]),
     "hyc_host_free": (None, [P]),
+    "hyc_set_decode_mode": (I, [P, I]),
+    "hyc_decode_path": (I, [P, C.c_char_p, I]),
+    "hyc_mega_timeline": (I, [P, P, I]),
     "hyc_quantize_q8k": (I, [P, P, I, I, P]),
     "hyc_block_ints": (I, [P, P, P, I, P]),
     "hyc_dequant_row": (I, [P, P, I, P]),

@@ -196,105 +196,96 @@ __device__ __forceinline__ void merge_warps(AttnSmem<HD, G> &S, float &M, float 
     }
 }
 
-// Decode v2: one query token at *pos_ptr; grid (kv_heads, splits of kDecSplit
-// keys), G warps, warp w = query head kvh*G + w.  The split's cached K/V rows
-// (positions < pos, written by earlier decode steps, i.e. at least two
-// kernels back) are copied to shared memory with cp.async BEFORE
-// griddepcontrol.wait; the current position comes from this kernel's own
-// rope/norm prologue.  K rows are stored with their 16-byte chunks rotated by
-// the row index so lanes reading 32 different rows hit different banks.
+// Decode attention, one query token at position pos: grid (kv_heads, splits
+// of kDecSplit keys).  Warps 0..G-1 are the query heads kvh*G + w, warp G
+// rotates/normalises this KV head's k and stores k and v.  The split's cached
+// K/V rows (positions < pos, written by earlier decode steps) are staged in
+// shared memory by the caller; the current position comes from the prologue.
+// The body is shared by the per-layer kernel (attn_decode2) and the
+// persistent decode kernel, which differ only in how the rows are staged, so
+// both produce bit-identical outputs.
 constexpr int kDecSplit = 128;
 
 template <int HD>
 __host__ __device__ inline size_t attn_dec_smem() { return (size_t)2 * kDecSplit * HD * 2; }
 
-template <int HD, int G>
-__global__ void __launch_bounds__((G + 1) * 32) attn_decode2(const __grid_constant__ AttnArgs a) {
-    extern __shared__ __align__(16) uint8_t dsm[];
-    uint16_t *sK = (uint16_t *)dsm;                       // [kDecSplit][HD] rotated chunks
-    uint16_t *sV = sK + (size_t)kDecSplit * HD;           // [kDecSplit][HD]
-    __shared__ __align__(16) float sq[G][HD];
-    __shared__ __align__(16) float skc[HD], svc[HD];
-    __shared__ int last;
-    constexpr int CH = HD / 8;                            // 16-byte chunks per row
-    constexpr int DPL = HD / 32;                          // output dims per lane (contiguous)
-    trace_mark(a.trace, 0);
-    pdl_trigger();
-    const int kvh = blockIdx.x, split = blockIdx.y;
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pos = *a.pos_ptr;  // written before this graph / >= 2 kernels back
-    const int j0 = split * kDecSplit;
-    if (pos < 0 || pos >= a.ctx || j0 > pos) return;
-    const int j1 = min(pos + 1, j0 + kDecSplit);
-    const int ncache = min(j1, pos) - j0;  // rows already in the cache
-    const uint16_t *Kg = a.kc + kvh * HD, *Vg = a.vc + kvh * HD;
-    for (int idx = threadIdx.x; idx < ncache * CH; idx += blockDim.x) {
-        const int j = idx / CH, c = idx - j * CH;
-        const size_t g = (size_t)(j0 + j) * a.kvdim + c * 8;
-        const unsigned dk = (unsigned)__cvta_generic_to_shared(sK + (size_t)j * HD + ((c + j) % CH) * 8);
-        const unsigned dv = (unsigned)__cvta_generic_to_shared(sV + (size_t)j * HD + c * 8);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk), "l"(Kg + g) : "memory");
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dv), "l"(Vg + g) : "memory");
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-    // constants of this position: rope row and the per-head norm weights
-    const float *cs = a.rope_cos + (size_t)pos * a.half, *sn = a.rope_sin + (size_t)pos * a.half;
+// Per-position constants a warp needs for the prologue: rope row and the
+// per-head norm weight (q_norm for the query warps, k_norm for the k/v warp).
+template <int HD>
+struct DecConsts {
     float rc[HD / 64], rs[HD / 64], nq[HD / 32];
+};
+
+template <int HD, int G>
+__device__ __forceinline__ void attn_dec_consts(const AttnArgs &a, int pos, DecConsts<HD> &k) {
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float *cs = a.rope_cos + (size_t)pos * a.half, *sn = a.rope_sin + (size_t)pos * a.half;
 #pragma unroll
     for (int i = 0; i < HD / 64; i++) {
-        rc[i] = __ldg(cs + lane + 32 * i);
-        rs[i] = __ldg(sn + lane + 32 * i);
+        k.rc[i] = __ldg(cs + lane + 32 * i);
+        k.rs[i] = __ldg(sn + lane + 32 * i);
     }
     const float *nrm = w < G ? a.q_norm : a.k_norm;
 #pragma unroll
-    for (int i = 0; i < HD / 32; i++) nq[i] = __ldg(nrm + lane + 32 * i);
-    pdl_wait();
-    trace_mark(a.trace, 1);
-    {
-        // warps 0..G-1: the G query heads; warp G: this KV head's k and v
-        float v[HD / 32];
-        const float *src = w < G ? a.qkv + (kvh * G + w) * HD : a.qkv + a.qdim + kvh * HD;
+    for (int i = 0; i < HD / 32; i++) k.nq[i] = __ldg(nrm + lane + 32 * i);
+}
+
+// Warps 0..G: rope + norm of the G query heads into sq, of k (and the bf16
+// rounding of k and v) into skc/svc; when `store`, k and v go to the cache.
+template <int HD, int G>
+__device__ __forceinline__ void attn_dec_prologue(const AttnArgs &a, int kvh, int pos, bool store, const DecConsts<HD> &k,
+                                                  float (*sq)[HD], float *skc, float *svc) {
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float v[HD / 32];
+    const float *src = w < G ? a.qkv + (kvh * G + w) * HD : a.qkv + a.qdim + kvh * HD;
 #pragma unroll
-        for (int i = 0; i < HD / 32; i++) v[i] = src[lane + 32 * i];
+    for (int i = 0; i < HD / 32; i++) v[i] = src[lane + 32 * i];
 #pragma unroll
-        for (int i = 0; i < HD / 64; i++) {
-            const float x0 = v[i], x1 = v[i + HD / 64];
-            v[i] = __fsub_rn(__fmul_rn(x0, rc[i]), __fmul_rn(x1, rs[i]));
-            v[i + HD / 64] = __fadd_rn(__fmul_rn(x0, rs[i]), __fmul_rn(x1, rc[i]));
-        }
-        float ssq = 0.f;
+    for (int i = 0; i < HD / 64; i++) {
+        const float x0 = v[i], x1 = v[i + HD / 64];
+        v[i] = __fsub_rn(__fmul_rn(x0, k.rc[i]), __fmul_rn(x1, k.rs[i]));
+        v[i + HD / 64] = __fadd_rn(__fmul_rn(x0, k.rs[i]), __fmul_rn(x1, k.rc[i]));
+    }
+    float ssq = 0.f;
 #pragma unroll
-        for (int i = 0; i < HD / 32; i++) ssq = __fadd_rn(ssq, __fmul_rn(v[i], v[i]));
-        ssq = warp_sum(ssq);
-        const float scale = 1.0f / sqrtf(ssq / (float)HD + a.eps);
+    for (int i = 0; i < HD / 32; i++) ssq = __fadd_rn(ssq, __fmul_rn(v[i], v[i]));
+    ssq = warp_sum(ssq);
+    const float scale = 1.0f / sqrtf(ssq / (float)HD + a.eps);
 #pragma unroll
-        for (int i = 0; i < HD / 32; i++) v[i] = __fmul_rn(__fmul_rn(v[i], scale), nq[i]);
-        if (w < G) {
+    for (int i = 0; i < HD / 32; i++) v[i] = __fmul_rn(__fmul_rn(v[i], scale), k.nq[i]);
+    if (w < G) {
 #pragma unroll
-            for (int i = 0; i < HD / 32; i++) sq[w][lane + 32 * i] = v[i];
-        } else {
-            const float *vr = a.qkv + a.qdim + a.kvdim + kvh * HD;
-            uint16_t *kd = a.kc + (size_t)pos * a.kvdim + kvh * HD, *vd = a.vc + (size_t)pos * a.kvdim + kvh * HD;
+        for (int i = 0; i < HD / 32; i++) sq[w][lane + 32 * i] = v[i];
+    } else {
+        const float *vr = a.qkv + a.qdim + a.kvdim + kvh * HD;
+        uint16_t *kd = a.kc + (size_t)pos * a.kvdim + kvh * HD, *vd = a.vc + (size_t)pos * a.kvdim + kvh * HD;
 #pragma unroll
-            for (int i = 0; i < HD / 32; i++) {
-                const int e = lane + 32 * i;
-                const uint16_t kb = f32_to_bf16_bits(v[i]), vb = f32_to_bf16_bits(vr[e]);
-                skc[e] = bf16_bits_to_f32(kb);
-                svc[e] = bf16_bits_to_f32(vb);
-                if (split == 0) {
-                    kd[e] = kb;
-                    vd[e] = vb;
-                }
+        for (int i = 0; i < HD / 32; i++) {
+            const int e = lane + 32 * i;
+            const uint16_t kb = f32_to_bf16_bits(v[i]), vb = f32_to_bf16_bits(vr[e]);
+            skc[e] = bf16_bits_to_f32(kb);
+            svc[e] = bf16_bits_to_f32(vb);
+            if (store) {
+                kd[e] = kb;
+                vd[e] = vb;
             }
         }
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
-    trace_mark(a.trace, 2);
-    if (w == G) {  // the k/v warp has no head of its own
-        trace_mark(a.trace, 3);
-        return;
-    }
+}
+
+// Warps 0..G-1 (query head kvh*G + w): scores over keys [j0, j1), softmax,
+// p.V, then either the final output (one split) or this split's partial and,
+// in the last split CTA to finish, the log-sum-exp merge.  krow(j, c) is the
+// 16-byte chunk c of cached K row j in shared memory, sV[j][HD] the V rows.
+// Synchronises the G head warps with named barrier `bar_id`.
+template <int HD, int G, typename KRow>
+__device__ __forceinline__ void attn_dec_main(const AttnArgs &a, int kvh, int split, int pos, KRow krow,
+                                              const uint16_t *sV, const float (*sq)[HD], const float *skc,
+                                              const float *svc, int *last, int bar_id) {
+    constexpr int CH = HD / 8;    // 16-byte chunks per row
+    constexpr int DPL = HD / 32;  // output dims per lane (contiguous)
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int j0 = split * kDecSplit, j1 = min(pos + 1, j0 + kDecSplit);
     // scores: warp w = head, lane handles keys j0 + lane + 32 i; each 8-dim q
     // chunk is read once and applied to all of the lane's keys
     constexpr int KPL = kDecSplit / 32;
@@ -311,7 +302,7 @@ __global__ void __launch_bounds__((G + 1) * 32) attn_decode2(const __grid_consta
             const int j = lane + 32 * i;
             if (32 * i >= nk) break;
             if (j < nk && j0 + j != pos) {
-                const uint4 kk = *(const uint4 *)(sK + (size_t)j * HD + ((c + j) % CH) * 8);
+                const uint4 kk = *krow(j, c);
                 const uint32_t kw[4] = {kk.x, kk.y, kk.z, kk.w};
 #pragma unroll
                 for (int q = 0; q < 4; q++) {
@@ -401,7 +392,6 @@ __global__ void __launch_bounds__((G + 1) * 32) attn_decode2(const __grid_consta
         const float inv = 1.0f / l;
 #pragma unroll
         for (int q = 0; q < DPL; q++) a.ao[h * HD + lane * DPL + q] = o[q] * inv;
-        trace_mark(a.trace, 3);
         return;
     }
     float *pp = a.part + (((size_t)kvh * a.max_splits + split) * G + w) * (HD + 2);
@@ -412,12 +402,11 @@ __global__ void __launch_bounds__((G + 1) * 32) attn_decode2(const __grid_consta
         pp[1] = l;
     }
     __threadfence();
-    // the k/v warp has exited: synchronise the G head warps only (named barrier 1)
-    asm volatile("bar.sync 1, %0;" ::"r"(G * 32) : "memory");
-    if (threadIdx.x == 0) last = atomicAdd(&a.tickets[kvh], 1) == nsplit - 1;
-    asm volatile("bar.sync 1, %0;" ::"r"(G * 32) : "memory");
-    trace_mark(a.trace, 3);
-    if (!last) return;
+    // only the G head warps take part: named barrier over G*32 threads
+    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(G * 32) : "memory");
+    if (threadIdx.x == 0) *last = atomicAdd(&a.tickets[kvh], 1) == nsplit - 1;
+    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(G * 32) : "memory");
+    if (!*last) return;
     __threadfence();
     float MM = -INFINITY;
     for (int sp = 0; sp < nsplit; sp++)
@@ -436,6 +425,53 @@ __global__ void __launch_bounds__((G + 1) * 32) attn_decode2(const __grid_consta
 #pragma unroll
     for (int q = 0; q < DPL; q++) a.ao[h * HD + lane * DPL + q] = OO[q] * inv;
     if (threadIdx.x == 0) a.tickets[kvh] = 0;
+}
+
+// The per-layer kernel: K rows are staged with their 16-byte chunks rotated
+// by the row index so lanes reading 32 different rows hit different banks;
+// the copies are issued BEFORE griddepcontrol.wait (the cached rows were
+// written at least two kernels back).
+template <int HD, int G>
+__global__ void __launch_bounds__((G + 1) * 32) attn_decode2(const __grid_constant__ AttnArgs a) {
+    extern __shared__ __align__(16) uint8_t dsm[];
+    uint16_t *sK = (uint16_t *)dsm;                       // [kDecSplit][HD] rotated chunks
+    uint16_t *sV = sK + (size_t)kDecSplit * HD;           // [kDecSplit][HD]
+    __shared__ __align__(16) float sq[G][HD];
+    __shared__ __align__(16) float skc[HD], svc[HD];
+    __shared__ int last;
+    constexpr int CH = HD / 8;
+    trace_mark(a.trace, 0);
+    pdl_trigger();
+    const int kvh = blockIdx.x, split = blockIdx.y;
+    const int w = threadIdx.x >> 5;
+    const int pos = *a.pos_ptr;  // written before this graph / >= 2 kernels back
+    const int j0 = split * kDecSplit;
+    if (pos < 0 || pos >= a.ctx || j0 > pos) return;
+    const int j1 = min(pos + 1, j0 + kDecSplit);
+    const int ncache = min(j1, pos) - j0;  // rows already in the cache
+    const uint16_t *Kg = a.kc + kvh * HD, *Vg = a.vc + kvh * HD;
+    for (int idx = threadIdx.x; idx < ncache * CH; idx += blockDim.x) {
+        const int j = idx / CH, c = idx - j * CH;
+        const size_t g = (size_t)(j0 + j) * a.kvdim + c * 8;
+        const unsigned dk = (unsigned)__cvta_generic_to_shared(sK + (size_t)j * HD + ((c + j) % CH) * 8);
+        const unsigned dv = (unsigned)__cvta_generic_to_shared(sV + (size_t)j * HD + c * 8);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk), "l"(Kg + g) : "memory");
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dv), "l"(Vg + g) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    DecConsts<HD> k;
+    attn_dec_consts<HD, G>(a, pos, k);
+    pdl_wait();
+    trace_mark(a.trace, 1);
+    attn_dec_prologue<HD, G>(a, kvh, pos, split == 0, k, sq, skc, svc);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    trace_mark(a.trace, 2);
+    if (w < G) {
+        const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * HD + ((c + j) % CH) * 8); };
+        attn_dec_main<HD, G>(a, kvh, split, pos, krow, sV, sq, skc, svc, &last, 1);
+    }
+    trace_mark(a.trace, 3);
 }
 
 // Prefill: token t (position *pos_ptr + t) attends to 0..pos inclusive; q

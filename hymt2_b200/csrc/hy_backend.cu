@@ -7,7 +7,9 @@
 //   embed -> L x [qkv GEMV | attention | o_proj GEMV (+residual) |
 //                 gate/up GEMV | down GEMV (SiLU*up prologue, +residual)]
 //         -> LM-head GEMV with fused argmax -> token feedback
-// and never synchronises with the host.
+// and never synchronises with the host.  For panel models with a Q6_K head
+// the decode loop can instead run as one persistent cooperative kernel for
+// any number of steps (hy_mega.cuh), bit-identical to the graph.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -20,6 +22,7 @@
 #include "../../include/hymt2_cuda.h"
 #include "hy_attn.cuh"
 #include "hy_gemv.cuh"
+#include "hy_mega.cuh"
 #include "hy_misc.cuh"
 
 using namespace hyk;
@@ -95,6 +98,16 @@ struct HyCtx {
     int g_dec_vocab = -1;
     bool trace_on = false;  // assign timeline slots to launches (debug)
     int trace_next = 0;
+    // persistent decode kernel
+    int decode_mode = 1;            // 0: persistent kernel when supported, 1: graph of per-layer launches
+    int mega_state = -1;            // -1 unchecked, 0 unsupported, 1 ready
+    char mega_why[128] = {0};       // why unsupported
+    MegaLayer *d_mega_layers = nullptr;
+    MegaSync *d_mega_sync = nullptr;
+    unsigned long long *d_tl = nullptr;
+    int tl_cap = 0;
+    MegaPlan mega_plan_v{};
+    void *mega_kernel = nullptr;
 };
 
 int trace_slot(HyCtx *c) { return c->trace_on && c->trace_next < kTraceSlots ? c->trace_next++ : -1; }
@@ -544,6 +557,181 @@ bool build_decode_graph(HyCtx *c) {
     return ok;
 }
 
+// ---------------------------------------------------------------- persistent decode
+
+template <int HD, int G, int CF>
+void *mega_kernel_for() {
+    return (void *)decode_mega<HD, G, CF>;
+}
+
+// Decide once per prepared model whether the persistent kernel can run it,
+// and build its device tables.  Unsupported shapes keep the graph path.
+bool mega_check(HyCtx *c) {
+    if (c->mega_state >= 0) return c->mega_state == 1;
+    c->mega_state = 0;
+    auto no = [&](const char *why) {
+        snprintf(c->mega_why, sizeof c->mega_why, "%s", why);
+        return false;
+    };
+    if (!c->fused || !c->outw || !c->embd) return no("model not prepared");
+    const int G = c->heads / c->kvh;
+    int CF = (c->F + 2047) / 2048;
+    if (CF == 2) CF = 3;
+    if (c->hd == 128 && G == 4 && CF == 3) c->mega_kernel = mega_kernel_for<128, 4, 3>();
+    else if (c->hd == 64 && G == 2 && CF == 1) c->mega_kernel = mega_kernel_for<64, 2, 1>();
+    else if (c->hd == 64 && G == 4 && CF == 1) c->mega_kernel = mega_kernel_for<64, 4, 1>();
+    else return no("head geometry / FFN width without a persistent-kernel instance");
+    if (c->H > 2048 || c->qd > 2048) return no("hidden or q width above 2048");
+    if (c->outw->fmt != FMT_Q6K || c->outw->k != c->H) return no("LM head is not Q6_K");
+    if (c->kvh > 64 || c->kvh * c->max_splits > c->nsm) return no("context too long for one attention CTA per split");
+    const HyWeight *w0 = c->layers[0].q;
+    for (const Layer &L : c->layers) {
+        const HyWeight *ws[7] = {L.q, L.k, L.v, L.o, L.g, L.u, L.d};
+        for (const HyWeight *w : ws)
+            if (w->fmt != FMT_PANEL || w->shift != w0->shift || w->off != w0->off) return no("layer weights not all panels");
+        if (L.g->n != c->F || L.u->n != c->F || L.d->n != c->H || L.o->n != c->H || L.q->n != c->qd ||
+            L.k->n != c->kvd || L.v->n != c->kvd)
+            return no("layer weight rows do not match the model");
+    }
+    int coop = 0;
+    if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->dev) != cudaSuccess || !coop)
+        return no("no cooperative launch");
+    c->mega_plan_v = mega_plan(c->nsm, c->H, c->F, c->qd, c->kvd, c->outw->n, c->hd);
+    if (cudaFuncSetAttribute(c->mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)c->mega_plan_v.bytes) != cudaSuccess) {
+        cudaGetLastError();
+        return no("shared-memory plan too large");
+    }
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, c->mega_kernel, kMegaThreads, c->mega_plan_v.bytes) !=
+            cudaSuccess ||
+        per_sm < 1) {
+        cudaGetLastError();
+        return no("persistent kernel does not fit on an SM");
+    }
+    std::vector<MegaLayer> tab(c->L);
+    for (int i = 0; i < c->L; i++) {
+        const Layer &L = c->layers[i];
+        const HyWeight *ws[7] = {L.q, L.k, L.v, L.o, L.g, L.u, L.d};
+        for (int j = 0; j < 7; j++) {
+            tab[i].w[j] = ws[j]->w;
+            tab[i].s[j] = ws[j]->s;
+        }
+        tab[i].attn_norm = L.attn_norm;
+        tab[i].ffn_norm = L.ffn_norm;
+        tab[i].q_norm = L.q_norm;
+        tab[i].k_norm = L.k_norm;
+        tab[i].kc = c->d_kv + (size_t)i * 2 * c->ctx * c->kvd;
+        tab[i].vc = tab[i].kc + (size_t)c->ctx * c->kvd;
+    }
+    if (!c->d_mega_layers) CK(c, cudaMalloc(&c->d_mega_layers, (size_t)c->L * sizeof(MegaLayer)));
+    if (!c->d_mega_sync) CK(c, cudaMalloc(&c->d_mega_sync, sizeof(MegaSync)));
+    CK(c, h2d(c, c->d_mega_layers, tab.data(), (size_t)c->L * sizeof(MegaLayer)));
+    CK(c, cudaMemsetAsync(c->d_mega_sync, 0, sizeof(MegaSync), c->st));
+    CK(c, cudaStreamSynchronize(c->st));  // the host table is a local
+    c->mega_state = 1;
+    return true;
+}
+
+bool use_mega(HyCtx *c) { return c->decode_mode == 0 && mega_check(c); }
+
+// `steps` greedy decode steps from the DecodeState's (tok, pos) in one launch.
+bool mega_launch(HyCtx *c, int steps) {
+    MegaArgs a;
+    memset(&a, 0, sizeof a);
+    const MegaPlan &p = c->mega_plan_v;
+    a.layers = c->d_mega_layers;
+    a.L = c->L;
+    a.H = c->H;
+    a.F = c->F;
+    a.kvh = c->kvh;
+    a.qd = c->qd;
+    a.kvd = c->kvd;
+    a.ctx = c->ctx;
+    a.shift = c->layers[0].q->shift;
+    a.off = c->layers[0].q->off;
+    a.eps = c->eps;
+    for (int i = 0; i < 5; i++) a.rpc[i] = p.rpc[i];
+    for (int i = 0; i < 4; i++) a.slot_off[i] = p.slot_off[i];
+    a.stage_off = p.stage_off;
+    a.attn_off = p.attn_off;
+    a.kmax = p.kmax;
+    AttnArgs &aa = a.attn;
+    aa.qkv = c->d_qkv;
+    aa.qkv_ld = c->qd + 2 * c->kvd;
+    aa.rope_cos = c->d_cos;
+    aa.rope_sin = c->d_sin;
+    aa.pos_ptr = &c->d_state->pos;
+    aa.nt = 1;
+    aa.heads = c->heads;
+    aa.kv_heads = c->kvh;
+    aa.hd = c->hd;
+    aa.kvdim = c->kvd;
+    aa.qdim = c->qd;
+    aa.ctx = c->ctx;
+    aa.half = c->half;
+    aa.eps = c->eps;
+    aa.scale = 1.0f / sqrtf((float)c->hd);
+    aa.ao = c->d_ao;
+    aa.part = c->d_part;
+    aa.split_len = kSplitLen;
+    aa.max_splits = c->max_splits;
+    aa.trace = -1;
+    a.head = desc(c->outw, nullptr, c->outw->n);
+    a.embd = desc(c->embd, nullptr, 0);
+    a.vocab_out = c->vocab_out > 0 ? c->vocab_out : c->outw->n;
+    a.out_norm = c->d_out_norm;
+    a.h = c->d_h;
+    a.qkv = c->d_qkv;
+    a.ao = c->d_ao;
+    a.act = c->d_g;
+    a.st = c->d_state;
+    a.out_ids = c->d_out_ids;
+    a.sync = c->d_mega_sync;
+    a.tl = c->trace_on ? c->d_tl : nullptr;
+    a.tl_cap = c->tl_cap;
+    a.steps = steps;
+    CK(c, cudaMemsetAsync(c->d_mega_sync, 0, sizeof(MegaSync), c->st));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c->nsm);
+    cfg.blockDim = dim3(kMegaThreads);
+    cfg.dynamicSmemBytes = p.bytes;
+    cfg.stream = c->st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    void *args[] = {&a};
+    CK(c, cudaLaunchKernelExC(&cfg, c->mega_kernel, args));
+    c->launches++;
+    return true;
+}
+
+// The persistent kernel reports failures through its error word.
+bool mega_status(HyCtx *c) {
+    if (c->mega_state != 1 || !c->d_mega_sync) return true;
+    int err = 0;
+    CK(c, cudaMemcpyAsync(&err, &c->d_mega_sync->err, 4, cudaMemcpyDeviceToHost, c->st));
+    CK(c, cudaStreamSynchronize(c->st));
+    if (err == MEGA_OK) return true;
+    static const char *what[] = {"", "grid barrier timed out", "position outside the context",
+                                 "weight slice copy timed out", "K/V row copy timed out"};
+    c->broken = true;
+    snprintf(c->err, sizeof c->err, "persistent decode kernel: %s", err > 0 && err < 5 ? what[err] : "unknown error");
+    return false;
+}
+
+// Decode steps through whichever path the model uses.
+bool decode_run(HyCtx *c, int steps) {
+    if (steps <= 0) return true;
+    if (use_mega(c)) return mega_launch(c, steps);
+    if (!build_decode_graph(c)) return false;
+    for (int i = 0; i < steps; i++)
+        if (!graph_launch(c, c->g_dec)) return false;
+    return true;
+}
+
 // ---------------------------------------------------------------- test hooks
 
 // Runs the GEMV prologue's quantiser (stage_q8k) and writes full host-layout
@@ -592,6 +780,14 @@ void free_fused(HyCtx *c) {
     c->d_out_ids = c->d_tokens = c->d_chunk_pos = nullptr;
     c->layers.clear();
     c->fused = false;
+    if (c->d_mega_layers) cudaFree(c->d_mega_layers);
+    if (c->d_mega_sync) cudaFree(c->d_mega_sync);
+    if (c->d_tl) cudaFree(c->d_tl);
+    c->d_mega_layers = nullptr;
+    c->d_mega_sync = nullptr;
+    c->d_tl = nullptr;
+    c->tl_cap = 0;
+    c->mega_state = -1;
 }
 
 void destroy_impl(void *impl) {
@@ -874,6 +1070,7 @@ bool fused_prepare(void *impl, const hy_fused_args *sh) {
     graph_reset(c->g_fwd1_logits);
     graph_reset(c->g_dec);
     c->g_dec_vocab = -1;
+    c->mega_state = -1;
     CK(c, cudaStreamSynchronize(c->st));
     c->fused = true;
     return true;
@@ -1005,7 +1202,7 @@ HYC_API int hyc_sync(void *impl) {
         fail(c, "cudaStreamSynchronize", e);
         return -1;
     }
-    return 0;
+    return mega_status(c) ? 0 : -1;
 }
 
 HYC_API int hyc_set_embedding(void *impl, hy_dweight *embd) {
@@ -1014,7 +1211,25 @@ HYC_API int hyc_set_embedding(void *impl, hy_dweight *embd) {
     c->embd = (HyWeight *)embd;
     graph_reset(c->g_dec);
     c->g_dec_vocab = -1;
+    c->mega_state = -1;
     return 0;
+}
+
+HYC_API int hyc_set_decode_mode(void *impl, int mode) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || mode < 0 || mode > 1) return -1;
+    c->decode_mode = mode;
+    return 0;
+}
+
+HYC_API int hyc_decode_path(void *impl, char *why, int cap) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->fused) return -1;
+    const int mega = use_mega(c) ? 1 : 0;
+    if (why && cap > 0)
+        snprintf(why, (size_t)cap, "%s", mega ? "persistent kernel"
+                                              : (c->decode_mode == 1 ? "graph (requested)" : c->mega_why));
+    return mega;
 }
 
 HYC_API long long hyc_launch_count(void *impl) { return impl ? ((HyCtx *)impl)->launches : 0; }
@@ -1059,9 +1274,9 @@ HYC_API int hyc_decode_begin(void *impl, const int *prompt, int n, int keep, int
             if (!launch(c, decode_finalize, dim3(1), dim3(32), 0, false, c->d_state, c->d_out_ids, -1)) return -1;
         }
     }
-    // the synchronous copies above were ordered before the launches; the graph
-    // for single-token steps is built once per vocab_out
-    if (!build_decode_graph(c)) return -1;
+    // the copies above were ordered before the launches; the graph for
+    // single-token steps is built once per vocab_out when it is the decode path
+    if (!use_mega(c) && !build_decode_graph(c)) return -1;
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) {
         fail(c, "decode_begin", e);
@@ -1072,19 +1287,17 @@ HYC_API int hyc_decode_begin(void *impl, const int *prompt, int n, int keep, int
 
 HYC_API int hyc_decode_steps(void *impl, int steps) {
     HyCtx *c = (HyCtx *)impl;
-    if (!c || c->broken || !c->fused || !build_decode_graph(c)) return -1;
-    for (int i = 0; i < steps; i++)
-        if (!graph_launch(c, c->g_dec)) return -1;
-    return 0;
+    if (!c || c->broken || !c->fused || steps < 0) return -1;
+    return decode_run(c, steps) ? 0 : -1;
 }
 
 HYC_API int hyc_decode_steps_host(void *impl, int steps, int *tok_io) {
     HyCtx *c = (HyCtx *)impl;
-    if (!c || c->broken || !c->fused || !tok_io || !build_decode_graph(c)) return -1;
+    if (!c || c->broken || !c->fused || !tok_io || steps < 0) return -1;
     if (cudaMemcpyAsync(&tok_io[0], &c->d_state->tok, 4, cudaMemcpyDeviceToHost, c->st) != cudaSuccess) return -1;
     for (int i = 0; i < steps; i++) {
         if (cudaMemcpyAsync(&c->d_state->tok, &tok_io[i], 4, cudaMemcpyHostToDevice, c->st) != cudaSuccess) return -1;
-        if (!graph_launch(c, c->g_dec)) return -1;
+        if (!decode_run(c, 1)) return -1;
         if (cudaMemcpyAsync(&tok_io[i + 1], &c->d_state->tok, 4, cudaMemcpyDeviceToHost, c->st) != cudaSuccess) return -1;
     }
     return 0;
@@ -1093,6 +1306,7 @@ HYC_API int hyc_decode_steps_host(void *impl, int steps, int *tok_io) {
 HYC_API int hyc_decode_read(void *impl, int *out_ids, int cap) {
     HyCtx *c = (HyCtx *)impl;
     if (!c || c->broken || !c->fused) return -1;
+    if (!mega_status(c)) return -1;
     DecodeState s;
     if (cudaMemcpyAsync(&s, c->d_state, sizeof s, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
         cudaStreamSynchronize(c->st) != cudaSuccess) {
@@ -1472,6 +1686,11 @@ HYC_API int hyc_trace(void *impl, int on) {
     if (!c) return -1;
     c->trace_on = on != 0;
     c->trace_next = 0;
+    if (c->trace_on && c->fused && !c->d_tl) {
+        c->tl_cap = 1 << 16;
+        if (cudaMalloc(&c->d_tl, (size_t)c->tl_cap * 8) != cudaSuccess) return -1;
+    }
+    if (c->d_tl && cudaMemsetAsync(c->d_tl, 0, (size_t)c->tl_cap * 8, c->st) != cudaSuccess) return -1;
     graph_reset(c->g_fwd1);
     graph_reset(c->g_fwd1_logits);
     graph_reset(c->g_dec);
@@ -1499,6 +1718,18 @@ HYC_API int hyc_trace_read(void *impl, unsigned long long *out, int max_slots) {
             cudaSuccess ||
         cudaMemcpyFromSymbol(out + (size_t)max_slots * 8, g_trace3, (size_t)n * 4 * sizeof(unsigned long long)) !=
             cudaSuccess)
+        return -1;
+    return n;
+}
+
+// Persistent-kernel timeline of the last traced launch: %globaltimer at every
+// phase edge of block 0 (step start, then before/after each grid barrier).
+HYC_API int hyc_mega_timeline(void *impl, unsigned long long *out, int cap) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || !out || !c->d_tl) return -1;
+    const int n = cap < c->tl_cap ? cap : c->tl_cap;
+    if (cudaStreamSynchronize(c->st) != cudaSuccess ||
+        cudaMemcpy(out, c->d_tl, (size_t)n * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
         return -1;
     return n;
 }

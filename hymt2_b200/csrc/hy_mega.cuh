@@ -1,0 +1,709 @@
+// hy_mega.cuh — persistent single-launch greedy decode for panel (STQ1_0 /
+// Q2_0C) models with a Q6_K LM head, on sm_100a.
+//
+// One cooperative launch, one 512-thread CTA per SM, runs `steps` decode
+// steps (reference src/model.c:914-958 gen_ids loop over forward_tokens,
+// :836-880 per layer).  Per layer the phases are separated by grid barriers:
+//   q|k|v GEMV (RMSNorm + Q8_K prologue) | attention (rope, q/k norm, bf16
+//   KV store, split-KV softmax) | o_proj GEMV (+residual) | gate|up GEMV
+//   (interleaved rows, SiLU*up epilogue) | down GEMV (+residual)
+// then the LM head with a fused argmax, the token bookkeeping of
+// decode_finalize and the next token's embedding.
+//
+// Each CTA owns fixed row slices of every GEMV, so while layer l runs it
+// streams its layer-(l+1) slices into four shared-memory slots with bulk
+// async copies (cp.async.bulk, no multicast) completing on mbarriers; the
+// attention CTAs stage their cached K/V rows the same way at the start of the
+// layer.  Every arithmetic step (norm reduction order, quantiser, per-row dot
+// products, attention body, head rows) is the one the per-layer kernels use,
+// so this path is bit-identical to the graph of per-layer launches.
+//
+// All waits are bounded by %globaltimer: on a timeout the kernel raises the
+// error word, every CTA leaves at its next barrier, and each CTA waits
+// (bounded) for its own copies in flight before returning.
+#pragma once
+#include "hy_attn.cuh"
+#include "hy_gemv.cuh"
+#include "hy_misc.cuh"
+
+namespace hyk {
+
+constexpr int kMegaThreads = 512;
+constexpr int kMegaWarps = kMegaThreads / 32;
+constexpr int kMegaRowAlign = 8;                           // row slices in multiples of 8
+constexpr unsigned long long kMegaWaitNs = 2000000000ull;  // 2 s bound on any wait
+constexpr int kMegaKPad = 16;                              // K rows padded in smem (bank spread)
+
+enum MegaErr { MEGA_OK = 0, MEGA_ERR_BARRIER = 1, MEGA_ERR_POS = 2, MEGA_ERR_WEIGHTS = 3, MEGA_ERR_KV = 4 };
+
+// Device-resident per-layer table.
+struct MegaLayer {
+    const uint8_t *w[7];  // panel codes: q k v o gate up down
+    const float *s[7];    // panel scales
+    const float *attn_norm, *ffn_norm, *q_norm, *k_norm;
+    uint16_t *kc, *vc;
+};
+
+// Cross-CTA words; the host zeroes the whole struct before each launch.
+struct MegaSync {
+    unsigned long long amax[2];  // argmax key per step parity
+    unsigned bar;                // grid barrier arrivals (monotonic within a launch)
+    int err;                     // MegaErr of the first failure
+    int tickets[64];             // attention split merge tickets per KV head
+};
+
+struct MegaArgs {
+    const MegaLayer *layers;
+    int L, H, F, kvh, qd, kvd, ctx;
+    int shift, off;           // panel code transform shared by all layer weights
+    float eps;
+    int rpc[5];               // rows per CTA: q|k|v, o, gate|up (merged), down, head
+    int slot_off[4];          // dynamic-smem offsets of the weight slots
+    int stage_off, attn_off;  // dynamic-smem offsets of the Q8_K stage and the K/V area
+    int kmax;                 // largest GEMV input length (stage plan)
+    AttnArgs attn;            // shape, rope tables, part buffer; per-layer fields set in-kernel
+    WDesc head, embd;
+    int vocab_out;
+    const float *out_norm;
+    float *h, *qkv, *ao, *act;
+    DecodeState *st;
+    int *out_ids;
+    MegaSync *sync;
+    unsigned long long *tl;   // optional timeline (block 0): globaltimer per phase edge
+    int tl_cap;
+    int steps;
+};
+
+// ---------------------------------------------------------------- primitives
+
+__device__ __forceinline__ unsigned smem_u32(const void *p) { return (unsigned)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t *bar) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect(uint64_t *bar, unsigned tx) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(tx) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t *bar, unsigned parity) {
+    unsigned ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the completion of phase `parity`; false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity) {
+    if (mbar_try(bar, parity)) return true;
+    const unsigned long long t0 = gtimer();
+    while (!mbar_try(bar, parity))
+        if (gtimer() - t0 > kMegaWaitNs) return false;
+    return true;
+}
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ int ld_relaxed_s32(const int *p) {
+    int v;
+    asm volatile("ld.relaxed.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void raise_err(const MegaArgs &a, int code) { atomicCAS(&a.sync->err, 0, code); }
+
+// Grid-wide barrier: every CTA adds 1 to the arrival counter and waits until
+// it reaches the running target.  Bounded; a timeout or another CTA's error
+// makes every CTA return false from here on.
+__device__ __forceinline__ bool grid_sync(const MegaArgs &a, unsigned &target, int *s_flag) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        target += gridDim.x;
+        __threadfence();
+        atomicAdd(&a.sync->bar, 1u);
+        int bad = 0;
+        if ((int)(ld_acquire_u32(&a.sync->bar) - target) < 0) {
+            const unsigned long long t0 = gtimer();
+            unsigned it = 0;
+            while ((int)(ld_acquire_u32(&a.sync->bar) - target) < 0) {
+                if ((++it & 63) == 0) {
+                    if (ld_relaxed_s32(&a.sync->err)) { bad = 1; break; }
+                    if (gtimer() - t0 > kMegaWaitNs) { raise_err(a, MEGA_ERR_BARRIER); bad = 1; break; }
+                }
+            }
+        }
+        if (!bad && ld_relaxed_s32(&a.sync->err)) bad = 1;
+        *s_flag = bad;
+    }
+    __syncthreads();
+    return *s_flag == 0;
+}
+
+__device__ __forceinline__ void tl_mark(const MegaArgs &a, int &idx) {
+    if (a.tl && blockIdx.x == 0 && threadIdx.x == 0 && idx < a.tl_cap) a.tl[idx] = gtimer();
+    idx++;
+}
+
+// ---------------------------------------------------------------- weight slots
+
+__host__ __device__ inline int mega_slot_bytes(int rpc, int K) {
+    return (int)align16((size_t)rpc * (K / 256) * 64) + (int)align16((size_t)rpc * (K / 256) * 4);
+}
+__host__ __device__ inline int mega_phase_k(int t, int H, int F, int qd) { return t == 1 ? qd : (t == 3 ? F : H); }
+__host__ __device__ inline int mega_phase_rows(int t, int H, int F, int qd, int kvd) {
+    return t == 0 ? qd + 2 * kvd : (t == 2 ? 2 * F : H);
+}
+
+// Thread 0: arm slot t's mbarrier and issue the bulk copies of this CTA's
+// rows of GEMV t of layer l (codes, then scales after an aligned gap).
+__device__ inline void mega_fill(const MegaArgs &a, uint8_t *smem, uint64_t *bar, int t, int l) {
+    const MegaLayer &ly = a.layers[l];
+    const int K = mega_phase_k(t, a.H, a.F, a.qd);
+    const int nb = K / 256, rb = nb * 64, rpc = a.rpc[t];
+    uint8_t *sw = smem + a.slot_off[t];
+    float *ss = (float *)(sw + align16((size_t)rpc * rb));
+    const int total = mega_phase_rows(t, a.H, a.F, a.qd, a.kvd);
+    const int r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, total);
+    if (r0 >= r1) {
+        mbar_expect(bar, 0);
+        return;
+    }
+    if (t == 2) {  // interleaved gate|up: gate rows at slot rows [0,n), up rows at [rpc/2, rpc/2+n)
+        const int g0 = r0 >> 1, n = ((r1 + 1) >> 1) - g0;
+        mbar_expect(bar, 2u * n * (rb + nb * 4));
+        bulk_g2s(sw, ly.w[4] + (size_t)g0 * rb, n * rb, bar);
+        bulk_g2s(sw + (size_t)(rpc >> 1) * rb, ly.w[5] + (size_t)g0 * rb, n * rb, bar);
+        bulk_g2s(ss, ly.s[4] + (size_t)g0 * nb, n * nb * 4, bar);
+        bulk_g2s(ss + (size_t)(rpc >> 1) * nb, ly.s[5] + (size_t)g0 * nb, n * nb * 4, bar);
+        return;
+    }
+    mbar_expect(bar, (unsigned)(r1 - r0) * (rb + nb * 4));
+    if (t == 0) {  // merged q|k|v rows
+        const int lim[3] = {a.qd, a.qd + a.kvd, a.qd + 2 * a.kvd};
+        int base = 0;
+        for (int wi = 0; wi < 3; wi++) {
+            const int s0 = max(r0, base), s1 = min(r1, lim[wi]);
+            if (s0 < s1) {
+                bulk_g2s(sw + (size_t)(s0 - r0) * rb, ly.w[wi] + (size_t)(s0 - base) * rb, (s1 - s0) * rb, bar);
+                bulk_g2s(ss + (size_t)(s0 - r0) * nb, ly.s[wi] + (size_t)(s0 - base) * nb, (s1 - s0) * nb * 4, bar);
+            }
+            base = lim[wi];
+        }
+        return;
+    }
+    const int wi = t == 1 ? 3 : 6;
+    bulk_g2s(sw, ly.w[wi] + (size_t)r0 * rb, (r1 - r0) * rb, bar);
+    bulk_g2s(ss, ly.s[wi] + (size_t)r0 * nb, (r1 - r0) * nb * 4, bar);
+}
+
+// ---------------------------------------------------------------- activation staging
+
+// fp32 input (x, or the stage's own s.x when x == nullptr), optionally
+// RMSNorm * norm_w, then Q8_K into shared memory.  With a norm, threads
+// 0..255 hold elements i = t + 256 j exactly as the 256-thread per-layer
+// kernels do, so the sum of squares (and everything after it) is
+// bit-identical; the extra warps contribute zeros to the block reduction.
+template <int SV>
+__device__ inline void mega_stage(const float *x, const float *norm_w, float eps, int K, Q8Smem &s) {
+    const int n4 = K >> 2, tid = threadIdx.x;
+    const float4 *src = x ? (const float4 *)x : (const float4 *)s.x;
+    if (norm_w) {
+        float4 xv[SV], wv[SV];
+#pragma unroll
+        for (int j = 0; j < SV; j++) {
+            const int i = tid + j * kGemvThreads;
+            if (tid < kGemvThreads && i < n4) {
+                xv[j] = src[i];
+                wv[j] = __ldg((const float4 *)norm_w + i);
+            }
+        }
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < SV; j++) {
+            const int i = tid + j * kGemvThreads;
+            if (tid < kGemvThreads && i < n4) {
+                ss = __fadd_rn(ss, __fmul_rn(xv[j].x, xv[j].x));
+                ss = __fadd_rn(ss, __fmul_rn(xv[j].y, xv[j].y));
+                ss = __fadd_rn(ss, __fmul_rn(xv[j].z, xv[j].z));
+                ss = __fadd_rn(ss, __fmul_rn(xv[j].w, xv[j].w));
+            }
+        }
+        ss = block_sum(ss, s.red);  // also orders every read of s.x before the writes below
+        const float scale = 1.0f / sqrtf(ss / (float)K + eps);
+#pragma unroll
+        for (int j = 0; j < SV; j++) {
+            const int i = tid + j * kGemvThreads;
+            if (tid < kGemvThreads && i < n4)
+                ((float4 *)s.x)[i] = make_float4(__fmul_rn(__fmul_rn(xv[j].x, scale), wv[j].x),
+                                                 __fmul_rn(__fmul_rn(xv[j].y, scale), wv[j].y),
+                                                 __fmul_rn(__fmul_rn(xv[j].z, scale), wv[j].z),
+                                                 __fmul_rn(__fmul_rn(xv[j].w, scale), wv[j].w));
+        }
+    } else if (x) {
+        for (int i = tid; i < n4; i += kMegaThreads) ((float4 *)s.x)[i] = src[i];
+    }
+    __syncthreads();
+    const int nb = K / 256;
+    for (int b = tid >> 5; b < nb; b += kMegaWarps) quantize_block_warp(s.x, s, 0, b, nb, K);
+    __syncthreads();
+}
+
+template <int CPL>
+__device__ __forceinline__ void mega_act(const Q8Smem &s, int K, int4 (&act)[CPL][4], float (&dblk)[CPL],
+                                         int (&sblk)[CPL]) {
+    const int lane = threadIdx.x & 31, nchunk = K / 64;
+#pragma unroll
+    for (int i = 0; i < CPL; i++) {
+        const int c = lane + 32 * i;
+        if (c < nchunk) {
+#pragma unroll
+            for (int l = 0; l < 4; l++) act[i][l] = *(const int4 *)&s.qp[(size_t)l * (K / 4) + c * 16];
+            dblk[i] = s.d[c >> 2];
+            sblk[i] = s.sum[c >> 2];
+        } else {
+#pragma unroll
+            for (int l = 0; l < 4; l++) act[i][l] = make_int4(0, 0, 0, 0);
+            dblk[i] = 0.f;
+            sblk[i] = 0;
+        }
+    }
+}
+
+// ---------------------------------------------------------------- panel rows from a slot
+
+// Rows [r0, r1) of the phase's merged row space, weights from the slot (row
+// rr = r - r0 at slot row srow(rr)), RG rows per warp iteration.  Same
+// per-row arithmetic as gemv_panel_dec.  epi(r, acc[], r1) runs on lane 0.
+template <int CPL, int RG, bool INTERLEAVED, typename Epi>
+__device__ __forceinline__ void mega_rows(int shift, int off, int r0, int r1, int rpc, const uint8_t *sw,
+                                         const float *ss, int K, const int4 (&act)[CPL][4], const float (&dblk)[CPL],
+                                         const int (&sblk)[CPL], Epi epi) {
+    const int nb = K / 256, nchunk = nb * 4, rb = nb * 64;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int rg = r0 + warp * RG; rg < r1; rg += kMegaWarps * RG) {
+        float acc[RG];
+        int srow[RG];
+#pragma unroll
+        for (int g = 0; g < RG; g++) {
+            acc[g] = 0.f;
+            const int rr = rg + g - r0;
+            srow[g] = INTERLEAVED ? ((rr & 1) * (rpc >> 1) + (rr >> 1)) : rr;
+        }
+#pragma unroll
+        for (int i = 0; i < CPL; i++) {
+            const int c = lane + 32 * i;
+            int e[RG];
+#pragma unroll
+            for (int g = 0; g < RG; g++) {
+                e[g] = 0;
+                if (c < nchunk && rg + g < r1)
+                    e[g] = panel_chunk_dot4(*(const uint4 *)(sw + (size_t)srow[g] * rb + c * 16), act[i]);
+            }
+#pragma unroll
+            for (int g = 0; g < RG; g++) e[g] += __shfl_xor_sync(0xffffffffu, e[g], 1);
+#pragma unroll
+            for (int g = 0; g < RG; g++) e[g] += __shfl_xor_sync(0xffffffffu, e[g], 2);
+            if (c < nchunk && (lane & 3) == 0) {
+#pragma unroll
+                for (int g = 0; g < RG; g++) {
+                    if (rg + g >= r1) break;
+                    const int v = e[g] * (1 << shift) - off * sblk[i];
+                    acc[g] += ss[(size_t)srow[g] * nb + (c >> 2)] * dblk[i] * (float)v;
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int g = 0; g < RG; g++) acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], o);
+        if (lane == 0) epi(rg, acc, r1);
+    }
+}
+
+// ---------------------------------------------------------------- LM head (Q6_K) with argmax
+
+// Rows [r0, r1) of the relayouted Q6_K head (ql | qh | scales | d planes per
+// row), two rows per warp iteration with all loads issued first.  Per-row
+// arithmetic is gemv_q6k's; returns the warp's best argmax key (lane 0).
+__device__ inline unsigned long long mega_head_q6k(const MegaArgs &a, const Q8Smem &s, int r0, int r1) {
+    constexpr int R = 2;
+    const WDesc &w = a.head;
+    const int K = a.H, nb = K / 256, nunit = nb * 4;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    unsigned long long best = 0;
+    for (int rg = r0 + warp * R; rg < r1; rg += kMegaWarps * R) {
+        float acc[R] = {0.f, 0.f};
+        for (int u0 = 0; u0 < nunit; u0 += 32) {
+            const int u = u0 + lane;
+            const bool ok = u < nunit;
+            const int b = u >> 2, hf = (u >> 1) & 1, sg = u & 1;
+            uint4 qa[R], qb[R], qh[R], scv[R];
+            float dw[R];
+#pragma unroll
+            for (int g = 0; g < R; g++) {
+                qa[g] = qb[g] = qh[g] = scv[g] = make_uint4(0, 0, 0, 0);
+                dw[g] = 0.f;
+                if (ok && rg + g < r1) {
+                    const uint8_t *row = w.w + (size_t)(rg + g) * w.stride;
+                    qa[g] = ldg_stream(row + (size_t)b * 128 + hf * 64 + sg * 16);
+                    qb[g] = ldg_stream(row + (size_t)b * 128 + hf * 64 + 32 + sg * 16);
+                    qh[g] = ldg_stream(row + (size_t)nb * 128 + (size_t)b * 64 + hf * 32 + sg * 16);
+                    scv[g] = __ldg((const uint4 *)(row + (size_t)nb * 192 + (size_t)b * 16));
+                    dw[g] = h2f(__ldg((const unsigned short *)(row + (size_t)nb * 208) + b));
+                }
+            }
+#pragma unroll
+            for (int g = 0; g < R; g++) {
+                const int8_t *sc = (const int8_t *)&scv[g];
+                const uint32_t A[4] = {qa[g].x, qa[g].y, qa[g].z, qa[g].w}, B[4] = {qb[g].x, qb[g].y, qb[g].z, qb[g].w};
+                const uint32_t Hh[4] = {qh[g].x, qh[g].y, qh[g].z, qh[g].w};
+                int acc_i = 0;
+                if (ok) {
+#pragma unroll
+                    for (int q = 0; q < 4; q++) {
+                        const int ch = hf * 2 + (q >> 1), l = (2 * q + sg) & 3;
+                        const int4 av = *(const int4 *)&s.qp[(size_t)l * (K / 4) + (b * 4 + piece_of_chunk(ch)) * 16];
+                        uint32_t code[4];
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const uint32_t src = (q & 1) ? B[j] : A[j];
+                            code[j] = ((src >> (4 * (q >> 1))) & 0x0f0f0f0fu) | (((Hh[j] >> (2 * q)) & 0x03030303u) << 4);
+                        }
+                        int tq = dp4a((int)code[0], av.x, 0);
+                        tq = dp4a((int)code[1], av.y, tq);
+                        tq = dp4a((int)code[2], av.z, tq);
+                        tq = dp4a((int)code[3], av.w, tq);
+                        const int sub = hf * 8 + 2 * q + sg;
+                        tq -= 32 * (int)s.bs[b * 16 + sub];
+                        acc_i += (int)sc[sub] * tq;
+                    }
+                }
+                acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 1);
+                acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 2);
+                if (ok && (lane & 3) == 0) acc[g] += dw[g] * s.d[b] * (float)acc_i;
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < R; g++) {
+            const float v = warp_sum(acc[g]);
+            const int r = rg + g;
+            if (lane == 0 && r < r1 && r < a.vocab_out) {
+                const unsigned long long key = argmax_key(v, (uint32_t)r);
+                if (key > best) best = key;
+            }
+        }
+    }
+    return best;
+}
+
+// ---------------------------------------------------------------- the kernel
+
+// Launch shape contract (checked by the host): grid = number of SMs, all
+// resident (cooperative launch); kvh * ceil(ctx/kDecSplit) <= grid; every
+// layer weight a panel with (shift, off); H, qd <= 2048 (one 64-element chunk
+// per lane) and F <= 2048 * CF; head Q6_K with k == H.
+template <int HD, int G, int CF>
+__global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_constant__ MegaArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ __align__(8) uint64_t mbar[5];  // 4 weight slots + K/V rows
+    __shared__ int s_flag, s_last;
+    __shared__ unsigned long long s_best[kMegaWarps];
+    __shared__ __align__(16) float sq[G][HD];
+    __shared__ __align__(16) float skc[HD], svc[HD];
+    constexpr int KROW = HD * 2 + kMegaKPad;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    Q8Smem st = q8_smem(smem + a.stage_off, 1, a.kmax);
+    uint8_t *sK = smem + a.attn_off;
+    uint16_t *sV = (uint16_t *)(smem + a.attn_off + (size_t)kDecSplit * KROW);
+    if (tid == 0) {
+        for (int i = 0; i < 5; i++) mbar_init(&mbar[i]);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    unsigned ph[5] = {0, 0, 0, 0, 0};  // parity each mbarrier completes next
+    unsigned pending = 0;              // bit i: a fill of mbarrier i is outstanding (thread 0 / warp 0)
+    unsigned target = 0;
+    int tli = 0;
+    int tok = a.st->tok, pos = a.st->pos;
+    bool ok = true;
+    if (tid == 0) {
+        for (int t = 0; t < 4; t++) mega_fill(a, smem, &mbar[t], t, 0);
+        pending |= 0xfu;
+    }
+    for (int step = 0; step < a.steps && ok; step++) {
+        if (pos < 0 || pos >= a.ctx) {
+            if (tid == 0) raise_err(a, MEGA_ERR_POS);
+            break;
+        }
+        const int nsplit = (pos + kDecSplit) / kDecSplit;
+        const bool is_attn = blockIdx.x < a.kvh * nsplit;
+        const int akvh = blockIdx.x % a.kvh, asplit = blockIdx.x / a.kvh;
+        tl_mark(a, tli);
+        // embedding of `tok` into the stage row; CTA b also writes its slice of h
+        {
+            const int t0 = (tok < 0 || tok >= a.embd.n) ? 0 : tok;
+            for (int e = tid; e < a.H; e += kMegaThreads) st.x[e] = dequant_elem(a.embd, t0, e);
+            const int per = (a.H + gridDim.x - 1) / gridDim.x;
+            const int e0 = blockIdx.x * per, e1 = min(a.H, e0 + per);
+            for (int e = e0 + tid; e < e1; e += kMegaThreads) a.h[e] = dequant_elem(a.embd, t0, e);
+            __syncthreads();
+        }
+        for (int l = 0; l < a.L && ok; l++) {
+            const MegaLayer &ly = a.layers[l];
+            const bool more = !(l + 1 == a.L && step + 1 == a.steps);  // refill for a following layer
+            const int nl = l + 1 < a.L ? l + 1 : 0;
+            AttnArgs aa = a.attn;
+            aa.kc = ly.kc;
+            aa.vc = ly.vc;
+            aa.q_norm = ly.q_norm;
+            aa.k_norm = ly.k_norm;
+            aa.tickets = a.sync->tickets;
+            // cached K/V rows of this CTA's attention split, staged during q|k|v
+            if (is_attn && warp == 0) {
+                const int j0 = asplit * kDecSplit;
+                const int ncache = max(0, min(pos, j0 + kDecSplit) - j0);
+                asm volatile("fence.proxy.async.global;" ::: "memory");  // rows written by generic stores
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                if (lane == 0) mbar_expect(&mbar[4], (unsigned)ncache * HD * 2 * 2);
+                __syncwarp();
+                const uint16_t *Kg = ly.kc + akvh * HD, *Vg = ly.vc + akvh * HD;
+                for (int j = lane; j < ncache; j += 32) {
+                    const size_t g = (size_t)(j0 + j) * a.kvd;
+                    bulk_g2s(sK + (size_t)j * KROW, Kg + g, HD * 2, &mbar[4]);
+                    bulk_g2s(sV + (size_t)j * HD, Vg + g, HD * 2, &mbar[4]);
+                }
+                pending |= 0x10u;
+            }
+            // ---- q|k|v
+            {
+                mega_stage<2>(l == 0 ? nullptr : a.h, ly.attn_norm, a.eps, a.H, st);
+                int4 act[1][4];
+                float dblk[1];
+                int sblk[1];
+                mega_act<1>(st, a.H, act, dblk, sblk);
+                if (!mbar_wait(&mbar[0], ph[0])) { raise_err(a, MEGA_ERR_WEIGHTS); ok = false; }
+                ph[0] ^= 1;
+                pending &= ~1u;
+                const int rpc = a.rpc[0], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.qd + 2 * a.kvd);
+                const uint8_t *sw = smem + a.slot_off[0];
+                const float *ss = (const float *)(sw + align16((size_t)rpc * (a.H / 256) * 64));
+                float *qkv = a.qkv;
+                if (ok)
+                    mega_rows<1, 4, false>(a.shift, a.off, r0, r1, rpc, sw, ss, a.H, act, dblk, sblk,
+                                           [&](int rg, const float *acc, int rend) {
+#pragma unroll
+                                               for (int g = 0; g < 4; g++)
+                                                   if (rg + g < rend) qkv[rg + g] = acc[g];
+                                           });
+                __syncthreads();
+                if (tid == 0 && more) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mega_fill(a, smem, &mbar[0], 0, nl);
+                    pending |= 1u;
+                }
+            }
+            tl_mark(a, tli);
+            if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            tl_mark(a, tli);
+            if (l == 0 && blockIdx.x == 0 && tid == 0) a.sync->amax[(step + 1) & 1] = 0ull;
+            // ---- attention
+            if (is_attn && warp <= G) {
+                DecConsts<HD> kc;
+                attn_dec_consts<HD, G>(aa, pos, kc);
+                attn_dec_prologue<HD, G>(aa, akvh, pos, asplit == 0, kc, sq, skc, svc);
+                const bool kv_ok = mbar_wait(&mbar[4], ph[4]);
+                if (!kv_ok) raise_err(a, MEGA_ERR_KV);
+                asm volatile("bar.sync 1, %0;" ::"r"((G + 1) * 32) : "memory");
+                if (warp < G && kv_ok) {
+                    const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * KROW + c * 16); };
+                    attn_dec_main<HD, G>(aa, akvh, asplit, pos, krow, sV, sq, skc, svc, &s_last, 2);
+                }
+            }
+            if (is_attn) {
+                ph[4] ^= 1;
+                pending &= ~0x10u;
+            }
+            tl_mark(a, tli);
+            if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            tl_mark(a, tli);
+            // ---- o_proj (+ residual)
+            {
+                mega_stage<2>(a.ao, nullptr, a.eps, a.qd, st);
+                int4 act[1][4];
+                float dblk[1];
+                int sblk[1];
+                mega_act<1>(st, a.qd, act, dblk, sblk);
+                if (!mbar_wait(&mbar[1], ph[1])) { raise_err(a, MEGA_ERR_WEIGHTS); ok = false; }
+                ph[1] ^= 1;
+                pending &= ~2u;
+                const int rpc = a.rpc[1], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.H);
+                const uint8_t *sw = smem + a.slot_off[1];
+                const float *ss = (const float *)(sw + align16((size_t)rpc * (a.qd / 256) * 64));
+                float *h = a.h;
+                if (ok)
+                    mega_rows<1, 4, false>(a.shift, a.off, r0, r1, rpc, sw, ss, a.qd, act, dblk, sblk,
+                                           [&](int rg, const float *acc, int rend) {
+#pragma unroll
+                                               for (int g = 0; g < 4; g++)
+                                                   if (rg + g < rend) h[rg + g] += acc[g];
+                                           });
+                __syncthreads();
+                if (tid == 0 && more) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mega_fill(a, smem, &mbar[1], 1, nl);
+                    pending |= 2u;
+                }
+            }
+            tl_mark(a, tli);
+            if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            tl_mark(a, tli);
+            // ---- gate|up (interleaved rows) -> silu(gate) * up
+            {
+                mega_stage<2>(a.h, ly.ffn_norm, a.eps, a.H, st);
+                int4 act[1][4];
+                float dblk[1];
+                int sblk[1];
+                mega_act<1>(st, a.H, act, dblk, sblk);
+                if (!mbar_wait(&mbar[2], ph[2])) { raise_err(a, MEGA_ERR_WEIGHTS); ok = false; }
+                ph[2] ^= 1;
+                pending &= ~4u;
+                const int rpc = a.rpc[2], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, 2 * a.F);
+                const uint8_t *sw = smem + a.slot_off[2];
+                const float *ss = (const float *)(sw + align16((size_t)rpc * (a.H / 256) * 64));
+                float *out = a.act;
+                if (ok)
+                    mega_rows<1, 4, true>(a.shift, a.off, r0, r1, rpc, sw, ss, a.H, act, dblk, sblk,
+                                          [&](int rg, const float *acc, int rend) {
+#pragma unroll
+                                              for (int g = 0; g + 1 < 4; g += 2) {
+                                                  if (rg + g + 1 >= rend) break;
+                                                  const float gt = acc[g], up = acc[g + 1];
+                                                  out[(rg + g) >> 1] = __fmul_rn(gt / (1.0f + expf(-gt)), up);
+                                              }
+                                          });
+                __syncthreads();
+                if (tid == 0 && more) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mega_fill(a, smem, &mbar[2], 2, nl);
+                    pending |= 4u;
+                }
+            }
+            tl_mark(a, tli);
+            if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            tl_mark(a, tli);
+            // ---- down (+ residual)
+            {
+                mega_stage<2 * CF>(a.act, nullptr, a.eps, a.F, st);
+                int4 act[CF][4];
+                float dblk[CF];
+                int sblk[CF];
+                mega_act<CF>(st, a.F, act, dblk, sblk);
+                if (!mbar_wait(&mbar[3], ph[3])) { raise_err(a, MEGA_ERR_WEIGHTS); ok = false; }
+                ph[3] ^= 1;
+                pending &= ~8u;
+                const int rpc = a.rpc[3], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.H);
+                const uint8_t *sw = smem + a.slot_off[3];
+                const float *ss = (const float *)(sw + align16((size_t)rpc * (a.F / 256) * 64));
+                float *h = a.h;
+                constexpr int RGD = CF == 1 ? 4 : 2;
+                if (ok)
+                    mega_rows<CF, RGD, false>(a.shift, a.off, r0, r1, rpc, sw, ss, a.F, act, dblk, sblk,
+                                              [&](int rg, const float *acc, int rend) {
+#pragma unroll
+                                                  for (int g = 0; g < RGD; g++)
+                                                      if (rg + g < rend) h[rg + g] += acc[g];
+                                              });
+                __syncthreads();
+                if (tid == 0 && more) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mega_fill(a, smem, &mbar[3], 3, nl);
+                    pending |= 8u;
+                }
+            }
+            tl_mark(a, tli);
+            if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            tl_mark(a, tli);
+        }
+        if (!ok) break;
+        // ---- LM head + argmax (rows < vocab_out compete)
+        {
+            mega_stage<2>(a.h, a.out_norm, a.eps, a.H, st);
+            const int rpc = a.rpc[4], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.head.n);
+            const unsigned long long best = mega_head_q6k(a, st, r0, r1);
+            if (lane == 0) s_best[warp] = best;
+            __syncthreads();
+            if (tid == 0) {
+                unsigned long long m = 0;
+                for (int i = 0; i < kMegaWarps; i++) m = s_best[i] > m ? s_best[i] : m;
+                if (m) atomicMax(&a.sync->amax[step & 1], m);
+            }
+        }
+        tl_mark(a, tli);
+        if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+        tl_mark(a, tli);
+        // ---- token bookkeeping (decode_finalize's rules), in every CTA
+        {
+            const unsigned long long key = *(volatile unsigned long long *)&a.sync->amax[step & 1];
+            const int idx = key ? (int)argmax_index(key) : 0;
+            if (blockIdx.x == 0 && tid == 0) {
+                DecodeState *ds = a.st;
+                if (!ds->stopped) {
+                    if (ds->step < ds->cap) a.out_ids[ds->step] = idx;
+                    ds->step++;
+                    for (int i = 0; i < ds->n_stop; i++)
+                        if (ds->stop_ids[i] == idx) ds->stopped = 1;
+                }
+            }
+            tok = idx;
+            pos += 1;
+        }
+    }
+    if (blockIdx.x == 0 && tid == 0) {
+        a.st->tok = tok;
+        a.st->pos = pos;
+        a.st->amax = 0ull;
+    }
+    // copies still in flight into this CTA's shared memory (error exits)
+    if (tid == 0) {
+        for (int i = 0; i < 4; i++)
+            if (pending & (1u << i)) mbar_wait(&mbar[i], ph[i]);
+    }
+    if (warp == 0 && (pending & 0x10u)) mbar_wait(&mbar[4], ph[4]);
+    __syncthreads();
+}
+
+// Dynamic shared memory plan of decode_mega for a model shape.
+struct MegaPlan {
+    int rpc[5], slot_off[4], stage_off, attn_off, kmax;
+    size_t bytes;
+};
+
+inline MegaPlan mega_plan(int grid, int H, int F, int qd, int kvd, int vocab, int HD) {
+    MegaPlan p;
+    size_t off = 0;
+    for (int t = 0; t < 4; t++) {
+        const int rows = mega_phase_rows(t, H, F, qd, kvd);
+        int r = (rows + grid - 1) / grid;
+        r = (r + kMegaRowAlign - 1) / kMegaRowAlign * kMegaRowAlign;
+        p.rpc[t] = r;
+        p.slot_off[t] = (int)off;
+        off += (size_t)mega_slot_bytes(r, mega_phase_k(t, H, F, qd));
+    }
+    p.rpc[4] = (vocab + grid - 1) / grid;
+    p.kmax = H > F ? H : F;
+    if (qd > p.kmax) p.kmax = qd;
+    p.stage_off = (int)off;
+    off += align16(q8_smem_bytes(1, p.kmax));
+    p.attn_off = (int)off;
+    off += (size_t)kDecSplit * (HD * 2 + kMegaKPad) + (size_t)kDecSplit * HD * 2;
+    p.bytes = off;
+    return p;
+}
+
+}  // namespace hyk

@@ -76,7 +76,10 @@ HYC_API int hyc_generate(void *impl, const int *prompt, int n, int keep, int max
 /* Lower-level decode control used by hyc_generate and the benchmark:
  *  hyc_decode_begin: prefill like hyc_generate and leave the first generated
  *    token on the device (no synchronisation);
- *  hyc_decode_steps: enqueue `steps` single-token decode graphs;
+ *  hyc_decode_steps: enqueue `steps` greedy single-token steps (one
+ *    persistent kernel launch when hyc_set_decode_mode selected it and the
+ *    model supports it, else one graph per step; both give bit-identical
+ *    results);
  *  hyc_decode_steps_host: the same, but every step's input token is copied
  *    from pinned host memory tok_io[s] and its result written back to
  *    tok_io[s+1] (tok_io must hold steps+1 ints, allocated with
@@ -93,6 +96,14 @@ HYC_API int hyc_decode_read(void *impl, int *out_ids, int cap);
 HYC_API int hyc_decode_rewind(void *impl, int pos, int tok);
 HYC_API void *hyc_host_alloc(size_t bytes);
 HYC_API void hyc_host_free(void *p);
+/* Decode path selection (no reference counterpart; the reference's host
+ * loop is src/model.c:914-958): mode 0 uses the persistent kernel whenever
+ * the prepared model supports it (panel layer weights, Q6_K head), mode 1
+ * always the graph of per-layer launches.  hyc_decode_path returns 1 when
+ * the next decode steps run the persistent kernel, 0 for the graph, and
+ * writes the reason. */
+HYC_API int hyc_set_decode_mode(void *impl, int mode);
+HYC_API int hyc_decode_path(void *impl, char *why, int cap);
 
 /* ---- kernel-level hooks for parity tests (host buffers, synchronous) -- */
 
@@ -132,6 +143,10 @@ HYC_API int hyc_debug_buffer(void *impl, int which, float *out, size_t count);
  * CTA 0 at its wait and its end; returns the number of slots in use. */
 HYC_API int hyc_trace(void *impl, int on);
 HYC_API int hyc_trace_read(void *impl, unsigned long long *out, int max_slots);
+/* Persistent decode kernel timeline of the last launch made while tracing:
+ * %globaltimer of block 0 at each step start and before/after every grid
+ * barrier (per step: 1 + 10 per layer + 2 stamps).  Returns stamps copied. */
+HYC_API int hyc_mega_timeline(void *impl, unsigned long long *out, int cap);
 /* bf16 KV rows [0, npos) of one layer of the fused cache. */
 HYC_API int hyc_kv_read(void *impl, int layer, int npos, uint16_t *k, uint16_t *v);
 /* RoPE tables exactly as the host loader computes them (src/model.c:537,576-586). */
