@@ -145,6 +145,15 @@ __device__ __forceinline__ bool grid_sync(const MegaArgs &a, unsigned &target, i
     return *s_flag == 0;
 }
 
+// Every thread of the CTA waits for slot `bar`; the outcome is made uniform
+// across the CTA (a timeout seen by any thread fails the whole CTA), so no
+// warp can diverge into a collective the others skip.
+__device__ __forceinline__ bool mega_slot_ready(const MegaArgs &a, uint64_t *bar, unsigned parity) {
+    const bool ready = __syncthreads_and(mbar_wait(bar, parity)) != 0;
+    if (!ready && threadIdx.x == 0) raise_err(a, MEGA_ERR_WEIGHTS);
+    return ready;
+}
+
 __device__ __forceinline__ void tl_mark(const MegaArgs &a, int &idx) {
     if (a.tl && blockIdx.x == 0 && threadIdx.x == 0 && idx < a.tl_cap) a.tl[idx] = gtimer();
     idx++;
@@ -412,7 +421,7 @@ template <int HD, int G, int CF>
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_constant__ MegaArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ __align__(8) uint64_t mbar[5];  // 4 weight slots + K/V rows
-    __shared__ int s_flag, s_last;
+    __shared__ int s_flag, s_last, s_kvbad;
     __shared__ unsigned long long s_best[kMegaWarps];
     __shared__ __align__(16) float sq[G][HD];
     __shared__ __align__(16) float skc[HD], svc[HD];
@@ -422,6 +431,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     uint8_t *sK = smem + a.attn_off;
     uint16_t *sV = (uint16_t *)(smem + a.attn_off + (size_t)kDecSplit * KROW);
     if (tid == 0) {
+        s_kvbad = 0;
         for (int i = 0; i < 5; i++) mbar_init(&mbar[i]);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -487,9 +497,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 float dblk[1];
                 int sblk[1];
                 mega_act<1>(st, a.H, act, dblk, sblk);
-                if (!mbar_wait(&mbar[0], ph[0])) { raise_err(a, MEGA_ERR_WEIGHTS); ok = false; }
-                ph[0] ^= 1;
-                pending &= ~1u;
+                if (mega_slot_ready(a, &mbar[0], ph[0])) {
+                    ph[0] ^= 1;
+                    pending &= ~1u;
+                } else {
+                    ok = false;
+                }
                 const int rpc = a.rpc[0], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.qd + 2 * a.kvd);
                 const uint8_t *sw = smem + a.slot_off[0];
                 const float *ss = (const float *)(sw + align16((size_t)rpc * (a.H / 256) * 64));
@@ -502,7 +515,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                                                    if (rg + g < rend) qkv[rg + g] = acc[g];
                                            });
                 __syncthreads();
-                if (tid == 0 && more) {
+                if (tid == 0 && more && ok) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     mega_fill(a, smem, &mbar[0], 0, nl);
                     pending |= 1u;
@@ -517,17 +530,22 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 DecConsts<HD> kc;
                 attn_dec_consts<HD, G>(aa, pos, kc);
                 attn_dec_prologue<HD, G>(aa, akvh, pos, asplit == 0, kc, sq, skc, svc);
-                const bool kv_ok = mbar_wait(&mbar[4], ph[4]);
-                if (!kv_ok) raise_err(a, MEGA_ERR_KV);
-                asm volatile("bar.sync 1, %0;" ::"r"((G + 1) * 32) : "memory");
-                if (warp < G && kv_ok) {
+                if (!mbar_wait(&mbar[4], ph[4])) {
+                    s_kvbad = 1;
+                    raise_err(a, MEGA_ERR_KV);
+                }
+                asm volatile("bar.sync 1, %0;" ::"r"((G + 1) * 32) : "memory");  // s_kvbad now uniform
+                if (warp < G && !s_kvbad) {
                     const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * KROW + c * 16); };
                     attn_dec_main<HD, G>(aa, akvh, asplit, pos, krow, sV, sq, skc, svc, &s_last, 2);
                 }
             }
             if (is_attn) {
-                ph[4] ^= 1;
-                pending &= ~0x10u;
+                __syncthreads();  // s_kvbad visible to every warp
+                if (!s_kvbad) {
+                    ph[4] ^= 1;
+                    pending &= ~0x10u;
+                }
             }
             tl_mark(a, tli);
             if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
@@ -539,9 +557,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 float dblk[1];
                 int sblk[1];
                 mega_act<1>(st, a.qd, act, dblk, sblk);
-                if (!mbar_wait(&mbar[1], ph[1])) { raise_err(a, MEGA_ERR_WEIGHTS); ok = false; }
-                ph[1] ^= 1;
-                pending &= ~2u;
+                if (mega_slot_ready(a, &mbar[1], ph[1])) {
+                    ph[1] ^= 1;
+                    pending &= ~2u;
+                } else {
+                    ok = false;
+                }
                 const int rpc = a.rpc[1], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.H);
                 const uint8_t *sw = smem + a.slot_off[1];
                 const float *ss = (const float *)(sw + align16((size_t)rpc * (a.qd / 256) * 64));
@@ -554,7 +575,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                                                    if (rg + g < rend) h[rg + g] += acc[g];
                                            });
                 __syncthreads();
-                if (tid == 0 && more) {
+                if (tid == 0 && more && ok) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     mega_fill(a, smem, &mbar[1], 1, nl);
                     pending |= 2u;
@@ -570,9 +591,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 float dblk[1];
                 int sblk[1];
                 mega_act<1>(st, a.H, act, dblk, sblk);
-                if (!mbar_wait(&mbar[2], ph[2])) { raise_err(a, MEGA_ERR_WEIGHTS); ok = false; }
-                ph[2] ^= 1;
-                pending &= ~4u;
+                if (mega_slot_ready(a, &mbar[2], ph[2])) {
+                    ph[2] ^= 1;
+                    pending &= ~4u;
+                } else {
+                    ok = false;
+                }
                 const int rpc = a.rpc[2], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, 2 * a.F);
                 const uint8_t *sw = smem + a.slot_off[2];
                 const float *ss = (const float *)(sw + align16((size_t)rpc * (a.H / 256) * 64));
@@ -588,7 +612,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                                               }
                                           });
                 __syncthreads();
-                if (tid == 0 && more) {
+                if (tid == 0 && more && ok) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     mega_fill(a, smem, &mbar[2], 2, nl);
                     pending |= 4u;
@@ -604,9 +628,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 float dblk[CF];
                 int sblk[CF];
                 mega_act<CF>(st, a.F, act, dblk, sblk);
-                if (!mbar_wait(&mbar[3], ph[3])) { raise_err(a, MEGA_ERR_WEIGHTS); ok = false; }
-                ph[3] ^= 1;
-                pending &= ~8u;
+                if (mega_slot_ready(a, &mbar[3], ph[3])) {
+                    ph[3] ^= 1;
+                    pending &= ~8u;
+                } else {
+                    ok = false;
+                }
                 const int rpc = a.rpc[3], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.H);
                 const uint8_t *sw = smem + a.slot_off[3];
                 const float *ss = (const float *)(sw + align16((size_t)rpc * (a.F / 256) * 64));
@@ -620,7 +647,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                                                       if (rg + g < rend) h[rg + g] += acc[g];
                                               });
                 __syncthreads();
-                if (tid == 0 && more) {
+                if (tid == 0 && more && ok) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     mega_fill(a, smem, &mbar[3], 3, nl);
                     pending |= 8u;
