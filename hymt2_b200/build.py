@@ -20,7 +20,7 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompil
               "-Xcompiler", "-Wall"]
 CSRC = os.path.join(_paths.PKG, "csrc")
 SOURCES = ["hy_backend.cu"]
-HEADERS = ["hy_common.cuh", "hy_gemv.cuh", "hy_attn.cuh", "hy_misc.cuh"]
+HEADERS = sorted(f for f in os.listdir(CSRC) if f.endswith(".cuh"))  # every header the sources include
 
 
 def _nvcc() -> str:

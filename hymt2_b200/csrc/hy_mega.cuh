@@ -154,9 +154,19 @@ __device__ __forceinline__ bool mega_slot_ready(const MegaArgs &a, uint64_t *bar
     return ready;
 }
 
+// Timeline (debug, a.tl non-null): [0, cap/2) phase edges of block 0;
+// [cap/2, cap/2 + 8192) sub-phase marks of block 0; then per-CTA marks of
+// one chosen (step, layer): 16 slots per CTA.
 __device__ __forceinline__ void tl_mark(const MegaArgs &a, int &idx) {
-    if (a.tl && blockIdx.x == 0 && threadIdx.x == 0 && idx < a.tl_cap) a.tl[idx] = gtimer();
+    if (a.tl && blockIdx.x == 0 && threadIdx.x == 0 && idx < a.tl_cap / 2) a.tl[idx] = gtimer();
     idx++;
+}
+__device__ __forceinline__ void tl_sub(const MegaArgs &a, int &idx) {
+    if (a.tl && blockIdx.x == 0 && threadIdx.x == 0 && idx < 8192) a.tl[a.tl_cap / 2 + idx] = gtimer();
+    idx++;
+}
+__device__ __forceinline__ void tl_cta(const MegaArgs &a, bool on, int slot) {
+    if (a.tl && on && threadIdx.x == 0) a.tl[a.tl_cap / 2 + 8192 + blockIdx.x * 16 + slot] = gtimer();
 }
 
 // ---------------------------------------------------------------- weight slots
@@ -439,7 +449,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     unsigned ph[5] = {0, 0, 0, 0, 0};  // parity each mbarrier completes next
     unsigned pending = 0;              // bit i: a fill of mbarrier i is outstanding (thread 0 / warp 0)
     unsigned target = 0;
-    int tli = 0;
+    int tli = 0, tls = 0;
     int tok = a.st->tok, pos = a.st->pos;
     bool ok = true;
     if (tid == 0) {
@@ -493,6 +503,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             // ---- q|k|v
             {
                 mega_stage<2>(l == 0 ? nullptr : a.h, ly.attn_norm, a.eps, a.H, st);
+                tl_sub(a, tls);
                 int4 act[1][4];
                 float dblk[1];
                 int sblk[1];
@@ -503,6 +514,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 } else {
                     ok = false;
                 }
+                tl_sub(a, tls);
                 const int rpc = a.rpc[0], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.qd + 2 * a.kvd);
                 const uint8_t *sw = smem + a.slot_off[0];
                 const float *ss = (const float *)(sw + align16((size_t)rpc * (a.H / 256) * 64));
@@ -514,6 +526,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                                                for (int g = 0; g < 4; g++)
                                                    if (rg + g < rend) qkv[rg + g] = acc[g];
                                            });
+                tl_sub(a, tls);
                 __syncthreads();
                 if (tid == 0 && more && ok) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -522,7 +535,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 }
             }
             tl_mark(a, tli);
+            tl_cta(a, step == 1 && l == 5, 0);
             if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            tl_cta(a, step == 1 && l == 5, 1);
             tl_mark(a, tli);
             if (l == 0 && blockIdx.x == 0 && tid == 0) a.sync->amax[(step + 1) & 1] = 0ull;
             // ---- attention
@@ -530,15 +545,18 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 DecConsts<HD> kc;
                 attn_dec_consts<HD, G>(aa, pos, kc);
                 attn_dec_prologue<HD, G>(aa, akvh, pos, asplit == 0, kc, sq, skc, svc);
+                tl_sub(a, tls);
                 if (!mbar_wait(&mbar[4], ph[4])) {
                     s_kvbad = 1;
                     raise_err(a, MEGA_ERR_KV);
                 }
                 asm volatile("bar.sync 1, %0;" ::"r"((G + 1) * 32) : "memory");  // s_kvbad now uniform
+                tl_sub(a, tls);
                 if (warp < G && !s_kvbad) {
                     const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * KROW + c * 16); };
                     attn_dec_main<HD, G>(aa, akvh, asplit, pos, krow, sV, sq, skc, svc, &s_last, 2);
                 }
+                tl_sub(a, tls);
             }
             if (is_attn) {
                 __syncthreads();  // s_kvbad visible to every warp
@@ -548,11 +566,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 }
             }
             tl_mark(a, tli);
+            tl_cta(a, step == 1 && l == 5, 2);
             if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            tl_cta(a, step == 1 && l == 5, 3);
             tl_mark(a, tli);
             // ---- o_proj (+ residual)
             {
                 mega_stage<2>(a.ao, nullptr, a.eps, a.qd, st);
+                tl_sub(a, tls);
                 int4 act[1][4];
                 float dblk[1];
                 int sblk[1];
@@ -563,6 +584,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 } else {
                     ok = false;
                 }
+                tl_sub(a, tls);
                 const int rpc = a.rpc[1], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.H);
                 const uint8_t *sw = smem + a.slot_off[1];
                 const float *ss = (const float *)(sw + align16((size_t)rpc * (a.qd / 256) * 64));
@@ -574,6 +596,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                                                for (int g = 0; g < 4; g++)
                                                    if (rg + g < rend) h[rg + g] += acc[g];
                                            });
+                tl_sub(a, tls);
                 __syncthreads();
                 if (tid == 0 && more && ok) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -582,11 +605,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 }
             }
             tl_mark(a, tli);
+            tl_cta(a, step == 1 && l == 5, 4);
             if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            tl_cta(a, step == 1 && l == 5, 5);
             tl_mark(a, tli);
             // ---- gate|up (interleaved rows) -> silu(gate) * up
             {
                 mega_stage<2>(a.h, ly.ffn_norm, a.eps, a.H, st);
+                tl_sub(a, tls);
                 int4 act[1][4];
                 float dblk[1];
                 int sblk[1];
@@ -597,6 +623,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 } else {
                     ok = false;
                 }
+                tl_sub(a, tls);
                 const int rpc = a.rpc[2], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, 2 * a.F);
                 const uint8_t *sw = smem + a.slot_off[2];
                 const float *ss = (const float *)(sw + align16((size_t)rpc * (a.H / 256) * 64));
@@ -611,6 +638,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                                                   out[(rg + g) >> 1] = __fmul_rn(gt / (1.0f + expf(-gt)), up);
                                               }
                                           });
+                tl_sub(a, tls);
                 __syncthreads();
                 if (tid == 0 && more && ok) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -619,11 +647,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 }
             }
             tl_mark(a, tli);
+            tl_cta(a, step == 1 && l == 5, 6);
             if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            tl_cta(a, step == 1 && l == 5, 7);
             tl_mark(a, tli);
             // ---- down (+ residual)
             {
                 mega_stage<2 * CF>(a.act, nullptr, a.eps, a.F, st);
+                tl_sub(a, tls);
                 int4 act[CF][4];
                 float dblk[CF];
                 int sblk[CF];
@@ -634,6 +665,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 } else {
                     ok = false;
                 }
+                tl_sub(a, tls);
                 const int rpc = a.rpc[3], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.H);
                 const uint8_t *sw = smem + a.slot_off[3];
                 const float *ss = (const float *)(sw + align16((size_t)rpc * (a.F / 256) * 64));
@@ -646,6 +678,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                                                   for (int g = 0; g < RGD; g++)
                                                       if (rg + g < rend) h[rg + g] += acc[g];
                                               });
+                tl_sub(a, tls);
                 __syncthreads();
                 if (tid == 0 && more && ok) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -654,7 +687,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 }
             }
             tl_mark(a, tli);
+            tl_cta(a, step == 1 && l == 5, 8);
             if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            tl_cta(a, step == 1 && l == 5, 9);
             tl_mark(a, tli);
         }
         if (!ok) break;
