@@ -273,92 +273,108 @@ __device__ __forceinline__ void attn_dec_prologue(const AttnArgs &a, int kvh, in
     }
 }
 
-// Warps 0..G-1 (query head kvh*G + w): scores over keys [j0, j1), softmax,
-// p.V, then either the final output (one split) or this split's partial and,
-// in the last split CTA to finish, the log-sum-exp merge.  krow(j, c) is the
-// 16-byte chunk c of cached K row j in shared memory, sV[j][HD] the V rows.
-// Synchronises the G head warps with named barrier `bar_id`.
+// Decode attention uses kDecWarps warps per (KV head, split): warp w takes
+// query head kvh*G + (w % G) and the key subset sub = w / G, one key per lane
+// (keys j0 + sub*32 + lane + k*32*NSUB), so every warp runs a short chain:
+// one dot product per key, a warp softmax over its keys, and p.V over its 32
+// (or 64) keys.  The NSUB partials of a head are then merged with the
+// log-sum-exp rule, and splits of long contexts are merged by the last CTA
+// of the KV head to finish.
+constexpr int kDecWarps = 16;
+
+template <int HD>
+struct DecScratch {
+    float pm[kDecWarps], pl[kDecWarps];
+    float po[kDecWarps][HD];
+    int last;
+};
+
+// All kDecWarps warps: scores over keys [j0, j1) of this split, softmax, p.V,
+// warp partials merged per head, then either the final output (one split) or
+// this split's partial and, in the last split CTA to finish, the merge.
+// krow(j, c) is the 16-byte chunk c of cached K row j in shared memory,
+// sV[j][HD] the V rows; key `pos` comes from skc/svc.  Synchronises the
+// kDecWarps warps with named barrier `bar_id` and the G head warps with
+// `bar_id + 1`.
 template <int HD, int G, typename KRow>
 __device__ __forceinline__ void attn_dec_main(const AttnArgs &a, int kvh, int split, int pos, KRow krow,
                                               const uint16_t *sV, const float (*sq)[HD], const float *skc,
-                                              const float *svc, int *last, int bar_id) {
+                                              const float *svc, DecScratch<HD> &S, int bar_id) {
     constexpr int CH = HD / 8;    // 16-byte chunks per row
     constexpr int DPL = HD / 32;  // output dims per lane (contiguous)
+    constexpr int NSUB = kDecWarps / G;
+    constexpr int KPW = (kDecSplit + NSUB * 32 - 1) / (NSUB * 32);  // keys per lane
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int j0 = split * kDecSplit, j1 = min(pos + 1, j0 + kDecSplit);
-    // scores: warp w = head, lane handles keys j0 + lane + 32 i; each 8-dim q
-    // chunk is read once and applied to all of the lane's keys
-    constexpr int KPL = kDecSplit / 32;
-    float acc[KPL];
-#pragma unroll
-    for (int i = 0; i < KPL; i++) acc[i] = 0.f;
-    const int nk = j1 - j0;
-#pragma unroll 2
-    for (int c = 0; c < CH; c++) {
-        const float4 qa = *(const float4 *)&sq[w][c * 8], qb = *(const float4 *)&sq[w][c * 8 + 4];
-        const float qf[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
-#pragma unroll
-        for (int i = 0; i < KPL; i++) {
-            const int j = lane + 32 * i;
-            if (32 * i >= nk) break;
-            if (j < nk && j0 + j != pos) {
-                const uint4 kk = *krow(j, c);
-                const uint32_t kw[4] = {kk.x, kk.y, kk.z, kk.w};
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    acc[i] = fmaf(qf[2 * q], bf16_bits_to_f32(kw[q] & 0xffffu), acc[i]);
-                    acc[i] = fmaf(qf[2 * q + 1], bf16_bits_to_f32(kw[q] >> 16), acc[i]);
-                }
-            }
-        }
-    }
-    float sc[KPL];
+    const int hh = w % G, sub = w / G;
+    const int j0 = split * kDecSplit, j1 = min(pos + 1, j0 + kDecSplit), nk = j1 - j0;
+    float s[KPW];
     float mx = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < KPL; i++) {
-        const int j = lane + 32 * i;
-        float s = -INFINITY;
+    for (int k = 0; k < KPW; k++) {
+        const int j = sub * 32 + lane + k * NSUB * 32;
+        s[k] = -INFINITY;
         if (j < nk) {
-            float dot = acc[i];
+            float dot = 0.f;
             if (j0 + j == pos) {
-                dot = 0.f;
-#pragma unroll 8
-                for (int d = 0; d < HD; d++) dot = fmaf(sq[w][d], skc[d], dot);
+#pragma unroll 4
+                for (int c = 0; c < CH; c++) {
+                    const float4 qa = *(const float4 *)&sq[hh][c * 8], qb = *(const float4 *)&sq[hh][c * 8 + 4];
+                    const float4 ka = *(const float4 *)&skc[c * 8], kb = *(const float4 *)&skc[c * 8 + 4];
+                    dot = fmaf(qa.x, ka.x, dot);
+                    dot = fmaf(qa.y, ka.y, dot);
+                    dot = fmaf(qa.z, ka.z, dot);
+                    dot = fmaf(qa.w, ka.w, dot);
+                    dot = fmaf(qb.x, kb.x, dot);
+                    dot = fmaf(qb.y, kb.y, dot);
+                    dot = fmaf(qb.z, kb.z, dot);
+                    dot = fmaf(qb.w, kb.w, dot);
+                }
+            } else {
+#pragma unroll 4
+                for (int c = 0; c < CH; c++) {
+                    const float4 qa = *(const float4 *)&sq[hh][c * 8], qb = *(const float4 *)&sq[hh][c * 8 + 4];
+                    const uint4 kk = *krow(j, c);
+                    dot = fmaf(qa.x, bf16_bits_to_f32(kk.x & 0xffffu), dot);
+                    dot = fmaf(qa.y, bf16_bits_to_f32(kk.x >> 16), dot);
+                    dot = fmaf(qa.z, bf16_bits_to_f32(kk.y & 0xffffu), dot);
+                    dot = fmaf(qa.w, bf16_bits_to_f32(kk.y >> 16), dot);
+                    dot = fmaf(qb.x, bf16_bits_to_f32(kk.z & 0xffffu), dot);
+                    dot = fmaf(qb.y, bf16_bits_to_f32(kk.z >> 16), dot);
+                    dot = fmaf(qb.z, bf16_bits_to_f32(kk.w & 0xffffu), dot);
+                    dot = fmaf(qb.w, bf16_bits_to_f32(kk.w >> 16), dot);
+                }
             }
-            s = dot * a.scale;
+            s[k] = dot * a.scale;
         }
-        sc[i] = s;
-        mx = fmaxf(mx, s);
+        mx = fmaxf(mx, s[k]);
     }
     mx = warp_max(mx);
     float l = 0.f;
 #pragma unroll
-    for (int i = 0; i < KPL; i++) {
-        sc[i] = (lane + 32 * i < nk) ? expf(sc[i] - mx) : 0.f;
-        l += sc[i];
+    for (int k = 0; k < KPW; k++) {
+        s[k] = (sub * 32 + lane + k * NSUB * 32 < nk) ? expf(s[k] - mx) : 0.f;
+        l += s[k];
     }
     l = warp_sum(l);
-    // o[d], d = lane*DPL + q: sum_j p_j v_j, four keys per step
     float o[DPL];
 #pragma unroll
     for (int q = 0; q < DPL; q++) o[q] = 0.f;
 #pragma unroll
-    for (int i = 0; i < KPL; i++) {
-        const int base = 32 * i;
-        if (base >= nk) break;
+    for (int k = 0; k < KPW; k++) {
+        const int base = sub * 32 + k * NSUB * 32;
         const int lim = min(32, nk - base);
         int jj = 0;
         for (; jj + 4 <= lim; jj += 4) {
             float p[4], vv[4][DPL];
 #pragma unroll
             for (int u = 0; u < 4; u++) {
-                p[u] = __shfl_sync(0xffffffffu, sc[i], jj + u);
-                const int jg = j0 + base + jj + u;
-                if (jg == pos) {
+                p[u] = __shfl_sync(0xffffffffu, s[k], jj + u);
+                const int jr = base + jj + u;
+                if (j0 + jr == pos) {
 #pragma unroll
                     for (int q = 0; q < DPL; q++) vv[u][q] = svc[lane * DPL + q];
                 } else {
-                    const uint16_t *vr = sV + (size_t)(base + jj + u) * HD + lane * DPL;
+                    const uint16_t *vr = sV + (size_t)jr * HD + lane * DPL;
                     if (DPL == 4) {
                         const uint2 x = *(const uint2 *)vr;
                         vv[u][0] = bf16_bits_to_f32(x.x & 0xffffu);
@@ -377,36 +393,58 @@ __device__ __forceinline__ void attn_dec_main(const AttnArgs &a, int kvh, int sp
                 for (int q = 0; q < DPL; q++) o[q] = fmaf(p[u], vv[u][q], o[q]);
         }
         for (; jj < lim; jj++) {
-            const float p = __shfl_sync(0xffffffffu, sc[i], jj);
-            const int jg = j0 + base + jj;
+            const float p = __shfl_sync(0xffffffffu, s[k], jj);
+            const int jr = base + jj;
 #pragma unroll
             for (int q = 0; q < DPL; q++) {
-                const float vq = jg == pos ? svc[lane * DPL + q] : bf16_bits_to_f32(sV[(size_t)(base + jj) * HD + lane * DPL + q]);
+                const float vq = j0 + jr == pos ? svc[lane * DPL + q] : bf16_bits_to_f32(sV[(size_t)jr * HD + lane * DPL + q]);
                 o[q] = fmaf(p, vq, o[q]);
             }
         }
     }
+    if (lane == 0) {
+        S.pm[w] = sub * 32 < nk ? mx : -INFINITY;
+        S.pl[w] = sub * 32 < nk ? l : 0.f;
+    }
+#pragma unroll
+    for (int q = 0; q < DPL; q++) S.po[w][lane * DPL + q] = o[q];
+    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(kDecWarps * 32) : "memory");
+    if (w >= G) return;
+    // warp w < G: head kvh*G + w merges its NSUB key subsets
+    float M = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < NSUB; u++) M = fmaxf(M, S.pm[w + u * G]);
+    float L = 0.f, O[DPL];
+#pragma unroll
+    for (int q = 0; q < DPL; q++) O[q] = 0.f;
+#pragma unroll
+    for (int u = 0; u < NSUB; u++) {
+        const int src = w + u * G;
+        const float f = S.pl[src] > 0.f ? expf(S.pm[src] - M) : 0.f;
+        L = fmaf(S.pl[src], f, L);
+#pragma unroll
+        for (int q = 0; q < DPL; q++) O[q] = fmaf(S.po[src][lane * DPL + q], f, O[q]);
+    }
     const int h = kvh * G + w;
     const int nsplit = (pos + kDecSplit) / kDecSplit;
     if (nsplit == 1) {
-        const float inv = 1.0f / l;
+        const float inv = 1.0f / L;
 #pragma unroll
-        for (int q = 0; q < DPL; q++) a.ao[h * HD + lane * DPL + q] = o[q] * inv;
+        for (int q = 0; q < DPL; q++) a.ao[h * HD + lane * DPL + q] = O[q] * inv;
         return;
     }
     float *pp = a.part + (((size_t)kvh * a.max_splits + split) * G + w) * (HD + 2);
 #pragma unroll
-    for (int q = 0; q < DPL; q++) pp[2 + lane * DPL + q] = o[q];
+    for (int q = 0; q < DPL; q++) pp[2 + lane * DPL + q] = O[q];
     if (lane == 0) {
-        pp[0] = mx;
-        pp[1] = l;
+        pp[0] = M;
+        pp[1] = L;
     }
     __threadfence();
-    // only the G head warps take part: named barrier over G*32 threads
-    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(G * 32) : "memory");
-    if (threadIdx.x == 0) *last = atomicAdd(&a.tickets[kvh], 1) == nsplit - 1;
-    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(G * 32) : "memory");
-    if (!*last) return;
+    asm volatile("bar.sync %0, %1;" ::"r"(bar_id + 1), "r"(G * 32) : "memory");
+    if (threadIdx.x == 0) S.last = atomicAdd(&a.tickets[kvh], 1) == nsplit - 1;
+    asm volatile("bar.sync %0, %1;" ::"r"(bar_id + 1), "r"(G * 32) : "memory");
+    if (!S.last) return;
     __threadfence();
     float MM = -INFINITY;
     for (int sp = 0; sp < nsplit; sp++)
@@ -427,18 +465,18 @@ __device__ __forceinline__ void attn_dec_main(const AttnArgs &a, int kvh, int sp
     if (threadIdx.x == 0) a.tickets[kvh] = 0;
 }
 
-// The per-layer kernel: K rows are staged with their 16-byte chunks rotated
-// by the row index so lanes reading 32 different rows hit different banks;
-// the copies are issued BEFORE griddepcontrol.wait (the cached rows were
-// written at least two kernels back).
+// The per-layer kernel (kDecWarps warps): K rows are staged with their
+// 16-byte chunks rotated by the row index so lanes reading different rows hit
+// different banks; the copies are issued BEFORE griddepcontrol.wait (the
+// cached rows were written at least two kernels back).
 template <int HD, int G>
-__global__ void __launch_bounds__((G + 1) * 32) attn_decode2(const __grid_constant__ AttnArgs a) {
+__global__ void __launch_bounds__(kDecWarps * 32) attn_decode2(const __grid_constant__ AttnArgs a) {
     extern __shared__ __align__(16) uint8_t dsm[];
     uint16_t *sK = (uint16_t *)dsm;                       // [kDecSplit][HD] rotated chunks
     uint16_t *sV = sK + (size_t)kDecSplit * HD;           // [kDecSplit][HD]
     __shared__ __align__(16) float sq[G][HD];
     __shared__ __align__(16) float skc[HD], svc[HD];
-    __shared__ int last;
+    __shared__ __align__(16) DecScratch<HD> S;
     constexpr int CH = HD / 8;
     trace_mark(a.trace, 0);
     pdl_trigger();
@@ -446,7 +484,8 @@ __global__ void __launch_bounds__((G + 1) * 32) attn_decode2(const __grid_consta
     const int w = threadIdx.x >> 5;
     const int pos = *a.pos_ptr;  // written before this graph / >= 2 kernels back
     const int j0 = split * kDecSplit;
-    if (pos < 0 || pos >= a.ctx || j0 > pos) return;
+    // the body's named barriers count kDecWarps warps: any other shape returns
+    if (blockDim.x != kDecWarps * 32 || pos < 0 || pos >= a.ctx || j0 > pos) return;
     const int j1 = min(pos + 1, j0 + kDecSplit);
     const int ncache = min(j1, pos) - j0;  // rows already in the cache
     const uint16_t *Kg = a.kc + kvh * HD, *Vg = a.vc + kvh * HD;
@@ -460,17 +499,15 @@ __global__ void __launch_bounds__((G + 1) * 32) attn_decode2(const __grid_consta
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
     DecConsts<HD> k;
-    attn_dec_consts<HD, G>(a, pos, k);
+    if (w <= G) attn_dec_consts<HD, G>(a, pos, k);
     pdl_wait();
     trace_mark(a.trace, 1);
-    attn_dec_prologue<HD, G>(a, kvh, pos, split == 0, k, sq, skc, svc);
+    if (w <= G) attn_dec_prologue<HD, G>(a, kvh, pos, split == 0, k, sq, skc, svc);
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
     trace_mark(a.trace, 2);
-    if (w < G) {
-        const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * HD + ((c + j) % CH) * 8); };
-        attn_dec_main<HD, G>(a, kvh, split, pos, krow, sV, sq, skc, svc, &last, 1);
-    }
+    const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * HD + ((c + j) % CH) * 8); };
+    attn_dec_main<HD, G>(a, kvh, split, pos, krow, sV, sq, skc, svc, S, 1);
     trace_mark(a.trace, 3);
 }
 

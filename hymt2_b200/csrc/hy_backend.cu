@@ -344,7 +344,7 @@ bool run_multi(HyCtx *c, HyWeight *const *ws, float *const *outs, const int *lds
 template <int HD, int G>
 bool attn_launch(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
     if (nt == 1)
-        return launch(c, attn_decode2<HD, G>, dim3(aa.kv_heads, aa.max_splits), dim3((G + 1) * 32), attn_dec_smem<HD>(),
+        return launch(c, attn_decode2<HD, G>, dim3(aa.kv_heads, aa.max_splits), dim3(kDecWarps * 32), attn_dec_smem<HD>(),
                       pdl, aa);
     int warps = aa.heads + aa.kv_heads;
     if (warps > 32) warps = 32;
@@ -582,6 +582,7 @@ bool mega_check(HyCtx *c) {
     else if (c->hd == 64 && G == 4 && CF == 1) c->mega_kernel = mega_kernel_for<64, 4, 1>();
     else return no("head geometry / FFN width without a persistent-kernel instance");
     if (c->H > 2048 || c->qd > 2048) return no("hidden or q width above 2048");
+    if (c->L > kMegaMaxLayers) return no("more layers than the persistent kernel's table holds");
     if (c->outw->fmt != FMT_Q6K || c->outw->k != c->H) return no("LM head is not Q6_K");
     if (c->kvh > 64 || c->kvh * c->max_splits > c->nsm) return no("context too long for one attention CTA per split");
     const HyWeight *w0 = c->layers[0].q;
@@ -1858,7 +1859,7 @@ HYC_API int hyc_attention_decode_noalloc(void *stream, int heads, int kv_heads, 
     aa.split_len = kDecSplit;
     aa.max_splits = splits;
     aa.trace = -1;
-    const dim3 grid(kv_heads, splits), block((G + 1) * 32);
+    const dim3 grid(kv_heads, splits), block(kDecWarps * 32);
     const size_t smem = hdim == 128 ? attn_dec_smem<128>() : attn_dec_smem<64>();
     cudaError_t e = cudaErrorInvalidValue;
 #define HY_NA(HD_, G_)                                                                    \

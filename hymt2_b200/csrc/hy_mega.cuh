@@ -118,15 +118,22 @@ __device__ __forceinline__ int ld_relaxed_s32(const int *p) {
 }
 __device__ __forceinline__ void raise_err(const MegaArgs &a, int code) { atomicCAS(&a.sync->err, 0, code); }
 
-// Grid-wide barrier: every CTA adds 1 to the arrival counter and waits until
-// it reaches the running target.  Bounded; a timeout or another CTA's error
-// makes every CTA return false from here on.
-__device__ __forceinline__ bool grid_sync(const MegaArgs &a, unsigned &target, int *s_flag) {
+// Grid-wide barrier in two halves.  bar_arrive: once every thread's writes
+// of the phase are done (__syncthreads), thread 0 publishes them
+// (__threadfence) and adds 1 to the arrival counter.  Work that does not
+// depend on other CTAs can run between the halves.  bar_wait: thread 0 polls
+// until the counter reaches the running target; bounded, and a timeout or
+// another CTA's error makes every CTA return false from here on.
+__device__ __forceinline__ void bar_arrive(const MegaArgs &a, unsigned &target) {
     __syncthreads();
+    target += gridDim.x;
     if (threadIdx.x == 0) {
-        target += gridDim.x;
         __threadfence();
         atomicAdd(&a.sync->bar, 1u);
+    }
+}
+__device__ __forceinline__ bool bar_wait(const MegaArgs &a, unsigned target, int *s_flag) {
+    if (threadIdx.x == 0) {
         int bad = 0;
         if ((int)(ld_acquire_u32(&a.sync->bar) - target) < 0) {
             const unsigned long long t0 = gtimer();
@@ -181,8 +188,9 @@ __host__ __device__ inline int mega_phase_rows(int t, int H, int F, int qd, int 
 
 // Thread 0: arm slot t's mbarrier and issue the bulk copies of this CTA's
 // rows of GEMV t of layer l (codes, then scales after an aligned gap).
-__device__ inline void mega_fill(const MegaArgs &a, uint8_t *smem, uint64_t *bar, int t, int l) {
-    const MegaLayer &ly = a.layers[l];
+__device__ inline void mega_fill(const MegaArgs &a, const MegaLayer *tab, uint8_t *smem, uint64_t *bar, int t,
+                                 int l) {
+    const MegaLayer &ly = tab[l];
     const int K = mega_phase_k(t, a.H, a.F, a.qd);
     const int nb = K / 256, rb = nb * 64, rpc = a.rpc[t];
     uint8_t *sw = smem + a.slot_off[t];
@@ -223,24 +231,37 @@ __device__ inline void mega_fill(const MegaArgs &a, uint8_t *smem, uint64_t *bar
 
 // ---------------------------------------------------------------- activation staging
 
+// RMSNorm weights of the next normalised phase, loaded before the barrier
+// wait (they are constants): threads 0..255 hold elements t + 256 j.
+template <int SV>
+struct NormPre {
+    float4 w[SV];
+};
+template <int SV>
+__device__ __forceinline__ void norm_preload(const float *norm_w, int K, NormPre<SV> &p) {
+    const int tid = threadIdx.x;
+#pragma unroll
+    for (int j = 0; j < SV; j++) {
+        const int i = tid + j * kGemvThreads;
+        if (tid < kGemvThreads && i < (K >> 2)) p.w[j] = __ldg((const float4 *)norm_w + i);
+    }
+}
+
 // fp32 input (x, or the stage's own s.x when x == nullptr), optionally
-// RMSNorm * norm_w, then Q8_K into shared memory.  With a norm, threads
-// 0..255 hold elements i = t + 256 j exactly as the 256-thread per-layer
-// kernels do, so the sum of squares (and everything after it) is
+// RMSNorm * (preloaded) weights, then Q8_K into shared memory.  With a norm,
+// threads 0..255 hold elements i = t + 256 j exactly as the 256-thread
+// per-layer kernels do, so the sum of squares (and everything after it) is
 // bit-identical; the extra warps contribute zeros to the block reduction.
 template <int SV>
-__device__ inline void mega_stage(const float *x, const float *norm_w, float eps, int K, Q8Smem &s) {
+__device__ inline void mega_stage(const float *x, const NormPre<SV> *pre, float eps, int K, Q8Smem &s) {
     const int n4 = K >> 2, tid = threadIdx.x;
     const float4 *src = x ? (const float4 *)x : (const float4 *)s.x;
-    if (norm_w) {
-        float4 xv[SV], wv[SV];
+    if (pre) {
+        float4 xv[SV];
 #pragma unroll
         for (int j = 0; j < SV; j++) {
             const int i = tid + j * kGemvThreads;
-            if (tid < kGemvThreads && i < n4) {
-                xv[j] = src[i];
-                wv[j] = __ldg((const float4 *)norm_w + i);
-            }
+            if (tid < kGemvThreads && i < n4) xv[j] = src[i];
         }
         float ss = 0.f;
 #pragma unroll
@@ -258,11 +279,13 @@ __device__ inline void mega_stage(const float *x, const float *norm_w, float eps
 #pragma unroll
         for (int j = 0; j < SV; j++) {
             const int i = tid + j * kGemvThreads;
-            if (tid < kGemvThreads && i < n4)
-                ((float4 *)s.x)[i] = make_float4(__fmul_rn(__fmul_rn(xv[j].x, scale), wv[j].x),
-                                                 __fmul_rn(__fmul_rn(xv[j].y, scale), wv[j].y),
-                                                 __fmul_rn(__fmul_rn(xv[j].z, scale), wv[j].z),
-                                                 __fmul_rn(__fmul_rn(xv[j].w, scale), wv[j].w));
+            if (tid < kGemvThreads && i < n4) {
+                const float4 wv = pre->w[j];
+                ((float4 *)s.x)[i] = make_float4(__fmul_rn(__fmul_rn(xv[j].x, scale), wv.x),
+                                                 __fmul_rn(__fmul_rn(xv[j].y, scale), wv.y),
+                                                 __fmul_rn(__fmul_rn(xv[j].z, scale), wv.z),
+                                                 __fmul_rn(__fmul_rn(xv[j].w, scale), wv.w));
+            }
         }
     } else if (x) {
         for (int i = tid; i < n4; i += kMegaThreads) ((float4 *)s.x)[i] = src[i];
@@ -423,47 +446,88 @@ __device__ inline unsigned long long mega_head_q6k(const MegaArgs &a, const Q8Sm
 
 // ---------------------------------------------------------------- the kernel
 
+constexpr int kMegaMaxLayers = 40;
+
+// Warp-wide: issue the cached K/V rows [j0, j0 + ncache) of KV head kvh of
+// layer `ly` into the K/V area (K rows padded to HD*2 + kMegaKPad bytes).
+template <int HD>
+__device__ __forceinline__ void mega_kv_fill(const MegaArgs &a, const MegaLayer &ly, uint8_t *sK, uint16_t *sV,
+                                             uint64_t *bar, int kvh, int j0, int ncache) {
+    constexpr int KROW = HD * 2 + kMegaKPad;
+    const int lane = threadIdx.x & 31;
+    asm volatile("fence.proxy.async.global;" ::: "memory");      // rows written by generic stores
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // area last read by generic loads
+    if (lane == 0) mbar_expect(bar, (unsigned)ncache * HD * 2 * 2);
+    __syncwarp();
+    const uint16_t *Kg = ly.kc + kvh * HD, *Vg = ly.vc + kvh * HD;
+    for (int j = lane; j < ncache; j += 32) {
+        const size_t g = (size_t)(j0 + j) * a.kvd;
+        bulk_g2s(sK + (size_t)j * KROW, Kg + g, HD * 2, bar);
+        bulk_g2s(sV + (size_t)j * HD, Vg + g, HD * 2, bar);
+    }
+}
+
 // Launch shape contract (checked by the host): grid = number of SMs, all
-// resident (cooperative launch); kvh * ceil(ctx/kDecSplit) <= grid; every
-// layer weight a panel with (shift, off); H, qd <= 2048 (one 64-element chunk
-// per lane) and F <= 2048 * CF; head Q6_K with k == H.
+// resident (cooperative launch); L <= kMegaMaxLayers; kvh * ceil(ctx /
+// kDecSplit) <= grid; every layer weight a panel with (shift, off); H, qd <=
+// 2048 (one 64-element chunk per lane) and F <= 2048 * CF; head Q6_K with
+// k == H.
+//
+// Between bar_arrive and bar_wait each CTA does the work that needs nothing
+// from other CTAs: it refills the weight slot it just consumed with the next
+// layer's slice, stages the next layer's K/V rows (after this layer's
+// attention), and loads the next phase's norm weights and rope constants.
 template <int HD, int G, int CF>
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_constant__ MegaArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ __align__(8) uint64_t mbar[5];  // 4 weight slots + K/V rows
-    __shared__ int s_flag, s_last, s_kvbad;
+    __shared__ int s_flag;
     __shared__ unsigned long long s_best[kMegaWarps];
     __shared__ __align__(16) float sq[G][HD];
     __shared__ __align__(16) float skc[HD], svc[HD];
+    __shared__ __align__(16) DecScratch<HD> S;
+    __shared__ __align__(16) MegaLayer tab[kMegaMaxLayers];
     constexpr int KROW = HD * 2 + kMegaKPad;
+    constexpr int RGQ = 2, RGO = 1, RGU = 6, RGD = 1;  // rows per warp iteration per phase
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     Q8Smem st = q8_smem(smem + a.stage_off, 1, a.kmax);
     uint8_t *sK = smem + a.attn_off;
     uint16_t *sV = (uint16_t *)(smem + a.attn_off + (size_t)kDecSplit * KROW);
+    for (int i = tid; i < a.L * (int)(sizeof(MegaLayer) / 8); i += kMegaThreads)
+        ((unsigned long long *)tab)[i] = ((const unsigned long long *)a.layers)[i];
     if (tid == 0) {
-        s_kvbad = 0;
         for (int i = 0; i < 5; i++) mbar_init(&mbar[i]);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
     unsigned ph[5] = {0, 0, 0, 0, 0};  // parity each mbarrier completes next
-    unsigned pending = 0;              // bit i: a fill of mbarrier i is outstanding (thread 0 / warp 0)
+    unsigned pending = 0;              // bit i: a fill of mbarrier i is outstanding (same in every thread)
     unsigned target = 0;
     int tli = 0, tls = 0;
     int tok = a.st->tok, pos = a.st->pos;
     bool ok = true;
-    if (tid == 0) {
-        for (int t = 0; t < 4; t++) mega_fill(a, smem, &mbar[t], t, 0);
-        pending |= 0xfu;
+    const int akvh = blockIdx.x % a.kvh, asplit = blockIdx.x / a.kvh, aj0 = asplit * kDecSplit;
+    const auto attn_cta = [&](int p) {
+        return p >= 0 && p < a.ctx && (int)blockIdx.x < a.kvh * ((p + kDecSplit) / kDecSplit);
+    };
+    const auto ncache_of = [&](int p) { return max(0, min(p, aj0 + kDecSplit) - aj0); };
+    // prime: layer 0's weight slots and K/V rows, the first norm weights
+    if (tid == 0)
+        for (int t = 0; t < 4; t++) mega_fill(a, tab, smem, &mbar[t], t, 0);
+    pending |= 0xfu;
+    if (a.steps > 0 && attn_cta(pos)) {
+        if (warp == 1) mega_kv_fill<HD>(a, tab[0], sK, sV, &mbar[4], akvh, aj0, ncache_of(pos));
+        pending |= 0x10u;
     }
+    NormPre<2> npre;
+    norm_preload<2>(tab[0].attn_norm, a.H, npre);
     for (int step = 0; step < a.steps && ok; step++) {
         if (pos < 0 || pos >= a.ctx) {
             if (tid == 0) raise_err(a, MEGA_ERR_POS);
+            ok = false;
             break;
         }
-        const int nsplit = (pos + kDecSplit) / kDecSplit;
-        const bool is_attn = blockIdx.x < a.kvh * nsplit;
-        const int akvh = blockIdx.x % a.kvh, asplit = blockIdx.x / a.kvh;
+        const bool is_attn = attn_cta(pos);
         tl_mark(a, tli);
         // embedding of `tok` into the stage row; CTA b also writes its slice of h
         {
@@ -475,34 +539,19 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             __syncthreads();
         }
         for (int l = 0; l < a.L && ok; l++) {
-            const MegaLayer &ly = a.layers[l];
-            const bool more = !(l + 1 == a.L && step + 1 == a.steps);  // refill for a following layer
+            const MegaLayer &ly = tab[l];
+            const bool more = !(l + 1 == a.L && step + 1 == a.steps);  // a following layer exists
             const int nl = l + 1 < a.L ? l + 1 : 0;
+            const int npos = l + 1 < a.L ? pos : pos + 1;  // position the following layer runs at
             AttnArgs aa = a.attn;
             aa.kc = ly.kc;
             aa.vc = ly.vc;
             aa.q_norm = ly.q_norm;
             aa.k_norm = ly.k_norm;
             aa.tickets = a.sync->tickets;
-            // cached K/V rows of this CTA's attention split, staged during q|k|v
-            if (is_attn && warp == 0) {
-                const int j0 = asplit * kDecSplit;
-                const int ncache = max(0, min(pos, j0 + kDecSplit) - j0);
-                asm volatile("fence.proxy.async.global;" ::: "memory");  // rows written by generic stores
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                if (lane == 0) mbar_expect(&mbar[4], (unsigned)ncache * HD * 2 * 2);
-                __syncwarp();
-                const uint16_t *Kg = ly.kc + akvh * HD, *Vg = ly.vc + akvh * HD;
-                for (int j = lane; j < ncache; j += 32) {
-                    const size_t g = (size_t)(j0 + j) * a.kvd;
-                    bulk_g2s(sK + (size_t)j * KROW, Kg + g, HD * 2, &mbar[4]);
-                    bulk_g2s(sV + (size_t)j * HD, Vg + g, HD * 2, &mbar[4]);
-                }
-                pending |= 0x10u;
-            }
             // ---- q|k|v
             {
-                mega_stage<2>(l == 0 ? nullptr : a.h, ly.attn_norm, a.eps, a.H, st);
+                mega_stage<2>(l == 0 ? nullptr : a.h, &npre, a.eps, a.H, st);
                 tl_sub(a, tls);
                 int4 act[1][4];
                 float dblk[1];
@@ -520,59 +569,57 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 const float *ss = (const float *)(sw + align16((size_t)rpc * (a.H / 256) * 64));
                 float *qkv = a.qkv;
                 if (ok)
-                    mega_rows<1, 4, false>(a.shift, a.off, r0, r1, rpc, sw, ss, a.H, act, dblk, sblk,
-                                           [&](int rg, const float *acc, int rend) {
+                    mega_rows<1, RGQ, false>(a.shift, a.off, r0, r1, rpc, sw, ss, a.H, act, dblk, sblk,
+                                             [&](int rg, const float *acc, int rend) {
 #pragma unroll
-                                               for (int g = 0; g < 4; g++)
-                                                   if (rg + g < rend) qkv[rg + g] = acc[g];
-                                           });
+                                                 for (int g = 0; g < RGQ; g++)
+                                                     if (rg + g < rend) qkv[rg + g] = acc[g];
+                                             });
                 tl_sub(a, tls);
-                __syncthreads();
-                if (tid == 0 && more && ok) {
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    mega_fill(a, smem, &mbar[0], 0, nl);
-                    pending |= 1u;
-                }
             }
             tl_mark(a, tli);
             tl_cta(a, step == 1 && l == 5, 0);
-            if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            bar_arrive(a, target);
+            if (more && ok) {
+                if (tid == 0) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mega_fill(a, tab, smem, &mbar[0], 0, nl);
+                }
+                pending |= 1u;
+            }
+            DecConsts<HD> kcs;
+            if (is_attn && warp <= G) attn_dec_consts<HD, G>(aa, pos, kcs);
+            if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
             tl_cta(a, step == 1 && l == 5, 1);
             tl_mark(a, tli);
             if (l == 0 && blockIdx.x == 0 && tid == 0) a.sync->amax[(step + 1) & 1] = 0ull;
-            // ---- attention
-            if (is_attn && warp <= G) {
-                DecConsts<HD> kc;
-                attn_dec_consts<HD, G>(aa, pos, kc);
-                attn_dec_prologue<HD, G>(aa, akvh, pos, asplit == 0, kc, sq, skc, svc);
-                tl_sub(a, tls);
-                if (!mbar_wait(&mbar[4], ph[4])) {
-                    s_kvbad = 1;
-                    raise_err(a, MEGA_ERR_KV);
-                }
-                asm volatile("bar.sync 1, %0;" ::"r"((G + 1) * 32) : "memory");  // s_kvbad now uniform
-                tl_sub(a, tls);
-                if (warp < G && !s_kvbad) {
-                    const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * KROW + c * 16); };
-                    attn_dec_main<HD, G>(aa, akvh, asplit, pos, krow, sV, sq, skc, svc, &s_last, 2);
-                }
-                tl_sub(a, tls);
-            }
+            // ---- attention (the CTAs of the splits that hold keys)
             if (is_attn) {
-                __syncthreads();  // s_kvbad visible to every warp
-                if (!s_kvbad) {
+                if (warp <= G) attn_dec_prologue<HD, G>(aa, akvh, pos, asplit == 0, kcs, sq, skc, svc);
+                tl_sub(a, tls);
+                if (__syncthreads_and(mbar_wait(&mbar[4], ph[4]))) {  // also publishes sq / skc / svc
                     ph[4] ^= 1;
                     pending &= ~0x10u;
+                } else {
+                    if (tid == 0) raise_err(a, MEGA_ERR_KV);
+                    ok = false;
                 }
+                tl_sub(a, tls);
+                if (ok) {
+                    const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * KROW + c * 16); };
+                    attn_dec_main<HD, G>(aa, akvh, asplit, pos, krow, sV, sq, skc, svc, S, 1);
+                }
+                tl_sub(a, tls);
             }
             tl_mark(a, tli);
             tl_cta(a, step == 1 && l == 5, 2);
-            if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            bar_arrive(a, target);
+            if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
             tl_cta(a, step == 1 && l == 5, 3);
             tl_mark(a, tli);
             // ---- o_proj (+ residual)
             {
-                mega_stage<2>(a.ao, nullptr, a.eps, a.qd, st);
+                mega_stage<2>(a.ao, (const NormPre<2> *)nullptr, a.eps, a.qd, st);
                 tl_sub(a, tls);
                 int4 act[1][4];
                 float dblk[1];
@@ -590,28 +637,36 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 const float *ss = (const float *)(sw + align16((size_t)rpc * (a.qd / 256) * 64));
                 float *h = a.h;
                 if (ok)
-                    mega_rows<1, 4, false>(a.shift, a.off, r0, r1, rpc, sw, ss, a.qd, act, dblk, sblk,
-                                           [&](int rg, const float *acc, int rend) {
+                    mega_rows<1, RGO, false>(a.shift, a.off, r0, r1, rpc, sw, ss, a.qd, act, dblk, sblk,
+                                             [&](int rg, const float *acc, int rend) {
 #pragma unroll
-                                               for (int g = 0; g < 4; g++)
-                                                   if (rg + g < rend) h[rg + g] += acc[g];
-                                           });
+                                                 for (int g = 0; g < RGO; g++)
+                                                     if (rg + g < rend) h[rg + g] += acc[g];
+                                             });
                 tl_sub(a, tls);
-                __syncthreads();
-                if (tid == 0 && more && ok) {
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    mega_fill(a, smem, &mbar[1], 1, nl);
-                    pending |= 2u;
-                }
             }
             tl_mark(a, tli);
             tl_cta(a, step == 1 && l == 5, 4);
-            if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            bar_arrive(a, target);
+            if (more && ok) {
+                if (tid == 0) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mega_fill(a, tab, smem, &mbar[1], 1, nl);
+                }
+                pending |= 2u;
+                // this layer's attention is done with the K/V area: stage the next layer's rows
+                if (attn_cta(npos)) {
+                    if (warp == 1) mega_kv_fill<HD>(a, tab[nl], sK, sV, &mbar[4], akvh, aj0, ncache_of(npos));
+                    pending |= 0x10u;
+                }
+            }
+            norm_preload<2>(ly.ffn_norm, a.H, npre);
+            if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
             tl_cta(a, step == 1 && l == 5, 5);
             tl_mark(a, tli);
             // ---- gate|up (interleaved rows) -> silu(gate) * up
             {
-                mega_stage<2>(a.h, ly.ffn_norm, a.eps, a.H, st);
+                mega_stage<2>(a.h, &npre, a.eps, a.H, st);
                 tl_sub(a, tls);
                 int4 act[1][4];
                 float dblk[1];
@@ -629,31 +684,33 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 const float *ss = (const float *)(sw + align16((size_t)rpc * (a.H / 256) * 64));
                 float *out = a.act;
                 if (ok)
-                    mega_rows<1, 4, true>(a.shift, a.off, r0, r1, rpc, sw, ss, a.H, act, dblk, sblk,
-                                          [&](int rg, const float *acc, int rend) {
+                    mega_rows<1, RGU, true>(a.shift, a.off, r0, r1, rpc, sw, ss, a.H, act, dblk, sblk,
+                                            [&](int rg, const float *acc, int rend) {
 #pragma unroll
-                                              for (int g = 0; g + 1 < 4; g += 2) {
-                                                  if (rg + g + 1 >= rend) break;
-                                                  const float gt = acc[g], up = acc[g + 1];
-                                                  out[(rg + g) >> 1] = __fmul_rn(gt / (1.0f + expf(-gt)), up);
-                                              }
-                                          });
+                                                for (int g = 0; g + 1 < RGU; g += 2) {
+                                                    if (rg + g + 1 >= rend) break;
+                                                    const float gt = acc[g], up = acc[g + 1];
+                                                    out[(rg + g) >> 1] = __fmul_rn(gt / (1.0f + expf(-gt)), up);
+                                                }
+                                            });
                 tl_sub(a, tls);
-                __syncthreads();
-                if (tid == 0 && more && ok) {
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    mega_fill(a, smem, &mbar[2], 2, nl);
-                    pending |= 4u;
-                }
             }
             tl_mark(a, tli);
             tl_cta(a, step == 1 && l == 5, 6);
-            if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            bar_arrive(a, target);
+            if (more && ok) {
+                if (tid == 0) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mega_fill(a, tab, smem, &mbar[2], 2, nl);
+                }
+                pending |= 4u;
+            }
+            if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
             tl_cta(a, step == 1 && l == 5, 7);
             tl_mark(a, tli);
             // ---- down (+ residual)
             {
-                mega_stage<2 * CF>(a.act, nullptr, a.eps, a.F, st);
+                mega_stage<2 * CF>(a.act, (const NormPre<2 * CF> *)nullptr, a.eps, a.F, st);
                 tl_sub(a, tls);
                 int4 act[CF][4];
                 float dblk[CF];
@@ -670,7 +727,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 const uint8_t *sw = smem + a.slot_off[3];
                 const float *ss = (const float *)(sw + align16((size_t)rpc * (a.F / 256) * 64));
                 float *h = a.h;
-                constexpr int RGD = CF == 1 ? 4 : 2;
                 if (ok)
                     mega_rows<CF, RGD, false>(a.shift, a.off, r0, r1, rpc, sw, ss, a.F, act, dblk, sblk,
                                               [&](int rg, const float *acc, int rend) {
@@ -679,23 +735,26 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                                                       if (rg + g < rend) h[rg + g] += acc[g];
                                               });
                 tl_sub(a, tls);
-                __syncthreads();
-                if (tid == 0 && more && ok) {
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    mega_fill(a, smem, &mbar[3], 3, nl);
-                    pending |= 8u;
-                }
             }
             tl_mark(a, tli);
             tl_cta(a, step == 1 && l == 5, 8);
-            if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+            bar_arrive(a, target);
+            if (more && ok) {
+                if (tid == 0) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mega_fill(a, tab, smem, &mbar[3], 3, nl);
+                }
+                pending |= 8u;
+            }
+            norm_preload<2>(l + 1 < a.L ? tab[l + 1].attn_norm : a.out_norm, a.H, npre);
+            if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
             tl_cta(a, step == 1 && l == 5, 9);
             tl_mark(a, tli);
         }
         if (!ok) break;
         // ---- LM head + argmax (rows < vocab_out compete)
         {
-            mega_stage<2>(a.h, a.out_norm, a.eps, a.H, st);
+            mega_stage<2>(a.h, &npre, a.eps, a.H, st);
             const int rpc = a.rpc[4], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.head.n);
             const unsigned long long best = mega_head_q6k(a, st, r0, r1);
             if (lane == 0) s_best[warp] = best;
@@ -707,7 +766,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             }
         }
         tl_mark(a, tli);
-        if (!grid_sync(a, target, &s_flag)) { ok = false; break; }
+        bar_arrive(a, target);
+        norm_preload<2>(tab[0].attn_norm, a.H, npre);
+        if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
         tl_mark(a, tli);
         // ---- token bookkeeping (decode_finalize's rules), in every CTA
         {
@@ -732,11 +793,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
         a.st->amax = 0ull;
     }
     // copies still in flight into this CTA's shared memory (error exits)
-    if (tid == 0) {
-        for (int i = 0; i < 4; i++)
+    if (tid == 0)
+        for (int i = 0; i < 5; i++)
             if (pending & (1u << i)) mbar_wait(&mbar[i], ph[i]);
-    }
-    if (warp == 0 && (pending & 0x10u)) mbar_wait(&mbar[4], ph[4]);
     __syncthreads();
 }
 
