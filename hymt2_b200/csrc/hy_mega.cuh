@@ -13,8 +13,8 @@
 // Each CTA owns fixed row slices of every GEMV, so while layer l runs it
 // streams its layer-(l+1) slices into four shared-memory slots with bulk
 // async copies (cp.async.bulk, no multicast) completing on mbarriers; the
-// attention CTAs stage their cached K/V rows the same way at the start of the
-// layer.  Every arithmetic step (norm reduction order, quantiser, per-row dot
+// attention CTAs stage the next layer's cached K/V rows with cp.async as soon
+// as the current layer's attention is done.  Every arithmetic step (norm reduction order, quantiser, per-row dot
 // products, attention body, head rows) is the one the per-layer kernels use,
 // so this path is bit-identical to the graph of per-layer launches.
 //
@@ -63,6 +63,8 @@ struct MegaArgs {
     int kmax;                 // largest GEMV input length (stage plan)
     AttnArgs attn;            // shape, rope tables, part buffer; per-layer fields set in-kernel
     WDesc head, embd;
+    const uint8_t *head_i8;   // int8 relayout of the Q6_K head (q6k_to_i8)
+    long long head_i8_stride;
     int vocab_out;
     const float *out_norm;
     float *h, *qkv, *ao, *act;
@@ -368,72 +370,63 @@ __device__ __forceinline__ void mega_rows(int shift, int off, int r0, int r1, in
     }
 }
 
-// ---------------------------------------------------------------- LM head (Q6_K) with argmax
+// ---------------------------------------------------------------- LM head with argmax
 
-// Rows [r0, r1) of the relayouted Q6_K head (ql | qh | scales | d planes per
-// row), two rows per warp iteration with all loads issued first.  Per-row
-// arithmetic is gemv_q6k's; returns the warp's best argmax key (lane 0).
-__device__ inline unsigned long long mega_head_q6k(const MegaArgs &a, const Q8Smem &s, int r0, int r1) {
-    constexpr int R = 2;
-    const WDesc &w = a.head;
+// Rows [r0, r1) of the int8 head (q6k_to_i8).  Lane u = 4b + p takes the
+// natural 64-element chunk ch = piece_of_chunk(p) of block b, i.e. the 64
+// activation bytes at piece position 4b + p of the plane-major stage, which
+// it keeps in registers for every row.  Per row: four 16-byte code loads, the
+// four sub-scales and the block's d; R rows per warp iteration with all loads
+// issued first.  The 4-lane block sum is the Q6_K GEMV's exact integer and
+// the float steps are gemv_q6k's, so the logits (and the argmax) are
+// identical.  Needs k <= 2048 (one unit per lane).
+__device__ inline unsigned long long mega_head_i8(const MegaArgs &a, const Q8Smem &s, int r0, int r1) {
+    constexpr int R = 3;
     const int K = a.H, nb = K / 256, nunit = nb * 4;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const bool ok = lane < nunit;
+    const int b = lane >> 2, p = lane & 3, ch = piece_of_chunk(p);
+    int4 av[4];
+#pragma unroll
+    for (int l = 0; l < 4; l++)
+        av[l] = ok ? *(const int4 *)&s.qp[(size_t)l * (K / 4) + (b * 4 + p) * 16] : make_int4(0, 0, 0, 0);
+    const float dact = ok ? s.d[b] : 0.f;
+    const size_t coff = (size_t)b * 256 + ch * 64, soff = (size_t)K + b * 16 + ch * 4, doff = (size_t)K + K / 16 + b * 4;
     unsigned long long best = 0;
     for (int rg = r0 + warp * R; rg < r1; rg += kMegaWarps * R) {
-        float acc[R] = {0.f, 0.f};
-        for (int u0 = 0; u0 < nunit; u0 += 32) {
-            const int u = u0 + lane;
-            const bool ok = u < nunit;
-            const int b = u >> 2, hf = (u >> 1) & 1, sg = u & 1;
-            uint4 qa[R], qb[R], qh[R], scv[R];
-            float dw[R];
+        uint4 c[R][4];
+        uint32_t sc[R];
+        float dw[R];
 #pragma unroll
-            for (int g = 0; g < R; g++) {
-                qa[g] = qb[g] = qh[g] = scv[g] = make_uint4(0, 0, 0, 0);
-                dw[g] = 0.f;
-                if (ok && rg + g < r1) {
-                    const uint8_t *row = w.w + (size_t)(rg + g) * w.stride;
-                    qa[g] = ldg_stream(row + (size_t)b * 128 + hf * 64 + sg * 16);
-                    qb[g] = ldg_stream(row + (size_t)b * 128 + hf * 64 + 32 + sg * 16);
-                    qh[g] = ldg_stream(row + (size_t)nb * 128 + (size_t)b * 64 + hf * 32 + sg * 16);
-                    scv[g] = __ldg((const uint4 *)(row + (size_t)nb * 192 + (size_t)b * 16));
-                    dw[g] = h2f(__ldg((const unsigned short *)(row + (size_t)nb * 208) + b));
-                }
-            }
+        for (int g = 0; g < R; g++) {
 #pragma unroll
-            for (int g = 0; g < R; g++) {
-                const int8_t *sc = (const int8_t *)&scv[g];
-                const uint32_t A[4] = {qa[g].x, qa[g].y, qa[g].z, qa[g].w}, B[4] = {qb[g].x, qb[g].y, qb[g].z, qb[g].w};
-                const uint32_t Hh[4] = {qh[g].x, qh[g].y, qh[g].z, qh[g].w};
-                int acc_i = 0;
-                if (ok) {
+            for (int l = 0; l < 4; l++) c[g][l] = make_uint4(0, 0, 0, 0);
+            sc[g] = 0;
+            dw[g] = 0.f;
+            if (ok && rg + g < r1) {
+                const uint8_t *row = a.head_i8 + (size_t)(rg + g) * a.head_i8_stride;
 #pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const int ch = hf * 2 + (q >> 1), l = (2 * q + sg) & 3;
-                        const int4 av = *(const int4 *)&s.qp[(size_t)l * (K / 4) + (b * 4 + piece_of_chunk(ch)) * 16];
-                        uint32_t code[4];
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            const uint32_t src = (q & 1) ? B[j] : A[j];
-                            code[j] = ((src >> (4 * (q >> 1))) & 0x0f0f0f0fu) | (((Hh[j] >> (2 * q)) & 0x03030303u) << 4);
-                        }
-                        int tq = dp4a((int)code[0], av.x, 0);
-                        tq = dp4a((int)code[1], av.y, tq);
-                        tq = dp4a((int)code[2], av.z, tq);
-                        tq = dp4a((int)code[3], av.w, tq);
-                        const int sub = hf * 8 + 2 * q + sg;
-                        tq -= 32 * (int)s.bs[b * 16 + sub];
-                        acc_i += (int)sc[sub] * tq;
-                    }
-                }
-                acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 1);
-                acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 2);
-                if (ok && (lane & 3) == 0) acc[g] += dw[g] * s.d[b] * (float)acc_i;
+                for (int l = 0; l < 4; l++) c[g][l] = ldg_stream(row + coff + l * 16);
+                sc[g] = __ldg((const uint32_t *)(row + soff));
+                dw[g] = __ldg((const float *)(row + doff));
             }
         }
 #pragma unroll
         for (int g = 0; g < R; g++) {
-            const float v = warp_sum(acc[g]);
+            int acc_i = 0;
+#pragma unroll
+            for (int l = 0; l < 4; l++) {
+                int t = dp4a((int)c[g][l].x, av[l].x, 0);
+                t = dp4a((int)c[g][l].y, av[l].y, t);
+                t = dp4a((int)c[g][l].z, av[l].z, t);
+                t = dp4a((int)c[g][l].w, av[l].w, t);
+                acc_i += (int)(int8_t)(sc[g] >> (8 * l)) * t;
+            }
+            acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 1);
+            acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 2);
+            float acc = 0.f;
+            if (ok && (lane & 3) == 0) acc += dw[g] * dact * (float)acc_i;
+            const float v = warp_sum(acc);
             const int r = rg + g;
             if (lane == 0 && r < r1 && r < a.vocab_out) {
                 const unsigned long long key = argmax_key(v, (uint32_t)r);
@@ -448,23 +441,22 @@ __device__ inline unsigned long long mega_head_q6k(const MegaArgs &a, const Q8Sm
 
 constexpr int kMegaMaxLayers = 40;
 
-// Warp-wide: issue the cached K/V rows [j0, j0 + ncache) of KV head kvh of
-// layer `ly` into the K/V area (K rows padded to HD*2 + kMegaKPad bytes).
+// All threads: cp.async the cached K/V rows [j0, j0 + ncache) of KV head
+// kvh of layer `ly` into the K/V area (K rows padded to HD*2 + kMegaKPad
+// bytes) as one commit group.  cp.async is a generic-proxy copy, so rows
+// that other CTAs stored before a grid barrier need no proxy fence.
 template <int HD>
 __device__ __forceinline__ void mega_kv_fill(const MegaArgs &a, const MegaLayer &ly, uint8_t *sK, uint16_t *sV,
-                                             uint64_t *bar, int kvh, int j0, int ncache) {
-    constexpr int KROW = HD * 2 + kMegaKPad;
-    const int lane = threadIdx.x & 31;
-    asm volatile("fence.proxy.async.global;" ::: "memory");      // rows written by generic stores
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // area last read by generic loads
-    if (lane == 0) mbar_expect(bar, (unsigned)ncache * HD * 2 * 2);
-    __syncwarp();
+                                             int kvh, int j0, int ncache) {
+    constexpr int KROW = HD * 2 + kMegaKPad, CH = HD / 8;
     const uint16_t *Kg = ly.kc + kvh * HD, *Vg = ly.vc + kvh * HD;
-    for (int j = lane; j < ncache; j += 32) {
-        const size_t g = (size_t)(j0 + j) * a.kvd;
-        bulk_g2s(sK + (size_t)j * KROW, Kg + g, HD * 2, bar);
-        bulk_g2s(sV + (size_t)j * HD, Vg + g, HD * 2, bar);
+    for (int idx = threadIdx.x; idx < ncache * CH; idx += kMegaThreads) {
+        const int j = idx / CH, c = idx - j * CH;
+        const size_t g = (size_t)(j0 + j) * a.kvd + c * 8;
+        cp_async16(sK + (size_t)j * KROW + c * 16, Kg + g);
+        cp_async16(sV + (size_t)j * HD + c * 8, Vg + g);
     }
+    asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
 // Launch shape contract (checked by the host): grid = number of SMs, all
@@ -480,7 +472,7 @@ __device__ __forceinline__ void mega_kv_fill(const MegaArgs &a, const MegaLayer 
 template <int HD, int G, int CF>
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_constant__ MegaArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ __align__(8) uint64_t mbar[5];  // 4 weight slots + K/V rows
+    __shared__ __align__(8) uint64_t mbar[4];  // weight slots
     __shared__ int s_flag;
     __shared__ unsigned long long s_best[kMegaWarps];
     __shared__ __align__(16) float sq[G][HD];
@@ -496,11 +488,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     for (int i = tid; i < a.L * (int)(sizeof(MegaLayer) / 8); i += kMegaThreads)
         ((unsigned long long *)tab)[i] = ((const unsigned long long *)a.layers)[i];
     if (tid == 0) {
-        for (int i = 0; i < 5; i++) mbar_init(&mbar[i]);
+        for (int i = 0; i < 4; i++) mbar_init(&mbar[i]);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
-    unsigned ph[5] = {0, 0, 0, 0, 0};  // parity each mbarrier completes next
+    unsigned ph[4] = {0, 0, 0, 0};  // parity each mbarrier completes next
     unsigned pending = 0;              // bit i: a fill of mbarrier i is outstanding (same in every thread)
     unsigned target = 0;
     int tli = 0, tls = 0;
@@ -515,10 +507,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     if (tid == 0)
         for (int t = 0; t < 4; t++) mega_fill(a, tab, smem, &mbar[t], t, 0);
     pending |= 0xfu;
-    if (a.steps > 0 && attn_cta(pos)) {
-        if (warp == 1) mega_kv_fill<HD>(a, tab[0], sK, sV, &mbar[4], akvh, aj0, ncache_of(pos));
-        pending |= 0x10u;
-    }
+    if (a.steps > 0 && attn_cta(pos)) mega_kv_fill<HD>(a, tab[0], sK, sV, akvh, aj0, ncache_of(pos));
     NormPre<2> npre;
     norm_preload<2>(tab[0].attn_norm, a.H, npre);
     for (int step = 0; step < a.steps && ok; step++) {
@@ -597,13 +586,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             if (is_attn) {
                 if (warp <= G) attn_dec_prologue<HD, G>(aa, akvh, pos, asplit == 0, kcs, sq, skc, svc);
                 tl_sub(a, tls);
-                if (__syncthreads_and(mbar_wait(&mbar[4], ph[4]))) {  // also publishes sq / skc / svc
-                    ph[4] ^= 1;
-                    pending &= ~0x10u;
-                } else {
-                    if (tid == 0) raise_err(a, MEGA_ERR_KV);
-                    ok = false;
-                }
+                asm volatile("cp.async.wait_group 0;" ::: "memory");
+                __syncthreads();  // K/V rows of every thread, and sq / skc / svc
                 tl_sub(a, tls);
                 if (ok) {
                     const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * KROW + c * 16); };
@@ -655,10 +639,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 }
                 pending |= 2u;
                 // this layer's attention is done with the K/V area: stage the next layer's rows
-                if (attn_cta(npos)) {
-                    if (warp == 1) mega_kv_fill<HD>(a, tab[nl], sK, sV, &mbar[4], akvh, aj0, ncache_of(npos));
-                    pending |= 0x10u;
-                }
+                if (attn_cta(npos)) mega_kv_fill<HD>(a, tab[nl], sK, sV, akvh, aj0, ncache_of(npos));
             }
             norm_preload<2>(ly.ffn_norm, a.H, npre);
             if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
@@ -756,7 +737,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
         {
             mega_stage<2>(a.h, &npre, a.eps, a.H, st);
             const int rpc = a.rpc[4], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.head.n);
-            const unsigned long long best = mega_head_q6k(a, st, r0, r1);
+            const unsigned long long best = mega_head_i8(a, st, r0, r1);
             if (lane == 0) s_best[warp] = best;
             __syncthreads();
             if (tid == 0) {
@@ -794,8 +775,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     }
     // copies still in flight into this CTA's shared memory (error exits)
     if (tid == 0)
-        for (int i = 0; i < 5; i++)
+        for (int i = 0; i < 4; i++)
             if (pending & (1u << i)) mbar_wait(&mbar[i], ph[i]);
+    asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
 }
 
