@@ -13,7 +13,10 @@ flush is needed between steps.
                max over ranks; whole job = ranks * steps / max time)
   e2e          the same decode through the public C ABI with every step's
                token copied in from / out to pinned host memory, wall-clock
-  roofline     the dominant kernel timed alone with CUDA events
+  roofline     the dominant kernel: the persistent decode kernel (one launch
+               runs up to 64 decode steps), each launch timed with CUDA
+               events; algorithmic bytes = every weight byte of a step plus
+               the K/V rows attention reads, per step times steps per launch
   cpu_baseline the reference's CPU library on this host (rank 0, N = 1)
 
 `--impl reference` times the reference's own CPU implementation of the path
@@ -55,6 +58,9 @@ OPS = {
     5: ("attention_decode", L, 2 * (PROMPT_LEN + GEN_LEN // 2) * KVD * 2),  # K+V bf16 rows at mid window
 }
 STEP_WEIGHT_BYTES = sum(b * n for op, (_, n, b) in OPS.items() if op != 5)
+# K/V rows read per step at the window's mean position (positions 48..111)
+STEP_KV_BYTES = L * 2 * (PROMPT_LEN + (GEN_LEN - 1) / 2) * KVD * 2
+STEP_BYTES = STEP_WEIGHT_BYTES + int(STEP_KV_BYTES)
 
 
 def parse():
@@ -67,6 +73,8 @@ def parse():
                                                          os.path.join(tempfile.gettempdir(), "hymt2_models")))
     p.add_argument("--cpu-tokens", type=int, default=24, help="decode tokens in the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--graph-breakdown", action="store_true",
+                   help="also time each kernel of the per-layer graph path alone")
     return p.parse_args()
 
 
@@ -222,6 +230,10 @@ def main():
             raise RuntimeError(f"{what}: {be.error()}")
 
     check(lib.hyc_decode_begin(impl, ids.ctypes.data, PROMPT_LEN, 0, GEN_LEN, None, 0, dm.vocab_out), "begin")
+    import ctypes
+    why = ctypes.create_string_buffer(128)
+    persistent = lib.hyc_decode_path(impl, why, 128) == 1
+    path_name = why.value.decode()
     first = np.zeros(1, dtype=np.int32)
     lib.hyc_decode_read(impl, first.ctypes.data, 1)
     tok0 = int(first[0])
@@ -281,10 +293,29 @@ def main():
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     lib.hyc_host_free(host)
 
-    # ---- roofline: each hot kernel timed alone (weights rotate over layers, > L2)
+    # ---- roofline of the dominant kernel
     peak, peak_kind = peaks()
     kernels = {}
-    for op, (name, per_step, nbytes) in OPS.items():
+    dom_entry = None
+    if persistent:
+        # one launch of the persistent kernel = GEN_LEN decode steps (the
+        # rewind before it is a 8-byte copy); CUDA events around each launch
+        n_launch = max(2, min(8, args.steps // GEN_LEN or 2))
+        evs = []
+        for _ in range(n_launch):
+            check(lib.hyc_decode_rewind(impl, PROMPT_LEN, tok0), "rewind")
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            check(lib.hyc_decode_steps(impl, GEN_LEN), "steps")
+            b.record(stream)
+            evs.append((a, b))
+        be.sync()
+        t = statistics.mean(x.elapsed_time(y) for x, y in evs)
+        nbytes = STEP_BYTES * GEN_LEN
+        dom_entry = ("decode_mega", {"ms_per_launch": round(t, 4), "launches_per_step": 1.0 / GEN_LEN,
+                                     "steps_per_launch": GEN_LEN, "bytes_per_launch": nbytes,
+                                     "gbs": round(nbytes / (t / 1e3) / 1e9, 1)})
+    for op, (name, per_step, nbytes) in (OPS.items() if (args.graph_breakdown or not persistent) else []):
         iters = 20 if op == 0 else 64
         check(lib.hyc_bench_op(impl, op, 4), "bench_op warm")
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -295,13 +326,18 @@ def main():
         t = a.elapsed_time(b) / iters
         kernels[name] = {"ms_per_launch": round(t, 5), "launches_per_step": per_step, "bytes_per_launch": nbytes,
                          "gbs": round(nbytes / (t / 1e3) / 1e9, 1), "share_of_step_ms": round(t * per_step, 4)}
-    dom = max(kernels, key=lambda k: kernels[k]["share_of_step_ms"])
-    dk = kernels[dom]
+    if dom_entry:
+        dom, dk = dom_entry
+    else:
+        dom = max(kernels, key=lambda k: kernels[k]["share_of_step_ms"])
+        dk = kernels[dom]
     traffic = None
     tfile = os.path.join(ROOT, "profiles", "dram_traffic_c0_stq.json")
     if os.path.exists(tfile):
         with open(tfile) as f:
-            traffic = json.load(f).get(dom)
+            tj = json.load(f).get(dom)
+        if tj:  # per-step DRAM bytes of one ncu capture, scaled to a launch
+            traffic = int(tj["dram_bytes_per_step"] * dk.get("steps_per_launch", 1))
 
     if rank == 0:
         step_ms = ms / args.steps
@@ -316,12 +352,14 @@ def main():
                        "l2": "weights 613 MB per step > 126 MB L2 (no flush needed)"},
             "e2e": {"value": round(world * args.steps / e2e_s, 2), "unit": UNIT, "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": 4,
-                    "path": "hyc_decode_steps_host: token in from pinned host, graph, token out to pinned host"},
+                    "path": f"hyc_decode_steps_host: token in from pinned host, one decode step ({path_name}), "
+                            f"token out to pinned host"},
+            "decode_path": path_name,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
                          "frac": round(dk["gbs"] / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                         "bytes_per_launch": dk["bytes_per_launch"]},
-            "roofline_step": {"bytes_per_step": STEP_WEIGHT_BYTES, "achieved_gbs": round(STEP_WEIGHT_BYTES / step_ms / 1e6, 1),
-                              "frac": round(STEP_WEIGHT_BYTES / step_ms / 1e6 / peak, 4)},
+                         "bytes_per_launch": dk["bytes_per_launch"], "ms_per_launch": dk["ms_per_launch"]},
+            "roofline_step": {"bytes_per_step": STEP_BYTES, "achieved_gbs": round(STEP_BYTES / step_ms / 1e6, 1),
+                              "frac": round(STEP_BYTES / step_ms / 1e6 / peak, 4)},
             "kernels": kernels,
             "gpu_launches": int(launches),
             "clocks": clk,

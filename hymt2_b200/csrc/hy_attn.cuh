@@ -236,10 +236,14 @@ template <int HD, int G>
 __device__ __forceinline__ void attn_dec_prologue(const AttnArgs &a, int kvh, int pos, bool store, const DecConsts<HD> &k,
                                                   float (*sq)[HD], float *skc, float *svc) {
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float v[HD / 32];
+    float v[HD / 32], vraw[HD / 32];
     const float *src = w < G ? a.qkv + (kvh * G + w) * HD : a.qkv + a.qdim + kvh * HD;
+    const float *vr = a.qkv + a.qdim + a.kvdim + kvh * HD;
 #pragma unroll
-    for (int i = 0; i < HD / 32; i++) v[i] = src[lane + 32 * i];
+    for (int i = 0; i < HD / 32; i++) {
+        v[i] = src[lane + 32 * i];
+        vraw[i] = w < G ? 0.f : vr[lane + 32 * i];  // the k/v warp loads v with k
+    }
 #pragma unroll
     for (int i = 0; i < HD / 64; i++) {
         const float x0 = v[i], x1 = v[i + HD / 64];
@@ -257,12 +261,11 @@ __device__ __forceinline__ void attn_dec_prologue(const AttnArgs &a, int kvh, in
 #pragma unroll
         for (int i = 0; i < HD / 32; i++) sq[w][lane + 32 * i] = v[i];
     } else {
-        const float *vr = a.qkv + a.qdim + a.kvdim + kvh * HD;
         uint16_t *kd = a.kc + (size_t)pos * a.kvdim + kvh * HD, *vd = a.vc + (size_t)pos * a.kvdim + kvh * HD;
 #pragma unroll
         for (int i = 0; i < HD / 32; i++) {
             const int e = lane + 32 * i;
-            const uint16_t kb = f32_to_bf16_bits(v[i]), vb = f32_to_bf16_bits(vr[e]);
+            const uint16_t kb = f32_to_bf16_bits(v[i]), vb = f32_to_bf16_bits(vraw[i]);
             skc[e] = bf16_bits_to_f32(kb);
             svc[e] = bf16_bits_to_f32(vb);
             if (store) {

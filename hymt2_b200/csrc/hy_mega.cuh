@@ -63,8 +63,6 @@ struct MegaArgs {
     int kmax;                 // largest GEMV input length (stage plan)
     AttnArgs attn;            // shape, rope tables, part buffer; per-layer fields set in-kernel
     WDesc head, embd;
-    const uint8_t *head_i8;   // int8 relayout of the Q6_K head (q6k_to_i8)
-    long long head_i8_stride;
     int vocab_out;
     const float *out_norm;
     float *h, *qkv, *ao, *act;
@@ -370,63 +368,72 @@ __device__ __forceinline__ void mega_rows(int shift, int off, int r0, int r1, in
     }
 }
 
-// ---------------------------------------------------------------- LM head with argmax
+// ---------------------------------------------------------------- LM head (Q6_K) with argmax
 
-// Rows [r0, r1) of the int8 head (q6k_to_i8).  Lane u = 4b + p takes the
-// natural 64-element chunk ch = piece_of_chunk(p) of block b, i.e. the 64
-// activation bytes at piece position 4b + p of the plane-major stage, which
-// it keeps in registers for every row.  Per row: four 16-byte code loads, the
-// four sub-scales and the block's d; R rows per warp iteration with all loads
-// issued first.  The 4-lane block sum is the Q6_K GEMV's exact integer and
-// the float steps are gemv_q6k's, so the logits (and the argmax) are
-// identical.  Needs k <= 2048 (one unit per lane).
-__device__ inline unsigned long long mega_head_i8(const MegaArgs &a, const Q8Smem &s, int r0, int r1) {
-    constexpr int R = 3;
+// Rows [r0, r1) of the relayouted Q6_K head (ql | qh | scales | d planes per
+// row), two rows per warp iteration with all loads issued first.  Per-row
+// arithmetic is gemv_q6k's; returns the warp's best argmax key (lane 0).
+__device__ inline unsigned long long mega_head_q6k(const MegaArgs &a, const Q8Smem &s, int r0, int r1) {
+    constexpr int R = 2;
+    const WDesc &w = a.head;
     const int K = a.H, nb = K / 256, nunit = nb * 4;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const bool ok = lane < nunit;
-    const int b = lane >> 2, p = lane & 3, ch = piece_of_chunk(p);
-    int4 av[4];
-#pragma unroll
-    for (int l = 0; l < 4; l++)
-        av[l] = ok ? *(const int4 *)&s.qp[(size_t)l * (K / 4) + (b * 4 + p) * 16] : make_int4(0, 0, 0, 0);
-    const float dact = ok ? s.d[b] : 0.f;
-    const size_t coff = (size_t)b * 256 + ch * 64, soff = (size_t)K + b * 16 + ch * 4, doff = (size_t)K + K / 16 + b * 4;
     unsigned long long best = 0;
     for (int rg = r0 + warp * R; rg < r1; rg += kMegaWarps * R) {
-        uint4 c[R][4];
-        uint32_t sc[R];
-        float dw[R];
+        float acc[R] = {0.f, 0.f};
+        for (int u0 = 0; u0 < nunit; u0 += 32) {
+            const int u = u0 + lane;
+            const bool ok = u < nunit;
+            const int b = u >> 2, hf = (u >> 1) & 1, sg = u & 1;
+            uint4 qa[R], qb[R], qh[R], scv[R];
+            float dw[R];
 #pragma unroll
-        for (int g = 0; g < R; g++) {
+            for (int g = 0; g < R; g++) {
+                qa[g] = qb[g] = qh[g] = scv[g] = make_uint4(0, 0, 0, 0);
+                dw[g] = 0.f;
+                if (ok && rg + g < r1) {
+                    const uint8_t *row = w.w + (size_t)(rg + g) * w.stride;
+                    qa[g] = ldg_stream(row + (size_t)b * 128 + hf * 64 + sg * 16);
+                    qb[g] = ldg_stream(row + (size_t)b * 128 + hf * 64 + 32 + sg * 16);
+                    qh[g] = ldg_stream(row + (size_t)nb * 128 + (size_t)b * 64 + hf * 32 + sg * 16);
+                    scv[g] = __ldg((const uint4 *)(row + (size_t)nb * 192 + (size_t)b * 16));
+                    dw[g] = h2f(__ldg((const unsigned short *)(row + (size_t)nb * 208) + b));
+                }
+            }
 #pragma unroll
-            for (int l = 0; l < 4; l++) c[g][l] = make_uint4(0, 0, 0, 0);
-            sc[g] = 0;
-            dw[g] = 0.f;
-            if (ok && rg + g < r1) {
-                const uint8_t *row = a.head_i8 + (size_t)(rg + g) * a.head_i8_stride;
+            for (int g = 0; g < R; g++) {
+                const int8_t *sc = (const int8_t *)&scv[g];
+                const uint32_t A[4] = {qa[g].x, qa[g].y, qa[g].z, qa[g].w}, B[4] = {qb[g].x, qb[g].y, qb[g].z, qb[g].w};
+                const uint32_t Hh[4] = {qh[g].x, qh[g].y, qh[g].z, qh[g].w};
+                int acc_i = 0;
+                if (ok) {
 #pragma unroll
-                for (int l = 0; l < 4; l++) c[g][l] = ldg_stream(row + coff + l * 16);
-                sc[g] = __ldg((const uint32_t *)(row + soff));
-                dw[g] = __ldg((const float *)(row + doff));
+                    for (int q = 0; q < 4; q++) {
+                        const int ch = hf * 2 + (q >> 1), l = (2 * q + sg) & 3;
+                        const int4 av = *(const int4 *)&s.qp[(size_t)l * (K / 4) + (b * 4 + piece_of_chunk(ch)) * 16];
+                        uint32_t code[4];
+#pragma unroll
+                        for (int j = 0; j < 4; j++) {
+                            const uint32_t src = (q & 1) ? B[j] : A[j];
+                            code[j] = ((src >> (4 * (q >> 1))) & 0x0f0f0f0fu) | (((Hh[j] >> (2 * q)) & 0x03030303u) << 4);
+                        }
+                        int tq = dp4a((int)code[0], av.x, 0);
+                        tq = dp4a((int)code[1], av.y, tq);
+                        tq = dp4a((int)code[2], av.z, tq);
+                        tq = dp4a((int)code[3], av.w, tq);
+                        const int sub = hf * 8 + 2 * q + sg;
+                        tq -= 32 * (int)s.bs[b * 16 + sub];
+                        acc_i += (int)sc[sub] * tq;
+                    }
+                }
+                acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 1);
+                acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 2);
+                if (ok && (lane & 3) == 0) acc[g] += dw[g] * s.d[b] * (float)acc_i;
             }
         }
 #pragma unroll
         for (int g = 0; g < R; g++) {
-            int acc_i = 0;
-#pragma unroll
-            for (int l = 0; l < 4; l++) {
-                int t = dp4a((int)c[g][l].x, av[l].x, 0);
-                t = dp4a((int)c[g][l].y, av[l].y, t);
-                t = dp4a((int)c[g][l].z, av[l].z, t);
-                t = dp4a((int)c[g][l].w, av[l].w, t);
-                acc_i += (int)(int8_t)(sc[g] >> (8 * l)) * t;
-            }
-            acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 1);
-            acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 2);
-            float acc = 0.f;
-            if (ok && (lane & 3) == 0) acc += dw[g] * dact * (float)acc_i;
-            const float v = warp_sum(acc);
+            const float v = warp_sum(acc[g]);
             const int r = rg + g;
             if (lane == 0 && r < r1 && r < a.vocab_out) {
                 const unsigned long long key = argmax_key(v, (uint32_t)r);
@@ -737,7 +744,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
         {
             mega_stage<2>(a.h, &npre, a.eps, a.H, st);
             const int rpc = a.rpc[4], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.head.n);
-            const unsigned long long best = mega_head_i8(a, st, r0, r1);
+            const unsigned long long best = mega_head_q6k(a, st, r0, r1);
             if (lane == 0) s_best[warp] = best;
             __syncthreads();
             if (tid == 0) {

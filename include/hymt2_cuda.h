@@ -77,9 +77,9 @@ HYC_API int hyc_generate(void *impl, const int *prompt, int n, int keep, int max
  *  hyc_decode_begin: prefill like hyc_generate and leave the first generated
  *    token on the device (no synchronisation);
  *  hyc_decode_steps: enqueue `steps` greedy single-token steps (one
- *    persistent kernel launch when hyc_set_decode_mode selected it and the
- *    model supports it, else one graph per step; both give bit-identical
- *    results);
+ *    persistent kernel launch when the model supports it and
+ *    hyc_set_decode_mode has not selected the graph, else one graph per
+ *    step; both give bit-identical results);
  *  hyc_decode_steps_host: the same, but every step's input token is copied
  *    from pinned host memory tok_io[s] and its result written back to
  *    tok_io[s+1] (tok_io must hold steps+1 ints, allocated with
@@ -97,9 +97,9 @@ HYC_API int hyc_decode_rewind(void *impl, int pos, int tok);
 HYC_API void *hyc_host_alloc(size_t bytes);
 HYC_API void hyc_host_free(void *p);
 /* Decode path selection (no reference counterpart; the reference's host
- * loop is src/model.c:914-958): mode 0 uses the persistent kernel whenever
- * the prepared model supports it (panel layer weights, Q6_K head), mode 1
- * always the graph of per-layer launches.  hyc_decode_path returns 1 when
+ * loop is src/model.c:914-958): mode 0 (the default) uses the persistent
+ * kernel whenever the prepared model supports it (panel layer weights, Q6_K
+ * head), mode 1 always the graph of per-layer launches.  hyc_decode_path returns 1 when
  * the next decode steps run the persistent kernel, 0 for the graph, and
  * writes the reason. */
 HYC_API int hyc_set_decode_mode(void *impl, int mode);
