@@ -598,6 +598,8 @@ bool mega_check(HyCtx *c) {
     if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->dev) != cudaSuccess || !coop)
         return no("no cooperative launch");
     c->mega_plan_v = mega_plan(c->nsm, c->H, c->F, c->qd, c->kvd, c->outw->n, c->hd);
+    if (c->outw->stride % 16 || !mega_head_ring(c->mega_plan_v, c->outw->stride))
+        return no("LM-head rows do not fit the shared-memory ring");
     if (cudaFuncSetAttribute(c->mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)c->mega_plan_v.bytes) != cudaSuccess) {
         cudaGetLastError();
@@ -657,6 +659,8 @@ bool mega_launch(HyCtx *c, int steps) {
     a.stage_off = p.stage_off;
     a.attn_off = p.attn_off;
     a.kmax = p.kmax;
+    a.head_ns = p.head_ns;
+    for (int i = 0; i < 4; i++) a.head_off[i] = p.head_off[i];
     AttnArgs &aa = a.attn;
     aa.qkv = c->d_qkv;
     aa.qkv_ld = c->qd + 2 * c->kvd;

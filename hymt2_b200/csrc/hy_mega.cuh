@@ -61,6 +61,8 @@ struct MegaArgs {
     int slot_off[4];          // dynamic-smem offsets of the weight slots
     int stage_off, attn_off;  // dynamic-smem offsets of the Q8_K stage and the K/V area
     int kmax;                 // largest GEMV input length (stage plan)
+    int head_ns;              // LM-head ring stages (kHeadRows rows each) and their smem offsets
+    int head_off[4];
     AttnArgs attn;            // shape, rope tables, part buffer; per-layer fields set in-kernel
     WDesc head, embd;
     int vocab_out;
@@ -370,78 +372,68 @@ __device__ __forceinline__ void mega_rows(int shift, int off, int r0, int r1, in
 
 // ---------------------------------------------------------------- LM head (Q6_K) with argmax
 
-// Rows [r0, r1) of the relayouted Q6_K head (ql | qh | scales | d planes per
-// row), two rows per warp iteration with all loads issued first.  Per-row
-// arithmetic is gemv_q6k's; returns the warp's best argmax key (lane 0).
-__device__ inline unsigned long long mega_head_q6k(const MegaArgs &a, const Q8Smem &s, int r0, int r1) {
-    constexpr int R = 2;
-    const WDesc &w = a.head;
-    const int K = a.H, nb = K / 256, nunit = nb * 4;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    unsigned long long best = 0;
-    for (int rg = r0 + warp * R; rg < r1; rg += kMegaWarps * R) {
-        float acc[R] = {0.f, 0.f};
-        for (int u0 = 0; u0 < nunit; u0 += 32) {
-            const int u = u0 + lane;
-            const bool ok = u < nunit;
-            const int b = u >> 2, hf = (u >> 1) & 1, sg = u & 1;
-            uint4 qa[R], qb[R], qh[R], scv[R];
-            float dw[R];
+// The head streams through a ring of shared-memory stages of kHeadRows rows
+// (one row per warp); each stage is one bulk copy of consecutive rows of the
+// relayouted Q6_K head (ql | qh | scales | d planes per row).
+constexpr int kHeadRows = kMegaWarps;
+
+// One Q6_K row held in shared memory against the stage's Q8_K activation;
+// the arithmetic (unit split, integer sums, float order, warp sum) is
+// gemv_q6k's, so the logit is identical.  Returns the sum on every lane.
+__device__ __forceinline__ float q6k_row_smem(const uint8_t *row, int nb, int K, const Q8Smem &s) {
+    const int lane = threadIdx.x & 31, nunit = nb * 4;
+    float acc = 0.f;
+    for (int u0 = 0; u0 < nunit; u0 += 32) {
+        const int u = u0 + lane;
+        const bool ok = u < nunit;
+        const int b = u >> 2, hf = (u >> 1) & 1, sg = u & 1;
+        uint4 qa = make_uint4(0, 0, 0, 0), qb = qa, qh = qa, scv = qa;
+        float dw = 0.f;
+        if (ok) {
+            qa = *(const uint4 *)(row + (size_t)b * 128 + hf * 64 + sg * 16);
+            qb = *(const uint4 *)(row + (size_t)b * 128 + hf * 64 + 32 + sg * 16);
+            qh = *(const uint4 *)(row + (size_t)nb * 128 + (size_t)b * 64 + hf * 32 + sg * 16);
+            scv = *(const uint4 *)(row + (size_t)nb * 192 + (size_t)b * 16);
+            dw = h2f(*(const unsigned short *)(row + (size_t)nb * 208 + 2 * b));
+        }
+        const int8_t *sc = (const int8_t *)&scv;
+        const uint32_t A[4] = {qa.x, qa.y, qa.z, qa.w}, B[4] = {qb.x, qb.y, qb.z, qb.w};
+        const uint32_t Hh[4] = {qh.x, qh.y, qh.z, qh.w};
+        int acc_i = 0;
+        if (ok) {
 #pragma unroll
-            for (int g = 0; g < R; g++) {
-                qa[g] = qb[g] = qh[g] = scv[g] = make_uint4(0, 0, 0, 0);
-                dw[g] = 0.f;
-                if (ok && rg + g < r1) {
-                    const uint8_t *row = w.w + (size_t)(rg + g) * w.stride;
-                    qa[g] = ldg_stream(row + (size_t)b * 128 + hf * 64 + sg * 16);
-                    qb[g] = ldg_stream(row + (size_t)b * 128 + hf * 64 + 32 + sg * 16);
-                    qh[g] = ldg_stream(row + (size_t)nb * 128 + (size_t)b * 64 + hf * 32 + sg * 16);
-                    scv[g] = __ldg((const uint4 *)(row + (size_t)nb * 192 + (size_t)b * 16));
-                    dw[g] = h2f(__ldg((const unsigned short *)(row + (size_t)nb * 208) + b));
+            for (int q = 0; q < 4; q++) {
+                const int ch = hf * 2 + (q >> 1), l = (2 * q + sg) & 3;
+                const int4 av = *(const int4 *)&s.qp[(size_t)l * (K / 4) + (b * 4 + piece_of_chunk(ch)) * 16];
+                uint32_t code[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const uint32_t src = (q & 1) ? B[j] : A[j];
+                    code[j] = ((src >> (4 * (q >> 1))) & 0x0f0f0f0fu) | (((Hh[j] >> (2 * q)) & 0x03030303u) << 4);
                 }
-            }
-#pragma unroll
-            for (int g = 0; g < R; g++) {
-                const int8_t *sc = (const int8_t *)&scv[g];
-                const uint32_t A[4] = {qa[g].x, qa[g].y, qa[g].z, qa[g].w}, B[4] = {qb[g].x, qb[g].y, qb[g].z, qb[g].w};
-                const uint32_t Hh[4] = {qh[g].x, qh[g].y, qh[g].z, qh[g].w};
-                int acc_i = 0;
-                if (ok) {
-#pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const int ch = hf * 2 + (q >> 1), l = (2 * q + sg) & 3;
-                        const int4 av = *(const int4 *)&s.qp[(size_t)l * (K / 4) + (b * 4 + piece_of_chunk(ch)) * 16];
-                        uint32_t code[4];
-#pragma unroll
-                        for (int j = 0; j < 4; j++) {
-                            const uint32_t src = (q & 1) ? B[j] : A[j];
-                            code[j] = ((src >> (4 * (q >> 1))) & 0x0f0f0f0fu) | (((Hh[j] >> (2 * q)) & 0x03030303u) << 4);
-                        }
-                        int tq = dp4a((int)code[0], av.x, 0);
-                        tq = dp4a((int)code[1], av.y, tq);
-                        tq = dp4a((int)code[2], av.z, tq);
-                        tq = dp4a((int)code[3], av.w, tq);
-                        const int sub = hf * 8 + 2 * q + sg;
-                        tq -= 32 * (int)s.bs[b * 16 + sub];
-                        acc_i += (int)sc[sub] * tq;
-                    }
-                }
-                acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 1);
-                acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 2);
-                if (ok && (lane & 3) == 0) acc[g] += dw[g] * s.d[b] * (float)acc_i;
+                int tq = dp4a((int)code[0], av.x, 0);
+                tq = dp4a((int)code[1], av.y, tq);
+                tq = dp4a((int)code[2], av.z, tq);
+                tq = dp4a((int)code[3], av.w, tq);
+                const int sub = hf * 8 + 2 * q + sg;
+                tq -= 32 * (int)s.bs[b * 16 + sub];
+                acc_i += (int)sc[sub] * tq;
             }
         }
-#pragma unroll
-        for (int g = 0; g < R; g++) {
-            const float v = warp_sum(acc[g]);
-            const int r = rg + g;
-            if (lane == 0 && r < r1 && r < a.vocab_out) {
-                const unsigned long long key = argmax_key(v, (uint32_t)r);
-                if (key > best) best = key;
-            }
-        }
+        acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 1);
+        acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 2);
+        if (ok && (lane & 3) == 0) acc += dw * s.d[b] * (float)acc_i;
     }
-    return best;
+    return warp_sum(acc);
+}
+
+// Thread 0: arm ring stage `si % ns` and copy rows [r0 + si*kHeadRows, ...)
+// of this CTA's head slice into it.
+__device__ __forceinline__ void head_fill(const MegaArgs &a, uint8_t *smem, uint64_t *hbar, int si, int r0, int r1) {
+    const int k = si % a.head_ns, row = r0 + si * kHeadRows, n = min(kHeadRows, r1 - row);
+    const unsigned bytes = (unsigned)n * (unsigned)a.head.stride;
+    mbar_expect(&hbar[k], bytes);
+    bulk_g2s(smem + a.head_off[k], a.head.w + (size_t)row * a.head.stride, bytes, &hbar[k]);
 }
 
 // ---------------------------------------------------------------- the kernel
@@ -480,6 +472,7 @@ template <int HD, int G, int CF>
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_constant__ MegaArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ __align__(8) uint64_t mbar[4];  // weight slots
+    __shared__ __align__(8) uint64_t hbar[4];  // LM-head ring stages
     __shared__ int s_flag;
     __shared__ unsigned long long s_best[kMegaWarps];
     __shared__ __align__(16) float sq[G][HD];
@@ -495,11 +488,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     for (int i = tid; i < a.L * (int)(sizeof(MegaLayer) / 8); i += kMegaThreads)
         ((unsigned long long *)tab)[i] = ((const unsigned long long *)a.layers)[i];
     if (tid == 0) {
-        for (int i = 0; i < 4; i++) mbar_init(&mbar[i]);
+        for (int i = 0; i < 4; i++) {
+            mbar_init(&mbar[i]);
+            mbar_init(&hbar[i]);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
     unsigned ph[4] = {0, 0, 0, 0};  // parity each mbarrier completes next
+    unsigned hph[4] = {0, 0, 0, 0}, hpend = 0;  // head ring: parities, stages in flight
     unsigned pending = 0;              // bit i: a fill of mbarrier i is outstanding (same in every thread)
     unsigned target = 0;
     int tli = 0, tls = 0;
@@ -510,6 +507,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
         return p >= 0 && p < a.ctx && (int)blockIdx.x < a.kvh * ((p + kDecSplit) / kDecSplit);
     };
     const auto ncache_of = [&](int p) { return max(0, min(p, aj0 + kDecSplit) - aj0); };
+    const int hr0 = blockIdx.x * a.rpc[4], hr1 = min(hr0 + a.rpc[4], a.head.n);
+    const int hst = hr1 > hr0 ? (hr1 - hr0 + kHeadRows - 1) / kHeadRows : 0;  // head ring stages per step
     // prime: layer 0's weight slots and K/V rows, the first norm weights
     if (tid == 0)
         for (int t = 0; t < 4; t++) mega_fill(a, tab, smem, &mbar[t], t, 0);
@@ -646,7 +645,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 }
                 pending |= 2u;
                 // this layer's attention is done with the K/V area: stage the next layer's rows
-                if (attn_cta(npos)) mega_kv_fill<HD>(a, tab[nl], sK, sV, akvh, aj0, ncache_of(npos));
+                // (after the last layer the area carries the LM-head ring; the next step's rows
+                // follow the head)
+                if (l + 1 < a.L && attn_cta(npos)) mega_kv_fill<HD>(a, tab[nl], sK, sV, akvh, aj0, ncache_of(npos));
             }
             norm_preload<2>(ly.ffn_norm, a.H, npre);
             if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
@@ -686,7 +687,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             tl_mark(a, tli);
             tl_cta(a, step == 1 && l == 5, 6);
             bar_arrive(a, target);
-            if (more && ok) {
+            if (more && ok && l + 1 < a.L) {  // after the last layer: once the head is done
                 if (tid == 0) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     mega_fill(a, tab, smem, &mbar[2], 2, nl);
@@ -727,12 +728,20 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             tl_mark(a, tli);
             tl_cta(a, step == 1 && l == 5, 8);
             bar_arrive(a, target);
-            if (more && ok) {
+            if (more && ok && l + 1 < a.L) {  // after the last layer: once the head is done
                 if (tid == 0) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     mega_fill(a, tab, smem, &mbar[3], 3, nl);
                 }
                 pending |= 8u;
+            }
+            if (l + 1 == a.L && ok) {
+                // gate|up and down slots and the K/V area are free: start the LM-head ring
+                if (tid == 0) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    for (int k = 0; k < a.head_ns && k < hst; k++) head_fill(a, smem, hbar, k, hr0, hr1);
+                }
+                for (int k = 0; k < a.head_ns && k < hst; k++) hpend |= 1u << k;
             }
             norm_preload<2>(l + 1 < a.L ? tab[l + 1].attn_norm : a.out_norm, a.H, npre);
             if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
@@ -740,11 +749,38 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             tl_mark(a, tli);
         }
         if (!ok) break;
-        // ---- LM head + argmax (rows < vocab_out compete)
+        // ---- LM head + argmax (rows < vocab_out compete), rows streamed through the ring
         {
             mega_stage<2>(a.h, &npre, a.eps, a.H, st);
-            const int rpc = a.rpc[4], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.head.n);
-            const unsigned long long best = mega_head_q6k(a, st, r0, r1);
+            const int nb = a.H / 256;
+            unsigned long long best = 0;
+            for (int si = 0; si < hst && ok; si++) {
+                const int k = si % a.head_ns;
+                if (__syncthreads_and(mbar_wait(&hbar[k], hph[k]))) {
+                    hph[k] ^= 1;
+                    hpend &= ~(1u << k);
+                } else {
+                    if (tid == 0) raise_err(a, MEGA_ERR_WEIGHTS);
+                    ok = false;
+                    break;
+                }
+                const int r = hr0 + si * kHeadRows + warp;
+                if (r < hr1) {
+                    const float v = q6k_row_smem(smem + a.head_off[k] + (size_t)warp * a.head.stride, nb, a.H, st);
+                    if (lane == 0 && r < a.vocab_out) {
+                        const unsigned long long key = argmax_key(v, (uint32_t)r);
+                        if (key > best) best = key;
+                    }
+                }
+                __syncthreads();  // stage k consumed
+                if (si + a.head_ns < hst) {
+                    if (tid == 0) {
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        head_fill(a, smem, hbar, si + a.head_ns, hr0, hr1);
+                    }
+                    hpend |= 1u << k;
+                }
+            }
             if (lane == 0) s_best[warp] = best;
             __syncthreads();
             if (tid == 0) {
@@ -756,6 +792,16 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
         tl_mark(a, tli);
         bar_arrive(a, target);
         norm_preload<2>(tab[0].attn_norm, a.H, npre);
+        if (ok && step + 1 < a.steps) {
+            // the ring is drained: layer 0's gate|up and down slices and K/V rows for the next step
+            if (tid == 0) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mega_fill(a, tab, smem, &mbar[2], 2, 0);
+                mega_fill(a, tab, smem, &mbar[3], 3, 0);
+            }
+            pending |= 4u | 8u;
+            if (attn_cta(pos + 1)) mega_kv_fill<HD>(a, tab[0], sK, sV, akvh, aj0, ncache_of(pos + 1));
+        }
         if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
         tl_mark(a, tli);
         // ---- token bookkeeping (decode_finalize's rules), in every CTA
@@ -782,8 +828,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     }
     // copies still in flight into this CTA's shared memory (error exits)
     if (tid == 0)
-        for (int i = 0; i < 4; i++)
+        for (int i = 0; i < 4; i++) {
             if (pending & (1u << i)) mbar_wait(&mbar[i], ph[i]);
+            if (hpend & (1u << i)) mbar_wait(&hbar[i], hph[i]);
+        }
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
 }
@@ -791,6 +839,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
 // Dynamic shared memory plan of decode_mega for a model shape.
 struct MegaPlan {
     int rpc[5], slot_off[4], stage_off, attn_off, kmax;
+    int head_ns, head_off[4];  // LM-head ring: stages placed in the gate|up + down slots and the K/V area
     size_t bytes;
 };
 
@@ -813,7 +862,19 @@ inline MegaPlan mega_plan(int grid, int H, int F, int qd, int kvd, int vocab, in
     p.attn_off = (int)off;
     off += (size_t)kDecSplit * (HD * 2 + kMegaKPad) + (size_t)kDecSplit * HD * 2;
     p.bytes = off;
+    p.head_ns = 0;
     return p;
+}
+
+// Place up to four head-ring stages of kHeadRows rows of `head_stride` bytes
+// in regions that are idle while the head runs; false if fewer than two fit.
+inline bool mega_head_ring(MegaPlan &p, long long head_stride) {
+    const size_t sb = (size_t)kHeadRows * (size_t)head_stride;
+    p.head_ns = 0;
+    for (size_t o = (size_t)p.slot_off[2]; o + sb <= (size_t)p.stage_off && p.head_ns < 4; o += sb)
+        p.head_off[p.head_ns++] = (int)o;
+    for (size_t o = (size_t)p.attn_off; o + sb <= p.bytes && p.head_ns < 4; o += sb) p.head_off[p.head_ns++] = (int)o;
+    return p.head_ns >= 2;
 }
 
 }  // namespace hyk
