@@ -107,6 +107,8 @@ struct HyCtx {
     unsigned long long *d_tl = nullptr;
     int tl_cap = 0;
     MegaPlan mega_plan_v{};
+    int head_keep = 0;              // head rows per CTA kept resident in L2 by the persistent kernel
+    size_t l2_bytes = 0;
     void *mega_kernel = nullptr;
 };
 
@@ -600,6 +602,9 @@ bool mega_check(HyCtx *c) {
     c->mega_plan_v = mega_plan(c->nsm, c->H, c->F, c->qd, c->kvd, c->outw->n, c->hd);
     if (c->outw->stride % 16 || !mega_head_ring(c->mega_plan_v, c->outw->stride))
         return no("LM-head rows do not fit the shared-memory ring");
+    // about three quarters of L2 holds the first rows of every CTA's head slice
+    // across tokens (the layer weights, read once per token, are evict-first)
+    c->head_keep = (int)((double)c->l2_bytes * 0.75 / ((double)c->nsm * (double)c->outw->stride));
     if (cudaFuncSetAttribute(c->mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)c->mega_plan_v.bytes) != cudaSuccess) {
         cudaGetLastError();
@@ -660,6 +665,7 @@ bool mega_launch(HyCtx *c, int steps) {
     a.attn_off = p.attn_off;
     a.kmax = p.kmax;
     a.head_ns = p.head_ns;
+    a.head_keep = c->head_keep;
     for (int i = 0; i < 4; i++) a.head_off[i] = p.head_off[i];
     AttnArgs &aa = a.attn;
     aa.qkv = c->d_qkv;
@@ -1161,6 +1167,7 @@ HYC_API void *hyc_create(int device, char *info, size_t cap) {
     HyCtx *c = new HyCtx();
     c->dev = device;
     c->nsm = p.multiProcessorCount;
+    c->l2_bytes = (size_t)p.l2CacheSize;
     init_kernel_attrs();
     set_smem(quantize_export);
     if (cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking) != cudaSuccess ||

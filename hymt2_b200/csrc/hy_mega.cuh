@@ -63,6 +63,7 @@ struct MegaArgs {
     int kmax;                 // largest GEMV input length (stage plan)
     int head_ns;              // LM-head ring stages (kHeadRows rows each) and their smem offsets
     int head_off[4];
+    int head_keep;            // rows of each CTA's head slice read with L2 evict-last (stay resident)
     AttnArgs attn;            // shape, rope tables, part buffer; per-layer fields set in-kernel
     WDesc head, embd;
     int vocab_out;
@@ -107,6 +108,27 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned by
                      smem_u32(dst)),
                  "l"(src), "r"(bytes), "r"(smem_u32(bar))
                  : "memory");
+}
+// The same copy with an L2 eviction policy (createpolicy): layer weights are
+// read once per token (evict first); the part of the LM head kept resident
+// across tokens is read with evict last.
+__device__ __forceinline__ void bulk_g2s_hint(void *dst, const void *src, unsigned bytes, uint64_t *bar,
+                                              uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
 }
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
     unsigned v;
@@ -192,6 +214,7 @@ __host__ __device__ inline int mega_phase_rows(int t, int H, int F, int qd, int 
 // rows of GEMV t of layer l (codes, then scales after an aligned gap).
 __device__ inline void mega_fill(const MegaArgs &a, const MegaLayer *tab, uint8_t *smem, uint64_t *bar, int t,
                                  int l) {
+    const uint64_t pol = l2_policy_evict_first();
     const MegaLayer &ly = tab[l];
     const int K = mega_phase_k(t, a.H, a.F, a.qd);
     const int nb = K / 256, rb = nb * 64, rpc = a.rpc[t];
@@ -206,10 +229,10 @@ __device__ inline void mega_fill(const MegaArgs &a, const MegaLayer *tab, uint8_
     if (t == 2) {  // interleaved gate|up: gate rows at slot rows [0,n), up rows at [rpc/2, rpc/2+n)
         const int g0 = r0 >> 1, n = ((r1 + 1) >> 1) - g0;
         mbar_expect(bar, 2u * n * (rb + nb * 4));
-        bulk_g2s(sw, ly.w[4] + (size_t)g0 * rb, n * rb, bar);
-        bulk_g2s(sw + (size_t)(rpc >> 1) * rb, ly.w[5] + (size_t)g0 * rb, n * rb, bar);
-        bulk_g2s(ss, ly.s[4] + (size_t)g0 * nb, n * nb * 4, bar);
-        bulk_g2s(ss + (size_t)(rpc >> 1) * nb, ly.s[5] + (size_t)g0 * nb, n * nb * 4, bar);
+        bulk_g2s_hint(sw, ly.w[4] + (size_t)g0 * rb, n * rb, bar, pol);
+        bulk_g2s_hint(sw + (size_t)(rpc >> 1) * rb, ly.w[5] + (size_t)g0 * rb, n * rb, bar, pol);
+        bulk_g2s_hint(ss, ly.s[4] + (size_t)g0 * nb, n * nb * 4, bar, pol);
+        bulk_g2s_hint(ss + (size_t)(rpc >> 1) * nb, ly.s[5] + (size_t)g0 * nb, n * nb * 4, bar, pol);
         return;
     }
     mbar_expect(bar, (unsigned)(r1 - r0) * (rb + nb * 4));
@@ -219,16 +242,16 @@ __device__ inline void mega_fill(const MegaArgs &a, const MegaLayer *tab, uint8_
         for (int wi = 0; wi < 3; wi++) {
             const int s0 = max(r0, base), s1 = min(r1, lim[wi]);
             if (s0 < s1) {
-                bulk_g2s(sw + (size_t)(s0 - r0) * rb, ly.w[wi] + (size_t)(s0 - base) * rb, (s1 - s0) * rb, bar);
-                bulk_g2s(ss + (size_t)(s0 - r0) * nb, ly.s[wi] + (size_t)(s0 - base) * nb, (s1 - s0) * nb * 4, bar);
+                bulk_g2s_hint(sw + (size_t)(s0 - r0) * rb, ly.w[wi] + (size_t)(s0 - base) * rb, (s1 - s0) * rb, bar, pol);
+                bulk_g2s_hint(ss + (size_t)(s0 - r0) * nb, ly.s[wi] + (size_t)(s0 - base) * nb, (s1 - s0) * nb * 4, bar, pol);
             }
             base = lim[wi];
         }
         return;
     }
     const int wi = t == 1 ? 3 : 6;
-    bulk_g2s(sw, ly.w[wi] + (size_t)r0 * rb, (r1 - r0) * rb, bar);
-    bulk_g2s(ss, ly.s[wi] + (size_t)r0 * nb, (r1 - r0) * nb * 4, bar);
+    bulk_g2s_hint(sw, ly.w[wi] + (size_t)r0 * rb, (r1 - r0) * rb, bar, pol);
+    bulk_g2s_hint(ss, ly.s[wi] + (size_t)r0 * nb, (r1 - r0) * nb * 4, bar, pol);
 }
 
 // ---------------------------------------------------------------- activation staging
@@ -433,7 +456,8 @@ __device__ __forceinline__ void head_fill(const MegaArgs &a, uint8_t *smem, uint
     const int k = si % a.head_ns, row = r0 + si * kHeadRows, n = min(kHeadRows, r1 - row);
     const unsigned bytes = (unsigned)n * (unsigned)a.head.stride;
     mbar_expect(&hbar[k], bytes);
-    bulk_g2s(smem + a.head_off[k], a.head.w + (size_t)row * a.head.stride, bytes, &hbar[k]);
+    const uint64_t pol = si * kHeadRows < a.head_keep ? l2_policy_evict_last() : l2_policy_evict_first();
+    bulk_g2s_hint(smem + a.head_off[k], a.head.w + (size_t)row * a.head.stride, bytes, &hbar[k], pol);
 }
 
 // ---------------------------------------------------------------- the kernel
