@@ -56,6 +56,15 @@ __device__ __forceinline__ float warp_max(float v) {
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
+// Byte i (0..15) of a 16-byte register vector.  Selecting the word and
+// shifting keeps the vector in registers; indexing it as a byte array with a
+// lane-dependent index would place it in local memory.
+__device__ __forceinline__ uint32_t u4_byte(const uint4 &v, int i) {
+    const int ws = i >> 2;
+    const uint32_t w = ws == 0 ? v.x : (ws == 1 ? v.y : (ws == 2 ? v.z : v.w));
+    return (w >> (8 * (i & 3))) & 0xffu;
+}
+
 __device__ __forceinline__ float bf16_bits_to_f32(uint32_t h16) { return __uint_as_float(h16 << 16); }
 
 // Round-to-nearest-even fp32 -> bf16 bits, identical to the host's integer

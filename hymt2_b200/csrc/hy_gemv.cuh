@@ -656,6 +656,11 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt(const __grid_const
 
 // ---------------------------------------------------------------- Q6_K
 
+// Sub-scale `sub` (0..15) of a Q6_K block whose 16 int8 scales are held in
+// scv.  Selecting the word and shifting keeps scv in registers; indexing it
+// as a byte array with a lane-dependent index would go through local memory.
+__device__ __forceinline__ int q6k_subscale(const uint4 &scv, int sub) { return (int)(int8_t)u4_byte(scv, sub); }
+
 // Unit = (block b, half hf, 16-group s): ql[hf*64+s*16..+16], ql[..+32],
 // qh[hf*32+s*16..+16] -> 64 codes in 4 quarters of 16; quarter q covers
 // natural elements hf*128 + q*32 + s*16 + [0,16) with sub-scale index
@@ -695,7 +700,6 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q6k(const __grid_constant__
                 scv = __ldg((const uint4 *)(row + (size_t)nb * 192 + (size_t)b * 16));
                 dw = h2f(__ldg((const unsigned short *)(row + (size_t)nb * 208) + b));
             }
-            const int8_t *sc = (const int8_t *)&scv;
             const uint32_t A[4] = {qa.x, qa.y, qa.z, qa.w}, B[4] = {qb.x, qb.y, qb.z, qb.w};
             const uint32_t Hh[4] = {qh.x, qh.y, qh.z, qh.w};
             uint32_t code[4][4];
@@ -725,7 +729,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q6k(const __grid_constant__
                         tq = dp4a((int)code[q][3], av.w, tq);
                         const int sub = hf * 8 + 2 * q + sg;
                         tq -= 32 * (int)s.bs[(size_t)t * nb * 16 + b * 16 + sub];
-                        acc_i += (int)sc[sub] * tq;
+                        acc_i += q6k_subscale(scv, sub) * tq;
                     }
                 }
                 acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 1);
@@ -745,13 +749,15 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q6k(const __grid_constant__
 
 // ---------------------------------------------------------------- Q4_K
 
-__device__ __forceinline__ void k4_scale_min(const uint8_t *q, int j, int &sc, int &mn) {
+// Scale and min of sub-block j from a Q4_K block header held in registers
+// (hdr = d, dmin, scales[12]; the scales start at byte 4).
+__device__ __forceinline__ void k4_scale_min(const uint4 &hdr, int j, int &sc, int &mn) {
     if (j < 4) {
-        sc = q[j] & 63;
-        mn = q[j + 4] & 63;
+        sc = (int)(u4_byte(hdr, 4 + j) & 63);
+        mn = (int)(u4_byte(hdr, 8 + j) & 63);
     } else {
-        sc = (q[j + 4] & 0x0f) | ((q[j - 4] >> 6) << 4);
-        mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+        sc = (int)((u4_byte(hdr, 8 + j) & 0x0f) | ((u4_byte(hdr, j) >> 6) << 4));
+        mn = (int)((u4_byte(hdr, 8 + j) >> 4) | ((u4_byte(hdr, 4 + j) >> 6) << 4));
     }
 }
 
@@ -789,11 +795,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q4k(const __grid_constant__
                 qv = ldg_stream(row + (size_t)b * 144 + 16 + g * 32 + sg * 16);
                 hdr = __ldg((const uint4 *)(row + (size_t)b * 144));
             }
-            const uint8_t *hb = (const uint8_t *)&hdr;
             int sc0, mn0, sc1, mn1;
-            k4_scale_min(hb + 4, 2 * g, sc0, mn0);
-            k4_scale_min(hb + 4, 2 * g + 1, sc1, mn1);
-            const float dd = h2f(*(const unsigned short *)hb), dm = h2f(*(const unsigned short *)(hb + 2));
+            k4_scale_min(hdr, 2 * g, sc0, mn0);
+            k4_scale_min(hdr, 2 * g + 1, sc1, mn1);
+            const float dd = h2f((unsigned short)(hdr.x & 0xffffu)), dm = h2f((unsigned short)(hdr.x >> 16));
             const uint32_t Q[4] = {qv.x, qv.y, qv.z, qv.w};
 #pragma unroll
             for (int t = 0; t < NT; t++) {

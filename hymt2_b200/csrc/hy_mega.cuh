@@ -419,7 +419,6 @@ __device__ __forceinline__ float q6k_row_smem(const uint8_t *row, int nb, int K,
             scv = *(const uint4 *)(row + (size_t)nb * 192 + (size_t)b * 16);
             dw = h2f(*(const unsigned short *)(row + (size_t)nb * 208 + 2 * b));
         }
-        const int8_t *sc = (const int8_t *)&scv;
         const uint32_t A[4] = {qa.x, qa.y, qa.z, qa.w}, B[4] = {qb.x, qb.y, qb.z, qb.w};
         const uint32_t Hh[4] = {qh.x, qh.y, qh.z, qh.w};
         int acc_i = 0;
@@ -440,7 +439,7 @@ __device__ __forceinline__ float q6k_row_smem(const uint8_t *row, int nb, int K,
                 tq = dp4a((int)code[3], av.w, tq);
                 const int sub = hf * 8 + 2 * q + sg;
                 tq -= 32 * (int)s.bs[b * 16 + sub];
-                acc_i += (int)sc[sub] * tq;
+                acc_i += q6k_subscale(scv, sub) * tq;
             }
         }
         acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 1);
@@ -778,9 +777,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             mega_stage<2>(a.h, &npre, a.eps, a.H, st);
             const int nb = a.H / 256;
             unsigned long long best = 0;
+            unsigned long long tw = 0, tc = 0, ts = 0, t0 = a.tl ? gtimer() : 0;
             for (int si = 0; si < hst && ok; si++) {
                 const int k = si % a.head_ns;
-                if (__syncthreads_and(mbar_wait(&hbar[k], hph[k]))) {
+                const bool ready = __syncthreads_and(mbar_wait(&hbar[k], hph[k]));
+                unsigned long long t1 = a.tl ? gtimer() : 0;
+                tw += t1 - t0;
+                if (ready) {
                     hph[k] ^= 1;
                     hpend &= ~(1u << k);
                 } else {
@@ -796,7 +799,16 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                         if (key > best) best = key;
                     }
                 }
+                if (a.tl) {
+                    t0 = gtimer();
+                    tc += t0 - t1;
+                }
                 __syncthreads();  // stage k consumed
+                if (a.tl) {
+                    t1 = gtimer();
+                    ts += t1 - t0;
+                    t0 = t1;
+                }
                 if (si + a.head_ns < hst) {
                     if (tid == 0) {
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -804,6 +816,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                     }
                     hpend |= 1u << k;
                 }
+            }
+            if (a.tl && blockIdx.x == 0 && tid == 0 && step < 8) {
+                a.tl[a.tl_cap / 2 + 6000 + step * 4 + 0] = tw;
+                a.tl[a.tl_cap / 2 + 6000 + step * 4 + 1] = tc;
+                a.tl[a.tl_cap / 2 + 6000 + step * 4 + 2] = ts;
+                a.tl[a.tl_cap / 2 + 6000 + step * 4 + 3] = hst;
             }
             if (lane == 0) s_best[warp] = best;
             __syncthreads();
