@@ -25,6 +25,8 @@ struct AttnArgs {
     float *part;            // decode split partials [kv_heads][max_splits][G][HD+2]
     int *tickets;           // [kv_heads], zero between launches
     int split_len, max_splits;
+    float *cpart;           // wide decode partials [heads][max_chunks][HD+2]
+    int max_chunks, units;  // attn_max_chunks(ctx); units available (SMs)
     int trace;              // timeline slot (< 0: off)
 };
 
@@ -512,6 +514,253 @@ __global__ void __launch_bounds__(kDecWarps * 32) attn_decode2(const __grid_cons
     const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * HD + ((c + j) % CH) * 8); };
     attn_dec_main<HD, G>(a, kvh, split, pos, krow, sV, sq, skc, svc, S, 1);
     trace_mark(a.trace, 3);
+}
+
+// ---------------------------------------------------------------- wide decode attention
+//
+// Decode attention as many small units: unit (KV head g, chunk c) handles the
+// G query heads of g over keys [c*cs, min((c+1)*cs, pos+1)), cs a multiple of
+// 32 chosen so that kv_heads * chunks <= units (the SM count), and writes one
+// partial (running max m, sum l, unnormalised p.V) per query head and chunk.
+// attn_merge_head turns a head's partials into its output with the
+// log-sum-exp rule.  Inside a unit (kDecWarps warps): warp w takes head
+// w % G and the key subset sub = w / G; four lanes share a key, each
+// multiplying HD/4 dimensions, so one warp scores 8 keys at once.  The
+// per-layer path runs units as attn_chunk_kernel + attn_merge_kernel; the
+// persistent kernel runs them as CTAs of its attention phase and merges in
+// its o_proj staging, with the same arithmetic.
+constexpr int kChunkMin = 32;   // smallest chunk (keys)
+constexpr int kChunkMax = 128;  // largest chunk: the staging area holds kChunkMax rows
+
+// Chunk length for position pos: the smallest multiple of 32 that keeps
+// kv_heads * ceil((pos + 1) / cs) <= units; 0 if even kChunkMax does not.
+__host__ __device__ inline int attn_chunk_len(int pos, int kv_heads, int units) {
+    for (int cs = kChunkMin; cs <= kChunkMax; cs += kChunkMin)
+        if (kv_heads * ((pos + cs) / cs) <= units) return cs;
+    return 0;
+}
+__host__ __device__ inline int attn_max_chunks(int ctx) { return (ctx + kChunkMin - 1) / kChunkMin; }
+
+template <int HD>
+struct ChunkScratch {
+    float pm[kDecWarps], pl[kDecWarps];
+    float po[kDecWarps][HD];
+};
+
+// All kDecWarps warps of a unit.  krow(j, c) is 16-byte chunk c of staged K
+// row j (j relative to the chunk start), sV[j][HD] the staged V rows; key
+// `pos` comes from skc/svc.  Writes part[(h * max_chunks + chunk) * (HD+2)]
+// = (m, l, o[HD]) for h = kvh*G .. kvh*G+G-1.  Synchronises the kDecWarps
+// warps with named barrier bar_id.
+template <int HD, int G, typename KRow>
+__device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int chunk, int cs, int pos, KRow krow,
+                                                const uint16_t *sV, const float (*sq)[HD], const float *skc,
+                                                const float *svc, ChunkScratch<HD> &S, int bar_id) {
+    constexpr int DQ = HD / 4;            // dims per lane in a 4-lane key group
+    constexpr int DPL = HD / 32;          // output dims per lane
+    constexpr int NSUB = kDecWarps / G;   // warps per head
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, grp = lane >> 2, qtr = lane & 3;
+    const int hh = w % G, sub = w / G;
+    const int j0 = chunk * cs, nk = min(pos + 1 - j0, cs);
+    const int kw = (cs + NSUB - 1) / NSUB;  // keys of this warp: [sub*kw, sub*kw + kw)
+    const int kb = sub * kw, ke = min(kb + kw, nk);
+    constexpr int KMAX = (kChunkMax / NSUB + 7) / 8;  // keys per lane group (upper bound)
+    float mloc = -INFINITY;
+    float s[KMAX];
+#pragma unroll
+    for (int t = 0; t < KMAX; t++) {
+        const int j = kb + grp + 8 * t;
+        s[t] = -INFINITY;
+        if (j < ke) {
+            float dot = 0.f;
+            const float *qv = &sq[hh][qtr * DQ];
+            if (j0 + j == pos) {
+                const float *kv = &skc[qtr * DQ];
+#pragma unroll
+                for (int d = 0; d < DQ; d += 4) {
+                    const float4 q4 = *(const float4 *)&qv[d], k4 = *(const float4 *)&kv[d];
+                    dot = fmaf(q4.x, k4.x, dot);
+                    dot = fmaf(q4.y, k4.y, dot);
+                    dot = fmaf(q4.z, k4.z, dot);
+                    dot = fmaf(q4.w, k4.w, dot);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < DQ / 8; c++) {
+                    const uint4 kk = *krow(j, qtr * (DQ / 8) + c);
+                    const float4 qa = *(const float4 *)&qv[c * 8], qb = *(const float4 *)&qv[c * 8 + 4];
+                    dot = fmaf(qa.x, bf16_bits_to_f32(kk.x & 0xffffu), dot);
+                    dot = fmaf(qa.y, bf16_bits_to_f32(kk.x >> 16), dot);
+                    dot = fmaf(qa.z, bf16_bits_to_f32(kk.y & 0xffffu), dot);
+                    dot = fmaf(qa.w, bf16_bits_to_f32(kk.y >> 16), dot);
+                    dot = fmaf(qb.x, bf16_bits_to_f32(kk.z & 0xffffu), dot);
+                    dot = fmaf(qb.y, bf16_bits_to_f32(kk.z >> 16), dot);
+                    dot = fmaf(qb.z, bf16_bits_to_f32(kk.w & 0xffffu), dot);
+                    dot = fmaf(qb.w, bf16_bits_to_f32(kk.w >> 16), dot);
+                }
+            }
+            s[t] = dot;  // partial over this lane's quarter of the dimensions
+        }
+    }
+    // the 4 quarters of each key: fixed butterfly order
+#pragma unroll
+    for (int t = 0; t < KMAX; t++) {
+        float v = s[t];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        const int j = kb + grp + 8 * t;
+        s[t] = j < ke ? v * a.scale : -INFINITY;
+        mloc = fmaxf(mloc, s[t]);
+    }
+    mloc = warp_max(mloc);
+    float lsum = 0.f;
+#pragma unroll
+    for (int t = 0; t < KMAX; t++) {
+        const int j = kb + grp + 8 * t;
+        s[t] = j < ke ? expf(s[t] - mloc) : 0.f;
+        if (qtr == 0) lsum += s[t];
+    }
+    lsum = warp_sum(lsum);
+    float o[DPL];
+#pragma unroll
+    for (int q = 0; q < DPL; q++) o[q] = 0.f;
+    for (int j = kb; j < ke; j++) {
+        const int t = (j - kb) >> 3, g8 = (j - kb) & 7;
+        float p = 0.f;
+#pragma unroll
+        for (int tt = 0; tt < KMAX; tt++)
+            if (tt == t) p = __shfl_sync(0xffffffffu, s[tt], g8 * 4);
+        float vv[DPL];
+        if (j0 + j == pos) {
+#pragma unroll
+            for (int q = 0; q < DPL; q++) vv[q] = svc[lane * DPL + q];
+        } else {
+            const uint16_t *vr = sV + (size_t)j * HD + lane * DPL;
+            if (DPL == 4) {
+                const uint2 x = *(const uint2 *)vr;
+                vv[0] = bf16_bits_to_f32(x.x & 0xffffu);
+                vv[1] = bf16_bits_to_f32(x.x >> 16);
+                vv[2] = bf16_bits_to_f32(x.y & 0xffffu);
+                vv[3] = bf16_bits_to_f32(x.y >> 16);
+            } else {
+#pragma unroll
+                for (int q = 0; q < DPL; q++) vv[q] = bf16_bits_to_f32(vr[q]);
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < DPL; q++) o[q] = fmaf(p, vv[q], o[q]);
+    }
+    if (lane == 0) {
+        S.pm[w] = kb < nk ? mloc : -INFINITY;
+        S.pl[w] = kb < nk ? lsum : 0.f;
+    }
+#pragma unroll
+    for (int q = 0; q < DPL; q++) S.po[w][lane * DPL + q] = o[q];
+    asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(kDecWarps * 32) : "memory");
+    if (w >= G) return;
+    float M = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < NSUB; u++) M = fmaxf(M, S.pm[w + u * G]);
+    float L = 0.f, O[DPL];
+#pragma unroll
+    for (int q = 0; q < DPL; q++) O[q] = 0.f;
+#pragma unroll
+    for (int u = 0; u < NSUB; u++) {
+        const int src = w + u * G;
+        const float f = S.pl[src] > 0.f ? expf(S.pm[src] - M) : 0.f;
+        L = fmaf(S.pl[src], f, L);
+#pragma unroll
+        for (int q = 0; q < DPL; q++) O[q] = fmaf(S.po[src][lane * DPL + q], f, O[q]);
+    }
+    float *pp = a.cpart + ((size_t)(kvh * G + w) * a.max_chunks + chunk) * (HD + 2);
+#pragma unroll
+    for (int q = 0; q < DPL; q++) pp[2 + lane * DPL + q] = O[q];
+    if (lane == 0) {
+        pp[0] = M;
+        pp[1] = L;
+    }
+}
+
+// One warp: output of head h from its nchunks partials (log-sum-exp merge in
+// chunk order), written to out[HD].
+template <int HD>
+__device__ __forceinline__ void attn_merge_head(const float *part, int max_chunks, int nchunks, int h, float *out) {
+    constexpr int DPL = HD / 32;
+    const int lane = threadIdx.x & 31;
+    const float *base = part + (size_t)h * max_chunks * (HD + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < nchunks; c++) M = fmaxf(M, __ldcg(base + (size_t)c * (HD + 2)));
+    float L = 0.f, O[DPL];
+#pragma unroll
+    for (int q = 0; q < DPL; q++) O[q] = 0.f;
+    for (int c = 0; c < nchunks; c++) {
+        const float *pc = base + (size_t)c * (HD + 2);
+        const float f = expf(__ldcg(pc) - M);
+        L = fmaf(__ldcg(pc + 1), f, L);
+#pragma unroll
+        for (int q = 0; q < DPL; q++) O[q] = fmaf(__ldcg(pc + 2 + lane * DPL + q), f, O[q]);
+    }
+    const float inv = 1.0f / L;
+#pragma unroll
+    for (int q = 0; q < DPL; q++) out[lane * DPL + q] = O[q] * inv;
+}
+
+// Per-layer form: grid (kv_heads, attn_max_chunks(ctx)); units past the
+// position's chunk count return.  Rows staged with cp.async (K rows padded
+// by 16 bytes so the 8 key groups of a warp read different banks).
+template <int HD, int G>
+__global__ void __launch_bounds__(kDecWarps * 32) attn_chunk_kernel(const __grid_constant__ AttnArgs a) {
+    constexpr int KROW = HD * 2 + 16, CH = HD / 8;
+    extern __shared__ __align__(16) uint8_t dsm[];
+    uint8_t *sK = dsm;
+    uint16_t *sV = (uint16_t *)(dsm + (size_t)kChunkMax * KROW);
+    __shared__ __align__(16) float sq[G][HD];
+    __shared__ __align__(16) float skc[HD], svc[HD];
+    __shared__ __align__(16) ChunkScratch<HD> S;
+    trace_mark(a.trace, 0);
+    pdl_trigger();
+    const int kvh = blockIdx.x, chunk = blockIdx.y, w = threadIdx.x >> 5;
+    const int pos = *a.pos_ptr;  // written before this graph / >= 2 kernels back
+    if (blockDim.x != kDecWarps * 32 || pos < 0 || pos >= a.ctx) return;
+    const int cs = attn_chunk_len(pos, a.kv_heads, a.units);
+    if (cs == 0 || chunk * cs > pos) return;
+    const int j0 = chunk * cs, ncache = max(0, min(pos, j0 + cs) - j0);
+    const uint16_t *Kg = a.kc + kvh * HD, *Vg = a.vc + kvh * HD;
+    for (int idx = threadIdx.x; idx < ncache * CH; idx += blockDim.x) {
+        const int j = idx / CH, c = idx - j * CH;
+        const size_t g = (size_t)(j0 + j) * a.kvdim + c * 8;
+        const unsigned dk = (unsigned)__cvta_generic_to_shared(sK + (size_t)j * KROW + c * 16);
+        const unsigned dv = (unsigned)__cvta_generic_to_shared(sV + (size_t)j * HD + c * 8);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk), "l"(Kg + g) : "memory");
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dv), "l"(Vg + g) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    DecConsts<HD> k;
+    if (w <= G) attn_dec_consts<HD, G>(a, pos, k);
+    pdl_wait();
+    trace_mark(a.trace, 1);
+    if (w <= G) attn_dec_prologue<HD, G>(a, kvh, pos, chunk == 0, k, sq, skc, svc);
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    trace_mark(a.trace, 2);
+    const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * KROW + c * 16); };
+    attn_chunk_main<HD, G>(a, kvh, chunk, cs, pos, krow, sV, sq, skc, svc, S, 1);
+    trace_mark(a.trace, 3);
+}
+
+template <int HD>
+__host__ __device__ inline size_t attn_chunk_smem() { return (size_t)kChunkMax * (HD * 2 + 16) + (size_t)kChunkMax * HD * 2; }
+
+// grid (heads), one warp: ao[h] from the partials of attn_chunk_kernel.
+template <int HD>
+__global__ void __launch_bounds__(32) attn_merge_kernel(const __grid_constant__ AttnArgs a) {
+    pdl_trigger();
+    pdl_wait();
+    const int pos = *a.pos_ptr;
+    if (pos < 0 || pos >= a.ctx) return;
+    const int cs = attn_chunk_len(pos, a.kv_heads, a.units);
+    if (cs == 0) return;
+    attn_merge_head<HD>(a.cpart, a.max_chunks, (pos + cs) / cs, blockIdx.x, a.ao + (size_t)blockIdx.x * HD);
 }
 
 // Prefill: token t (position *pos_ptr + t) attends to 0..pos inclusive; q

@@ -86,6 +86,8 @@ struct HyCtx {
     uint16_t *d_kv = nullptr;
     float *d_h = nullptr, *d_qkv = nullptr, *d_ao = nullptr, *d_g = nullptr, *d_u = nullptr, *d_logits = nullptr;
     float *d_part = nullptr;
+    float *d_cpart = nullptr;       // wide decode attention partials [heads][max_chunks][hd+2]
+    int max_chunks = 0;
     int *d_tickets = nullptr;
     int max_splits = 0;
     DecodeState *d_state = nullptr;
@@ -232,6 +234,14 @@ void init_kernel_attrs() {
     set_smem(attn_decode2<64, 2>);
     set_smem(attn_decode2<64, 4>);
     set_smem(attn_decode2<64, 8>);
+    set_smem(attn_chunk_kernel<128, 1>);
+    set_smem(attn_chunk_kernel<128, 2>);
+    set_smem(attn_chunk_kernel<128, 4>);
+    set_smem(attn_chunk_kernel<128, 8>);
+    set_smem(attn_chunk_kernel<64, 1>);
+    set_smem(attn_chunk_kernel<64, 2>);
+    set_smem(attn_chunk_kernel<64, 4>);
+    set_smem(attn_chunk_kernel<64, 8>);
 }
 
 // One launch for nt <= NT tokens.
@@ -345,6 +355,13 @@ bool run_multi(HyCtx *c, HyWeight *const *ws, float *const *outs, const int *lds
 
 template <int HD, int G>
 bool attn_launch(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
+    if (nt == 1 && aa.cpart && attn_chunk_len(aa.ctx - 1, aa.kv_heads, aa.units) > 0) {
+        // wide decode attention: units of (KV head, key chunk), then the per-head merge
+        if (!launch(c, attn_chunk_kernel<HD, G>, dim3(aa.kv_heads, aa.max_chunks), dim3(kDecWarps * 32),
+                    attn_chunk_smem<HD>(), pdl, aa))
+            return false;
+        return launch(c, attn_merge_kernel<HD>, dim3(aa.heads), dim3(32), 0, pdl, aa);
+    }
     if (nt == 1)
         return launch(c, attn_decode2<HD, G>, dim3(aa.kv_heads, aa.max_splits), dim3(kDecWarps * 32), attn_dec_smem<HD>(),
                       pdl, aa);
@@ -461,6 +478,9 @@ bool layer_forward(HyCtx *c, int li, int nt, const int *pos_ptr, bool pdl) {
         aa.scale = 1.0f / sqrtf((float)c->hd);
         aa.ao = c->d_ao;
         aa.part = c->d_part;
+        aa.cpart = c->d_cpart;
+        aa.max_chunks = c->max_chunks;
+        aa.units = c->nsm;
         aa.tickets = c->d_tickets;
         aa.split_len = kSplitLen;
         aa.max_splits = c->max_splits;
@@ -586,7 +606,8 @@ bool mega_check(HyCtx *c) {
     if (c->H > 2048 || c->qd > 2048) return no("hidden or q width above 2048");
     if (c->L > kMegaMaxLayers) return no("more layers than the persistent kernel's table holds");
     if (c->outw->fmt != FMT_Q6K || c->outw->k != c->H) return no("LM head is not Q6_K");
-    if (c->kvh > 64 || c->kvh * c->max_splits > c->nsm) return no("context too long for one attention CTA per split");
+    if (c->kvh > 64 || attn_chunk_len(c->ctx - 1, c->kvh, c->nsm) == 0)
+        return no("context too long for the attention units of one launch");
     const HyWeight *w0 = c->layers[0].q;
     for (const Layer &L : c->layers) {
         const HyWeight *ws[7] = {L.q, L.k, L.v, L.o, L.g, L.u, L.d};
@@ -685,6 +706,9 @@ bool mega_launch(HyCtx *c, int steps) {
     aa.scale = 1.0f / sqrtf((float)c->hd);
     aa.ao = c->d_ao;
     aa.part = c->d_part;
+        aa.cpart = c->d_cpart;
+        aa.max_chunks = c->max_chunks;
+        aa.units = c->nsm;
     aa.split_len = kSplitLen;
     aa.max_splits = c->max_splits;
     aa.trace = -1;
@@ -779,13 +803,13 @@ void free_fused(HyCtx *c) {
     graph_reset(c->g_dec);
     c->g_dec_vocab = -1;
     void *ptrs[] = {c->d_norms, c->d_out_norm, c->d_cos, c->d_sin, c->d_kv, c->d_h, c->d_qkv, c->d_ao,
-                    c->d_g, c->d_u, c->d_logits, c->d_part, c->d_tickets, c->d_state, c->d_out_ids,
+                    c->d_g, c->d_u, c->d_logits, c->d_part, c->d_cpart, c->d_tickets, c->d_state, c->d_out_ids,
                     c->d_tokens, c->d_chunk_pos};
     for (void *p : ptrs)
         if (p) cudaFree(p);
     c->d_norms = c->d_out_norm = c->d_cos = c->d_sin = nullptr;
     c->d_kv = nullptr;
-    c->d_h = c->d_qkv = c->d_ao = c->d_g = c->d_u = c->d_logits = c->d_part = nullptr;
+    c->d_h = c->d_qkv = c->d_ao = c->d_g = c->d_u = c->d_logits = c->d_part = c->d_cpart = nullptr;
     c->d_tickets = nullptr;
     c->d_state = nullptr;
     c->d_out_ids = c->d_tokens = c->d_chunk_pos = nullptr;
@@ -1038,6 +1062,8 @@ bool fused_prepare(void *impl, const hy_fused_args *sh) {
         CK(c, cudaMalloc(&c->d_u, T * c->F * 4));
         CK(c, cudaMalloc(&c->d_logits, vocab * 4));
         CK(c, cudaMalloc(&c->d_part, (size_t)c->kvh * c->max_splits * G * (c->hd + 2) * 4));
+        c->max_chunks = attn_max_chunks(c->ctx);
+        CK(c, cudaMalloc(&c->d_cpart, (size_t)c->heads * c->max_chunks * (c->hd + 2) * 4));
         CK(c, cudaMalloc(&c->d_tickets, (size_t)c->kvh * 4));
         CK(c, cudaMemsetAsync(c->d_tickets, 0, (size_t)c->kvh * 4, c->st));
         CK(c, cudaMalloc(&c->d_state, sizeof(DecodeState)));
@@ -1514,6 +1540,9 @@ HYC_API int hyc_bench_op(void *impl, int op, int iters) {
             aa.scale = 1.0f / sqrtf((float)c->hd);
             aa.ao = c->d_ao;
             aa.part = c->d_part;
+        aa.cpart = c->d_cpart;
+        aa.max_chunks = c->max_chunks;
+        aa.units = c->nsm;
             aa.tickets = c->d_tickets;
             aa.split_len = kSplitLen;
             aa.max_splits = c->max_splits;
@@ -1620,7 +1649,8 @@ HYC_API int hyc_attention_test(void *impl, int heads, int kv_heads, int hdim, in
     const int splits = (ctx + kSplitLen - 1) / kSplitLen;
     const size_t qkv_b = (size_t)nt * (qd + 2 * kvd) * 4, kv_b = (size_t)ctx * kvd * 2, tab_b = (size_t)ctx * half * 4;
     float *dqkv = nullptr, *dqn = nullptr, *dkn = nullptr, *dcos = nullptr, *dsin = nullptr, *dao = nullptr,
-          *dpart = nullptr;
+          *dpart = nullptr, *dcpart = nullptr;
+    const int max_chunks = attn_max_chunks(ctx);
     uint16_t *dkc = nullptr, *dvc = nullptr;
     int *dtick = nullptr, *dpos = nullptr;
     bool ok = cudaMalloc(&dqkv, qkv_b) == cudaSuccess && cudaMalloc(&dkc, kv_b) == cudaSuccess &&
@@ -1628,6 +1658,7 @@ HYC_API int hyc_attention_test(void *impl, int heads, int kv_heads, int hdim, in
               cudaMalloc(&dkn, hdim * 4) == cudaSuccess && cudaMalloc(&dcos, tab_b) == cudaSuccess &&
               cudaMalloc(&dsin, tab_b) == cudaSuccess && cudaMalloc(&dao, (size_t)nt * qd * 4) == cudaSuccess &&
               cudaMalloc(&dpart, (size_t)kv_heads * splits * G * (hdim + 2) * 4) == cudaSuccess &&
+              cudaMalloc(&dcpart, (size_t)heads * max_chunks * (hdim + 2) * 4) == cudaSuccess &&
               cudaMalloc(&dtick, kv_heads * 4) == cudaSuccess && cudaMalloc(&dpos, 4) == cudaSuccess &&
               cudaMemsetAsync(dtick, 0, kv_heads * 4, c->st) == cudaSuccess &&
               h2d(c, dpos, &pos0, 4) == cudaSuccess &&
@@ -1665,13 +1696,16 @@ HYC_API int hyc_attention_test(void *impl, int heads, int kv_heads, int hdim, in
         aa.tickets = dtick;
         aa.split_len = kSplitLen;
         aa.max_splits = splits;
+        aa.cpart = dcpart;
+        aa.max_chunks = max_chunks;
+        aa.units = c->nsm;
         ok = attention(c, aa, nt, false) &&
              cudaMemcpyAsync(ao, dao, (size_t)nt * qd * 4, cudaMemcpyDeviceToHost, c->st) == cudaSuccess &&
              cudaMemcpyAsync(kc, dkc, kv_b, cudaMemcpyDeviceToHost, c->st) == cudaSuccess &&
              cudaMemcpyAsync(vc, dvc, kv_b, cudaMemcpyDeviceToHost, c->st) == cudaSuccess &&
              cudaStreamSynchronize(c->st) == cudaSuccess;
     }
-    void *ptrs[] = {dqkv, dqn, dkn, dcos, dsin, dao, dpart, dkc, dvc, dtick, dpos};
+    void *ptrs[] = {dqkv, dqn, dkn, dcos, dsin, dao, dpart, dcpart, dkc, dvc, dtick, dpos};
     for (void *p : ptrs) cudaFree(p);
     return ok ? 0 : -1;
 }

@@ -321,6 +321,19 @@ __device__ inline void mega_stage(const float *x, const NormPre<SV> *pre, float 
     __syncthreads();
 }
 
+// o_proj staging: the attention output of every head, merged from the wide
+// attention's chunk partials (attn_merge_head, one warp per head), then Q8_K.
+template <int HD>
+__device__ inline void mega_stage_attn(const MegaArgs &a, int pos, Q8Smem &s) {
+    const int cs = attn_chunk_len(pos, a.kvh, gridDim.x), nch = (pos + cs) / cs, heads = a.qd / HD;
+    for (int h = threadIdx.x >> 5; h < heads; h += kMegaWarps)
+        attn_merge_head<HD>(a.attn.cpart, a.attn.max_chunks, nch, h, s.x + (size_t)h * HD);
+    __syncthreads();
+    const int nb = a.qd / 256;
+    for (int b = threadIdx.x >> 5; b < nb; b += kMegaWarps) quantize_block_warp(s.x, s, 0, b, nb, a.qd);
+    __syncthreads();
+}
+
 template <int CPL>
 __device__ __forceinline__ void mega_act(const Q8Smem &s, int K, int4 (&act)[CPL][4], float (&dblk)[CPL],
                                          int (&sblk)[CPL]) {
@@ -500,7 +513,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     __shared__ unsigned long long s_best[kMegaWarps];
     __shared__ __align__(16) float sq[G][HD];
     __shared__ __align__(16) float skc[HD], svc[HD];
-    __shared__ __align__(16) DecScratch<HD> S;
+    __shared__ __align__(16) ChunkScratch<HD> S;
     __shared__ __align__(16) MegaLayer tab[kMegaMaxLayers];
     constexpr int KROW = HD * 2 + kMegaKPad;
     constexpr int RGQ = 2, RGO = 1, RGU = 6, RGD = 1;  // rows per warp iteration per phase
@@ -525,18 +538,22 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     int tli = 0, tls = 0;
     int tok = a.st->tok, pos = a.st->pos;
     bool ok = true;
-    const int akvh = blockIdx.x % a.kvh, asplit = blockIdx.x / a.kvh, aj0 = asplit * kDecSplit;
+    // attention unit of this CTA: (KV head akvh, key chunk achunk) of the wide decode attention
+    const int akvh = blockIdx.x % a.kvh, achunk = blockIdx.x / a.kvh;
+    const auto cs_of = [&](int p) { return attn_chunk_len(p, a.kvh, gridDim.x); };
     const auto attn_cta = [&](int p) {
-        return p >= 0 && p < a.ctx && (int)blockIdx.x < a.kvh * ((p + kDecSplit) / kDecSplit);
+        const int cs = cs_of(p);
+        return p >= 0 && p < a.ctx && cs > 0 && (int)blockIdx.x < a.kvh * ((p + cs) / cs);
     };
-    const auto ncache_of = [&](int p) { return max(0, min(p, aj0 + kDecSplit) - aj0); };
+    const auto j0_of = [&](int p) { return achunk * cs_of(p); };
+    const auto ncache_of = [&](int p) { return max(0, min(p, j0_of(p) + cs_of(p)) - j0_of(p)); };
     const int hr0 = blockIdx.x * a.rpc[4], hr1 = min(hr0 + a.rpc[4], a.head.n);
     const int hst = hr1 > hr0 ? (hr1 - hr0 + kHeadRows - 1) / kHeadRows : 0;  // head ring stages per step
     // prime: layer 0's weight slots and K/V rows, the first norm weights
     if (tid == 0)
         for (int t = 0; t < 4; t++) mega_fill(a, tab, smem, &mbar[t], t, 0);
     pending |= 0xfu;
-    if (a.steps > 0 && attn_cta(pos)) mega_kv_fill<HD>(a, tab[0], sK, sV, akvh, aj0, ncache_of(pos));
+    if (a.steps > 0 && attn_cta(pos)) mega_kv_fill<HD>(a, tab[0], sK, sV, akvh, j0_of(pos), ncache_of(pos));
     NormPre<2> npre;
     norm_preload<2>(tab[0].attn_norm, a.H, npre);
     for (int step = 0; step < a.steps && ok; step++) {
@@ -613,14 +630,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             if (l == 0 && blockIdx.x == 0 && tid == 0) a.sync->amax[(step + 1) & 1] = 0ull;
             // ---- attention (the CTAs of the splits that hold keys)
             if (is_attn) {
-                if (warp <= G) attn_dec_prologue<HD, G>(aa, akvh, pos, asplit == 0, kcs, sq, skc, svc);
+                if (warp <= G) attn_dec_prologue<HD, G>(aa, akvh, pos, achunk == 0, kcs, sq, skc, svc);
                 tl_sub(a, tls);
                 asm volatile("cp.async.wait_group 0;" ::: "memory");
                 __syncthreads();  // K/V rows of every thread, and sq / skc / svc
                 tl_sub(a, tls);
                 if (ok) {
                     const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * KROW + c * 16); };
-                    attn_dec_main<HD, G>(aa, akvh, asplit, pos, krow, sV, sq, skc, svc, S, 1);
+                    attn_chunk_main<HD, G>(aa, akvh, achunk, cs_of(pos), pos, krow, sV, sq, skc, svc, S, 1);
                 }
                 tl_sub(a, tls);
             }
@@ -632,7 +649,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             tl_mark(a, tli);
             // ---- o_proj (+ residual)
             {
-                mega_stage<2>(a.ao, (const NormPre<2> *)nullptr, a.eps, a.qd, st);
+                mega_stage_attn<HD>(a, pos, st);
                 tl_sub(a, tls);
                 int4 act[1][4];
                 float dblk[1];
@@ -670,7 +687,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 // this layer's attention is done with the K/V area: stage the next layer's rows
                 // (after the last layer the area carries the LM-head ring; the next step's rows
                 // follow the head)
-                if (l + 1 < a.L && attn_cta(npos)) mega_kv_fill<HD>(a, tab[nl], sK, sV, akvh, aj0, ncache_of(npos));
+                if (l + 1 < a.L && attn_cta(npos)) mega_kv_fill<HD>(a, tab[nl], sK, sV, akvh, j0_of(npos), ncache_of(npos));
             }
             norm_preload<2>(ly.ffn_norm, a.H, npre);
             if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
@@ -842,7 +859,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 mega_fill(a, tab, smem, &mbar[3], 3, 0);
             }
             pending |= 4u | 8u;
-            if (attn_cta(pos + 1)) mega_kv_fill<HD>(a, tab[0], sK, sV, akvh, aj0, ncache_of(pos + 1));
+            if (attn_cta(pos + 1)) mega_kv_fill<HD>(a, tab[0], sK, sV, akvh, j0_of(pos + 1), ncache_of(pos + 1));
         }
         if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
         tl_mark(a, tli);
