@@ -534,7 +534,9 @@ constexpr int kChunkMax = 128;  // largest chunk: the staging area holds kChunkM
 
 // Chunk length for position pos: the smallest multiple of 32 that keeps
 // kv_heads * ceil((pos + 1) / cs) <= units; 0 if even kChunkMax does not.
+constexpr int kMaxUnits = 160;  // attention units per position (>= the SM count of a B200)
 __host__ __device__ inline int attn_chunk_len(int pos, int kv_heads, int units) {
+    if (units > kMaxUnits) units = kMaxUnits;
     for (int cs = kChunkMin; cs <= kChunkMax; cs += kChunkMin)
         if (kv_heads * ((pos + cs) / cs) <= units) return cs;
     return 0;
@@ -585,19 +587,26 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
                     dot = fmaf(q4.w, k4.w, dot);
                 }
             } else {
+                // one accumulator per 16-byte chunk (independent chains), then a fixed-order sum
+                float part[DQ / 8];
+                uint4 kk[DQ / 8];
+#pragma unroll
+                for (int c = 0; c < DQ / 8; c++) kk[c] = *krow(j, qtr * (DQ / 8) + c);
 #pragma unroll
                 for (int c = 0; c < DQ / 8; c++) {
-                    const uint4 kk = *krow(j, qtr * (DQ / 8) + c);
                     const float4 qa = *(const float4 *)&qv[c * 8], qb = *(const float4 *)&qv[c * 8 + 4];
-                    dot = fmaf(qa.x, bf16_bits_to_f32(kk.x & 0xffffu), dot);
-                    dot = fmaf(qa.y, bf16_bits_to_f32(kk.x >> 16), dot);
-                    dot = fmaf(qa.z, bf16_bits_to_f32(kk.y & 0xffffu), dot);
-                    dot = fmaf(qa.w, bf16_bits_to_f32(kk.y >> 16), dot);
-                    dot = fmaf(qb.x, bf16_bits_to_f32(kk.z & 0xffffu), dot);
-                    dot = fmaf(qb.y, bf16_bits_to_f32(kk.z >> 16), dot);
-                    dot = fmaf(qb.z, bf16_bits_to_f32(kk.w & 0xffffu), dot);
-                    dot = fmaf(qb.w, bf16_bits_to_f32(kk.w >> 16), dot);
+                    float d = qa.x * bf16_bits_to_f32(kk[c].x & 0xffffu);
+                    d = fmaf(qa.y, bf16_bits_to_f32(kk[c].x >> 16), d);
+                    d = fmaf(qa.z, bf16_bits_to_f32(kk[c].y & 0xffffu), d);
+                    d = fmaf(qa.w, bf16_bits_to_f32(kk[c].y >> 16), d);
+                    d = fmaf(qb.x, bf16_bits_to_f32(kk[c].z & 0xffffu), d);
+                    d = fmaf(qb.y, bf16_bits_to_f32(kk[c].z >> 16), d);
+                    d = fmaf(qb.z, bf16_bits_to_f32(kk[c].w & 0xffffu), d);
+                    d = fmaf(qb.w, bf16_bits_to_f32(kk[c].w >> 16), d);
+                    part[c] = d;
                 }
+#pragma unroll
+                for (int c = 0; c < DQ / 8; c++) dot += part[c];
             }
             s[t] = dot;  // partial over this lane's quarter of the dimensions
         }
@@ -624,13 +633,16 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
     float o[DPL];
 #pragma unroll
     for (int q = 0; q < DPL; q++) o[q] = 0.f;
-    for (int j = kb; j < ke; j++) {
-        const int t = (j - kb) >> 3, g8 = (j - kb) & 7;
+    // p of key j lives in s[(j - kb) >> 3] of lane group (j - kb) & 7
+    const auto p_of = [&](int j) {
+        const int t = (j - kb) >> 3, src = ((j - kb) & 7) * 4;
         float p = 0.f;
 #pragma unroll
         for (int tt = 0; tt < KMAX; tt++)
-            if (tt == t) p = __shfl_sync(0xffffffffu, s[tt], g8 * 4);
-        float vv[DPL];
+            if (tt == t) p = __shfl_sync(0xffffffffu, s[tt], src);
+        return p;
+    };
+    const auto v_of = [&](int j, float (&vv)[DPL]) {
         if (j0 + j == pos) {
 #pragma unroll
             for (int q = 0; q < DPL; q++) vv[q] = svc[lane * DPL + q];
@@ -647,6 +659,24 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
                 for (int q = 0; q < DPL; q++) vv[q] = bf16_bits_to_f32(vr[q]);
             }
         }
+    };
+    int j = kb;
+    for (; j + 4 <= ke; j += 4) {  // four keys' p and V rows fetched before any FMA
+        float p[4], vv[4][DPL];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            p[u] = p_of(j + u);
+            v_of(j + u, vv[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+            for (int q = 0; q < DPL; q++) o[q] = fmaf(p[u], vv[u][q], o[q]);
+    }
+    for (; j < ke; j++) {
+        float vv[DPL];
+        const float p = p_of(j);
+        v_of(j, vv);
 #pragma unroll
         for (int q = 0; q < DPL; q++) o[q] = fmaf(p, vv[q], o[q]);
     }
@@ -683,22 +713,62 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
 
 // One warp: output of head h from its nchunks partials (log-sum-exp merge in
 // chunk order), written to out[HD].
+// Lane c holds chunk c's (m, l) (chunks beyond 32 fold in lane order); M by
+// warp max, L by warp sum of l_c e^(m_c - M), O over chunks in order with the
+// chunk weights broadcast from their lanes and four chunks' rows loaded at once.
 template <int HD>
 __device__ __forceinline__ void attn_merge_head(const float *part, int max_chunks, int nchunks, int h, float *out) {
     constexpr int DPL = HD / 32;
     const int lane = threadIdx.x & 31;
     const float *base = part + (size_t)h * max_chunks * (HD + 2);
-    float M = -INFINITY;
-    for (int c = 0; c < nchunks; c++) M = fmaxf(M, __ldcg(base + (size_t)c * (HD + 2)));
-    float L = 0.f, O[DPL];
+    constexpr int NR = (kMaxUnits + 31) / 32;  // nchunks <= kMaxUnits (attn_chunk_len)
+    float mc[NR], lc[NR];
+#pragma unroll
+    for (int r = 0; r < NR; r++) {
+        const int c = lane + 32 * r;
+        mc[r] = c < nchunks ? __ldcg(base + (size_t)c * (HD + 2)) : -INFINITY;
+        lc[r] = c < nchunks ? __ldcg(base + (size_t)c * (HD + 2) + 1) : 0.f;
+    }
+    float mm = mc[0];
+#pragma unroll
+    for (int r = 1; r < NR; r++) mm = fmaxf(mm, mc[r]);
+    const float M = warp_max(mm);
+    float f[NR], lf = 0.f;
+#pragma unroll
+    for (int r = 0; r < NR; r++) {
+        f[r] = lane + 32 * r < nchunks ? expf(mc[r] - M) : 0.f;
+        lf = fmaf(lc[r], f[r], lf);
+    }
+    const float L = warp_sum(lf);
+    const auto f_of = [&](int cc) {  // weight of chunk cc, from lane cc % 32
+        float v = 0.f;
+#pragma unroll
+        for (int r = 0; r < NR; r++)
+            if ((cc >> 5) == r) v = __shfl_sync(0xffffffffu, f[r], cc & 31);
+        return v;
+    };
+    float O[DPL];
 #pragma unroll
     for (int q = 0; q < DPL; q++) O[q] = 0.f;
-    for (int c = 0; c < nchunks; c++) {
-        const float *pc = base + (size_t)c * (HD + 2);
-        const float f = expf(__ldcg(pc) - M);
-        L = fmaf(__ldcg(pc + 1), f, L);
+    int c = 0;
+    for (; c + 4 <= nchunks; c += 4) {
+        float fw[4], ov[4][DPL];
 #pragma unroll
-        for (int q = 0; q < DPL; q++) O[q] = fmaf(__ldcg(pc + 2 + lane * DPL + q), f, O[q]);
+        for (int u = 0; u < 4; u++) {
+            const int cc = c + u;
+            fw[u] = f_of(cc);
+#pragma unroll
+            for (int q = 0; q < DPL; q++) ov[u][q] = __ldcg(base + (size_t)cc * (HD + 2) + 2 + lane * DPL + q);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+#pragma unroll
+            for (int q = 0; q < DPL; q++) O[q] = fmaf(ov[u][q], fw[u], O[q]);
+    }
+    for (; c < nchunks; c++) {
+        const float fw = f_of(c);
+#pragma unroll
+        for (int q = 0; q < DPL; q++) O[q] = fmaf(__ldcg(base + (size_t)c * (HD + 2) + 2 + lane * DPL + q), fw, O[q]);
     }
     const float inv = 1.0f / L;
 #pragma unroll
