@@ -530,6 +530,8 @@ __global__ void __launch_bounds__(kDecWarps * 32) attn_decode2(const __grid_cons
 // persistent kernel runs them as CTAs of its attention phase and merges in
 // its o_proj staging, with the same arithmetic.
 constexpr int kChunkMin = 32;   // smallest chunk (keys)
+constexpr int kChunkKPad = 64;  // staged K rows padded by 64 bytes: two key groups hit disjoint banks
+constexpr int kPartPad = 4;     // partial = (m, l, -, -, o[HD]): o 16-byte aligned
 constexpr int kChunkMax = 128;  // largest chunk: the staging area holds kChunkMax rows
 
 // Chunk length for position pos: the smallest multiple of 32 that keeps
@@ -574,27 +576,34 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
         const int j = kb + grp + 8 * t;
         s[t] = -INFINITY;
         if (j < ke) {
+            // lane quarter qtr takes the 8-dim chunks qtr + 4i (bank-spread q and K reads);
+            // one accumulator per chunk (independent chains), then a fixed-order sum
             float dot = 0.f;
-            const float *qv = &sq[hh][qtr * DQ];
+            float part[DQ / 8];
             if (j0 + j == pos) {
-                const float *kv = &skc[qtr * DQ];
-#pragma unroll
-                for (int d = 0; d < DQ; d += 4) {
-                    const float4 q4 = *(const float4 *)&qv[d], k4 = *(const float4 *)&kv[d];
-                    dot = fmaf(q4.x, k4.x, dot);
-                    dot = fmaf(q4.y, k4.y, dot);
-                    dot = fmaf(q4.z, k4.z, dot);
-                    dot = fmaf(q4.w, k4.w, dot);
-                }
-            } else {
-                // one accumulator per 16-byte chunk (independent chains), then a fixed-order sum
-                float part[DQ / 8];
-                uint4 kk[DQ / 8];
-#pragma unroll
-                for (int c = 0; c < DQ / 8; c++) kk[c] = *krow(j, qtr * (DQ / 8) + c);
 #pragma unroll
                 for (int c = 0; c < DQ / 8; c++) {
-                    const float4 qa = *(const float4 *)&qv[c * 8], qb = *(const float4 *)&qv[c * 8 + 4];
+                    const int d0 = (qtr + 4 * c) * 8;
+                    const float4 qa = *(const float4 *)&sq[hh][d0], qb = *(const float4 *)&sq[hh][d0 + 4];
+                    const float4 ka = *(const float4 *)&skc[d0], kb4 = *(const float4 *)&skc[d0 + 4];
+                    float d = qa.x * ka.x;
+                    d = fmaf(qa.y, ka.y, d);
+                    d = fmaf(qa.z, ka.z, d);
+                    d = fmaf(qa.w, ka.w, d);
+                    d = fmaf(qb.x, kb4.x, d);
+                    d = fmaf(qb.y, kb4.y, d);
+                    d = fmaf(qb.z, kb4.z, d);
+                    d = fmaf(qb.w, kb4.w, d);
+                    part[c] = d;
+                }
+            } else {
+                uint4 kk[DQ / 8];
+#pragma unroll
+                for (int c = 0; c < DQ / 8; c++) kk[c] = *krow(j, qtr + 4 * c);
+#pragma unroll
+                for (int c = 0; c < DQ / 8; c++) {
+                    const int d0 = (qtr + 4 * c) * 8;
+                    const float4 qa = *(const float4 *)&sq[hh][d0], qb = *(const float4 *)&sq[hh][d0 + 4];
                     float d = qa.x * bf16_bits_to_f32(kk[c].x & 0xffffu);
                     d = fmaf(qa.y, bf16_bits_to_f32(kk[c].x >> 16), d);
                     d = fmaf(qa.z, bf16_bits_to_f32(kk[c].y & 0xffffu), d);
@@ -605,9 +614,9 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
                     d = fmaf(qb.w, bf16_bits_to_f32(kk[c].w >> 16), d);
                     part[c] = d;
                 }
-#pragma unroll
-                for (int c = 0; c < DQ / 8; c++) dot += part[c];
             }
+#pragma unroll
+            for (int c = 0; c < DQ / 8; c++) dot += part[c];
             s[t] = dot;  // partial over this lane's quarter of the dimensions
         }
     }
@@ -702,9 +711,9 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
 #pragma unroll
         for (int q = 0; q < DPL; q++) O[q] = fmaf(S.po[src][lane * DPL + q], f, O[q]);
     }
-    float *pp = a.cpart + ((size_t)(kvh * G + w) * a.max_chunks + chunk) * (HD + 2);
+    float *pp = a.cpart + ((size_t)(kvh * G + w) * a.max_chunks + chunk) * (HD + kPartPad);
 #pragma unroll
-    for (int q = 0; q < DPL; q++) pp[2 + lane * DPL + q] = O[q];
+    for (int q = 0; q < DPL; q++) pp[kPartPad + lane * DPL + q] = O[q];
     if (lane == 0) {
         pp[0] = M;
         pp[1] = L;
@@ -713,21 +722,49 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
 
 // One warp: output of head h from its nchunks partials (log-sum-exp merge in
 // chunk order), written to out[HD].
-// Lane c holds chunk c's (m, l) (chunks beyond 32 fold in lane order); M by
-// warp max, L by warp sum of l_c e^(m_c - M), O over chunks in order with the
-// chunk weights broadcast from their lanes and four chunks' rows loaded at once.
+// Lane c holds chunk c's (m, l); M by warp max, L by warp sum of
+// l_c e^(m_c - M) (lane order), O over chunks in chunk order with the chunk
+// weights broadcast from their lanes.  Every load of the first four chunks is
+// issued before any arithmetic.
+// DPL consecutive floats (DPL = 2 or 4, naturally aligned) through L2.
+template <int DPL>
+__device__ __forceinline__ void ldcg_dpl(const float *p, float (&v)[DPL]) {
+    if constexpr (DPL == 4) {
+        const float4 x = __ldcg((const float4 *)p);
+        v[0] = x.x;
+        v[1] = x.y;
+        v[2] = x.z;
+        v[3] = x.w;
+    } else {
+        const float2 x = __ldcg((const float2 *)p);
+        v[0] = x.x;
+        v[1] = x.y;
+    }
+}
+
 template <int HD>
 __device__ __forceinline__ void attn_merge_head(const float *part, int max_chunks, int nchunks, int h, float *out) {
-    constexpr int DPL = HD / 32;
+    constexpr int DPL = HD / 32, ST = HD + kPartPad;
     const int lane = threadIdx.x & 31;
-    const float *base = part + (size_t)h * max_chunks * (HD + 2);
+    const float *base = part + (size_t)h * max_chunks * ST;
     constexpr int NR = (kMaxUnits + 31) / 32;  // nchunks <= kMaxUnits (attn_chunk_len)
     float mc[NR], lc[NR];
 #pragma unroll
     for (int r = 0; r < NR; r++) {
         const int c = lane + 32 * r;
-        mc[r] = c < nchunks ? __ldcg(base + (size_t)c * (HD + 2)) : -INFINITY;
-        lc[r] = c < nchunks ? __ldcg(base + (size_t)c * (HD + 2) + 1) : 0.f;
+        const float2 ml = c < nchunks ? __ldcg((const float2 *)(base + (size_t)c * ST)) : make_float2(-INFINITY, 0.f);
+        mc[r] = ml.x;
+        lc[r] = ml.y;
+    }
+    float ov0[4][DPL];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        if (u < nchunks) {
+            ldcg_dpl<DPL>(base + (size_t)u * ST + kPartPad + lane * DPL, ov0[u]);
+        } else {
+#pragma unroll
+            for (int q = 0; q < DPL; q++) ov0[u][q] = 0.f;
+        }
     }
     float mm = mc[0];
 #pragma unroll
@@ -750,25 +787,20 @@ __device__ __forceinline__ void attn_merge_head(const float *part, int max_chunk
     float O[DPL];
 #pragma unroll
     for (int q = 0; q < DPL; q++) O[q] = 0.f;
-    int c = 0;
-    for (; c + 4 <= nchunks; c += 4) {
-        float fw[4], ov[4][DPL];
 #pragma unroll
-        for (int u = 0; u < 4; u++) {
-            const int cc = c + u;
-            fw[u] = f_of(cc);
+    for (int u = 0; u < 4; u++) {
+        if (u < nchunks) {
+            const float fw = f_of(u);
 #pragma unroll
-            for (int q = 0; q < DPL; q++) ov[u][q] = __ldcg(base + (size_t)cc * (HD + 2) + 2 + lane * DPL + q);
+            for (int q = 0; q < DPL; q++) O[q] = fmaf(ov0[u][q], fw, O[q]);
         }
-#pragma unroll
-        for (int u = 0; u < 4; u++)
-#pragma unroll
-            for (int q = 0; q < DPL; q++) O[q] = fmaf(ov[u][q], fw[u], O[q]);
     }
-    for (; c < nchunks; c++) {
+    for (int c = 4; c < nchunks; c++) {
         const float fw = f_of(c);
+        float vv[DPL];
+        ldcg_dpl<DPL>(base + (size_t)c * ST + kPartPad + lane * DPL, vv);
 #pragma unroll
-        for (int q = 0; q < DPL; q++) O[q] = fmaf(__ldcg(base + (size_t)c * (HD + 2) + 2 + lane * DPL + q), fw, O[q]);
+        for (int q = 0; q < DPL; q++) O[q] = fmaf(vv[q], fw, O[q]);
     }
     const float inv = 1.0f / L;
 #pragma unroll
@@ -780,7 +812,7 @@ __device__ __forceinline__ void attn_merge_head(const float *part, int max_chunk
 // by 16 bytes so the 8 key groups of a warp read different banks).
 template <int HD, int G>
 __global__ void __launch_bounds__(kDecWarps * 32) attn_chunk_kernel(const __grid_constant__ AttnArgs a) {
-    constexpr int KROW = HD * 2 + 16, CH = HD / 8;
+    constexpr int KROW = HD * 2 + kChunkKPad, CH = HD / 8;
     extern __shared__ __align__(16) uint8_t dsm[];
     uint8_t *sK = dsm;
     uint16_t *sV = (uint16_t *)(dsm + (size_t)kChunkMax * KROW);
@@ -819,7 +851,9 @@ __global__ void __launch_bounds__(kDecWarps * 32) attn_chunk_kernel(const __grid
 }
 
 template <int HD>
-__host__ __device__ inline size_t attn_chunk_smem() { return (size_t)kChunkMax * (HD * 2 + 16) + (size_t)kChunkMax * HD * 2; }
+__host__ __device__ inline size_t attn_chunk_smem() {
+    return (size_t)kChunkMax * (HD * 2 + kChunkKPad) + (size_t)kChunkMax * HD * 2;
+}
 
 // grid (heads), one warp: ao[h] from the partials of attn_chunk_kernel.
 template <int HD>

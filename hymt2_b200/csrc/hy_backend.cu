@@ -1063,7 +1063,7 @@ bool fused_prepare(void *impl, const hy_fused_args *sh) {
         CK(c, cudaMalloc(&c->d_logits, vocab * 4));
         CK(c, cudaMalloc(&c->d_part, (size_t)c->kvh * c->max_splits * G * (c->hd + 2) * 4));
         c->max_chunks = attn_max_chunks(c->ctx);
-        CK(c, cudaMalloc(&c->d_cpart, (size_t)c->heads * c->max_chunks * (c->hd + 2) * 4));
+        CK(c, cudaMalloc(&c->d_cpart, (size_t)c->heads * c->max_chunks * (c->hd + kPartPad) * 4));
         CK(c, cudaMalloc(&c->d_tickets, (size_t)c->kvh * 4));
         CK(c, cudaMemsetAsync(c->d_tickets, 0, (size_t)c->kvh * 4, c->st));
         CK(c, cudaMalloc(&c->d_state, sizeof(DecodeState)));
@@ -1658,7 +1658,7 @@ HYC_API int hyc_attention_test(void *impl, int heads, int kv_heads, int hdim, in
               cudaMalloc(&dkn, hdim * 4) == cudaSuccess && cudaMalloc(&dcos, tab_b) == cudaSuccess &&
               cudaMalloc(&dsin, tab_b) == cudaSuccess && cudaMalloc(&dao, (size_t)nt * qd * 4) == cudaSuccess &&
               cudaMalloc(&dpart, (size_t)kv_heads * splits * G * (hdim + 2) * 4) == cudaSuccess &&
-              cudaMalloc(&dcpart, (size_t)heads * max_chunks * (hdim + 2) * 4) == cudaSuccess &&
+              cudaMalloc(&dcpart, (size_t)heads * max_chunks * (hdim + kPartPad) * 4) == cudaSuccess &&
               cudaMalloc(&dtick, kv_heads * 4) == cudaSuccess && cudaMalloc(&dpos, 4) == cudaSuccess &&
               cudaMemsetAsync(dtick, 0, kv_heads * 4, c->st) == cudaSuccess &&
               h2d(c, dpos, &pos0, 4) == cudaSuccess &&

@@ -32,7 +32,7 @@ constexpr int kMegaThreads = 512;
 constexpr int kMegaWarps = kMegaThreads / 32;
 constexpr int kMegaRowAlign = 8;                           // row slices in multiples of 8
 constexpr unsigned long long kMegaWaitNs = 2000000000ull;  // 2 s bound on any wait
-constexpr int kMegaKPad = 16;                              // K rows padded in smem (bank spread)
+constexpr int kMegaKPad = kChunkKPad;                      // K rows padded in smem (bank spread)
 
 enum MegaErr { MEGA_OK = 0, MEGA_ERR_BARRIER = 1, MEGA_ERR_POS = 2, MEGA_ERR_WEIGHTS = 3, MEGA_ERR_KV = 4 };
 
