@@ -25,8 +25,10 @@ struct AttnArgs {
     float *part;            // decode split partials [kv_heads][max_splits][G][HD+2]
     int *tickets;           // [kv_heads], zero between launches
     int split_len, max_splits;
-    float *cpart;           // wide decode partials [heads][max_chunks][HD+2]
+    float *cpart;           // wide decode partials [heads][max_chunks][HD+kPartPad]
     int max_chunks, units;  // attn_max_chunks(ctx); units available (SMs)
+    unsigned long long *tpart;  // if set: partials as tagged words (float bits | ptag << 32) instead
+    unsigned ptag;
     int trace;              // timeline slot (< 0: off)
 };
 
@@ -234,13 +236,16 @@ __device__ __forceinline__ void attn_dec_consts(const AttnArgs &a, int pos, DecC
 
 // Warps 0..G: rope + norm of the G query heads into sq, of k (and the bf16
 // rounding of k and v) into skc/svc; when `store`, k and v go to the cache.
+// q of the G heads (qs[G*HD]), k (ks[HD]) and v (vs[HD]) of this KV head,
+// pre-rope, from any memory (the per-layer kernels pass the qkv row itself).
 template <int HD, int G>
 __device__ __forceinline__ void attn_dec_prologue(const AttnArgs &a, int kvh, int pos, bool store, const DecConsts<HD> &k,
-                                                  float (*sq)[HD], float *skc, float *svc) {
+                                                  float (*sq)[HD], float *skc, float *svc, const float *qs,
+                                                  const float *ks, const float *vs) {
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     float v[HD / 32], vraw[HD / 32];
-    const float *src = w < G ? a.qkv + (kvh * G + w) * HD : a.qkv + a.qdim + kvh * HD;
-    const float *vr = a.qkv + a.qdim + a.kvdim + kvh * HD;
+    const float *src = w < G ? qs + w * HD : ks;
+    const float *vr = vs;
 #pragma unroll
     for (int i = 0; i < HD / 32; i++) {
         v[i] = src[lane + 32 * i];
@@ -507,7 +512,8 @@ __global__ void __launch_bounds__(kDecWarps * 32) attn_decode2(const __grid_cons
     if (w <= G) attn_dec_consts<HD, G>(a, pos, k);
     pdl_wait();
     trace_mark(a.trace, 1);
-    if (w <= G) attn_dec_prologue<HD, G>(a, kvh, pos, split == 0, k, sq, skc, svc);
+    if (w <= G) attn_dec_prologue<HD, G>(a, kvh, pos, split == 0, k, sq, skc, svc, a.qkv + (kvh * G) * HD,
+                                        a.qkv + a.qdim + kvh * HD, a.qkv + a.qdim + a.kvdim + kvh * HD);
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
     trace_mark(a.trace, 2);
@@ -711,12 +717,28 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
 #pragma unroll
         for (int q = 0; q < DPL; q++) O[q] = fmaf(S.po[src][lane * DPL + q], f, O[q]);
     }
-    float *pp = a.cpart + ((size_t)(kvh * G + w) * a.max_chunks + chunk) * (HD + kPartPad);
+    const size_t po = ((size_t)(kvh * G + w) * a.max_chunks + chunk) * (HD + kPartPad);
+    if (a.tpart) {
+        unsigned long long *tp = a.tpart + po;
 #pragma unroll
-    for (int q = 0; q < DPL; q++) pp[kPartPad + lane * DPL + q] = O[q];
-    if (lane == 0) {
-        pp[0] = M;
-        pp[1] = L;
+        for (int q = 0; q < DPL; q += 2)
+            asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(tp + kPartPad + lane * DPL + q),
+                         "l"((unsigned long long)__float_as_uint(O[q]) | ((unsigned long long)a.ptag << 32)),
+                         "l"((unsigned long long)__float_as_uint(O[q + 1]) | ((unsigned long long)a.ptag << 32))
+                         : "memory");
+        if (lane == 0)
+            asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(tp),
+                         "l"((unsigned long long)__float_as_uint(M) | ((unsigned long long)a.ptag << 32)),
+                         "l"((unsigned long long)__float_as_uint(L) | ((unsigned long long)a.ptag << 32))
+                         : "memory");
+    } else {
+        float *pp = a.cpart + po;
+#pragma unroll
+        for (int q = 0; q < DPL; q++) pp[kPartPad + lane * DPL + q] = O[q];
+        if (lane == 0) {
+            pp[0] = M;
+            pp[1] = L;
+        }
     }
 }
 
@@ -726,33 +748,42 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
 // l_c e^(m_c - M) (lane order), O over chunks in chunk order with the chunk
 // weights broadcast from their lanes.  Every load of the first four chunks is
 // issued before any arithmetic.
-// DPL consecutive floats (DPL = 2 or 4, naturally aligned) through L2.
-template <int DPL>
-__device__ __forceinline__ void ldcg_dpl(const float *p, float (&v)[DPL]) {
-    if constexpr (DPL == 4) {
-        const float4 x = __ldcg((const float4 *)p);
-        v[0] = x.x;
-        v[1] = x.y;
-        v[2] = x.z;
-        v[3] = x.w;
-    } else {
-        const float2 x = __ldcg((const float2 *)p);
-        v[0] = x.x;
-        v[1] = x.y;
-    }
-}
-
+// Partials of one head in plain memory: (m, l) of chunk c and its o slice.
 template <int HD>
-__device__ __forceinline__ void attn_merge_head(const float *part, int max_chunks, int nchunks, int h, float *out) {
-    constexpr int DPL = HD / 32, ST = HD + kPartPad;
+struct PlainPartLoader {
+    const float *base;  // head's first chunk
+    __device__ __forceinline__ float2 ml(int c) const { return __ldcg((const float2 *)(base + (size_t)c * (HD + kPartPad))); }
+    template <int DPL>
+    __device__ __forceinline__ void o(int c, int lane, float (&v)[DPL]) const {
+        const float *p = base + (size_t)c * (HD + kPartPad) + kPartPad + lane * DPL;
+        if constexpr (DPL == 4) {
+            const float4 x = __ldcg((const float4 *)p);
+            v[0] = x.x;
+            v[1] = x.y;
+            v[2] = x.z;
+            v[3] = x.w;
+        } else {
+            const float2 x = __ldcg((const float2 *)p);
+            v[0] = x.x;
+            v[1] = x.y;
+        }
+    }
+};
+
+// One warp: output of a head from its nchunks partials.  Lane c holds chunk
+// c's (m, l); M by warp max, L by warp sum of l_c e^(m_c - M) (lane order), O
+// over chunks in chunk order with the chunk weights broadcast from their
+// lanes; the first four chunks' rows are loaded before any arithmetic.
+template <int HD, typename Loader>
+__device__ __forceinline__ void attn_merge_head_with(const Loader &ld, int nchunks, float *out) {
+    constexpr int DPL = HD / 32;
     const int lane = threadIdx.x & 31;
-    const float *base = part + (size_t)h * max_chunks * ST;
     constexpr int NR = (kMaxUnits + 31) / 32;  // nchunks <= kMaxUnits (attn_chunk_len)
     float mc[NR], lc[NR];
 #pragma unroll
     for (int r = 0; r < NR; r++) {
         const int c = lane + 32 * r;
-        const float2 ml = c < nchunks ? __ldcg((const float2 *)(base + (size_t)c * ST)) : make_float2(-INFINITY, 0.f);
+        const float2 ml = c < nchunks ? ld.ml(c) : make_float2(-INFINITY, 0.f);
         mc[r] = ml.x;
         lc[r] = ml.y;
     }
@@ -760,7 +791,7 @@ __device__ __forceinline__ void attn_merge_head(const float *part, int max_chunk
 #pragma unroll
     for (int u = 0; u < 4; u++) {
         if (u < nchunks) {
-            ldcg_dpl<DPL>(base + (size_t)u * ST + kPartPad + lane * DPL, ov0[u]);
+            ld.template o<DPL>(u, lane, ov0[u]);
         } else {
 #pragma unroll
             for (int q = 0; q < DPL; q++) ov0[u][q] = 0.f;
@@ -798,13 +829,19 @@ __device__ __forceinline__ void attn_merge_head(const float *part, int max_chunk
     for (int c = 4; c < nchunks; c++) {
         const float fw = f_of(c);
         float vv[DPL];
-        ldcg_dpl<DPL>(base + (size_t)c * ST + kPartPad + lane * DPL, vv);
+        ld.template o<DPL>(c, lane, vv);
 #pragma unroll
         for (int q = 0; q < DPL; q++) O[q] = fmaf(vv[q], fw, O[q]);
     }
     const float inv = 1.0f / L;
 #pragma unroll
     for (int q = 0; q < DPL; q++) out[lane * DPL + q] = O[q] * inv;
+}
+
+template <int HD>
+__device__ __forceinline__ void attn_merge_head(const float *part, int max_chunks, int nchunks, int h, float *out) {
+    const PlainPartLoader<HD> ld{part + (size_t)h * max_chunks * (HD + kPartPad)};
+    attn_merge_head_with<HD>(ld, nchunks, out);
 }
 
 // Per-layer form: grid (kv_heads, attn_max_chunks(ctx)); units past the
@@ -841,7 +878,9 @@ __global__ void __launch_bounds__(kDecWarps * 32) attn_chunk_kernel(const __grid
     if (w <= G) attn_dec_consts<HD, G>(a, pos, k);
     pdl_wait();
     trace_mark(a.trace, 1);
-    if (w <= G) attn_dec_prologue<HD, G>(a, kvh, pos, chunk == 0, k, sq, skc, svc);
+    if (w <= G)
+        attn_dec_prologue<HD, G>(a, kvh, pos, chunk == 0, k, sq, skc, svc, a.qkv + (kvh * G) * HD,
+                                 a.qkv + a.qdim + kvh * HD, a.qkv + a.qdim + a.kvdim + kvh * HD);
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
     trace_mark(a.trace, 2);
