@@ -542,7 +542,7 @@ constexpr int kChunkMax = 128;  // largest chunk: the staging area holds kChunkM
 
 // Chunk length for position pos: the smallest multiple of 32 that keeps
 // kv_heads * ceil((pos + 1) / cs) <= units; 0 if even kChunkMax does not.
-constexpr int kMaxUnits = 160;  // attention units per position (>= the SM count of a B200)
+constexpr int kMaxUnits = 64;   // attention units per position (two chunk weights per lane in the merge)
 __host__ __device__ inline int attn_chunk_len(int pos, int kv_heads, int units) {
     if (units > kMaxUnits) units = kMaxUnits;
     for (int cs = kChunkMin; cs <= kChunkMax; cs += kChunkMin)

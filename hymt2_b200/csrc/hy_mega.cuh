@@ -966,7 +966,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             tl_mark(a, tli);
             // ---- down (+ residual)
             if (d0 < d1) {
-                if (!mega_stage_t<2 * CF>(a.tact, T(step, l, 3), (const NormPre<2 * CF> *)nullptr, a.eps, a.F, st)) {
+                if (!mega_stage_t<CF>(a.tact, T(step, l, 3), (const NormPre<CF> *)nullptr, a.eps, a.F, st)) {
                     if (tid == 0) raise_err(a, MEGA_ERR_BARRIER);
                     ok = false;
                     break;
