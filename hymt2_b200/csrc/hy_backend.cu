@@ -658,7 +658,7 @@ bool mega_check(HyCtx *c) {
     }
     {
         const size_t words = (size_t)c->H + (size_t)(c->qd + 2 * c->kvd) + (size_t)c->F +
-                             (size_t)c->heads * c->max_chunks * (c->hd + kPartPad);
+                             (size_t)c->heads * c->max_chunks * (c->hd + kPartPad) + (size_t)2 * c->nsm;  // + done words
         if (c->tag_words != words) {
             if (c->d_tag) cudaFree(c->d_tag);
             c->d_tag = nullptr;
@@ -743,6 +743,7 @@ bool mega_launch(HyCtx *c, int steps) {
     a.tqkv = a.th + c->H;
     a.tact = a.tqkv + (c->qd + 2 * c->kvd);
     a.tpart = a.tact + c->F;
+    a.done = (unsigned *)(a.tpart + (size_t)c->heads * c->max_chunks * (c->hd + kPartPad));
     a.tag0 = c->mega_tag;
     c->mega_tag += (unsigned)steps * (unsigned)(c->L + 1) * 4u + 4u;  // this launch's tags are never reused soon
     a.tl = c->trace_on ? c->d_tl : nullptr;

@@ -70,7 +70,8 @@ struct MegaArgs {
     const float *out_norm;
     float *h, *qkv, *ao, *act;
     unsigned long long *th, *tqkv, *tact, *tpart;  // tagged activations: h, q|k|v, silu*up, attention partials
-    unsigned tag0;                                 // first tag of this launch
+    unsigned *done;  // per-CTA done words [4][grid]: o_proj rows, down rows, gate|up rows, attention unit
+    unsigned tag0;   // first tag of this launch
     DecodeState *st;
     int *out_ids;
     MegaSync *sync;
@@ -573,6 +574,35 @@ __device__ __forceinline__ bool tpoll1(const unsigned long long *p, unsigned tag
     return true;
 }
 
+// Done words: after its rows of a phase a producer CTA stores the phase's
+// tag into done[cta] (no fence).  A consumer first lets one warp poll the
+// nprod producers' done words (a few hundred bytes instead of the whole
+// vector, so 148 pollers do not flood the L2 lines of the data), then loads
+// the tagged data, whose own tags still decide.  Bounded; false on timeout.
+__device__ __forceinline__ void done_mark(unsigned *done, unsigned tag) {
+    __syncthreads();
+    if (threadIdx.x == 0) asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(done + blockIdx.x), "r"(tag) : "memory");
+}
+__device__ __forceinline__ bool done_wait(const unsigned *done, int nprod, unsigned tag) {
+    bool good = true;
+    if (threadIdx.x < 32) {
+        const unsigned long long t0 = gtimer();
+        for (int p = threadIdx.x; p < nprod; p += 32) {
+            unsigned v;
+            for (;;) {
+                asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(done + p) : "memory");
+                if (v == tag) break;
+                if (gtimer() - t0 > kMegaWaitNs) {
+                    good = false;
+                    break;
+                }
+            }
+            if (!good) break;
+        }
+    }
+    return __syncthreads_and(good) != 0;
+}
+
 // Staging from tagged words: optional RMSNorm (threads 0..255 hold elements
 // t + 256 j, as mega_stage), then Q8_K.  Returns false (uniformly) if a poll
 // timed out.
@@ -768,6 +798,12 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     const int o0 = blockIdx.x * a.rpc[1], o1 = min(o0 + a.rpc[1], a.H);
     const int u0 = blockIdx.x * a.rpc[2], u1 = min(u0 + a.rpc[2], 2 * a.F);
     const int d0 = blockIdx.x * a.rpc[3], d1 = min(d0 + a.rpc[3], a.H);
+    // producer CTAs per phase (the CTAs that own rows) and their done words
+    const int n_o = min((int)gridDim.x, (a.H + a.rpc[1] - 1) / a.rpc[1]);
+    const int n_u = min((int)gridDim.x, (2 * a.F + a.rpc[2] - 1) / a.rpc[2]);
+    const int n_d = min((int)gridDim.x, (a.H + a.rpc[3] - 1) / a.rpc[3]);
+    unsigned *done_o = a.done, *done_d = a.done + gridDim.x, *done_u = a.done + 2 * gridDim.x,
+             *done_a = a.done + 3 * gridDim.x;
     // prime: layer 0's weight slots and K/V rows, the first norm weights
     if (tid == 0)
         for (int t = 0; t < 4; t++) mega_fill(a, tab, smem, &mbar[t], t, 0);
@@ -818,7 +854,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             if (q0 < q1) {
                 bool good = true;
                 if (l == 0) mega_stage<2>(nullptr, &npre, a.eps, a.H, st);  // the stage row holds the embedding
-                else good = mega_stage_t<2>(a.th, T(step, l, 0), &npre, a.eps, a.H, st);
+                else good = done_wait(done_d, n_d, T(step, l, 0)) && mega_stage_t<2>(a.th, T(step, l, 0), &npre, a.eps, a.H, st);
                 if (!good) { if (tid == 0) raise_err(a, MEGA_ERR_BARRIER); ok = false; break; }
                 tl_sub(a, tls);
                 int4 act[1][4];
@@ -881,7 +917,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * KROW + c * 16); };
                 attn_chunk_main<HD, G>(aa, akvh, achunk, cs_of(pos), pos, krow, sV, sq, skc, svc, S, 1);
                 tl_sub(a, tls);
-                __syncthreads();  // every read of the K/V area is done
+                done_mark(done_a, T(step, l, 1));  // partials published; every read of the K/V area is done
                 // the next layer's K/V rows (after the last layer the area carries the LM-head
                 // ring; the next step's rows follow the head)
                 if (l + 1 < a.L && attn_cta(npos)) mega_kv_fill<HD>(a, tab[nl], sK, sV, akvh, j0_of(npos), ncache_of(npos));
@@ -892,7 +928,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             tl_mark(a, tli);
             // ---- o_proj (+ residual)
             if (o0 < o1) {
-                if (!mega_stage_attn_t<HD>(a, pos, T(step, l, 1), st)) {
+                const int cs = cs_of(pos);
+                if (!done_wait(done_a, a.kvh * ((pos + cs) / cs), T(step, l, 1)) ||
+                    !mega_stage_attn_t<HD>(a, pos, T(step, l, 1), st)) {
                     if (tid == 0) raise_err(a, MEGA_ERR_BARRIER);
                     ok = false;
                     break;
@@ -924,13 +962,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 tl_sub(a, tls); tl_sub(a, tls); tl_sub(a, tls);
             }
             if (__syncthreads_or(bad)) { if (tid == 0) raise_err(a, MEGA_ERR_BARRIER); ok = false; break; }
+            if (o0 < o1) done_mark(done_o, T(step, l, 2));
             if (more) slot_refill(1, nl);
             norm_preload<2>(ly.ffn_norm, a.H, npre);
             tl_mark(a, tli);
             tl_mark(a, tli);
             // ---- gate|up (interleaved rows) -> silu(gate) * up
             if (u0 < u1) {
-                if (!mega_stage_t<2>(a.th, T(step, l, 2), &npre, a.eps, a.H, st)) {
+                if (!done_wait(done_o, n_o, T(step, l, 2)) || !mega_stage_t<2>(a.th, T(step, l, 2), &npre, a.eps, a.H, st)) {
                     if (tid == 0) raise_err(a, MEGA_ERR_BARRIER);
                     ok = false;
                     break;
@@ -960,13 +999,15 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 if (!slot_take(2)) { ok = false; break; }
                 tl_sub(a, tls); tl_sub(a, tls); tl_sub(a, tls);
             }
-            __syncthreads();  // slot 2 consumed
+            if (u0 < u1) done_mark(done_u, T(step, l, 3));  // also: slot 2 consumed
+            else __syncthreads();
             if (more && l + 1 < a.L) slot_refill(2, nl);  // after the last layer: once the head is done
             tl_mark(a, tli);
             tl_mark(a, tli);
             // ---- down (+ residual)
             if (d0 < d1) {
-                if (!mega_stage_t<CF>(a.tact, T(step, l, 3), (const NormPre<CF> *)nullptr, a.eps, a.F, st)) {
+                if (!done_wait(done_u, n_u, T(step, l, 3)) ||
+                    !mega_stage_t<CF>(a.tact, T(step, l, 3), (const NormPre<CF> *)nullptr, a.eps, a.F, st)) {
                     if (tid == 0) raise_err(a, MEGA_ERR_BARRIER);
                     ok = false;
                     break;
@@ -998,6 +1039,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 tl_sub(a, tls); tl_sub(a, tls); tl_sub(a, tls);
             }
             if (__syncthreads_or(bad)) { if (tid == 0) raise_err(a, MEGA_ERR_BARRIER); ok = false; break; }
+            if (d0 < d1) done_mark(done_d, T(step, l + 1, 0));
             if (more && l + 1 < a.L) slot_refill(3, nl);  // after the last layer: once the head is done
             if (l + 1 == a.L) {
                 // gate|up and down slots and the K/V area are free: start the LM-head ring
@@ -1014,7 +1056,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
         if (!ok) break;
         // ---- LM head + argmax (rows < vocab_out compete), rows streamed through the ring
         {
-            if (!mega_stage_t<2>(a.th, T(step, a.L, 0), &npre, a.eps, a.H, st)) {
+            if (!done_wait(done_d, n_d, T(step, a.L, 0)) || !mega_stage_t<2>(a.th, T(step, a.L, 0), &npre, a.eps, a.H, st)) {
                 if (tid == 0) raise_err(a, MEGA_ERR_BARRIER);
                 ok = false;
                 break;
