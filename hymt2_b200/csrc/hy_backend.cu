@@ -106,9 +106,6 @@ struct HyCtx {
     char mega_why[128] = {0};       // why unsupported
     MegaLayer *d_mega_layers = nullptr;
     MegaSync *d_mega_sync = nullptr;
-    unsigned long long *d_tag = nullptr;  // tagged activations of the persistent kernel: h | q,k,v | act | partials
-    size_t tag_words = 0;
-    unsigned mega_tag = 1;                // next launch's first tag (0 = never written)
     unsigned long long *d_tl = nullptr;
     int tl_cap = 0;
     MegaPlan mega_plan_v{};
@@ -656,19 +653,6 @@ bool mega_check(HyCtx *c) {
         tab[i].kc = c->d_kv + (size_t)i * 2 * c->ctx * c->kvd;
         tab[i].vc = tab[i].kc + (size_t)c->ctx * c->kvd;
     }
-    {
-        const size_t words = (size_t)c->H + (size_t)(c->qd + 2 * c->kvd) + (size_t)c->F +
-                             (size_t)c->heads * c->max_chunks * (c->hd + kPartPad) + (size_t)2 * c->nsm;  // + done words
-        if (c->tag_words != words) {
-            if (c->d_tag) cudaFree(c->d_tag);
-            c->d_tag = nullptr;
-            c->tag_words = 0;
-            CK(c, cudaMalloc(&c->d_tag, words * 8));
-            c->tag_words = words;
-        }
-        CK(c, cudaMemsetAsync(c->d_tag, 0, words * 8, c->st));
-        c->mega_tag = 1;
-    }
     if (!c->d_mega_layers) CK(c, cudaMalloc(&c->d_mega_layers, (size_t)c->L * sizeof(MegaLayer)));
     if (!c->d_mega_sync) CK(c, cudaMalloc(&c->d_mega_sync, sizeof(MegaSync)));
     CK(c, h2d(c, c->d_mega_layers, tab.data(), (size_t)c->L * sizeof(MegaLayer)));
@@ -739,13 +723,6 @@ bool mega_launch(HyCtx *c, int steps) {
     a.st = c->d_state;
     a.out_ids = c->d_out_ids;
     a.sync = c->d_mega_sync;
-    a.th = c->d_tag;
-    a.tqkv = a.th + c->H;
-    a.tact = a.tqkv + (c->qd + 2 * c->kvd);
-    a.tpart = a.tact + c->F;
-    a.done = (unsigned *)(a.tpart + (size_t)c->heads * c->max_chunks * (c->hd + kPartPad));
-    a.tag0 = c->mega_tag;
-    c->mega_tag += (unsigned)steps * (unsigned)(c->L + 1) * 4u + 4u;  // this launch's tags are never reused soon
     a.tl = c->trace_on ? c->d_tl : nullptr;
     a.tl_cap = c->tl_cap;
     a.steps = steps;
@@ -841,9 +818,6 @@ void free_fused(HyCtx *c) {
     if (c->d_mega_layers) cudaFree(c->d_mega_layers);
     if (c->d_mega_sync) cudaFree(c->d_mega_sync);
     if (c->d_tl) cudaFree(c->d_tl);
-    if (c->d_tag) cudaFree(c->d_tag);
-    c->d_tag = nullptr;
-    c->tag_words = 0;
     c->d_mega_layers = nullptr;
     c->d_mega_sync = nullptr;
     c->d_tl = nullptr;

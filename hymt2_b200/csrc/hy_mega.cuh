@@ -69,9 +69,6 @@ struct MegaArgs {
     int vocab_out;
     const float *out_norm;
     float *h, *qkv, *ao, *act;
-    unsigned long long *th, *tqkv, *tact, *tpart;  // tagged activations: h, q|k|v, silu*up, attention partials
-    unsigned *done;  // per-CTA done words [4][grid]: o_proj rows, down rows, gate|up rows, attention unit
-    unsigned tag0;   // first tag of this launch
     DecodeState *st;
     int *out_ids;
     MegaSync *sync;
@@ -497,251 +494,16 @@ __device__ __forceinline__ void mega_kv_fill(const MegaArgs &a, const MegaLayer 
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-// ---------------------------------------------------------------- tagged activations
-//
-// Between the phases of a step every activation value travels as one 64-bit
-// word: the float's bits, and in the upper half a tag naming (launch, step,
-// layer, phase).  A consumer polls exactly the words it needs until their tags
-// match; a 64-bit access is single-copy atomic, so a matching tag implies the
-// value beside it.  This replaces a grid barrier plus a load by the load.
-// Reuse of a buffer is safe by the data flow itself: every rewrite of a
-// buffer depends (through the values it is computed from) on every CTA that
-// reads the buffer's previous contents having read them, because a CTA reads
-// a phase's input only when it computes rows of that phase.
-
-__device__ __forceinline__ unsigned long long tword(float v, unsigned tag) {
-    return (unsigned long long)__float_as_uint(v) | ((unsigned long long)tag << 32);
-}
-__device__ __forceinline__ void tstore(unsigned long long *p, float v, unsigned tag) {
-    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(tword(v, tag)) : "memory");
-}
-__device__ __forceinline__ unsigned long long tload(const unsigned long long *p) {
-    unsigned long long r;
-    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(r) : "l"(p) : "memory");
-    return r;
-}
-__device__ __forceinline__ ulonglong2 tload2(const unsigned long long *p) {  // 16-byte aligned
-    ulonglong2 r;
-    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(r.x), "=l"(r.y) : "l"(p) : "memory");
-    return r;
-}
-__device__ __forceinline__ bool tag_is(unsigned long long w, unsigned tag) { return (unsigned)(w >> 32) == tag; }
-__device__ __forceinline__ float tval(unsigned long long w) { return __uint_as_float((unsigned)w); }
-
-// Poll n groups of four consecutive words (32-byte aligned) until every tag
-// matches; all groups' loads are in flight together.  Bounded; false on
-// timeout.
-template <int NG>
-__device__ __forceinline__ bool tpoll4(const unsigned long long *const (&p)[NG], const bool (&use)[NG], unsigned tag,
-                                       float4 (&out)[NG]) {
-    ulonglong2 lo[NG], hi[NG];
-    bool done[NG];
-    unsigned long long t0 = 0;
-    for (int round = 0;; round++) {
-#pragma unroll
-        for (int g = 0; g < NG; g++)
-            if (use[g] && (round == 0 || !done[g])) {
-                lo[g] = tload2(p[g]);
-                hi[g] = tload2(p[g] + 2);
-            }
-        bool all = true;
-#pragma unroll
-        for (int g = 0; g < NG; g++) {
-            if (!use[g]) continue;
-            done[g] = tag_is(lo[g].x, tag) && tag_is(lo[g].y, tag) && tag_is(hi[g].x, tag) && tag_is(hi[g].y, tag);
-            all = all && done[g];
-        }
-        if (all) break;
-        if (round == 0) t0 = gtimer();
-        else if (gtimer() - t0 > kMegaWaitNs) return false;
-    }
-#pragma unroll
-    for (int g = 0; g < NG; g++)
-        if (use[g]) out[g] = make_float4(tval(lo[g].x), tval(lo[g].y), tval(hi[g].x), tval(hi[g].y));
-    return true;
-}
-// One word; bounded; false on timeout.
-__device__ __forceinline__ bool tpoll1(const unsigned long long *p, unsigned tag, float &v) {
-    unsigned long long w = tload(p);
-    if (!tag_is(w, tag)) {
-        const unsigned long long t0 = gtimer();
-        do {
-            if (gtimer() - t0 > kMegaWaitNs) return false;
-            w = tload(p);
-        } while (!tag_is(w, tag));
-    }
-    v = tval(w);
-    return true;
-}
-
-// Done words: after its rows of a phase a producer CTA stores the phase's
-// tag into done[cta] (no fence).  A consumer first lets one warp poll the
-// nprod producers' done words (a few hundred bytes instead of the whole
-// vector, so 148 pollers do not flood the L2 lines of the data), then loads
-// the tagged data, whose own tags still decide.  Bounded; false on timeout.
-__device__ __forceinline__ void done_mark(unsigned *done, unsigned tag) {
-    __syncthreads();
-    if (threadIdx.x == 0) asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(done + blockIdx.x), "r"(tag) : "memory");
-}
-__device__ __forceinline__ bool done_wait(const unsigned *done, int nprod, unsigned tag) {
-    bool good = true;
-    if (threadIdx.x < 32) {
-        const unsigned long long t0 = gtimer();
-        for (int p = threadIdx.x; p < nprod; p += 32) {
-            unsigned v;
-            for (;;) {
-                asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(done + p) : "memory");
-                if (v == tag) break;
-                if (gtimer() - t0 > kMegaWaitNs) {
-                    good = false;
-                    break;
-                }
-            }
-            if (!good) break;
-        }
-    }
-    return __syncthreads_and(good) != 0;
-}
-
-// Staging from tagged words: optional RMSNorm (threads 0..255 hold elements
-// t + 256 j, as mega_stage), then Q8_K.  Returns false (uniformly) if a poll
-// timed out.
-template <int SV>
-__device__ inline bool mega_stage_t(const unsigned long long *x, unsigned tag, const NormPre<SV> *pre, float eps, int K,
-                                    Q8Smem &s) {
-    const int n4 = K >> 2, tid = threadIdx.x;
-    bool good = true;
-    if (pre) {
-        const unsigned long long *p[SV];
-        bool use[SV];
-        float4 xv[SV];
-#pragma unroll
-        for (int j = 0; j < SV; j++) {
-            const int i = tid + j * kGemvThreads;
-            use[j] = tid < kGemvThreads && i < n4;
-            p[j] = x + 4 * (size_t)(use[j] ? i : 0);
-        }
-        good = tpoll4<SV>(p, use, tag, xv);
-        float ss = 0.f;
-#pragma unroll
-        for (int j = 0; j < SV; j++) {
-            if (use[j]) {
-                ss = __fadd_rn(ss, __fmul_rn(xv[j].x, xv[j].x));
-                ss = __fadd_rn(ss, __fmul_rn(xv[j].y, xv[j].y));
-                ss = __fadd_rn(ss, __fmul_rn(xv[j].z, xv[j].z));
-                ss = __fadd_rn(ss, __fmul_rn(xv[j].w, xv[j].w));
-            }
-        }
-        if (!__syncthreads_and(good)) return false;
-        ss = block_sum(ss, s.red);
-        const float scale = 1.0f / sqrtf(ss / (float)K + eps);
-#pragma unroll
-        for (int j = 0; j < SV; j++) {
-            const int i = tid + j * kGemvThreads;
-            if (use[j]) {
-                const float4 wv = pre->w[j];
-                ((float4 *)s.x)[i] = make_float4(__fmul_rn(__fmul_rn(xv[j].x, scale), wv.x),
-                                                 __fmul_rn(__fmul_rn(xv[j].y, scale), wv.y),
-                                                 __fmul_rn(__fmul_rn(xv[j].z, scale), wv.z),
-                                                 __fmul_rn(__fmul_rn(xv[j].w, scale), wv.w));
-            }
-        }
-    } else {
-        constexpr int NG = SV;  // groups of four per thread at kMegaThreads threads
-        const unsigned long long *p[NG];
-        bool use[NG];
-        float4 xv[NG];
-#pragma unroll
-        for (int j = 0; j < NG; j++) {
-            const int i = tid + j * kMegaThreads;
-            use[j] = i < n4;
-            p[j] = x + 4 * (size_t)(use[j] ? i : 0);
-        }
-        good = tpoll4<NG>(p, use, tag, xv);
-#pragma unroll
-        for (int j = 0; j < NG; j++)
-            if (use[j]) ((float4 *)s.x)[tid + j * kMegaThreads] = xv[j];
-        if (!__syncthreads_and(good)) return false;
-    }
-    __syncthreads();
-    const int nb = K / 256;
-    for (int b = tid >> 5; b < nb; b += kMegaWarps) quantize_block_warp(s.x, s, 0, b, nb, K);
-    __syncthreads();
-    return true;
-}
-
-// Partials of one head as tagged words (attn_chunk_main with a.tpart set).
-template <int HD>
-struct TaggedPartLoader {
-    const unsigned long long *base;
-    unsigned tag;
-    bool *bad;
-    __device__ __forceinline__ float2 ml(int c) const {
-        const unsigned long long *p = base + (size_t)c * (HD + kPartPad);
-        ulonglong2 w = tload2(p);
-        if (!(tag_is(w.x, tag) && tag_is(w.y, tag))) {
-            const unsigned long long t0 = gtimer();
-            do {
-                if (gtimer() - t0 > kMegaWaitNs) {
-                    *bad = true;
-                    return make_float2(0.f, 1.f);
-                }
-                w = tload2(p);
-            } while (!(tag_is(w.x, tag) && tag_is(w.y, tag)));
-        }
-        return make_float2(tval(w.x), tval(w.y));
-    }
-    template <int DPL>
-    __device__ __forceinline__ void o(int c, int lane, float (&v)[DPL]) const {
-        const unsigned long long *p = base + (size_t)c * (HD + kPartPad) + kPartPad + lane * DPL;
-#pragma unroll
-        for (int q = 0; q < DPL; q += 2) {
-            ulonglong2 w = tload2(p + q);
-            if (!(tag_is(w.x, tag) && tag_is(w.y, tag))) {
-                const unsigned long long t0 = gtimer();
-                do {
-                    if (gtimer() - t0 > kMegaWaitNs) {
-                        *bad = true;
-                        break;
-                    }
-                    w = tload2(p + q);
-                } while (!(tag_is(w.x, tag) && tag_is(w.y, tag)));
-            }
-            v[q] = tval(w.x);
-            v[q + 1] = tval(w.y);
-        }
-    }
-};
-
-// o_proj staging from tagged partials: every head merged (one warp per head)
-// into the stage row, then Q8_K.  False (uniformly) on a poll timeout.
-template <int HD>
-__device__ inline bool mega_stage_attn_t(const MegaArgs &a, int pos, unsigned tag, Q8Smem &s) {
-    const int cs = attn_chunk_len(pos, a.kvh, gridDim.x), nch = (pos + cs) / cs, heads = a.qd / HD;
-    bool bad = false;
-    for (int h = threadIdx.x >> 5; h < heads; h += kMegaWarps) {
-        const TaggedPartLoader<HD> ld{a.tpart + (size_t)h * a.attn.max_chunks * (HD + kPartPad), tag, &bad};
-        attn_merge_head_with<HD>(ld, nch, s.x + (size_t)h * HD);
-    }
-    if (!__syncthreads_and(!bad)) return false;
-    const int nb = a.qd / 256;
-    for (int b = threadIdx.x >> 5; b < nb; b += kMegaWarps) quantize_block_warp(s.x, s, 0, b, nb, a.qd);
-    __syncthreads();
-    return true;
-}
-
 // Launch shape contract (checked by the host): grid = number of SMs, all
-// resident (cooperative launch); L <= kMegaMaxLayers; attention units of a
-// position fit the grid (attn_chunk_len); every layer weight a panel with
-// (shift, off); H, qd <= 2048 (one 64-element chunk per lane) and F <= 2048 *
-// CF; head Q6_K with k == H.
+// resident (cooperative launch); L <= kMegaMaxLayers; kvh * ceil(ctx /
+// kDecSplit) <= grid; every layer weight a panel with (shift, off); H, qd <=
+// 2048 (one 64-element chunk per lane) and F <= 2048 * CF; head Q6_K with
+// k == H.
 //
-// Per layer a CTA runs each phase it has rows in: it polls the phase's input
-// words (tagged by the producing phase), stages and quantises them, waits for
-// its weight slice in shared memory, computes its rows and stores them as
-// tagged words, then refills the slot with the next layer's slice.  CTAs with
-// no rows in a phase only keep the slot's mbarrier in step.  The LM head is
-// the one grid-wide barrier per step (its argmax needs every CTA's rows).
+// Between bar_arrive and bar_wait each CTA does the work that needs nothing
+// from other CTAs: it refills the weight slot it just consumed with the next
+// layer's slice, stages the next layer's K/V rows (after this layer's
+// attention), and loads the next phase's norm weights and rope constants.
 template <int HD, int G, int CF>
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_constant__ MegaArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
@@ -751,7 +513,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     __shared__ unsigned long long s_best[kMegaWarps];
     __shared__ __align__(16) float sq[G][HD];
     __shared__ __align__(16) float skc[HD], svc[HD];
-    __shared__ __align__(16) float sqkv[(G + 2) * HD];  // this unit's q | k | v words, untagged
     __shared__ __align__(16) ChunkScratch<HD> S;
     __shared__ __align__(16) MegaLayer tab[kMegaMaxLayers];
     constexpr int KROW = HD * 2 + kMegaKPad;
@@ -777,11 +538,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     int tli = 0, tls = 0;
     int tok = a.st->tok, pos = a.st->pos;
     bool ok = true;
-    // tags: h entering layer l = T(l,0); q|k|v and attention partials = T(l,1);
-    // h after o_proj = T(l,2); silu(gate)*up = T(l,3); h entering the head = T(L,0)
-    const auto T = [&](int step, int l, int ph_) {
-        return a.tag0 + ((unsigned)(step * (a.L + 1) + l) << 2) + (unsigned)ph_;
-    };
     // attention unit of this CTA: (KV head akvh, key chunk achunk) of the wide decode attention
     const int akvh = blockIdx.x % a.kvh, achunk = blockIdx.x / a.kvh;
     const auto cs_of = [&](int p) { return attn_chunk_len(p, a.kvh, gridDim.x); };
@@ -793,17 +549,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     const auto ncache_of = [&](int p) { return max(0, min(p, j0_of(p) + cs_of(p)) - j0_of(p)); };
     const int hr0 = blockIdx.x * a.rpc[4], hr1 = min(hr0 + a.rpc[4], a.head.n);
     const int hst = hr1 > hr0 ? (hr1 - hr0 + kHeadRows - 1) / kHeadRows : 0;  // head ring stages per step
-    // row ranges of this CTA per phase (fixed for the launch)
-    const int q0 = blockIdx.x * a.rpc[0], q1 = min(q0 + a.rpc[0], a.qd + 2 * a.kvd);
-    const int o0 = blockIdx.x * a.rpc[1], o1 = min(o0 + a.rpc[1], a.H);
-    const int u0 = blockIdx.x * a.rpc[2], u1 = min(u0 + a.rpc[2], 2 * a.F);
-    const int d0 = blockIdx.x * a.rpc[3], d1 = min(d0 + a.rpc[3], a.H);
-    // producer CTAs per phase (the CTAs that own rows) and their done words
-    const int n_o = min((int)gridDim.x, (a.H + a.rpc[1] - 1) / a.rpc[1]);
-    const int n_u = min((int)gridDim.x, (2 * a.F + a.rpc[2] - 1) / a.rpc[2]);
-    const int n_d = min((int)gridDim.x, (a.H + a.rpc[3] - 1) / a.rpc[3]);
-    unsigned *done_o = a.done, *done_d = a.done + gridDim.x, *done_u = a.done + 2 * gridDim.x,
-             *done_a = a.done + 3 * gridDim.x;
     // prime: layer 0's weight slots and K/V rows, the first norm weights
     if (tid == 0)
         for (int t = 0; t < 4; t++) mega_fill(a, tab, smem, &mbar[t], t, 0);
@@ -811,22 +556,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     if (a.steps > 0 && attn_cta(pos)) mega_kv_fill<HD>(a, tab[0], sK, sV, akvh, j0_of(pos), ncache_of(pos));
     NormPre<2> npre;
     norm_preload<2>(tab[0].attn_norm, a.H, npre);
-    // consume slot t's fill; uniform false (and error raised) on timeout
-    const auto slot_take = [&](int t) {
-        if (mega_slot_ready(a, &mbar[t], ph[t])) {
-            ph[t] ^= 1;
-            pending &= ~(1u << t);
-            return true;
-        }
-        return false;
-    };
-    const auto slot_refill = [&](int t, int nl) {
-        if (tid == 0) {
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mega_fill(a, tab, smem, &mbar[t], t, nl);
-        }
-        pending |= 1u << t;
-    };
     for (int step = 0; step < a.steps && ok; step++) {
         if (pos < 0 || pos >= a.ctx) {
             if (tid == 0) raise_err(a, MEGA_ERR_POS);
@@ -835,13 +564,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
         }
         const bool is_attn = attn_cta(pos);
         tl_mark(a, tli);
-        // embedding of `tok` into the stage row; CTA b also publishes its slice of h
+        // embedding of `tok` into the stage row; CTA b also writes its slice of h
         {
             const int t0 = (tok < 0 || tok >= a.embd.n) ? 0 : tok;
             for (int e = tid; e < a.H; e += kMegaThreads) st.x[e] = dequant_elem(a.embd, t0, e);
             const int per = (a.H + gridDim.x - 1) / gridDim.x;
             const int e0 = blockIdx.x * per, e1 = min(a.H, e0 + per);
-            for (int e = e0 + tid; e < e1; e += kMegaThreads) tstore(a.th + e, dequant_elem(a.embd, t0, e), T(step, 0, 0));
+            for (int e = e0 + tid; e < e1; e += kMegaThreads) a.h[e] = dequant_elem(a.embd, t0, e);
             __syncthreads();
         }
         for (int l = 0; l < a.L && ok; l++) {
@@ -849,199 +578,206 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             const bool more = !(l + 1 == a.L && step + 1 == a.steps);  // a following layer exists
             const int nl = l + 1 < a.L ? l + 1 : 0;
             const int npos = l + 1 < a.L ? pos : pos + 1;  // position the following layer runs at
-            bool bad = false;
+            AttnArgs aa = a.attn;
+            aa.kc = ly.kc;
+            aa.vc = ly.vc;
+            aa.q_norm = ly.q_norm;
+            aa.k_norm = ly.k_norm;
+            aa.tickets = a.sync->tickets;
             // ---- q|k|v
-            if (q0 < q1) {
-                bool good = true;
-                if (l == 0) mega_stage<2>(nullptr, &npre, a.eps, a.H, st);  // the stage row holds the embedding
-                else good = done_wait(done_d, n_d, T(step, l, 0)) && mega_stage_t<2>(a.th, T(step, l, 0), &npre, a.eps, a.H, st);
-                if (!good) { if (tid == 0) raise_err(a, MEGA_ERR_BARRIER); ok = false; break; }
+            {
+                mega_stage<2>(l == 0 ? nullptr : a.h, &npre, a.eps, a.H, st);
                 tl_sub(a, tls);
                 int4 act[1][4];
                 float dblk[1];
                 int sblk[1];
                 mega_act<1>(st, a.H, act, dblk, sblk);
-                if (!slot_take(0)) { ok = false; break; }
-                tl_sub(a, tls);
-                const uint8_t *sw = smem + a.slot_off[0];
-                const float *ss = (const float *)(sw + align16((size_t)a.rpc[0] * (a.H / 256) * 64));
-                const unsigned tq = T(step, l, 1);
-                unsigned long long *tqkv = a.tqkv;
-                mega_rows<1, RGQ, false>(a.shift, a.off, q0, q1, a.rpc[0], sw, ss, a.H, act, dblk, sblk,
-                                         [&](int rg, const float *acc, int rend) {
-#pragma unroll
-                                             for (int g = 0; g < RGQ; g++)
-                                                 if (rg + g < rend) tstore(tqkv + rg + g, acc[g], tq);
-                                         });
-                tl_sub(a, tls);
-            } else {
-                if (!slot_take(0)) { ok = false; break; }
-                tl_sub(a, tls); tl_sub(a, tls); tl_sub(a, tls);
-            }
-            __syncthreads();  // slot 0 consumed
-            if (more) slot_refill(0, nl);
-            tl_mark(a, tli);
-            tl_mark(a, tli);
-            // ---- attention (the units of this position)
-            if (is_attn) {
-                AttnArgs aa = a.attn;
-                aa.kc = ly.kc;
-                aa.vc = ly.vc;
-                aa.q_norm = ly.q_norm;
-                aa.k_norm = ly.k_norm;
-                aa.tpart = a.tpart;
-                aa.ptag = T(step, l, 1);
-                DecConsts<HD> kcs;
-                if (warp <= G) attn_dec_consts<HD, G>(aa, pos, kcs);
-                // this unit's q (G heads), k and v words
-                bool got = true;
-                {
-                    const unsigned tq = T(step, l, 1);
-                    for (int i = tid; i < (G + 2) * HD; i += kMegaThreads) {
-                        const size_t gi = i < G * HD ? (size_t)akvh * G * HD + i
-                                                     : (i < (G + 1) * HD ? (size_t)a.qd + akvh * HD + (i - G * HD)
-                                                                         : (size_t)a.qd + a.kvd + akvh * HD + (i - (G + 1) * HD));
-                        float v = 0.f;
-                        got = tpoll1(a.tqkv + gi, tq, v) && got;
-                        sqkv[i] = v;
-                    }
+                if (mega_slot_ready(a, &mbar[0], ph[0])) {
+                    ph[0] ^= 1;
+                    pending &= ~1u;
+                } else {
+                    ok = false;
                 }
-                if (!__syncthreads_and(got)) { if (tid == 0) raise_err(a, MEGA_ERR_BARRIER); ok = false; break; }
+                tl_sub(a, tls);
+                const int rpc = a.rpc[0], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.qd + 2 * a.kvd);
+                const uint8_t *sw = smem + a.slot_off[0];
+                const float *ss = (const float *)(sw + align16((size_t)rpc * (a.H / 256) * 64));
+                float *qkv = a.qkv;
+                if (ok)
+                    mega_rows<1, RGQ, false>(a.shift, a.off, r0, r1, rpc, sw, ss, a.H, act, dblk, sblk,
+                                             [&](int rg, const float *acc, int rend) {
+#pragma unroll
+                                                 for (int g = 0; g < RGQ; g++)
+                                                     if (rg + g < rend) qkv[rg + g] = acc[g];
+                                             });
+                tl_sub(a, tls);
+            }
+            tl_mark(a, tli);
+            tl_cta(a, step == 1 && l == 5, 0);
+            bar_arrive(a, target);
+            if (more && ok) {
+                if (tid == 0) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mega_fill(a, tab, smem, &mbar[0], 0, nl);
+                }
+                pending |= 1u;
+            }
+            DecConsts<HD> kcs;
+            if (is_attn && warp <= G) attn_dec_consts<HD, G>(aa, pos, kcs);
+            if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
+            tl_cta(a, step == 1 && l == 5, 1);
+            tl_mark(a, tli);
+            if (l == 0 && blockIdx.x == 0 && tid == 0) a.sync->amax[(step + 1) & 1] = 0ull;
+            // ---- attention (the CTAs of the splits that hold keys)
+            if (is_attn) {
                 if (warp <= G)
-                    attn_dec_prologue<HD, G>(aa, akvh, pos, achunk == 0, kcs, sq, skc, svc, sqkv, sqkv + G * HD,
-                                             sqkv + (G + 1) * HD);
+                    attn_dec_prologue<HD, G>(aa, akvh, pos, achunk == 0, kcs, sq, skc, svc, aa.qkv + (akvh * G) * HD,
+                                             aa.qkv + aa.qdim + akvh * HD, aa.qkv + aa.qdim + aa.kvdim + akvh * HD);
                 tl_sub(a, tls);
                 asm volatile("cp.async.wait_group 0;" ::: "memory");
                 __syncthreads();  // K/V rows of every thread, and sq / skc / svc
                 tl_sub(a, tls);
-                const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * KROW + c * 16); };
-                attn_chunk_main<HD, G>(aa, akvh, achunk, cs_of(pos), pos, krow, sV, sq, skc, svc, S, 1);
+                if (ok) {
+                    const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * KROW + c * 16); };
+                    attn_chunk_main<HD, G>(aa, akvh, achunk, cs_of(pos), pos, krow, sV, sq, skc, svc, S, 1);
+                }
                 tl_sub(a, tls);
-                done_mark(done_a, T(step, l, 1));  // partials published; every read of the K/V area is done
-                // the next layer's K/V rows (after the last layer the area carries the LM-head
-                // ring; the next step's rows follow the head)
-                if (l + 1 < a.L && attn_cta(npos)) mega_kv_fill<HD>(a, tab[nl], sK, sV, akvh, j0_of(npos), ncache_of(npos));
-            } else {
-                tl_sub(a, tls); tl_sub(a, tls); tl_sub(a, tls);
             }
             tl_mark(a, tli);
+            tl_cta(a, step == 1 && l == 5, 2);
+            bar_arrive(a, target);
+            if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
+            tl_cta(a, step == 1 && l == 5, 3);
             tl_mark(a, tli);
             // ---- o_proj (+ residual)
-            if (o0 < o1) {
-                const int cs = cs_of(pos);
-                if (!done_wait(done_a, a.kvh * ((pos + cs) / cs), T(step, l, 1)) ||
-                    !mega_stage_attn_t<HD>(a, pos, T(step, l, 1), st)) {
-                    if (tid == 0) raise_err(a, MEGA_ERR_BARRIER);
-                    ok = false;
-                    break;
-                }
+            {
+                mega_stage_attn<HD>(a, pos, st);
                 tl_sub(a, tls);
                 int4 act[1][4];
                 float dblk[1];
                 int sblk[1];
                 mega_act<1>(st, a.qd, act, dblk, sblk);
-                if (!slot_take(1)) { ok = false; break; }
+                if (mega_slot_ready(a, &mbar[1], ph[1])) {
+                    ph[1] ^= 1;
+                    pending &= ~2u;
+                } else {
+                    ok = false;
+                }
                 tl_sub(a, tls);
+                const int rpc = a.rpc[1], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.H);
                 const uint8_t *sw = smem + a.slot_off[1];
-                const float *ss = (const float *)(sw + align16((size_t)a.rpc[1] * (a.qd / 256) * 64));
-                const unsigned tin = T(step, l, 0), tout = T(step, l, 2);
-                unsigned long long *th = a.th;
-                mega_rows<1, RGO, false>(a.shift, a.off, o0, o1, a.rpc[1], sw, ss, a.qd, act, dblk, sblk,
-                                         [&](int rg, const float *acc, int rend) {
+                const float *ss = (const float *)(sw + align16((size_t)rpc * (a.qd / 256) * 64));
+                float *h = a.h;
+                if (ok)
+                    mega_rows<1, RGO, false>(a.shift, a.off, r0, r1, rpc, sw, ss, a.qd, act, dblk, sblk,
+                                             [&](int rg, const float *acc, int rend) {
 #pragma unroll
-                                             for (int g = 0; g < RGO; g++)
-                                                 if (rg + g < rend) {
-                                                     float hv = 0.f;
-                                                     bad |= !tpoll1(th + rg + g, tin, hv);
-                                                     tstore(th + rg + g, hv + acc[g], tout);
-                                                 }
-                                         });
+                                                 for (int g = 0; g < RGO; g++)
+                                                     if (rg + g < rend) h[rg + g] += acc[g];
+                                             });
                 tl_sub(a, tls);
-            } else {
-                if (!slot_take(1)) { ok = false; break; }
-                tl_sub(a, tls); tl_sub(a, tls); tl_sub(a, tls);
             }
-            if (__syncthreads_or(bad)) { if (tid == 0) raise_err(a, MEGA_ERR_BARRIER); ok = false; break; }
-            if (o0 < o1) done_mark(done_o, T(step, l, 2));
-            if (more) slot_refill(1, nl);
-            norm_preload<2>(ly.ffn_norm, a.H, npre);
             tl_mark(a, tli);
+            tl_cta(a, step == 1 && l == 5, 4);
+            bar_arrive(a, target);
+            if (more && ok) {
+                if (tid == 0) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mega_fill(a, tab, smem, &mbar[1], 1, nl);
+                }
+                pending |= 2u;
+                // this layer's attention is done with the K/V area: stage the next layer's rows
+                // (after the last layer the area carries the LM-head ring; the next step's rows
+                // follow the head)
+                if (l + 1 < a.L && attn_cta(npos)) mega_kv_fill<HD>(a, tab[nl], sK, sV, akvh, j0_of(npos), ncache_of(npos));
+            }
+            norm_preload<2>(ly.ffn_norm, a.H, npre);
+            if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
+            tl_cta(a, step == 1 && l == 5, 5);
             tl_mark(a, tli);
             // ---- gate|up (interleaved rows) -> silu(gate) * up
-            if (u0 < u1) {
-                if (!done_wait(done_o, n_o, T(step, l, 2)) || !mega_stage_t<2>(a.th, T(step, l, 2), &npre, a.eps, a.H, st)) {
-                    if (tid == 0) raise_err(a, MEGA_ERR_BARRIER);
-                    ok = false;
-                    break;
-                }
+            {
+                mega_stage<2>(a.h, &npre, a.eps, a.H, st);
                 tl_sub(a, tls);
                 int4 act[1][4];
                 float dblk[1];
                 int sblk[1];
                 mega_act<1>(st, a.H, act, dblk, sblk);
-                if (!slot_take(2)) { ok = false; break; }
+                if (mega_slot_ready(a, &mbar[2], ph[2])) {
+                    ph[2] ^= 1;
+                    pending &= ~4u;
+                } else {
+                    ok = false;
+                }
                 tl_sub(a, tls);
+                const int rpc = a.rpc[2], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, 2 * a.F);
                 const uint8_t *sw = smem + a.slot_off[2];
-                const float *ss = (const float *)(sw + align16((size_t)a.rpc[2] * (a.H / 256) * 64));
-                const unsigned tout = T(step, l, 3);
-                unsigned long long *tact = a.tact;
-                mega_rows<1, RGU, true>(a.shift, a.off, u0, u1, a.rpc[2], sw, ss, a.H, act, dblk, sblk,
-                                        [&](int rg, const float *acc, int rend) {
+                const float *ss = (const float *)(sw + align16((size_t)rpc * (a.H / 256) * 64));
+                float *out = a.act;
+                if (ok)
+                    mega_rows<1, RGU, true>(a.shift, a.off, r0, r1, rpc, sw, ss, a.H, act, dblk, sblk,
+                                            [&](int rg, const float *acc, int rend) {
 #pragma unroll
-                                            for (int g = 0; g + 1 < RGU; g += 2) {
-                                                if (rg + g + 1 >= rend) break;
-                                                const float gt = acc[g], up = acc[g + 1];
-                                                tstore(tact + ((rg + g) >> 1), __fmul_rn(gt / (1.0f + expf(-gt)), up), tout);
-                                            }
-                                        });
+                                                for (int g = 0; g + 1 < RGU; g += 2) {
+                                                    if (rg + g + 1 >= rend) break;
+                                                    const float gt = acc[g], up = acc[g + 1];
+                                                    out[(rg + g) >> 1] = __fmul_rn(gt / (1.0f + expf(-gt)), up);
+                                                }
+                                            });
                 tl_sub(a, tls);
-            } else {
-                if (!slot_take(2)) { ok = false; break; }
-                tl_sub(a, tls); tl_sub(a, tls); tl_sub(a, tls);
             }
-            if (u0 < u1) done_mark(done_u, T(step, l, 3));  // also: slot 2 consumed
-            else __syncthreads();
-            if (more && l + 1 < a.L) slot_refill(2, nl);  // after the last layer: once the head is done
             tl_mark(a, tli);
+            tl_cta(a, step == 1 && l == 5, 6);
+            bar_arrive(a, target);
+            if (more && ok && l + 1 < a.L) {  // after the last layer: once the head is done
+                if (tid == 0) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mega_fill(a, tab, smem, &mbar[2], 2, nl);
+                }
+                pending |= 4u;
+            }
+            if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
+            tl_cta(a, step == 1 && l == 5, 7);
             tl_mark(a, tli);
             // ---- down (+ residual)
-            if (d0 < d1) {
-                if (!done_wait(done_u, n_u, T(step, l, 3)) ||
-                    !mega_stage_t<CF>(a.tact, T(step, l, 3), (const NormPre<CF> *)nullptr, a.eps, a.F, st)) {
-                    if (tid == 0) raise_err(a, MEGA_ERR_BARRIER);
-                    ok = false;
-                    break;
-                }
+            {
+                mega_stage<2 * CF>(a.act, (const NormPre<2 * CF> *)nullptr, a.eps, a.F, st);
                 tl_sub(a, tls);
                 int4 act[CF][4];
                 float dblk[CF];
                 int sblk[CF];
                 mega_act<CF>(st, a.F, act, dblk, sblk);
-                if (!slot_take(3)) { ok = false; break; }
+                if (mega_slot_ready(a, &mbar[3], ph[3])) {
+                    ph[3] ^= 1;
+                    pending &= ~8u;
+                } else {
+                    ok = false;
+                }
                 tl_sub(a, tls);
+                const int rpc = a.rpc[3], r0 = blockIdx.x * rpc, r1 = min(r0 + rpc, a.H);
                 const uint8_t *sw = smem + a.slot_off[3];
-                const float *ss = (const float *)(sw + align16((size_t)a.rpc[3] * (a.F / 256) * 64));
-                const unsigned tin = T(step, l, 2), tout = T(step, l + 1, 0);
-                unsigned long long *th = a.th;
-                mega_rows<CF, RGD, false>(a.shift, a.off, d0, d1, a.rpc[3], sw, ss, a.F, act, dblk, sblk,
-                                          [&](int rg, const float *acc, int rend) {
+                const float *ss = (const float *)(sw + align16((size_t)rpc * (a.F / 256) * 64));
+                float *h = a.h;
+                if (ok)
+                    mega_rows<CF, RGD, false>(a.shift, a.off, r0, r1, rpc, sw, ss, a.F, act, dblk, sblk,
+                                              [&](int rg, const float *acc, int rend) {
 #pragma unroll
-                                              for (int g = 0; g < RGD; g++)
-                                                  if (rg + g < rend) {
-                                                      float hv = 0.f;
-                                                      bad |= !tpoll1(th + rg + g, tin, hv);
-                                                      tstore(th + rg + g, hv + acc[g], tout);
-                                                  }
-                                          });
+                                                  for (int g = 0; g < RGD; g++)
+                                                      if (rg + g < rend) h[rg + g] += acc[g];
+                                              });
                 tl_sub(a, tls);
-            } else {
-                if (!slot_take(3)) { ok = false; break; }
-                tl_sub(a, tls); tl_sub(a, tls); tl_sub(a, tls);
             }
-            if (__syncthreads_or(bad)) { if (tid == 0) raise_err(a, MEGA_ERR_BARRIER); ok = false; break; }
-            if (d0 < d1) done_mark(done_d, T(step, l + 1, 0));
-            if (more && l + 1 < a.L) slot_refill(3, nl);  // after the last layer: once the head is done
-            if (l + 1 == a.L) {
+            tl_mark(a, tli);
+            tl_cta(a, step == 1 && l == 5, 8);
+            bar_arrive(a, target);
+            if (more && ok && l + 1 < a.L) {  // after the last layer: once the head is done
+                if (tid == 0) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    mega_fill(a, tab, smem, &mbar[3], 3, nl);
+                }
+                pending |= 8u;
+            }
+            if (l + 1 == a.L && ok) {
                 // gate|up and down slots and the K/V area are free: start the LM-head ring
                 if (tid == 0) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1050,22 +786,23 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 for (int k = 0; k < a.head_ns && k < hst; k++) hpend |= 1u << k;
             }
             norm_preload<2>(l + 1 < a.L ? tab[l + 1].attn_norm : a.out_norm, a.H, npre);
-            tl_mark(a, tli);
+            if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
+            tl_cta(a, step == 1 && l == 5, 9);
             tl_mark(a, tli);
         }
         if (!ok) break;
         // ---- LM head + argmax (rows < vocab_out compete), rows streamed through the ring
         {
-            if (!done_wait(done_d, n_d, T(step, a.L, 0)) || !mega_stage_t<2>(a.th, T(step, a.L, 0), &npre, a.eps, a.H, st)) {
-                if (tid == 0) raise_err(a, MEGA_ERR_BARRIER);
-                ok = false;
-                break;
-            }
+            mega_stage<2>(a.h, &npre, a.eps, a.H, st);
             const int nb = a.H / 256;
             unsigned long long best = 0;
+            unsigned long long tw = 0, tc = 0, ts = 0, t0 = a.tl ? gtimer() : 0;
             for (int si = 0; si < hst && ok; si++) {
                 const int k = si % a.head_ns;
-                if (__syncthreads_and(mbar_wait(&hbar[k], hph[k]))) {
+                const bool ready = __syncthreads_and(mbar_wait(&hbar[k], hph[k]));
+                unsigned long long t1 = a.tl ? gtimer() : 0;
+                tw += t1 - t0;
+                if (ready) {
                     hph[k] ^= 1;
                     hpend &= ~(1u << k);
                 } else {
@@ -1081,7 +818,16 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                         if (key > best) best = key;
                     }
                 }
+                if (a.tl) {
+                    t0 = gtimer();
+                    tc += t0 - t1;
+                }
                 __syncthreads();  // stage k consumed
+                if (a.tl) {
+                    t1 = gtimer();
+                    ts += t1 - t0;
+                    t0 = t1;
+                }
                 if (si + a.head_ns < hst) {
                     if (tid == 0) {
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -1090,12 +836,17 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                     hpend |= 1u << k;
                 }
             }
+            if (a.tl && blockIdx.x == 0 && tid == 0 && step < 8) {
+                a.tl[a.tl_cap / 2 + 6000 + step * 4 + 0] = tw;
+                a.tl[a.tl_cap / 2 + 6000 + step * 4 + 1] = tc;
+                a.tl[a.tl_cap / 2 + 6000 + step * 4 + 2] = ts;
+                a.tl[a.tl_cap / 2 + 6000 + step * 4 + 3] = hst;
+            }
             if (lane == 0) s_best[warp] = best;
             __syncthreads();
             if (tid == 0) {
                 unsigned long long m = 0;
                 for (int i = 0; i < kMegaWarps; i++) m = s_best[i] > m ? s_best[i] : m;
-                __threadfence();  // orders this step's max after the reset of its slot (block 0, last step)
                 if (m) atomicMax(&a.sync->amax[step & 1], m);
             }
         }
@@ -1119,10 +870,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             const unsigned long long key = *(volatile unsigned long long *)&a.sync->amax[step & 1];
             const int idx = key ? (int)argmax_index(key) : 0;
             if (blockIdx.x == 0 && tid == 0) {
-                // every CTA has read the previous step's slot (all passed this barrier): clear it for
-                // the next step; the fence orders the clear before this CTA's next rows
-                atomicExch(&a.sync->amax[(step + 1) & 1], 0ull);
-                __threadfence();
                 DecodeState *ds = a.st;
                 if (!ds->stopped) {
                     if (ds->step < ds->cap) a.out_ids[ds->step] = idx;
