@@ -106,6 +106,8 @@ struct HyCtx {
     char mega_why[128] = {0};       // why unsupported
     MegaLayer *d_mega_layers = nullptr;
     MegaSync *d_mega_sync = nullptr;
+    uint8_t *d_head_i8 = nullptr;   // int8 planes of the Q6_K head for the persistent kernel
+    size_t head_i8_bytes = 0;
     unsigned long long *d_tl = nullptr;
     int tl_cap = 0;
     MegaPlan mega_plan_v{};
@@ -621,11 +623,11 @@ bool mega_check(HyCtx *c) {
     if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->dev) != cudaSuccess || !coop)
         return no("no cooperative launch");
     c->mega_plan_v = mega_plan(c->nsm, c->H, c->F, c->qd, c->kvd, c->outw->n, c->hd);
-    if (c->outw->stride % 16 || !mega_head_ring(c->mega_plan_v, c->outw->stride))
+    if (!mega_head_ring(c->mega_plan_v, head_i8_stride(c->H)))
         return no("LM-head rows do not fit the shared-memory ring");
     // about three quarters of L2 holds the first rows of every CTA's head slice
     // across tokens (the layer weights, read once per token, are evict-first)
-    c->head_keep = (int)((double)c->l2_bytes * 0.75 / ((double)c->nsm * (double)c->outw->stride));
+    c->head_keep = (int)((double)c->l2_bytes * 0.75 / ((double)c->nsm * (double)head_i8_stride(c->H)));
     if (cudaFuncSetAttribute(c->mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)c->mega_plan_v.bytes) != cudaSuccess) {
         cudaGetLastError();
@@ -652,6 +654,20 @@ bool mega_check(HyCtx *c) {
         tab[i].k_norm = L.k_norm;
         tab[i].kc = c->d_kv + (size_t)i * 2 * c->ctx * c->kvd;
         tab[i].vc = tab[i].kc + (size_t)c->ctx * c->kvd;
+    }
+    {
+        const size_t hb = (size_t)c->outw->n * head_i8_stride(c->H);
+        if (c->head_i8_bytes != hb) {
+            if (c->d_head_i8) cudaFree(c->d_head_i8);
+            c->d_head_i8 = nullptr;
+            c->head_i8_bytes = 0;
+            CK(c, cudaMalloc(&c->d_head_i8, hb));
+            c->head_i8_bytes = hb;
+        }
+        const long long groups = (long long)c->outw->n * (c->H / 16);
+        q6k_to_i8<<<(unsigned)((groups + 255) / 256), 256, 0, c->st>>>(desc(c->outw, nullptr, 0), c->d_head_i8,
+                                                                     head_i8_stride(c->H));
+        CK(c, cudaGetLastError());
     }
     if (!c->d_mega_layers) CK(c, cudaMalloc(&c->d_mega_layers, (size_t)c->L * sizeof(MegaLayer)));
     if (!c->d_mega_sync) CK(c, cudaMalloc(&c->d_mega_sync, sizeof(MegaSync)));
@@ -714,6 +730,8 @@ bool mega_launch(HyCtx *c, int steps) {
     aa.trace = -1;
     a.head = desc(c->outw, nullptr, c->outw->n);
     a.embd = desc(c->embd, nullptr, 0);
+    a.head_i8 = c->d_head_i8;
+    a.head_i8_stride = head_i8_stride(c->H);
     a.vocab_out = c->vocab_out > 0 ? c->vocab_out : c->outw->n;
     a.out_norm = c->d_out_norm;
     a.h = c->d_h;
@@ -818,6 +836,9 @@ void free_fused(HyCtx *c) {
     if (c->d_mega_layers) cudaFree(c->d_mega_layers);
     if (c->d_mega_sync) cudaFree(c->d_mega_sync);
     if (c->d_tl) cudaFree(c->d_tl);
+    if (c->d_head_i8) cudaFree(c->d_head_i8);
+    c->d_head_i8 = nullptr;
+    c->head_i8_bytes = 0;
     c->d_mega_layers = nullptr;
     c->d_mega_sync = nullptr;
     c->d_tl = nullptr;

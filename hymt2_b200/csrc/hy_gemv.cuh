@@ -558,8 +558,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_panel_dec(const __grid_cons
                 }
             }
         }
+        // only lanes 4k hold partial sums: three butterfly levels bring them to lane 0
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
+        for (int o = 16; o >= 4; o >>= 1)
 #pragma unroll
             for (int g = 0; g < RG; g++) acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], o);
         if (a.epi == EPI_SILU) {

@@ -66,6 +66,8 @@ struct MegaArgs {
     int head_keep;            // rows of each CTA's head slice read with L2 evict-last (stay resident)
     AttnArgs attn;            // shape, rope tables, part buffer; per-layer fields set in-kernel
     WDesc head, embd;
+    const uint8_t *head_i8;   // int8 planes of the Q6_K head (q6k_to_i8), streamed by the ring
+    long long head_i8_stride;
     int vocab_out;
     const float *out_norm;
     float *h, *qkv, *ao, *act;
@@ -176,12 +178,13 @@ __device__ __forceinline__ bool bar_wait(const MegaArgs &a, unsigned target, int
     return *s_flag == 0;
 }
 
-// Every thread of the CTA waits for slot `bar`; the outcome is made uniform
-// across the CTA (a timeout seen by any thread fails the whole CTA), so no
-// warp can diverge into a collective the others skip.
+// Each warp waits for slot `bar`; the outcome is uniform within the warp
+// (its row loop uses warp shuffles).  A warp that times out raises the error
+// word, skips its rows and still reaches every CTA barrier; the next grid
+// barrier then stops every CTA.
 __device__ __forceinline__ bool mega_slot_ready(const MegaArgs &a, uint64_t *bar, unsigned parity) {
-    const bool ready = __syncthreads_and(mbar_wait(bar, parity)) != 0;
-    if (!ready && threadIdx.x == 0) raise_err(a, MEGA_ERR_WEIGHTS);
+    const bool ready = __all_sync(0xffffffffu, mbar_wait(bar, parity)) != 0;
+    if (!ready && (threadIdx.x & 31) == 0) raise_err(a, MEGA_ERR_WEIGHTS);
     return ready;
 }
 
@@ -398,8 +401,9 @@ __device__ __forceinline__ void mega_rows(int shift, int off, int r0, int r1, in
                 }
             }
         }
+        // only lanes 4k hold partial sums: three butterfly levels bring them to lane 0
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
+        for (int o = 16; o >= 4; o >>= 1)
 #pragma unroll
             for (int g = 0; g < RG; g++) acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], o);
         if (lane == 0) epi(rg, acc, r1);
@@ -462,14 +466,41 @@ __device__ __forceinline__ float q6k_row_smem(const uint8_t *row, int nb, int K,
     return warp_sum(acc);
 }
 
+// One int8 head row (q6k_to_i8 layout) in shared memory against the Q8_K
+// activation held in registers (av, this lane's unit; dact its block's d).
+// Same block integers and float steps as q6k_row_smem / gemv_q6k.
+__device__ __forceinline__ float i8_row_smem(const uint8_t *row, int K, const int4 (&av)[4], float dact, bool ok) {
+    const int lane = threadIdx.x & 31;
+    int acc_i = 0;
+    float dw = 0.f;
+    if (ok) {
+        const uint32_t sc = *(const uint32_t *)(row + K + lane * 4);
+        dw = *(const float *)(row + K + K / 16 + (lane >> 2) * 4);
+#pragma unroll
+        for (int l = 0; l < 4; l++) {
+            const int4 c = *(const int4 *)(row + (size_t)l * (K / 4) + lane * 16);
+            int t = dp4a(c.x, av[l].x, 0);
+            t = dp4a(c.y, av[l].y, t);
+            t = dp4a(c.z, av[l].z, t);
+            t = dp4a(c.w, av[l].w, t);
+            acc_i += (int)(int8_t)(sc >> (8 * l)) * t;
+        }
+    }
+    acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 1);
+    acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 2);
+    float acc = 0.f;
+    if (ok && (lane & 3) == 0) acc += dw * dact * (float)acc_i;
+    return warp_sum(acc);
+}
+
 // Thread 0: arm ring stage `si % ns` and copy rows [r0 + si*kHeadRows, ...)
 // of this CTA's head slice into it.
 __device__ __forceinline__ void head_fill(const MegaArgs &a, uint8_t *smem, uint64_t *hbar, int si, int r0, int r1) {
     const int k = si % a.head_ns, row = r0 + si * kHeadRows, n = min(kHeadRows, r1 - row);
-    const unsigned bytes = (unsigned)n * (unsigned)a.head.stride;
+    const unsigned bytes = (unsigned)n * (unsigned)a.head_i8_stride;
     mbar_expect(&hbar[k], bytes);
     const uint64_t pol = si * kHeadRows < a.head_keep ? l2_policy_evict_last() : l2_policy_evict_first();
-    bulk_g2s_hint(smem + a.head_off[k], a.head.w + (size_t)row * a.head.stride, bytes, &hbar[k], pol);
+    bulk_g2s_hint(smem + a.head_off[k], a.head_i8 + (size_t)row * a.head_i8_stride, bytes, &hbar[k], pol);
 }
 
 // ---------------------------------------------------------------- the kernel
@@ -794,7 +825,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
         // ---- LM head + argmax (rows < vocab_out compete), rows streamed through the ring
         {
             mega_stage<2>(a.h, &npre, a.eps, a.H, st);
-            const int nb = a.H / 256;
+            // this lane's unit of the activation, kept in registers for every row
+            const bool uok = lane < a.H / 64;
+            int4 hav[4];
+#pragma unroll
+            for (int l = 0; l < 4; l++)
+                hav[l] = uok ? *(const int4 *)&st.qp[(size_t)l * (a.H / 4) + lane * 16] : make_int4(0, 0, 0, 0);
+            const float hd = uok ? st.d[lane >> 2] : 0.f;
             unsigned long long best = 0;
             unsigned long long tw = 0, tc = 0, ts = 0, t0 = a.tl ? gtimer() : 0;
             for (int si = 0; si < hst && ok; si++) {
@@ -812,7 +849,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 }
                 const int r = hr0 + si * kHeadRows + warp;
                 if (r < hr1) {
-                    const float v = q6k_row_smem(smem + a.head_off[k] + (size_t)warp * a.head.stride, nb, a.H, st);
+                    const float v = i8_row_smem(smem + a.head_off[k] + (size_t)warp * a.head_i8_stride, a.H, hav, hd, uok);
                     if (lane == 0 && r < a.vocab_out) {
                         const unsigned long long key = argmax_key(v, (uint32_t)r);
                         if (key > best) best = key;
