@@ -145,18 +145,15 @@ __device__ __forceinline__ int ld_relaxed_s32(const int *p) {
 __device__ __forceinline__ void raise_err(const MegaArgs &a, int code) { atomicCAS(&a.sync->err, 0, code); }
 
 // Grid-wide barrier in two halves.  bar_arrive: once every thread's writes
-// of the phase are done (__syncthreads), thread 0 publishes them
-// (__threadfence) and adds 1 to the arrival counter.  Work that does not
+// of the phase are done (__syncthreads), thread 0 adds 1 to the arrival
+// counter with release semantics (publishing them).  Work that does not
 // depend on other CTAs can run between the halves.  bar_wait: thread 0 polls
 // until the counter reaches the running target; bounded, and a timeout or
 // another CTA's error makes every CTA return false from here on.
 __device__ __forceinline__ void bar_arrive(const MegaArgs &a, unsigned &target) {
     __syncthreads();
     target += gridDim.x;
-    if (threadIdx.x == 0) {
-        __threadfence();
-        atomicAdd(&a.sync->bar, 1u);
-    }
+    if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&a.sync->bar) : "memory");
 }
 __device__ __forceinline__ bool bar_wait(const MegaArgs &a, unsigned target, int *s_flag) {
     if (threadIdx.x == 0) {
@@ -711,12 +708,14 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             tl_mark(a, tli);
             tl_cta(a, step == 1 && l == 5, 4);
             bar_arrive(a, target);
-            if (more && ok) {
+            if (more && ok && l + 1 < a.L) {  // after the last layer: once the head is done
                 if (tid == 0) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     mega_fill(a, tab, smem, &mbar[1], 1, nl);
                 }
                 pending |= 2u;
+            }
+            if (more && ok) {
                 // this layer's attention is done with the K/V area: stage the next layer's rows
                 // (after the last layer the area carries the LM-head ring; the next step's rows
                 // follow the head)
@@ -809,7 +808,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 pending |= 8u;
             }
             if (l + 1 == a.L && ok) {
-                // gate|up and down slots and the K/V area are free: start the LM-head ring
+                // o_proj, gate|up and down slots and the K/V area are free: start the LM-head ring
                 if (tid == 0) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     for (int k = 0; k < a.head_ns && k < hst; k++) head_fill(a, smem, hbar, k, hr0, hr1);
@@ -894,10 +893,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             // the ring is drained: layer 0's gate|up and down slices and K/V rows for the next step
             if (tid == 0) {
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                mega_fill(a, tab, smem, &mbar[1], 1, 0);
                 mega_fill(a, tab, smem, &mbar[2], 2, 0);
                 mega_fill(a, tab, smem, &mbar[3], 3, 0);
             }
-            pending |= 4u | 8u;
+            pending |= 2u | 4u | 8u;
             if (attn_cta(pos + 1)) mega_kv_fill<HD>(a, tab[0], sK, sV, akvh, j0_of(pos + 1), ncache_of(pos + 1));
         }
         if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
@@ -937,17 +937,21 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
 // Dynamic shared memory plan of decode_mega for a model shape.
 struct MegaPlan {
     int rpc[5], slot_off[4], stage_off, attn_off, kmax;
-    int head_ns, head_off[4];  // LM-head ring: stages placed in the gate|up + down slots and the K/V area
+    int head_ns, head_off[4];  // LM-head ring: stages placed in the o_proj, gate|up, down slots and the K/V area
     size_t bytes;
 };
 
 inline MegaPlan mega_plan(int grid, int H, int F, int qd, int kvd, int vocab, int HD) {
     MegaPlan p;
     size_t off = 0;
+    // row slices as even as the bulk copies allow: with >= 4 blocks per row the
+    // per-row scales are a multiple of 16 bytes and slices only need to be even
+    // (gate|up pairs); shorter rows keep multiples of kMegaRowAlign
+    const int align = (H % 1024 == 0 && F % 1024 == 0 && qd % 1024 == 0) ? 2 : kMegaRowAlign;
     for (int t = 0; t < 4; t++) {
         const int rows = mega_phase_rows(t, H, F, qd, kvd);
         int r = (rows + grid - 1) / grid;
-        r = (r + kMegaRowAlign - 1) / kMegaRowAlign * kMegaRowAlign;
+        r = (r + align - 1) / align * align;
         p.rpc[t] = r;
         p.slot_off[t] = (int)off;
         off += (size_t)mega_slot_bytes(r, mega_phase_k(t, H, F, qd));
@@ -969,7 +973,7 @@ inline MegaPlan mega_plan(int grid, int H, int F, int qd, int kvd, int vocab, in
 inline bool mega_head_ring(MegaPlan &p, long long head_stride) {
     const size_t sb = (size_t)kHeadRows * (size_t)head_stride;
     p.head_ns = 0;
-    for (size_t o = (size_t)p.slot_off[2]; o + sb <= (size_t)p.stage_off && p.head_ns < 4; o += sb)
+    for (size_t o = (size_t)p.slot_off[1]; o + sb <= (size_t)p.stage_off && p.head_ns < 4; o += sb)
         p.head_off[p.head_ns++] = (int)o;
     for (size_t o = (size_t)p.attn_off; o + sb <= p.bytes && p.head_ns < 4; o += sb) p.head_off[p.head_ns++] = (int)o;
     return p.head_ns >= 2;
