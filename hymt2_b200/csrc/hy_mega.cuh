@@ -890,7 +890,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
         bar_arrive(a, target);
         norm_preload<2>(tab[0].attn_norm, a.H, npre);
         if (ok && step + 1 < a.steps) {
-            // the ring is drained: layer 0's gate|up and down slices and K/V rows for the next step
+            // the ring is drained: layer 0's o_proj, gate|up and down slices and K/V rows for the next step
             if (tid == 0) {
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 mega_fill(a, tab, smem, &mbar[1], 1, 0);
@@ -944,10 +944,7 @@ struct MegaPlan {
 inline MegaPlan mega_plan(int grid, int H, int F, int qd, int kvd, int vocab, int HD) {
     MegaPlan p;
     size_t off = 0;
-    // row slices as even as the bulk copies allow: with >= 4 blocks per row the
-    // per-row scales are a multiple of 16 bytes and slices only need to be even
-    // (gate|up pairs); shorter rows keep multiples of kMegaRowAlign
-    const int align = (H % 1024 == 0 && F % 1024 == 0 && qd % 1024 == 0) ? 2 : kMegaRowAlign;
+    const int align = kMegaRowAlign;
     for (int t = 0; t < 4; t++) {
         const int rows = mega_phase_rows(t, H, F, qd, kvd);
         int r = (rows + grid - 1) / grid;
