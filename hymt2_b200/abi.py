@@ -78,6 +78,8 @@ SIGNATURES = {
     "hyc_host_alloc": (P, [Z]),
     "hyc_host_free": (None, [P]),
     "hyc_set_decode_mode": (I, [P, I]),
+    "hyc_set_tc": (I, [P, I]),
+    "hyc_tc_test": (I, [P, P, I, P, P, P, F, I, P]),
     "hyc_decode_path": (I, [P, C.c_char_p, I]),
     "hyc_mega_timeline": (I, [P, P, I]),
     "hyc_quantize_q8k": (I, [P, P, I, I, P]),

@@ -24,6 +24,7 @@
 #include "hy_gemv.cuh"
 #include "hy_mega.cuh"
 #include "hy_misc.cuh"
+#include "hy_tc.cuh"
 
 using namespace hyk;
 
@@ -48,6 +49,8 @@ struct HyWeight {
     float *d_out;   // matmul op output [MAX_BATCH][n] (lazy)
     float *h_out;   // pinned alias returned by weight_out (lazy)
     HyCtx *c;
+    int8_t *tc_w;   // tensor-core tiles of a panel weight (lazy, hy_tc.cuh layout)
+    float *tc_ws;   // their block scales
 };
 
 struct Layer {
@@ -111,6 +114,12 @@ struct HyCtx {
     unsigned long long *d_tl = nullptr;
     int tl_cap = 0;
     MegaPlan mega_plan_v{};
+    // tensor-core path for multi-token chunks (hy_tc.cuh)
+    bool tc_on = true;
+    int8_t *d_tca = nullptr;        // tiled Q8_K codes of up to kMaxChunk tokens
+    float *d_tcad = nullptr;        // their block scales
+    int *d_tcerr = nullptr;         // set by tc_gemm on a bounded-wait timeout
+    size_t tca_bytes = 0;
     int head_keep = 0;              // head rows per CTA kept resident in L2 by the persistent kernel
     size_t l2_bytes = 0;
     void *mega_kernel = nullptr;
@@ -244,6 +253,7 @@ void init_kernel_attrs() {
     set_smem(attn_chunk_kernel<64, 2>);
     set_smem(attn_chunk_kernel<64, 4>);
     set_smem(attn_chunk_kernel<64, 8>);
+    set_smem(tc_gemm);
 }
 
 // One launch for nt <= NT tokens.
@@ -353,6 +363,92 @@ bool run_multi(HyCtx *c, HyWeight *const *ws, float *const *outs, const int *lds
     return true;
 }
 
+// ---------------------------------------------------------------- tensor-core chunks
+
+constexpr int kTcMinTokens = 32;  // chunks at least this long use the tensor-core GEMM
+
+bool tc_usable(HyCtx *c, int nt, HyWeight *const *ws, int cnt) {
+    if (!c->tc_on || nt < kTcMinTokens || nt > kMaxChunk) return false;
+    for (int i = 0; i < cnt; i++)
+        if (ws[i]->fmt != FMT_PANEL || ws[i]->k % 256) return false;
+    return true;
+}
+
+// Tensor-core tiles of a panel weight, built on first use.
+bool tc_weight(HyCtx *c, HyWeight *w) {
+    if (w->tc_w) return true;
+    const int ntiles = (w->n + kTcN - 1) / kTcN;
+    CK(c, cudaMalloc(&w->tc_w, (size_t)ntiles * w->nb * kTcBBytes));
+    CK(c, cudaMalloc(&w->tc_ws, (size_t)ntiles * w->nb * kTcN * 4));
+    const long long total = (long long)ntiles * kTcN * w->nb * 16;
+    tc_panel_to_tiled<<<(unsigned)((total + 255) / 256), 256, 0, c->st>>>(desc(w, nullptr, 0), w->tc_w, w->tc_ws);
+    CK(c, cudaGetLastError());
+    return true;
+}
+
+bool tc_scratch(HyCtx *c, int K) {
+    const size_t nbmax = (size_t)(K / 256), bytes = (size_t)(kMaxChunk / kTcM) * nbmax * kTcABytes;
+    if (bytes <= c->tca_bytes) return true;
+    if (c->d_tca) cudaFree(c->d_tca);
+    if (c->d_tcad) cudaFree(c->d_tcad);
+    c->d_tca = nullptr;
+    c->d_tcad = nullptr;
+    c->tca_bytes = 0;
+    CK(c, cudaMalloc(&c->d_tca, bytes));
+    CK(c, cudaMalloc(&c->d_tcad, (size_t)kMaxChunk * nbmax * 4));
+    if (!c->d_tcerr) {
+        CK(c, cudaMalloc(&c->d_tcerr, 4));
+        CK(c, cudaMemsetAsync(c->d_tcerr, 0, 4, c->st));
+    }
+    c->tca_bytes = bytes;
+    return true;
+}
+
+// nt tokens through up to three panel weights sharing one activation
+// prologue (pro.act / x / x2 / norm_w / eps, pro.k = K): one quantise launch
+// writing tiled Q8_K codes, then one tensor-core GEMM per weight; outs[i] is
+// [nt][lds[i]], stored (epi 0) or accumulated (epi 1).
+bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float *const *outs, const int *lds,
+               int cnt, int epi) {
+    const int K = pro.k, nb = K / 256, tpad = (nt + kTcM - 1) / kTcM * kTcM;
+    if (!tc_scratch(c, K)) return false;
+    for (int i = 0; i < cnt; i++)
+        if (!tc_weight(c, ws[i])) return false;
+    if (!launch(c, tc_quantize, dim3(tpad), dim3(kGemvThreads), (size_t)(K + 64) * 4, false, pro, nt, c->d_tca,
+                c->d_tcad))
+        return false;
+    for (int i = 0; i < cnt; i++) {
+        TcArgs ta;
+        ta.a = c->d_tca;
+        ta.ad = c->d_tcad;
+        ta.w = ws[i]->tc_w;
+        ta.ws = ws[i]->tc_ws;
+        ta.out = outs[i];
+        ta.ldo = lds[i];
+        ta.T = nt;
+        ta.N = ws[i]->n;
+        ta.nb = nb;
+        ta.epi = epi;
+        ta.err = c->d_tcerr;
+        if (!launch(c, tc_gemm, dim3(tpad / kTcM, (ws[i]->n + kTcN - 1) / kTcN), dim3(kTcThreads), tc_smem_bytes(),
+                    false, ta))
+            return false;
+    }
+    return true;
+}
+
+// The tensor-core GEMM reports a timed-out wait through its error word.
+bool tc_status(HyCtx *c) {
+    if (!c->d_tcerr) return true;
+    int err = 0;
+    CK(c, cudaMemcpyAsync(&err, c->d_tcerr, 4, cudaMemcpyDeviceToHost, c->st));
+    CK(c, cudaStreamSynchronize(c->st));
+    if (!err) return true;
+    c->broken = true;
+    snprintf(c->err, sizeof c->err, "tensor-core GEMM: a pipeline wait timed out");
+    return false;
+}
+
 // ---------------------------------------------------------------- fused layer loop
 
 template <int HD, int G>
@@ -414,6 +510,7 @@ bool gateup_forward(HyCtx *c, const Layer &L, int nt, bool pdl) {
     HyWeight *ws[2] = {L.g, L.u};
     float *outs[2] = {c->d_g, c->d_u};
     const int lds[2] = {c->F, c->F};
+    if (tc_usable(c, nt, ws, 2)) return tc_linear(c, a, nt, ws, outs, lds, 2, 0);
     a.epi = EPI_STORE;
     return run_multi(c, ws, outs, lds, 2, a, pdl);
 }
@@ -429,6 +526,12 @@ bool down_forward(HyCtx *c, const Layer &L, int nt, bool pdl, float *dst) {
         a.x2 = c->d_u;
     }
     a.ldx = c->F;
+    {
+        HyWeight *ws[1] = {L.d};
+        float *outs[1] = {dst};
+        const int lds[1] = {c->H};
+        if (tc_usable(c, nt, ws, 1)) return tc_linear(c, a, nt, ws, outs, lds, 1, 1);
+    }
     a.epi = EPI_ADD;
     a.nw = 1;
     a.rows_total = L.d->n;
@@ -453,8 +556,12 @@ bool layer_forward(HyCtx *c, int li, int nt, const int *pos_ptr, bool pdl) {
         a.ldx = c->H;
         a.norm_w = L.attn_norm;
         a.eps = c->eps;
-        a.epi = EPI_STORE;
-        if (!run_multi(c, ws, outs, lds, 3, a, pdl)) return false;
+        if (tc_usable(c, nt, ws, 3)) {
+            if (!tc_linear(c, a, nt, ws, outs, lds, 3, 0)) return false;
+        } else {
+            a.epi = EPI_STORE;
+            if (!run_multi(c, ws, outs, lds, 3, a, pdl)) return false;
+        }
     }
     {
         AttnArgs aa;
@@ -493,11 +600,18 @@ bool layer_forward(HyCtx *c, int li, int nt, const int *pos_ptr, bool pdl) {
         a.act = ACT_VEC;
         a.x = c->d_ao;
         a.ldx = c->qd;
-        a.epi = EPI_ADD;
-        a.nw = 1;
-        a.rows_total = L.o->n;
-        a.w[0] = desc(L.o, c->d_h, c->H);
-        if (!run_gemv(c, a, pdl)) return false;
+        HyWeight *ws[1] = {L.o};
+        float *outs[1] = {c->d_h};
+        const int lds[1] = {c->H};
+        if (tc_usable(c, nt, ws, 1)) {
+            if (!tc_linear(c, a, nt, ws, outs, lds, 1, 1)) return false;
+        } else {
+            a.epi = EPI_ADD;
+            a.nw = 1;
+            a.rows_total = L.o->n;
+            a.w[0] = desc(L.o, c->d_h, c->H);
+            if (!run_gemv(c, a, pdl)) return false;
+        }
     }
     return ffn_forward(c, L, nt, pdl);
 }
@@ -854,6 +968,9 @@ void destroy_impl(void *impl) {
     if (c->d_xq) cudaFree(c->d_xq);
     if (c->d_x32) cudaFree(c->d_x32);
     if (c->d_ints) cudaFree(c->d_ints);
+    if (c->d_tca) cudaFree(c->d_tca);
+    if (c->d_tcad) cudaFree(c->d_tcad);
+    if (c->d_tcerr) cudaFree(c->d_tcerr);
     if (c->h_pinned_int) cudaFreeHost(c->h_pinned_int);
     if (c->st) cudaStreamDestroy(c->st);
     delete c;
@@ -866,6 +983,8 @@ void release(hy_dweight *hw) {
     if (w->s) cudaFree(w->s);
     if (w->d_out) cudaFree(w->d_out);
     if (w->h_out) cudaFreeHost(w->h_out);
+    if (w->tc_w) cudaFree(w->tc_w);
+    if (w->tc_ws) cudaFree(w->tc_ws);
     delete w;
 }
 
@@ -1171,7 +1290,7 @@ bool fused_forward(void *impl, hy_fused_args *a) {
     if (a->want_logits)
         CK(c, cudaMemcpyAsync(a->logits, c->d_logits, (size_t)c->outw->n * 4, cudaMemcpyDeviceToHost, c->st));
     CK(c, cudaStreamSynchronize(c->st));
-    return true;
+    return tc_status(c);
 }
 
 const hy_device_ops kOps = {destroy_impl, upload, release, matmul, is_software, weight_out, fused_prepare,
@@ -1261,7 +1380,7 @@ HYC_API int hyc_sync(void *impl) {
         fail(c, "cudaStreamSynchronize", e);
         return -1;
     }
-    return mega_status(c) ? 0 : -1;
+    return mega_status(c) && tc_status(c) ? 0 : -1;
 }
 
 HYC_API int hyc_set_embedding(void *impl, hy_dweight *embd) {
@@ -1272,6 +1391,50 @@ HYC_API int hyc_set_embedding(void *impl, hy_dweight *embd) {
     c->g_dec_vocab = -1;
     c->mega_state = -1;
     return 0;
+}
+
+HYC_API int hyc_set_tc(void *impl, int on) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c) return -1;
+    c->tc_on = on != 0;
+    return 0;
+}
+
+HYC_API int hyc_tc_test(void *impl, hy_dweight *hw, int act, const float *x, const float *x2, const float *norm_w,
+                        float eps, int nt, float *out) {
+    HyCtx *c = (HyCtx *)impl;
+    HyWeight *w = (HyWeight *)hw;
+    if (!c || c->broken || !w || w->fmt != FMT_PANEL || nt < 1 || nt > kMaxChunk || act < ACT_VEC || act > ACT_SILU ||
+        (act == ACT_NORM && !norm_w) || (act == ACT_SILU && !x2))
+        return -1;
+    if (cudaSetDevice(c->dev) != cudaSuccess) return -1;
+    const int K = w->k;
+    float *dx = nullptr, *dx2 = nullptr, *dn = nullptr, *dout = nullptr;
+    bool ok = cudaMalloc(&dx, (size_t)nt * K * 4) == cudaSuccess && cudaMalloc(&dx2, (size_t)nt * K * 4) == cudaSuccess &&
+              cudaMalloc(&dn, (size_t)K * 4) == cudaSuccess && cudaMalloc(&dout, (size_t)nt * w->n * 4) == cudaSuccess &&
+              h2d(c, dx, x, (size_t)nt * K * 4) == cudaSuccess &&
+              (!x2 || h2d(c, dx2, x2, (size_t)nt * K * 4) == cudaSuccess) &&
+              (!norm_w || h2d(c, dn, norm_w, (size_t)K * 4) == cudaSuccess);
+    if (ok) {
+        GemvArgs pro = gemv_args(nt, K);
+        pro.act = act;
+        pro.x = dx;
+        pro.x2 = dx2;
+        pro.ldx = K;
+        pro.norm_w = dn;
+        pro.eps = eps;
+        HyWeight *ws[1] = {w};
+        float *outs[1] = {dout};
+        const int lds[1] = {w->n};
+        ok = tc_linear(c, pro, nt, ws, outs, lds, 1, 0) &&
+             cudaMemcpyAsync(out, dout, (size_t)nt * w->n * 4, cudaMemcpyDeviceToHost, c->st) == cudaSuccess &&
+             cudaStreamSynchronize(c->st) == cudaSuccess && tc_status(c);
+    }
+    cudaFree(dx);
+    cudaFree(dx2);
+    cudaFree(dn);
+    cudaFree(dout);
+    return ok ? 0 : -1;
 }
 
 HYC_API int hyc_set_decode_mode(void *impl, int mode) {
@@ -1365,7 +1528,7 @@ HYC_API int hyc_decode_steps_host(void *impl, int steps, int *tok_io) {
 HYC_API int hyc_decode_read(void *impl, int *out_ids, int cap) {
     HyCtx *c = (HyCtx *)impl;
     if (!c || c->broken || !c->fused) return -1;
-    if (!mega_status(c)) return -1;
+    if (!mega_status(c) || !tc_status(c)) return -1;
     DecodeState s;
     if (cudaMemcpyAsync(&s, c->d_state, sizeof s, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
         cudaStreamSynchronize(c->st) != cudaSuccess) {

@@ -1,0 +1,336 @@
+// hy_tc.cuh — int8 tensor-core GEMM for batched prefill / multi-sequence
+// decode on sm_100a: tcgen05.mma kind::i8, accumulators in TMEM.
+//
+// Y[t][n] = sum_b ad[t][b] * ws[n][b] * S_b[t][n],  S_b = sum_{k in block b} A[t][k] W[n][k]
+// with A the Q8_K codes of the activations (per-256-block scale ad) and W the
+// weight as small integers (per-256-block scale ws).  For panel weights
+// (STQ1_0 / Q2_0C) W = code * 2^shift - off is exactly the value the panel
+// GEMV multiplies (reference src/kernels.c:565-581), so every S_b is the
+// reference's per-block integer; the blocks are combined in fp32.
+//
+// Operands live in global memory pre-tiled in the UMMA canonical K-major
+// layout without swizzle: a tile of R rows x 256 K is 32 x (R/8) core
+// matrices of 8 rows x 16 bytes; core (row group g, 16-byte k chunk c) sits
+// at (c * R/8 + g) * 128 bytes.  One bulk copy moves a whole tile.
+//
+// CTA = 128 tokens x 256 weight rows; warp 0 streams (A, W, ws) tiles of one
+// K block per stage into a 2-stage ring, warp 1 (one thread) issues 8 MMAs of
+// K = 32 per block into one of two TMEM accumulators (256 columns each), and
+// 16 epilogue warps (4 per TMEM lane quarter, 64 columns each) read the
+// block's int32 results with tcgen05.ld and fold them into fp32 registers
+// while the next block's MMAs run.  Every wait is bounded; TMEM is released
+// on every exit.
+#pragma once
+#include "hy_common.cuh"
+#include "hy_gemv.cuh"
+
+namespace hyk {
+
+constexpr int kTcM = 128;       // tokens per tile (TMEM lanes)
+constexpr int kTcN = 256;       // weight rows per tile (accumulator columns)
+constexpr int kTcKB = 256;      // K per stage: one Q8_K block
+constexpr int kTcStages = 2;
+constexpr int kTcEpiWarps = 16;
+constexpr int kTcThreads = (4 + kTcEpiWarps) * 32;  // warp 0 producer, 1 MMA, 2-3 idle, 4.. epilogue
+constexpr int kTcABytes = kTcM * kTcKB;             // 32 KB
+constexpr int kTcBBytes = kTcN * kTcKB;             // 64 KB
+constexpr int kTcWsBytes = kTcN * 4;                // 1 KB
+constexpr int kTcStageBytes = kTcABytes + kTcBBytes + kTcWsBytes;
+constexpr unsigned long long kTcWaitNs = 2000000000ull;
+
+__host__ __device__ inline size_t tc_smem_bytes() { return (size_t)kTcStages * kTcStageBytes + 1024; }
+
+// Byte offset of (row r, k) inside a canonical tile of R rows x 256 K.
+__host__ __device__ inline size_t tc_tile_off(int r, int k, int R) {
+    return ((size_t)(k >> 4) * (R / 8) + (r >> 3)) * 128 + (size_t)(r & 7) * 16 + (k & 15);
+}
+
+struct TcArgs {
+    const int8_t *a;   // tiled activations [ceil(T/128)][nb][128 x 256]
+    const float *ad;   // activation block scales [T_pad][nb]
+    const int8_t *w;   // tiled weight [ceil(N/256)][nb][256 x 256]
+    const float *ws;   // tiled weight block scales [ceil(N/256)][nb][256]
+    float *out;        // [T][ldo]
+    int ldo, T, N, nb;
+    int epi;           // 0: out = y, 1: out += y
+    int *err;          // set on a bounded-wait timeout
+};
+
+__device__ __forceinline__ uint32_t tc_smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void tc_mbar_init(uint64_t *b, unsigned count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(tc_smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void tc_mbar_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc_smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void tc_mbar_expect(uint64_t *b, unsigned tx) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_smem_u32(b)), "r"(tx) : "memory");
+}
+__device__ __forceinline__ bool tc_mbar_try(uint64_t *b, unsigned parity) {
+    unsigned ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(tc_smem_u32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool tc_mbar_wait(uint64_t *b, unsigned parity) {
+    if (tc_mbar_try(b, parity)) return true;
+    const unsigned long long t0 = gtimer();
+    while (!tc_mbar_try(b, parity))
+        if (gtimer() - t0 > kTcWaitNs) return false;
+    return true;
+}
+__device__ __forceinline__ void tc_bulk(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     tc_smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(tc_smem_u32(bar))
+                 : "memory");
+}
+
+// UMMA shared-memory descriptor of MMA step s (k chunks 2s, 2s+1) of a
+// canonical tile of R rows: no swizzle, LBO = distance between k chunks,
+// SBO = distance between 8-row groups, version 1.
+__device__ __forceinline__ uint64_t tc_desc(const void *tile, int s, int R) {
+    const uint32_t addr = tc_smem_u32(tile) + (uint32_t)s * 2u * (uint32_t)(R / 8) * 128u;
+    const uint64_t lbo = (uint64_t)((R / 8) * 128) >> 4, sbo = 128 >> 4;
+    return (uint64_t)((addr >> 4) & 0x3FFFu) | (lbo << 16) | (sbo << 32) | (1ull << 46);
+}
+// Instruction descriptor: D s32, A s8, B s8, both K-major, N, M.
+__host__ __device__ constexpr uint32_t tc_idesc(int M, int N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, int acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc)
+        : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t *b) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(tc_smem_u32(b))
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+
+// 32 lanes x 16 columns of 32-bit words from TMEM (this warp's lane quarter).
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__ TcArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf[2], acce[2], fin;
+    __shared__ uint32_t s_tmem;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt = blockIdx.x, ntile = blockIdx.y, nb = a.nb;
+    uint8_t *stage = (uint8_t *)(((uintptr_t)smem + 1023) & ~(uintptr_t)1023);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kTcStages; s++) {
+            tc_mbar_init(&full[s], 1);
+            tc_mbar_init(&empty[s], 1 + kTcEpiWarps);  // MMA commit + every epilogue warp (block scales read)
+        }
+        for (int b = 0; b < 2; b++) {
+            tc_mbar_init(&accf[b], 1);
+            tc_mbar_init(&acce[b], kTcEpiWarps);
+        }
+        tc_mbar_init(&fin, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(tc_smem_u32(&s_tmem))
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    bool ok = true;
+    if (warp == 0) {
+        // producer: A tile, W tile and W block scales of each K block
+        if (lane == 0) {
+            for (int kb = 0; kb < nb && ok; kb++) {
+                const int s = kb % kTcStages, use = kb / kTcStages;
+                if (use > 0 && !tc_mbar_wait(&empty[s], (use - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *st = stage + (size_t)s * kTcStageBytes;
+                tc_mbar_expect(&full[s], kTcStageBytes);
+                tc_bulk(st, a.a + ((size_t)mt * nb + kb) * kTcABytes, kTcABytes, &full[s]);
+                tc_bulk(st + kTcABytes, a.w + ((size_t)ntile * nb + kb) * kTcBBytes, kTcBBytes, &full[s]);
+                tc_bulk(st + kTcABytes + kTcBBytes, a.ws + ((size_t)ntile * nb + kb) * kTcN, kTcWsBytes, &full[s]);
+            }
+            if (!ok) atomicExch(a.err, 1);
+        }
+    } else if (warp == 1) {
+        // MMA issuer: 8 MMAs (K = 32 each) per block into accumulator kb % 2
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc_idesc(kTcM, kTcN);
+            for (int kb = 0; kb < nb && ok; kb++) {
+                const int s = kb % kTcStages, use = kb / kTcStages, buf = kb & 1, ub = kb >> 1;
+                if (!tc_mbar_wait(&full[s], use & 1) || (ub > 0 && !tc_mbar_wait(&acce[buf], (ub - 1) & 1))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint8_t *st = stage + (size_t)s * kTcStageBytes;
+#pragma unroll
+                for (int k = 0; k < kTcKB / 32; k++)
+                    tc_mma(tmem + (uint32_t)buf * kTcN, tc_desc(st, k, kTcM), tc_desc(st + kTcABytes, k, kTcN), idesc,
+                           k > 0);
+                tc_commit(&empty[s]);
+                tc_commit(&accf[buf]);
+            }
+            tc_commit(&fin);  // completes when every MMA issued above has
+            if (!tc_mbar_wait(&fin, 0)) ok = false;
+            if (!ok) atomicExch(a.err, 1);
+        }
+    } else if (warp >= 4) {
+        // epilogue: lane quarter q (tokens 32q..32q+31 of the tile), columns part*64 ..
+        const int e = warp - 4, q = warp & 3, part = e >> 2;
+        const int t = mt * kTcM + q * 32 + lane;
+        float acc[64];
+#pragma unroll
+        for (int j = 0; j < 64; j++) acc[j] = 0.f;
+        for (int kb = 0; kb < nb && ok; kb++) {
+            const int s = kb % kTcStages, buf = kb & 1, ub = kb >> 1;
+            if (!tc_mbar_wait(&accf[buf], ub & 1)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const float yd = t < a.T ? __ldg(a.ad + (size_t)t * nb + kb) : 0.f;
+            const float *wsb = (const float *)(stage + (size_t)s * kTcStageBytes + kTcABytes + kTcBBytes) + part * 64;
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                uint32_t r[16];
+                tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kTcN + part * 64 + c * 16), r);
+#pragma unroll
+                for (int j = 0; j < 16; j++)
+                    acc[c * 16 + j] = fmaf((float)(int)r[j], yd * wsb[c * 16 + j], acc[c * 16 + j]);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                tc_mbar_arrive(&acce[buf]);
+                tc_mbar_arrive(&empty[s]);
+            }
+        }
+        if (ok && t < a.T) {
+            float *o = a.out + (size_t)t * a.ldo;
+            const int n0 = ntile * kTcN + part * 64;
+#pragma unroll
+            for (int j = 0; j < 64; j++) {
+                const int n = n0 + j;
+                if (n < a.N) o[n] = a.epi ? o[n] + acc[j] : acc[j];
+            }
+        }
+        if (!ok && lane == 0) atomicExch(a.err, 1);
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------- operand preparation
+
+// Panel weight -> tiled int8 W = code * 2^shift - off, rows past n are zero,
+// and the tiled block scales (zero past n).  One thread per (row, 16 codes).
+__global__ void tc_panel_to_tiled(const __grid_constant__ WDesc w, int8_t *tw, float *tws) {
+    const int nb = w.k / 256, ntiles = (w.n + kTcN - 1) / kTcN;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long total = (long long)ntiles * kTcN * nb * 16;
+    if (i >= total) return;
+    const int g16 = (int)(i % 16);                      // 16-element group in the block
+    const int b = (int)((i / 16) % nb);
+    const int rr = (int)(i / (16LL * nb));              // padded row
+    const int tile = rr / kTcN, r = rr % kTcN;
+    int8_t *dst = tw + ((size_t)tile * nb + b) * kTcBBytes;
+    const int ch = g16 >> 2, l = g16 & 3;               // natural chunk of 64, plane
+    for (int j = 0; j < 16; j++) {
+        int v = 0;
+        if (rr < w.n) {
+            const uint8_t byte = w.w[(size_t)rr * w.stride + (size_t)b * 64 + piece_of_chunk(ch) * 16 + j];
+            v = ((byte >> (2 * l)) & 3) * (1 << w.shift) - w.off;
+        }
+        dst[tc_tile_off(r, g16 * 16 + j, kTcN)] = (int8_t)v;
+    }
+    if (g16 == 0) tws[((size_t)tile * nb + b) * kTcN + r] = rr < w.n ? w.s[(size_t)rr * nb + b] : 0.f;
+}
+
+// Activation rows -> Q8_K, written as tiled int8 codes plus block scales.
+// One CTA (kGemvThreads) per token; the fp32 row is built by stage_fp32 (the
+// GEMV prologues: as is, RMSNorm*w, SiLU*up) and each 256 block quantised by
+// one warp with quantize_block_warp's arithmetic (bit-identical codes).
+// Tokens past T (padding of the last tile) get zero codes.
+__global__ void __launch_bounds__(kGemvThreads) tc_quantize(const __grid_constant__ GemvArgs a, int T, int8_t *ta,
+                                                             float *ad) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int K = a.k, nb = K / 256, t = blockIdx.x;
+    float *x = (float *)smem;
+    float *red = x + K;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int mt = t / kTcM, r = t % kTcM;
+    if (t >= T) {
+        for (int b = warp; b < nb; b += kGemvThreads / 32) {
+            int8_t *dst = ta + ((size_t)mt * nb + b) * kTcABytes + tc_tile_off(r, lane * 8, kTcM);
+            *(uint2 *)dst = make_uint2(0, 0);
+            if (lane == 0) ad[(size_t)t * nb + b] = 0.f;
+        }
+        return;
+    }
+    stage_fp32<kStageVec>(a, t, x, red, K);
+    __syncthreads();
+    for (int b = warp; b < nb; b += kGemvThreads / 32) {
+        const float *p = x + b * 256 + lane * 8;
+        const float4 v0 = *(const float4 *)&p[0], v1 = *(const float4 *)&p[4];
+        const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        float ba = 0.f, lv = 0.f;
+        int li = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float av = fabsf(v[j]);
+            if (av > ba) { ba = av; lv = v[j]; li = lane * 8 + j; }
+        }
+        const unsigned mbits = __reduce_max_sync(0xffffffffu, __float_as_uint(ba));
+        const unsigned cand = (__float_as_uint(ba) == mbits) ? (unsigned)li : 0x7fffffffu;
+        const int bi = (int)__reduce_min_sync(0xffffffffu, cand);
+        ba = __uint_as_float(mbits);
+        const float bv = __shfl_sync(0xffffffffu, lv, (bi >> 3) & 31);
+        int q[8];
+        float d = 0.f;
+        if (ba == 0.f) {
+#pragma unroll
+            for (int j = 0; j < 8; j++) q[j] = 0;
+        } else {
+            const float iscale = -127.f / bv;
+            d = 1.f / iscale;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const float f = __fmul_rn(iscale, v[j]);
+                int rr = isfinite(f) ? __float2int_rn(f) : 0;
+                q[j] = rr > 127 ? 127 : (rr < -127 ? -127 : rr);
+            }
+        }
+        const uint32_t lo = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
+        const uint32_t hi = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
+        *(uint2 *)(ta + ((size_t)mt * nb + b) * kTcABytes + tc_tile_off(r, lane * 8, kTcM)) = make_uint2(lo, hi);
+        if (lane == 0) ad[(size_t)t * nb + b] = d;
+    }
+}
+
+}  // namespace hyk

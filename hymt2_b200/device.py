@@ -134,6 +134,19 @@ class Backend:
             raise BackendError("gemv_test: " + self.error())
         return out
 
+    def tc_test(self, h: int, act: int, x, rows: int, x2=None, norm_w=None, eps: float = 1e-5) -> np.ndarray:
+        """One panel weight through the tensor-core GEMM path (hyc_tc_test)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        nt = x.shape[0]
+        out = np.zeros((nt, rows), dtype=np.float32)
+        x2p = None if x2 is None else np.ascontiguousarray(x2, dtype=np.float32)
+        nwp = None if norm_w is None else np.ascontiguousarray(norm_w, dtype=np.float32)
+        rc = self.lib.hyc_tc_test(self.impl, h, act, x.ctypes.data, None if x2p is None else x2p.ctypes.data,
+                                  None if nwp is None else nwp.ctypes.data, eps, nt, out.ctypes.data)
+        if rc != 0:
+            raise BackendError("tc_test: " + self.error())
+        return out
+
     def attention_test(self, heads, kv_heads, hd, ctx, qkv, pos0, kc, vc, q_norm, k_norm, cos, sin, eps=1e-5):
         qkv = np.ascontiguousarray(qkv, dtype=np.float32)
         nt = qkv.shape[0]

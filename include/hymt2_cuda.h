@@ -103,6 +103,16 @@ HYC_API void hyc_host_free(void *p);
  * the next decode steps run the persistent kernel, 0 for the graph, and
  * writes the reason. */
 HYC_API int hyc_set_decode_mode(void *impl, int mode);
+/* Tensor-core path for multi-token chunks (no reference counterpart; it
+ * serves the same forward_batch chunks, src/model.c:798-909): with on != 0
+ * (the default) chunks of >= 32 tokens over panel (STQ1_0 / Q2_0C) weights
+ * run the tcgen05 int8 GEMM with TMEM accumulators; 0 keeps the dp4a GEMV
+ * kernels.  hyc_tc_test runs one panel weight through that GEMM on host
+ * inputs (act as hyc_gemv_test: 1 plain, 2 RMSNorm*w, 3 SiLU(x)*x2; nt 1..256)
+ * and writes out[t*n + r]. */
+HYC_API int hyc_set_tc(void *impl, int on);
+HYC_API int hyc_tc_test(void *impl, hy_dweight *w, int act, const float *x, const float *x2, const float *norm_w,
+                        float eps, int nt, float *out);
 HYC_API int hyc_decode_path(void *impl, char *why, int cap);
 
 /* ---- kernel-level hooks for parity tests (host buffers, synchronous) -- */

@@ -1,0 +1,77 @@
+"""The tcgen05 int8 tensor-core GEMM that multi-token chunks over panel
+weights use (needs a B200), through the C ABI.
+
+  - one panel weight (STQ1_0, Q2_0C) on 1..200 tokens with each activation
+    prologue (plain, RMSNorm*w, SiLU*up): against the oracle's host sequence
+    (Q8_K quantiser, panel rows; reference src/kernels.c:128-165, 565-581)
+    within 1e-4 relative, and against the dp4a GEMV on the same inputs
+    (same block integers, fp32 sums in another order) within 1e-5;
+  - whole prompts: a 150-token prefill through the tensor-core chunks gives
+    the logits of the GEMV chunks (1e-4) and of the oracle (the reference's
+    spread rule), and the same greedy ids.
+"""
+import numpy as np
+import pytest
+
+from conftest import rand_act, rand_blocks
+
+pytestmark = pytest.mark.gpu
+
+TYPES = {"STQ1_0": 43, "Q2_0C": 40}
+
+
+@pytest.mark.parametrize("name", list(TYPES))
+@pytest.mark.parametrize("act", [1, 2, 3])
+@pytest.mark.parametrize("k,rows", [(512, 48), (2048, 300), (6144, 512)])
+@pytest.mark.parametrize("nt", [1, 37, 128, 200])
+def test_tc_gemm(backend, oracle, name, act, k, rows, nt):
+    from hymt2_b200.device import weight_from_bytes
+    gt = TYPES[name]
+    rng = np.random.default_rng(k + act * 7 + nt + rows)
+    raw = rand_blocks(rng, gt, rows, k)
+    h = backend.upload(weight_from_bytes(gt, raw, rows, k))
+    try:
+        x = rand_act(rng, nt, k) * 3.0
+        x2 = rand_act(rng, nt, k)
+        nw = (1.0 + 0.2 * rng.standard_normal(k)).astype(np.float32)
+        kw = dict(x2=x2 if act == 3 else None, norm_w=nw if act == 2 else None)
+        got = backend.tc_test(h, act, x, rows, **kw)
+        w = oracle.weight(gt, raw, rows, k, panel=True)
+        want = oracle.prologue_matmul(w, act, x, x2 if act == 3 else None, nw if act == 2 else None)
+        scale = max(np.abs(want).max(), 1e-6)
+        assert np.abs(got - want).max() / scale < 1e-4
+        gemv = backend.gemv_test(h, act, x, rows, **kw)
+        assert np.abs(got - gemv).max() / scale < 1e-5
+    finally:
+        backend.release(h)
+
+
+@pytest.mark.parametrize("cfg", ["t_stq", "t_q2c"])
+def test_tc_prefill(backend, oracle, synth, model_dir, cfg):
+    import np_forward
+    import oracle as O
+    from hymt2_b200.device import DeviceModel
+    path = synth.ensure(cfg, model_dir)
+    dm = DeviceModel(path, backend, ctx=512)
+    om = O.OracleModel(oracle, path, ctx=512)
+    lib, impl = backend.lib, backend.impl
+    try:
+        ids = np.random.default_rng(44).integers(0, dm.vocab_out, 150).tolist()
+        _, spread, tol = np_forward.spread_tolerance(oracle, path, ids)
+        assert lib.hyc_set_tc(impl, 0) == 0
+        _, lg_gemv = dm.forward(ids, 0)
+        assert lib.hyc_set_tc(impl, 1) == 0
+        _, lg_tc = dm.forward(ids, 0)
+        _, lg_o = om.forward(ids, 0)
+        scale = np.abs(lg_o).max()
+        assert np.abs(lg_tc - lg_gemv).max() / scale < 1e-4
+        assert np.abs(lg_tc - lg_o).max() / scale <= tol
+        dm.cache = []
+        got = dm.generate(ids, 8)
+        om.reset()
+        want, steps = om.greedy(ids, 8, chunk=16, step_logits=True)
+        assert got == want or np.abs(np.sort(steps[0])[-1] - np.sort(steps[0])[-2]) <= 2 * tol * np.abs(steps[0]).max()
+    finally:
+        lib.hyc_set_tc(impl, 1)
+        dm.close()
+        om.close()
