@@ -5,7 +5,8 @@ weights use (needs a B200), through the C ABI.
     prologue (plain, RMSNorm*w, SiLU*up): against the oracle's host sequence
     (Q8_K quantiser, panel rows; reference src/kernels.c:128-165, 565-581)
     within 1e-4 relative, and against the dp4a GEMV on the same inputs
-    (same block integers, fp32 sums in another order) within 1e-5;
+    (same block integers, fp32 sums in another order) within 1e-5 where the
+    GEMV hook takes the token count (<= 16);
   - whole prompts: a 150-token prefill through the tensor-core chunks gives
     the logits of the GEMV chunks (1e-4) and of the oracle (the reference's
     spread rule), and the same greedy ids.
@@ -40,8 +41,9 @@ def test_tc_gemm(backend, oracle, name, act, k, rows, nt):
         want = oracle.prologue_matmul(w, act, x, x2 if act == 3 else None, nw if act == 2 else None)
         scale = max(np.abs(want).max(), 1e-6)
         assert np.abs(got - want).max() / scale < 1e-4
-        gemv = backend.gemv_test(h, act, x, rows, **kw)
-        assert np.abs(got - gemv).max() / scale < 1e-5
+        if nt <= 16:  # the GEMV test hook takes the reference's MAX_BATCH tokens
+            gemv = backend.gemv_test(h, act, x, rows, **kw)
+            assert np.abs(got - gemv).max() / scale < 1e-5
     finally:
         backend.release(h)
 
