@@ -58,6 +58,11 @@ class DeviceOps(C.Structure):
                 ("fused_forward", FORWARD)]
 
 
+class ServeStats(C.Structure):
+    _fields_ = [("steps", C.c_longlong), ("decode_tokens", C.c_longlong), ("prefill_tokens", C.c_longlong),
+                ("prefix_hits", C.c_longlong), ("prefix_tokens", C.c_longlong), ("generated", C.c_longlong)]
+
+
 # Every symbol include/hymt2_cuda.h declares, with its ctypes signature.
 P, I, F, Z = C.c_void_p, C.c_int, C.c_float, C.c_size_t
 SIGNATURES = {
@@ -81,6 +86,11 @@ SIGNATURES = {
     "hyc_set_tc": (I, [P, I]),
     "hyc_tc_test": (I, [P, P, I, P, P, P, F, I, P]),
     "hyc_decode_path": (I, [P, C.c_char_p, I]),
+    "hyc_batch_prepare": (I, [P, I, I, I, I]),
+    "hyc_batch_forward": (I, [P, P, P, P, I, P, I, I, P, P]),
+    "hyc_batch_kv_copy": (I, [P, I, I, I]),
+    "hyc_batch_kv_read": (I, [P, I, I, I, P, P]),
+    "hyc_serve": (I, [P, P, P, I, I, I, I, P, C.POINTER(ServeStats)]),
     "hyc_mega_timeline": (I, [P, P, I]),
     "hyc_quantize_q8k": (I, [P, P, I, I, P]),
     "hyc_block_ints": (I, [P, P, P, I, P]),

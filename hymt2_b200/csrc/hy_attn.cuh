@@ -30,7 +30,18 @@ struct AttnArgs {
     unsigned long long *tpart;  // if set: partials as tagged words (float bits | ptag << 32) instead
     unsigned ptag;
     int trace;              // timeline slot (< 0: off)
+    // ragged batch of several sequences (prefill kernels only): token t sits
+    // at position tok_pos[t] of sequence slot tok_slot[t], whose cache starts
+    // slot_stride elements after the previous slot's (kc/vc: slot 0)
+    const int *tok_pos, *tok_slot;
+    long long slot_stride;
 };
+
+// Position of token t and the element offset of its sequence's cache.
+__device__ __forceinline__ int attn_tok_pos(const AttnArgs &a, int t) { return a.tok_pos ? a.tok_pos[t] : *a.pos_ptr + t; }
+__device__ __forceinline__ long long attn_tok_kv(const AttnArgs &a, int t) {
+    return a.tok_slot ? (long long)a.tok_slot[t] * a.slot_stride : 0;
+}
 
 // NeoX rotation + per-head RMSNorm of one head held as v[i] = x[lane + 32 i].
 template <int HD>
@@ -63,7 +74,8 @@ __global__ void rope_norm_store(const __grid_constant__ AttnArgs a) {
     pdl_trigger();
     pdl_wait();
     const int t = blockIdx.x, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pos = *a.pos_ptr + t;
+    const int pos = attn_tok_pos(a, t);
+    const long long kvo = attn_tok_kv(a, t);
     const float *cs = a.rope_cos + (size_t)pos * a.half, *sn = a.rope_sin + (size_t)pos * a.half;
     float *row = a.qkv + (size_t)t * a.qkv_ld;
     for (int hh = w; hh < a.heads + a.kv_heads; hh += blockDim.x >> 5) {
@@ -79,7 +91,8 @@ __global__ void rope_norm_store(const __grid_constant__ AttnArgs a) {
         } else {
             const int kvh = hh - a.heads;
             const float *vs = row + a.qdim + a.kvdim + kvh * HD;
-            uint16_t *kd = a.kc + (size_t)pos * a.kvdim + kvh * HD, *vd = a.vc + (size_t)pos * a.kvdim + kvh * HD;
+            uint16_t *kd = a.kc + kvo + (size_t)pos * a.kvdim + kvh * HD,
+                     *vd = a.vc + kvo + (size_t)pos * a.kvdim + kvh * HD;
 #pragma unroll
             for (int i = 0; i < HD / 32; i++) {
                 kd[lane + 32 * i] = f32_to_bf16_bits(v[i]);
@@ -93,9 +106,9 @@ __global__ void rope_norm_store(const __grid_constant__ AttnArgs a) {
 // KV head kvh, query rows in sq[G][HD].  Key `cur` (if >= 0) is taken from
 // sk/sv (values already bf16-rounded) instead of the cache.
 template <int HD, int G>
-__device__ __forceinline__ void attend_range(const AttnArgs &a, int kvh, int j0, int j1, int cur, const float (*sq)[HD],
-                                             const float *sk, const float *sv, float (&m)[G], float (&l)[G],
-                                             float (&o)[G][HD / 32]) {
+__device__ __forceinline__ void attend_range(const AttnArgs &a, const uint16_t *kc, const uint16_t *vc, int kvh, int j0,
+                                             int j1, int cur, const float (*sq)[HD], const float *sk, const float *sv,
+                                             float (&m)[G], float (&l)[G], float (&o)[G][HD / 32]) {
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
     for (int h = 0; h < G; h++) {
@@ -104,7 +117,7 @@ __device__ __forceinline__ void attend_range(const AttnArgs &a, int kvh, int j0,
 #pragma unroll
         for (int i = 0; i < HD / 32; i++) o[h][i] = 0.f;
     }
-    const uint16_t *Kb = a.kc + kvh * HD, *Vb = a.vc + kvh * HD;
+    const uint16_t *Kb = kc + kvh * HD, *Vb = vc + kvh * HD;
     for (int tile = j0 + w * 32; tile < j1; tile += G * 32) {
         const int j = tile + lane;
         const bool valid = j < j1;
@@ -916,13 +929,14 @@ __global__ void __launch_bounds__(G * 32) attn_prefill(const __grid_constant__ A
     const int kvh = blockIdx.x, t = blockIdx.y;
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_wait();
-    const int pos = *a.pos_ptr + t;
+    const int pos = attn_tok_pos(a, t);
+    const long long kvo = attn_tok_kv(a, t);
     const float *qr = a.qkv + (size_t)t * a.qkv_ld + (kvh * G + w) * HD;
 #pragma unroll
     for (int i = 0; i < HD / 32; i++) S.sq[w][lane + 32 * i] = qr[lane + 32 * i];
     __syncthreads();
     float m[G], l[G], o[G][HD / 32];
-    attend_range<HD, G>(a, kvh, 0, pos + 1, -1, S.sq, S.sk, S.sv, m, l, o);
+    attend_range<HD, G>(a, a.kc + kvo, a.vc + kvo, kvh, 0, pos + 1, -1, S.sq, S.sk, S.sv, m, l, o);
 #pragma unroll
     for (int h = 0; h < G; h++) {
         if (lane == 0) {

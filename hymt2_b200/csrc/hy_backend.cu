@@ -63,6 +63,8 @@ struct Graph {
     long long kernels = 0;
 };
 
+struct Batch;
+
 struct HyCtx {
     int dev = 0;
     cudaStream_t st = nullptr;
@@ -116,13 +118,15 @@ struct HyCtx {
     MegaPlan mega_plan_v{};
     // tensor-core path for multi-token chunks (hy_tc.cuh)
     bool tc_on = true;
-    int8_t *d_tca = nullptr;        // tiled Q8_K codes of up to kMaxChunk tokens
+    int max_tokens = kMaxChunk;     // tokens per forward pass (the batch engine raises it)
+    int8_t *d_tca = nullptr;        // tiled Q8_K codes of up to max_tokens tokens
     float *d_tcad = nullptr;        // their block scales
     int *d_tcerr = nullptr;         // set by tc_gemm on a bounded-wait timeout
     size_t tca_bytes = 0;
     int head_keep = 0;              // head rows per CTA kept resident in L2 by the persistent kernel
     size_t l2_bytes = 0;
     void *mega_kernel = nullptr;
+    Batch *bat = nullptr;           // ragged multi-sequence batches (hy_batch.cuh)
 };
 
 int trace_slot(HyCtx *c) { return c->trace_on && c->trace_next < kTraceSlots ? c->trace_next++ : -1; }
@@ -253,7 +257,9 @@ void init_kernel_attrs() {
     set_smem(attn_chunk_kernel<64, 2>);
     set_smem(attn_chunk_kernel<64, 4>);
     set_smem(attn_chunk_kernel<64, 8>);
-    set_smem(tc_gemm);
+    set_smem(tc_gemm<1>);
+    set_smem(tc_gemm<2>);
+    set_smem(tc_gemm<3>);
 }
 
 // One launch for nt <= NT tokens.
@@ -368,26 +374,33 @@ bool run_multi(HyCtx *c, HyWeight *const *ws, float *const *outs, const int *lds
 constexpr int kTcMinTokens = 32;  // chunks at least this long use the tensor-core GEMM
 
 bool tc_usable(HyCtx *c, int nt, HyWeight *const *ws, int cnt) {
-    if (!c->tc_on || nt < kTcMinTokens || nt > kMaxChunk) return false;
+    if (!c->tc_on || nt < kTcMinTokens || nt > c->max_tokens) return false;
     for (int i = 0; i < cnt; i++)
-        if (ws[i]->fmt != FMT_PANEL || ws[i]->k % 256) return false;
+        if (!tc_planes(ws[i]->fmt) || ws[i]->k % 256) return false;
     return true;
 }
 
-// Tensor-core tiles of a panel weight, built on first use.
+// Tensor-core planes and scales of a weight, built on first use.
 bool tc_weight(HyCtx *c, HyWeight *w) {
     if (w->tc_w) return true;
-    const int ntiles = (w->n + kTcN - 1) / kTcN;
-    CK(c, cudaMalloc(&w->tc_w, (size_t)ntiles * w->nb * kTcBBytes));
-    CK(c, cudaMalloc(&w->tc_ws, (size_t)ntiles * w->nb * kTcN * 4));
-    const long long total = (long long)ntiles * kTcN * w->nb * 16;
-    tc_panel_to_tiled<<<(unsigned)((total + 255) / 256), 256, 0, c->st>>>(desc(w, nullptr, 0), w->tc_w, w->tc_ws);
+    const int P = tc_planes(w->fmt), N = tc_n(P);
+    REQ(c, P > 0, "weight format has no tensor-core form");
+    const int ntiles = (w->n + N - 1) / N;
+    CK(c, cudaMalloc(&w->tc_w, (size_t)ntiles * w->nb * tc_bbytes(P)));
+    CK(c, cudaMalloc(&w->tc_ws, (size_t)ntiles * w->nb * tc_sbytes(P)));
+    const long long total = (long long)ntiles * N * w->nb * 16;
+    const unsigned grid = (unsigned)((total + 255) / 256);
+    const WDesc d = desc(w, nullptr, 0);
+    if (P == 1) tc_weight_to_tiled<1><<<grid, 256, 0, c->st>>>(d, w->tc_w, w->tc_ws);
+    else if (P == 2) tc_weight_to_tiled<2><<<grid, 256, 0, c->st>>>(d, w->tc_w, w->tc_ws);
+    else tc_weight_to_tiled<3><<<grid, 256, 0, c->st>>>(d, w->tc_w, w->tc_ws);
     CK(c, cudaGetLastError());
     return true;
 }
 
 bool tc_scratch(HyCtx *c, int K) {
-    const size_t nbmax = (size_t)(K / 256), bytes = (size_t)(kMaxChunk / kTcM) * nbmax * kTcABytes;
+    const size_t nbmax = (size_t)(K / 256), tmax = (size_t)(c->max_tokens + kTcM - 1) / kTcM * kTcM;
+    const size_t bytes = tmax * nbmax * kTcKB;
     if (bytes <= c->tca_bytes) return true;
     if (c->d_tca) cudaFree(c->d_tca);
     if (c->d_tcad) cudaFree(c->d_tcad);
@@ -395,7 +408,7 @@ bool tc_scratch(HyCtx *c, int K) {
     c->d_tcad = nullptr;
     c->tca_bytes = 0;
     CK(c, cudaMalloc(&c->d_tca, bytes));
-    CK(c, cudaMalloc(&c->d_tcad, (size_t)kMaxChunk * nbmax * 4));
+    CK(c, cudaMalloc(&c->d_tcad, tmax * nbmax * 4));
     if (!c->d_tcerr) {
         CK(c, cudaMalloc(&c->d_tcerr, 4));
         CK(c, cudaMemsetAsync(c->d_tcerr, 0, 4, c->st));
@@ -404,7 +417,7 @@ bool tc_scratch(HyCtx *c, int K) {
     return true;
 }
 
-// nt tokens through up to three panel weights sharing one activation
+// nt tokens through up to three weights sharing one activation
 // prologue (pro.act / x / x2 / norm_w / eps, pro.k = K): one quantise launch
 // writing tiled Q8_K codes, then one tensor-core GEMM per weight; outs[i] is
 // [nt][lds[i]], stored (epi 0) or accumulated (epi 1).
@@ -430,9 +443,13 @@ bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float
         ta.nb = nb;
         ta.epi = epi;
         ta.err = c->d_tcerr;
-        if (!launch(c, tc_gemm, dim3(tpad / kTcM, (ws[i]->n + kTcN - 1) / kTcN), dim3(kTcThreads), tc_smem_bytes(),
-                    false, ta))
-            return false;
+        const int P = tc_planes(ws[i]->fmt);
+        const dim3 grid(tpad / kTcM, (ws[i]->n + tc_n(P) - 1) / tc_n(P));
+        bool ok;
+        if (P == 1) ok = launch(c, tc_gemm<1>, grid, dim3(kTcThreads), tc_smem_bytes(1), false, ta);
+        else if (P == 2) ok = launch(c, tc_gemm<2>, grid, dim3(kTcThreads), tc_smem_bytes(2), false, ta);
+        else ok = launch(c, tc_gemm<3>, grid, dim3(kTcThreads), tc_smem_bytes(3), false, ta);
+        if (!ok) return false;
     }
     return true;
 }
@@ -453,14 +470,14 @@ bool tc_status(HyCtx *c) {
 
 template <int HD, int G>
 bool attn_launch(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
-    if (nt == 1 && aa.cpart && attn_chunk_len(aa.ctx - 1, aa.kv_heads, aa.units) > 0) {
+    if (nt == 1 && !aa.tok_pos && aa.cpart && attn_chunk_len(aa.ctx - 1, aa.kv_heads, aa.units) > 0) {
         // wide decode attention: units of (KV head, key chunk), then the per-head merge
         if (!launch(c, attn_chunk_kernel<HD, G>, dim3(aa.kv_heads, aa.max_chunks), dim3(kDecWarps * 32),
                     attn_chunk_smem<HD>(), pdl, aa))
             return false;
         return launch(c, attn_merge_kernel<HD>, dim3(aa.heads), dim3(32), 0, pdl, aa);
     }
-    if (nt == 1)
+    if (nt == 1 && !aa.tok_pos)
         return launch(c, attn_decode2<HD, G>, dim3(aa.kv_heads, aa.max_splits), dim3(kDecWarps * 32), attn_dec_smem<HD>(),
                       pdl, aa);
     int warps = aa.heads + aa.kv_heads;
@@ -491,10 +508,38 @@ bool ffn_pair_ok(const Layer &L, int nt) {
            L.g->shift == L.u->shift && L.g->off == L.u->off;
 }
 
-bool gateup_forward(HyCtx *c, const Layer &L, int nt, bool pdl) {
+// Activation buffers and cache addressing of one forward pass: either the
+// single sequence of the fused ops (token t at *pos_ptr + t of one cache) or
+// a ragged batch (token t at tok_pos[t] of sequence slot tok_slot[t]).
+struct Fwd {
+    float *h, *qkv, *ao, *g, *u;  // [tokens][H | qd + 2 kvd | qd | F | F]
+    uint16_t *kv;                 // layer li's K cache at kv + li * layer_stride, V kv_ctx rows later
+    size_t layer_stride;
+    long long slot_stride;        // elements between two slots' caches (batch)
+    int kv_ctx;
+    const int *pos_ptr;
+    const int *tok_pos, *tok_slot;
+};
+
+Fwd fwd_single(HyCtx *c, const int *pos_ptr) {
+    Fwd f;
+    memset(&f, 0, sizeof f);
+    f.h = c->d_h;
+    f.qkv = c->d_qkv;
+    f.ao = c->d_ao;
+    f.g = c->d_g;
+    f.u = c->d_u;
+    f.kv = c->d_kv;
+    f.layer_stride = (size_t)2 * c->ctx * c->kvd;
+    f.kv_ctx = c->ctx;
+    f.pos_ptr = pos_ptr;
+    return f;
+}
+
+bool gateup_forward(HyCtx *c, const Fwd &f, const Layer &L, int nt, bool pdl) {
     GemvArgs a = gemv_args(nt, c->H);
     a.act = ACT_NORM;
-    a.x = c->d_h;
+    a.x = f.h;
     a.ldx = c->H;
     a.norm_w = L.ffn_norm;
     a.eps = c->eps;
@@ -503,27 +548,27 @@ bool gateup_forward(HyCtx *c, const Layer &L, int nt, bool pdl) {
         a.nw = 2;
         a.interleave = 1;
         a.rows_total = 2 * L.g->n;
-        a.w[0] = desc(L.g, c->d_g, c->F);
+        a.w[0] = desc(L.g, f.g, c->F);
         a.w[1] = desc(L.u, nullptr, c->F);
         return run_gemv(c, a, pdl);
     }
     HyWeight *ws[2] = {L.g, L.u};
-    float *outs[2] = {c->d_g, c->d_u};
+    float *outs[2] = {f.g, f.u};
     const int lds[2] = {c->F, c->F};
     if (tc_usable(c, nt, ws, 2)) return tc_linear(c, a, nt, ws, outs, lds, 2, 0);
     a.epi = EPI_STORE;
     return run_multi(c, ws, outs, lds, 2, a, pdl);
 }
 
-bool down_forward(HyCtx *c, const Layer &L, int nt, bool pdl, float *dst) {
+bool down_forward(HyCtx *c, const Fwd &f, const Layer &L, int nt, bool pdl, float *dst) {
     GemvArgs a = gemv_args(nt, c->F);
     if (ffn_pair_ok(L, nt)) {
-        a.act = ACT_VEC;  // d_g already holds silu(gate)*up
-        a.x = c->d_g;
+        a.act = ACT_VEC;  // g already holds silu(gate)*up
+        a.x = f.g;
     } else {
         a.act = ACT_SILU;
-        a.x = c->d_g;
-        a.x2 = c->d_u;
+        a.x = f.g;
+        a.x2 = f.u;
     }
     a.ldx = c->F;
     {
@@ -539,20 +584,20 @@ bool down_forward(HyCtx *c, const Layer &L, int nt, bool pdl, float *dst) {
     return run_gemv(c, a, pdl);
 }
 
-bool ffn_forward(HyCtx *c, const Layer &L, int nt, bool pdl) {
-    return gateup_forward(c, L, nt, pdl) && down_forward(c, L, nt, pdl, c->d_h);
+bool ffn_forward(HyCtx *c, const Fwd &f, const Layer &L, int nt, bool pdl) {
+    return gateup_forward(c, f, L, nt, pdl) && down_forward(c, f, L, nt, pdl, f.h);
 }
 
-bool layer_forward(HyCtx *c, int li, int nt, const int *pos_ptr, bool pdl) {
+bool layer_forward(HyCtx *c, const Fwd &f, int li, int nt, bool pdl) {
     const Layer &L = c->layers[li];
     const int qkv_ld = c->qd + 2 * c->kvd;
     {
         HyWeight *ws[3] = {L.q, L.k, L.v};
-        float *outs[3] = {c->d_qkv, c->d_qkv + c->qd, c->d_qkv + c->qd + c->kvd};
+        float *outs[3] = {f.qkv, f.qkv + c->qd, f.qkv + c->qd + c->kvd};
         const int lds[3] = {qkv_ld, qkv_ld, qkv_ld};
         GemvArgs a = gemv_args(nt, c->H);
         a.act = ACT_NORM;
-        a.x = c->d_h;
+        a.x = f.h;
         a.ldx = c->H;
         a.norm_w = L.attn_norm;
         a.eps = c->eps;
@@ -566,26 +611,29 @@ bool layer_forward(HyCtx *c, int li, int nt, const int *pos_ptr, bool pdl) {
     {
         AttnArgs aa;
         memset(&aa, 0, sizeof aa);
-        aa.qkv = c->d_qkv;
+        aa.qkv = f.qkv;
         aa.qkv_ld = qkv_ld;
-        aa.kc = c->d_kv + (size_t)li * 2 * c->ctx * c->kvd;
-        aa.vc = aa.kc + (size_t)c->ctx * c->kvd;
+        aa.kc = f.kv + (size_t)li * f.layer_stride;
+        aa.vc = aa.kc + (size_t)f.kv_ctx * c->kvd;
         aa.q_norm = L.q_norm;
         aa.k_norm = L.k_norm;
         aa.rope_cos = c->d_cos;
         aa.rope_sin = c->d_sin;
-        aa.pos_ptr = pos_ptr;
+        aa.pos_ptr = f.pos_ptr;
+        aa.tok_pos = f.tok_pos;
+        aa.tok_slot = f.tok_slot;
+        aa.slot_stride = f.slot_stride;
         aa.nt = nt;
         aa.heads = c->heads;
         aa.kv_heads = c->kvh;
         aa.hd = c->hd;
         aa.kvdim = c->kvd;
         aa.qdim = c->qd;
-        aa.ctx = c->ctx;
+        aa.ctx = f.kv_ctx;
         aa.half = c->half;
         aa.eps = c->eps;
         aa.scale = 1.0f / sqrtf((float)c->hd);
-        aa.ao = c->d_ao;
+        aa.ao = f.ao;
         aa.part = c->d_part;
         aa.cpart = c->d_cpart;
         aa.max_chunks = c->max_chunks;
@@ -598,10 +646,10 @@ bool layer_forward(HyCtx *c, int li, int nt, const int *pos_ptr, bool pdl) {
     {
         GemvArgs a = gemv_args(nt, c->qd);
         a.act = ACT_VEC;
-        a.x = c->d_ao;
+        a.x = f.ao;
         a.ldx = c->qd;
         HyWeight *ws[1] = {L.o};
-        float *outs[1] = {c->d_h};
+        float *outs[1] = {f.h};
         const int lds[1] = {c->H};
         if (tc_usable(c, nt, ws, 1)) {
             if (!tc_linear(c, a, nt, ws, outs, lds, 1, 1)) return false;
@@ -609,11 +657,11 @@ bool layer_forward(HyCtx *c, int li, int nt, const int *pos_ptr, bool pdl) {
             a.epi = EPI_ADD;
             a.nw = 1;
             a.rows_total = L.o->n;
-            a.w[0] = desc(L.o, c->d_h, c->H);
+            a.w[0] = desc(L.o, f.h, c->H);
             if (!run_gemv(c, a, pdl)) return false;
         }
     }
-    return ffn_forward(c, L, nt, pdl);
+    return ffn_forward(c, f, L, nt, pdl);
 }
 
 // LM head on one token's residual x (RMSNorm with out_norm first).
@@ -638,10 +686,14 @@ bool head_forward(HyCtx *c, const float *x, bool store_logits, bool argmax, bool
     return run_gemv(c, a, pdl, 2);
 }
 
-bool layers_forward(HyCtx *c, int nt, const int *pos_ptr, bool pdl) {
+bool layers_forward(HyCtx *c, const Fwd &f, int nt, bool pdl) {
     for (int li = 0; li < c->L; li++)
-        if (!layer_forward(c, li, nt, pos_ptr, pdl)) return false;
+        if (!layer_forward(c, f, li, nt, pdl)) return false;
     return true;
+}
+
+bool layers_forward(HyCtx *c, int nt, const int *pos_ptr, bool pdl) {
+    return layers_forward(c, fwd_single(c, pos_ptr), nt, pdl);
 }
 
 // ---------------------------------------------------------------- graphs
@@ -929,7 +981,10 @@ __global__ void __launch_bounds__(kGemvThreads) quantize_export(const __grid_con
 
 // ---------------------------------------------------------------- vtable ops
 
+void batch_free(HyCtx *c);
+
 void free_fused(HyCtx *c) {
+    batch_free(c);
     graph_reset(c->g_fwd1);
     graph_reset(c->g_fwd1_logits);
     graph_reset(c->g_dec);
@@ -1293,6 +1348,8 @@ bool fused_forward(void *impl, hy_fused_args *a) {
     return tc_status(c);
 }
 
+#include "hy_batch.cuh"
+
 const hy_device_ops kOps = {destroy_impl, upload, release, matmul, is_software, weight_out, fused_prepare,
                             fused_forward};
 
@@ -1404,7 +1461,7 @@ HYC_API int hyc_tc_test(void *impl, hy_dweight *hw, int act, const float *x, con
                         float eps, int nt, float *out) {
     HyCtx *c = (HyCtx *)impl;
     HyWeight *w = (HyWeight *)hw;
-    if (!c || c->broken || !w || w->fmt != FMT_PANEL || nt < 1 || nt > kMaxChunk || act < ACT_VEC || act > ACT_SILU ||
+    if (!c || c->broken || !w || !tc_planes(w->fmt) || nt < 1 || nt > kMaxChunk || act < ACT_VEC || act > ACT_SILU ||
         (act == ACT_NORM && !norm_w) || (act == ACT_SILU && !x2))
         return -1;
     if (cudaSetDevice(c->dev) != cudaSuccess) return -1;
@@ -1435,6 +1492,79 @@ HYC_API int hyc_tc_test(void *impl, hy_dweight *hw, int act, const float *x, con
     cudaFree(dn);
     cudaFree(dout);
     return ok ? 0 : -1;
+}
+
+HYC_API int hyc_batch_prepare(void *impl, int slots, int slot_ctx, int max_tokens, int max_out) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || cudaSetDevice(c->dev) != cudaSuccess) return -1;
+    return batch_prepare(c, slots, slot_ctx, max_tokens, max_out) ? 0 : -1;
+}
+
+HYC_API int hyc_batch_forward(void *impl, const int *tokens, const int *tok_slot, const int *tok_pos, int nt,
+                              const int *out_rows, int nout, int vocab_out, int *out_ids, float *logits) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->bat || !tokens || !tok_slot || !tok_pos || cudaSetDevice(c->dev) != cudaSuccess)
+        return -1;
+    Batch &b = *c->bat;
+    if (nt < 1 || nt > b.max_tokens || nout < 0 || nout > b.max_out || (nout > 0 && (!out_rows || !out_ids))) return -1;
+    for (int t = 0; t < nt; t++)
+        if (tok_slot[t] < 0 || tok_slot[t] >= b.slots || tok_pos[t] < 0 || tok_pos[t] >= b.slot_ctx) return -1;
+    for (int i = 0; i < nout; i++)
+        if (out_rows[i] < 0 || out_rows[i] >= nt) return -1;
+    const int vo = vocab_out > 0 && vocab_out <= c->outw->n ? vocab_out : c->outw->n;
+    const size_t T = (size_t)b.max_tokens;
+    memcpy(b.h_in, tokens, (size_t)nt * 4);
+    memcpy(b.h_in + T, tok_slot, (size_t)nt * 4);
+    memcpy(b.h_in + 2 * T, tok_pos, (size_t)nt * 4);
+    if (nout > 0) memcpy(b.h_in + 3 * T, out_rows, (size_t)nout * 4);
+    if (!batch_upload(c, nt, nout) || !batch_run(c, nt, nout, vo)) return -1;
+    if (nout > 0) {
+        if (cudaMemcpyAsync(b.h_ids, b.d_ids, (size_t)nout * 4, cudaMemcpyDeviceToHost, c->st) != cudaSuccess) return -1;
+        if (logits && cudaMemcpyAsync(logits, b.logits, (size_t)nout * c->outw->n * 4, cudaMemcpyDeviceToHost, c->st) !=
+                          cudaSuccess)
+            return -1;
+    }
+    if (cudaStreamSynchronize(c->st) != cudaSuccess) {
+        fail(c, "batch_forward", cudaGetLastError());
+        return -1;
+    }
+    if (!tc_status(c)) return -1;
+    if (nout > 0) memcpy(out_ids, b.h_ids, (size_t)nout * 4);
+    return 0;
+}
+
+HYC_API int hyc_batch_kv_copy(void *impl, int src_slot, int dst_slot, int npos) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->bat || cudaSetDevice(c->dev) != cudaSuccess) return -1;
+    const Batch &b = *c->bat;
+    if (src_slot < 0 || src_slot > b.slots || dst_slot < 0 || dst_slot > b.slots || npos < 0 || npos > b.slot_ctx)
+        return -1;
+    return kv_copy(c, src_slot, dst_slot, npos) && cudaStreamSynchronize(c->st) == cudaSuccess ? 0 : -1;
+}
+
+HYC_API int hyc_batch_kv_read(void *impl, int slot, int layer, int npos, uint16_t *k, uint16_t *v) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->bat || !k || !v || cudaSetDevice(c->dev) != cudaSuccess) return -1;
+    const Batch &b = *c->bat;
+    if (slot < 0 || slot > b.slots || layer < 0 || layer >= c->L || npos < 1 || npos > b.slot_ctx) return -1;
+    const uint16_t *kc = b.kv + (size_t)layer * b.layer_stride(c) + (size_t)slot * b.slot_stride(c);
+    const uint16_t *vc = kc + (size_t)b.slot_ctx * c->kvd;
+    if (cudaMemcpyAsync(k, kc, (size_t)npos * c->kvd * 2, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
+        cudaMemcpyAsync(v, vc, (size_t)npos * c->kvd * 2, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
+        cudaStreamSynchronize(c->st) != cudaSuccess)
+        return -1;
+    return 0;
+}
+
+HYC_API int hyc_serve(void *impl, const int *prompts, const int *prompt_off, int nreq, int max_new, int vocab_out,
+                      int step_tokens, int *out_ids, hyc_serve_stats *stats) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->bat || !prompts || !prompt_off || nreq < 0 || !out_ids ||
+        cudaSetDevice(c->dev) != cudaSuccess)
+        return -1;
+    hyc_serve_stats local;
+    const int vo = vocab_out > 0 && vocab_out <= c->outw->n ? vocab_out : c->outw->n;
+    return serve_run(c, prompts, prompt_off, nreq, max_new, vo, step_tokens, out_ids, stats ? stats : &local) ? 0 : -1;
 }
 
 HYC_API int hyc_set_decode_mode(void *impl, int mode) {
@@ -1687,9 +1817,9 @@ HYC_API int hyc_bench_op(void *impl, int op, int iters) {
             a.epi = EPI_STORE;
             ok = run_multi(c, ws, outs, lds, 3, a, true);
         } else if (op == 2) {
-            ok = gateup_forward(c, L, 1, true);
+            ok = gateup_forward(c, fwd_single(c, &c->d_state->pos), L, 1, true);
         } else if (op == 3) {
-            ok = down_forward(c, L, 1, true, c->d_tmp_h());
+            ok = down_forward(c, fwd_single(c, &c->d_state->pos), L, 1, true, c->d_tmp_h());
         } else if (op == 4) {
             GemvArgs a = gemv_args(1, L.o->k);
             a.act = ACT_VEC;

@@ -1,0 +1,330 @@
+// hy_batch.cuh — ragged multi-sequence batches and the continuous-batching
+// server built on them.  Part of hy_backend.cu's translation unit (it uses
+// HyCtx, the layer loop and the tensor-core linear defined there).
+//
+// A batch is a list of tokens, token t at position tok_pos[t] of sequence
+// slot tok_slot[t].  Every slot owns a bf16 KV cache of slot_ctx rows per
+// layer, laid out [L][slots + 1][K | V][slot_ctx][kvdim]; slot `slots` holds
+// the server's shared-prefix cache.  One forward pass embeds every token,
+// runs all layers over the whole batch (tensor-core GEMMs from kTcMinTokens
+// tokens up, so a step of 256 decode tokens or a 32 x 256 prefill is one
+// GEMM per projection), then the LM head over the selected rows with one
+// argmax per row (reference semantics: first maximum wins, src/model.c:945-948).
+//
+// The server (reference gen_ids, src/model.c:914-958, for many requests at
+// once): every step feeds one token of each decoding sequence plus prompt
+// chunks of newly admitted ones, up to a token budget; a request whose
+// prompt shares at least kServeMinPrefix leading tokens with the cached
+// prefix starts from a device copy of those KV rows (the reference's
+// longest-common-prefix reuse, src/model.c:931-936, across requests), and
+// the last prompt token is always recomputed for its logits.
+
+constexpr int kServeMinPrefix = 8;  // shortest shared prefix worth a cache copy
+
+struct Batch {
+    int slots = 0, slot_ctx = 0, max_tokens = 0, max_out = 0;
+    uint16_t *kv = nullptr;
+    float *h = nullptr, *qkv = nullptr, *ao = nullptr, *g = nullptr, *u = nullptr;
+    int *d_in = nullptr;   // tok [max_tokens] | slot [max_tokens] | pos [max_tokens] | rows [max_out]
+    int *h_in = nullptr;   // pinned staging of d_in
+    float *sel = nullptr;  // [max_out][H] residual rows for the head
+    float *logits = nullptr;  // [max_out][vocab]
+    int *d_ids = nullptr, *h_ids = nullptr;
+    size_t kv_elems(const HyCtx *c) const { return (size_t)c->L * (slots + 1) * 2 * slot_ctx * c->kvd; }
+    long long slot_stride(const HyCtx *c) const { return (long long)2 * slot_ctx * c->kvd; }
+    size_t layer_stride(const HyCtx *c) const { return (size_t)(slots + 1) * 2 * slot_ctx * c->kvd; }
+    int *tok() const { return d_in; }
+    int *slot() const { return d_in + max_tokens; }
+    int *pos() const { return d_in + 2 * max_tokens; }
+    int *rows() const { return d_in + 3 * max_tokens; }
+};
+
+// ---------------------------------------------------------------- kernels
+
+// sel[i] = h[rows[i]]
+__global__ void batch_gather(const float *h, int H, const int *rows, float *sel) {
+    const float4 *src = (const float4 *)(h + (size_t)rows[blockIdx.x] * H);
+    float4 *dst = (float4 *)(sel + (size_t)blockIdx.x * H);
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) dst[i] = src[i];
+}
+
+// ids[r] = first index of the maximum of logits[r][0 .. n)
+__global__ void __launch_bounds__(1024) rows_argmax(const float *logits, long long ld, int n, int *ids) {
+    __shared__ unsigned long long red[32];
+    const float *row = logits + (size_t)blockIdx.x * ld;
+    unsigned long long best = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const unsigned long long k = argmax_key(row[i], (uint32_t)i);
+        if (k > best) best = k;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+        if (v > best) best = v;
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) red[w] = best;
+    __syncthreads();
+    if (w == 0) {
+        best = l < (int)(blockDim.x >> 5) ? red[l] : 0ull;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const unsigned long long v = __shfl_xor_sync(0xffffffffu, best, o);
+            if (v > best) best = v;
+        }
+        if (l == 0) ids[blockIdx.x] = best ? (int)argmax_index(best) : 0;
+    }
+}
+
+// Rows [0, npos) of every layer's K and V cache: slot src -> slot dst.
+// grid (layers, 2); 16-byte words.
+__global__ void kv_copy_rows(uint16_t *kv, size_t layer_stride, long long slot_stride, long long v_off, int src, int dst,
+                             long long words) {
+    const size_t base = (size_t)blockIdx.x * layer_stride + (blockIdx.y ? (size_t)v_off : 0);
+    const uint4 *s = (const uint4 *)(kv + base + (size_t)src * slot_stride);
+    uint4 *d = (uint4 *)(kv + base + (size_t)dst * slot_stride);
+    for (long long i = threadIdx.x; i < words; i += blockDim.x) d[i] = s[i];
+}
+
+// ---------------------------------------------------------------- host side
+
+void batch_free(HyCtx *c) {
+    Batch *b = c->bat;
+    if (!b) return;
+    cudaFree(b->kv);
+    cudaFree(b->h);
+    cudaFree(b->qkv);
+    cudaFree(b->ao);
+    cudaFree(b->g);
+    cudaFree(b->u);
+    cudaFree(b->d_in);
+    cudaFree(b->sel);
+    cudaFree(b->logits);
+    cudaFree(b->d_ids);
+    if (b->h_in) cudaFreeHost(b->h_in);
+    if (b->h_ids) cudaFreeHost(b->h_ids);
+    delete b;
+    c->bat = nullptr;
+    c->max_tokens = kMaxChunk;
+}
+
+bool batch_prepare(HyCtx *c, int slots, int slot_ctx, int max_tokens, int max_out) {
+    REQ(c, c->fused && c->embd && c->outw, "model not prepared (fused_prepare, embedding, LM head)");
+    REQ(c, slots >= 1 && slot_ctx >= 1 && slot_ctx <= c->ctx && max_tokens >= 1 && max_out >= 1 &&
+               max_out <= max_tokens,
+        "bad batch geometry (slot_ctx must not exceed the prepared context)");
+    if (c->bat && c->bat->slots == slots && c->bat->slot_ctx == slot_ctx && c->bat->max_tokens == max_tokens &&
+        c->bat->max_out == max_out)
+        return true;
+    batch_free(c);
+    Batch *b = new Batch();
+    c->bat = b;
+    b->slots = slots;
+    b->slot_ctx = slot_ctx;
+    b->max_tokens = max_tokens;
+    b->max_out = max_out;
+    const size_t T = (size_t)max_tokens;
+    CK(c, cudaMalloc(&b->kv, b->kv_elems(c) * 2));
+    CK(c, cudaMemsetAsync(b->kv, 0, b->kv_elems(c) * 2, c->st));
+    CK(c, cudaMalloc(&b->h, T * c->H * 4));
+    CK(c, cudaMalloc(&b->qkv, T * (c->qd + 2 * c->kvd) * 4));
+    CK(c, cudaMalloc(&b->ao, T * c->qd * 4));
+    CK(c, cudaMalloc(&b->g, T * c->F * 4));
+    CK(c, cudaMalloc(&b->u, T * c->F * 4));
+    CK(c, cudaMalloc(&b->d_in, (3 * T + max_out) * 4));
+    CK(c, cudaMallocHost(&b->h_in, (3 * T + max_out) * 4));
+    CK(c, cudaMalloc(&b->sel, (size_t)max_out * c->H * 4));
+    CK(c, cudaMalloc(&b->logits, (size_t)max_out * c->outw->n * 4));
+    CK(c, cudaMalloc(&b->d_ids, (size_t)max_out * 4));
+    CK(c, cudaMallocHost(&b->h_ids, (size_t)max_out * 4));
+    c->max_tokens = max_tokens > kMaxChunk ? max_tokens : kMaxChunk;
+    CK(c, cudaStreamSynchronize(c->st));
+    return true;
+}
+
+Fwd fwd_batch(HyCtx *c) {
+    const Batch &b = *c->bat;
+    Fwd f;
+    memset(&f, 0, sizeof f);
+    f.h = b.h;
+    f.qkv = b.qkv;
+    f.ao = b.ao;
+    f.g = b.g;
+    f.u = b.u;
+    f.kv = b.kv;
+    f.layer_stride = b.layer_stride(c);
+    f.slot_stride = b.slot_stride(c);
+    f.kv_ctx = b.slot_ctx;
+    f.tok_pos = b.pos();
+    f.tok_slot = b.slot();
+    return f;
+}
+
+// Upload nt tokens (tok / slot / pos) and nout head rows from the pinned
+// staging area (filled by the caller at the same offsets as on the device).
+bool batch_upload(HyCtx *c, int nt, int nout) {
+    Batch &b = *c->bat;
+    const size_t T = (size_t)b.max_tokens;
+    for (int part = 0; part < 3; part++)
+        CK(c, cudaMemcpyAsync(b.d_in + part * T, b.h_in + part * T, (size_t)nt * 4, cudaMemcpyHostToDevice, c->st));
+    if (nout > 0)
+        CK(c, cudaMemcpyAsync(b.rows(), b.h_in + 3 * T, (size_t)nout * 4, cudaMemcpyHostToDevice, c->st));
+    return true;
+}
+
+// One forward pass over the uploaded batch; argmax ids of the nout head rows
+// (over the first vocab_out logits) land in b.d_ids, the logits in b.logits.
+bool batch_run(HyCtx *c, int nt, int nout, int vocab_out) {
+    Batch &b = *c->bat;
+    if (!launch(c, embed_rows, dim3(nt), dim3(256), 0, false, desc(c->embd, nullptr, 0), (const int *)b.tok(), b.h, -1))
+        return false;
+    if (!layers_forward(c, fwd_batch(c), nt, false)) return false;
+    if (nout < 1) return true;
+    if (!launch(c, batch_gather, dim3(nout), dim3(128), 0, false, (const float *)b.h, c->H, (const int *)b.rows(),
+                b.sel))
+        return false;
+    HyWeight *ws[1] = {c->outw};
+    float *outs[1] = {b.logits};
+    const int lds[1] = {c->outw->n};
+    GemvArgs a = gemv_args(nout, c->H);
+    a.act = ACT_NORM;
+    a.x = b.sel;
+    a.ldx = c->H;
+    a.norm_w = c->d_out_norm;
+    a.eps = c->eps;
+    if (tc_usable(c, nout, ws, 1)) {
+        if (!tc_linear(c, a, nout, ws, outs, lds, 1, 0)) return false;
+    } else {
+        a.epi = EPI_STORE;
+        a.nw = 1;
+        a.rows_total = c->outw->n;
+        a.w[0] = desc(c->outw, b.logits, c->outw->n);
+        if (!run_gemv(c, a, false, 2)) return false;
+    }
+    return launch(c, rows_argmax, dim3(nout), dim3(1024), 0, false, (const float *)b.logits, (long long)c->outw->n,
+                  vocab_out, b.d_ids);
+}
+
+bool kv_copy(HyCtx *c, int src, int dst, int npos) {
+    Batch &b = *c->bat;
+    const long long words = (long long)npos * c->kvd * 2 / 16;
+    if (words < 1) return true;
+    return launch(c, kv_copy_rows, dim3(c->L, 2), dim3(256), 0, false, b.kv, b.layer_stride(c), b.slot_stride(c),
+                  (long long)b.slot_ctx * c->kvd, src, dst, words);
+}
+
+// ---------------------------------------------------------------- server
+
+struct ServeSeq {
+    int req, slot, n, fed, gen, last;
+};
+
+bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_new, int vocab_out, int step_tokens,
+               int *out, hyc_serve_stats *st) {
+    Batch &b = *c->bat;
+    const int S = b.slots, T = b.max_tokens;
+    REQ(c, step_tokens >= 1 && step_tokens <= T, "step token budget exceeds the batch capacity");
+    REQ(c, max_new >= 1 && b.max_out >= S, "batch head rows must cover every slot");
+    for (int r = 0; r < nreq; r++) {
+        const int n = off[r + 1] - off[r];
+        REQ(c, n >= 1 && n + max_new - 1 <= b.slot_ctx, "request does not fit a slot's context");
+    }
+    std::vector<int> free_slots;
+    for (int s = S - 1; s >= 0; s--) free_slots.push_back(s);
+    std::vector<ServeSeq> act;
+    std::vector<int> ptoks;  // tokens whose KV rows the prefix slot holds
+    int next = 0, done = 0;
+    std::vector<int> row_seq;
+    memset(st, 0, sizeof *st);
+    int *h_tok = b.h_in, *h_slot = b.h_in + T, *h_pos = b.h_in + 2 * T, *h_rows = b.h_in + 3 * T;
+    while (done < nreq) {
+        // admit while there are free slots
+        while (!free_slots.empty() && next < nreq) {
+            ServeSeq q;
+            q.req = next++;
+            q.slot = free_slots.back();
+            free_slots.pop_back();
+            q.n = off[q.req + 1] - off[q.req];
+            q.fed = 0;
+            q.gen = 0;
+            q.last = -1;
+            const int *p = prompts + off[q.req];
+            int l = 0;
+            const int lmax = (int)ptoks.size() < q.n - 1 ? (int)ptoks.size() : q.n - 1;
+            while (l < lmax && p[l] == ptoks[l]) l++;
+            if (l >= kServeMinPrefix) {
+                if (!kv_copy(c, S, q.slot, l)) return false;
+                q.fed = l;
+                st->prefix_hits++;
+                st->prefix_tokens += l;
+            }
+            act.push_back(q);
+        }
+        // one step: a token of every decoding sequence, then prompt chunks
+        int nt = 0, nout = 0;
+        row_seq.clear();
+        for (size_t i = 0; i < act.size(); i++) {
+            ServeSeq &q = act[i];
+            if (q.fed < q.n || nt >= step_tokens) continue;
+            h_tok[nt] = q.last;
+            h_slot[nt] = q.slot;
+            h_pos[nt] = q.n + q.gen - 1;
+            h_rows[nout++] = nt++;
+            row_seq.push_back((int)i);
+            st->decode_tokens++;
+        }
+        for (size_t i = 0; i < act.size() && nt < step_tokens; i++) {
+            ServeSeq &q = act[i];
+            if (q.fed >= q.n) continue;
+            const int *p = prompts + off[q.req];
+            const int take = (q.n - q.fed) < (step_tokens - nt) ? (q.n - q.fed) : (step_tokens - nt);
+            for (int j = 0; j < take; j++) {
+                h_tok[nt] = p[q.fed + j];
+                h_slot[nt] = q.slot;
+                h_pos[nt] = q.fed + j;
+                nt++;
+            }
+            q.fed += take;
+            st->prefill_tokens += take;
+            if (q.fed == q.n) {
+                h_rows[nout++] = nt - 1;
+                row_seq.push_back((int)i);
+            }
+        }
+        REQ(c, nt > 0, "server made no progress");
+        if (!batch_upload(c, nt, nout) || !batch_run(c, nt, nout, vocab_out)) return false;
+        // the first finished prompt becomes the shared-prefix cache
+        if (ptoks.empty())
+            for (size_t i = 0; i < act.size(); i++) {
+                const ServeSeq &q = act[i];
+                if (q.fed == q.n && q.gen == 0 && q.n > kServeMinPrefix) {
+                    if (!kv_copy(c, q.slot, S, q.n - 1)) return false;
+                    ptoks.assign(prompts + off[q.req], prompts + off[q.req] + q.n - 1);
+                    break;
+                }
+            }
+        CK(c, cudaMemcpyAsync(b.h_ids, b.d_ids, (size_t)nout * 4, cudaMemcpyDeviceToHost, c->st));
+        CK(c, cudaStreamSynchronize(c->st));
+        st->steps++;
+        for (int i = 0; i < nout; i++) {
+            ServeSeq &q = act[row_seq[i]];
+            const int id = b.h_ids[i];
+            out[(size_t)q.req * max_new + q.gen] = id;
+            q.gen++;
+            q.last = id;
+        }
+        // retire finished sequences
+        size_t w = 0;
+        for (size_t i = 0; i < act.size(); i++) {
+            if (act[i].fed == act[i].n && act[i].gen >= max_new) {
+                free_slots.push_back(act[i].slot);
+                done++;
+                st->generated += max_new;
+            } else {
+                act[w++] = act[i];
+            }
+        }
+        act.resize(w);
+    }
+    return tc_status(c);
+}

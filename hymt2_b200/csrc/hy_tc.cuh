@@ -1,25 +1,35 @@
 // hy_tc.cuh — int8 tensor-core GEMM for batched prefill / multi-sequence
 // decode on sm_100a: tcgen05.mma kind::i8, accumulators in TMEM.
 //
-// Y[t][n] = sum_b ad[t][b] * ws[n][b] * S_b[t][n],  S_b = sum_{k in block b} A[t][k] W[n][k]
-// with A the Q8_K codes of the activations (per-256-block scale ad) and W the
-// weight as small integers (per-256-block scale ws).  For panel weights
-// (STQ1_0 / Q2_0C) W = code * 2^shift - off is exactly the value the panel
-// GEMV multiplies (reference src/kernels.c:565-581), so every S_b is the
-// reference's per-block integer; the blocks are combined in fp32.
+// Y[t][n] = sum_b ad[t][b] * (ws1[n][b] * S1_b[t][n] - ws2[n][b] * S2_b[t][n])
+// with A the Q8_K codes of the activations (per-256-block scale ad) and the
+// weight held as P int8 planes per 256-block, chosen so that every S is the
+// reference's per-block integer, exactly:
+//   P = 1  panel (STQ1_0 / Q2_0C): W = code * 2^shift - off, the value the
+//          panel GEMV multiplies (reference src/kernels.c:565-581); S1 = A.W,
+//          ws1 = the panel scale.
+//   P = 2  Q6_K: W' = sc_j * (q6 - 32) split as 64 * hi + lo (lo in 0..63);
+//          S1 = 64 * (A.hi) + A.lo = the reference's `acc`
+//          (src/kernels.c:808-835), ws1 = d.
+//   P = 3  Q4_K: W' = sc_j * q4 split the same way gives `sumi`; the third
+//          plane holds the sub-block min m_j at each of its 32 elements, so
+//          S2 = A.m = sum_j m_j * bsum_j is `summ` (src/kernels.c:861-877);
+//          ws1 = d, ws2 = dmin.
+// The blocks are combined in fp32.
 //
 // Operands live in global memory pre-tiled in the UMMA canonical K-major
 // layout without swizzle: a tile of R rows x 256 K is 32 x (R/8) core
 // matrices of 8 rows x 16 bytes; core (row group g, 16-byte k chunk c) sits
 // at (c * R/8 + g) * 128 bytes.  One bulk copy moves a whole tile.
 //
-// CTA = 128 tokens x 256 weight rows; warp 0 streams (A, W, ws) tiles of one
-// K block per stage into a 2-stage ring, warp 1 (one thread) issues 8 MMAs of
-// K = 32 per block into one of two TMEM accumulators (256 columns each), and
-// 16 epilogue warps (4 per TMEM lane quarter, 64 columns each) read the
-// block's int32 results with tcgen05.ld and fold them into fp32 registers
-// while the next block's MMAs run.  Every wait is bounded; TMEM is released
-// on every exit.
+// CTA = 128 tokens x N weight rows (N = 256 / 128 / 64 for P = 1 / 2 / 3, so
+// one accumulator set is at most 256 TMEM columns and two fit): warp 0
+// streams (A, W planes, scales) of one K block per stage into a 2-stage
+// ring, warp 1 (one thread) issues 8 x P MMAs of K = 32 per block into one
+// of two TMEM accumulator sets, and warps 2-17 (4 per TMEM lane
+// quarter, N/4 columns each) read the block's int32 results with
+// tcgen05.ld and fold them into fp32 registers while the next block's MMAs
+// run.  Every wait is bounded; TMEM is released on every exit.
 #pragma once
 #include "hy_common.cuh"
 #include "hy_gemv.cuh"
@@ -27,18 +37,25 @@
 namespace hyk {
 
 constexpr int kTcM = 128;       // tokens per tile (TMEM lanes)
-constexpr int kTcN = 256;       // weight rows per tile (accumulator columns)
 constexpr int kTcKB = 256;      // K per stage: one Q8_K block
 constexpr int kTcStages = 2;
 constexpr int kTcEpiWarps = 16;
-constexpr int kTcThreads = (4 + kTcEpiWarps) * 32;  // warp 0 producer, 1 MMA, 2-3 idle, 4.. epilogue
+constexpr int kTcThreads = (2 + kTcEpiWarps) * 32;  // warp 0 producer, 1 MMA, 2.. epilogue
 constexpr int kTcABytes = kTcM * kTcKB;             // 32 KB
-constexpr int kTcBBytes = kTcN * kTcKB;             // 64 KB
-constexpr int kTcWsBytes = kTcN * 4;                // 1 KB
-constexpr int kTcStageBytes = kTcABytes + kTcBBytes + kTcWsBytes;
 constexpr unsigned long long kTcWaitNs = 2000000000ull;
 
-__host__ __device__ inline size_t tc_smem_bytes() { return (size_t)kTcStages * kTcStageBytes + 1024; }
+// Weight rows per tile for P planes.
+__host__ __device__ constexpr int tc_n(int P) { return P == 1 ? 256 : (P == 2 ? 128 : 64); }
+// Bytes of one (tile, block) of the tiled weight: P planes of N x 256.
+__host__ __device__ constexpr int tc_bbytes(int P) { return P * tc_n(P) * kTcKB; }
+// Bytes of one (tile, block) of the tiled scales: ws1[N] then ws2[N].
+__host__ __device__ constexpr int tc_sbytes(int P) { return 2 * tc_n(P) * 4; }
+__host__ __device__ constexpr int tc_stage_bytes(int P) { return kTcABytes + tc_bbytes(P) + tc_sbytes(P); }
+__host__ __device__ inline size_t tc_smem_bytes(int P) { return (size_t)kTcStages * tc_stage_bytes(P) + 1024; }
+// Planes of a device weight format (0: not on the tensor-core path).
+__host__ __device__ constexpr int tc_planes(int fmt) {
+    return fmt == FMT_PANEL ? 1 : (fmt == FMT_Q6K ? 2 : (fmt == FMT_Q4K ? 3 : 0));
+}
 
 // Byte offset of (row r, k) inside a canonical tile of R rows x 256 K.
 __host__ __device__ inline size_t tc_tile_off(int r, int k, int R) {
@@ -48,8 +65,8 @@ __host__ __device__ inline size_t tc_tile_off(int r, int k, int R) {
 struct TcArgs {
     const int8_t *a;   // tiled activations [ceil(T/128)][nb][128 x 256]
     const float *ad;   // activation block scales [T_pad][nb]
-    const int8_t *w;   // tiled weight [ceil(N/256)][nb][256 x 256]
-    const float *ws;   // tiled weight block scales [ceil(N/256)][nb][256]
+    const int8_t *w;   // tiled weight [ceil(N/n)][nb][P][n x 256]
+    const float *ws;   // tiled weight scales [ceil(N/n)][nb][2][n]
     float *out;        // [T][ldo]
     int ldo, T, N, nb;
     int epi;           // 0: out = y, 1: out += y
@@ -125,10 +142,18 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr)
         : "memory");
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// int32 -> fp32 for |v| < 2^22 without the conversion unit: the bits of
+// 1.5 * 2^23 + v.  Exact, so fmaf(tc_magic(v), s, -1.5 * 2^23 * s) rounds
+// v * s once, like fmaf on (float)v, whenever 1.5 * 2^23 * s is exact.
+__device__ __forceinline__ float tc_magic(uint32_t v) { return __int_as_float((int)(v + 0x4B400000u)); }
+constexpr float kTcMagic = 12582912.0f;  // 1.5 * 2^23
+
+template <int P>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__ TcArgs a) {
+    constexpr int N = tc_n(P), C = N / 4, BB = tc_bbytes(P), SB = tc_sbytes(P), STB = tc_stage_bytes(P);
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf[2], acce[2], fin;
     __shared__ uint32_t s_tmem;
@@ -158,7 +183,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
     const uint32_t tmem = s_tmem;
     bool ok = true;
     if (warp == 0) {
-        // producer: A tile, W tile and W block scales of each K block
+        // producer: A tile, W planes and W block scales of each K block
         if (lane == 0) {
             for (int kb = 0; kb < nb && ok; kb++) {
                 const int s = kb % kTcStages, use = kb / kTcStages;
@@ -166,18 +191,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                     ok = false;
                     break;
                 }
-                uint8_t *st = stage + (size_t)s * kTcStageBytes;
-                tc_mbar_expect(&full[s], kTcStageBytes);
+                uint8_t *st = stage + (size_t)s * STB;
+                tc_mbar_expect(&full[s], STB);
                 tc_bulk(st, a.a + ((size_t)mt * nb + kb) * kTcABytes, kTcABytes, &full[s]);
-                tc_bulk(st + kTcABytes, a.w + ((size_t)ntile * nb + kb) * kTcBBytes, kTcBBytes, &full[s]);
-                tc_bulk(st + kTcABytes + kTcBBytes, a.ws + ((size_t)ntile * nb + kb) * kTcN, kTcWsBytes, &full[s]);
+                tc_bulk(st + kTcABytes, a.w + ((size_t)ntile * nb + kb) * BB, BB, &full[s]);
+                tc_bulk(st + kTcABytes + BB, (const uint8_t *)a.ws + ((size_t)ntile * nb + kb) * SB, SB, &full[s]);
             }
             if (!ok) atomicExch(a.err, 1);
         }
     } else if (warp == 1) {
-        // MMA issuer: 8 MMAs (K = 32 each) per block into accumulator kb % 2
+        // MMA issuer: 8 x P MMAs (K = 32 each) per block into accumulator set kb % 2
         if (lane == 0) {
-            constexpr uint32_t idesc = tc_idesc(kTcM, kTcN);
+            constexpr uint32_t idesc = tc_idesc(kTcM, N);
             for (int kb = 0; kb < nb && ok; kb++) {
                 const int s = kb % kTcStages, use = kb / kTcStages, buf = kb & 1, ub = kb >> 1;
                 if (!tc_mbar_wait(&full[s], use & 1) || (ub > 0 && !tc_mbar_wait(&acce[buf], (ub - 1) & 1))) {
@@ -185,11 +210,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                     break;
                 }
                 tc_fence_after();
-                const uint8_t *st = stage + (size_t)s * kTcStageBytes;
+                const uint8_t *st = stage + (size_t)s * STB;
 #pragma unroll
                 for (int k = 0; k < kTcKB / 32; k++)
-                    tc_mma(tmem + (uint32_t)buf * kTcN, tc_desc(st, k, kTcM), tc_desc(st + kTcABytes, k, kTcN), idesc,
-                           k > 0);
+#pragma unroll
+                    for (int p = 0; p < P; p++)
+                        tc_mma(tmem + (uint32_t)(buf * P * N + p * N), tc_desc(st, k, kTcM),
+                               tc_desc(st + kTcABytes + p * N * kTcKB, k, N), idesc, k > 0);
                 tc_commit(&empty[s]);
                 tc_commit(&accf[buf]);
             }
@@ -197,13 +224,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
             if (!tc_mbar_wait(&fin, 0)) ok = false;
             if (!ok) atomicExch(a.err, 1);
         }
-    } else if (warp >= 4) {
-        // epilogue: lane quarter q (tokens 32q..32q+31 of the tile), columns part*64 ..
-        const int e = warp - 4, q = warp & 3, part = e >> 2;
+    } else {
+        // epilogue: lane quarter q = warp % 4 (the TMEM lanes this warp may
+        // read: tokens 32q..32q+31 of the tile), columns part*C ..; each run
+        // of four consecutive warps covers all four quarters
+        const int e = warp - 2, q = warp & 3, part = e >> 2;
         const int t = mt * kTcM + q * 32 + lane;
-        float acc[64];
+        float acc[C];
 #pragma unroll
-        for (int j = 0; j < 64; j++) acc[j] = 0.f;
+        for (int j = 0; j < C; j++) acc[j] = 0.f;
         for (int kb = 0; kb < nb && ok; kb++) {
             const int s = kb % kTcStages, buf = kb & 1, ub = kb >> 1;
             if (!tc_mbar_wait(&accf[buf], ub & 1)) {
@@ -212,14 +241,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
             }
             tc_fence_after();
             const float yd = t < a.T ? __ldg(a.ad + (size_t)t * nb + kb) : 0.f;
-            const float *wsb = (const float *)(stage + (size_t)s * kTcStageBytes + kTcABytes + kTcBBytes) + part * 64;
+            const float *ws1 = (const float *)(stage + (size_t)s * STB + kTcABytes + BB) + part * C;
+            const float *ws2 = ws1 + N;
+            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * P * N + part * C);
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
-                uint32_t r[16];
-                tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kTcN + part * 64 + c * 16), r);
+            for (int c = 0; c < C / 16; c++) {
+                uint32_t r[P][16];
 #pragma unroll
-                for (int j = 0; j < 16; j++)
-                    acc[c * 16 + j] = fmaf((float)(int)r[j], yd * wsb[c * 16 + j], acc[c * 16 + j]);
+                for (int p = 0; p < P; p++) tc_ld16(tbase + (uint32_t)(p * N + c * 16), r[p]);
+                tc_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                    const int n = c * 16 + j;
+                    float v;
+                    if constexpr (P == 1) {
+                        // |S| <= 256 * 127 * 3 < 2^22; ws2 holds -1.5 * 2^23 * ws1 (exact: ws1 is an f16)
+                        v = fmaf(tc_magic(r[0][j]), ws1[n], ws2[n]);
+                    } else {
+                        const int s1 = (int)(r[0][j] << 6) + (int)r[1][j];
+                        v = (float)s1 * ws1[n];
+                        if constexpr (P == 3) v = fmaf(-(float)(int)r[2][j], ws2[n], v);
+                    }
+                    acc[n] = fmaf(v, yd, acc[n]);
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -230,11 +274,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
         }
         if (ok && t < a.T) {
             float *o = a.out + (size_t)t * a.ldo;
-            const int n0 = ntile * kTcN + part * 64;
+            const int n0 = ntile * N + part * C;
+            if ((a.ldo & 3) == 0 && n0 + C <= a.N) {
 #pragma unroll
-            for (int j = 0; j < 64; j++) {
-                const int n = n0 + j;
-                if (n < a.N) o[n] = a.epi ? o[n] + acc[j] : acc[j];
+                for (int j = 0; j < C; j += 4) {
+                    float4 v = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                    if (a.epi) {
+                        const float4 p = *(const float4 *)(o + n0 + j);
+                        v.x += p.x;
+                        v.y += p.y;
+                        v.z += p.z;
+                        v.w += p.w;
+                    }
+                    *(float4 *)(o + n0 + j) = v;
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < C; j++) {
+                    const int n = n0 + j;
+                    if (n < a.N) o[n] = a.epi ? o[n] + acc[j] : acc[j];
+                }
             }
         }
         if (!ok && lane == 0) atomicExch(a.err, 1);
@@ -248,28 +307,87 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
 
 // ---------------------------------------------------------------- operand preparation
 
-// Panel weight -> tiled int8 W = code * 2^shift - off, rows past n are zero,
-// and the tiled block scales (zero past n).  One thread per (row, 16 codes).
-__global__ void tc_panel_to_tiled(const __grid_constant__ WDesc w, int8_t *tw, float *tws) {
-    const int nb = w.k / 256, ntiles = (w.n + kTcN - 1) / kTcN;
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    const long long total = (long long)ntiles * kTcN * nb * 16;
-    if (i >= total) return;
-    const int g16 = (int)(i % 16);                      // 16-element group in the block
-    const int b = (int)((i / 16) % nb);
-    const int rr = (int)(i / (16LL * nb));              // padded row
-    const int tile = rr / kTcN, r = rr % kTcN;
-    int8_t *dst = tw + ((size_t)tile * nb + b) * kTcBBytes;
-    const int ch = g16 >> 2, l = g16 & 3;               // natural chunk of 64, plane
-    for (int j = 0; j < 16; j++) {
-        int v = 0;
-        if (rr < w.n) {
-            const uint8_t byte = w.w[(size_t)rr * w.stride + (size_t)b * 64 + piece_of_chunk(ch) * 16 + j];
-            v = ((byte >> (2 * l)) & 3) * (1 << w.shift) - w.off;
-        }
-        dst[tc_tile_off(r, g16 * 16 + j, kTcN)] = (int8_t)v;
+// Integer plane values of element x (0..255) of block b of row r, and the
+// block's scales, in each format's device layout (the element decode of
+// dequant_elem).  Rows past n give zeros.
+template <int P>
+__device__ inline void tc_elem(const WDesc &w, int r, int b, int x, int (&v)[P]) {
+    const uint8_t *row = w.w + (size_t)r * w.stride;
+    const int nb = w.k / 256;
+    if constexpr (P == 1) {
+        const int ch = x >> 6, l = (x >> 4) & 3, i = x & 15;
+        const uint8_t byte = row[(size_t)b * 64 + piece_of_chunk(ch) * 16 + i];
+        v[0] = ((byte >> (2 * l)) & 3) * (1 << w.shift) - w.off;
+    } else if constexpr (P == 2) {
+        const int half = x >> 7, q = (x & 127) >> 5, l = x & 31;
+        const uint8_t lb = row[(size_t)b * 128 + half * 64 + l + (q & 1) * 32];
+        const int lo = (q & 2) ? (lb >> 4) : (lb & 15);
+        const int hi = (row[(size_t)nb * 128 + (size_t)b * 64 + half * 32 + l] >> (2 * q)) & 3;
+        const int sc = (int8_t)row[(size_t)nb * 192 + (size_t)b * 16 + half * 8 + 2 * q + (l >> 4)];
+        const int wv = sc * ((lo | (hi << 4)) - 32);  // -4096 .. 3937
+        v[0] = wv >> 6;                               // arithmetic: floor
+        v[1] = wv & 63;
+    } else {
+        const uint8_t *blk = row + (size_t)b * 144;
+        const int g = x >> 6, hi = (x >> 5) & 1, l = x & 31, j = 2 * g + hi;
+        const uint8_t *q = blk + 4;
+        int sc, mn;
+        if (j < 4) { sc = q[j] & 63; mn = q[j + 4] & 63; }
+        else { sc = (q[j + 4] & 0x0f) | ((q[j - 4] >> 6) << 4); mn = (q[j + 4] >> 4) | ((q[j] >> 6) << 4); }
+        const uint8_t qb = blk[16 + 32 * g + l];
+        const int wv = sc * (hi ? (qb >> 4) : (qb & 15));  // 0 .. 945
+        v[0] = wv >> 6;
+        v[1] = wv & 63;
+        v[2] = mn;
     }
-    if (g16 == 0) tws[((size_t)tile * nb + b) * kTcN + r] = rr < w.n ? w.s[(size_t)rr * nb + b] : 0.f;
+}
+
+template <int P>
+__device__ inline void tc_block_scales(const WDesc &w, int r, int b, float &s1, float &s2) {
+    const uint8_t *row = w.w + (size_t)r * w.stride;
+    const int nb = w.k / 256;
+    if constexpr (P == 1) {
+        s1 = w.s[(size_t)r * nb + b];
+        s2 = -kTcMagic * s1;  // exact: s1 is an f16 value
+    } else if constexpr (P == 2) {
+        s1 = h2f((uint16_t)(row[(size_t)nb * 208 + 2 * b] | (row[(size_t)nb * 208 + 2 * b + 1] << 8)));
+        s2 = 0.f;
+    } else {
+        const uint8_t *blk = row + (size_t)b * 144;
+        s1 = h2f((uint16_t)(blk[0] | (blk[1] << 8)));
+        s2 = h2f((uint16_t)(blk[2] | (blk[3] << 8)));
+    }
+}
+
+// Device weight -> tiled int8 planes and tiled block scales.  One thread per
+// (padded row, block, 16-element group).
+template <int P>
+__global__ void tc_weight_to_tiled(const __grid_constant__ WDesc w, int8_t *tw, float *tws) {
+    constexpr int N = tc_n(P);
+    const int nb = w.k / 256, ntiles = (w.n + N - 1) / N;
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long long total = (long long)ntiles * N * nb * 16;
+    if (i >= total) return;
+    const int g16 = (int)(i % 16);
+    const int b = (int)((i / 16) % nb);
+    const int rr = (int)(i / (16LL * nb));  // padded row
+    const int tile = rr / N, r = rr % N;
+    int8_t *dst = tw + ((size_t)tile * nb + b) * tc_bbytes(P);
+    for (int j = 0; j < 16; j++) {
+        int v[P];
+#pragma unroll
+        for (int p = 0; p < P; p++) v[p] = 0;
+        if (rr < w.n) tc_elem<P>(w, rr, b, g16 * 16 + j, v);
+#pragma unroll
+        for (int p = 0; p < P; p++) dst[(size_t)p * N * kTcKB + tc_tile_off(r, g16 * 16 + j, N)] = (int8_t)v[p];
+    }
+    if (g16 == 0) {
+        float s1 = 0.f, s2 = 0.f;
+        if (rr < w.n) tc_block_scales<P>(w, rr, b, s1, s2);
+        float *sd = tws + ((size_t)tile * nb + b) * 2 * N;
+        sd[r] = s1;
+        sd[N + r] = s2;
+    }
 }
 
 // Activation rows -> Q8_K, written as tiled int8 codes plus block scales.

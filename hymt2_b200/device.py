@@ -289,6 +289,48 @@ class DeviceModel:
         self.cache = ids + fed
         return gen
 
+    # ---- ragged multi-sequence batches and the continuous-batching server
+    def batch_prepare(self, slots: int, slot_ctx: int, max_tokens: int, max_out: int | None = None) -> None:
+        mo = slots if max_out is None else max_out
+        if self.be.lib.hyc_batch_prepare(self.be.impl, slots, slot_ctx, max_tokens, mo) != 0:
+            raise BackendError("batch_prepare: " + self.be.error())
+        self.batch_vocab = self.g.tensors.get("output.weight", self.g.tensors["token_embd.weight"]).n
+
+    def batch_forward(self, tokens, slots, positions, out_rows, want_logits: bool = False):
+        """One pass over a ragged batch; argmax ids of the out_rows tokens (and their logits)."""
+        tk = np.ascontiguousarray(tokens, dtype=np.int32)
+        sl = np.ascontiguousarray(slots, dtype=np.int32)
+        ps = np.ascontiguousarray(positions, dtype=np.int32)
+        rows = np.ascontiguousarray(out_rows, dtype=np.int32)
+        ids = np.zeros(max(len(rows), 1), dtype=np.int32)
+        lg = np.zeros((len(rows), self.batch_vocab), dtype=np.float32) if want_logits else None
+        rc = self.be.lib.hyc_batch_forward(self.be.impl, tk.ctypes.data, sl.ctypes.data, ps.ctypes.data, len(tk),
+                                           rows.ctypes.data, len(rows), self.vocab_out, ids.ctypes.data, _ptr(lg))
+        if rc != 0:
+            raise BackendError("batch_forward: " + self.be.error())
+        return ids[:len(rows)], lg
+
+    def batch_kv(self, slot: int, layer: int, npos: int):
+        kvd = self.hp.kv_heads * self.hp.hdim
+        k = np.zeros(npos * kvd, dtype=np.uint16)
+        v = np.zeros_like(k)
+        if self.be.lib.hyc_batch_kv_read(self.be.impl, slot, layer, npos, k.ctypes.data, v.ctypes.data) != 0:
+            raise BackendError("batch_kv_read")
+        return k.reshape(npos, kvd), v.reshape(npos, kvd)
+
+    def serve(self, prompts, max_new: int, step_tokens: int):
+        """Greedy generation for many requests with continuous batching; returns ([nreq][max_new] ids, stats)."""
+        flat = np.ascontiguousarray(np.concatenate([np.asarray(p, dtype=np.int32) for p in prompts]))
+        off = np.zeros(len(prompts) + 1, dtype=np.int32)
+        off[1:] = np.cumsum([len(p) for p in prompts])
+        out = np.zeros((len(prompts), max_new), dtype=np.int32)
+        st = abi.ServeStats()
+        rc = self.be.lib.hyc_serve(self.be.impl, flat.ctypes.data, off.ctypes.data, len(prompts), max_new,
+                                   self.vocab_out, step_tokens, out.ctypes.data, C.byref(st))
+        if rc != 0:
+            raise BackendError("serve: " + self.be.error())
+        return out, {f: getattr(st, f) for f, _ in abi.ServeStats._fields_}
+
     def kv(self, layer: int, npos: int):
         kvd = self.hp.kv_heads * self.hp.hdim
         k = np.zeros(npos * kvd, dtype=np.uint16)

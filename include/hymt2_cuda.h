@@ -105,15 +105,52 @@ HYC_API void hyc_host_free(void *p);
 HYC_API int hyc_set_decode_mode(void *impl, int mode);
 /* Tensor-core path for multi-token chunks (no reference counterpart; it
  * serves the same forward_batch chunks, src/model.c:798-909): with on != 0
- * (the default) chunks of >= 32 tokens over panel (STQ1_0 / Q2_0C) weights
- * run the tcgen05 int8 GEMM with TMEM accumulators; 0 keeps the dp4a GEMV
- * kernels.  hyc_tc_test runs one panel weight through that GEMM on host
- * inputs (act as hyc_gemv_test: 1 plain, 2 RMSNorm*w, 3 SiLU(x)*x2; nt 1..256)
- * and writes out[t*n + r]. */
+ * (the default) chunks of >= 32 tokens over STQ1_0 / Q2_0C panel, Q4_K and
+ * Q6_K weights run the tcgen05 int8 GEMM with TMEM accumulators; 0 keeps
+ * the dp4a GEMV kernels.  hyc_tc_test runs one such weight through that
+ * GEMM on host inputs (act as hyc_gemv_test: 1 plain, 2 RMSNorm*w,
+ * 3 SiLU(x)*x2; nt 1..256) and writes out[t*n + r]. */
 HYC_API int hyc_set_tc(void *impl, int on);
 HYC_API int hyc_tc_test(void *impl, hy_dweight *w, int act, const float *x, const float *x2, const float *norm_w,
                         float eps, int nt, float *out);
 HYC_API int hyc_decode_path(void *impl, char *why, int cap);
+
+/* ---- ragged multi-sequence batches and the continuous-batching server --
+ * (additive extension, no reference counterpart: the reference serves one
+ * sequence per handle, src/model.c:914-958; these run many of them through
+ * one forward pass).  After fused_prepare and hyc_set_embedding:
+ * hyc_batch_prepare allocates `slots` sequence caches of slot_ctx rows
+ * (slot_ctx <= the prepared ctx) plus one shared-prefix cache, and
+ * activations for up to max_tokens tokens per pass with up to max_out head
+ * rows.  hyc_batch_forward runs one pass over host arrays: token t is
+ * tokens[t] at position tok_pos[t] of slot tok_slot[t] (its K/V row is
+ * written there; it attends to rows 0..tok_pos[t] of that slot, which must
+ * be filled by this or earlier passes; no (slot, position) twice in one
+ * pass).  For each i < nout, out_ids[i] is the argmax over the first
+ * vocab_out logits (all when <= 0) of token out_rows[i], after the output
+ * RMSNorm and LM head; `logits` (optional) receives them as [nout][n_vocab].
+ * hyc_batch_kv_copy copies rows 0..npos-1 of every layer from one slot to
+ * another (slot `slots` is the prefix cache); hyc_batch_kv_read reads one
+ * slot's layer like hyc_kv_read.
+ * hyc_serve generates max_new greedy tokens for each of nreq requests
+ * (request r = prompts[prompt_off[r] .. prompt_off[r+1])), as the
+ * reference's gen_ids would one request at a time, with continuous batching
+ * over the prepared slots: each pass feeds one token of every decoding
+ * request plus prompt chunks of newly admitted ones, at most step_tokens in
+ * all (<= max_tokens; max_out must be >= slots), and a prompt that shares
+ * >= 8 leading tokens with the first completed prompt starts from a copy of
+ * those cached rows (always recomputing its last prompt token).  out_ids
+ * is [nreq][max_new].  All return 0 or -1 (hyc_last_error). */
+typedef struct hyc_serve_stats {
+    long long steps, decode_tokens, prefill_tokens, prefix_hits, prefix_tokens, generated;
+} hyc_serve_stats;
+HYC_API int hyc_batch_prepare(void *impl, int slots, int slot_ctx, int max_tokens, int max_out);
+HYC_API int hyc_batch_forward(void *impl, const int *tokens, const int *tok_slot, const int *tok_pos, int nt,
+                              const int *out_rows, int nout, int vocab_out, int *out_ids, float *logits);
+HYC_API int hyc_batch_kv_copy(void *impl, int src_slot, int dst_slot, int npos);
+HYC_API int hyc_batch_kv_read(void *impl, int slot, int layer, int npos, uint16_t *k, uint16_t *v);
+HYC_API int hyc_serve(void *impl, const int *prompts, const int *prompt_off, int nreq, int max_new, int vocab_out,
+                      int step_tokens, int *out_ids, hyc_serve_stats *stats);
 
 /* ---- kernel-level hooks for parity tests (host buffers, synchronous) -- */
 

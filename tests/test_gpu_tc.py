@@ -1,7 +1,9 @@
-"""The tcgen05 int8 tensor-core GEMM that multi-token chunks over panel
-weights use (needs a B200), through the C ABI.
+"""The tcgen05 int8 tensor-core GEMM that multi-token chunks use (needs a
+B200), through the C ABI.
 
-  - one panel weight (STQ1_0, Q2_0C) on 1..200 tokens with each activation
+  - one weight (STQ1_0, Q2_0C panels; Q4_K, Q6_K as int8 planes, also with
+    extreme sub-scales so the 64*hi + lo split meets its bounds) on 1..200
+    tokens with each activation
     prologue (plain, RMSNorm*w, SiLU*up): against the oracle's host sequence
     (Q8_K quantiser, panel rows; reference src/kernels.c:128-165, 565-581)
     within 1e-4 relative except for rare one-code Q8_K rounding flips of the
@@ -20,7 +22,19 @@ from conftest import rand_act, rand_blocks
 
 pytestmark = pytest.mark.gpu
 
-TYPES = {"STQ1_0": 43, "Q2_0C": 40}
+TYPES = {"STQ1_0": 43, "Q2_0C": 40, "Q4_K": 12, "Q6_K": 14, "Q4_K_ext": 12, "Q6_K_ext": 14}
+
+
+def _extreme(raw: np.ndarray, gt: int, rng) -> np.ndarray:
+    """Sub-scales at the ends of their ranges (Q6_K int8 -128 / 127, Q4_K 6-bit 63)."""
+    raw = raw.copy()
+    if gt == 14:
+        blk = raw.reshape(-1, 210)
+        blk[:, 192:208] = rng.choice(np.array([0x80, 0x7F, 0x81, 0x01], dtype=np.uint8), size=(blk.shape[0], 16))
+    else:
+        blk = raw.reshape(-1, 144)
+        blk[:, 4:16] = 0xFF
+    return raw
 
 
 @pytest.mark.parametrize("name", list(TYPES))
@@ -32,6 +46,8 @@ def test_tc_gemm(backend, oracle, name, act, k, rows, nt):
     gt = TYPES[name]
     rng = np.random.default_rng(k + act * 7 + nt + rows)
     raw = rand_blocks(rng, gt, rows, k)
+    if name.endswith("_ext"):
+        raw = _extreme(raw, gt, rng)
     h = backend.upload(weight_from_bytes(gt, raw, rows, k))
     try:
         x = rand_act(rng, nt, k) * 3.0
