@@ -173,7 +173,21 @@ bool launch(HyCtx *c, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
-    if (e != cudaSuccess) return fail(c, "kernel launch", e);
+    if (e != cudaSuccess) {
+        fail(c, "kernel launch", e);
+        if (e == cudaErrorLaunchOutOfResources) {  // say which limit
+            cudaFuncAttributes fa;
+            int optin = 0;
+            cudaFuncGetAttributes(&fa, (const void *)kern);
+            cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->dev);
+            const size_t used = strlen(c->err);
+            snprintf(c->err + used, sizeof c->err - used,
+                     " (block %u, dyn smem %zu of max %d, static %zu, opt-in %d, regs %d, max threads %d)",
+                     block.x * block.y * block.z, smem, fa.maxDynamicSharedSizeBytes, fa.sharedSizeBytes, optin,
+                     fa.numRegs, fa.maxThreadsPerBlock);
+        }
+        return false;
+    }
     c->launches++;
     c->capture_kernels++;
     return true;
@@ -211,8 +225,8 @@ bool is_q8_fmt(int fmt) { return fmt == FMT_PANEL || fmt == FMT_Q4K || fmt == FM
 // ---------------------------------------------------------------- GEMV dispatch
 
 template <typename K>
-void set_smem(K kern) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxDynSmem);
+void set_smem(K kern, size_t bytes = kMaxDynSmem) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
 void init_kernel_attrs() {
@@ -257,9 +271,9 @@ void init_kernel_attrs() {
     set_smem(attn_chunk_kernel<64, 2>);
     set_smem(attn_chunk_kernel<64, 4>);
     set_smem(attn_chunk_kernel<64, 8>);
-    set_smem(tc_gemm<1>);
-    set_smem(tc_gemm<2>);
-    set_smem(tc_gemm<3>);
+    set_smem(tc_gemm<1>, tc_smem_bytes(1));
+    set_smem(tc_gemm<2>, tc_smem_bytes(2));
+    set_smem(tc_gemm<3>, tc_smem_bytes(3));
 }
 
 // One launch for nt <= NT tokens.
@@ -443,8 +457,8 @@ bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float
         ta.nb = nb;
         ta.epi = epi;
         ta.err = c->d_tcerr;
-        const int P = tc_planes(ws[i]->fmt);
-        const dim3 grid(tpad / kTcM, (ws[i]->n + tc_n(P) - 1) / tc_n(P));
+        const int P = tc_planes(ws[i]->fmt), ntiles = tc_tiles(P, nt, ws[i]->n);
+        const dim3 grid(ntiles < c->nsm ? ntiles : c->nsm);
         bool ok;
         if (P == 1) ok = launch(c, tc_gemm<1>, grid, dim3(kTcThreads), tc_smem_bytes(1), false, ta);
         else if (P == 2) ok = launch(c, tc_gemm<2>, grid, dim3(kTcThreads), tc_smem_bytes(2), false, ta);

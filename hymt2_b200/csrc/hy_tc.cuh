@@ -18,18 +18,24 @@
 // The blocks are combined in fp32.
 //
 // Operands live in global memory pre-tiled in the UMMA canonical K-major
-// layout without swizzle: a tile of R rows x 256 K is 32 x (R/8) core
+// layout without swizzle: a tile of R rows x K is (K/16) x (R/8) core
 // matrices of 8 rows x 16 bytes; core (row group g, 16-byte k chunk c) sits
-// at (c * R/8 + g) * 128 bytes.  One bulk copy moves a whole tile.
+// at (c * R/8 + g) * 128 bytes, so each half block (K = 128) of a tile is
+// contiguous.  Activations: [m tile][block][128 x 256]; weights: [n tile]
+// [block][half][plane][N x 128], so one bulk copy moves the A half or all
+// planes of the B half of a stage.
 //
-// CTA = 128 tokens x N weight rows (N = 256 / 128 / 64 for P = 1 / 2 / 3, so
-// one accumulator set is at most 256 TMEM columns and two fit): warp 0
-// streams (A, W planes, scales) of one K block per stage into a 2-stage
-// ring, warp 1 (one thread) issues 8 x P MMAs of K = 32 per block into one
-// of two TMEM accumulator sets, and warps 2-17 (4 per TMEM lane
-// quarter, N/4 columns each) read the block's int32 results with
-// tcgen05.ld and fold them into fp32 registers while the next block's MMAs
-// run.  Every wait is bounded; TMEM is released on every exit.
+// Persistent CTAs (one per SM) walk the (m, n) tiles m-fastest, so the
+// CTAs running at one time share each weight tile through L2.  Per CTA:
+// warp 0 streams half blocks (A, B planes) into a 4-stage ring and each
+// block's scales into a 4-entry ring of their own; warp 1 (one thread)
+// issues 4 x P MMAs of K = 32 per half block into one of two TMEM
+// accumulator sets (N = 256 / 128 / 64 for P = 1 / 2 / 3, so one set is at
+// most 256 columns); warps 2-17 (4 per TMEM lane quarter, N/4 columns each)
+// read a finished block's int32 results with tcgen05.ld and fold them into
+// fp32 registers while the MMAs of the next block (or tile) run.  A stage is
+// released by the MMA commit alone, a scale entry and an accumulator set by
+// the epilogue.  Every wait is bounded; TMEM is released on every exit.
 #pragma once
 #include "hy_common.cuh"
 #include "hy_gemv.cuh"
@@ -37,8 +43,10 @@
 namespace hyk {
 
 constexpr int kTcM = 128;       // tokens per tile (TMEM lanes)
-constexpr int kTcKB = 256;      // K per stage: one Q8_K block
-constexpr int kTcStages = 2;
+constexpr int kTcKB = 256;      // K per Q8_K block
+constexpr int kTcKH = 128;      // K per stage: half a block
+constexpr int kTcStages = 4;
+constexpr int kTcScaleSlots = 4;
 constexpr int kTcEpiWarps = 16;
 constexpr int kTcThreads = (2 + kTcEpiWarps) * 32;  // warp 0 producer, 1 MMA, 2.. epilogue
 constexpr int kTcABytes = kTcM * kTcKB;             // 32 KB
@@ -46,32 +54,47 @@ constexpr unsigned long long kTcWaitNs = 2000000000ull;
 
 // Weight rows per tile for P planes.
 __host__ __device__ constexpr int tc_n(int P) { return P == 1 ? 256 : (P == 2 ? 128 : 64); }
-// Bytes of one (tile, block) of the tiled weight: P planes of N x 256.
+// Bytes of one (tile, block) of the tiled weight: 2 halves x P planes of N x 128.
 __host__ __device__ constexpr int tc_bbytes(int P) { return P * tc_n(P) * kTcKB; }
 // Bytes of one (tile, block) of the tiled scales: ws1[N] then ws2[N].
 __host__ __device__ constexpr int tc_sbytes(int P) { return 2 * tc_n(P) * 4; }
-__host__ __device__ constexpr int tc_stage_bytes(int P) { return kTcABytes + tc_bbytes(P) + tc_sbytes(P); }
-__host__ __device__ inline size_t tc_smem_bytes(int P) { return (size_t)kTcStages * tc_stage_bytes(P) + 1024; }
+// One stage: the A half (128 x 128) and the B half (P planes of N x 128).
+__host__ __device__ constexpr int tc_stage_bytes(int P) { return kTcABytes / 2 + tc_bbytes(P) / 2; }
+__host__ __device__ inline size_t tc_smem_bytes(int P) {
+    return (size_t)kTcStages * tc_stage_bytes(P) + (size_t)kTcScaleSlots * tc_sbytes(P) + 1024;
+}
+static_assert(4 * (kTcABytes / 2 + 256 * kTcKB / 2) + 4 * 2 * 256 * 4 + 1024 <= 227 * 1024, "tc stages exceed shared memory");
 // Planes of a device weight format (0: not on the tensor-core path).
 __host__ __device__ constexpr int tc_planes(int fmt) {
     return fmt == FMT_PANEL ? 1 : (fmt == FMT_Q6K ? 2 : (fmt == FMT_Q4K ? 3 : 0));
 }
 
-// Byte offset of (row r, k) inside a canonical tile of R rows x 256 K.
+// Byte offset of (row r, k) inside a canonical tile of R rows (any K).
 __host__ __device__ inline size_t tc_tile_off(int r, int k, int R) {
     return ((size_t)(k >> 4) * (R / 8) + (r >> 3)) * 128 + (size_t)(r & 7) * 16 + (k & 15);
+}
+// Byte offset of (plane p, row r, k in 0..255) inside one (tile, block) of
+// a tiled weight: half k / 128, then plane, then the N x 128 canonical tile.
+__host__ __device__ inline size_t tc_wtile_off(int P, int p, int r, int k) {
+    const int N = tc_n(P);
+    return ((size_t)(k >> 7) * P + p) * N * kTcKH + tc_tile_off(r, k & 127, N);
 }
 
 struct TcArgs {
     const int8_t *a;   // tiled activations [ceil(T/128)][nb][128 x 256]
     const float *ad;   // activation block scales [T_pad][nb]
-    const int8_t *w;   // tiled weight [ceil(N/n)][nb][P][n x 256]
+    const int8_t *w;   // tiled weight [ceil(N/n)][nb][2][P][n x 128]
     const float *ws;   // tiled weight scales [ceil(N/n)][nb][2][n]
     float *out;        // [T][ldo]
     int ldo, T, N, nb;
     int epi;           // 0: out = y, 1: out += y
     int *err;          // set on a bounded-wait timeout
 };
+
+// Number of (m, n) tiles of a GEMM.
+__host__ __device__ inline int tc_tiles(int P, int T, int N) {
+    return ((T + kTcM - 1) / kTcM) * ((N + tc_n(P) - 1) / tc_n(P));
+}
 
 __device__ __forceinline__ uint32_t tc_smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -143,6 +166,18 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "r"(taddr)
         : "memory");
 }
+// 32 lanes x 8 columns.
+__device__ __forceinline__ void tc_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
+}
+template <int W>
+__device__ __forceinline__ void tc_ld(uint32_t taddr, uint32_t (&r)[W]) {
+    if constexpr (W == 16) tc_ld16(taddr, r);
+    else tc_ld8(taddr, r);
+}
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // int32 -> fp32 for |v| < 2^22 without the conversion unit: the bits of
@@ -153,17 +188,24 @@ constexpr float kTcMagic = 12582912.0f;  // 1.5 * 2^23
 
 template <int P>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__ TcArgs a) {
-    constexpr int N = tc_n(P), C = N / 4, BB = tc_bbytes(P), SB = tc_sbytes(P), STB = tc_stage_bytes(P);
+    constexpr int N = tc_n(P), C = N / 4, BH = tc_bbytes(P) / 2, AH = kTcABytes / 2, SB = tc_sbytes(P);
+    constexpr int STB = tc_stage_bytes(P);
     extern __shared__ __align__(1024) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf[2], acce[2], fin;
+    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], sfull[kTcScaleSlots], sempty[kTcScaleSlots],
+        accf[2], acce[2], fin;
     __shared__ uint32_t s_tmem;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int mt = blockIdx.x, ntile = blockIdx.y, nb = a.nb;
+    const int nb = a.nb, ntm = (a.T + kTcM - 1) / kTcM, ntiles = tc_tiles(P, a.T, a.N);
     uint8_t *stage = (uint8_t *)(((uintptr_t)smem + 1023) & ~(uintptr_t)1023);
+    uint8_t *scales = stage + (size_t)kTcStages * STB;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcStages; s++) {
             tc_mbar_init(&full[s], 1);
-            tc_mbar_init(&empty[s], 1 + kTcEpiWarps);  // MMA commit + every epilogue warp (block scales read)
+            tc_mbar_init(&empty[s], 1);  // the MMA commit
+        }
+        for (int s = 0; s < kTcScaleSlots; s++) {
+            tc_mbar_init(&sfull[s], 1);
+            tc_mbar_init(&sempty[s], kTcEpiWarps);
         }
         for (int b = 0; b < 2; b++) {
             tc_mbar_init(&accf[b], 1);
@@ -183,42 +225,64 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
     const uint32_t tmem = s_tmem;
     bool ok = true;
     if (warp == 0) {
-        // producer: A tile, W planes and W block scales of each K block
+        // producer: per block its scales, then two half-block stages
         if (lane == 0) {
-            for (int kb = 0; kb < nb && ok; kb++) {
-                const int s = kb % kTcStages, use = kb / kTcStages;
-                if (use > 0 && !tc_mbar_wait(&empty[s], (use - 1) & 1)) {
-                    ok = false;
-                    break;
+            int g = 0, hs = 0;  // blocks and half blocks issued by this CTA
+            for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+                const int mt = tile % ntm, nt = tile / ntm;
+                for (int kb = 0; kb < nb && ok; kb++, g++) {
+                    const int sl = g % kTcScaleSlots, su = g / kTcScaleSlots;
+                    if (su > 0 && !tc_mbar_wait(&sempty[sl], (su - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_mbar_expect(&sfull[sl], SB);
+                    tc_bulk(scales + (size_t)sl * SB, (const uint8_t *)a.ws + ((size_t)nt * nb + kb) * SB, SB, &sfull[sl]);
+                    for (int h = 0; h < 2 && ok; h++, hs++) {
+                        const int s = hs % kTcStages, use = hs / kTcStages;
+                        if (use > 0 && !tc_mbar_wait(&empty[s], (use - 1) & 1)) {
+                            ok = false;
+                            break;
+                        }
+                        uint8_t *st = stage + (size_t)s * STB;
+                        tc_mbar_expect(&full[s], STB);
+                        tc_bulk(st, a.a + ((size_t)mt * nb + kb) * kTcABytes + (size_t)h * AH, AH, &full[s]);
+                        tc_bulk(st + AH, a.w + ((size_t)nt * nb + kb) * tc_bbytes(P) + (size_t)h * BH, BH, &full[s]);
+                    }
                 }
-                uint8_t *st = stage + (size_t)s * STB;
-                tc_mbar_expect(&full[s], STB);
-                tc_bulk(st, a.a + ((size_t)mt * nb + kb) * kTcABytes, kTcABytes, &full[s]);
-                tc_bulk(st + kTcABytes, a.w + ((size_t)ntile * nb + kb) * BB, BB, &full[s]);
-                tc_bulk(st + kTcABytes + BB, (const uint8_t *)a.ws + ((size_t)ntile * nb + kb) * SB, SB, &full[s]);
             }
             if (!ok) atomicExch(a.err, 1);
         }
     } else if (warp == 1) {
-        // MMA issuer: 8 x P MMAs (K = 32 each) per block into accumulator set kb % 2
+        // MMA issuer: 4 x P MMAs (K = 32 each) per half block into accumulator set g % 2
         if (lane == 0) {
             constexpr uint32_t idesc = tc_idesc(kTcM, N);
-            for (int kb = 0; kb < nb && ok; kb++) {
-                const int s = kb % kTcStages, use = kb / kTcStages, buf = kb & 1, ub = kb >> 1;
-                if (!tc_mbar_wait(&full[s], use & 1) || (ub > 0 && !tc_mbar_wait(&acce[buf], (ub - 1) & 1))) {
-                    ok = false;
-                    break;
+            int g = 0, hs = 0;
+            for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+                for (int kb = 0; kb < nb && ok; kb++, g++) {
+                    const int buf = g & 1, ub = g >> 1;
+                    if (ub > 0 && !tc_mbar_wait(&acce[buf], (ub - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    for (int h = 0; h < 2; h++, hs++) {
+                        const int s = hs % kTcStages, use = hs / kTcStages;
+                        if (!tc_mbar_wait(&full[s], use & 1)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint8_t *st = stage + (size_t)s * STB;
+#pragma unroll
+                        for (int k = 0; k < kTcKH / 32; k++)
+#pragma unroll
+                            for (int p = 0; p < P; p++)
+                                tc_mma(tmem + (uint32_t)(buf * P * N + p * N), tc_desc(st, k, kTcM),
+                                       tc_desc(st + AH + p * N * kTcKH, k, N), idesc, (h | k) != 0);
+                        tc_commit(&empty[s]);
+                    }
+                    if (ok) tc_commit(&accf[buf]);
                 }
-                tc_fence_after();
-                const uint8_t *st = stage + (size_t)s * STB;
-#pragma unroll
-                for (int k = 0; k < kTcKB / 32; k++)
-#pragma unroll
-                    for (int p = 0; p < P; p++)
-                        tc_mma(tmem + (uint32_t)(buf * P * N + p * N), tc_desc(st, k, kTcM),
-                               tc_desc(st + kTcABytes + p * N * kTcKB, k, N), idesc, k > 0);
-                tc_commit(&empty[s]);
-                tc_commit(&accf[buf]);
             }
             tc_commit(&fin);  // completes when every MMA issued above has
             if (!tc_mbar_wait(&fin, 0)) ok = false;
@@ -229,70 +293,77 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
         // read: tokens 32q..32q+31 of the tile), columns part*C ..; each run
         // of four consecutive warps covers all four quarters
         const int e = warp - 2, q = warp & 3, part = e >> 2;
-        const int t = mt * kTcM + q * 32 + lane;
-        float acc[C];
+        int g = 0;
+        for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+            const int mt = tile % ntm, nt = tile / ntm;
+            const int t = mt * kTcM + q * 32 + lane;
+            float acc[C];
 #pragma unroll
-        for (int j = 0; j < C; j++) acc[j] = 0.f;
-        for (int kb = 0; kb < nb && ok; kb++) {
-            const int s = kb % kTcStages, buf = kb & 1, ub = kb >> 1;
-            if (!tc_mbar_wait(&accf[buf], ub & 1)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const float yd = t < a.T ? __ldg(a.ad + (size_t)t * nb + kb) : 0.f;
-            const float *ws1 = (const float *)(stage + (size_t)s * STB + kTcABytes + BB) + part * C;
-            const float *ws2 = ws1 + N;
-            const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * P * N + part * C);
+            for (int j = 0; j < C; j++) acc[j] = 0.f;
+            for (int kb = 0; kb < nb; kb++, g++) {
+                const int buf = g & 1, ub = g >> 1, sl = g % kTcScaleSlots;
+                if (!tc_mbar_wait(&accf[buf], ub & 1) || !tc_mbar_wait(&sfull[sl], (g / kTcScaleSlots) & 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const float yd = t < a.T ? __ldg(a.ad + (size_t)t * nb + kb) : 0.f;
+                const float *ws1 = (const float *)(scales + (size_t)sl * SB) + part * C;
+                const float *ws2 = ws1 + N;
+                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * P * N + part * C);
+                // P = 1 reads 8 columns at a time: its 64 accumulators leave
+                // fewer registers for the loaded words
+                constexpr int CW = P == 1 ? 8 : 16;
 #pragma unroll
-            for (int c = 0; c < C / 16; c++) {
-                uint32_t r[P][16];
+                for (int c = 0; c < C / CW; c++) {
+                    uint32_t r[P][CW];
 #pragma unroll
-                for (int p = 0; p < P; p++) tc_ld16(tbase + (uint32_t)(p * N + c * 16), r[p]);
-                tc_wait_ld();
+                    for (int p = 0; p < P; p++) tc_ld<CW>(tbase + (uint32_t)(p * N + c * CW), r[p]);
+                    tc_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
-                    const int n = c * 16 + j;
-                    float v;
-                    if constexpr (P == 1) {
-                        // |S| <= 256 * 127 * 3 < 2^22; ws2 holds -1.5 * 2^23 * ws1 (exact: ws1 is an f16)
-                        v = fmaf(tc_magic(r[0][j]), ws1[n], ws2[n]);
-                    } else {
-                        const int s1 = (int)(r[0][j] << 6) + (int)r[1][j];
-                        v = (float)s1 * ws1[n];
-                        if constexpr (P == 3) v = fmaf(-(float)(int)r[2][j], ws2[n], v);
+                    for (int j = 0; j < CW; j++) {
+                        const int n = c * CW + j;
+                        float v;
+                        if constexpr (P == 1) {
+                            // |S| <= 256 * 127 * 3 < 2^22; ws2 holds -1.5 * 2^23 * ws1 (exact: ws1 is an f16)
+                            v = fmaf(tc_magic(r[0][j]), ws1[n], ws2[n]);
+                        } else {
+                            const int s1 = (int)(r[0][j] << 6) + (int)r[1][j];
+                            v = (float)s1 * ws1[n];
+                            if constexpr (P == 3) v = fmaf(-(float)(int)r[2][j], ws2[n], v);
+                        }
+                        acc[n] = fmaf(v, yd, acc[n]);
                     }
-                    acc[n] = fmaf(v, yd, acc[n]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    tc_mbar_arrive(&acce[buf]);
+                    tc_mbar_arrive(&sempty[sl]);
                 }
             }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                tc_mbar_arrive(&acce[buf]);
-                tc_mbar_arrive(&empty[s]);
-            }
-        }
-        if (ok && t < a.T) {
-            float *o = a.out + (size_t)t * a.ldo;
-            const int n0 = ntile * N + part * C;
-            if ((a.ldo & 3) == 0 && n0 + C <= a.N) {
+            if (ok && t < a.T) {
+                float *o = a.out + (size_t)t * a.ldo;
+                const int n0 = nt * N + part * C;
+                if ((a.ldo & 3) == 0 && n0 + C <= a.N) {
 #pragma unroll
-                for (int j = 0; j < C; j += 4) {
-                    float4 v = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
-                    if (a.epi) {
-                        const float4 p = *(const float4 *)(o + n0 + j);
-                        v.x += p.x;
-                        v.y += p.y;
-                        v.z += p.z;
-                        v.w += p.w;
+                    for (int j = 0; j < C; j += 4) {
+                        float4 v = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
+                        if (a.epi) {
+                            const float4 p = *(const float4 *)(o + n0 + j);
+                            v.x += p.x;
+                            v.y += p.y;
+                            v.z += p.z;
+                            v.w += p.w;
+                        }
+                        *(float4 *)(o + n0 + j) = v;
                     }
-                    *(float4 *)(o + n0 + j) = v;
-                }
-            } else {
+                } else {
 #pragma unroll
-                for (int j = 0; j < C; j++) {
-                    const int n = n0 + j;
-                    if (n < a.N) o[n] = a.epi ? o[n] + acc[j] : acc[j];
+                    for (int j = 0; j < C; j++) {
+                        const int n = n0 + j;
+                        if (n < a.N) o[n] = a.epi ? o[n] + acc[j] : acc[j];
+                    }
                 }
             }
         }
@@ -379,7 +450,7 @@ __global__ void tc_weight_to_tiled(const __grid_constant__ WDesc w, int8_t *tw, 
         for (int p = 0; p < P; p++) v[p] = 0;
         if (rr < w.n) tc_elem<P>(w, rr, b, g16 * 16 + j, v);
 #pragma unroll
-        for (int p = 0; p < P; p++) dst[(size_t)p * N * kTcKB + tc_tile_off(r, g16 * 16 + j, N)] = (int8_t)v[p];
+        for (int p = 0; p < P; p++) dst[tc_wtile_off(P, p, r, g16 * 16 + j)] = (int8_t)v[p];
     }
     if (g16 == 0) {
         float s1 = 0.f, s2 = 0.f;
