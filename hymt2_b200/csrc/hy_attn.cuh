@@ -35,6 +35,11 @@ struct AttnArgs {
     // slot_stride elements after the previous slot's (kc/vc: slot 0)
     const int *tok_pos, *tok_slot;
     long long slot_stride;
+    // query blocks of the tensor-core prefill kernel: (first token, count)
+    // pairs of <= kFaQ consecutive positions of one slot; null: tokens
+    // 16b .. 16b+15 of one sequence
+    const int *qblk;
+    int nqb;
 };
 
 // Position of token t and the element offset of its sequence's cache.
@@ -953,6 +958,236 @@ __global__ void __launch_bounds__(G * 32) attn_prefill(const __grid_constant__ A
     float *dst = a.ao + (size_t)t * a.qdim + (kvh * G + w) * HD;
 #pragma unroll
     for (int i = 0; i < HD / 32; i++) dst[lane + 32 * i] = O[i] * inv;
+}
+
+// ---------------------------------------------------------------- prefill attention on tensor cores
+//
+// Causal GQA attention for multi-token passes (reference attn_task,
+// src/model.c:768-795: scores q.k / sqrt(hd), max-subtracted expf, sum of
+// p.v normalised by the sum of p), with q/k/v already rotated, normalised and
+// stored by rope_norm_store.  CTA = one query block (<= 16 consecutive
+// tokens of one sequence) x one KV head; warp w owns q head kvh*G + w, its
+// 16 rows the block's tokens.  K/V tiles of 64 keys are staged with cp.async
+// (double-buffered, rows padded by 8 elements so fragment loads hit distinct
+// banks) and multiplied with mma.sync m16n8k16 bf16 into fp32 accumulators
+// with an online softmax.  K and V are bf16 already; q and p are fp32 and
+// enter the bf16 MMAs as three bf16 terms (x = x1 + x2 + x3, each the bf16
+// rounding of what the previous ones leave), so every product keeps at
+// least fp32's 24 bits and the sums stay fp32.
+constexpr int kFaQ = 16;   // query tokens per block
+constexpr int kFaK = 64;   // keys per tile
+
+template <int HD>
+__host__ __device__ constexpr int fa_row() { return HD + 8; }  // padded bf16 row
+constexpr int kFaTerms = 3;  // bf16 terms of q and p
+template <int HD, int G>
+__host__ __device__ constexpr size_t fa_smem() {
+    return (size_t)G * kFaQ * fa_row<HD>() * 2 * kFaTerms + (size_t)2 * 2 * kFaK * fa_row<HD>() * 2;
+}
+
+__device__ __forceinline__ uint32_t fa_pack(float lo, float hi) {
+    const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *(const uint32_t *)&v;
+}
+// x = t[0] + t[1] + t[2] in bf16, packed pairs (element 0 in the low half);
+// each remainder is exact in fp32
+__device__ __forceinline__ void fa_split(float x0, float x1, uint32_t (&t)[kFaTerms]) {
+#pragma unroll
+    for (int i = 0; i < kFaTerms; i++) {
+        const __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
+        t[i] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+        x0 -= __bfloat162float(h0);
+        x1 -= __bfloat162float(h1);
+    }
+}
+__device__ __forceinline__ void fa_mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void fa_ldm4(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void fa_ldm4t(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+
+// Stage keys [k0, k0 + 64) (rows past kend zero-filled) of K and V.
+template <int HD, int G>
+__device__ __forceinline__ void fa_stage(const uint16_t *Kg, const uint16_t *Vg, int kvdim, int k0, int kend,
+                                         uint16_t *sk, uint16_t *sv) {
+    constexpr int CH = HD / 8;  // 16-byte chunks per row
+    for (int i = threadIdx.x; i < kFaK * CH; i += G * 32) {
+        const int r = i / CH, c = i % CH, key = k0 + r;
+        uint16_t *dk = sk + r * fa_row<HD>() + c * 8, *dv = sv + r * fa_row<HD>() + c * 8;
+        if (key < kend) {
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dk)),
+                         "l"(Kg + (size_t)key * kvdim + c * 8)
+                         : "memory");
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dv)),
+                         "l"(Vg + (size_t)key * kvdim + c * 8)
+                         : "memory");
+        } else {
+            *(uint4 *)dk = make_uint4(0, 0, 0, 0);
+            *(uint4 *)dv = make_uint4(0, 0, 0, 0);
+        }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// grid (query blocks, kv_heads), G warps.
+template <int HD, int G>
+__global__ void __launch_bounds__(G * 32) attn_fa(const __grid_constant__ AttnArgs a) {
+    pdl_trigger();
+    extern __shared__ __align__(16) uint8_t smem[];
+    constexpr int R = fa_row<HD>(), NT = HD / 8;  // dim n-tiles of O
+    uint16_t *qs = (uint16_t *)smem;                 // [term][G][16][R]
+    uint16_t *sk0 = qs + kFaTerms * G * kFaQ * R;    // [2 stages][K | V][64][R]
+    const int kvh = blockIdx.y, w = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+    pdl_wait();
+    int t0, nq;
+    if (a.qblk) {
+        t0 = a.qblk[2 * blockIdx.x];
+        nq = a.qblk[2 * blockIdx.x + 1];
+    } else {
+        t0 = blockIdx.x * kFaQ;
+        nq = min(kFaQ, a.nt - t0);
+    }
+    const int pos0 = attn_tok_pos(a, t0);  // the block's positions are pos0 .. pos0 + nq - 1
+    const long long kvo = attn_tok_kv(a, t0);
+    const int kend = pos0 + nq;
+    const int head = kvh * G + w;
+    // q rows of this warp's head -> bf16 terms (rows past nq repeat the last token)
+    for (int i = lane; i < kFaQ * HD / 2; i += 32) {
+        const int r = i / (HD / 2), d = (i % (HD / 2)) * 2;
+        const int t = t0 + min(r, nq - 1);
+        const float2 v = *(const float2 *)(a.qkv + (size_t)t * a.qkv_ld + head * HD + d);
+        uint32_t tt[kFaTerms];
+        fa_split(v.x, v.y, tt);
+#pragma unroll
+        for (int x = 0; x < kFaTerms; x++) *(uint32_t *)(qs + ((size_t)(x * G + w) * kFaQ + r) * R + d) = tt[x];
+    }
+    const uint16_t *Kg = a.kc + kvo + kvh * HD, *Vg = a.vc + kvo + kvh * HD;
+    const int ntiles = (kend + kFaK - 1) / kFaK;
+    fa_stage<HD, G>(Kg, Vg, a.kvdim, 0, kend, sk0, sk0 + kFaK * R);
+    const int qp0 = pos0 + min(g, nq - 1), qp1 = pos0 + min(g + 8, nq - 1);  // positions of rows g, g + 8
+    float o[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; j++) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    const float scale = a.scale;
+    for (int kt = 0; kt < ntiles; kt++) {
+        uint16_t *sk = sk0 + (size_t)(kt & 1) * 2 * kFaK * R, *sv = sk + kFaK * R;
+        if (kt + 1 < ntiles) {
+            uint16_t *nk = sk0 + (size_t)((kt + 1) & 1) * 2 * kFaK * R;
+            fa_stage<HD, G>(Kg, Vg, a.kvdim, (kt + 1) * kFaK, kend, nk, nk + kFaK * R);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        // S = q . K^T for 64 keys: 8 key n-tiles x HD/16 k-steps, hi and lo
+        float s[8][4];
+#pragma unroll
+        for (int j = 0; j < 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; kk++) {
+            const int ro = ((lane >> 3) & 1) * 8 + (lane & 7), co = kk * 16 + (lane >> 4) * 8;
+            uint32_t aq[kFaTerms][4];
+#pragma unroll
+            for (int x = 0; x < kFaTerms; x++) fa_ldm4(aq[x], qs + ((size_t)(x * G + w) * kFaQ + ro) * R + co);
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const uint16_t *kr = sk + (j * 8 + g) * R + kk * 16 + 2 * tq;
+                const uint32_t b0 = *(const uint32_t *)kr, b1 = *(const uint32_t *)(kr + 8);
+#pragma unroll
+                for (int x = kFaTerms - 1; x >= 0; x--) fa_mma(s[j], aq[x], b0, b1);  // small terms first
+            }
+        }
+        // online softmax over this tile (rows g and g + 8 of the warp)
+        const int kb = kt * kFaK;
+        float tm0 = -INFINITY, tm1 = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int key = kb + j * 8 + 2 * tq;
+            s[j][0] = key <= qp0 ? s[j][0] * scale : -INFINITY;
+            s[j][1] = key + 1 <= qp0 ? s[j][1] * scale : -INFINITY;
+            s[j][2] = key <= qp1 ? s[j][2] * scale : -INFINITY;
+            s[j][3] = key + 1 <= qp1 ? s[j][3] * scale : -INFINITY;
+            tm0 = fmaxf(tm0, fmaxf(s[j][0], s[j][1]));
+            tm1 = fmaxf(tm1, fmaxf(s[j][2], s[j][3]));
+        }
+        tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, 1));
+        tm0 = fmaxf(tm0, __shfl_xor_sync(0xffffffffu, tm0, 2));
+        tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, 1));
+        tm1 = fmaxf(tm1, __shfl_xor_sync(0xffffffffu, tm1, 2));
+        const float mn0 = fmaxf(m0, tm0), mn1 = fmaxf(m1, tm1);  // finite: key 0 is always visible
+        const float c0 = expf(m0 - mn0), c1 = expf(m1 - mn1);
+        m0 = mn0;
+        m1 = mn1;
+        l0 *= c0;
+        l1 *= c1;
+#pragma unroll
+        for (int j = 0; j < NT; j++) {
+            o[j][0] *= c0;
+            o[j][1] *= c0;
+            o[j][2] *= c1;
+            o[j][3] *= c1;
+        }
+        // P (hi / lo) as A fragments, then O += P . V over 4 key k-steps
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+            float p[8];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int j = 2 * kk + u;
+                p[4 * u + 0] = expf(s[j][0] - mn0);
+                p[4 * u + 1] = expf(s[j][1] - mn0);
+                p[4 * u + 2] = expf(s[j][2] - mn1);
+                p[4 * u + 3] = expf(s[j][3] - mn1);
+                l0 += p[4 * u + 0] + p[4 * u + 1];
+                l1 += p[4 * u + 2] + p[4 * u + 3];
+            }
+            uint32_t pa[kFaTerms][4], tt[kFaTerms];
+            // A fragment order: row g keys 2t | row g+8 keys 2t | row g keys 8+2t | row g+8 keys 8+2t
+#pragma unroll
+            for (int f = 0; f < 4; f++) {
+                fa_split(p[2 * f], p[2 * f + 1], tt);
+#pragma unroll
+                for (int x = 0; x < kFaTerms; x++) pa[x][f] = tt[x];
+            }
+#pragma unroll
+            for (int j = 0; j < NT; j += 2) {
+                // V rows kk*16 .. +15, dims 8j .. 8j + 15: four transposed 8x8 matrices
+                const int vr = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8, vc = j * 8 + (lane >> 4) * 8;
+                uint32_t b[4];
+                fa_ldm4t(b, sv + vr * R + vc);
+#pragma unroll
+                for (int x = kFaTerms - 1; x >= 0; x--) {
+                    fa_mma(o[j], pa[x], b[0], b[1]);
+                    fa_mma(o[j + 1], pa[x], b[2], b[3]);
+                }
+            }
+        }
+        __syncthreads();  // the stage is refilled next
+    }
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+#pragma unroll
+    for (int j = 0; j < NT; j++) {
+        const int d = j * 8 + 2 * tq;
+        if (g < nq) *(float2 *)(a.ao + (size_t)(t0 + g) * a.qdim + head * HD + d) = make_float2(o[j][0] * i0, o[j][1] * i0);
+        if (g + 8 < nq)
+            *(float2 *)(a.ao + (size_t)(t0 + g + 8) * a.qdim + head * HD + d) = make_float2(o[j][2] * i1, o[j][3] * i1);
+    }
 }
 
 }  // namespace hyk

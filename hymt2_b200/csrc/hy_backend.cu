@@ -271,9 +271,19 @@ void init_kernel_attrs() {
     set_smem(attn_chunk_kernel<64, 2>);
     set_smem(attn_chunk_kernel<64, 4>);
     set_smem(attn_chunk_kernel<64, 8>);
-    set_smem(tc_gemm<1>, tc_smem_bytes(1));
-    set_smem(tc_gemm<2>, tc_smem_bytes(2));
-    set_smem(tc_gemm<3>, tc_smem_bytes(3));
+    set_smem(attn_fa<128, 1>, fa_smem<128, 1>());
+    set_smem(attn_fa<128, 2>, fa_smem<128, 2>());
+    set_smem(attn_fa<128, 4>, fa_smem<128, 4>());
+    set_smem(attn_fa<128, 8>, fa_smem<128, 8>());
+    set_smem(attn_fa<64, 1>, fa_smem<64, 1>());
+    set_smem(attn_fa<64, 2>, fa_smem<64, 2>());
+    set_smem(attn_fa<64, 4>, fa_smem<64, 4>());
+    set_smem(attn_fa<64, 8>, fa_smem<64, 8>());
+    set_smem(tc_gemm<1, 256>, tc_smem_bytes(1, 256));
+    set_smem(tc_gemm<1, 64>, tc_smem_bytes(1, 64));
+    set_smem(tc_gemm<2, 128>, tc_smem_bytes(2, 128));
+    set_smem(tc_gemm<2, 64>, tc_smem_bytes(2, 64));
+    set_smem(tc_gemm<3, 64>, tc_smem_bytes(3, 64));
 }
 
 // One launch for nt <= NT tokens.
@@ -457,12 +467,18 @@ bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float
         ta.nb = nb;
         ta.epi = epi;
         ta.err = c->d_tcerr;
-        const int P = tc_planes(ws[i]->fmt), ntiles = tc_tiles(P, nt, ws[i]->n);
-        const dim3 grid(ntiles < c->nsm ? ntiles : c->nsm);
+        // MMA rows: the whole weight tile, or 64-row slices of it when the
+        // whole tiles would leave SMs idle
+        const int P = tc_planes(ws[i]->fmt);
+        const int NM = tc_tiles(P, tc_n(P), nt, ws[i]->n) >= c->nsm ? tc_n(P) : 64;
+        const int ntiles = tc_tiles(P, NM, nt, ws[i]->n);
+        const dim3 grid(ntiles < c->nsm ? ntiles : c->nsm), blk(kTcThreads);
         bool ok;
-        if (P == 1) ok = launch(c, tc_gemm<1>, grid, dim3(kTcThreads), tc_smem_bytes(1), false, ta);
-        else if (P == 2) ok = launch(c, tc_gemm<2>, grid, dim3(kTcThreads), tc_smem_bytes(2), false, ta);
-        else ok = launch(c, tc_gemm<3>, grid, dim3(kTcThreads), tc_smem_bytes(3), false, ta);
+        if (P == 1 && NM == 256) ok = launch(c, tc_gemm<1, 256>, grid, blk, tc_smem_bytes(1, 256), false, ta);
+        else if (P == 1) ok = launch(c, tc_gemm<1, 64>, grid, blk, tc_smem_bytes(1, 64), false, ta);
+        else if (P == 2 && NM == 128) ok = launch(c, tc_gemm<2, 128>, grid, blk, tc_smem_bytes(2, 128), false, ta);
+        else if (P == 2) ok = launch(c, tc_gemm<2, 64>, grid, blk, tc_smem_bytes(2, 64), false, ta);
+        else ok = launch(c, tc_gemm<3, 64>, grid, blk, tc_smem_bytes(3, 64), false, ta);
         if (!ok) return false;
     }
     return true;
@@ -497,7 +513,10 @@ bool attn_launch(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
     int warps = aa.heads + aa.kv_heads;
     if (warps > 32) warps = 32;
     if (!launch(c, rope_norm_store<HD>, dim3(nt), dim3(warps * 32), 0, pdl, aa)) return false;
-    return launch(c, attn_prefill<HD, G>, dim3(aa.kv_heads, nt), dim3(G * 32), 0, pdl, aa);
+    const int nqb = aa.qblk ? aa.nqb : (nt + kFaQ - 1) / kFaQ;
+    if (nqb == nt)  // one token per sequence (a batch of decode steps): the per-token kernel is faster
+        return launch(c, attn_prefill<HD, G>, dim3(aa.kv_heads, nt), dim3(G * 32), 0, pdl, aa);
+    return launch(c, attn_fa<HD, G>, dim3(nqb, aa.kv_heads), dim3(G * 32), fa_smem<HD, G>(), pdl, aa);
 }
 
 bool attention(HyCtx *c, const AttnArgs &aa_in, int nt, bool pdl) {
@@ -533,6 +552,8 @@ struct Fwd {
     int kv_ctx;
     const int *pos_ptr;
     const int *tok_pos, *tok_slot;
+    const int *qblk;              // batch: attention query blocks (first token, count)
+    int nqb;
 };
 
 Fwd fwd_single(HyCtx *c, const int *pos_ptr) {
@@ -637,6 +658,8 @@ bool layer_forward(HyCtx *c, const Fwd &f, int li, int nt, bool pdl) {
         aa.tok_pos = f.tok_pos;
         aa.tok_slot = f.tok_slot;
         aa.slot_stride = f.slot_stride;
+        aa.qblk = f.qblk;
+        aa.nqb = f.nqb;
         aa.nt = nt;
         aa.heads = c->heads;
         aa.kv_heads = c->kvh;

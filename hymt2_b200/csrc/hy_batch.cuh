@@ -25,8 +25,10 @@ struct Batch {
     int slots = 0, slot_ctx = 0, max_tokens = 0, max_out = 0;
     uint16_t *kv = nullptr;
     float *h = nullptr, *qkv = nullptr, *ao = nullptr, *g = nullptr, *u = nullptr;
-    int *d_in = nullptr;   // tok [max_tokens] | slot [max_tokens] | pos [max_tokens] | rows [max_out]
+    // tok [max_tokens] | slot [max_tokens] | pos [max_tokens] | rows [max_out] | qblk [2 max_tokens]
+    int *d_in = nullptr;
     int *h_in = nullptr;   // pinned staging of d_in
+    int nqb = 0;           // attention query blocks of the uploaded pass
     float *sel = nullptr;  // [max_out][H] residual rows for the head
     float *logits = nullptr;  // [max_out][vocab]
     int *d_ids = nullptr, *h_ids = nullptr;
@@ -37,6 +39,8 @@ struct Batch {
     int *slot() const { return d_in + max_tokens; }
     int *pos() const { return d_in + 2 * max_tokens; }
     int *rows() const { return d_in + 3 * max_tokens; }
+    size_t qblk_off() const { return (size_t)3 * max_tokens + max_out; }
+    size_t in_ints() const { return (size_t)5 * max_tokens + max_out; }
 };
 
 // ---------------------------------------------------------------- kernels
@@ -131,8 +135,8 @@ bool batch_prepare(HyCtx *c, int slots, int slot_ctx, int max_tokens, int max_ou
     CK(c, cudaMalloc(&b->ao, T * c->qd * 4));
     CK(c, cudaMalloc(&b->g, T * c->F * 4));
     CK(c, cudaMalloc(&b->u, T * c->F * 4));
-    CK(c, cudaMalloc(&b->d_in, (3 * T + max_out) * 4));
-    CK(c, cudaMallocHost(&b->h_in, (3 * T + max_out) * 4));
+    CK(c, cudaMalloc(&b->d_in, b->in_ints() * 4));
+    CK(c, cudaMallocHost(&b->h_in, b->in_ints() * 4));
     CK(c, cudaMalloc(&b->sel, (size_t)max_out * c->H * 4));
     CK(c, cudaMalloc(&b->logits, (size_t)max_out * c->outw->n * 4));
     CK(c, cudaMalloc(&b->d_ids, (size_t)max_out * 4));
@@ -157,18 +161,40 @@ Fwd fwd_batch(HyCtx *c) {
     f.kv_ctx = b.slot_ctx;
     f.tok_pos = b.pos();
     f.tok_slot = b.slot();
+    f.qblk = b.d_in + b.qblk_off();
+    f.nqb = b.nqb;
     return f;
 }
 
 // Upload nt tokens (tok / slot / pos) and nout head rows from the pinned
-// staging area (filled by the caller at the same offsets as on the device).
+// staging area (filled by the caller at the same offsets as on the device),
+// with the attention query blocks: runs of <= kFaQ tokens of one slot at
+// consecutive positions.
 bool batch_upload(HyCtx *c, int nt, int nout) {
     Batch &b = *c->bat;
     const size_t T = (size_t)b.max_tokens;
+    const int *slot = b.h_in + T, *pos = b.h_in + 2 * T;
+    int *qb = b.h_in + b.qblk_off();
+    int nqb = 0;
+    for (int t = 0; t < nt; t++) {
+        if (nqb > 0) {
+            int *blk = qb + 2 * (nqb - 1);
+            const int last = blk[0] + blk[1] - 1;
+            if (blk[1] < kFaQ && slot[t] == slot[last] && pos[t] == pos[last] + 1) {
+                blk[1]++;
+                continue;
+            }
+        }
+        qb[2 * nqb] = t;
+        qb[2 * nqb + 1] = 1;
+        nqb++;
+    }
+    b.nqb = nqb;
     for (int part = 0; part < 3; part++)
         CK(c, cudaMemcpyAsync(b.d_in + part * T, b.h_in + part * T, (size_t)nt * 4, cudaMemcpyHostToDevice, c->st));
     if (nout > 0)
         CK(c, cudaMemcpyAsync(b.rows(), b.h_in + 3 * T, (size_t)nout * 4, cudaMemcpyHostToDevice, c->st));
+    CK(c, cudaMemcpyAsync(b.d_in + b.qblk_off(), qb, (size_t)nqb * 8, cudaMemcpyHostToDevice, c->st));
     return true;
 }
 

@@ -1,5 +1,6 @@
 // hy_common.cuh — shared device helpers for the hymt2 sm_100a backend.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>

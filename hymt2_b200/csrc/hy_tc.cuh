@@ -58,12 +58,15 @@ __host__ __device__ constexpr int tc_n(int P) { return P == 1 ? 256 : (P == 2 ? 
 __host__ __device__ constexpr int tc_bbytes(int P) { return P * tc_n(P) * kTcKB; }
 // Bytes of one (tile, block) of the tiled scales: ws1[N] then ws2[N].
 __host__ __device__ constexpr int tc_sbytes(int P) { return 2 * tc_n(P) * 4; }
-// One stage: the A half (128 x 128) and the B half (P planes of N x 128).
-__host__ __device__ constexpr int tc_stage_bytes(int P) { return kTcABytes / 2 + tc_bbytes(P) / 2; }
-__host__ __device__ inline size_t tc_smem_bytes(int P) {
-    return (size_t)kTcStages * tc_stage_bytes(P) + (size_t)kTcScaleSlots * tc_sbytes(P) + 1024;
+// One stage: the A half (128 x 128) and the B half (P planes of NM x 128).
+__host__ __device__ constexpr int tc_stage_bytes(int P, int NM) { return kTcABytes / 2 + P * NM * kTcKH; }
+// One scale-ring entry: ws1[NM], ws2[NM], then the 128 activation scales.
+__host__ __device__ constexpr int tc_slot_bytes(int NM) { return 2 * NM * 4 + kTcM * 4; }
+__host__ __device__ inline size_t tc_smem_bytes(int P, int NM) {
+    return (size_t)kTcStages * tc_stage_bytes(P, NM) + (size_t)kTcScaleSlots * tc_slot_bytes(NM) + 1024;
 }
-static_assert(4 * (kTcABytes / 2 + 256 * kTcKB / 2) + 4 * 2 * 256 * 4 + 1024 <= 227 * 1024, "tc stages exceed shared memory");
+static_assert(4 * (kTcABytes / 2 + 256 * kTcKH) + 4 * (2 * 256 * 4 + kTcM * 4) + 1024 <= 227 * 1024,
+              "tc stages exceed shared memory");
 // Planes of a device weight format (0: not on the tensor-core path).
 __host__ __device__ constexpr int tc_planes(int fmt) {
     return fmt == FMT_PANEL ? 1 : (fmt == FMT_Q6K ? 2 : (fmt == FMT_Q4K ? 3 : 0));
@@ -82,7 +85,7 @@ __host__ __device__ inline size_t tc_wtile_off(int P, int p, int r, int k) {
 
 struct TcArgs {
     const int8_t *a;   // tiled activations [ceil(T/128)][nb][128 x 256]
-    const float *ad;   // activation block scales [T_pad][nb]
+    const float *ad;   // activation block scales [ceil(T/128)][nb][128]
     const int8_t *w;   // tiled weight [ceil(N/n)][nb][2][P][n x 128]
     const float *ws;   // tiled weight scales [ceil(N/n)][nb][2][n]
     float *out;        // [T][ldo]
@@ -91,9 +94,9 @@ struct TcArgs {
     int *err;          // set on a bounded-wait timeout
 };
 
-// Number of (m, n) tiles of a GEMM.
-__host__ __device__ inline int tc_tiles(int P, int T, int N) {
-    return ((T + kTcM - 1) / kTcM) * ((N + tc_n(P) - 1) / tc_n(P));
+// Number of (m, n) tiles of a GEMM whose MMAs cover NM weight rows.
+__host__ __device__ inline int tc_tiles(int P, int NM, int T, int N) {
+    return ((T + kTcM - 1) / kTcM) * ((N + tc_n(P) - 1) / tc_n(P)) * (tc_n(P) / NM);
 }
 
 __device__ __forceinline__ uint32_t tc_smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -186,18 +189,21 @@ __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sy
 __device__ __forceinline__ float tc_magic(uint32_t v) { return __int_as_float((int)(v + 0x4B400000u)); }
 constexpr float kTcMagic = 12582912.0f;  // 1.5 * 2^23
 
-template <int P>
+// P planes; MMAs of NM weight rows, a slice of the N = tc_n(P) rows of
+// each weight tile (NM < N gives small token counts more CTAs).
+template <int P, int NM>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__ TcArgs a) {
-    constexpr int N = tc_n(P), C = N / 4, BH = tc_bbytes(P) / 2, AH = kTcABytes / 2, SB = tc_sbytes(P);
-    constexpr int STB = tc_stage_bytes(P);
+    constexpr int N = tc_n(P), SUB = N / NM, C = NM / 4, AH = kTcABytes / 2, SB = tc_sbytes(P);
+    constexpr int STB = tc_stage_bytes(P, NM), SLB = tc_slot_bytes(NM);
+    static_assert(N % NM == 0 && NM % 64 == 0, "MMA rows must be a slice of the weight tile");
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], sfull[kTcScaleSlots], sempty[kTcScaleSlots],
         accf[2], acce[2], fin;
     __shared__ uint32_t s_tmem;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nb = a.nb, ntm = (a.T + kTcM - 1) / kTcM, ntiles = tc_tiles(P, a.T, a.N);
+    const int nb = a.nb, ntm = (a.T + kTcM - 1) / kTcM, ntiles = tc_tiles(P, NM, a.T, a.N);
     uint8_t *stage = (uint8_t *)(((uintptr_t)smem + 1023) & ~(uintptr_t)1023);
-    uint8_t *scales = stage + (size_t)kTcStages * STB;
+    uint8_t *slots = stage + (size_t)kTcStages * STB;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kTcStages; s++) {
             tc_mbar_init(&full[s], 1);
@@ -225,19 +231,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
     const uint32_t tmem = s_tmem;
     bool ok = true;
     if (warp == 0) {
-        // producer: per block its scales, then two half-block stages
+        // producer: per block its scales (weight slice, then activations),
+        // then two half-block stages (A half, B planes of the slice)
         if (lane == 0) {
             int g = 0, hs = 0;  // blocks and half blocks issued by this CTA
             for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-                const int mt = tile % ntm, nt = tile / ntm;
+                const int mt = tile % ntm, ns = tile / ntm, nt = ns / SUB, si = ns % SUB;
                 for (int kb = 0; kb < nb && ok; kb++, g++) {
                     const int sl = g % kTcScaleSlots, su = g / kTcScaleSlots;
                     if (su > 0 && !tc_mbar_wait(&sempty[sl], (su - 1) & 1)) {
                         ok = false;
                         break;
                     }
-                    tc_mbar_expect(&sfull[sl], SB);
-                    tc_bulk(scales + (size_t)sl * SB, (const uint8_t *)a.ws + ((size_t)nt * nb + kb) * SB, SB, &sfull[sl]);
+                    uint8_t *sd = slots + (size_t)sl * SLB;
+                    const uint8_t *ws = (const uint8_t *)a.ws + ((size_t)nt * nb + kb) * SB + (size_t)si * NM * 4;
+                    tc_mbar_expect(&sfull[sl], SLB);
+                    tc_bulk(sd, ws, NM * 4, &sfull[sl]);
+                    tc_bulk(sd + NM * 4, ws + N * 4, NM * 4, &sfull[sl]);
+                    tc_bulk(sd + 2 * NM * 4, a.ad + ((size_t)mt * nb + kb) * kTcM, kTcM * 4, &sfull[sl]);
                     for (int h = 0; h < 2 && ok; h++, hs++) {
                         const int s = hs % kTcStages, use = hs / kTcStages;
                         if (use > 0 && !tc_mbar_wait(&empty[s], (use - 1) & 1)) {
@@ -247,7 +258,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                         uint8_t *st = stage + (size_t)s * STB;
                         tc_mbar_expect(&full[s], STB);
                         tc_bulk(st, a.a + ((size_t)mt * nb + kb) * kTcABytes + (size_t)h * AH, AH, &full[s]);
-                        tc_bulk(st + AH, a.w + ((size_t)nt * nb + kb) * tc_bbytes(P) + (size_t)h * BH, BH, &full[s]);
+                        const int8_t *wb = a.w + ((size_t)nt * nb + kb) * tc_bbytes(P) + (size_t)h * P * N * kTcKH;
+                        if constexpr (SUB == 1) {
+                            tc_bulk(st + AH, wb, P * N * kTcKH, &full[s]);
+                        } else {
+                            // the slice's 8-row groups of each 16-byte K chunk: NM * 16 contiguous bytes
+#pragma unroll
+                            for (int p = 0; p < P; p++)
+#pragma unroll
+                                for (int c = 0; c < kTcKH / 16; c++)
+                                    tc_bulk(st + AH + (size_t)(p * kTcKH / 16 + c) * NM * 16,
+                                            wb + (size_t)p * N * kTcKH + ((size_t)c * (N / 8) + si * (NM / 8)) * 128,
+                                            NM * 16, &full[s]);
+                        }
                     }
                 }
             }
@@ -256,7 +279,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
     } else if (warp == 1) {
         // MMA issuer: 4 x P MMAs (K = 32 each) per half block into accumulator set g % 2
         if (lane == 0) {
-            constexpr uint32_t idesc = tc_idesc(kTcM, N);
+            constexpr uint32_t idesc = tc_idesc(kTcM, NM);
             int g = 0, hs = 0;
             for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
                 for (int kb = 0; kb < nb && ok; kb++, g++) {
@@ -277,8 +300,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                         for (int k = 0; k < kTcKH / 32; k++)
 #pragma unroll
                             for (int p = 0; p < P; p++)
-                                tc_mma(tmem + (uint32_t)(buf * P * N + p * N), tc_desc(st, k, kTcM),
-                                       tc_desc(st + AH + p * N * kTcKH, k, N), idesc, (h | k) != 0);
+                                tc_mma(tmem + (uint32_t)(buf * P * NM + p * NM), tc_desc(st, k, kTcM),
+                                       tc_desc(st + AH + p * NM * kTcKH, k, NM), idesc, (h | k) != 0);
                         tc_commit(&empty[s]);
                     }
                     if (ok) tc_commit(&accf[buf]);
@@ -295,7 +318,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
         const int e = warp - 2, q = warp & 3, part = e >> 2;
         int g = 0;
         for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-            const int mt = tile % ntm, nt = tile / ntm;
+            const int mt = tile % ntm, ns = tile / ntm;
             const int t = mt * kTcM + q * 32 + lane;
             float acc[C];
 #pragma unroll
@@ -307,32 +330,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                     break;
                 }
                 tc_fence_after();
-                const float yd = t < a.T ? __ldg(a.ad + (size_t)t * nb + kb) : 0.f;
-                const float *ws1 = (const float *)(scales + (size_t)sl * SB) + part * C;
-                const float *ws2 = ws1 + N;
-                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * P * N + part * C);
-                // P = 1 reads 8 columns at a time: its 64 accumulators leave
+                const float *sd = (const float *)(slots + (size_t)sl * SLB);
+                const float yd = sd[2 * NM + q * 32 + lane];  // 0 past T (the quantiser pads with zeros)
+                const float4 *ws1 = (const float4 *)(sd + part * C), *ws2 = (const float4 *)(sd + NM + part * C);
+                const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * P * NM + part * C);
+                // P = 1 reads 8 columns at a time: its accumulators leave
                 // fewer registers for the loaded words
-                constexpr int CW = P == 1 ? 8 : 16;
+                constexpr int CW = (P == 1 && C > 16) ? 8 : 16;
 #pragma unroll
                 for (int c = 0; c < C / CW; c++) {
                     uint32_t r[P][CW];
 #pragma unroll
-                    for (int p = 0; p < P; p++) tc_ld<CW>(tbase + (uint32_t)(p * N + c * CW), r[p]);
+                    for (int p = 0; p < P; p++) tc_ld<CW>(tbase + (uint32_t)(p * NM + c * CW), r[p]);
                     tc_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < CW; j++) {
-                        const int n = c * CW + j;
-                        float v;
-                        if constexpr (P == 1) {
-                            // |S| <= 256 * 127 * 3 < 2^22; ws2 holds -1.5 * 2^23 * ws1 (exact: ws1 is an f16)
-                            v = fmaf(tc_magic(r[0][j]), ws1[n], ws2[n]);
-                        } else {
-                            const int s1 = (int)(r[0][j] << 6) + (int)r[1][j];
-                            v = (float)s1 * ws1[n];
-                            if constexpr (P == 3) v = fmaf(-(float)(int)r[2][j], ws2[n], v);
+                    for (int j4 = 0; j4 < CW / 4; j4++) {
+                        const float4 w1 = ws1[c * CW / 4 + j4];
+                        float4 w2 = make_float4(0.f, 0.f, 0.f, 0.f);
+                        if constexpr (P != 2) w2 = ws2[c * CW / 4 + j4];
+                        const float w1v[4] = {w1.x, w1.y, w1.z, w1.w}, w2v[4] = {w2.x, w2.y, w2.z, w2.w};
+#pragma unroll
+                        for (int jj = 0; jj < 4; jj++) {
+                            const int j = j4 * 4 + jj, n = c * CW + j;
+                            float v;
+                            if constexpr (P == 1) {
+                                // |S| <= 256 * 127 * 3 < 2^22; ws2 holds -1.5 * 2^23 * ws1 (exact: ws1 is an f16)
+                                v = fmaf(tc_magic(r[0][j]), w1v[jj], w2v[jj]);
+                            } else {
+                                const int s1 = (int)(r[0][j] << 6) + (int)r[1][j];
+                                v = (float)s1 * w1v[jj];
+                                if constexpr (P == 3) v = fmaf(-(float)(int)r[2][j], w2v[jj], v);
+                            }
+                            acc[n] = fmaf(v, yd, acc[n]);
                         }
-                        acc[n] = fmaf(v, yd, acc[n]);
                     }
                 }
                 tc_fence_before();
@@ -344,7 +374,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
             }
             if (ok && t < a.T) {
                 float *o = a.out + (size_t)t * a.ldo;
-                const int n0 = nt * N + part * C;
+                const int n0 = ns * NM + part * C;
                 if ((a.ldo & 3) == 0 && n0 + C <= a.N) {
 #pragma unroll
                     for (int j = 0; j < C; j += 4) {
@@ -461,7 +491,8 @@ __global__ void tc_weight_to_tiled(const __grid_constant__ WDesc w, int8_t *tw, 
     }
 }
 
-// Activation rows -> Q8_K, written as tiled int8 codes plus block scales.
+// Activation rows -> Q8_K, written as tiled int8 codes plus block scales
+// (tiled too: [m tile][block][128]).
 // One CTA (kGemvThreads) per token; the fp32 row is built by stage_fp32 (the
 // GEMV prologues: as is, RMSNorm*w, SiLU*up) and each 256 block quantised by
 // one warp with quantize_block_warp's arithmetic (bit-identical codes).
@@ -478,7 +509,7 @@ __global__ void __launch_bounds__(kGemvThreads) tc_quantize(const __grid_constan
         for (int b = warp; b < nb; b += kGemvThreads / 32) {
             int8_t *dst = ta + ((size_t)mt * nb + b) * kTcABytes + tc_tile_off(r, lane * 8, kTcM);
             *(uint2 *)dst = make_uint2(0, 0);
-            if (lane == 0) ad[(size_t)t * nb + b] = 0.f;
+            if (lane == 0) ad[((size_t)mt * nb + b) * kTcM + r] = 0.f;
         }
         return;
     }
@@ -518,7 +549,7 @@ __global__ void __launch_bounds__(kGemvThreads) tc_quantize(const __grid_constan
         const uint32_t lo = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
         const uint32_t hi = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
         *(uint2 *)(ta + ((size_t)mt * nb + b) * kTcABytes + tc_tile_off(r, lane * 8, kTcM)) = make_uint2(lo, hi);
-        if (lane == 0) ad[(size_t)t * nb + b] = d;
+        if (lane == 0) ad[((size_t)mt * nb + b) * kTcM + r] = d;
     }
 }
 
