@@ -18,6 +18,11 @@ flush is needed between steps.
                events; algorithmic bytes = every weight byte of a step plus
                the K/V rows attention reads, per step times steps per launch
   cpu_baseline the reference's CPU library on this host (rank 0, N = 1)
+  serving      config 3 on every GPU: 4096 requests sharded over the ranks,
+               continuous batching of <= 256 sequences per GPU (generated tok/s)
+  prefill_c2   config 2 (N = 1): 32 x 256-token Q4_K_M prefill on the tensor
+               cores, with its int8 roofline and the reference CPU prefill
+  decode_c1    config 1 (N = 1): Q2_0C bs1 decode after a 512-token prompt
 
 `--impl reference` times the reference's own CPU implementation of the path
 (oracle/_ref/libhymt2_ref.so, built from its sources) on the same config.
@@ -75,6 +80,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--graph-breakdown", action="store_true",
                    help="also time each kernel of the per-layer graph path alone")
+    p.add_argument("--serve-requests", type=int, default=4096, help="config-3 requests (all GPUs); 0 skips")
+    p.add_argument("--no-extra", action="store_true", help="skip the config 1 / config 2 lines (N = 1 only)")
     return p.parse_args()
 
 
@@ -128,6 +135,33 @@ class Clocks:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
+def int8_peak(torch) -> tuple[float, str]:
+    """Dense int8 TOPS of this GPU: cuBLASLt int8 GEMM (torch._int_mm, 8192^3,
+    best of 5); 2x the measured bf16 figure if that is unavailable."""
+    try:
+        n = 8192
+        a = torch.randint(-127, 127, (n, n), dtype=torch.int8, device="cuda")
+        b = torch.randint(-127, 127, (n, n), dtype=torch.int8, device="cuda").t().contiguous().t()
+        torch._int_mm(a, b)
+        best = None
+        for _ in range(5):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            torch.cuda.synchronize()
+            t = e0.elapsed_time(e1)
+            best = t if best is None else min(best, t)
+        del a, b
+        return 2 * n ** 3 / (best / 1e3) / 1e12, "measured (torch._int_mm 8192^3 burst)"
+    except Exception:  # noqa: BLE001
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                return 2 * float(json.load(f)["bf16_tflops"]), "2x measured bf16"
+        except (OSError, KeyError, ValueError):
+            return 2 * 1590.0, "2x fallback bf16"
+
+
 def ensure_model(rank, local, world, model_dir, dist):
     from hymt2_b200 import synth
     if world > 1 and local != 0:
@@ -168,6 +202,184 @@ def cpu_baseline(path: str, ntok: int) -> dict:
             "isa": ref.isa(), "cpu": cpu,
             "sample": f"reference hymt2 CPU path (oracle/_ref, {ref.isa()}, {threads} threads): 48-token prompt "
                       f"prefill ({pre_ms:.0f} ms) then {ntok} greedy decode tokens at positions 48..{47 + ntok}"}
+
+
+SERVE_PREFIX, SERVE_MAX_NEW, SERVE_SLOTS, SERVE_STEP_TOKENS = 24, 64, 256, 512
+
+
+def serve_requests(n: int) -> list[list[int]]:
+    """Config 3 requests: lengths uniform in [16, 128]; the first min(len, 24)
+    ids are one shared prefix, the rest uniform over the vocab (seed 3)."""
+    rng = np.random.default_rng(3)
+    prefix = rng.integers(0, VOCAB, SERVE_PREFIX).tolist()
+    out = []
+    for _ in range(n):
+        ln = int(rng.integers(16, 129))
+        k = min(ln, SERVE_PREFIX)
+        out.append(prefix[:k] + rng.integers(0, VOCAB, ln - k).tolist())
+    return out
+
+
+def bench_serving(dm, stream, torch, rank, world, nreq, max_over_ranks, barrier) -> dict:
+    """Config 3 on this rank's shard (requests r, r + N, ...): continuous
+    batching over 256 slots, 64 greedy tokens per request, device-timed
+    around the whole serve call (host scheduling included)."""
+    reqs = serve_requests(nreq)[rank::world]
+    dm.batch_prepare(slots=SERVE_SLOTS, slot_ctx=128 + SERVE_MAX_NEW, max_tokens=SERVE_STEP_TOKENS,
+                     max_out=SERVE_SLOTS)
+    dm.serve(reqs[:min(len(reqs), 300)], 4, SERVE_STEP_TOKENS)  # warm-up: tensor-core weight tiles, clocks
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record(stream)
+    out, st = dm.serve(reqs, SERVE_MAX_NEW, SERVE_STEP_TOKENS)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    total_gen = SERVE_MAX_NEW * nreq
+    return {"value": round(total_gen / (ms / 1e3), 1), "unit": "generated tok/s", "n_gpus": world,
+            "requests": nreq, "requests_per_gpu": len(reqs), "max_new": SERVE_MAX_NEW, "slots_per_gpu": SERVE_SLOTS,
+            "step_token_budget": SERVE_STEP_TOKENS, "ms": round(ms, 2), "wall_s_rank0": round(wall, 3),
+            "steps_rank0": st["steps"], "prefill_tokens_rank0": st["prefill_tokens"],
+            "prefix_hits_rank0": st["prefix_hits"], "prefix_tokens_rank0": st["prefix_tokens"],
+            "tokens_per_s_incl_prefill": round((st["decode_tokens"] + st["prefill_tokens"]) * world / (ms / 1e3), 1),
+            "workload": "c3: c0_stq model, 4096 requests (prompt U[16,128] ids with a shared 24-token prefix), "
+                        "64 greedy tokens each, continuous batching <= 256 sequences per GPU, requests sharded "
+                        "round-robin over the GPUs with no collective; time = max over ranks"}
+
+
+C2_SEQS, C2_LEN = 32, 256
+INT8_OPS_PER_TOKEN = 2 * 1_543_503_872          # layer int8 MACs x 2 per token (c2 shapes)
+HEAD_OPS_PER_SEQ = 2 * VOCAB * H                # the LM head runs on each sequence's last token
+
+
+def ref_prefill_cpu(path: str, ntok: int) -> dict:
+    """Reference CPU prefill of one ntok-token prompt (all physical cores)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    os.environ["HYMT2_DEVICE"] = "cpu"
+    ref = O.Reference()
+    cores = int(ref.lib.refh_physical_cores())
+    m = ref.load(path, threads=cores, ctx=ntok + 8)
+    try:
+        ids = np.random.default_rng(2).integers(0, VOCAB, ntok).tolist()
+        _, _, pre_ms, _, _ = m.greedy(ids, 1)
+        threads = m.threads()
+    finally:
+        m.close()
+    return {"value": round(ntok / (pre_ms / 1e3), 2), "unit": "prefill tok/s", "cores": threads,
+            "kind": "reference", "sample": f"reference CPU ({ref.isa()}, {threads} threads): one {ntok}-token "
+                                           f"prompt prefill (its 16-token chunks), {pre_ms:.0f} ms"}
+
+
+def bench_prefill(args, be, torch, tops, tops_kind) -> dict:
+    """Config 2: 32 independent sequences x 256 seeded ids (seed 2) through
+    one ragged batch pass each (all 8192 tokens in every GEMM, LM head +
+    argmax on each sequence's last token), CUDA events over 5 passes."""
+    from hymt2_b200 import synth
+    from hymt2_b200.device import DeviceModel
+    path = synth.ensure("c2_q4km", args.model_dir)
+    dm = DeviceModel(path, be, ctx=C2_LEN)
+    try:
+        rng = np.random.default_rng(2)
+        toks = rng.integers(0, VOCAB, C2_SEQS * C2_LEN)
+        slots = np.repeat(np.arange(C2_SEQS), C2_LEN)
+        pos = np.tile(np.arange(C2_LEN), C2_SEQS)
+        rows = np.arange(C2_SEQS) * C2_LEN + C2_LEN - 1
+        dm.batch_prepare(slots=C2_SEQS, slot_ctx=C2_LEN, max_tokens=C2_SEQS * C2_LEN, max_out=C2_SEQS)
+        stream = torch.cuda.ExternalStream(be.stream())
+        for _ in range(3):
+            dm.batch_forward(toks, slots, pos, rows)
+        n = 5
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(n):
+            dm.batch_forward(toks, slots, pos, rows)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / n
+        ntok = C2_SEQS * C2_LEN
+        ops = INT8_OPS_PER_TOKEN * ntok + HEAD_OPS_PER_SEQ * C2_SEQS
+        achieved = ops / (ms / 1e3) / 1e12
+        out = {"value": round(ntok / (ms / 1e3), 1), "unit": "prefill tok/s", "ms_per_pass": round(ms, 3),
+               "tokens_per_pass": ntok,
+               "workload": "c2_q4km (Q4_K q/k/o/gate/up, Q6_K v/down/head): 32 sequences x 256 seeded ids, one "
+                           "ragged pass (every projection one tcgen05 int8 GEMM over 8192 tokens), head + argmax on "
+                           "each last token; host ids in, host ids out, synchronous",
+               "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(tops, 1),
+                            "unit": "TOPS (int8, useful ops)", "frac": round(achieved / tops, 4),
+                            "peak_kind": tops_kind, "ops_per_pass": ops,
+                            "note": "Q4_K weights run as 3 exact int8 planes and Q6_K as 2, so the tensor pipe "
+                                    "does ~2.7x the useful ops"}}
+        if not args.no_cpu_baseline:
+            try:
+                out["cpu_baseline"] = ref_prefill_cpu(path, C2_LEN)
+            except Exception as e:  # noqa: BLE001
+                out["cpu_baseline"] = {"unavailable": str(e)}
+        return out
+    finally:
+        dm.close()
+
+
+C1_PROMPT, C1_GEN = 512, 128
+
+
+def bench_c1(args, be, torch, peak) -> dict:
+    """Config 1: Q2_0C layers, bs1 greedy decode of 128 tokens after a
+    512-token seeded prompt (seed 1); CUDA events over the 127 decode steps."""
+    from hymt2_b200 import synth
+    from hymt2_b200.device import DeviceModel
+    path = synth.ensure("c1_q2c", args.model_dir)
+    dm = DeviceModel(path, be, ctx=1024)
+    try:
+        lib, impl = be.lib, be.impl
+        ids = np.random.default_rng(1).integers(0, VOCAB, C1_PROMPT).astype(np.int32)
+        stream = torch.cuda.ExternalStream(be.stream())
+        for _ in range(2):
+            if lib.hyc_decode_begin(impl, ids.ctypes.data, C1_PROMPT, 0, C1_GEN, None, 0, dm.vocab_out) != 0:
+                raise RuntimeError("decode_begin: " + be.error())
+            be.sync()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            if lib.hyc_decode_steps(impl, C1_GEN - 1) != 0:
+                raise RuntimeError("decode_steps: " + be.error())
+            e1.record(stream)
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        out_ids = np.zeros(C1_GEN, dtype=np.int32)
+        if lib.hyc_decode_read(impl, out_ids.ctypes.data, C1_GEN) != C1_GEN:
+            raise RuntimeError("decode_read: " + be.error())
+        # bytes per step: Q2_0C panel weights (same 68 B / 256 as STQ1_0) + Q6_K head + K/V rows at mean position
+        kv = L * 2 * (C1_PROMPT + (C1_GEN - 1) / 2) * KVD * 2
+        step_bytes = STEP_WEIGHT_BYTES + kv
+        step_ms = ms / (C1_GEN - 1)
+        out = {"value": round((C1_GEN - 1) / (ms / 1e3), 1), "unit": UNIT, "ms_per_step": round(step_ms, 4),
+               "workload": "c1_q2c: Q2_0C layers (panel), Q6_K tied head; bs1 greedy decode, 512-token seeded "
+                           "prompt, 128 tokens (positions 512..639), persistent decode kernel",
+               "roofline_step": {"bytes_per_step": int(step_bytes),
+                                 "achieved_gbs": round(step_bytes / step_ms / 1e6, 1),
+                                 "frac": round(step_bytes / step_ms / 1e6 / peak, 4)}}
+        if not args.no_cpu_baseline:
+            try:
+                sys.path.insert(0, os.path.join(ROOT, "oracle"))
+                import oracle as O
+                os.environ["HYMT2_DEVICE"] = "cpu"
+                ref = O.Reference()
+                cores = int(ref.lib.refh_physical_cores())
+                m = ref.load(path, threads=cores, ctx=1024)
+                _, _, pre_ms, dec_ms, _ = m.greedy(ids.tolist(), 9)
+                thr = m.threads()
+                m.close()
+                out["cpu_baseline"] = {"value": round(8 / (dec_ms / 1e3), 2), "unit": UNIT, "cores": thr,
+                                       "kind": "reference",
+                                       "sample": f"reference CPU ({ref.isa()}, {thr} threads): 512-token prompt "
+                                                 f"({pre_ms:.0f} ms), then 8 decode tokens"}
+            except Exception as e:  # noqa: BLE001
+                out["cpu_baseline"] = {"unavailable": str(e)}
+        return out
+    finally:
+        dm.close()
 
 
 def run_reference_arm(args, rank, world):
@@ -339,6 +551,11 @@ def main():
         if tj:  # per-step DRAM bytes of one ncu capture, scaled to a launch
             traffic = int(tj["dram_bytes_per_step"] * dk.get("steps_per_launch", 1))
 
+    # ---- config 3: continuous-batching serving on every GPU (bs256/GPU)
+    serving = None
+    if args.serve_requests > 0:
+        serving = bench_serving(dm, stream, torch, rank, world, args.serve_requests, max_over_ranks, barrier)
+
     if rank == 0:
         step_ms = ms / args.steps
         value = world * args.steps / (ms / 1e3)
@@ -370,8 +587,21 @@ def main():
                 out["cpu_baseline"] = cpu_baseline(path, args.cpu_tokens)
             except Exception as e:  # noqa: BLE001 - report, do not fail the GPU number
                 out["cpu_baseline"] = {"unavailable": str(e)}
-        print(json.dumps(out))
+        if serving:
+            serving["cpu_baseline_note"] = ("the reference serves one request at a time: its rate is the bs1 "
+                                            "cpu_baseline above")
+            out["serving"] = serving
     dm.close()
+    if rank == 0 and world == 1 and not args.no_extra:
+        tops, tops_kind = int8_peak(torch)
+        for key, fn in (("prefill_c2", lambda: bench_prefill(args, be, torch, tops, tops_kind)),
+                        ("decode_c1", lambda: bench_c1(args, be, torch, peak))):
+            try:
+                out[key] = fn()
+            except Exception as e:  # noqa: BLE001 - report, do not lose the headline
+                out[key] = {"unavailable": str(e)}
+    if rank == 0:
+        print(json.dumps(out))
     be.close()
     if dist:
         dist.barrier()
