@@ -443,7 +443,7 @@ bool tc_scratch(HyCtx *c, int K) {
 
 // nt tokens through up to three weights sharing one activation
 // prologue (pro.act / x / x2 / norm_w / eps, pro.k = K): one quantise launch
-// writing tiled Q8_K codes, then one tensor-core GEMM per weight; outs[i] is
+// writing tiled Q8_K codes, then one tensor-core GEMM per weight format; outs[i] is
 // [nt][lds[i]], stored (epi 0) or accumulated (epi 1).
 bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float *const *outs, const int *lds,
                int cnt, int epi) {
@@ -454,24 +454,33 @@ bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float
     if (!launch(c, tc_quantize, dim3(tpad), dim3(kGemvThreads), (size_t)(K + 64) * 4, false, pro, nt, c->d_tca,
                 c->d_tcad))
         return false;
+    // one persistent launch per weight format (the weights of a launch share the activation tiles)
+    bool done[kTcMaxW] = {false, false, false};
     for (int i = 0; i < cnt; i++) {
+        if (done[i]) continue;
+        const int P = tc_planes(ws[i]->fmt);
         TcArgs ta;
+        memset(&ta, 0, sizeof ta);
         ta.a = c->d_tca;
         ta.ad = c->d_tcad;
-        ta.w = ws[i]->tc_w;
-        ta.ws = ws[i]->tc_ws;
-        ta.out = outs[i];
-        ta.ldo = lds[i];
         ta.T = nt;
-        ta.N = ws[i]->n;
         ta.nb = nb;
         ta.epi = epi;
         ta.err = c->d_tcerr;
+        for (int j = i; j < cnt; j++) {
+            if (done[j] || tc_planes(ws[j]->fmt) != P) continue;
+            ta.w[ta.nw] = ws[j]->tc_w;
+            ta.ws[ta.nw] = ws[j]->tc_ws;
+            ta.out[ta.nw] = outs[j];
+            ta.ldo[ta.nw] = lds[j];
+            ta.N[ta.nw] = ws[j]->n;
+            ta.nw++;
+            done[j] = true;
+        }
         // MMA rows: the whole weight tile, or 64-row slices of it when the
         // whole tiles would leave SMs idle
-        const int P = tc_planes(ws[i]->fmt);
-        const int NM = tc_tiles(P, tc_n(P), nt, ws[i]->n) >= c->nsm ? tc_n(P) : 64;
-        const int ntiles = tc_tiles(P, NM, nt, ws[i]->n);
+        const int NM = tc_tiles_all(P, tc_n(P), ta) >= c->nsm ? tc_n(P) : 64;
+        const int ntiles = tc_tiles_all(P, NM, ta);
         const dim3 grid(ntiles < c->nsm ? ntiles : c->nsm), blk(kTcThreads);
         bool ok;
         if (P == 1 && NM == 256) ok = launch(c, tc_gemm<1, 256>, grid, blk, tc_smem_bytes(1, 256), false, ta);

@@ -45,8 +45,8 @@ namespace hyk {
 constexpr int kTcM = 128;       // tokens per tile (TMEM lanes)
 constexpr int kTcKB = 256;      // K per Q8_K block
 constexpr int kTcKH = 128;      // K per stage: half a block
-constexpr int kTcStages = 4;
-constexpr int kTcScaleSlots = 4;
+constexpr int kTcMaxStages = 8;      // half-block stages in flight (at most)
+constexpr int kTcSmemBudget = 226 * 1024;  // of 227 KB per block, leaving the static barriers room
 constexpr int kTcEpiWarps = 16;
 constexpr int kTcThreads = (2 + kTcEpiWarps) * 32;  // warp 0 producer, 1 MMA, 2.. epilogue
 constexpr int kTcABytes = kTcM * kTcKB;             // 32 KB
@@ -62,11 +62,18 @@ __host__ __device__ constexpr int tc_sbytes(int P) { return 2 * tc_n(P) * 4; }
 __host__ __device__ constexpr int tc_stage_bytes(int P, int NM) { return kTcABytes / 2 + P * NM * kTcKH; }
 // One scale-ring entry: ws1[NM], ws2[NM], then the 128 activation scales.
 __host__ __device__ constexpr int tc_slot_bytes(int NM) { return 2 * NM * 4 + kTcM * 4; }
-__host__ __device__ inline size_t tc_smem_bytes(int P, int NM) {
-    return (size_t)kTcStages * tc_stage_bytes(P, NM) + (size_t)kTcScaleSlots * tc_slot_bytes(NM) + 1024;
+// Stages: as many as the shared-memory budget holds (up to 8) next to a
+// scale ring with an entry per block in flight plus two.
+__host__ __device__ constexpr int tc_stages(int P, int NM) {
+    int s = kTcMaxStages;
+    while (s > 2 && s * tc_stage_bytes(P, NM) + (s / 2 + 2) * tc_slot_bytes(NM) + 1024 > kTcSmemBudget) s--;
+    return s;
 }
-static_assert(4 * (kTcABytes / 2 + 256 * kTcKH) + 4 * (2 * 256 * 4 + kTcM * 4) + 1024 <= 227 * 1024,
-              "tc stages exceed shared memory");
+__host__ __device__ constexpr int tc_slots(int P, int NM) { return tc_stages(P, NM) / 2 + 2; }
+__host__ __device__ inline size_t tc_smem_bytes(int P, int NM) {
+    return (size_t)tc_stages(P, NM) * tc_stage_bytes(P, NM) + (size_t)tc_slots(P, NM) * tc_slot_bytes(NM) + 1024;
+}
+static_assert(tc_stages(1, 256) >= 4 && tc_stages(3, 64) >= 4, "tc pipeline too shallow");
 // Planes of a device weight format (0: not on the tensor-core path).
 __host__ __device__ constexpr int tc_planes(int fmt) {
     return fmt == FMT_PANEL ? 1 : (fmt == FMT_Q6K ? 2 : (fmt == FMT_Q4K ? 3 : 0));
@@ -83,13 +90,17 @@ __host__ __device__ inline size_t tc_wtile_off(int P, int p, int r, int k) {
     return ((size_t)(k >> 7) * P + p) * N * kTcKH + tc_tile_off(r, k & 127, N);
 }
 
+constexpr int kTcMaxW = 3;  // weights of one launch (same format, same activation)
+
 struct TcArgs {
     const int8_t *a;   // tiled activations [ceil(T/128)][nb][128 x 256]
     const float *ad;   // activation block scales [ceil(T/128)][nb][128]
-    const int8_t *w;   // tiled weight [ceil(N/n)][nb][2][P][n x 128]
-    const float *ws;   // tiled weight scales [ceil(N/n)][nb][2][n]
-    float *out;        // [T][ldo]
-    int ldo, T, N, nb;
+    int nw;            // weights in this launch; their tiles follow one another
+    const int8_t *w[kTcMaxW];   // tiled weight [ceil(N/n)][nb][2][P][n x 128]
+    const float *ws[kTcMaxW];   // tiled weight scales [ceil(N/n)][nb][2][n]
+    float *out[kTcMaxW];        // [T][ldo]
+    int ldo[kTcMaxW], N[kTcMaxW];
+    int T, nb;
     int epi;           // 0: out = y, 1: out += y
     int *err;          // set on a bounded-wait timeout
 };
@@ -97,6 +108,23 @@ struct TcArgs {
 // Number of (m, n) tiles of a GEMM whose MMAs cover NM weight rows.
 __host__ __device__ inline int tc_tiles(int P, int NM, int T, int N) {
     return ((T + kTcM - 1) / kTcM) * ((N + tc_n(P) - 1) / tc_n(P)) * (tc_n(P) / NM);
+}
+__host__ __device__ inline int tc_tiles_all(int P, int NM, const TcArgs &a) {
+    int n = 0;
+    for (int i = 0; i < a.nw; i++) n += tc_tiles(P, NM, a.T, a.N[i]);
+    return n;
+}
+// Tile -> (weight, m tile, NM-row slice of that weight).
+__device__ __forceinline__ int tc_locate(int P, int NM, const TcArgs &a, int ntm, int tile, int &mt, int &ns) {
+    int wi = 0;
+    for (; wi < a.nw - 1; wi++) {
+        const int tw = tc_tiles(P, NM, a.T, a.N[wi]);
+        if (tile < tw) break;
+        tile -= tw;
+    }
+    mt = tile % ntm;
+    ns = tile / ntm;
+    return wi;
 }
 
 __device__ __forceinline__ uint32_t tc_smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -195,13 +223,14 @@ template <int P, int NM>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__ TcArgs a) {
     constexpr int N = tc_n(P), SUB = N / NM, C = NM / 4, AH = kTcABytes / 2, SB = tc_sbytes(P);
     constexpr int STB = tc_stage_bytes(P, NM), SLB = tc_slot_bytes(NM);
+    constexpr int kTcStages = tc_stages(P, NM), kTcScaleSlots = tc_slots(P, NM);
     static_assert(N % NM == 0 && NM % 64 == 0, "MMA rows must be a slice of the weight tile");
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], sfull[kTcScaleSlots], sempty[kTcScaleSlots],
         accf[2], acce[2], fin;
     __shared__ uint32_t s_tmem;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nb = a.nb, ntm = (a.T + kTcM - 1) / kTcM, ntiles = tc_tiles(P, NM, a.T, a.N);
+    const int nb = a.nb, ntm = (a.T + kTcM - 1) / kTcM, ntiles = tc_tiles_all(P, NM, a);
     uint8_t *stage = (uint8_t *)(((uintptr_t)smem + 1023) & ~(uintptr_t)1023);
     uint8_t *slots = stage + (size_t)kTcStages * STB;
     if (threadIdx.x == 0) {
@@ -236,7 +265,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
         if (lane == 0) {
             int g = 0, hs = 0;  // blocks and half blocks issued by this CTA
             for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-                const int mt = tile % ntm, ns = tile / ntm, nt = ns / SUB, si = ns % SUB;
+                int mt, ns;
+                const int wi = tc_locate(P, NM, a, ntm, tile, mt, ns), nt = ns / SUB, si = ns % SUB;
                 for (int kb = 0; kb < nb && ok; kb++, g++) {
                     const int sl = g % kTcScaleSlots, su = g / kTcScaleSlots;
                     if (su > 0 && !tc_mbar_wait(&sempty[sl], (su - 1) & 1)) {
@@ -244,7 +274,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                         break;
                     }
                     uint8_t *sd = slots + (size_t)sl * SLB;
-                    const uint8_t *ws = (const uint8_t *)a.ws + ((size_t)nt * nb + kb) * SB + (size_t)si * NM * 4;
+                    const uint8_t *ws = (const uint8_t *)a.ws[wi] + ((size_t)nt * nb + kb) * SB + (size_t)si * NM * 4;
                     tc_mbar_expect(&sfull[sl], SLB);
                     tc_bulk(sd, ws, NM * 4, &sfull[sl]);
                     tc_bulk(sd + NM * 4, ws + N * 4, NM * 4, &sfull[sl]);
@@ -258,7 +288,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                         uint8_t *st = stage + (size_t)s * STB;
                         tc_mbar_expect(&full[s], STB);
                         tc_bulk(st, a.a + ((size_t)mt * nb + kb) * kTcABytes + (size_t)h * AH, AH, &full[s]);
-                        const int8_t *wb = a.w + ((size_t)nt * nb + kb) * tc_bbytes(P) + (size_t)h * P * N * kTcKH;
+                        const int8_t *wb = a.w[wi] + ((size_t)nt * nb + kb) * tc_bbytes(P) + (size_t)h * P * N * kTcKH;
                         if constexpr (SUB == 1) {
                             tc_bulk(st + AH, wb, P * N * kTcKH, &full[s]);
                         } else {
@@ -318,7 +348,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
         const int e = warp - 2, q = warp & 3, part = e >> 2;
         int g = 0;
         for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-            const int mt = tile % ntm, ns = tile / ntm;
+            int mt, ns;
+            const int wi = tc_locate(P, NM, a, ntm, tile, mt, ns);
             const int t = mt * kTcM + q * 32 + lane;
             float acc[C];
 #pragma unroll
@@ -373,9 +404,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                 }
             }
             if (ok && t < a.T) {
-                float *o = a.out + (size_t)t * a.ldo;
-                const int n0 = ns * NM + part * C;
-                if ((a.ldo & 3) == 0 && n0 + C <= a.N) {
+                float *o = a.out[wi] + (size_t)t * a.ldo[wi];
+                const int n0 = ns * NM + part * C, nmax = a.N[wi];
+                if ((a.ldo[wi] & 3) == 0 && n0 + C <= nmax) {
 #pragma unroll
                     for (int j = 0; j < C; j += 4) {
                         float4 v = make_float4(acc[j], acc[j + 1], acc[j + 2], acc[j + 3]);
@@ -392,7 +423,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
 #pragma unroll
                     for (int j = 0; j < C; j++) {
                         const int n = n0 + j;
-                        if (n < a.N) o[n] = a.epi ? o[n] + acc[j] : acc[j];
+                        if (n < nmax) o[n] = a.epi ? o[n] + acc[j] : acc[j];
                     }
                 }
             }
