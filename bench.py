@@ -82,7 +82,41 @@ def parse():
                    help="also time each kernel of the per-layer graph path alone")
     p.add_argument("--serve-requests", type=int, default=4096, help="config-3 requests (all GPUs); 0 skips")
     p.add_argument("--no-extra", action="store_true", help="skip the config 1 / config 2 lines (N = 1 only)")
+    p.add_argument("--profile-pass", choices=["c2", "c3step"],
+                   help="for ncu --profile-from-start off: warm up, then run one batch pass of config 2 "
+                        "(32 x 256 prefill) or one config-3-shaped step (256 decode tokens at position 100) "
+                        "between cuProfilerStart/Stop, and exit")
+    p.add_argument("--layers", type=int, default=32, help="model layers for --profile-pass")
     return p.parse_args()
+
+
+def profile_pass(args):
+    """One batch pass bracketed by cuProfilerStart / cuProfilerStop."""
+    import ctypes
+    from hymt2_b200 import synth
+    from hymt2_b200.device import Backend, DeviceModel
+    cfg = "c2_q4km" if args.profile_pass == "c2" else "c0_stq"
+    be = Backend(0)
+    dm = DeviceModel(synth.ensure(cfg, args.model_dir, layers=args.layers), be, ctx=512)
+    rng = np.random.default_rng(0)
+    if args.profile_pass == "c2":
+        dm.batch_prepare(slots=C2_SEQS, slot_ctx=C2_LEN, max_tokens=C2_SEQS * C2_LEN, max_out=C2_SEQS)
+        toks = rng.integers(0, VOCAB, C2_SEQS * C2_LEN)
+        slots, pos = np.repeat(np.arange(C2_SEQS), C2_LEN), np.tile(np.arange(C2_LEN), C2_SEQS)
+        rows = np.arange(C2_SEQS) * C2_LEN + C2_LEN - 1
+    else:
+        dm.batch_prepare(slots=SERVE_SLOTS, slot_ctx=256, max_tokens=SERVE_SLOTS, max_out=SERVE_SLOTS)
+        toks, slots = rng.integers(0, VOCAB, SERVE_SLOTS), np.arange(SERVE_SLOTS)
+        pos, rows = np.full(SERVE_SLOTS, 100), np.arange(SERVE_SLOTS)
+    for _ in range(2):
+        dm.batch_forward(toks, slots, pos, rows)
+    cu = ctypes.CDLL("libcuda.so.1")
+    cu.cuProfilerStart()
+    dm.batch_forward(toks, slots, pos, rows)
+    cu.cuProfilerStop()
+    dm.close()
+    be.close()
+    print("profiled one pass")
 
 
 def dist_env():
@@ -419,6 +453,9 @@ def run_reference_arm(args, rank, world):
 def main():
     args = parse()
     rank, local, world = dist_env()
+    if args.profile_pass:
+        profile_pass(args)
+        return
     if args.impl == "reference":
         run_reference_arm(args, rank, world)
         return

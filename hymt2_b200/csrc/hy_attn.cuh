@@ -967,7 +967,7 @@ __global__ void __launch_bounds__(G * 32) attn_prefill(const __grid_constant__ A
 // p.v normalised by the sum of p), with q/k/v already rotated, normalised and
 // stored by rope_norm_store.  CTA = one query block (<= 16 consecutive
 // tokens of one sequence) x one KV head; warp w owns q head kvh*G + w, its
-// 16 rows the block's tokens.  K/V tiles of 64 keys are staged with cp.async
+// 16 rows the block's tokens.  K/V tiles of 32 keys are staged with cp.async
 // (double-buffered, rows padded by 8 elements so fragment loads hit distinct
 // banks) and multiplied with mma.sync m16n8k16 bf16 into fp32 accumulators
 // with an online softmax.  K and V are bf16 already; q and p are fp32 and
@@ -975,7 +975,7 @@ __global__ void __launch_bounds__(G * 32) attn_prefill(const __grid_constant__ A
 // rounding of what the previous ones leave), so every product keeps at
 // least fp32's 24 bits and the sums stay fp32.
 constexpr int kFaQ = 16;   // query tokens per block
-constexpr int kFaK = 64;   // keys per tile
+constexpr int kFaK = 32;   // keys per tile (two CTAs of 4 warps fit an SM)
 
 template <int HD>
 __host__ __device__ constexpr int fa_row() { return HD + 8; }  // padded bf16 row
@@ -1017,7 +1017,7 @@ __device__ __forceinline__ void fa_ldm4t(uint32_t (&r)[4], const void *p) {
                  : "r"((uint32_t)__cvta_generic_to_shared(p)));
 }
 
-// Stage keys [k0, k0 + 64) (rows past kend zero-filled) of K and V.
+// Stage keys [k0, k0 + kFaK) (rows past kend zero-filled) of K and V.
 template <int HD, int G>
 __device__ __forceinline__ void fa_stage(const uint16_t *Kg, const uint16_t *Vg, int kvdim, int k0, int kend,
                                          uint16_t *sk, uint16_t *sv) {
@@ -1091,10 +1091,11 @@ __global__ void __launch_bounds__(G * 32) attn_fa(const __grid_constant__ AttnAr
             asm volatile("cp.async.wait_group 0;" ::: "memory");
         }
         __syncthreads();
-        // S = q . K^T for 64 keys: 8 key n-tiles x HD/16 k-steps, hi and lo
-        float s[8][4];
+        // S = q . K^T for kFaK keys: kFaK/8 key n-tiles x HD/16 k-steps, every q term
+        constexpr int NS = kFaK / 8;
+        float s[NS][4];
 #pragma unroll
-        for (int j = 0; j < 8; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+        for (int j = 0; j < NS; j++) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; kk++) {
             const int ro = ((lane >> 3) & 1) * 8 + (lane & 7), co = kk * 16 + (lane >> 4) * 8;
@@ -1102,7 +1103,7 @@ __global__ void __launch_bounds__(G * 32) attn_fa(const __grid_constant__ AttnAr
 #pragma unroll
             for (int x = 0; x < kFaTerms; x++) fa_ldm4(aq[x], qs + ((size_t)(x * G + w) * kFaQ + ro) * R + co);
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
+            for (int j = 0; j < NS; j++) {
                 const uint16_t *kr = sk + (j * 8 + g) * R + kk * 16 + 2 * tq;
                 const uint32_t b0 = *(const uint32_t *)kr, b1 = *(const uint32_t *)(kr + 8);
 #pragma unroll
@@ -1113,7 +1114,7 @@ __global__ void __launch_bounds__(G * 32) attn_fa(const __grid_constant__ AttnAr
         const int kb = kt * kFaK;
         float tm0 = -INFINITY, tm1 = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
+        for (int j = 0; j < NS; j++) {
             const int key = kb + j * 8 + 2 * tq;
             s[j][0] = key <= qp0 ? s[j][0] * scale : -INFINITY;
             s[j][1] = key + 1 <= qp0 ? s[j][1] * scale : -INFINITY;
@@ -1139,9 +1140,9 @@ __global__ void __launch_bounds__(G * 32) attn_fa(const __grid_constant__ AttnAr
             o[j][2] *= c1;
             o[j][3] *= c1;
         }
-        // P (hi / lo) as A fragments, then O += P . V over 4 key k-steps
+        // P (three bf16 terms) as A fragments, then O += P . V over kFaK/16 key k-steps
 #pragma unroll
-        for (int kk = 0; kk < 4; kk++) {
+        for (int kk = 0; kk < kFaK / 16; kk++) {
             float p[8];
 #pragma unroll
             for (int u = 0; u < 2; u++) {
