@@ -446,12 +446,12 @@ bool tc_scratch(HyCtx *c, int K) {
 // writing tiled Q8_K codes, then one tensor-core GEMM per weight format; outs[i] is
 // [nt][lds[i]], stored (epi 0) or accumulated (epi 1).
 bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float *const *outs, const int *lds,
-               int cnt, int epi) {
+               int cnt, int epi, bool pdl) {
     const int K = pro.k, nb = K / 256, tpad = (nt + kTcM - 1) / kTcM * kTcM;
     if (!tc_scratch(c, K)) return false;
     for (int i = 0; i < cnt; i++)
         if (!tc_weight(c, ws[i])) return false;
-    if (!launch(c, tc_quantize, dim3(tpad), dim3(kGemvThreads), (size_t)(K + 64) * 4, false, pro, nt, c->d_tca,
+    if (!launch(c, tc_quantize, dim3(tpad), dim3(kGemvThreads), (size_t)(K + 64) * 4, pdl, pro, nt, c->d_tca,
                 c->d_tcad))
         return false;
     // one persistent launch per weight format (the weights of a launch share the activation tiles)
@@ -483,11 +483,11 @@ bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float
         const int ntiles = tc_tiles_all(P, NM, ta);
         const dim3 grid(ntiles < c->nsm ? ntiles : c->nsm), blk(kTcThreads);
         bool ok;
-        if (P == 1 && NM == 256) ok = launch(c, tc_gemm<1, 256>, grid, blk, tc_smem_bytes(1, 256), false, ta);
-        else if (P == 1) ok = launch(c, tc_gemm<1, 64>, grid, blk, tc_smem_bytes(1, 64), false, ta);
-        else if (P == 2 && NM == 128) ok = launch(c, tc_gemm<2, 128>, grid, blk, tc_smem_bytes(2, 128), false, ta);
-        else if (P == 2) ok = launch(c, tc_gemm<2, 64>, grid, blk, tc_smem_bytes(2, 64), false, ta);
-        else ok = launch(c, tc_gemm<3, 64>, grid, blk, tc_smem_bytes(3, 64), false, ta);
+        if (P == 1 && NM == 256) ok = launch(c, tc_gemm<1, 256>, grid, blk, tc_smem_bytes(1, 256), pdl, ta);
+        else if (P == 1) ok = launch(c, tc_gemm<1, 64>, grid, blk, tc_smem_bytes(1, 64), pdl, ta);
+        else if (P == 2 && NM == 128) ok = launch(c, tc_gemm<2, 128>, grid, blk, tc_smem_bytes(2, 128), pdl, ta);
+        else if (P == 2) ok = launch(c, tc_gemm<2, 64>, grid, blk, tc_smem_bytes(2, 64), pdl, ta);
+        else ok = launch(c, tc_gemm<3, 64>, grid, blk, tc_smem_bytes(3, 64), pdl, ta);
         if (!ok) return false;
     }
     return true;
@@ -599,7 +599,7 @@ bool gateup_forward(HyCtx *c, const Fwd &f, const Layer &L, int nt, bool pdl) {
     HyWeight *ws[2] = {L.g, L.u};
     float *outs[2] = {f.g, f.u};
     const int lds[2] = {c->F, c->F};
-    if (tc_usable(c, nt, ws, 2)) return tc_linear(c, a, nt, ws, outs, lds, 2, 0);
+    if (tc_usable(c, nt, ws, 2)) return tc_linear(c, a, nt, ws, outs, lds, 2, 0, pdl);
     a.epi = EPI_STORE;
     return run_multi(c, ws, outs, lds, 2, a, pdl);
 }
@@ -619,7 +619,7 @@ bool down_forward(HyCtx *c, const Fwd &f, const Layer &L, int nt, bool pdl, floa
         HyWeight *ws[1] = {L.d};
         float *outs[1] = {dst};
         const int lds[1] = {c->H};
-        if (tc_usable(c, nt, ws, 1)) return tc_linear(c, a, nt, ws, outs, lds, 1, 1);
+        if (tc_usable(c, nt, ws, 1)) return tc_linear(c, a, nt, ws, outs, lds, 1, 1, pdl);
     }
     a.epi = EPI_ADD;
     a.nw = 1;
@@ -646,7 +646,7 @@ bool layer_forward(HyCtx *c, const Fwd &f, int li, int nt, bool pdl) {
         a.norm_w = L.attn_norm;
         a.eps = c->eps;
         if (tc_usable(c, nt, ws, 3)) {
-            if (!tc_linear(c, a, nt, ws, outs, lds, 3, 0)) return false;
+            if (!tc_linear(c, a, nt, ws, outs, lds, 3, 0, pdl)) return false;
         } else {
             a.epi = EPI_STORE;
             if (!run_multi(c, ws, outs, lds, 3, a, pdl)) return false;
@@ -698,7 +698,7 @@ bool layer_forward(HyCtx *c, const Fwd &f, int li, int nt, bool pdl) {
         float *outs[1] = {f.h};
         const int lds[1] = {c->H};
         if (tc_usable(c, nt, ws, 1)) {
-            if (!tc_linear(c, a, nt, ws, outs, lds, 1, 1)) return false;
+            if (!tc_linear(c, a, nt, ws, outs, lds, 1, 1, pdl)) return false;
         } else {
             a.epi = EPI_ADD;
             a.nw = 1;
@@ -1529,7 +1529,7 @@ HYC_API int hyc_tc_test(void *impl, hy_dweight *hw, int act, const float *x, con
         HyWeight *ws[1] = {w};
         float *outs[1] = {dout};
         const int lds[1] = {w->n};
-        ok = tc_linear(c, pro, nt, ws, outs, lds, 1, 0) &&
+        ok = tc_linear(c, pro, nt, ws, outs, lds, 1, 0, false) &&
              cudaMemcpyAsync(out, dout, (size_t)nt * w->n * 4, cudaMemcpyDeviceToHost, c->st) == cudaSuccess &&
              cudaStreamSynchronize(c->st) == cudaSuccess && tc_status(c);
     }

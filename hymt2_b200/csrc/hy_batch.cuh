@@ -202,9 +202,11 @@ bool batch_upload(HyCtx *c, int nt, int nout) {
 // (over the first vocab_out logits) land in b.d_ids, the logits in b.logits.
 bool batch_run(HyCtx *c, int nt, int nout, int vocab_out) {
     Batch &b = *c->bat;
-    if (!launch(c, embed_rows, dim3(nt), dim3(256), 0, false, desc(c->embd, nullptr, 0), (const int *)b.tok(), b.h, -1))
+    // every kernel of the pass is a programmatic dependent of the one before
+    // (each waits for it before touching its data; setup overlaps its tail)
+    if (!launch(c, embed_rows, dim3(nt), dim3(256), 0, true, desc(c->embd, nullptr, 0), (const int *)b.tok(), b.h, -1))
         return false;
-    if (!layers_forward(c, fwd_batch(c), nt, false)) return false;
+    if (!layers_forward(c, fwd_batch(c), nt, true)) return false;
     if (nout < 1) return true;
     if (!launch(c, batch_gather, dim3(nout), dim3(128), 0, false, (const float *)b.h, c->H, (const int *)b.rows(),
                 b.sel))
@@ -219,7 +221,7 @@ bool batch_run(HyCtx *c, int nt, int nout, int vocab_out) {
     a.norm_w = c->d_out_norm;
     a.eps = c->eps;
     if (tc_usable(c, nout, ws, 1)) {
-        if (!tc_linear(c, a, nout, ws, outs, lds, 1, 0)) return false;
+        if (!tc_linear(c, a, nout, ws, outs, lds, 1, 0, true)) return false;
     } else {
         a.epi = EPI_STORE;
         a.nw = 1;

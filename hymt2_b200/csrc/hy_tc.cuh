@@ -228,6 +228,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], sfull[kTcScaleSlots], sempty[kTcScaleSlots],
         accf[2], acce[2], fin;
+    // launched as a programmatic dependent: barrier setup and the TMEM
+    // allocation overlap the previous kernel; the producer waits for it
+    // before its first copy (everything else follows the producer)
+    pdl_trigger();
     __shared__ uint32_t s_tmem;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nb = a.nb, ntm = (a.T + kTcM - 1) / kTcM, ntiles = tc_tiles_all(P, NM, a);
@@ -263,6 +267,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
         // producer: per block its scales (weight slice, then activations),
         // then two half-block stages (A half, B planes of the slice)
         if (lane == 0) {
+            pdl_wait();
             int g = 0, hs = 0;  // blocks and half blocks issued by this CTA
             for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
                 int mt, ns;
@@ -531,6 +536,8 @@ __global__ void tc_weight_to_tiled(const __grid_constant__ WDesc w, int8_t *tw, 
 __global__ void __launch_bounds__(kGemvThreads) tc_quantize(const __grid_constant__ GemvArgs a, int T, int8_t *ta,
                                                              float *ad) {
     extern __shared__ __align__(16) uint8_t smem[];
+    pdl_trigger();
+    pdl_wait();  // the codes and scales are still the previous GEMM's operand until it completes
     const int K = a.k, nb = K / 256, t = blockIdx.x;
     float *x = (float *)smem;
     float *red = x + K;
