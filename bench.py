@@ -241,6 +241,24 @@ def cpu_baseline(path: str, ntok: int) -> dict:
 SERVE_PREFIX, SERVE_MAX_NEW, SERVE_SLOTS, SERVE_STEP_TOKENS = 24, 64, 256, 512
 
 
+def shard(items: list, rank: int, world: int) -> list:
+    """This rank's share of independent requests: r, r + N, r + 2N, ..."""
+    return items[rank::world]
+
+
+def max_over_ranks_fn(dist, device):
+    """Max of a per-rank float over the process group (identity without one)."""
+    import torch
+
+    def f(x: float) -> float:
+        if not dist:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+    return f
+
+
 def serve_requests(n: int) -> list[list[int]]:
     """Config 3 requests: lengths uniform in [16, 128]; the first min(len, 24)
     ids are one shared prefix, the rest uniform over the vocab (seed 3)."""
@@ -258,7 +276,7 @@ def bench_serving(dm, stream, torch, rank, world, nreq, max_over_ranks, barrier)
     """Config 3 on this rank's shard (requests r, r + N, ...): continuous
     batching over 256 slots, 64 greedy tokens per request, device-timed
     around the whole serve call (host scheduling included)."""
-    reqs = serve_requests(nreq)[rank::world]
+    reqs = shard(serve_requests(nreq), rank, world)
     dm.batch_prepare(slots=SERVE_SLOTS, slot_ctx=128 + SERVE_MAX_NEW, max_tokens=SERVE_STEP_TOKENS,
                      max_out=SERVE_SLOTS)
     dm.serve(reqs[:min(len(reqs), 300)], 4, SERVE_STEP_TOKENS)  # warm-up: tensor-core weight tiles, clocks
@@ -504,12 +522,7 @@ def main():
         torch.cuda.synchronize()
         be.sync()
 
-    def max_over_ranks(x):
-        if not dist:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    max_over_ranks = max_over_ranks_fn(dist, "cuda")
 
     # ---- device-resident decode
     w0 = time.perf_counter()
