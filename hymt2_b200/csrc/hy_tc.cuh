@@ -22,14 +22,15 @@
 // matrices of 8 rows x 16 bytes; core (row group g, 16-byte k chunk c) sits
 // at (c * R/8 + g) * 128 bytes, so each half block (K = 128) of a tile is
 // contiguous.  Activations: [m tile][block][128 x 256]; weights: [n tile]
-// [block][half][plane][N x 128], so one bulk copy moves the A half or all
-// planes of the B half of a stage.
+// [block][half][P*N x 128] with the planes stacked as rows, so one bulk copy
+// moves the A half or the B half of a stage and one MMA (N' = P*NM <= 256)
+// multiplies the activations with every plane, reading them once.
 //
 // Persistent CTAs (one per SM) walk the (m, n) tiles m-fastest, so the
 // CTAs running at one time share each weight tile through L2.  Per CTA:
-// warp 0 streams half blocks (A, B planes) into a 4-stage ring and each
-// block's scales into a 4-entry ring of their own; warp 1 (one thread)
-// issues 4 x P MMAs of K = 32 per half block into one of two TMEM
+// warp 0 streams half blocks (A, B planes) into a 3..8-stage ring and each
+// block's scales into a ring of their own; warp 1 (one thread)
+// issues 4 MMAs of K = 32 (N' = P*NM) per half block into one of two TMEM
 // accumulator sets (N = 256 / 128 / 64 for P = 1 / 2 / 3, so one set is at
 // most 256 columns); warps 2-17 (4 per TMEM lane quarter, N/4 columns each)
 // read a finished block's int32 results with tcgen05.ld and fold them into
@@ -84,10 +85,12 @@ __host__ __device__ inline size_t tc_tile_off(int r, int k, int R) {
     return ((size_t)(k >> 4) * (R / 8) + (r >> 3)) * 128 + (size_t)(r & 7) * 16 + (k & 15);
 }
 // Byte offset of (plane p, row r, k in 0..255) inside one (tile, block) of
-// a tiled weight: half k / 128, then plane, then the N x 128 canonical tile.
+// a tiled weight: half k / 128, then ONE canonical tile of P*N rows holding
+// the planes stacked (row p*N + r), so a single MMA of N' = P*NM covers
+// every plane and reads the activation tile once.
 __host__ __device__ inline size_t tc_wtile_off(int P, int p, int r, int k) {
     const int N = tc_n(P);
-    return ((size_t)(k >> 7) * P + p) * N * kTcKH + tc_tile_off(r, k & 127, N);
+    return (size_t)(k >> 7) * P * N * kTcKH + tc_tile_off(p * N + r, k & 127, P * N);
 }
 
 constexpr int kTcMaxW = 3;  // weights of one launch (same format, same activation)
@@ -297,13 +300,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                         if constexpr (SUB == 1) {
                             tc_bulk(st + AH, wb, P * N * kTcKH, &full[s]);
                         } else {
-                            // the slice's 8-row groups of each 16-byte K chunk: NM * 16 contiguous bytes
+                            // per 16-byte K chunk and plane, the slice's 8-row groups: NM * 16
+                            // contiguous bytes, placed as rows p*NM .. of a P*NM-row tile
 #pragma unroll
-                            for (int p = 0; p < P; p++)
+                            for (int c = 0; c < kTcKH / 16; c++)
 #pragma unroll
-                                for (int c = 0; c < kTcKH / 16; c++)
-                                    tc_bulk(st + AH + (size_t)(p * kTcKH / 16 + c) * NM * 16,
-                                            wb + (size_t)p * N * kTcKH + ((size_t)c * (N / 8) + si * (NM / 8)) * 128,
+                                for (int p = 0; p < P; p++)
+                                    tc_bulk(st + AH + ((size_t)c * (P * NM / 8) + p * (NM / 8)) * 128,
+                                            wb + ((size_t)c * (P * N / 8) + p * (N / 8) + si * (NM / 8)) * 128,
                                             NM * 16, &full[s]);
                         }
                     }
@@ -312,9 +316,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
             if (!ok) atomicExch(a.err, 1);
         }
     } else if (warp == 1) {
-        // MMA issuer: 4 x P MMAs (K = 32 each) per half block into accumulator set g % 2
+        // MMA issuer: 4 MMAs (K = 32, N = P*NM: every plane at once) per half
+        // block into accumulator set g % 2
         if (lane == 0) {
-            constexpr uint32_t idesc = tc_idesc(kTcM, NM);
+            constexpr uint32_t idesc = tc_idesc(kTcM, P * NM);
             int g = 0, hs = 0;
             for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
                 for (int kb = 0; kb < nb && ok; kb++, g++) {
@@ -333,10 +338,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                         const uint8_t *st = stage + (size_t)s * STB;
 #pragma unroll
                         for (int k = 0; k < kTcKH / 32; k++)
-#pragma unroll
-                            for (int p = 0; p < P; p++)
-                                tc_mma(tmem + (uint32_t)(buf * P * NM + p * NM), tc_desc(st, k, kTcM),
-                                       tc_desc(st + AH + p * NM * kTcKH, k, NM), idesc, (h | k) != 0);
+                            tc_mma(tmem + (uint32_t)(buf * P * NM), tc_desc(st, k, kTcM), tc_desc(st + AH, k, P * NM),
+                                   idesc, (h | k) != 0);
                         tc_commit(&empty[s]);
                     }
                     if (ok) tc_commit(&accf[buf]);
