@@ -451,9 +451,17 @@ bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float
     if (!tc_scratch(c, K)) return false;
     for (int i = 0; i < cnt; i++)
         if (!tc_weight(c, ws[i])) return false;
-    if (!launch(c, tc_quantize, dim3(tpad), dim3(kGemvThreads), (size_t)(K + 64) * 4, pdl, pro, nt, c->d_tca,
-                c->d_tcad))
-        return false;
+    {
+        const dim3 g(tpad), b(kGemvThreads);
+        const size_t sm = (size_t)(K + 64) * 4;
+        const int sv = (K / 4 + kGemvThreads - 1) / kGemvThreads;
+        bool ok;
+        if (sv <= 2) ok = launch(c, tc_quantize<2>, g, b, sm, pdl, pro, nt, c->d_tca, c->d_tcad);
+        else if (sv <= 4) ok = launch(c, tc_quantize<4>, g, b, sm, pdl, pro, nt, c->d_tca, c->d_tcad);
+        else if (sv <= 6) ok = launch(c, tc_quantize<6>, g, b, sm, pdl, pro, nt, c->d_tca, c->d_tcad);
+        else ok = launch(c, tc_quantize<kStageVec>, g, b, sm, pdl, pro, nt, c->d_tca, c->d_tcad);
+        if (!ok) return false;
+    }
     // one persistent launch per weight format (the weights of a launch share the activation tiles)
     bool done[kTcMaxW] = {false, false, false};
     for (int i = 0; i < cnt; i++) {

@@ -536,6 +536,9 @@ __global__ void tc_weight_to_tiled(const __grid_constant__ WDesc w, int8_t *tw, 
 // GEMV prologues: as is, RMSNorm*w, SiLU*up) and each 256 block quantised by
 // one warp with quantize_block_warp's arithmetic (bit-identical codes).
 // Tokens past T (padding of the last tile) get zero codes.
+// SV = float4 loads per thread (K <= 1024 * SV): the staged arithmetic is the
+// same for any SV that covers K, a smaller one only needs fewer registers.
+template <int SV>
 __global__ void __launch_bounds__(kGemvThreads) tc_quantize(const __grid_constant__ GemvArgs a, int T, int8_t *ta,
                                                              float *ad) {
     extern __shared__ __align__(16) uint8_t smem[];
@@ -554,7 +557,7 @@ __global__ void __launch_bounds__(kGemvThreads) tc_quantize(const __grid_constan
         }
         return;
     }
-    stage_fp32<kStageVec>(a, t, x, red, K);
+    stage_fp32<SV>(a, t, x, red, K);
     __syncthreads();
     for (int b = warp; b < nb; b += kGemvThreads / 32) {
         const float *p = x + b * 256 + lane * 8;
