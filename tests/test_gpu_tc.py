@@ -101,3 +101,26 @@ def test_tc_prefill(backend, oracle, synth, model_dir, cfg):
         lib.hyc_set_tc(impl, 1)
         dm.close()
         om.close()
+
+
+@pytest.mark.parametrize("name", ["STQ1_0", "Q6_K", "Q4_K"])
+@pytest.mark.parametrize("k,rows,nt", [(512, 48, 40), (2048, 6144, 200), (512, 20480, 256)])
+def test_tc_gemm_tile_widths(backend, oracle, name, k, rows, nt):
+    """Every MMA width the launch picks (64-row slices while whole tiles
+    would leave SMs idle, whole 256 / 128 / 64-row tiles otherwise) gives the
+    oracle's result."""
+    from hymt2_b200.device import weight_from_bytes
+    gt = TYPES[name]
+    rng = np.random.default_rng(k + rows + nt)
+    raw = rand_blocks(rng, gt, rows, k)
+    h = backend.upload(weight_from_bytes(gt, raw, rows, k))
+    try:
+        x = rand_act(rng, nt, k) * 3.0
+        nw = (1.0 + 0.2 * rng.standard_normal(k)).astype(np.float32)
+        got = backend.tc_test(h, 2, x, rows, norm_w=nw)
+        want = oracle.prologue_matmul(oracle.weight(gt, raw, rows, k, panel=True), 2, x, None, nw)
+        rel = np.abs(got - want) / max(np.abs(want).max(), 1e-6)
+        flipped = (rel > 1e-4).any(axis=1).mean()
+        assert flipped < 0.05 and rel.max() < 5e-3, (rel.max(), flipped)
+    finally:
+        backend.release(h)
