@@ -456,7 +456,11 @@ bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float
         const size_t sm = (size_t)(K + 64) * 4;
         const int sv = (K / 4 + kGemvThreads - 1) / kGemvThreads;
         bool ok;
-        if (sv <= 2) ok = launch(c, tc_quantize<2>, g, b, sm, pdl, pro, nt, c->d_tca, c->d_tcad);
+        if ((pro.act == ACT_VEC || pro.act == ACT_SILU) && pro.ldx % 8 == 0) {
+            const long long warps = (long long)tpad * nb;
+            ok = launch(c, tc_quantize_blocks, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, pdl, pro, nt, tpad,
+                        c->d_tca, c->d_tcad);
+        } else if (sv <= 2) ok = launch(c, tc_quantize<2>, g, b, sm, pdl, pro, nt, c->d_tca, c->d_tcad);
         else if (sv <= 4) ok = launch(c, tc_quantize<4>, g, b, sm, pdl, pro, nt, c->d_tca, c->d_tcad);
         else if (sv <= 6) ok = launch(c, tc_quantize<6>, g, b, sm, pdl, pro, nt, c->d_tca, c->d_tcad);
         else ok = launch(c, tc_quantize<kStageVec>, g, b, sm, pdl, pro, nt, c->d_tca, c->d_tcad);

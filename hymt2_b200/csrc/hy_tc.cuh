@@ -530,6 +530,47 @@ __global__ void tc_weight_to_tiled(const __grid_constant__ WDesc w, int8_t *tw, 
     }
 }
 
+// Q8_K codes of one 256 block held by a warp (lane: elements 8 lane ..
+// 8 lane + 7), written into the tiled operand (token row r of m tile mt)
+// with its scale: quantize_block_warp's arithmetic (first index of the
+// largest |x|, iscale = -127/max, d = 1/iscale, round-half-even, clip +-127,
+// non-finite products -> 0).
+__device__ __forceinline__ void tc_quant_store(const float (&v)[8], int8_t *ta, float *ad, int mt, int nb, int b,
+                                               int r) {
+    const int lane = threadIdx.x & 31;
+    float ba = 0.f, lv = 0.f;
+    int li = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const float av = fabsf(v[j]);
+        if (av > ba) { ba = av; lv = v[j]; li = lane * 8 + j; }
+    }
+    const unsigned mbits = __reduce_max_sync(0xffffffffu, __float_as_uint(ba));
+    const unsigned cand = (__float_as_uint(ba) == mbits) ? (unsigned)li : 0x7fffffffu;
+    const int bi = (int)__reduce_min_sync(0xffffffffu, cand);
+    ba = __uint_as_float(mbits);
+    const float bv = __shfl_sync(0xffffffffu, lv, (bi >> 3) & 31);
+    int q[8];
+    float d = 0.f;
+    if (ba == 0.f) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) q[j] = 0;
+    } else {
+        const float iscale = -127.f / bv;
+        d = 1.f / iscale;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const float f = __fmul_rn(iscale, v[j]);
+            int rr = isfinite(f) ? __float2int_rn(f) : 0;
+            q[j] = rr > 127 ? 127 : (rr < -127 ? -127 : rr);
+        }
+    }
+    const uint32_t lo = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
+    const uint32_t hi = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
+    *(uint2 *)(ta + ((size_t)mt * nb + b) * kTcABytes + tc_tile_off(r, lane * 8, kTcM)) = make_uint2(lo, hi);
+    if (lane == 0) ad[((size_t)mt * nb + b) * kTcM + r] = d;
+}
+
 // Activation rows -> Q8_K, written as tiled int8 codes plus block scales
 // (tiled too: [m tile][block][128]).
 // One CTA (kGemvThreads) per token; the fp32 row is built by stage_fp32 (the
@@ -563,38 +604,41 @@ __global__ void __launch_bounds__(kGemvThreads) tc_quantize(const __grid_constan
         const float *p = x + b * 256 + lane * 8;
         const float4 v0 = *(const float4 *)&p[0], v1 = *(const float4 *)&p[4];
         const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        float ba = 0.f, lv = 0.f;
-        int li = 0x7fffffff;
-#pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const float av = fabsf(v[j]);
-            if (av > ba) { ba = av; lv = v[j]; li = lane * 8 + j; }
-        }
-        const unsigned mbits = __reduce_max_sync(0xffffffffu, __float_as_uint(ba));
-        const unsigned cand = (__float_as_uint(ba) == mbits) ? (unsigned)li : 0x7fffffffu;
-        const int bi = (int)__reduce_min_sync(0xffffffffu, cand);
-        ba = __uint_as_float(mbits);
-        const float bv = __shfl_sync(0xffffffffu, lv, (bi >> 3) & 31);
-        int q[8];
-        float d = 0.f;
-        if (ba == 0.f) {
-#pragma unroll
-            for (int j = 0; j < 8; j++) q[j] = 0;
-        } else {
-            const float iscale = -127.f / bv;
-            d = 1.f / iscale;
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const float f = __fmul_rn(iscale, v[j]);
-                int rr = isfinite(f) ? __float2int_rn(f) : 0;
-                q[j] = rr > 127 ? 127 : (rr < -127 ? -127 : rr);
-            }
-        }
-        const uint32_t lo = (q[0] & 0xff) | ((q[1] & 0xff) << 8) | ((q[2] & 0xff) << 16) | ((uint32_t)(q[3] & 0xff) << 24);
-        const uint32_t hi = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
-        *(uint2 *)(ta + ((size_t)mt * nb + b) * kTcABytes + tc_tile_off(r, lane * 8, kTcM)) = make_uint2(lo, hi);
-        if (lane == 0) ad[((size_t)mt * nb + b) * kTcM + r] = d;
+        tc_quant_store(v, ta, ad, mt, nb, b, r);
     }
+}
+
+// Activations that need no row-wide reduction (as is; SiLU(x) * x2): one
+// warp per (token, 256 block), the element arithmetic of stage_fp32 and the
+// quantiser of tc_quantize, so the codes are the same; no CTA barrier, so
+// every block of every token is in flight at once.  Tokens T .. tpad - 1 get
+// zero codes.
+__global__ void __launch_bounds__(256) tc_quantize_blocks(const __grid_constant__ GemvArgs a, int T, int tpad,
+                                                          int8_t *ta, float *ad) {
+    pdl_trigger();
+    pdl_wait();  // the codes and scales are still the previous GEMM's operand until it completes
+    const int nb = a.k / 256, lane = threadIdx.x & 31;
+    const long long wid = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (wid >= (long long)tpad * nb) return;
+    const int t = (int)(wid / nb), b = (int)(wid % nb), mt = t / kTcM, r = t % kTcM;
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) v[j] = 0.f;
+    if (t < T) {
+        const size_t off = (size_t)t * a.ldx + (size_t)b * 256 + lane * 8;
+        const float4 x0 = *(const float4 *)(a.x + off), x1 = *(const float4 *)(a.x + off + 4);
+        const float xs[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+        if (a.act == ACT_SILU) {
+            const float4 u0 = *(const float4 *)(a.x2 + off), u1 = *(const float4 *)(a.x2 + off + 4);
+            const float us[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = __fmul_rn(xs[j] / (1.0f + expf(-xs[j])), us[j]);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; j++) v[j] = xs[j];
+        }
+    }
+    tc_quant_store(v, ta, ad, mt, nb, b, r);
 }
 
 }  // namespace hyk
