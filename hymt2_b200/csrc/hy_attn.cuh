@@ -78,7 +78,9 @@ template <int HD>
 __global__ void rope_norm_store(const __grid_constant__ AttnArgs a) {
     pdl_trigger();
     pdl_wait();
-    const int t = blockIdx.x, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // the grid strides over the tokens (a few CTAs per SM, not one per token)
+    for (int t = blockIdx.x; t < a.nt; t += gridDim.x) {
     const int pos = attn_tok_pos(a, t);
     const long long kvo = attn_tok_kv(a, t);
     const float *cs = a.rope_cos + (size_t)pos * a.half, *sn = a.rope_sin + (size_t)pos * a.half;
@@ -104,6 +106,7 @@ __global__ void rope_norm_store(const __grid_constant__ AttnArgs a) {
                 vd[lane + 32 * i] = f32_to_bf16_bits(vs[lane + 32 * i]);
             }
         }
+    }
     }
 }
 

@@ -457,9 +457,9 @@ bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float
         const int sv = (K / 4 + kGemvThreads - 1) / kGemvThreads;
         bool ok;
         if ((pro.act == ACT_VEC || pro.act == ACT_SILU) && pro.ldx % 8 == 0) {
-            const long long warps = (long long)tpad * nb;
-            ok = launch(c, tc_quantize_blocks, dim3((unsigned)((warps + 7) / 8)), dim3(256), 0, pdl, pro, nt, tpad,
-                        c->d_tca, c->d_tcad);
+            const long long ctas = ((long long)tpad * nb + 7) / 8;
+            const unsigned grid = (unsigned)(ctas < 8LL * c->nsm ? ctas : 8LL * c->nsm);
+            ok = launch(c, tc_quantize_blocks, dim3(grid), dim3(256), 0, pdl, pro, nt, tpad, c->d_tca, c->d_tcad);
         } else if (sv <= 2) ok = launch(c, tc_quantize<2>, g, b, sm, pdl, pro, nt, c->d_tca, c->d_tcad);
         else if (sv <= 4) ok = launch(c, tc_quantize<4>, g, b, sm, pdl, pro, nt, c->d_tca, c->d_tcad);
         else if (sv <= 6) ok = launch(c, tc_quantize<6>, g, b, sm, pdl, pro, nt, c->d_tca, c->d_tcad);
@@ -533,7 +533,8 @@ bool attn_launch(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
                       pdl, aa);
     int warps = aa.heads + aa.kv_heads;
     if (warps > 32) warps = 32;
-    if (!launch(c, rope_norm_store<HD>, dim3(nt), dim3(warps * 32), 0, pdl, aa)) return false;
+    const int rgrid = nt < 4 * c->nsm ? nt : 4 * c->nsm;
+    if (!launch(c, rope_norm_store<HD>, dim3(rgrid), dim3(warps * 32), 0, pdl, aa)) return false;
     const int nqb = aa.qblk ? aa.nqb : (nt + kFaQ - 1) / kFaQ;
     if (nqb == nt)  // one token per sequence (a batch of decode steps): the per-token kernel is faster
         return launch(c, attn_prefill<HD, G>, dim3(aa.kv_heads, nt), dim3(G * 32), 0, pdl, aa);

@@ -618,8 +618,9 @@ __global__ void __launch_bounds__(256) tc_quantize_blocks(const __grid_constant_
     pdl_trigger();
     pdl_wait();  // the codes and scales are still the previous GEMM's operand until it completes
     const int nb = a.k / 256, lane = threadIdx.x & 31;
-    const long long wid = (long long)blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (wid >= (long long)tpad * nb) return;
+    const long long nw = (long long)tpad * nb;
+    // the grid strides over the (token, block) pairs
+    for (long long wid = (long long)blockIdx.x * 8 + (threadIdx.x >> 5); wid < nw; wid += (long long)gridDim.x * 8) {
     const int t = (int)(wid / nb), b = (int)(wid % nb), mt = t / kTcM, r = t % kTcM;
     float v[8];
 #pragma unroll
@@ -639,6 +640,7 @@ __global__ void __launch_bounds__(256) tc_quantize_blocks(const __grid_constant_
         }
     }
     tc_quant_store(v, ta, ad, mt, nb, b, r);
+    }
 }
 
 }  // namespace hyk
