@@ -86,6 +86,7 @@ SIGNATURES = {
     "hyc_set_tc": (I, [P, I]),
     "hyc_tc_test": (I, [P, P, I, P, P, P, F, I, P]),
     "hyc_decode_path": (I, [P, C.c_char_p, I]),
+    "hyc_wait_probe": (I, [P, C.c_ulonglong, P]),
     "hyc_batch_prepare": (I, [P, I, I, I, I]),
     "hyc_batch_forward": (I, [P, P, P, P, I, P, I, I, P, P]),
     "hyc_batch_kv_copy": (I, [P, I, I, I]),

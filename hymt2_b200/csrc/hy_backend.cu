@@ -1409,6 +1409,31 @@ bool fused_forward(void *impl, hy_fused_args *a) {
 
 #include "hy_batch.cuh"
 
+// Failure-detection probe: the bounded waits of the persistent decode kernel
+// (grid barrier on its arrival counter) and of the tensor-core GEMM (an
+// mbarrier phase) given targets that nothing reaches and a limit of
+// limit_ns.  out[0] = what the grid-barrier wait returned (0: gave up),
+// out[1] = the error word it raised, out[2] = what the mbarrier wait
+// returned.  Nothing traps, faults or hangs: each wait gives up after the
+// limit and the kernel returns.
+__global__ void wait_probe(MegaSync *sync, unsigned long long limit_ns, int *out) {
+    __shared__ __align__(8) uint64_t mb;
+    __shared__ int flag;
+    MegaArgs a;
+    memset(&a, 0, sizeof a);
+    a.sync = sync;
+    const bool passed = bar_wait(a, gridDim.x + 1, &flag, limit_ns);  // one arrival more than the grid makes
+    if (threadIdx.x == 0) {
+        out[0] = passed;
+        out[1] = ld_relaxed_s32(&sync->err);
+        tc_mbar_init(&mb, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    const bool done = tc_mbar_wait(&mb, 0, limit_ns);  // nothing arrives: phase 0 never completes
+    if (threadIdx.x == 0) out[2] = done;
+}
+
 const hy_device_ops kOps = {destroy_impl, upload, release, matmul, is_software, weight_out, fused_prepare,
                             fused_forward};
 
@@ -1624,6 +1649,22 @@ HYC_API int hyc_serve(void *impl, const int *prompts, const int *prompt_off, int
     hyc_serve_stats local;
     const int vo = vocab_out > 0 && vocab_out <= c->outw->n ? vocab_out : c->outw->n;
     return serve_run(c, prompts, prompt_off, nreq, max_new, vo, step_tokens, out_ids, stats ? stats : &local) ? 0 : -1;
+}
+
+HYC_API int hyc_wait_probe(void *impl, unsigned long long limit_ns, int *out) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !out || limit_ns == 0 || limit_ns > 1000000000ull || cudaSetDevice(c->dev) != cudaSuccess)
+        return -1;
+    MegaSync *d_sync = nullptr;
+    int *d_out = nullptr;
+    bool ok = cudaMalloc(&d_sync, sizeof(MegaSync)) == cudaSuccess && cudaMalloc(&d_out, 3 * sizeof(int)) == cudaSuccess &&
+              cudaMemsetAsync(d_sync, 0, sizeof(MegaSync), c->st) == cudaSuccess &&
+              launch(c, wait_probe, dim3(1), dim3(32), 0, false, d_sync, limit_ns, d_out) &&
+              cudaMemcpyAsync(out, d_out, 3 * sizeof(int), cudaMemcpyDeviceToHost, c->st) == cudaSuccess &&
+              cudaStreamSynchronize(c->st) == cudaSuccess;
+    cudaFree(d_sync);
+    cudaFree(d_out);
+    return ok ? 0 : -1;
 }
 
 HYC_API int hyc_set_decode_mode(void *impl, int mode) {

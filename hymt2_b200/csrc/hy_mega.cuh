@@ -155,7 +155,8 @@ __device__ __forceinline__ void bar_arrive(const MegaArgs &a, unsigned &target) 
     target += gridDim.x;
     if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(&a.sync->bar) : "memory");
 }
-__device__ __forceinline__ bool bar_wait(const MegaArgs &a, unsigned target, int *s_flag) {
+__device__ __forceinline__ bool bar_wait(const MegaArgs &a, unsigned target, int *s_flag,
+                                         unsigned long long limit_ns = kMegaWaitNs) {
     if (threadIdx.x == 0) {
         int bad = 0;
         if ((int)(ld_acquire_u32(&a.sync->bar) - target) < 0) {
@@ -164,7 +165,7 @@ __device__ __forceinline__ bool bar_wait(const MegaArgs &a, unsigned target, int
             while ((int)(ld_acquire_u32(&a.sync->bar) - target) < 0) {
                 if ((++it & 63) == 0) {
                     if (ld_relaxed_s32(&a.sync->err)) { bad = 1; break; }
-                    if (gtimer() - t0 > kMegaWaitNs) { raise_err(a, MEGA_ERR_BARRIER); bad = 1; break; }
+                    if (gtimer() - t0 > limit_ns) { raise_err(a, MEGA_ERR_BARRIER); bad = 1; break; }
                 }
             }
         }

@@ -150,11 +150,11 @@ __device__ __forceinline__ bool tc_mbar_try(uint64_t *b, unsigned parity) {
         : "memory");
     return ok != 0;
 }
-__device__ __forceinline__ bool tc_mbar_wait(uint64_t *b, unsigned parity) {
+__device__ __forceinline__ bool tc_mbar_wait(uint64_t *b, unsigned parity, unsigned long long limit_ns = kTcWaitNs) {
     if (tc_mbar_try(b, parity)) return true;
     const unsigned long long t0 = gtimer();
     while (!tc_mbar_try(b, parity))
-        if (gtimer() - t0 > kTcWaitNs) return false;
+        if (gtimer() - t0 > limit_ns) return false;
     return true;
 }
 __device__ __forceinline__ void tc_bulk(void *dst, const void *src, unsigned bytes, uint64_t *bar) {

@@ -114,6 +114,15 @@ HYC_API int hyc_set_tc(void *impl, int on);
 HYC_API int hyc_tc_test(void *impl, hy_dweight *w, int act, const float *x, const float *x2, const float *norm_w,
                         float eps, int nt, float *out);
 HYC_API int hyc_decode_path(void *impl, char *why, int cap);
+/* Failure detection without a fault: runs the bounded waits of the
+ * persistent decode kernel (grid barrier) and of the tensor-core GEMM
+ * (mbarrier) on targets nothing reaches, each giving up after limit_ns
+ * (<= 1 s; the kernels themselves use 2 s).  out[0] = 1 if the barrier wait
+ * passed (expected 0), out[1] = the error word it raised (expected 1, the
+ * barrier timeout code the persistent kernel reports through
+ * hyc_decode_read), out[2] = 1 if the mbarrier wait completed (expected 0).
+ * The handle stays usable afterwards.  Returns 0 or -1. */
+HYC_API int hyc_wait_probe(void *impl, unsigned long long limit_ns, int *out);
 
 /* ---- ragged multi-sequence batches and the continuous-batching server --
  * (additive extension, no reference counterpart: the reference serves one

@@ -112,3 +112,22 @@ def test_persistent_matches_graph_full_size(backend, synth, model_dir):
         _compare(dm, backend, ids, 20, [12, 7])
     finally:
         dm.close()
+
+
+def test_bounded_waits_report_and_leave_the_handle_usable(backend, synth, model_dir):
+    """The grid barrier of the persistent kernel and the mbarrier waits of
+    the tensor-core GEMM give up after their limit (here 2 ms on targets
+    that nothing reaches) and report it through status words the host reads;
+    no trap, no fault, no hang, and the same handle then decodes normally."""
+    import time
+    from hymt2_b200.device import DeviceModel
+    out = np.zeros(3, dtype=np.int32)
+    t0 = time.perf_counter()
+    assert backend.lib.hyc_wait_probe(backend.impl, 2_000_000, out.ctypes.data) == 0, backend.error()
+    assert time.perf_counter() - t0 >= 0.004     # both waits ran out their 2 ms
+    assert out.tolist() == [0, 1, 0]             # barrier gave up, raised the barrier timeout code; mbarrier gave up
+    dm = DeviceModel(synth.ensure("t_stq", model_dir), backend, ctx=128)
+    try:
+        assert len(dm.generate([1, 2, 3, 4], 4)) == 4
+    finally:
+        dm.close()
