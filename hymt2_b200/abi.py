@@ -91,7 +91,7 @@ SIGNATURES = {
     "hyc_batch_forward": (I, [P, P, P, P, I, P, I, I, P, P]),
     "hyc_batch_kv_copy": (I, [P, I, I, I]),
     "hyc_batch_kv_read": (I, [P, I, I, I, P, P]),
-    "hyc_serve": (I, [P, P, P, I, I, I, I, P, C.POINTER(ServeStats)]),
+    "hyc_serve": (I, [P, P, P, I, I, P, I, I, I, P, P, C.POINTER(ServeStats)]),
     "hyc_mega_timeline": (I, [P, P, I]),
     "hyc_quantize_q8k": (I, [P, P, I, I, P]),
     "hyc_block_ints": (I, [P, P, P, I, P]),

@@ -1640,15 +1640,19 @@ HYC_API int hyc_batch_kv_read(void *impl, int slot, int layer, int npos, uint16_
     return 0;
 }
 
-HYC_API int hyc_serve(void *impl, const int *prompts, const int *prompt_off, int nreq, int max_new, int vocab_out,
-                      int step_tokens, int *out_ids, hyc_serve_stats *stats) {
+HYC_API int hyc_serve(void *impl, const int *prompts, const int *prompt_off, int nreq, int max_new,
+                      const int *stop_ids, int n_stop, int vocab_out, int step_tokens, int *out_ids, int *out_len,
+                      hyc_serve_stats *stats) {
     HyCtx *c = (HyCtx *)impl;
-    if (!c || c->broken || !c->bat || !prompts || !prompt_off || nreq < 0 || !out_ids ||
-        cudaSetDevice(c->dev) != cudaSuccess)
+    if (!c || c->broken || !c->bat || !prompts || !prompt_off || nreq < 0 || !out_ids || !out_len || n_stop < 0 ||
+        n_stop > 16 || (n_stop > 0 && !stop_ids) || cudaSetDevice(c->dev) != cudaSuccess)
         return -1;
     hyc_serve_stats local;
     const int vo = vocab_out > 0 && vocab_out <= c->outw->n ? vocab_out : c->outw->n;
-    return serve_run(c, prompts, prompt_off, nreq, max_new, vo, step_tokens, out_ids, stats ? stats : &local) ? 0 : -1;
+    return serve_run(c, prompts, prompt_off, nreq, max_new, stop_ids, n_stop, vo, step_tokens, out_ids, out_len,
+                     stats ? stats : &local)
+               ? 0
+               : -1;
 }
 
 HYC_API int hyc_wait_probe(void *impl, unsigned long long limit_ns, int *out) {

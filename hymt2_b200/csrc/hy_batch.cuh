@@ -12,7 +12,8 @@
 // argmax per row (reference semantics: first maximum wins, src/model.c:945-948).
 //
 // The server (reference gen_ids, src/model.c:914-958, for many requests at
-// once): every step feeds one token of each decoding sequence plus prompt
+// once; a request ends at max_new ids or at its first stop id, which then
+// frees its slot): every step feeds one token of each decoding sequence plus prompt
 // chunks of newly admitted ones, up to a token budget; a request whose
 // prompt shares at least kServeMinPrefix leading tokens with the cached
 // prefix starts from a device copy of those KV rows (the reference's
@@ -245,10 +246,11 @@ bool kv_copy(HyCtx *c, int src, int dst, int npos) {
 
 struct ServeSeq {
     int req, slot, n, fed, gen, last;
+    bool stopped;  // emitted a stop id
 };
 
-bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_new, int vocab_out, int step_tokens,
-               int *out, hyc_serve_stats *st) {
+bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_new, const int *stop_ids, int n_stop,
+               int vocab_out, int step_tokens, int *out, int *out_len, hyc_serve_stats *st) {
     Batch &b = *c->bat;
     const int S = b.slots, T = b.max_tokens;
     REQ(c, step_tokens >= 1 && step_tokens <= T, "step token budget exceeds the batch capacity");
@@ -264,6 +266,7 @@ bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_n
     int next = 0, done = 0;
     std::vector<int> row_seq;
     memset(st, 0, sizeof *st);
+    for (size_t i = 0; i < (size_t)nreq * max_new; i++) out[i] = -1;
     int *h_tok = b.h_in, *h_slot = b.h_in + T, *h_pos = b.h_in + 2 * T, *h_rows = b.h_in + 3 * T;
     while (done < nreq) {
         // admit while there are free slots
@@ -276,6 +279,7 @@ bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_n
             q.fed = 0;
             q.gen = 0;
             q.last = -1;
+            q.stopped = false;
             const int *p = prompts + off[q.req];
             int l = 0;
             const int lmax = (int)ptoks.size() < q.n - 1 ? (int)ptoks.size() : q.n - 1;
@@ -340,14 +344,17 @@ bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_n
             out[(size_t)q.req * max_new + q.gen] = id;
             q.gen++;
             q.last = id;
+            for (int k = 0; k < n_stop; k++)
+                if (id == stop_ids[k]) q.stopped = true;
         }
         // retire finished sequences
         size_t w = 0;
         for (size_t i = 0; i < act.size(); i++) {
-            if (act[i].fed == act[i].n && act[i].gen >= max_new) {
+            if (act[i].stopped || (act[i].fed == act[i].n && act[i].gen >= max_new)) {
                 free_slots.push_back(act[i].slot);
                 done++;
-                st->generated += max_new;
+                st->generated += act[i].gen;
+                out_len[act[i].req] = act[i].stopped ? act[i].gen - 1 : act[i].gen;  // the stop id is not output
             } else {
                 act[w++] = act[i];
             }

@@ -318,18 +318,26 @@ class DeviceModel:
             raise BackendError("batch_kv_read")
         return k.reshape(npos, kvd), v.reshape(npos, kvd)
 
-    def serve(self, prompts, max_new: int, step_tokens: int):
-        """Greedy generation for many requests with continuous batching; returns ([nreq][max_new] ids, stats)."""
+    def serve(self, prompts, max_new: int, step_tokens: int, stop=()):
+        """Greedy generation for many requests with continuous batching.
+
+        Returns ([nreq][max_new] ids: the ids before a stop id, the stop id, then -1; stats with
+        "lengths", the ids per request before its stop id)."""
         flat = np.ascontiguousarray(np.concatenate([np.asarray(p, dtype=np.int32) for p in prompts]))
         off = np.zeros(len(prompts) + 1, dtype=np.int32)
         off[1:] = np.cumsum([len(p) for p in prompts])
         out = np.zeros((len(prompts), max_new), dtype=np.int32)
+        lens = np.zeros(len(prompts), dtype=np.int32)
+        stops = np.asarray(list(stop) or [0], dtype=np.int32)
         st = abi.ServeStats()
         rc = self.be.lib.hyc_serve(self.be.impl, flat.ctypes.data, off.ctypes.data, len(prompts), max_new,
-                                   self.vocab_out, step_tokens, out.ctypes.data, C.byref(st))
+                                   stops.ctypes.data, len(stop), self.vocab_out, step_tokens, out.ctypes.data,
+                                   lens.ctypes.data, C.byref(st))
         if rc != 0:
             raise BackendError("serve: " + self.be.error())
-        return out, {f: getattr(st, f) for f, _ in abi.ServeStats._fields_}
+        stats = {f: getattr(st, f) for f, _ in abi.ServeStats._fields_}
+        stats["lengths"] = lens
+        return out, stats
 
     def kv(self, layer: int, npos: int):
         kvd = self.hp.kv_heads * self.hp.hdim

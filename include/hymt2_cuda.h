@@ -148,8 +148,11 @@ HYC_API int hyc_wait_probe(void *impl, unsigned long long limit_ns, int *out);
  * request plus prompt chunks of newly admitted ones, at most step_tokens in
  * all (<= max_tokens; max_out must be >= slots), and a prompt that shares
  * >= 8 leading tokens with the first completed prompt starts from a copy of
- * those cached rows (always recomputing its last prompt token).  out_ids
- * is [nreq][max_new].  All return 0 or -1 (hyc_last_error). */
+ * those cached rows (always recomputing its last prompt token).  A request
+ * also ends at its first id in stop_ids (n_stop <= 16), as the reference's
+ * loop breaks there.  out_ids is [nreq][max_new]: the ids before the stop
+ * id, then the stop id, then -1; out_len[r] counts the ids before the stop
+ * id (max_new when none came).  All return 0 or -1 (hyc_last_error). */
 typedef struct hyc_serve_stats {
     long long steps, decode_tokens, prefill_tokens, prefix_hits, prefix_tokens, generated;
 } hyc_serve_stats;
@@ -158,8 +161,9 @@ HYC_API int hyc_batch_forward(void *impl, const int *tokens, const int *tok_slot
                               const int *out_rows, int nout, int vocab_out, int *out_ids, float *logits);
 HYC_API int hyc_batch_kv_copy(void *impl, int src_slot, int dst_slot, int npos);
 HYC_API int hyc_batch_kv_read(void *impl, int slot, int layer, int npos, uint16_t *k, uint16_t *v);
-HYC_API int hyc_serve(void *impl, const int *prompts, const int *prompt_off, int nreq, int max_new, int vocab_out,
-                      int step_tokens, int *out_ids, hyc_serve_stats *stats);
+HYC_API int hyc_serve(void *impl, const int *prompts, const int *prompt_off, int nreq, int max_new,
+                      const int *stop_ids, int n_stop, int vocab_out, int step_tokens, int *out_ids, int *out_len,
+                      hyc_serve_stats *stats);
 
 /* ---- kernel-level hooks for parity tests (host buffers, synchronous) -- */
 

@@ -171,3 +171,30 @@ def test_batch_rejects_bad_input(backend, synth, model_dir):
             dm.batch_prepare(slots=2, slot_ctx=129, max_tokens=64)
     finally:
         dm.close()
+
+
+def test_serve_stop_ids(backend, synth, model_dir):
+    """A request ends at its first stop id (not output; its slot is reused at
+    once); the ids before it are the ones the same request gives without
+    stop ids."""
+    from hymt2_b200.device import DeviceModel
+    dm = DeviceModel(synth.ensure("t_stq", model_dir), backend, ctx=256)
+    try:
+        rng = np.random.default_rng(23)
+        prompts = [rng.integers(0, dm.vocab_out, int(rng.integers(10, 40))).tolist() for _ in range(12)]
+        dm.batch_prepare(slots=4, slot_ctx=64, max_tokens=64)
+        free, st0 = dm.serve(prompts, 8, step_tokens=48)
+        assert (st0["lengths"] == 8).all()
+        stop = int(free[0, 2])
+        out, st = dm.serve(prompts, 8, step_tokens=48, stop=[stop])
+        for r in range(len(prompts)):
+            row = free[r].tolist()
+            n = row.index(stop) if stop in row else 8
+            assert st["lengths"][r] == n, (r, st["lengths"][r], n)
+            assert out[r, :n].tolist() == row[:n]
+            if n < 8:
+                assert out[r, n] == stop and (out[r, n + 1:] == -1).all()
+        assert st["lengths"][0] == free[0].tolist().index(stop) <= 2  # its first occurrence ends request 0
+        assert st["generated"] < st0["generated"]
+    finally:
+        dm.close()
