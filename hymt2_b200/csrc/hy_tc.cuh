@@ -227,10 +227,12 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
     constexpr int N = tc_n(P), SUB = N / NM, C = NM / 4, AH = kTcABytes / 2, SB = tc_sbytes(P);
     constexpr int STB = tc_stage_bytes(P, NM), SLB = tc_slot_bytes(NM);
     constexpr int kTcStages = tc_stages(P, NM), kTcScaleSlots = tc_slots(P, NM);
+    // accumulator sets: as many as TMEM holds, up to 4 (the MMA runs that many blocks ahead of the epilogue)
+    constexpr int NBUF = 512 / (P * NM) > 4 ? 4 : 512 / (P * NM);
     static_assert(N % NM == 0 && NM % 64 == 0, "MMA rows must be a slice of the weight tile");
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], sfull[kTcScaleSlots], sempty[kTcScaleSlots],
-        accf[2], acce[2], fin;
+        accf[4], acce[4], fin;
     // launched as a programmatic dependent: barrier setup and the TMEM
     // allocation overlap the previous kernel; the producer waits for it
     // before its first copy (everything else follows the producer)
@@ -249,7 +251,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
             tc_mbar_init(&sfull[s], 1);
             tc_mbar_init(&sempty[s], kTcEpiWarps);
         }
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < NBUF; b++) {
             tc_mbar_init(&accf[b], 1);
             tc_mbar_init(&acce[b], kTcEpiWarps);
         }
@@ -323,7 +325,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
             int g = 0, hs = 0;
             for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
                 for (int kb = 0; kb < nb && ok; kb++, g++) {
-                    const int buf = g & 1, ub = g >> 1;
+                    const int buf = g % NBUF, ub = g / NBUF;
                     if (ub > 0 && !tc_mbar_wait(&acce[buf], (ub - 1) & 1)) {
                         ok = false;
                         break;
@@ -363,7 +365,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
 #pragma unroll
             for (int j = 0; j < C; j++) acc[j] = 0.f;
             for (int kb = 0; kb < nb; kb++, g++) {
-                const int buf = g & 1, ub = g >> 1, sl = g % kTcScaleSlots;
+                const int buf = g % NBUF, ub = g / NBUF, sl = g % kTcScaleSlots;
                 if (!tc_mbar_wait(&accf[buf], ub & 1) || !tc_mbar_wait(&sfull[sl], (g / kTcScaleSlots) & 1)) {
                     ok = false;
                     break;
