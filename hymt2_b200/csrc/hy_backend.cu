@@ -51,6 +51,7 @@ struct HyWeight {
     HyCtx *c;
     int8_t *tc_w;   // tensor-core tiles of a panel weight (lazy, hy_tc.cuh layout)
     float *tc_ws;   // their block scales
+    int8_t *tc_w64; // the tiles 64-row slices first (lazy: launches of 64-row slices of wider tiles)
 };
 
 struct Layer {
@@ -422,6 +423,20 @@ bool tc_weight(HyCtx *c, HyWeight *w) {
     return true;
 }
 
+// The slice-first copy of a weight's tiles, built on first use.
+bool tc_slices(HyCtx *c, HyWeight *w) {
+    if (w->tc_w64) return true;
+    const int P = tc_planes(w->fmt), N = tc_n(P);
+    const size_t bytes = (size_t)((w->n + N - 1) / N) * w->nb * tc_bbytes(P);
+    CK(c, cudaMalloc(&w->tc_w64, bytes));
+    const long long units = (long long)(bytes / 16);
+    const unsigned grid = (unsigned)((units + 255) / 256);
+    if (P == 1) tc_tiles_to_slices<1><<<grid, 256, 0, c->st>>>(w->tc_w, w->tc_w64, units);
+    else tc_tiles_to_slices<2><<<grid, 256, 0, c->st>>>(w->tc_w, w->tc_w64, units);
+    CK(c, cudaGetLastError());
+    return true;
+}
+
 bool tc_scratch(HyCtx *c, int K) {
     const size_t nbmax = (size_t)(K / 256), tmax = (size_t)(c->max_tokens + kTcM - 1) / kTcM * kTcM;
     const size_t bytes = tmax * nbmax * kTcKB;
@@ -493,6 +508,13 @@ bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float
         // whole tiles would leave SMs idle
         const int NM = tc_tiles_all(P, tc_n(P), ta) >= c->nsm ? tc_n(P) : 64;
         const int ntiles = tc_tiles_all(P, NM, ta);
+        if (NM < tc_n(P))
+            for (int j = 0; j < cnt; j++)
+                if (tc_planes(ws[j]->fmt) == P) {
+                    if (!tc_slices(c, ws[j])) return false;
+                    for (int q = 0; q < ta.nw; q++)
+                        if (ta.w[q] == ws[j]->tc_w) ta.w64[q] = ws[j]->tc_w64;
+                }
         const dim3 grid(ntiles < c->nsm ? ntiles : c->nsm), blk(kTcThreads);
         bool ok;
         if (P == 1 && NM == 256) ok = launch(c, tc_gemm<1, 256>, grid, blk, tc_smem_bytes(1, 256), pdl, ta);
@@ -1099,6 +1121,7 @@ void release(hy_dweight *hw) {
     if (w->h_out) cudaFreeHost(w->h_out);
     if (w->tc_w) cudaFree(w->tc_w);
     if (w->tc_ws) cudaFree(w->tc_ws);
+    if (w->tc_w64) cudaFree(w->tc_w64);
     delete w;
 }
 

@@ -24,7 +24,10 @@
 // contiguous.  Activations: [m tile][block][128 x 256]; weights: [n tile]
 // [block][half][P*N x 128] with the planes stacked as rows, so one bulk copy
 // moves the A half or the B half of a stage and one MMA (N' = P*NM <= 256)
-// multiplies the activations with every plane, reading them once.
+// multiplies the activations with every plane, reading them once.  Launches
+// that multiply 64-row slices of 256 / 128-row tiles (short passes) read a
+// second copy of the weight ordered slice first, [n tile][block][half]
+// [slice][P*64 x 128], so a slice's half block is one bulk copy too.
 //
 // Persistent CTAs (one per SM) walk the (m, n) tiles m-fastest, so the
 // CTAs running at one time share each weight tile through L2.  Per CTA:
@@ -100,6 +103,7 @@ struct TcArgs {
     const float *ad;   // activation block scales [ceil(T/128)][nb][128]
     int nw;            // weights in this launch; their tiles follow one another
     const int8_t *w[kTcMaxW];   // tiled weight [ceil(N/n)][nb][2][P][n x 128]
+    const int8_t *w64[kTcMaxW]; // the same, 64-row slices first (launches with NM = 64 < n)
     const float *ws[kTcMaxW];   // tiled weight scales [ceil(N/n)][nb][2][n]
     float *out[kTcMaxW];        // [T][ldo]
     int ldo[kTcMaxW], N[kTcMaxW];
@@ -230,6 +234,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
     // accumulator sets: as many as TMEM holds, up to 4 (the MMA runs that many blocks ahead of the epilogue)
     constexpr int NBUF = 512 / (P * NM) > 4 ? 4 : 512 / (P * NM);
     static_assert(N % NM == 0 && NM % 64 == 0, "MMA rows must be a slice of the weight tile");
+    static_assert(SUB == 1 || NM == 64, "slices are read from the 64-row slice-first copy");
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], sfull[kTcScaleSlots], sempty[kTcScaleSlots],
         accf[4], acce[4], fin;
@@ -302,15 +307,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                         if constexpr (SUB == 1) {
                             tc_bulk(st + AH, wb, P * N * kTcKH, &full[s]);
                         } else {
-                            // per 16-byte K chunk and plane, the slice's 8-row groups: NM * 16
-                            // contiguous bytes, placed as rows p*NM .. of a P*NM-row tile
-#pragma unroll
-                            for (int c = 0; c < kTcKH / 16; c++)
-#pragma unroll
-                                for (int p = 0; p < P; p++)
-                                    tc_bulk(st + AH + ((size_t)c * (P * NM / 8) + p * (NM / 8)) * 128,
-                                            wb + ((size_t)c * (P * N / 8) + p * (N / 8) + si * (NM / 8)) * 128,
-                                            NM * 16, &full[s]);
+                            // the slice-first copy: the slice's P*64 x 128 canonical tile is contiguous
+                            const int8_t *wsl = a.w64[wi] + ((size_t)nt * nb + kb) * tc_bbytes(P) +
+                                                (size_t)h * P * N * kTcKH + (size_t)si * P * NM * kTcKH;
+                            tc_bulk(st + AH, wsl, P * NM * kTcKH, &full[s]);
                         }
                     }
                 }
@@ -530,6 +530,20 @@ __global__ void tc_weight_to_tiled(const __grid_constant__ WDesc w, int8_t *tw, 
         sd[r] = s1;
         sd[N + r] = s2;
     }
+}
+
+// The slice-first copy of a tiled weight (P planes, N = tc_n(P) > 64 rows per
+// tile): each half block [chunk c][plane p][row r][16 bytes] becomes
+// [slice r / 64][c][p][r % 64][16 bytes]; one thread per 16 bytes.
+template <int P>
+__global__ void tc_tiles_to_slices(const int8_t *tw, int8_t *tw64, long long units) {
+    constexpr int N = tc_n(P), HU = (kTcKH / 16) * P * N;  // 16-byte units per half block
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= units) return;
+    const long long hb = i / HU;
+    const int u = (int)(i % HU), r = u % N, cp = u / N;  // cp = c * P + p
+    const long long o = hb * HU + (long long)(r / 64) * ((kTcKH / 16) * P * 64) + (long long)cp * 64 + (r % 64);
+    ((uint4 *)tw64)[o] = ((const uint4 *)tw)[i];
 }
 
 // Q8_K codes of one 256 block held by a warp (lane: elements 8 lane ..
