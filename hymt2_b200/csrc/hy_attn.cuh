@@ -27,8 +27,6 @@ struct AttnArgs {
     int split_len, max_splits;
     float *cpart;           // wide decode partials [heads][max_chunks][HD+kPartPad]
     int max_chunks, units;  // attn_max_chunks(ctx); units available (SMs)
-    unsigned long long *tpart;  // if set: partials as tagged words (float bits | ptag << 32) instead
-    unsigned ptag;
     int trace;              // timeline slot (< 0: off)
     // ragged batch of several sequences (prefill kernels only): token t sits
     // at position tok_pos[t] of sequence slot tok_slot[t], whose cache starts
@@ -739,27 +737,12 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
         for (int q = 0; q < DPL; q++) O[q] = fmaf(S.po[src][lane * DPL + q], f, O[q]);
     }
     const size_t po = ((size_t)(kvh * G + w) * a.max_chunks + chunk) * (HD + kPartPad);
-    if (a.tpart) {
-        unsigned long long *tp = a.tpart + po;
+    float *pp = a.cpart + po;
 #pragma unroll
-        for (int q = 0; q < DPL; q += 2)
-            asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(tp + kPartPad + lane * DPL + q),
-                         "l"((unsigned long long)__float_as_uint(O[q]) | ((unsigned long long)a.ptag << 32)),
-                         "l"((unsigned long long)__float_as_uint(O[q + 1]) | ((unsigned long long)a.ptag << 32))
-                         : "memory");
-        if (lane == 0)
-            asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(tp),
-                         "l"((unsigned long long)__float_as_uint(M) | ((unsigned long long)a.ptag << 32)),
-                         "l"((unsigned long long)__float_as_uint(L) | ((unsigned long long)a.ptag << 32))
-                         : "memory");
-    } else {
-        float *pp = a.cpart + po;
-#pragma unroll
-        for (int q = 0; q < DPL; q++) pp[kPartPad + lane * DPL + q] = O[q];
-        if (lane == 0) {
-            pp[0] = M;
-            pp[1] = L;
-        }
+    for (int q = 0; q < DPL; q++) pp[kPartPad + lane * DPL + q] = O[q];
+    if (lane == 0) {
+        pp[0] = M;
+        pp[1] = L;
     }
 }
 
