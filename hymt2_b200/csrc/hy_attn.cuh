@@ -910,13 +910,101 @@ __global__ void __launch_bounds__(32) attn_merge_kernel(const __grid_constant__ 
     attn_merge_head<HD>(a.cpart, a.max_chunks, (pos + cs) / cs, blockIdx.x, a.ao + (size_t)blockIdx.x * HD);
 }
 
+// attn_prefill's dynamic shared memory: per warp the V rows of one 32-key tile.
+template <int HD, int G>
+__host__ __device__ constexpr size_t prefill_stage_bytes() {
+    return (size_t)G * 32 * HD * 2;
+}
+
+// attend_range over keys [0, j1) that are all in the cache, with every global
+// load of a tile in flight at once: the tile's V rows go to this warp's
+// shared buffer sv (cp.async) before the scores are computed, and each lane
+// loads its key's whole K row into registers.  The arithmetic, and its order,
+// is attend_range's, so the results are bit-identical to it.
+template <int HD, int G>
+__device__ __forceinline__ void attend_range_staged(const AttnArgs &a, const uint16_t *kc, const uint16_t *vc, int kvh,
+                                                    int j1, const float (*sq)[HD], uint16_t *sv, float (&m)[G],
+                                                    float (&l)[G], float (&o)[G][HD / 32]) {
+    constexpr int CH = HD / 8;  // 16-byte chunks per row
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll
+    for (int h = 0; h < G; h++) {
+        m[h] = -INFINITY;
+        l[h] = 0.f;
+#pragma unroll
+        for (int i = 0; i < HD / 32; i++) o[h][i] = 0.f;
+    }
+    const uint16_t *Kb = kc + kvh * HD, *Vb = vc + kvh * HD;
+    for (int tile = w * 32; tile < j1; tile += G * 32) {
+        const int nk = min(32, j1 - tile);
+        for (int i = lane; i < nk * CH; i += 32) {
+            const int r = i / CH, c = i - r * CH;
+            cp_async16(sv + r * HD + c * 8, Vb + (size_t)(tile + r) * a.kvdim + c * 8);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        const int j = tile + lane;
+        const bool valid = j < j1;
+        float s[G];
+#pragma unroll
+        for (int h = 0; h < G; h++) s[h] = 0.f;
+        if (valid) {
+            const uint16_t *kr = Kb + (size_t)j * a.kvdim;
+            uint4 kk[CH];
+#pragma unroll
+            for (int c = 0; c < CH; c++) kk[c] = *(const uint4 *)(kr + c * 8);
+#pragma unroll
+            for (int c = 0; c < CH; c++) {
+                const uint32_t kw[4] = {kk[c].x, kk[c].y, kk[c].z, kk[c].w};
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    const float k0 = bf16_bits_to_f32(kw[q] & 0xffffu), k1 = bf16_bits_to_f32(kw[q] >> 16);
+#pragma unroll
+                    for (int h = 0; h < G; h++) {
+                        s[h] = fmaf(sq[h][c * 8 + 2 * q], k0, s[h]);
+                        s[h] = fmaf(sq[h][c * 8 + 2 * q + 1], k1, s[h]);
+                    }
+                }
+            }
+        }
+        float p[G];
+#pragma unroll
+        for (int h = 0; h < G; h++) {
+            const float sc = valid ? s[h] * a.scale : -INFINITY;
+            const float mt = warp_max(sc);
+            const float mn = fmaxf(m[h], mt);
+            const float corr = expf(m[h] - mn);
+            p[h] = valid ? expf(sc - mn) : 0.f;
+            l[h] = l[h] * corr + warp_sum(p[h]);
+            m[h] = mn;
+#pragma unroll
+            for (int i = 0; i < HD / 32; i++) o[h][i] *= corr;
+        }
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncwarp();
+        for (int jj = 0; jj < nk; jj++) {
+            float vv[HD / 32];
+#pragma unroll
+            for (int i = 0; i < HD / 32; i++) vv[i] = bf16_bits_to_f32(sv[jj * HD + lane + 32 * i]);
+#pragma unroll
+            for (int h = 0; h < G; h++) {
+                const float pj = __shfl_sync(0xffffffffu, p[h], jj);
+#pragma unroll
+                for (int i = 0; i < HD / 32; i++) o[h][i] = fmaf(pj, vv[i], o[h][i]);
+            }
+        }
+        __syncwarp();  // the buffer is free for the next tile
+    }
+}
+
 // Prefill: token t (position *pos_ptr + t) attends to 0..pos inclusive; q
 // already rotated/normalised and k/v already in the cache (rope_norm_store).
-// grid (kv_heads, nt), G warps.
+// grid (kv_heads, nt), G warps, prefill_stage_bytes<HD, G>() of dynamic
+// shared memory.
 template <int HD, int G>
 __global__ void __launch_bounds__(G * 32) attn_prefill(const __grid_constant__ AttnArgs a) {
     pdl_trigger();
     __shared__ AttnSmem<HD, G> S;
+    extern __shared__ __align__(16) uint8_t dsm[];
     const int kvh = blockIdx.x, t = blockIdx.y;
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_wait();
@@ -927,7 +1015,7 @@ __global__ void __launch_bounds__(G * 32) attn_prefill(const __grid_constant__ A
     for (int i = 0; i < HD / 32; i++) S.sq[w][lane + 32 * i] = qr[lane + 32 * i];
     __syncthreads();
     float m[G], l[G], o[G][HD / 32];
-    attend_range<HD, G>(a, a.kc + kvo, a.vc + kvo, kvh, 0, pos + 1, -1, S.sq, S.sk, S.sv, m, l, o);
+    attend_range_staged<HD, G>(a, a.kc + kvo, a.vc + kvo, kvh, pos + 1, S.sq, (uint16_t *)dsm + w * 32 * HD, m, l, o);
 #pragma unroll
     for (int h = 0; h < G; h++) {
         if (lane == 0) {

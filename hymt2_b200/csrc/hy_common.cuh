@@ -138,4 +138,10 @@ struct WDesc {
     int fmt, n, k, shift, off, ld;
 };
 
+// 16-byte asynchronous global -> shared copy (L2 only), one commit group per caller.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+
 }  // namespace hyk

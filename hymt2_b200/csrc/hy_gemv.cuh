@@ -446,10 +446,6 @@ __host__ __device__ inline size_t panel_dec_smem(int rows_per_cta, int K) {
     return align16((size_t)rows_per_cta * nb * 64) + align16((size_t)rows_per_cta * nb * 4) + q8_smem_bytes(1, K);
 }
 
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
-}
 __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
     const unsigned d = (unsigned)__cvta_generic_to_shared(dst);
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
