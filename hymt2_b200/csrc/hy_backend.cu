@@ -481,7 +481,7 @@ bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float
         bool ok;
         if ((pro.act == ACT_VEC || pro.act == ACT_SILU) && pro.ldx % 8 == 0) {
             const long long ctas = ((long long)tpad * nb + 7) / 8;
-            const unsigned grid = (unsigned)(ctas < 8LL * c->nsm ? ctas : 8LL * c->nsm);
+            const unsigned grid = (unsigned)(ctas < 32LL * c->nsm ? ctas : 32LL * c->nsm);
             ok = launch(c, tc_quantize_blocks, dim3(grid), dim3(256), 0, pdl, pro, nt, tpad, c->d_tca, c->d_tcad);
         } else if (sv <= 2) ok = launch(c, tc_quantize<2>, g, b, sm, pdl, pro, nt, c->d_tca, c->d_tcad);
         else if (sv <= 4) ok = launch(c, tc_quantize<4>, g, b, sm, pdl, pro, nt, c->d_tca, c->d_tcad);
@@ -563,7 +563,7 @@ bool attn_launch(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
                       pdl, aa);
     int warps = aa.heads + aa.kv_heads;
     if (warps > 32) warps = 32;
-    const int rgrid = nt < 4 * c->nsm ? nt : 4 * c->nsm;
+    const int rgrid = nt < 16 * c->nsm ? nt : 16 * c->nsm;
     if (!launch(c, rope_norm_store<HD>, dim3(rgrid), dim3(warps * 32), 0, pdl, aa)) return false;
     const int nqb = aa.qblk ? aa.nqb : (nt + kFaQ - 1) / kFaQ;
     if (nqb == nt)  // one token per sequence (a batch of decode steps): the per-token kernel is faster
