@@ -23,6 +23,8 @@ flush is needed between steps.
   prefill_c2   config 2 (N = 1): 32 x 256-token Q4_K_M prefill on the tensor
                cores, with its int8 roofline and the reference CPU prefill
   decode_c1    config 1 (N = 1): Q2_0C bs1 decode after a 512-token prompt
+  decode_c4    config 4's model on ONE GPU (its tensor parallelism is not
+               built): Q8_0 bs1 decode at KV length 4096, graph path
 
 `--impl reference` times the reference's own CPU implementation of the path
 (oracle/_ref/libhymt2_ref.so, built from its sources) on the same config.
@@ -434,6 +436,73 @@ def bench_c1(args, be, torch, peak) -> dict:
         dm.close()
 
 
+C4_PROMPT, C4_GEN = 4096, 64
+# config 4 bytes per decode step: Q8_0 (34 B per 32 weights) layers and tied head as stored
+C4_LAYER_BYTES = L * ((QD + 2 * KVD) * H + H * QD + 3 * FFN * H) * 34 // 32
+C4_HEAD_BYTES = VOCAB * H * 34 // 32
+
+
+def bench_c4(args, be, torch, peak) -> dict:
+    """Config 4's model (Q8_0 everywhere, tied Q8_0 head) on one GPU: bs1
+    greedy decode of 64 tokens after a 4096-token seeded prompt, so the
+    attention reads K/V rows at positions 4096..4159; CUDA events over the 63
+    decode steps (one CUDA graph of per-layer kernels per step).  The
+    reference's tensor-parallel split of this config is not built here."""
+    from hymt2_b200 import synth
+    from hymt2_b200.device import DeviceModel
+    path = synth.ensure("c4_q8_0", args.model_dir)
+    dm = DeviceModel(path, be, ctx=C4_PROMPT + C4_GEN + 64)
+    try:
+        lib, impl = be.lib, be.impl
+        ids = np.random.default_rng(1).integers(0, VOCAB, C4_PROMPT).astype(np.int32)
+        stream = torch.cuda.ExternalStream(be.stream())
+        for _ in range(2):
+            if lib.hyc_decode_begin(impl, ids.ctypes.data, C4_PROMPT, 0, C4_GEN, None, 0, dm.vocab_out) != 0:
+                raise RuntimeError("decode_begin: " + be.error())
+            be.sync()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            if lib.hyc_decode_steps(impl, C4_GEN - 1) != 0:
+                raise RuntimeError("decode_steps: " + be.error())
+            e1.record(stream)
+            torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        import ctypes
+        why = ctypes.create_string_buffer(128)
+        lib.hyc_decode_path(impl, why, 128)
+        path_why = why.value.decode()
+        kv = L * 2 * (C4_PROMPT + (C4_GEN - 1) / 2) * KVD * 2
+        step_bytes = C4_LAYER_BYTES + C4_HEAD_BYTES + kv
+        step_ms = ms / (C4_GEN - 1)
+        out = {"value": round((C4_GEN - 1) / (ms / 1e3), 1), "unit": UNIT, "ms_per_step": round(step_ms, 4),
+               "workload": "c4_q8_0 on one GPU: Q8_0 layers and tied Q8_0 head (fp32 activations); bs1 greedy "
+                           "decode, 4096-token seeded prompt, 64 tokens (positions 4096..4159); tensor "
+                           "parallelism of config 4 not built",
+               "roofline_step": {"bytes_per_step": int(step_bytes),
+                                 "achieved_gbs": round(step_bytes / step_ms / 1e6, 1),
+                                 "frac": round(step_bytes / step_ms / 1e6 / peak, 4)},
+               "cpu_baseline": {"unavailable": "the reference's Q8_0 rows are scalar fp32 on the CPU; a 4096-token "
+                                               "prefill there is far beyond this bench's time budget"}}
+        if path_why:
+            out["decode_path"] = path_why
+        return out
+    finally:
+        dm.close()
+
+
+def quant_gemv_entry(kernels, peak):
+    """The quant-GEMV HBM figure: the STQ1_0 panel gate|up GEMV at one token
+    (two 6144 x 2048 panels, the reference kernel benchmark's shape, in one
+    launch), bytes as streamed / CUDA-event time per launch, cycling over the
+    32 layers' weights (more than L2 holds)."""
+    k = kernels.get("gate_up_gemv_panel")
+    if not k:
+        return None
+    return {"kernel": "gate_up_gemv_panel (gemv_panel_dec, STQ1_0 panel 2 x 6144 x 2048, nt 1)",
+            "gbs": k["gbs"], "frac": round(k["gbs"] / peak, 4), "bytes_per_launch": k["bytes_per_launch"],
+            "ms_per_launch": k["ms_per_launch"]}
+
+
 def run_reference_arm(args, rank, world):
     if rank != 0:
         return
@@ -577,8 +646,13 @@ def main():
         dom_entry = ("decode_mega", {"ms_per_launch": round(t, 4), "launches_per_step": 1.0 / GEN_LEN,
                                      "steps_per_launch": GEN_LEN, "bytes_per_launch": nbytes,
                                      "gbs": round(nbytes / (t / 1e3) / 1e9, 1)})
-    for op, (name, per_step, nbytes) in (OPS.items() if (args.graph_breakdown or not persistent) else []):
-        iters = 20 if op == 0 else 64
+    # per-layer kernels, each over all 32 layers' weights in turn (more bytes than L2 holds); the four
+    # layer GEMVs always (the quant-GEMV HBM figure), the head and attention with --graph-breakdown or
+    # when the step runs as a graph
+    for op, (name, per_step, nbytes) in OPS.items():
+        if op in (0, 5) and not (args.graph_breakdown or not persistent):
+            continue
+        iters = 20 if op == 0 else 128
         check(lib.hyc_bench_op(impl, op, 4), "bench_op warm")
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
@@ -628,6 +702,7 @@ def main():
             "roofline_step": {"bytes_per_step": STEP_BYTES, "achieved_gbs": round(STEP_BYTES / step_ms / 1e6, 1),
                               "frac": round(STEP_BYTES / step_ms / 1e6 / peak, 4)},
             "kernels": kernels,
+            "quant_gemv": quant_gemv_entry(kernels, peak),
             "gpu_launches": int(launches),
             "clocks": clk,
             "device": be.info,
@@ -645,7 +720,8 @@ def main():
     if rank == 0 and world == 1 and not args.no_extra:
         tops, tops_kind = int8_peak(torch)
         for key, fn in (("prefill_c2", lambda: bench_prefill(args, be, torch, tops, tops_kind)),
-                        ("decode_c1", lambda: bench_c1(args, be, torch, peak))):
+                        ("decode_c1", lambda: bench_c1(args, be, torch, peak)),
+                        ("decode_c4", lambda: bench_c4(args, be, torch, peak))):
             try:
                 out[key] = fn()
             except Exception as e:  # noqa: BLE001 - report, do not lose the headline

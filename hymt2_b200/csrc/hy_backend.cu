@@ -345,6 +345,12 @@ bool gemv_launch(HyCtx *c, const GemvArgs &a_in, bool pdl, int ctas_per_sm) {
     }
     const int NT = a.nt == 1 ? 1 : 4;
     const size_t smem = fp_smem_bytes(NT, a.k);
+    if (NT == 1) {
+        // one token: the rows stream from HBM, so up to 2 CTAs per SM keep more loads in flight
+        const int cap = c->nsm * (ctas_per_sm > 2 ? ctas_per_sm : 2);
+        grid = (a.rows_total + kGemvWarps - 1) / kGemvWarps;
+        if (grid > cap) grid = cap;
+    }
     if (fmt == FMT_Q80) return NT == 1 ? launch(c, gemv_fp<FMT_Q80, 1>, grid, blk, smem, pdl, a)
                                        : launch(c, gemv_fp<FMT_Q80, 4>, grid, blk, smem, pdl, a);
     if (fmt == FMT_F16) return NT == 1 ? launch(c, gemv_fp<FMT_F16, 1>, grid, blk, smem, pdl, a)

@@ -20,6 +20,7 @@
 namespace hyk {
 
 constexpr int kGemvWarps = 8;
+constexpr int kFpInFlight = 8;  // gemv_fp: 16-byte weight units per lane loaded ahead
 constexpr int kGemvThreads = kGemvWarps * 32;
 
 struct GemvArgs {
@@ -889,18 +890,36 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_fp(const __grid_constant__ 
         float acc[NT];
 #pragma unroll
         for (int t = 0; t < NT; t++) acc[t] = 0.f;
-        for (int u0 = 0; u0 < nunit; u0 += 32) {
+        // kFpInFlight 16-byte units of the row per lane are loaded before any
+        // arithmetic (enough bytes in flight to cover HBM latency); the
+        // arithmetic and its order are per unit as before
+        constexpr int PF = kFpInFlight;
+        for (int c0 = 0; c0 < nunit; c0 += 32 * PF) {
+        uint4 vv[PF];
+        unsigned short sv[PF];
+#pragma unroll
+        for (int i = 0; i < PF; i++) {
+            const int u = c0 + 32 * i + lane;
+            if (u < nunit) {
+                vv[i] = ldg_stream(row + (size_t)u * 16);
+                if (FMT == FMT_Q80) sv[i] = __ldg((const unsigned short *)(row + K) + (u >> 1));
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < PF; i++) {
+            const int u0 = c0 + 32 * i;
+            if (u0 >= nunit) break;  // uniform across the warp
             const int u = u0 + lane;
             const bool ok = u < nunit;
             float wf[E];
             float scale = 1.f;
             if (ok) {
-                const uint4 v = ldg_stream(row + (size_t)u * 16);
+                const uint4 v = vv[i];
                 if (FMT == FMT_Q80) {
                     const int8_t *q = (const int8_t *)&v;
 #pragma unroll
                     for (int j = 0; j < E; j++) wf[j] = (float)q[j];
-                    scale = h2f(__ldg((const unsigned short *)(row + K) + (u >> 1)));
+                    scale = h2f(sv[i]);
                 } else if (FMT == FMT_F16) {
                     const __half *h = (const __half *)&v;
 #pragma unroll
@@ -936,6 +955,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_fp(const __grid_constant__ 
                     acc[t] += p;
                 }
             }
+        }
         }
 #pragma unroll
         for (int t = 0; t < NT; t++) acc[t] = warp_sum(acc[t]);

@@ -99,6 +99,30 @@ def test_device_greedy_matches_oracle(backend, oracle, tiny_models, cfg):
         om.close()
 
 
+@pytest.mark.parametrize("cfg", ["t_stq", "t_q8_0"])
+def test_long_context_decode_matches_oracle(backend, oracle, tiny_models, cfg):
+    """Greedy decode past position 4096 (the KV length of the Q8_0 config):
+    a 4100-token prefill, then decode steps whose attention spans 33 key
+    splits, give the oracle's ids.  Near ties are judged with a fixed 1e-3
+    relative margin (the fp64-vs-fp32 spread rule needs minutes of numpy at
+    this length; it measures ~1e-5 for these models)."""
+    import oracle as O
+    from hymt2_b200.device import DeviceModel
+    path = tiny_models[cfg]
+    ctx, n = 4224, 4100
+    dm = DeviceModel(path, backend, ctx=ctx)
+    om = O.OracleModel(oracle, path, ctx=ctx)
+    try:
+        ids = np.random.default_rng(9).integers(0, dm.vocab_out, n).tolist()
+        got = dm.generate(ids, 4)
+        want, steps = om.greedy(ids, 4, chunk=16, step_logits=True)
+        d = _first_divergence(got, want)
+        assert d is None or _near_tie(steps[d], 1e-3), (cfg, got, want)
+    finally:
+        dm.close()
+        om.close()
+
+
 def test_decode_host_io_path_same_ids(backend, tiny_models):
     """The end-to-end form (each step's token through pinned host memory)
     yields the same stream as the device-resident loop."""
