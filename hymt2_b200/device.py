@@ -323,6 +323,8 @@ class DeviceModel:
 
         Returns ([nreq][max_new] ids: the ids before a stop id, the stop id, then -1; stats with
         "lengths", the ids per request before its stop id)."""
+        if len(prompts) == 0:
+            return np.zeros((0, max_new), dtype=np.int32), {"lengths": np.zeros(0, dtype=np.int32)}
         flat = np.ascontiguousarray(np.concatenate([np.asarray(p, dtype=np.int32) for p in prompts]))
         off = np.zeros(len(prompts) + 1, dtype=np.int32)
         off[1:] = np.cumsum([len(p) for p in prompts])

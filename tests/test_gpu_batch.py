@@ -198,3 +198,24 @@ def test_serve_stop_ids(backend, synth, model_dir):
         assert st["generated"] < st0["generated"]
     finally:
         dm.close()
+
+
+def test_serve_edge_cases(backend, synth, model_dir):
+    """No requests gives no output; a request longer than a slot's context is
+    refused on the host and the handle stays usable; token ids outside the
+    vocabulary embed as id 0 (as the persistent decode kernel treats them)."""
+    from hymt2_b200.device import BackendError, DeviceModel
+    dm = DeviceModel(synth.ensure("t_stq", model_dir), backend, ctx=128)
+    try:
+        dm.batch_prepare(slots=4, slot_ctx=64, max_tokens=64, max_out=4)
+        out, stats = dm.serve([], 4, 32)
+        assert out.shape == (0, 4) and len(stats["lengths"]) == 0
+        with pytest.raises(BackendError):
+            dm.serve([[1] * 62], 4, 32)          # 62 + 4 - 1 > 64 positions
+        a = [5, 17, 400, 3, 99, 250, 7, 1]
+        out1, _ = dm.serve([a[:3] + [0] + a[4:]], 6, 32)
+        out2, _ = dm.serve([a[:3] + [10 ** 6] + a[4:]], 6, 32)
+        out3, _ = dm.serve([a[:3] + [-5] + a[4:]], 6, 32)
+        assert out1.tolist() == out2.tolist() == out3.tolist()
+    finally:
+        dm.close()
