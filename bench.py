@@ -84,19 +84,39 @@ def parse():
                    help="also time each kernel of the per-layer graph path alone")
     p.add_argument("--serve-requests", type=int, default=4096, help="config-3 requests (all GPUs); 0 skips")
     p.add_argument("--no-extra", action="store_true", help="skip the config 1 / config 2 lines (N = 1 only)")
-    p.add_argument("--profile-pass", choices=["c2", "c3step"],
+    p.add_argument("--profile-pass", choices=["c2", "c3step", "c4step"],
                    help="for ncu --profile-from-start off: warm up, then run one batch pass of config 2 "
-                        "(32 x 256 prefill) or one config-3-shaped step (256 decode tokens at position 100) "
-                        "between cuProfilerStart/Stop, and exit")
+                        "(32 x 256 prefill), one config-3-shaped step (256 decode tokens at position 100) or two "
+                        "config-4 decode steps (Q8_0, KV 4096) between cuProfilerStart/Stop, and exit")
     p.add_argument("--layers", type=int, default=32, help="model layers for --profile-pass")
     return p.parse_args()
 
 
 def profile_pass(args):
-    """One batch pass bracketed by cuProfilerStart / cuProfilerStop."""
+    """One batch pass (c2, c3step) or two config-4 decode steps (c4step)
+    bracketed by cuProfilerStart / cuProfilerStop."""
     import ctypes
     from hymt2_b200 import synth
     from hymt2_b200.device import Backend, DeviceModel
+    if args.profile_pass == "c4step":
+        be = Backend(0)
+        dm = DeviceModel(synth.ensure("c4_q8_0", args.model_dir, layers=args.layers), be, ctx=C4_PROMPT + 128)
+        lib, impl = be.lib, be.impl
+        ids = np.random.default_rng(1).integers(0, VOCAB, C4_PROMPT).astype(np.int32)
+        if lib.hyc_decode_begin(impl, ids.ctypes.data, C4_PROMPT, 0, 16, None, 0, dm.vocab_out) != 0 or \
+                lib.hyc_decode_steps(impl, 3) != 0:
+            raise RuntimeError(be.error())
+        be.sync()
+        cu = ctypes.CDLL("libcuda.so.1")
+        cu.cuProfilerStart()
+        if lib.hyc_decode_steps(impl, 2) != 0:
+            raise RuntimeError(be.error())
+        be.sync()
+        cu.cuProfilerStop()
+        dm.close()
+        be.close()
+        print("profiled two decode steps")
+        return
     cfg = "c2_q4km" if args.profile_pass == "c2" else "c0_stq"
     be = Backend(0)
     dm = DeviceModel(synth.ensure(cfg, args.model_dir, layers=args.layers), be, ctx=512)
