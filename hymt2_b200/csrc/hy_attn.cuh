@@ -108,93 +108,9 @@ __global__ void rope_norm_store(const __grid_constant__ AttnArgs a) {
     }
 }
 
-// Core loop shared by decode and prefill: keys [j0, j1) for the G heads of
-// KV head kvh, query rows in sq[G][HD].  Key `cur` (if >= 0) is taken from
-// sk/sv (values already bf16-rounded) instead of the cache.
-template <int HD, int G>
-__device__ __forceinline__ void attend_range(const AttnArgs &a, const uint16_t *kc, const uint16_t *vc, int kvh, int j0,
-                                             int j1, int cur, const float (*sq)[HD], const float *sk, const float *sv,
-                                             float (&m)[G], float (&l)[G], float (&o)[G][HD / 32]) {
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-    for (int h = 0; h < G; h++) {
-        m[h] = -INFINITY;
-        l[h] = 0.f;
-#pragma unroll
-        for (int i = 0; i < HD / 32; i++) o[h][i] = 0.f;
-    }
-    const uint16_t *Kb = kc + kvh * HD, *Vb = vc + kvh * HD;
-    for (int tile = j0 + w * 32; tile < j1; tile += G * 32) {
-        const int j = tile + lane;
-        const bool valid = j < j1;
-        float s[G];
-#pragma unroll
-        for (int h = 0; h < G; h++) s[h] = 0.f;
-        if (valid) {
-            if (j == cur) {
-#pragma unroll 4
-                for (int d = 0; d < HD; d++) {
-                    const float kv = sk[d];
-#pragma unroll
-                    for (int h = 0; h < G; h++) s[h] = fmaf(sq[h][d], kv, s[h]);
-                }
-            } else {
-                const uint16_t *kr = Kb + (size_t)j * a.kvdim;
-#pragma unroll 2
-                for (int d8 = 0; d8 < HD; d8 += 8) {
-                    const uint4 kk = *(const uint4 *)(kr + d8);
-                    const uint32_t kw[4] = {kk.x, kk.y, kk.z, kk.w};
-#pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const float k0 = bf16_bits_to_f32(kw[q] & 0xffffu), k1 = bf16_bits_to_f32(kw[q] >> 16);
-#pragma unroll
-                        for (int h = 0; h < G; h++) {
-                            s[h] = fmaf(sq[h][d8 + 2 * q], k0, s[h]);
-                            s[h] = fmaf(sq[h][d8 + 2 * q + 1], k1, s[h]);
-                        }
-                    }
-                }
-            }
-        }
-        float p[G];
-#pragma unroll
-        for (int h = 0; h < G; h++) {
-            const float sc = valid ? s[h] * a.scale : -INFINITY;
-            const float mt = warp_max(sc);
-            const float mn = fmaxf(m[h], mt);
-            const float corr = expf(m[h] - mn);
-            p[h] = valid ? expf(sc - mn) : 0.f;
-            l[h] = l[h] * corr + warp_sum(p[h]);
-            m[h] = mn;
-#pragma unroll
-            for (int i = 0; i < HD / 32; i++) o[h][i] *= corr;
-        }
-        const int nk = min(32, j1 - tile);
-        for (int jj = 0; jj < nk; jj++) {
-            const int jk = tile + jj;
-            float vv[HD / 32];
-            if (jk == cur) {
-#pragma unroll
-                for (int i = 0; i < HD / 32; i++) vv[i] = sv[lane + 32 * i];
-            } else {
-                const uint16_t *vr = Vb + (size_t)jk * a.kvdim;
-#pragma unroll
-                for (int i = 0; i < HD / 32; i++) vv[i] = bf16_bits_to_f32(vr[lane + 32 * i]);
-            }
-#pragma unroll
-            for (int h = 0; h < G; h++) {
-                const float pj = __shfl_sync(0xffffffffu, p[h], jj);
-#pragma unroll
-                for (int i = 0; i < HD / 32; i++) o[h][i] = fmaf(pj, vv[i], o[h][i]);
-            }
-        }
-    }
-}
-
 template <int HD, int G>
 struct AttnSmem {
     float sq[G][HD];
-    float sk[HD], sv[HD];
     float pm[G][G], pl[G][G];
     float po[G][G][HD];
     int last;
@@ -916,11 +832,12 @@ __host__ __device__ constexpr size_t prefill_stage_bytes() {
     return (size_t)G * 32 * HD * 2;
 }
 
-// attend_range over keys [0, j1) that are all in the cache, with every global
-// load of a tile in flight at once: the tile's V rows go to this warp's
-// shared buffer sv (cp.async) before the scores are computed, and each lane
-// loads its key's whole K row into registers.  The arithmetic, and its order,
-// is attend_range's, so the results are bit-identical to it.
+// Keys [0, j1) of KV head kvh (all in the cache) for the G query heads in
+// sq[G][HD]: warp w takes the 32-key tiles w*32 + k*G*32, one key per lane
+// (scores over d in order, a warp softmax per tile, then p.V over the tile's
+// keys in order).  Every global load of a tile is in flight at once: the V
+// rows go to this warp's shared buffer sv (cp.async) before the scores, and
+// each lane loads its key's whole K row into registers.
 template <int HD, int G>
 __device__ __forceinline__ void attend_range_staged(const AttnArgs &a, const uint16_t *kc, const uint16_t *vc, int kvh,
                                                     int j1, const float (*sq)[HD], uint16_t *sv, float (&m)[G],
