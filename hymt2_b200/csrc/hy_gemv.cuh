@@ -857,6 +857,52 @@ struct FpFmt<FMT_F32> { static constexpr int kElems = 4; };
 // [NT][K] permuted activations, then a [K] staging row and 64 floats of reduction space.
 __host__ __device__ inline size_t fp_smem_bytes(int NT, int K) { return align16((size_t)NT * K * 4) + (size_t)K * 4 + 64 * 4; }
 
+// One 16-byte weight unit u of a row at one token, folded into this lane's
+// accumulator: gemv_fp's per-unit arithmetic for token 0 (Q8_0: the two
+// 16-element halves of a 32-block are summed across the lane pair, then
+// scaled once).
+template <int FMT>
+__device__ __forceinline__ void fp_unit1(const uint4 &v, unsigned short s16, bool ok, const float *sx, int nunit, int u,
+                                         float &acc) {
+    constexpr int E = FpFmt<FMT>::kElems, QPU = E / 4;
+    const int lane = threadIdx.x & 31;
+    float wf[E];
+    float scale = 1.f;
+    if (ok) {
+        if (FMT == FMT_Q80) {
+            const int8_t *q = (const int8_t *)&v;
+#pragma unroll
+            for (int j = 0; j < E; j++) wf[j] = (float)q[j];
+            scale = h2f(s16);
+        } else if (FMT == FMT_F16) {
+            const __half *h = (const __half *)&v;
+#pragma unroll
+            for (int j = 0; j < E; j++) wf[j] = __half2float(h[j]);
+        } else {
+            const float *f = (const float *)&v;
+#pragma unroll
+            for (int j = 0; j < E; j++) wf[j] = f[j];
+        }
+    }
+    float p = 0.f;
+    if (ok) {
+#pragma unroll
+        for (int q = 0; q < QPU; q++) {
+            const float4 xv = *(const float4 *)&sx[((size_t)q * nunit + u) * 4];
+            p = fmaf(wf[4 * q + 0], xv.x, p);
+            p = fmaf(wf[4 * q + 1], xv.y, p);
+            p = fmaf(wf[4 * q + 2], xv.z, p);
+            p = fmaf(wf[4 * q + 3], xv.w, p);
+        }
+    }
+    if (FMT == FMT_Q80) {
+        p += __shfl_xor_sync(0xffffffffu, p, 1);
+        if ((lane & 1) == 0) acc += scale * p;
+    } else {
+        acc += p;
+    }
+}
+
 template <int FMT, int NT>
 __global__ void __launch_bounds__(kGemvThreads) gemv_fp(const __grid_constant__ GemvArgs a) {
     trace_mark(a.trace, 0);
@@ -882,12 +928,65 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_fp(const __grid_constant__ 
     }
     trace_mark(a.trace, 2);
     unsigned long long best = 0;
+    if constexpr (NT == 1) {
+        // one token: each warp streams two rows at once (rows r and r + nw), kFpInFlight / 2
+        // units of each per lane loaded before the arithmetic, so a K = 2048 row (4 units per
+        // lane) still keeps 8 loads in flight; per row the arithmetic is the loop's below
+        constexpr int PF2 = kFpInFlight / 2;
+        for (int r = gw; r < a.rows_total; r += 2 * nw) {
+            const int rb = r + nw;
+            const bool two = rb < a.rows_total;  // uniform across the warp
+            int wa, la, wb = 0, lb = 0;
+            map_row(a, r, wa, la);
+            if (two) map_row(a, rb, wb, lb);
+            const WDesc &WA = wsel(a, wa);
+            const WDesc &WB = wsel(a, two ? wb : wa);
+            const uint8_t *rowa = WA.w + (size_t)la * WA.stride;
+            const uint8_t *rowb = two ? WB.w + (size_t)lb * WB.stride : rowa;
+            float acca = 0.f, accb = 0.f;
+            for (int c0 = 0; c0 < nunit; c0 += 32 * PF2) {
+                uint4 va[PF2], vb[PF2];
+                unsigned short sa[PF2], sb[PF2];
+#pragma unroll
+                for (int i = 0; i < PF2; i++) {
+                    const int u = c0 + 32 * i + lane;
+                    sa[i] = sb[i] = 0;
+                    if (u < nunit) {
+                        va[i] = ldg_stream(rowa + (size_t)u * 16);
+                        if (two) vb[i] = ldg_stream(rowb + (size_t)u * 16);
+                        if (FMT == FMT_Q80) {
+                            sa[i] = __ldg((const unsigned short *)(rowa + K) + (u >> 1));
+                            if (two) sb[i] = __ldg((const unsigned short *)(rowb + K) + (u >> 1));
+                        }
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < PF2; i++) {
+                    const int u0 = c0 + 32 * i;
+                    if (u0 >= nunit) break;  // uniform across the warp
+                    const int u = u0 + lane;
+                    const bool ok = u < nunit;
+                    fp_unit1<FMT>(va[i], sa[i], ok, sx, nunit, u, acca);
+                    if (two) fp_unit1<FMT>(vb[i], sb[i], ok, sx, nunit, u, accb);
+                }
+            }
+            float res[1] = {warp_sum(acca)};
+            row_epilogue<1>(a, WA, la, r, res, best);
+            if (two) {
+                res[0] = warp_sum(accb);
+                row_epilogue<1>(a, WB, lb, rb, res, best);
+            }
+        }
+        argmax_commit(a, best, red);
+        return;
+    }
     for (int r = gw; r < a.rows_total; r += nw) {
         int wi, lr;
         map_row(a, r, wi, lr);
         const WDesc &w = wsel(a, wi);
         const uint8_t *row = w.w + (size_t)lr * w.stride;
         float acc[NT];
+
 #pragma unroll
         for (int t = 0; t < NT; t++) acc[t] = 0.f;
         // kFpInFlight 16-byte units of the row per lane are loaded before any
