@@ -49,26 +49,31 @@ def _run(cmd: list[str], cwd: str | None = None) -> None:
         raise RuntimeError("build step failed: %s\n%s\n%s" % (" ".join(cmd), r.stdout[-4000:], r.stderr[-4000:]))
 
 
-def build_backend(force: bool = False) -> None:
+def build_backend(force: bool = False, trace: bool = False) -> None:
+    """The product backend (.so and .a); with trace=True instead the
+    measurement variant libhymt2_cuda_trace.so (-DHYK_TRACE: per-kernel and
+    persistent-kernel %globaltimer timelines)."""
     deps = [os.path.join(CSRC, f) for f in SOURCES + HEADERS]
     deps += [os.path.join(_paths.ROOT, "include", h) for h in ("hy_device_abi.h", "hymt2_cuda.h")]
     deps.append(os.path.abspath(__file__))
-    so, ar = _paths.BACKEND_LIB, _paths.BACKEND_ARCHIVE
-    if not force and not _stale(so, deps) and not _stale(ar, deps):
+    so, ar = (_paths.TRACE_LIB, None) if trace else (_paths.BACKEND_LIB, _paths.BACKEND_ARCHIVE)
+    if not force and not _stale(so, deps) and (ar is None or not _stale(ar, deps)):
         return
-    objdir = os.path.join(_paths.PKG, "_build")
+    objdir = os.path.join(_paths.PKG, "_build", "trace" if trace else "product")
     os.makedirs(objdir, exist_ok=True)
     objs = []
     for src in SOURCES:
         obj = os.path.join(objdir, src.replace(".cu", ".o"))
-        _run([_nvcc(), *ARCH, *NVCC_FLAGS, "-c", os.path.join(CSRC, src), "-o", obj])
+        _run([_nvcc(), *ARCH, *NVCC_FLAGS, *(["-DHYK_TRACE"] if trace else []), "-c", os.path.join(CSRC, src),
+              "-o", obj])
         objs.append(obj)
     tmp = so + ".tmp"
     _run([_nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", tmp, *objs, "-lrt", "-ldl", "-lpthread"])
     os.replace(tmp, so)
-    if os.path.exists(ar):
-        os.remove(ar)
-    _run(["ar", "rcs", ar, *objs])
+    if ar:
+        if os.path.exists(ar):
+            os.remove(ar)
+        _run(["ar", "rcs", ar, *objs])
 
 
 def build_synth(force: bool = False) -> None:
@@ -100,5 +105,9 @@ def build_all(force: bool = False) -> None:
 
 
 if __name__ == "__main__":
+    if "--trace" in sys.argv:
+        build_backend(force="--force" in sys.argv, trace=True)
+        print("built:", _paths.TRACE_LIB)
+        sys.exit(0)
     build_all(force="--force" in sys.argv)
     print("built:", _paths.BACKEND_LIB, _paths.BACKEND_ARCHIVE, _paths.SYNTH_LIB)

@@ -230,10 +230,25 @@ void set_smem(K kern, size_t bytes = kMaxDynSmem) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
-void init_kernel_attrs() {
-    static bool done = false;
-    if (done) return;
-    done = true;
+void init_kernel_attrs_current();
+
+// Dynamic shared-memory limits are a per-device property of each kernel:
+// raise them once for every device this process uses, with that device
+// current (hyc_create, and the first allocation-free call on a device).
+constexpr int kMaxDevices = 128;
+std::mutex g_attr_mu;
+bool g_attr_done[kMaxDevices] = {false};
+
+bool init_kernel_attrs(int dev) {
+    if (dev < 0 || dev >= kMaxDevices) return false;
+    std::lock_guard<std::mutex> lock(g_attr_mu);
+    if (g_attr_done[dev]) return true;
+    init_kernel_attrs_current();
+    g_attr_done[dev] = cudaGetLastError() == cudaSuccess;
+    return g_attr_done[dev];
+}
+
+void init_kernel_attrs_current() {
     set_smem(gemv_panel_nt1<1>);
     set_smem(gemv_panel_nt1<2>);
     set_smem(gemv_panel_nt1<3>);
@@ -293,6 +308,11 @@ void init_kernel_attrs() {
     set_smem(tc_gemm<2, 128>, tc_smem_bytes(2, 128));
     set_smem(tc_gemm<2, 64>, tc_smem_bytes(2, 64));
     set_smem(tc_gemm<3, 64>, tc_smem_bytes(3, 64));
+    set_smem(tc_gemm<1, 256, true>, tc_smem_bytes(1, 256));
+    set_smem(tc_gemm<1, 64, true>, tc_smem_bytes(1, 64));
+    set_smem(tc_gemm<2, 128, true>, tc_smem_bytes(2, 128));
+    set_smem(tc_gemm<2, 64, true>, tc_smem_bytes(2, 64));
+    set_smem(tc_gemm<3, 64, true>, tc_smem_bytes(3, 64));
 }
 
 // One launch for nt <= NT tokens.
@@ -470,6 +490,29 @@ bool tc_scratch(HyCtx *c, int K) {
     return true;
 }
 
+// One tensor-core GEMM launch over the weights in `ta` (all P planes).  MMA
+// rows: the whole weight tile, or 64-row slices of it when the whole tiles
+// would leave SMs idle (read from the slice-first copy, built on first use).
+// INTS: the test instantiation that also stores the per-block integers.
+template <bool INTS = false>
+bool tc_gemm_launch(HyCtx *c, TcArgs &ta, int P, HyWeight *const *ws, int cnt, bool pdl) {
+    const int NM = tc_tiles_all(P, tc_n(P), ta) >= c->nsm ? tc_n(P) : 64;
+    const int ntiles = tc_tiles_all(P, NM, ta);
+    if (NM < tc_n(P))
+        for (int j = 0; j < cnt; j++)
+            if (tc_planes(ws[j]->fmt) == P) {
+                if (!tc_slices(c, ws[j])) return false;
+                for (int q = 0; q < ta.nw; q++)
+                    if (ta.w[q] == ws[j]->tc_w) ta.w64[q] = ws[j]->tc_w64;
+            }
+    const dim3 grid(ntiles < c->nsm ? ntiles : c->nsm), blk(kTcThreads);
+    if (P == 1 && NM == 256) return launch(c, tc_gemm<1, 256, INTS>, grid, blk, tc_smem_bytes(1, 256), pdl, ta);
+    if (P == 1) return launch(c, tc_gemm<1, 64, INTS>, grid, blk, tc_smem_bytes(1, 64), pdl, ta);
+    if (P == 2 && NM == 128) return launch(c, tc_gemm<2, 128, INTS>, grid, blk, tc_smem_bytes(2, 128), pdl, ta);
+    if (P == 2) return launch(c, tc_gemm<2, 64, INTS>, grid, blk, tc_smem_bytes(2, 64), pdl, ta);
+    return launch(c, tc_gemm<3, 64, INTS>, grid, blk, tc_smem_bytes(3, 64), pdl, ta);
+}
+
 // nt tokens through up to three weights sharing one activation
 // prologue (pro.act / x / x2 / norm_w / eps, pro.k = K): one quantise launch
 // writing tiled Q8_K codes, then one tensor-core GEMM per weight format; outs[i] is
@@ -518,25 +561,7 @@ bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float
             ta.nw++;
             done[j] = true;
         }
-        // MMA rows: the whole weight tile, or 64-row slices of it when the
-        // whole tiles would leave SMs idle
-        const int NM = tc_tiles_all(P, tc_n(P), ta) >= c->nsm ? tc_n(P) : 64;
-        const int ntiles = tc_tiles_all(P, NM, ta);
-        if (NM < tc_n(P))
-            for (int j = 0; j < cnt; j++)
-                if (tc_planes(ws[j]->fmt) == P) {
-                    if (!tc_slices(c, ws[j])) return false;
-                    for (int q = 0; q < ta.nw; q++)
-                        if (ta.w[q] == ws[j]->tc_w) ta.w64[q] = ws[j]->tc_w64;
-                }
-        const dim3 grid(ntiles < c->nsm ? ntiles : c->nsm), blk(kTcThreads);
-        bool ok;
-        if (P == 1 && NM == 256) ok = launch(c, tc_gemm<1, 256>, grid, blk, tc_smem_bytes(1, 256), pdl, ta);
-        else if (P == 1) ok = launch(c, tc_gemm<1, 64>, grid, blk, tc_smem_bytes(1, 64), pdl, ta);
-        else if (P == 2 && NM == 128) ok = launch(c, tc_gemm<2, 128>, grid, blk, tc_smem_bytes(2, 128), pdl, ta);
-        else if (P == 2) ok = launch(c, tc_gemm<2, 64>, grid, blk, tc_smem_bytes(2, 64), pdl, ta);
-        else ok = launch(c, tc_gemm<3, 64>, grid, blk, tc_smem_bytes(3, 64), pdl, ta);
-        if (!ok) return false;
+        if (!tc_gemm_launch(c, ta, P, ws, cnt, pdl)) return false;
     }
     return true;
 }
@@ -1513,7 +1538,11 @@ HYC_API void *hyc_create(int device, char *info, size_t cap) {
     c->dev = device;
     c->nsm = p.multiProcessorCount;
     c->l2_bytes = (size_t)p.l2CacheSize;
-    init_kernel_attrs();
+    if (!init_kernel_attrs(device)) {
+        if (info && cap) snprintf(info, cap, "setting kernel shared-memory limits on device %d failed", device);
+        delete c;
+        return nullptr;
+    }
     set_smem(quantize_export);
     if (cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking) != cudaSuccess ||
         cudaHostAlloc((void **)&c->h_pinned_int, 4096, cudaHostAllocDefault) != cudaSuccess) {
@@ -1614,6 +1643,51 @@ HYC_API int hyc_tc_test(void *impl, hy_dweight *hw, int act, const float *x, con
     cudaFree(dn);
     cudaFree(dout);
     return ok ? 0 : -1;
+}
+
+HYC_API int hyc_tc_block_ints(void *impl, hy_dweight *hw, const q8k_block *xq, int nt, int32_t *out) {
+    HyCtx *c = (HyCtx *)impl;
+    HyWeight *w = (HyWeight *)hw;
+    if (!c || c->broken || !w || !xq || !out || !tc_planes(w->fmt) || w->k % 256 || nt < 1 || nt > 65536) return -1;
+    if (cudaSetDevice(c->dev) != cudaSuccess) return -1;
+    const int P = tc_planes(w->fmt), nb = w->nb, per = P == 3 ? 2 * nb : nb, tpad = (nt + kTcM - 1) / kTcM * kTcM;
+    if (nt > c->max_tokens) c->max_tokens = nt;  // the tiled activation scratch grows to nt tokens
+    if (!tc_scratch(c, w->k) || !tc_weight(c, w)) return -1;
+    q8k_block *dxq = nullptr;
+    int32_t *dints = nullptr;
+    float *dout = nullptr;
+    const size_t xb = (size_t)nt * nb * sizeof(q8k_block), ib = (size_t)nt * w->n * per * 4;
+    bool ok = cudaMalloc(&dxq, xb) == cudaSuccess && cudaMalloc(&dints, ib) == cudaSuccess &&
+              cudaMalloc(&dout, (size_t)nt * w->n * 4) == cudaSuccess && h2d(c, dxq, xq, xb) == cudaSuccess;
+    if (ok) {
+        const long long units = (long long)tpad * nb * 16;
+        tc_from_q8k<<<(unsigned)((units + 255) / 256), 256, 0, c->st>>>(dxq, nt, tpad, nb, c->d_tca, c->d_tcad);
+        ok = cudaGetLastError() == cudaSuccess;
+    }
+    if (ok) {
+        TcArgs ta;
+        memset(&ta, 0, sizeof ta);
+        ta.a = c->d_tca;
+        ta.ad = c->d_tcad;
+        ta.T = nt;
+        ta.nb = nb;
+        ta.err = c->d_tcerr;
+        ta.nw = 1;
+        ta.w[0] = w->tc_w;
+        ta.ws[0] = w->tc_ws;
+        ta.out[0] = dout;
+        ta.ldo[0] = w->n;
+        ta.N[0] = w->n;
+        ta.ints = dints;
+        HyWeight *ws[1] = {w};
+        ok = tc_gemm_launch<true>(c, ta, P, ws, 1, false) &&
+             cudaMemcpyAsync(out, dints, ib, cudaMemcpyDeviceToHost, c->st) == cudaSuccess &&
+             cudaStreamSynchronize(c->st) == cudaSuccess && tc_status(c);
+    }
+    cudaFree(dxq);
+    cudaFree(dints);
+    cudaFree(dout);
+    return ok ? per : -1;
 }
 
 HYC_API int hyc_batch_prepare(void *impl, int slots, int slot_ctx, int max_tokens, int max_out) {
@@ -2184,6 +2258,7 @@ HYC_API int hyc_debug_buffer(void *impl, int which, float *out, size_t count) {
 // Debug timeline: on != 0 rebuilds the graphs with one slot per kernel launch
 // (launch / past-wait / past-prologue / end in %globaltimer ns).
 HYC_API int hyc_trace(void *impl, int on) {
+#ifdef HYK_TRACE
     HyCtx *c = (HyCtx *)impl;
     if (!c) return -1;
     c->trace_on = on != 0;
@@ -2206,10 +2281,16 @@ HYC_API int hyc_trace(void *impl, int on) {
                    cudaStreamSynchronize(c->st) == cudaSuccess
                ? 0
                : -1;
+#else
+    (void)impl;
+    (void)on;
+    return -1;  // this library was built without the timeline (HYK_TRACE)
+#endif
 }
 
 // Copy the timeline (slots * 4 values) and return the number of slots in use.
 HYC_API int hyc_trace_read(void *impl, unsigned long long *out, int max_slots) {
+#ifdef HYK_TRACE
     HyCtx *c = (HyCtx *)impl;
     if (!c || !out) return -1;
     const int n = c->trace_next < max_slots ? c->trace_next : max_slots;
@@ -2222,11 +2303,18 @@ HYC_API int hyc_trace_read(void *impl, unsigned long long *out, int max_slots) {
             cudaSuccess)
         return -1;
     return n;
+#else
+    (void)impl;
+    (void)out;
+    (void)max_slots;
+    return -1;  // this library was built without the timeline (HYK_TRACE)
+#endif
 }
 
 // Persistent-kernel timeline of the last traced launch: %globaltimer at every
 // phase edge of block 0 (step start, then before/after each grid barrier).
 HYC_API int hyc_mega_timeline(void *impl, unsigned long long *out, int cap) {
+#ifdef HYK_TRACE
     HyCtx *c = (HyCtx *)impl;
     if (!c || !out || !c->d_tl) return -1;
     const int n = cap < c->tl_cap ? cap : c->tl_cap;
@@ -2234,6 +2322,12 @@ HYC_API int hyc_mega_timeline(void *impl, unsigned long long *out, int cap) {
         cudaMemcpy(out, c->d_tl, (size_t)n * 8, cudaMemcpyDeviceToHost) != cudaSuccess)
         return -1;
     return n;
+#else
+    (void)impl;
+    (void)out;
+    (void)cap;
+    return -1;  // this library was built without the timeline (HYK_TRACE)
+#endif
 }
 
 // ---------------------------------------------------------------- allocation-free decode attention
@@ -2323,7 +2417,8 @@ HYC_API int hyc_attention_decode_noalloc(void *stream, int heads, int kv_heads, 
                 cudaGetLastError();
                 return noalloc_fail(err, err_cap, -3, "cudaGetSymbolAddress failed for the scratch array");
             }
-            init_kernel_attrs();
+            if (!init_kernel_attrs(dev))
+                return noalloc_fail(err, err_cap, -3, "setting kernel shared-memory limits failed");
             sc.part = (float *)p;
             sc.tickets = (int *)t;
             sc.ready = true;

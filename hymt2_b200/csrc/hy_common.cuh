@@ -86,19 +86,22 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p) {
     return r;
 }
 
-// Optional per-kernel timeline (debug): slot s holds [launch of CTA 0,
-// CTA 0 past griddepcontrol.wait, CTA 0 past its prologue, last CTA end] in
-// %globaltimer nanoseconds.  Slot < 0 disables recording.
-constexpr int kTraceSlots = 1024;
-__device__ unsigned long long g_trace[kTraceSlots][4];
-__device__ unsigned long long g_trace2[kTraceSlots][4];  // sub-phases of CTA 0
-__device__ unsigned long long g_trace3[kTraceSlots][4];  // CTA 0: clock64 and globaltimer at wait / end
-
 __device__ __forceinline__ unsigned long long gtimer() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
     return t;
 }
+
+// Optional per-kernel timeline, compiled in only with -DHYK_TRACE (the
+// measurement build; the product library has none of it): slot s holds
+// [launch of CTA 0, CTA 0 past griddepcontrol.wait, CTA 0 past its prologue,
+// last CTA end] in %globaltimer nanoseconds.  Slot < 0 disables recording.
+constexpr int kTraceSlots = 1024;
+#ifdef HYK_TRACE
+__device__ unsigned long long g_trace[kTraceSlots][4];
+__device__ unsigned long long g_trace2[kTraceSlots][4];  // sub-phases of CTA 0
+__device__ unsigned long long g_trace3[kTraceSlots][4];  // CTA 0: clock64 and globaltimer at wait / end
+
 __device__ __forceinline__ void trace_mark(int slot, int which) {
     if (slot >= 0 && slot < kTraceSlots && threadIdx.x == 0) {
         const unsigned long long t = gtimer();
@@ -115,6 +118,10 @@ __device__ __forceinline__ void trace_sub(int slot, int which) {
     if (slot >= 0 && slot < kTraceSlots && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0)
         g_trace2[slot][which] = gtimer();
 }
+#else
+__device__ __forceinline__ void trace_mark(int, int) {}
+__device__ __forceinline__ void trace_sub(int, int) {}
+#endif
 
 // Monotone 64-bit argmax key: larger value wins, equal values -> smaller index
 // wins (the host loop keeps the first maximum with a strict '>').  NaN never

@@ -186,9 +186,10 @@ __device__ __forceinline__ bool mega_slot_ready(const MegaArgs &a, uint64_t *bar
     return ready;
 }
 
-// Timeline (debug, a.tl non-null): [0, cap/2) phase edges of block 0;
-// [cap/2, cap/2 + 8192) sub-phase marks of block 0; then per-CTA marks of
-// one chosen (step, layer): 16 slots per CTA.
+// Timeline (measurement builds with -DHYK_TRACE and a.tl non-null): [0,
+// cap/2) phase edges of block 0; [cap/2, cap/2 + 8192) sub-phase marks of
+// block 0; then per-CTA marks of one chosen (step, layer): 16 slots per CTA.
+#ifdef HYK_TRACE
 __device__ __forceinline__ void tl_mark(const MegaArgs &a, int &idx) {
     if (a.tl && blockIdx.x == 0 && threadIdx.x == 0 && idx < a.tl_cap / 2) a.tl[idx] = gtimer();
     idx++;
@@ -200,6 +201,11 @@ __device__ __forceinline__ void tl_sub(const MegaArgs &a, int &idx) {
 __device__ __forceinline__ void tl_cta(const MegaArgs &a, bool on, int slot) {
     if (a.tl && on && threadIdx.x == 0) a.tl[a.tl_cap / 2 + 8192 + blockIdx.x * 16 + slot] = gtimer();
 }
+#else
+__device__ __forceinline__ void tl_mark(const MegaArgs &, int &) {}
+__device__ __forceinline__ void tl_sub(const MegaArgs &, int &) {}
+__device__ __forceinline__ void tl_cta(const MegaArgs &, bool, int) {}
+#endif
 
 // ---------------------------------------------------------------- weight slots
 
@@ -833,12 +839,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 hav[l] = uok ? *(const int4 *)&st.qp[(size_t)l * (a.H / 4) + lane * 16] : make_int4(0, 0, 0, 0);
             const float hd = uok ? st.d[lane >> 2] : 0.f;
             unsigned long long best = 0;
-            unsigned long long tw = 0, tc = 0, ts = 0, t0 = a.tl ? gtimer() : 0;
             for (int si = 0; si < hst && ok; si++) {
                 const int k = si % a.head_ns;
                 const bool ready = __syncthreads_and(mbar_wait(&hbar[k], hph[k]));
-                unsigned long long t1 = a.tl ? gtimer() : 0;
-                tw += t1 - t0;
                 if (ready) {
                     hph[k] ^= 1;
                     hpend &= ~(1u << k);
@@ -855,16 +858,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                         if (key > best) best = key;
                     }
                 }
-                if (a.tl) {
-                    t0 = gtimer();
-                    tc += t0 - t1;
-                }
                 __syncthreads();  // stage k consumed
-                if (a.tl) {
-                    t1 = gtimer();
-                    ts += t1 - t0;
-                    t0 = t1;
-                }
                 if (si + a.head_ns < hst) {
                     if (tid == 0) {
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -872,12 +866,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                     }
                     hpend |= 1u << k;
                 }
-            }
-            if (a.tl && blockIdx.x == 0 && tid == 0 && step < 8) {
-                a.tl[a.tl_cap / 2 + 6000 + step * 4 + 0] = tw;
-                a.tl[a.tl_cap / 2 + 6000 + step * 4 + 1] = tc;
-                a.tl[a.tl_cap / 2 + 6000 + step * 4 + 2] = ts;
-                a.tl[a.tl_cap / 2 + 6000 + step * 4 + 3] = hst;
             }
             if (lane == 0) s_best[warp] = best;
             __syncthreads();

@@ -110,6 +110,7 @@ struct TcArgs {
     int T, nb;
     int epi;           // 0: out = y, 1: out += y
     int *err;          // set on a bounded-wait timeout
+    int32_t *ints;     // tc_gemm<P, NM, true> only: per-block integers [T][N][nb] (Q4_K: [T][N][nb][2])
 };
 
 // Number of (m, n) tiles of a GEMM whose MMAs cover NM weight rows.
@@ -225,8 +226,11 @@ __device__ __forceinline__ float tc_magic(uint32_t v) { return __int_as_float((i
 constexpr float kTcMagic = 12582912.0f;  // 1.5 * 2^23
 
 // P planes; MMAs of NM weight rows, a slice of the N = tc_n(P) rows of
-// each weight tile (NM < N gives small token counts more CTAs).
-template <int P, int NM>
+// each weight tile (NM < N gives small token counts more CTAs).  INTS (test
+// instantiations only) also stores every block's integers as the epilogue
+// reads them from TMEM: the panel S = A.W, Q6_K acc = 64 S_hi + S_lo, Q4_K
+// sumi = 64 S_hi + S_lo and summ = S_m.
+template <int P, int NM, bool INTS = false>
 __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__ TcArgs a) {
     constexpr int N = tc_n(P), SUB = N / NM, C = NM / 4, AH = kTcABytes / 2, SB = tc_sbytes(P);
     constexpr int STB = tc_stage_bytes(P, NM), SLB = tc_slot_bytes(NM);
@@ -384,6 +388,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
 #pragma unroll
                     for (int p = 0; p < P; p++) tc_ld<CW>(tbase + (uint32_t)(p * NM + c * CW), r[p]);
                     tc_wait_ld();
+                    if constexpr (INTS) {
+                        const int nmax = a.N[wi];
+                        for (int j = 0; j < CW; j++) {
+                            const int n = ns * NM + part * C + c * CW + j;
+                            if (t >= a.T || n >= nmax) continue;
+                            const size_t o = (size_t)t * nmax + n;
+                            if constexpr (P == 1) {
+                                a.ints[o * nb + kb] = (int)r[0][j];
+                            } else if constexpr (P == 2) {
+                                a.ints[o * nb + kb] = (int)(r[0][j] << 6) + (int)r[1][j];
+                            } else {
+                                a.ints[(o * nb + kb) * 2] = (int)(r[0][j] << 6) + (int)r[1][j];
+                                a.ints[(o * nb + kb) * 2 + 1] = (int)r[2][j];
+                            }
+                        }
+                    }
 #pragma unroll
                     for (int j4 = 0; j4 < CW / 4; j4++) {
                         const float4 w1 = ws1[c * CW / 4 + j4];
@@ -585,6 +605,22 @@ __device__ __forceinline__ void tc_quant_store(const float (&v)[8], int8_t *ta, 
     const uint32_t hi = (q[4] & 0xff) | ((q[5] & 0xff) << 8) | ((q[6] & 0xff) << 16) | ((uint32_t)(q[7] & 0xff) << 24);
     *(uint2 *)(ta + ((size_t)mt * nb + b) * kTcABytes + tc_tile_off(r, lane * 8, kTcM)) = make_uint2(lo, hi);
     if (lane == 0) ad[((size_t)mt * nb + b) * kTcM + r] = d;
+}
+
+// Host-made Q8_K blocks [T][nb] (natural-order codes qs, scale d) written as
+// the tiled activation operand, with no prologue: the test hook that reads
+// the GEMM's block integers feeds it exactly the codes the oracle uses.  One
+// thread per (padded token, block, 16-byte chunk); tokens T .. tpad - 1 get
+// zero codes.
+__global__ void tc_from_q8k(const q8k_block *xq, int T, int tpad, int nb, int8_t *ta, float *ad) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)tpad * nb * 16) return;
+    const int k16 = (int)(i % 16), b = (int)((i / 16) % nb), t = (int)(i / (16LL * nb));
+    const int mt = t / kTcM, r = t % kTcM;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (t < T) v = *(const uint4 *)&xq[(size_t)t * nb + b].qs[k16 * 16];
+    *(uint4 *)(ta + ((size_t)mt * nb + b) * kTcABytes + tc_tile_off(r, k16 * 16, kTcM)) = v;
+    if (k16 == 0) ad[((size_t)mt * nb + b) * kTcM + r] = t < T ? xq[(size_t)t * nb + b].d : 0.f;
 }
 
 // Activation rows -> Q8_K, written as tiled int8 codes plus block scales

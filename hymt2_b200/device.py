@@ -24,11 +24,14 @@ _lib = None
 
 
 def load_library() -> C.CDLL:
+    """The backend library; HYMT2_TRACE=1 selects the measurement build with
+    the %globaltimer timelines (python -m hymt2_b200.build --trace)."""
     global _lib
     if _lib is None:
-        if not os.path.exists(_paths.BACKEND_LIB):
-            raise RuntimeError(f"{_paths.BACKEND_LIB} not built: run __graft_entry__.build()")
-        _lib = abi.bind(C.CDLL(_paths.BACKEND_LIB))
+        path = _paths.TRACE_LIB if os.environ.get("HYMT2_TRACE") == "1" else _paths.BACKEND_LIB
+        if not os.path.exists(path):
+            raise RuntimeError(f"{path} not built: run __graft_entry__.build()")
+        _lib = abi.bind(C.CDLL(path))
     return _lib
 
 
@@ -111,6 +114,14 @@ class Backend:
         r = self.lib.hyc_block_ints(self.impl, h, xq.ctypes.data, nt, out.ctypes.data)
         if r != per:
             raise BackendError(f"block_ints returned {r}: " + self.error())
+        return out
+
+    def tc_block_ints(self, h: int, xq: np.ndarray, nt: int, rows: int, per: int) -> np.ndarray:
+        """Per-block integers of the tensor-core GEMM (hyc_tc_block_ints)."""
+        out = np.zeros((nt, rows, per), dtype=np.int32)
+        r = self.lib.hyc_tc_block_ints(self.impl, h, xq.ctypes.data, nt, out.ctypes.data)
+        if r != per:
+            raise BackendError(f"tc_block_ints returned {r}: " + self.error())
         return out
 
     def matmul_f32(self, h: int, x: np.ndarray, rows: int) -> np.ndarray:

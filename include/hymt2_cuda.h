@@ -172,6 +172,13 @@ HYC_API int hyc_quantize_q8k(void *impl, const float *x, int k, int nt, q8k_bloc
 /* Exact per-block int32 accumulators of the GEMV for host blocks xq[nt][k/256]:
  * out[t][row][b] (Q4_K: pairs sumi, summ).  Returns ints per (t, row). */
 HYC_API int hyc_block_ints(void *impl, hy_dweight *w, const q8k_block *xq, int nt, int32_t *out);
+/* The same per-block integers from the tcgen05 GEMM that chunks of >= 32
+ * tokens use (STQ1_0 / Q2_0C panels, Q4_K, Q6_K), read from TMEM for host
+ * blocks xq[nt][k/256] (no activation prologue), nt up to 65536, with the
+ * launch shape (whole or 64-row-slice tiles) the product path picks for nt:
+ * out[t][row][b] (Q4_K: pairs sumi, summ; reference src/kernels.c:565-581,
+ * 808-835, 861-877).  Returns ints per (t, row). */
+HYC_API int hyc_tc_block_ints(void *impl, hy_dweight *w, const q8k_block *xq, int nt, int32_t *out);
 /* One row of a device weight as fp32. */
 HYC_API int hyc_dequant_row(void *impl, hy_dweight *w, int row, float *dst);
 /* fp32-activation GEMV (Q8_0 / F16 / F32 weights): out[t*n + r]. */
@@ -241,6 +248,9 @@ HYC_API int hyc_bench_op(void *impl, int op, int iters);
  * kv_heads <= 64 — larger shapes return -2.  Returns 0, -1 (bad argument),
  * -2 (beyond the scratch maximum) or -3 (CUDA error); `err` (optional)
  * receives a message.  Work is enqueued on `stream` (a cudaStream_t).
+ * *d_pos is read on the device only, so keeping 0 <= *d_pos < ctx is the
+ * caller's job: for a position outside that range the kernel writes nothing
+ * (d_ao and both caches keep their contents) and the call still returns 0.
  * The first call on a device looks up the scratch address (once per device,
  * with that device current); make that first call before any stream
  * capture.  All calls share the one scratch array and it keeps the last

@@ -124,3 +124,36 @@ def test_tc_gemm_tile_widths(backend, oracle, name, k, rows, nt):
         assert flipped < 0.05 and rel.max() < 5e-3, (rel.max(), flipped)
     finally:
         backend.release(h)
+
+
+@pytest.mark.parametrize("name", list(TYPES))
+@pytest.mark.parametrize("k,rows,nt", [(2048, 300, 32), (2048, 300, 128), (512, 300, 200), (2048, 300, 256),
+                                       (6144, 64, 37), (512, 128, 8192), (512, 640, 8192)])
+def test_tc_block_ints_exact(backend, oracle, name, k, rows, nt):
+    """The tcgen05 GEMM's per-block int32 accumulators (read back from TMEM
+    by its epilogue) equal the reference's block integers bit for bit: the
+    panel `(enc << shift) - off * sum` (src/kernels.c:565-581), Q6_K `acc`
+    (:808-835), Q4_K `sumi` and `summ` (:861-877), for host-made Q8_K blocks
+    (no device prologue).  The shapes reach both launch forms the product
+    picks: 64-row slices of the weight tiles (few tiles) and whole tiles
+    (8192 tokens x 640 rows)."""
+    from hymt2_b200.device import weight_from_bytes
+    gt = TYPES[name]
+    rng = np.random.default_rng(k + rows + nt + gt)
+    raw = rand_blocks(rng, gt, rows, k)
+    if name.endswith("_ext"):
+        raw = _extreme(raw, gt, rng)
+    h = backend.upload(weight_from_bytes(gt, raw, rows, k))
+    try:
+        x = rand_act(rng, nt, k) * 3.0
+        x[0, :256] = 0.0                                   # an all-zero block
+        if nt > 2:
+            x[1, :256] = 1.0                               # ties for the first maximum
+            x[2, 256:512] = np.linspace(-5.0, 5.0, 256)    # exact halves on the grid
+        xq = oracle.quantize(x)
+        w = oracle.weight(gt, raw, rows, k, panel=True)
+        want = oracle.block_ints(w, xq, nt)
+        got = backend.tc_block_ints(h, xq, nt, rows, want.shape[2])
+        assert np.array_equal(got, want), f"{(got != want).sum()} of {got.size} block integers differ"
+    finally:
+        backend.release(h)

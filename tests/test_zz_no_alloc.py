@@ -17,13 +17,14 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-HEADS, KVH, HD, CTX = 16, 4, 128, 1024
+# the scratch holds kv_heads * ceil(ctx / 128) * group * (hdim + 2) floats
+SCRATCH_FLOATS, SPLIT = 131072, 128
 
 
-def _rope(lib):
-    cos = np.zeros(CTX * (HD // 2), dtype=np.float32)
+def _rope(lib, hd, ctx):
+    cos = np.zeros(ctx * (hd // 2), dtype=np.float32)
     sin = np.zeros_like(cos)
-    assert lib.hyc_rope_tables(10000.0, 1000.0, HD, HD, CTX, cos.ctypes.data, sin.ctypes.data) == 0
+    assert lib.hyc_rope_tables(10000.0, 1000.0, hd, hd, ctx, cos.ctypes.data, sin.ctypes.data) == 0
     return cos, sin
 
 
@@ -31,23 +32,39 @@ def _bf16(x):
     return (np.asarray(x, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16)
 
 
-def test_noalloc_attention_matches_allocating_entry_point():
+def _geometry(hd, group):
+    """The fewest KV heads (a power of two, at least 2) whose largest context
+    the fixed scratch accepts is at most 64 splits, and that context."""
+    kvh = 2
+    while SCRATCH_FLOATS // (kvh * group * (hd + 2)) > 64:
+        kvh *= 2
+    return kvh, SCRATCH_FLOATS // (kvh * group * (hd + 2)) * SPLIT
+
+
+@pytest.mark.parametrize("hd", [64, 128])
+@pytest.mark.parametrize("group", [1, 2, 4, 8])
+def test_noalloc_attention_matches_allocating_entry_point(hd, group):
+    """Every (hdim, group) the entry point dispatches, at a position inside
+    the first 128 keys (one split: the output is written without the
+    scratch), mid-context, and at the last position of the largest context
+    the scratch limit allows; each as two calls in a row (pos, pos + 1) so
+    the second call starts from the scratch contents the first one left."""
     import torch
 
     from hymt2_b200.device import Backend
 
+    kvh, ctx = _geometry(hd, group)
+    heads = kvh * group
     be = Backend(0)
     lib = be.lib
     try:
-        rng = np.random.default_rng(2024)
-        qd, kvd = HEADS * HD, KVH * HD
-        cos, sin = _rope(lib)
-        qn = (1.0 + 0.2 * rng.standard_normal(HD)).astype(np.float32)
-        kn = (1.0 + 0.2 * rng.standard_normal(HD)).astype(np.float32)
-        kc = np.zeros((CTX, kvd), dtype=np.uint16)
-        vc = np.zeros((CTX, kvd), dtype=np.uint16)
-        kc[:300] = _bf16(rng.standard_normal((300, kvd)))
-        vc[:300] = _bf16(rng.standard_normal((300, kvd)))
+        rng = np.random.default_rng(2024 + hd + group)
+        qd, kvd = heads * hd, kvh * hd
+        cos, sin = _rope(lib, hd, ctx)
+        qn = (1.0 + 0.2 * rng.standard_normal(hd)).astype(np.float32)
+        kn = (1.0 + 0.2 * rng.standard_normal(hd)).astype(np.float32)
+        kc = _bf16(rng.standard_normal((ctx, kvd)))
+        vc = _bf16(rng.standard_normal((ctx, kvd)))
 
         dev = torch.device("cuda", 0)
         d_kc = torch.from_numpy(kc.view(np.int16).copy()).to(dev)
@@ -58,28 +75,29 @@ def test_noalloc_attention_matches_allocating_entry_point():
         stream = torch.cuda.current_stream(dev)
         err = ctypes.create_string_buffer(256)
 
-        for pos in (300, 301):          # two calls in a row; 3 splits each (scratch in use)
+        for pos in (37, 38, 300, 301, ctx - 2, ctx - 1):
             qkv = (rng.standard_normal((1, qd + 2 * kvd)) * 2.0).astype(np.float32)
             # allocating entry point on host copies of the same cache state
             kc_ref, vc_ref = d_kc.cpu().numpy().view(np.uint16).copy(), d_vc.cpu().numpy().view(np.uint16).copy()
-            want = be.attention_test(HEADS, KVH, HD, CTX, qkv, pos, kc_ref, vc_ref, qn, kn, cos, sin)
+            want = be.attention_test(heads, kvh, hd, ctx, qkv, pos, kc_ref, vc_ref, qn, kn, cos, sin)
             d_qkv = torch.from_numpy(qkv.reshape(-1).copy()).to(dev)
             d_pos = torch.tensor([pos], dtype=torch.int32, device=dev)
             rc = lib.hyc_attention_decode_noalloc(
-                ctypes.c_void_p(stream.cuda_stream), HEADS, KVH, HD, CTX, d_pos.data_ptr(), 1e-5, d_qkv.data_ptr(),
+                ctypes.c_void_p(stream.cuda_stream), heads, kvh, hd, ctx, d_pos.data_ptr(), 1e-5, d_qkv.data_ptr(),
                 d_kc.data_ptr(), d_vc.data_ptr(), d_qn.data_ptr(), d_kn.data_ptr(), d_cos.data_ptr(),
                 d_sin.data_ptr(), d_ao.data_ptr(), err, 256)
             assert rc == 0, err.value.decode()
             torch.cuda.synchronize(dev)
             got = d_ao.cpu().numpy()[None]
             rel = np.abs(got - want).max() / max(np.abs(want).max(), 1e-6)
-            assert rel < 1e-4, (pos, rel)
+            assert rel < 1e-4, (hd, group, pos, rel)
             kc_got, vc_got = d_kc.cpu().numpy().view(np.uint16), d_vc.cpu().numpy().view(np.uint16)
             assert np.array_equal(vc_got[pos], vc_ref[pos]) and np.array_equal(kc_got[pos], kc_ref[pos])
 
-        # a shape beyond the fixed scratch is refused with a clear error
+        # one split more than the fixed scratch holds is refused with a clear error
+        big = (SCRATCH_FLOATS // (kvh * group * (hd + 2)) + 1) * SPLIT
         rc = lib.hyc_attention_decode_noalloc(
-            ctypes.c_void_p(stream.cuda_stream), 64, 64, 128, 65536, d_pos.data_ptr(), 1e-5, d_qkv.data_ptr(),
+            ctypes.c_void_p(stream.cuda_stream), heads, kvh, hd, big, d_pos.data_ptr(), 1e-5, d_qkv.data_ptr(),
             d_kc.data_ptr(), d_vc.data_ptr(), d_qn.data_ptr(), d_kn.data_ptr(), d_cos.data_ptr(), d_sin.data_ptr(),
             d_ao.data_ptr(), err, 256)
         assert rc == -2 and b"scratch limit" in err.value
