@@ -96,16 +96,58 @@ __device__ inline float block_sum(float v, float *red) {
 // Needs K % 4 == 0 and K <= 4 * kStageVec * blockDim.x.
 constexpr int kStageVec = 8;
 
+// RMSNorm inputs are staged block-wise: warp w of nw holds the Q8_K blocks
+// b = w, w + nw, ... (lane l: elements 256 b + 8 l .. 8 l + 7), so the sum of
+// squares has one fixed order for any CTA size: each block's 8 squares per
+// lane in element order, the warp butterfly per block, then the blocks in
+// index order (norm_ss).  Float4 j of a thread is block w + (j >> 1) nw,
+// half j & 1 of the lane's 8 elements.
+__device__ __forceinline__ int norm_f4(int j, int warp, int lane, int nw) {
+    return (warp + (j >> 1) * nw) * 64 + lane * 2 + (j & 1);
+}
+
 // The RMSNorm weight is a constant: load it before griddepcontrol.wait.
 template <int SV = kStageVec>
 __device__ inline void preload_norm(const GemvArgs &a, float4 (&nv)[SV], int K) {
     if (a.act != ACT_NORM) return;
     const float4 *y4 = (const float4 *)a.norm_w;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
 #pragma unroll
     for (int j = 0; j < SV; j++) {
-        const int i = threadIdx.x + j * blockDim.x;
+        const int i = norm_f4(j, warp, lane, nw);
         if (i < (K >> 2)) nv[j] = __ldg(y4 + i);
     }
+}
+
+// Sum of squares of the block-wise staged values xv (see norm_f4): per block
+// the lane's 8 squares in element order and the warp butterfly, written to
+// red[b]; then every thread adds red[0 .. nb-1] in order.  Needs nb <= 64
+// and every thread of the CTA.
+template <int SV>
+__device__ __forceinline__ float norm_ss(const float4 (&xv)[SV], int K, float *red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int nb = (K + 255) / 256, n4 = K >> 2;
+#pragma unroll
+    for (int j = 0; j < SV; j += 2) {
+        const int b = warp + (j >> 1) * nw;
+        float s = 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            if (j + h < SV && norm_f4(j + h, warp, lane, nw) < n4) {
+                const float4 v = xv[j + h];
+                s = __fadd_rn(s, __fmul_rn(v.x, v.x));
+                s = __fadd_rn(s, __fmul_rn(v.y, v.y));
+                s = __fadd_rn(s, __fmul_rn(v.z, v.z));
+                s = __fadd_rn(s, __fmul_rn(v.w, v.w));
+            }
+        }
+        s = warp_sum(s);
+        if (lane == 0 && b < nb) red[b] = s;
+    }
+    __syncthreads();
+    float ss = 0.f;
+    for (int b = 0; b < nb; b++) ss = __fadd_rn(ss, red[b]);
+    return ss;
 }
 
 template <int SV = kStageVec>
@@ -115,41 +157,43 @@ __device__ inline void stage_fp32(const GemvArgs &a, int t, float *dst, float *r
     const float4 *y4 = a.act == ACT_NORM ? (const float4 *)a.norm_w
                                          : (a.act == ACT_SILU ? (const float4 *)(a.x2 + (size_t)t * a.ldx) : nullptr);
     const int n4 = K >> 2;
-    float4 xv[SV], yv[SV];
-#pragma unroll
-    for (int j = 0; j < SV; j++) {
-        const int i = threadIdx.x + j * blockDim.x;
-        if (i < n4) {
-            xv[j] = x4[i];
-            if (pre && a.act == ACT_NORM) yv[j] = (*pre)[j];
-            else if (y4) yv[j] = __ldg(y4 + i);
-        }
-    }
     float4 *d4 = (float4 *)dst;
     if (a.act == ACT_NORM) {
-        float ss = 0.f;
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+        float4 xv[SV], yv[SV];
 #pragma unroll
         for (int j = 0; j < SV; j++) {
-            const int i = threadIdx.x + j * blockDim.x;
+            const int i = norm_f4(j, warp, lane, nw);
+            xv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
             if (i < n4) {
-                ss = __fadd_rn(ss, __fmul_rn(xv[j].x, xv[j].x));
-                ss = __fadd_rn(ss, __fmul_rn(xv[j].y, xv[j].y));
-                ss = __fadd_rn(ss, __fmul_rn(xv[j].z, xv[j].z));
-                ss = __fadd_rn(ss, __fmul_rn(xv[j].w, xv[j].w));
+                xv[j] = x4[i];
+                yv[j] = pre ? (*pre)[j] : __ldg(y4 + i);
             }
         }
-        ss = block_sum(ss, red);
+        __syncthreads();  // red and dst may still be read by the previous token's quantiser
+        const float ss = norm_ss<SV>(xv, K, red);
         const float scale = 1.0f / sqrtf(ss / (float)K + a.eps);
 #pragma unroll
         for (int j = 0; j < SV; j++) {
-            const int i = threadIdx.x + j * blockDim.x;
+            const int i = norm_f4(j, warp, lane, nw);
             if (i < n4)
                 d4[i] = make_float4(__fmul_rn(__fmul_rn(xv[j].x, scale), yv[j].x),
                                     __fmul_rn(__fmul_rn(xv[j].y, scale), yv[j].y),
                                     __fmul_rn(__fmul_rn(xv[j].z, scale), yv[j].z),
                                     __fmul_rn(__fmul_rn(xv[j].w, scale), yv[j].w));
         }
-    } else if (a.act == ACT_SILU) {
+        return;
+    }
+    float4 xv[SV], yv[SV];
+#pragma unroll
+    for (int j = 0; j < SV; j++) {
+        const int i = threadIdx.x + j * blockDim.x;
+        if (i < n4) {
+            xv[j] = x4[i];
+            if (y4) yv[j] = __ldg(y4 + i);
+        }
+    }
+    if (a.act == ACT_SILU) {
 #pragma unroll
         for (int j = 0; j < SV; j++) {
             const int i = threadIdx.x + j * blockDim.x;
@@ -172,11 +216,9 @@ __device__ inline void stage_fp32(const GemvArgs &a, int t, float *dst, float *r
 // plane-major codes and block constants for token t.  Bit-identical to the
 // host quantiser: first index of the largest |x|, iscale = -127/max,
 // d = 1/iscale, round-half-even, clip +-127, non-finite products -> 0.
-__device__ inline void quantize_block_warp(const float *src, Q8Smem &s, int t, int b, int nb, int K) {
+// The block's values are in registers: lane l holds elements 8 l .. 8 l + 7.
+__device__ inline void quantize_vals_warp(const float (&v)[8], Q8Smem &s, int t, int b, int nb, int K) {
     const int lane = threadIdx.x & 31;
-    const float *p = src + b * 256 + lane * 8;
-    const float4 v0 = *(const float4 *)&p[0], v1 = *(const float4 *)&p[4];
-    const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
     // lane-local first maximum of |x|, then one redux for the max and one
     // for the smallest index holding it (finite |x| bit patterns order like
     // the values; NaN never qualifies, as in the host's strict '>')
@@ -225,6 +267,14 @@ __device__ inline void quantize_block_warp(const float *src, Q8Smem &s, int t, i
         s.d[t * nb + b] = d;
         s.sum[t * nb + b] = total;
     }
+}
+
+__device__ inline void quantize_block_warp(const float *src, Q8Smem &s, int t, int b, int nb, int K) {
+    const int lane = threadIdx.x & 31;
+    const float *p = src + b * 256 + lane * 8;
+    const float4 v0 = *(const float4 *)&p[0], v1 = *(const float4 *)&p[4];
+    const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    quantize_vals_warp(v, s, t, b, nb, K);
 }
 
 // Build the Q8_K activation of all nt tokens in shared memory.

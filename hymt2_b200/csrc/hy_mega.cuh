@@ -264,67 +264,71 @@ __device__ inline void mega_fill(const MegaArgs &a, const MegaLayer *tab, uint8_
 // ---------------------------------------------------------------- activation staging
 
 // RMSNorm weights of the next normalised phase, loaded before the barrier
-// wait (they are constants): threads 0..255 hold elements t + 256 j.
-template <int SV>
+// wait (they are constants), in the block-wise staging layout of norm_f4 with
+// this CTA's warps: warp b < K/256 holds block b (lane l: elements 8l..8l+7).
 struct NormPre {
-    float4 w[SV];
+    float4 w[2];
 };
-template <int SV>
-__device__ __forceinline__ void norm_preload(const float *norm_w, int K, NormPre<SV> &p) {
-    const int tid = threadIdx.x;
-#pragma unroll
-    for (int j = 0; j < SV; j++) {
-        const int i = tid + j * kGemvThreads;
-        if (tid < kGemvThreads && i < (K >> 2)) p.w[j] = __ldg((const float4 *)norm_w + i);
+__device__ __forceinline__ void norm_preload(const float *norm_w, int K, NormPre &p) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < K / 256) {
+        p.w[0] = __ldg((const float4 *)norm_w + norm_f4(0, warp, lane, kMegaWarps));
+        p.w[1] = __ldg((const float4 *)norm_w + norm_f4(1, warp, lane, kMegaWarps));
     }
 }
 
-// fp32 input (x, or the stage's own s.x when x == nullptr), optionally
-// RMSNorm * (preloaded) weights, then Q8_K into shared memory.  With a norm,
-// threads 0..255 hold elements i = t + 256 j exactly as the 256-thread
-// per-layer kernels do, so the sum of squares (and everything after it) is
-// bit-identical; the extra warps contribute zeros to the block reduction.
-template <int SV>
-__device__ inline void mega_stage(const float *x, const NormPre<SV> *pre, float eps, int K, Q8Smem &s) {
-    const int n4 = K >> 2, tid = threadIdx.x;
-    const float4 *src = x ? (const float4 *)x : (const float4 *)s.x;
-    if (pre) {
-        float4 xv[SV];
-#pragma unroll
-        for (int j = 0; j < SV; j++) {
-            const int i = tid + j * kGemvThreads;
-            if (tid < kGemvThreads && i < n4) xv[j] = src[i];
-        }
-        float ss = 0.f;
-#pragma unroll
-        for (int j = 0; j < SV; j++) {
-            const int i = tid + j * kGemvThreads;
-            if (tid < kGemvThreads && i < n4) {
-                ss = __fadd_rn(ss, __fmul_rn(xv[j].x, xv[j].x));
-                ss = __fadd_rn(ss, __fmul_rn(xv[j].y, xv[j].y));
-                ss = __fadd_rn(ss, __fmul_rn(xv[j].z, xv[j].z));
-                ss = __fadd_rn(ss, __fmul_rn(xv[j].w, xv[j].w));
-            }
-        }
-        ss = block_sum(ss, s.red);  // also orders every read of s.x before the writes below
-        const float scale = 1.0f / sqrtf(ss / (float)K + eps);
-#pragma unroll
-        for (int j = 0; j < SV; j++) {
-            const int i = tid + j * kGemvThreads;
-            if (tid < kGemvThreads && i < n4) {
-                const float4 wv = pre->w[j];
-                ((float4 *)s.x)[i] = make_float4(__fmul_rn(__fmul_rn(xv[j].x, scale), wv.x),
-                                                 __fmul_rn(__fmul_rn(xv[j].y, scale), wv.y),
-                                                 __fmul_rn(__fmul_rn(xv[j].z, scale), wv.z),
-                                                 __fmul_rn(__fmul_rn(xv[j].w, scale), wv.w));
-            }
-        }
-    } else if (x) {
-        for (int i = tid; i < n4; i += kMegaThreads) ((float4 *)s.x)[i] = src[i];
+// x (K <= 256 * kMegaWarps inputs, global or shared) -> RMSNorm * preloaded
+// weights -> Q8_K in shared memory.  Warp b < K/256 loads, normalises and
+// quantises block b in its registers; the sum of squares is norm_ss's fixed
+// order, so codes and scales are those of the per-layer kernels (stage_fp32
+// and quantize_block_warp).
+__device__ inline void mega_stage_norm(const float *x, const NormPre &pre, float eps, int K, Q8Smem &s) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nb = K / 256;
+    float4 xv[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+    if (warp < nb) {
+        xv[0] = ((const float4 *)x)[norm_f4(0, warp, lane, kMegaWarps)];
+        xv[1] = ((const float4 *)x)[norm_f4(1, warp, lane, kMegaWarps)];
+    }
+    const float ss = norm_ss<2>(xv, K, s.red);
+    const float scale = 1.0f / sqrtf(ss / (float)K + eps);
+    if (warp < nb) {
+        const float v[8] = {__fmul_rn(__fmul_rn(xv[0].x, scale), pre.w[0].x),
+                            __fmul_rn(__fmul_rn(xv[0].y, scale), pre.w[0].y),
+                            __fmul_rn(__fmul_rn(xv[0].z, scale), pre.w[0].z),
+                            __fmul_rn(__fmul_rn(xv[0].w, scale), pre.w[0].w),
+                            __fmul_rn(__fmul_rn(xv[1].x, scale), pre.w[1].x),
+                            __fmul_rn(__fmul_rn(xv[1].y, scale), pre.w[1].y),
+                            __fmul_rn(__fmul_rn(xv[1].z, scale), pre.w[1].z),
+                            __fmul_rn(__fmul_rn(xv[1].w, scale), pre.w[1].w)};
+        quantize_vals_warp(v, s, 0, warp, nb, K);
     }
     __syncthreads();
-    const int nb = K / 256;
-    for (int b = tid >> 5; b < nb; b += kMegaWarps) quantize_block_warp(s.x, s, 0, b, nb, K);
+}
+
+// x (K inputs as they are) -> Q8_K: warp w quantises blocks w, w + 16, ...
+// (NBW of them) in its registers, every load issued before any arithmetic;
+// the values and element order of quantize_block_warp.
+template <int NBW>
+__device__ inline void mega_stage_plain(const float *x, int K, Q8Smem &s) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nb = K / 256;
+    float4 xv[NBW][2];
+#pragma unroll
+    for (int i = 0; i < NBW; i++) {
+        const int b = warp + kMegaWarps * i;
+        if (b < nb) {
+            xv[i][0] = ((const float4 *)x)[b * 64 + lane * 2];
+            xv[i][1] = ((const float4 *)x)[b * 64 + lane * 2 + 1];
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < NBW; i++) {
+        const int b = warp + kMegaWarps * i;
+        if (b < nb) {
+            const float v[8] = {xv[i][0].x, xv[i][0].y, xv[i][0].z, xv[i][0].w,
+                                xv[i][1].x, xv[i][1].y, xv[i][1].z, xv[i][1].w};
+            quantize_vals_warp(v, s, 0, b, nb, K);
+        }
+    }
     __syncthreads();
 }
 
@@ -589,8 +593,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
         for (int t = 0; t < 4; t++) mega_fill(a, tab, smem, &mbar[t], t, 0);
     pending |= 0xfu;
     if (a.steps > 0 && attn_cta(pos)) mega_kv_fill<HD>(a, tab[0], sK, sV, akvh, j0_of(pos), ncache_of(pos));
-    NormPre<2> npre;
-    norm_preload<2>(tab[0].attn_norm, a.H, npre);
+    NormPre npre;
+    norm_preload(tab[0].attn_norm, a.H, npre);
     for (int step = 0; step < a.steps && ok; step++) {
         if (pos < 0 || pos >= a.ctx) {
             if (tid == 0) raise_err(a, MEGA_ERR_POS);
@@ -621,7 +625,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             aa.tickets = a.sync->tickets;
             // ---- q|k|v
             {
-                mega_stage<2>(l == 0 ? nullptr : a.h, &npre, a.eps, a.H, st);
+                mega_stage_norm(l == 0 ? st.x : a.h, npre, a.eps, a.H, st);
                 tl_sub(a, tls);
                 int4 act[1][4];
                 float dblk[1];
@@ -728,13 +732,13 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 // follow the head)
                 if (l + 1 < a.L && attn_cta(npos)) mega_kv_fill<HD>(a, tab[nl], sK, sV, akvh, j0_of(npos), ncache_of(npos));
             }
-            norm_preload<2>(ly.ffn_norm, a.H, npre);
+            norm_preload(ly.ffn_norm, a.H, npre);
             if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
             tl_cta(a, step == 1 && l == 5, 5);
             tl_mark(a, tli);
             // ---- gate|up (interleaved rows) -> silu(gate) * up
             {
-                mega_stage<2>(a.h, &npre, a.eps, a.H, st);
+                mega_stage_norm(a.h, npre, a.eps, a.H, st);
                 tl_sub(a, tls);
                 int4 act[1][4];
                 float dblk[1];
@@ -778,7 +782,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             tl_mark(a, tli);
             // ---- down (+ residual)
             {
-                mega_stage<2 * CF>(a.act, (const NormPre<2 * CF> *)nullptr, a.eps, a.F, st);
+                mega_stage_plain<(CF * 8 + kMegaWarps - 1) / kMegaWarps>(a.act, a.F, st);
                 tl_sub(a, tls);
                 int4 act[CF][4];
                 float dblk[CF];
@@ -822,7 +826,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 }
                 for (int k = 0; k < a.head_ns && k < hst; k++) hpend |= 1u << k;
             }
-            norm_preload<2>(l + 1 < a.L ? tab[l + 1].attn_norm : a.out_norm, a.H, npre);
+            norm_preload(l + 1 < a.L ? tab[l + 1].attn_norm : a.out_norm, a.H, npre);
             if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
             tl_cta(a, step == 1 && l == 5, 9);
             tl_mark(a, tli);
@@ -830,7 +834,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
         if (!ok) break;
         // ---- LM head + argmax (rows < vocab_out compete), rows streamed through the ring
         {
-            mega_stage<2>(a.h, &npre, a.eps, a.H, st);
+            mega_stage_norm(a.h, npre, a.eps, a.H, st);
             // this lane's unit of the activation, kept in registers for every row
             const bool uok = lane < a.H / 64;
             int4 hav[4];
@@ -877,7 +881,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
         }
         tl_mark(a, tli);
         bar_arrive(a, target);
-        norm_preload<2>(tab[0].attn_norm, a.H, npre);
+        norm_preload(tab[0].attn_norm, a.H, npre);
         if (ok && step + 1 < a.steps) {
             // the ring is drained: layer 0's o_proj, gate|up and down slices and K/V rows for the next step
             if (tid == 0) {
