@@ -490,6 +490,7 @@ template <int HD>
 struct ChunkScratch {
     float pm[kDecWarps], pl[kDecWarps];
     float po[kDecWarps][HD];
+    float pw[kDecWarps][kChunkMax / 2];  // each warp's key probabilities (a warp holds <= cs/2 keys)
 };
 
 // All kDecWarps warps of a unit.  krow(j, c) is 16-byte chunk c of staged K
@@ -497,10 +498,15 @@ struct ChunkScratch {
 // `pos` comes from skc/svc.  Writes part[(h * max_chunks + chunk) * (HD+2)]
 // = (m, l, o[HD]) for h = kvh*G .. kvh*G+G-1.  Synchronises the kDecWarps
 // warps with named barrier bar_id.
-template <int HD, int G, typename KRow>
+struct NoMark {
+    __device__ __forceinline__ void operator()() const {}
+};
+
+template <int HD, int G, typename KRow, typename Mark = NoMark>
 __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int chunk, int cs, int pos, KRow krow,
                                                 const uint16_t *sV, const float (*sq)[HD], const float *skc,
-                                                const float *svc, ChunkScratch<HD> &S, int bar_id) {
+                                                const float *svc, ChunkScratch<HD> &S, int bar_id,
+                                                Mark mark = Mark()) {
     constexpr int DQ = HD / 4;            // dims per lane in a 4-lane key group
     constexpr int DPL = HD / 32;          // output dims per lane
     constexpr int NSUB = kDecWarps / G;   // warps per head
@@ -571,6 +577,7 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
         s[t] = j < ke ? v * a.scale : -INFINITY;
         mloc = fmaxf(mloc, s[t]);
     }
+    mark();
     mloc = warp_max(mloc);
     float lsum = 0.f;
 #pragma unroll
@@ -580,18 +587,21 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
         if (qtr == 0) lsum += s[t];
     }
     lsum = warp_sum(lsum);
+    mark();
     float o[DPL];
 #pragma unroll
     for (int q = 0; q < DPL; q++) o[q] = 0.f;
-    // p of key j lives in s[(j - kb) >> 3] of lane group (j - kb) & 7
-    const auto p_of = [&](int j) {
-        const int t = (j - kb) >> 3, src = ((j - kb) & 7) * 4;
-        float p = 0.f;
+    // the warp's key probabilities go through shared memory, so p.V reads each
+    // key's p with one broadcast load instead of a shuffle per candidate slot
+    if (qtr == 0) {
 #pragma unroll
-        for (int tt = 0; tt < KMAX; tt++)
-            if (tt == t) p = __shfl_sync(0xffffffffu, s[tt], src);
-        return p;
-    };
+        for (int t = 0; t < KMAX; t++) {
+            const int j = kb + grp + 8 * t;
+            if (j < ke) S.pw[w][j - kb] = s[t];
+        }
+    }
+    __syncwarp();
+    const auto p_of = [&](int j) { return S.pw[w][j - kb]; };
     const auto v_of = [&](int j, float (&vv)[DPL]) {
         if (j0 + j == pos) {
 #pragma unroll
@@ -630,6 +640,7 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
 #pragma unroll
         for (int q = 0; q < DPL; q++) o[q] = fmaf(p, vv[q], o[q]);
     }
+    mark();
     if (lane == 0) {
         S.pm[w] = kb < nk ? mloc : -INFINITY;
         S.pl[w] = kb < nk ? lsum : 0.f;
@@ -637,6 +648,7 @@ __device__ __forceinline__ void attn_chunk_main(const AttnArgs &a, int kvh, int 
 #pragma unroll
     for (int q = 0; q < DPL; q++) S.po[w][lane * DPL + q] = o[q];
     asm volatile("bar.sync %0, %1;" ::"r"(bar_id), "r"(kDecWarps * 32) : "memory");
+    mark();
     if (w >= G) return;
     float M = -INFINITY;
 #pragma unroll

@@ -25,6 +25,7 @@
 #include "hy_mega.cuh"
 #include "hy_misc.cuh"
 #include "hy_tc.cuh"
+#include "hy_tp.cuh"
 
 using namespace hyk;
 
@@ -112,8 +113,6 @@ struct HyCtx {
     char mega_why[128] = {0};       // why unsupported
     MegaLayer *d_mega_layers = nullptr;
     MegaSync *d_mega_sync = nullptr;
-    uint8_t *d_head_i8 = nullptr;   // int8 planes of the Q6_K head for the persistent kernel
-    size_t head_i8_bytes = 0;
     unsigned long long *d_tl = nullptr;
     int tl_cap = 0;
     MegaPlan mega_plan_v{};
@@ -124,10 +123,17 @@ struct HyCtx {
     float *d_tcad = nullptr;        // their block scales
     int *d_tcerr = nullptr;         // set by tc_gemm on a bounded-wait timeout
     size_t tca_bytes = 0;
-    int head_keep = 0;              // head rows per CTA kept resident in L2 by the persistent kernel
     size_t l2_bytes = 0;
     void *mega_kernel = nullptr;
     Batch *bat = nullptr;           // ragged multi-sequence batches (hy_batch.cuh)
+    // tensor parallelism: this handle holds one rank's share of a split model (hy_tp.cuh)
+    int tp_rank = 0, tp_world = 1, tp_vocab0 = 0;
+    bool tp_on = false;             // connected to its peers: o_proj / down / head exchange
+    uint8_t *d_tp_area = nullptr;   // own exchange area, exported to the peers
+    float *d_tp_part = nullptr;     // partial o_proj / down products [kMaxChunk][H]
+    int *d_tp_err = nullptr;
+    long long tp_cap = 0;
+    TpArgs tp{};
 };
 
 int trace_slot(HyCtx *c) { return c->trace_on && c->trace_next < kTraceSlots ? c->trace_next++ : -1; }
@@ -679,7 +685,8 @@ bool gateup_forward(HyCtx *c, const Fwd &f, const Layer &L, int nt, bool pdl) {
     return run_multi(c, ws, outs, lds, 2, a, pdl);
 }
 
-bool down_forward(HyCtx *c, const Fwd &f, const Layer &L, int nt, bool pdl, float *dst) {
+// dst += down(act) (store instead when !accumulate: a tensor-parallel partial)
+bool down_forward(HyCtx *c, const Fwd &f, const Layer &L, int nt, bool pdl, float *dst, bool accumulate = true) {
     GemvArgs a = gemv_args(nt, c->F);
     if (ffn_pair_ok(L, nt)) {
         a.act = ACT_VEC;  // g already holds silu(gate)*up
@@ -694,17 +701,32 @@ bool down_forward(HyCtx *c, const Fwd &f, const Layer &L, int nt, bool pdl, floa
         HyWeight *ws[1] = {L.d};
         float *outs[1] = {dst};
         const int lds[1] = {c->H};
-        if (tc_usable(c, nt, ws, 1)) return tc_linear(c, a, nt, ws, outs, lds, 1, 1, pdl);
+        if (tc_usable(c, nt, ws, 1)) return tc_linear(c, a, nt, ws, outs, lds, 1, accumulate ? 1 : 0, pdl);
     }
-    a.epi = EPI_ADD;
+    a.epi = accumulate ? EPI_ADD : EPI_STORE;
     a.nw = 1;
     a.rows_total = L.d->n;
     a.w[0] = desc(L.d, dst, c->H);
     return run_gemv(c, a, pdl);
 }
 
+// Tensor parallelism: h[0 .. nt*H) += the sum over ranks of their partial
+// products in d_tp_part (one-shot push over peer memory, hy_tp.cuh).
+bool tp_reduce(HyCtx *c, float *h, int nt) {
+    TpArgs a = c->tp;
+    a.h = h;
+    a.part = c->d_tp_part;
+    a.n = nt * c->H;
+    const int ctas = std::min(kTpMaxCtas, (a.n + kTpSlice - 1) / kTpSlice);
+    a.slice = ((a.n + ctas - 1) / ctas + 3) & ~3;
+    return launch(c, tp_allreduce_add, dim3(ctas), dim3(kTpThreads), 0, false, a);
+}
+
 bool ffn_forward(HyCtx *c, const Fwd &f, const Layer &L, int nt, bool pdl) {
-    return gateup_forward(c, f, L, nt, pdl) && down_forward(c, f, L, nt, pdl, f.h);
+    if (!c->tp_on) return gateup_forward(c, f, L, nt, pdl) && down_forward(c, f, L, nt, pdl, f.h);
+    // tensor parallelism: the rank's partial down product, then h += the sum over ranks
+    return gateup_forward(c, f, L, nt, pdl) && down_forward(c, f, L, nt, pdl, c->d_tp_part, false) &&
+           tp_reduce(c, f.h, nt);
 }
 
 bool layer_forward(HyCtx *c, const Fwd &f, int li, int nt, bool pdl) {
@@ -765,22 +787,26 @@ bool layer_forward(HyCtx *c, const Fwd &f, int li, int nt, bool pdl) {
         if (!attention(c, aa, nt, pdl)) return false;
     }
     {
+        // tensor parallelism: the rank's partial product, then h += the sum over ranks
+        float *dst = c->tp_on ? c->d_tp_part : f.h;
+        const int epi = c->tp_on ? 0 : 1;
         GemvArgs a = gemv_args(nt, c->qd);
         a.act = ACT_VEC;
         a.x = f.ao;
         a.ldx = c->qd;
         HyWeight *ws[1] = {L.o};
-        float *outs[1] = {f.h};
+        float *outs[1] = {dst};
         const int lds[1] = {c->H};
         if (tc_usable(c, nt, ws, 1)) {
-            if (!tc_linear(c, a, nt, ws, outs, lds, 1, 1, pdl)) return false;
+            if (!tc_linear(c, a, nt, ws, outs, lds, 1, epi, pdl)) return false;
         } else {
-            a.epi = EPI_ADD;
+            a.epi = epi ? EPI_ADD : EPI_STORE;
             a.nw = 1;
             a.rows_total = L.o->n;
-            a.w[0] = desc(L.o, f.h, c->H);
+            a.w[0] = desc(L.o, dst, c->H);
             if (!run_gemv(c, a, pdl)) return false;
         }
+        if (c->tp_on && !tp_reduce(c, f.h, nt)) return false;
     }
     return ffn_forward(c, f, L, nt, pdl);
 }
@@ -798,13 +824,22 @@ bool head_forward(HyCtx *c, const float *x, bool store_logits, bool argmax, bool
     a.rows_total = c->outw->n;
     a.w[0] = desc(c->outw, store_logits ? c->d_logits : nullptr, c->outw->n);
     if (argmax) {
+        // rows below vocab_out compete; a tensor-parallel rank holds rows tp_vocab0 .. of the vocabulary
+        const int lim = (c->vocab_out > 0 ? c->vocab_out : c->outw->n + c->tp_vocab0) - c->tp_vocab0;
         a.epi = EPI_ARGMAX;
         a.amax = &c->d_state->amax;
-        a.amax_rows = c->vocab_out > 0 ? c->vocab_out : c->outw->n;
+        a.amax_rows = std::max(0, std::min(lim, c->outw->n));
+        a.amax_base = c->tp_vocab0;
     } else {
         a.epi = EPI_STORE;
     }
-    return run_gemv(c, a, pdl, 2);
+    if (!run_gemv(c, a, pdl, 2)) return false;
+    if (argmax && c->tp_on) {  // the greedy token: the largest key over the ranks' vocabulary slices
+        TpArgs t = c->tp;
+        t.key = &c->d_state->amax;
+        return launch(c, tp_argmax_exchange, dim3(1), dim3(32), 0, false, t);
+    }
+    return true;
 }
 
 bool layers_forward(HyCtx *c, const Fwd &f, int nt, bool pdl) {
@@ -910,11 +945,10 @@ bool mega_check(HyCtx *c) {
     if (cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->dev) != cudaSuccess || !coop)
         return no("no cooperative launch");
     c->mega_plan_v = mega_plan(c->nsm, c->H, c->F, c->qd, c->kvd, c->outw->n, c->hd);
-    if (!mega_head_ring(c->mega_plan_v, head_i8_stride(c->H)))
-        return no("LM-head rows do not fit the shared-memory ring");
+    if (!mega_head_ring(c->mega_plan_v, c->outw->stride))
+        return no("LM-head rows do not fit the shared-memory rings");
     // about three quarters of L2 holds the first rows of every CTA's head slice
     // across tokens (the layer weights, read once per token, are evict-first)
-    c->head_keep = (int)((double)c->l2_bytes * 0.75 / ((double)c->nsm * (double)head_i8_stride(c->H)));
     if (cudaFuncSetAttribute(c->mega_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)c->mega_plan_v.bytes) != cudaSuccess) {
         cudaGetLastError();
@@ -941,20 +975,6 @@ bool mega_check(HyCtx *c) {
         tab[i].k_norm = L.k_norm;
         tab[i].kc = c->d_kv + (size_t)i * 2 * c->ctx * c->kvd;
         tab[i].vc = tab[i].kc + (size_t)c->ctx * c->kvd;
-    }
-    {
-        const size_t hb = (size_t)c->outw->n * head_i8_stride(c->H);
-        if (c->head_i8_bytes != hb) {
-            if (c->d_head_i8) cudaFree(c->d_head_i8);
-            c->d_head_i8 = nullptr;
-            c->head_i8_bytes = 0;
-            CK(c, cudaMalloc(&c->d_head_i8, hb));
-            c->head_i8_bytes = hb;
-        }
-        const long long groups = (long long)c->outw->n * (c->H / 16);
-        q6k_to_i8<<<(unsigned)((groups + 255) / 256), 256, 0, c->st>>>(desc(c->outw, nullptr, 0), c->d_head_i8,
-                                                                     head_i8_stride(c->H));
-        CK(c, cudaGetLastError());
     }
     if (!c->d_mega_layers) CK(c, cudaMalloc(&c->d_mega_layers, (size_t)c->L * sizeof(MegaLayer)));
     if (!c->d_mega_sync) CK(c, cudaMalloc(&c->d_mega_sync, sizeof(MegaSync)));
@@ -988,9 +1008,9 @@ bool mega_launch(HyCtx *c, int steps) {
     a.stage_off = p.stage_off;
     a.attn_off = p.attn_off;
     a.kmax = p.kmax;
-    a.head_ns = p.head_ns;
-    a.head_keep = c->head_keep;
-    for (int i = 0; i < 4; i++) a.head_off[i] = p.head_off[i];
+    a.head_reg[0] = p.head_reg[0];
+    a.head_reg[1] = p.head_reg[1];
+    a.head_n1 = p.head_n1;
     AttnArgs &aa = a.attn;
     aa.qkv = c->d_qkv;
     aa.qkv_ld = c->qd + 2 * c->kvd;
@@ -1017,8 +1037,6 @@ bool mega_launch(HyCtx *c, int steps) {
     aa.trace = -1;
     a.head = desc(c->outw, nullptr, c->outw->n);
     a.embd = desc(c->embd, nullptr, 0);
-    a.head_i8 = c->d_head_i8;
-    a.head_i8_stride = head_i8_stride(c->H);
     a.vocab_out = c->vocab_out > 0 ? c->vocab_out : c->outw->n;
     a.out_norm = c->d_out_norm;
     a.h = c->d_h;
@@ -1126,9 +1144,6 @@ void free_fused(HyCtx *c) {
     if (c->d_mega_layers) cudaFree(c->d_mega_layers);
     if (c->d_mega_sync) cudaFree(c->d_mega_sync);
     if (c->d_tl) cudaFree(c->d_tl);
-    if (c->d_head_i8) cudaFree(c->d_head_i8);
-    c->d_head_i8 = nullptr;
-    c->head_i8_bytes = 0;
     c->d_mega_layers = nullptr;
     c->d_mega_sync = nullptr;
     c->d_tl = nullptr;

@@ -41,6 +41,7 @@ struct GemvArgs {
     int epi;
     unsigned long long *amax;
     int amax_rows;
+    int amax_base;  // added to the row index in the argmax key (a vocabulary slice's first row)
     int32_t *ints;  // optional exact per-block integers [nt][rows][nblk]
     int trace;      // timeline slot (< 0: off)
     int interleave; // 2 weights of equal n: merged row m -> weight m & 1, row m >> 1
@@ -340,7 +341,7 @@ __device__ __forceinline__ void row_epilogue(const GemvArgs &a, const WDesc &w, 
     if (a.epi == EPI_ARGMAX) {
         if (w.out) w.out[lr] = res[0];
         if (row < a.amax_rows) {
-            const unsigned long long key = argmax_key(res[0], (uint32_t)row);
+            const unsigned long long key = argmax_key(res[0], (uint32_t)(row + a.amax_base));
             if (key > best) best = key;
         }
         return;
@@ -371,22 +372,31 @@ __device__ inline void argmax_commit(const GemvArgs &a, unsigned long long best,
 
 // ---------------------------------------------------------------- PANEL (STQ1_0 / Q2_0C)
 
+// dp4a of unsigned weight bytes (0..255) with signed activation bytes.
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
 // Exact block integer of one 16-byte panel chunk against 64 activation bytes
-// (4 planes x 16): sum_l sum_i code_l(w[i]) * a_l[i].
-__device__ __forceinline__ int panel_chunk_dot(const uint4 wv, const int4 *act4) {
+// (4 planes x 16): sum_l sum_i code_l(w[i]) * a_l[i].  Plane l's codes are
+// masked in place (bits 2l..2l+1 of every byte, no shift), so its dot product
+// is 4^l times the plane's sum, an exact multiple that an arithmetic shift
+// divides back out; four independent dp4a chains, one per plane.
+__device__ __forceinline__ int panel_chunk_dot4(const uint4 wv, const int4 *act4) {
     const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
-    int e = 0;
+    int e0 = 0, e1 = 0, e2 = 0, e3 = 0;
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-        const int a0 = ((const int *)&act4[0])[j], a1 = ((const int *)&act4[1])[j];
-        const int a2 = ((const int *)&act4[2])[j], a3 = ((const int *)&act4[3])[j];
-        e = dp4a((int)(wd[j] & 0x03030303u), a0, e);
-        e = dp4a((int)((wd[j] >> 2) & 0x03030303u), a1, e);
-        e = dp4a((int)((wd[j] >> 4) & 0x03030303u), a2, e);
-        e = dp4a((int)((wd[j] >> 6) & 0x03030303u), a3, e);
+        e0 = dp4a_us(wd[j] & 0x03030303u, ((const int *)&act4[0])[j], e0);
+        e1 = dp4a_us(wd[j] & 0x0c0c0c0cu, ((const int *)&act4[1])[j], e1);
+        e2 = dp4a_us(wd[j] & 0x30303030u, ((const int *)&act4[2])[j], e2);
+        e3 = dp4a_us(wd[j] & 0xc0c0c0c0u, ((const int *)&act4[3])[j], e3);
     }
-    return e;
+    return (e0 + (e1 >> 2)) + ((e2 >> 4) + (e3 >> 6));
 }
+__device__ __forceinline__ int panel_chunk_dot(const uint4 wv, const int4 *act4) { return panel_chunk_dot4(wv, act4); }
 
 // Decode (nt == 1): the lane's activation chunks live in registers for the
 // whole launch.  CPL = 16-byte chunks per lane per row (K <= 2048*CPL).
@@ -502,20 +512,6 @@ __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(src) : "memory");
 }
 
-// Exact block integer of one 16-byte panel chunk with four independent
-// dp4a chains (one per 2-bit plane) so the adds overlap.
-__device__ __forceinline__ int panel_chunk_dot4(const uint4 wv, const int4 *act4) {
-    const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
-    int e0 = 0, e1 = 0, e2 = 0, e3 = 0;
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        e0 = dp4a((int)(wd[j] & 0x03030303u), ((const int *)&act4[0])[j], e0);
-        e1 = dp4a((int)((wd[j] >> 2) & 0x03030303u), ((const int *)&act4[1])[j], e1);
-        e2 = dp4a((int)((wd[j] >> 4) & 0x03030303u), ((const int *)&act4[2])[j], e2);
-        e3 = dp4a((int)((wd[j] >> 6) & 0x03030303u), ((const int *)&act4[3])[j], e3);
-    }
-    return (e0 + e1) + (e2 + e3);
-}
 
 template <int CPL>
 __global__ void __launch_bounds__(kGemvThreads) gemv_panel_dec(const __grid_constant__ GemvArgs a, int rows_per_cta) {

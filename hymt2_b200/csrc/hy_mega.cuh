@@ -61,13 +61,9 @@ struct MegaArgs {
     int slot_off[4];          // dynamic-smem offsets of the weight slots
     int stage_off, attn_off;  // dynamic-smem offsets of the Q8_K stage and the K/V area
     int kmax;                 // largest GEMV input length (stage plan)
-    int head_ns;              // LM-head ring stages (kHeadRows rows each) and their smem offsets
-    int head_off[4];
-    int head_keep;            // rows of each CTA's head slice read with L2 evict-last (stay resident)
+    int head_reg[2], head_n1;  // LM-head row slots: head_n1 of them from head_reg[0], the rest from head_reg[1]
     AttnArgs attn;            // shape, rope tables, part buffer; per-layer fields set in-kernel
     WDesc head, embd;
-    const uint8_t *head_i8;   // int8 planes of the Q6_K head (q6k_to_i8), streamed by the ring
-    long long head_i8_stride;
     int vocab_out;
     const float *out_norm;
     float *h, *qkv, *ao, *act;
@@ -370,7 +366,10 @@ __device__ __forceinline__ void mega_act(const Q8Smem &s, int K, int4 (&act)[CPL
 
 // Rows [r0, r1) of the phase's merged row space, weights from the slot (row
 // rr = r - r0 at slot row srow(rr)), RG rows per warp iteration.  Same
-// per-row arithmetic as gemv_panel_dec.  epi(r, acc[], r1) runs on lane 0.
+// per-row arithmetic as gemv_panel_dec.  After the butterfly every lane 4s
+// holds all RG sums; epi(r, acc[], r1, s) runs on lanes 4s (s = 0..7), each
+// finishing the rows (or row pairs) of its index s, so the epilogues of a
+// group run side by side.
 template <int CPL, int RG, bool INTERLEAVED, typename Epi>
 __device__ __forceinline__ void mega_rows(int shift, int off, int r0, int r1, int rpc, const uint8_t *sw,
                                          const float *ss, int K, const int4 (&act)[CPL][4], const float (&dblk)[CPL],
@@ -414,101 +413,102 @@ __device__ __forceinline__ void mega_rows(int shift, int off, int r0, int r1, in
         for (int o = 16; o >= 4; o >>= 1)
 #pragma unroll
             for (int g = 0; g < RG; g++) acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], o);
-        if (lane == 0) epi(rg, acc, r1);
+        if ((lane & 3) == 0) epi(rg, acc, r1, lane >> 2);
     }
 }
 
 // ---------------------------------------------------------------- LM head (Q6_K) with argmax
 
-// The head streams through a ring of shared-memory stages of kHeadRows rows
-// (one row per warp); each stage is one bulk copy of consecutive rows of the
-// relayouted Q6_K head (ql | qh | scales | d planes per row).
-constexpr int kHeadRows = kMegaWarps;
+// The head's native Q6_K rows (device layout ql | qh | scales | d per row)
+// stream through a private ring of kHeadRing row slots per warp, filled with
+// cp.async (16-byte copies spread over the lanes, one commit group per row),
+// so each warp keeps kHeadRing rows in flight and no CTA barrier separates
+// the rows.  Warp w takes rows r0 + w, r0 + w + 16, ... of its CTA's slice.
+constexpr int kHeadRing = 5;
 
-// One Q6_K row held in shared memory against the stage's Q8_K activation;
-// the arithmetic (unit split, integer sums, float order, warp sum) is
-// gemv_q6k's, so the logit is identical.  Returns the sum on every lane.
-__device__ __forceinline__ float q6k_row_smem(const uint8_t *row, int nb, int K, const Q8Smem &s) {
-    const int lane = threadIdx.x & 31, nunit = nb * 4;
-    float acc = 0.f;
-    for (int u0 = 0; u0 < nunit; u0 += 32) {
-        const int u = u0 + lane;
-        const bool ok = u < nunit;
-        const int b = u >> 2, hf = (u >> 1) & 1, sg = u & 1;
-        uint4 qa = make_uint4(0, 0, 0, 0), qb = qa, qh = qa, scv = qa;
-        float dw = 0.f;
-        if (ok) {
-            qa = *(const uint4 *)(row + (size_t)b * 128 + hf * 64 + sg * 16);
-            qb = *(const uint4 *)(row + (size_t)b * 128 + hf * 64 + 32 + sg * 16);
-            qh = *(const uint4 *)(row + (size_t)nb * 128 + (size_t)b * 64 + hf * 32 + sg * 16);
-            scv = *(const uint4 *)(row + (size_t)nb * 192 + (size_t)b * 16);
-            dw = h2f(*(const unsigned short *)(row + (size_t)nb * 208 + 2 * b));
-        }
-        const uint32_t A[4] = {qa.x, qa.y, qa.z, qa.w}, B[4] = {qb.x, qb.y, qb.z, qb.w};
-        const uint32_t Hh[4] = {qh.x, qh.y, qh.z, qh.w};
-        int acc_i = 0;
-        if (ok) {
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const int ch = hf * 2 + (q >> 1), l = (2 * q + sg) & 3;
-                const int4 av = *(const int4 *)&s.qp[(size_t)l * (K / 4) + (b * 4 + piece_of_chunk(ch)) * 16];
-                uint32_t code[4];
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const uint32_t src = (q & 1) ? B[j] : A[j];
-                    code[j] = ((src >> (4 * (q >> 1))) & 0x0f0f0f0fu) | (((Hh[j] >> (2 * q)) & 0x03030303u) << 4);
-                }
-                int tq = dp4a((int)code[0], av.x, 0);
-                tq = dp4a((int)code[1], av.y, tq);
-                tq = dp4a((int)code[2], av.z, tq);
-                tq = dp4a((int)code[3], av.w, tq);
-                const int sub = hf * 8 + 2 * q + sg;
-                tq -= 32 * (int)s.bs[b * 16 + sub];
-                acc_i += q6k_subscale(scv, sub) * tq;
-            }
-        }
-        acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 1);
-        acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 2);
-        if (ok && (lane & 3) == 0) acc += dw * s.d[b] * (float)acc_i;
-    }
-    return warp_sum(acc);
+__device__ __forceinline__ uint8_t *head_slot(const MegaArgs &a, uint8_t *smem, int warp, int k) {
+    const int i = warp * kHeadRing + k;
+    const long long rb = a.head.stride;
+    return smem + (i < a.head_n1 ? a.head_reg[0] + (long long)i * rb : a.head_reg[1] + (long long)(i - a.head_n1) * rb);
 }
 
-// One int8 head row (q6k_to_i8 layout) in shared memory against the Q8_K
-// activation held in registers (av, this lane's unit; dact its block's d).
-// Same block integers and float steps as q6k_row_smem / gemv_q6k.
-__device__ __forceinline__ float i8_row_smem(const uint8_t *row, int K, const int4 (&av)[4], float dact, bool ok) {
-    const int lane = threadIdx.x & 31;
+__device__ __forceinline__ void cp_async16_hint(void *dst, const void *src, uint64_t pol) {
+    asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "l"(pol)
+                 : "memory");
+}
+
+// Warp: copy head row `row` (if the warp has it) into slot k and commit one
+// group per lane (empty when there is no row, so every lane's group count
+// stays one per ring step).  Every head byte is read once per step.
+__device__ __forceinline__ void head_row_issue(const MegaArgs &a, uint8_t *smem, int k, int row, int r0, int r1) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    (void)r0;
+    if (row < r1) {
+        const uint64_t pol = l2_policy_evict_first();
+        const uint8_t *src = a.head.w + (size_t)row * a.head.stride;
+        uint8_t *dst = head_slot(a, smem, warp, k);
+        for (int c = lane * 16; c < (int)a.head.stride; c += 32 * 16) cp_async16_hint(dst + c, src + c, pol);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+// This lane's unit of the head activation (K <= 2048: one 64-element unit
+// per lane), kept in registers for every row: the Q8_K codes each of its four
+// 16-element groups meets, their bsums and the block scale.
+struct HeadAct {
+    int4 av[4];
+    int bs[4];
+    float d;
+};
+__device__ __forceinline__ void head_act_load(const Q8Smem &s, int K, HeadAct &h) {
+    const int u = threadIdx.x & 31, b = u >> 2, hf = (u >> 1) & 1, sg = u & 1;
+    const bool ok = u < K / 64;
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        const int ch = hf * 2 + (q >> 1), l = (2 * q + sg) & 3;
+        h.av[q] = ok ? *(const int4 *)&s.qp[(size_t)l * (K / 4) + (b * 4 + piece_of_chunk(ch)) * 16] : make_int4(0, 0, 0, 0);
+        h.bs[q] = ok ? (int)s.bs[b * 16 + hf * 8 + 2 * q + sg] : 0;
+    }
+    h.d = ok ? s.d[b] : 0.f;
+}
+
+// One native Q6_K row in shared memory against the register-held activation:
+// the unit split, integer sums, float steps and warp sum of gemv_q6k (and
+// q6k_row_smem) for K <= 2048, so the logit is the per-layer kernels' own.
+__device__ __forceinline__ float q6k_row_regs(const uint8_t *row, int nb, const HeadAct &h) {
+    const int u = threadIdx.x & 31, b = u >> 2, hf = (u >> 1) & 1, sg = u & 1;
+    const bool ok = u < nb * 4;
     int acc_i = 0;
     float dw = 0.f;
     if (ok) {
-        const uint32_t sc = *(const uint32_t *)(row + K + lane * 4);
-        dw = *(const float *)(row + K + K / 16 + (lane >> 2) * 4);
+        const uint4 qa = *(const uint4 *)(row + (size_t)b * 128 + hf * 64 + sg * 16);
+        const uint4 qb = *(const uint4 *)(row + (size_t)b * 128 + hf * 64 + 32 + sg * 16);
+        const uint4 qh = *(const uint4 *)(row + (size_t)nb * 128 + (size_t)b * 64 + hf * 32 + sg * 16);
+        const uint4 scv = *(const uint4 *)(row + (size_t)nb * 192 + (size_t)b * 16);
+        dw = h2f(*(const unsigned short *)(row + (size_t)nb * 208 + 2 * b));
+        const uint32_t A[4] = {qa.x, qa.y, qa.z, qa.w}, B[4] = {qb.x, qb.y, qb.z, qb.w};
+        const uint32_t Hh[4] = {qh.x, qh.y, qh.z, qh.w};
 #pragma unroll
-        for (int l = 0; l < 4; l++) {
-            const int4 c = *(const int4 *)(row + (size_t)l * (K / 4) + lane * 16);
-            int t = dp4a(c.x, av[l].x, 0);
-            t = dp4a(c.y, av[l].y, t);
-            t = dp4a(c.z, av[l].z, t);
-            t = dp4a(c.w, av[l].w, t);
-            acc_i += (int)(int8_t)(sc >> (8 * l)) * t;
+        for (int q = 0; q < 4; q++) {
+            uint32_t code[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const uint32_t src = (q & 1) ? B[j] : A[j];
+                code[j] = ((src >> (4 * (q >> 1))) & 0x0f0f0f0fu) | (((Hh[j] >> (2 * q)) & 0x03030303u) << 4);
+            }
+            int tq = dp4a((int)code[0], h.av[q].x, 0);
+            tq = dp4a((int)code[1], h.av[q].y, tq);
+            tq = dp4a((int)code[2], h.av[q].z, tq);
+            tq = dp4a((int)code[3], h.av[q].w, tq);
+            tq -= 32 * h.bs[q];
+            acc_i += q6k_subscale(scv, hf * 8 + 2 * q + sg) * tq;
         }
     }
     acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 1);
     acc_i += __shfl_xor_sync(0xffffffffu, acc_i, 2);
     float acc = 0.f;
-    if (ok && (lane & 3) == 0) acc += dw * dact * (float)acc_i;
+    if (ok && (u & 3) == 0) acc += dw * h.d * (float)acc_i;
     return warp_sum(acc);
-}
-
-// Thread 0: arm ring stage `si % ns` and copy rows [r0 + si*kHeadRows, ...)
-// of this CTA's head slice into it.
-__device__ __forceinline__ void head_fill(const MegaArgs &a, uint8_t *smem, uint64_t *hbar, int si, int r0, int r1) {
-    const int k = si % a.head_ns, row = r0 + si * kHeadRows, n = min(kHeadRows, r1 - row);
-    const unsigned bytes = (unsigned)n * (unsigned)a.head_i8_stride;
-    mbar_expect(&hbar[k], bytes);
-    const uint64_t pol = si * kHeadRows < a.head_keep ? l2_policy_evict_last() : l2_policy_evict_first();
-    bulk_g2s_hint(smem + a.head_off[k], a.head_i8 + (size_t)row * a.head_i8_stride, bytes, &hbar[k], pol);
 }
 
 // ---------------------------------------------------------------- the kernel
@@ -547,7 +547,6 @@ template <int HD, int G, int CF>
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_constant__ MegaArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ __align__(8) uint64_t mbar[4];  // weight slots
-    __shared__ __align__(8) uint64_t hbar[4];  // LM-head ring stages
     __shared__ int s_flag;
     __shared__ unsigned long long s_best[kMegaWarps];
     __shared__ __align__(16) float sq[G][HD];
@@ -565,13 +564,11 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     if (tid == 0) {
         for (int i = 0; i < 4; i++) {
             mbar_init(&mbar[i]);
-            mbar_init(&hbar[i]);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncthreads();
     unsigned ph[4] = {0, 0, 0, 0};  // parity each mbarrier completes next
-    unsigned hph[4] = {0, 0, 0, 0}, hpend = 0;  // head ring: parities, stages in flight
     unsigned pending = 0;              // bit i: a fill of mbarrier i is outstanding (same in every thread)
     unsigned target = 0;
     int tli = 0, tls = 0;
@@ -587,7 +584,6 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     const auto j0_of = [&](int p) { return achunk * cs_of(p); };
     const auto ncache_of = [&](int p) { return max(0, min(p, j0_of(p) + cs_of(p)) - j0_of(p)); };
     const int hr0 = blockIdx.x * a.rpc[4], hr1 = min(hr0 + a.rpc[4], a.head.n);
-    const int hst = hr1 > hr0 ? (hr1 - hr0 + kHeadRows - 1) / kHeadRows : 0;  // head ring stages per step
     // prime: layer 0's weight slots and K/V rows, the first norm weights
     if (tid == 0)
         for (int t = 0; t < 4; t++) mega_fill(a, tab, smem, &mbar[t], t, 0);
@@ -644,10 +640,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 float *qkv = a.qkv;
                 if (ok)
                     mega_rows<1, RGQ, false>(a.shift, a.off, r0, r1, rpc, sw, ss, a.H, act, dblk, sblk,
-                                             [&](int rg, const float *acc, int rend) {
+                                             [&](int rg, const float *acc, int rend, int sel) {
 #pragma unroll
                                                  for (int g = 0; g < RGQ; g++)
-                                                     if (rg + g < rend) qkv[rg + g] = acc[g];
+                                                     if (g == sel && rg + g < rend) qkv[rg + g] = acc[g];
                                              });
                 tl_sub(a, tls);
             }
@@ -678,7 +674,22 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 tl_sub(a, tls);
                 if (ok) {
                     const auto krow = [&](int j, int c) { return (const uint4 *)(sK + (size_t)j * KROW + c * 16); };
+#ifdef HYK_TRACE
+                    // attention sub-marks of block 0, layer 5 of step 1: [cap/2 + 7000 ..)
+                    int am = 0;
+                    const auto mark = [&]() {
+                        if (a.tl && blockIdx.x == 0 && threadIdx.x == 0 && step == 1 && l == 5)
+                            a.tl[a.tl_cap / 2 + 7000 + am] = gtimer();
+                        am++;
+                    };
+                    if (a.tl && blockIdx.x == 0 && threadIdx.x == 0 && step == 1 && l == 5)
+                        a.tl[a.tl_cap / 2 + 7010] = gtimer();
+                    attn_chunk_main<HD, G>(aa, akvh, achunk, cs_of(pos), pos, krow, sV, sq, skc, svc, S, 1, mark);
+                    if (a.tl && blockIdx.x == 0 && threadIdx.x == 0 && step == 1 && l == 5)
+                        a.tl[a.tl_cap / 2 + 7011] = gtimer();
+#else
                     attn_chunk_main<HD, G>(aa, akvh, achunk, cs_of(pos), pos, krow, sV, sq, skc, svc, S, 1);
+#endif
                 }
                 tl_sub(a, tls);
             }
@@ -709,10 +720,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 float *h = a.h;
                 if (ok)
                     mega_rows<1, RGO, false>(a.shift, a.off, r0, r1, rpc, sw, ss, a.qd, act, dblk, sblk,
-                                             [&](int rg, const float *acc, int rend) {
+                                             [&](int rg, const float *acc, int rend, int sel) {
 #pragma unroll
                                                  for (int g = 0; g < RGO; g++)
-                                                     if (rg + g < rend) h[rg + g] += acc[g];
+                                                     if (g == sel && rg + g < rend) h[rg + g] += acc[g];
                                              });
                 tl_sub(a, tls);
             }
@@ -757,10 +768,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 float *out = a.act;
                 if (ok)
                     mega_rows<1, RGU, true>(a.shift, a.off, r0, r1, rpc, sw, ss, a.H, act, dblk, sblk,
-                                            [&](int rg, const float *acc, int rend) {
+                                            [&](int rg, const float *acc, int rend, int sel) {
 #pragma unroll
                                                 for (int g = 0; g + 1 < RGU; g += 2) {
-                                                    if (rg + g + 1 >= rend) break;
+                                                    if (g != 2 * sel || rg + g + 1 >= rend) continue;
                                                     const float gt = acc[g], up = acc[g + 1];
                                                     out[(rg + g) >> 1] = __fmul_rn(gt / (1.0f + expf(-gt)), up);
                                                 }
@@ -801,10 +812,10 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 float *h = a.h;
                 if (ok)
                     mega_rows<CF, RGD, false>(a.shift, a.off, r0, r1, rpc, sw, ss, a.F, act, dblk, sblk,
-                                              [&](int rg, const float *acc, int rend) {
+                                              [&](int rg, const float *acc, int rend, int sel) {
 #pragma unroll
                                                   for (int g = 0; g < RGD; g++)
-                                                      if (rg + g < rend) h[rg + g] += acc[g];
+                                                      if (g == sel && rg + g < rend) h[rg + g] += acc[g];
                                               });
                 tl_sub(a, tls);
             }
@@ -819,12 +830,9 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
                 pending |= 8u;
             }
             if (l + 1 == a.L && ok) {
-                // o_proj, gate|up and down slots and the K/V area are free: start the LM-head ring
-                if (tid == 0) {
-                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                    for (int k = 0; k < a.head_ns && k < hst; k++) head_fill(a, smem, hbar, k, hr0, hr1);
-                }
-                for (int k = 0; k < a.head_ns && k < hst; k++) hpend |= 1u << k;
+                // o_proj, gate|up and down slots and the K/V area are free: start every warp's
+                // LM-head ring (no copy of this step's K/V rows is pending: the last layer stages none)
+                for (int k = 0; k < kHeadRing; k++) head_row_issue(a, smem, k, hr0 + warp + k * kMegaWarps, hr0, hr1);
             }
             norm_preload(l + 1 < a.L ? tab[l + 1].attn_norm : a.out_norm, a.H, npre);
             if (!bar_wait(a, target, &s_flag)) { ok = false; break; }
@@ -832,45 +840,30 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             tl_mark(a, tli);
         }
         if (!ok) break;
-        // ---- LM head + argmax (rows < vocab_out compete), rows streamed through the ring
+        // ---- LM head + argmax (rows < vocab_out compete), rows streamed through the warp rings
         {
             mega_stage_norm(a.h, npre, a.eps, a.H, st);
-            // this lane's unit of the activation, kept in registers for every row
-            const bool uok = lane < a.H / 64;
-            int4 hav[4];
-#pragma unroll
-            for (int l = 0; l < 4; l++)
-                hav[l] = uok ? *(const int4 *)&st.qp[(size_t)l * (a.H / 4) + lane * 16] : make_int4(0, 0, 0, 0);
-            const float hd = uok ? st.d[lane >> 2] : 0.f;
+            tl_sub(a, tls);
+            HeadAct hact;
+            head_act_load(st, a.H, hact);
+            const int nb = a.H / 256;
             unsigned long long best = 0;
-            for (int si = 0; si < hst && ok; si++) {
-                const int k = si % a.head_ns;
-                const bool ready = __syncthreads_and(mbar_wait(&hbar[k], hph[k]));
-                if (ready) {
-                    hph[k] ^= 1;
-                    hpend &= ~(1u << k);
-                } else {
-                    if (tid == 0) raise_err(a, MEGA_ERR_WEIGHTS);
-                    ok = false;
-                    break;
+            int j = 0;
+            for (int row = hr0 + warp; row < hr1; row += kMegaWarps, j++) {
+                const int k = j % kHeadRing;
+                // the oldest of this lane's kHeadRing groups (row j) has landed; then every lane's
+                asm volatile("cp.async.wait_group %0;" ::"n"(kHeadRing - 1) : "memory");
+                __syncwarp();
+                const float v = q6k_row_regs(head_slot(a, smem, warp, k), nb, hact);
+                if (lane == 0 && row < a.vocab_out) {
+                    const unsigned long long key = argmax_key(v, (uint32_t)row);
+                    if (key > best) best = key;
                 }
-                const int r = hr0 + si * kHeadRows + warp;
-                if (r < hr1) {
-                    const float v = i8_row_smem(smem + a.head_off[k] + (size_t)warp * a.head_i8_stride, a.H, hav, hd, uok);
-                    if (lane == 0 && r < a.vocab_out) {
-                        const unsigned long long key = argmax_key(v, (uint32_t)r);
-                        if (key > best) best = key;
-                    }
-                }
-                __syncthreads();  // stage k consumed
-                if (si + a.head_ns < hst) {
-                    if (tid == 0) {
-                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                        head_fill(a, smem, hbar, si + a.head_ns, hr0, hr1);
-                    }
-                    hpend |= 1u << k;
-                }
+                __syncwarp();  // slot k consumed by every lane
+                head_row_issue(a, smem, k, row + kHeadRing * kMegaWarps, hr0, hr1);
             }
+            asm volatile("cp.async.wait_all;" ::: "memory");
+            tl_sub(a, tls);
             if (lane == 0) s_best[warp] = best;
             __syncthreads();
             if (tid == 0) {
@@ -919,10 +912,8 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     }
     // copies still in flight into this CTA's shared memory (error exits)
     if (tid == 0)
-        for (int i = 0; i < 4; i++) {
+        for (int i = 0; i < 4; i++)
             if (pending & (1u << i)) mbar_wait(&mbar[i], ph[i]);
-            if (hpend & (1u << i)) mbar_wait(&hbar[i], hph[i]);
-        }
     asm volatile("cp.async.wait_all;" ::: "memory");
     __syncthreads();
 }
@@ -930,7 +921,7 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
 // Dynamic shared memory plan of decode_mega for a model shape.
 struct MegaPlan {
     int rpc[5], slot_off[4], stage_off, attn_off, kmax;
-    int head_ns, head_off[4];  // LM-head ring: stages placed in the o_proj, gate|up, down slots and the K/V area
+    int head_reg[2], head_n1;  // LM-head row slots: in the o_proj, gate|up, down slots, then the K/V area
     size_t bytes;
 };
 
@@ -954,19 +945,22 @@ inline MegaPlan mega_plan(int grid, int H, int F, int qd, int kvd, int vocab, in
     p.attn_off = (int)off;
     off += (size_t)kDecSplit * (HD * 2 + kMegaKPad) + (size_t)kDecSplit * HD * 2;
     p.bytes = off;
-    p.head_ns = 0;
+    p.head_n1 = 0;
     return p;
 }
 
-// Place up to four head-ring stages of kHeadRows rows of `head_stride` bytes
-// in regions that are idle while the head runs; false if fewer than two fit.
+// Place the kHeadRing row slots of every warp (rows of `head_stride` bytes, a
+// multiple of 16) in the regions that are idle while the head runs: the
+// o_proj, gate|up and down weight slots, then the K/V area.  False if they
+// do not fit.
 inline bool mega_head_ring(MegaPlan &p, long long head_stride) {
-    const size_t sb = (size_t)kHeadRows * (size_t)head_stride;
-    p.head_ns = 0;
-    for (size_t o = (size_t)p.slot_off[1]; o + sb <= (size_t)p.stage_off && p.head_ns < 4; o += sb)
-        p.head_off[p.head_ns++] = (int)o;
-    for (size_t o = (size_t)p.attn_off; o + sb <= p.bytes && p.head_ns < 4; o += sb) p.head_off[p.head_ns++] = (int)o;
-    return p.head_ns >= 2;
+    if (head_stride <= 0 || head_stride % 16) return false;
+    const long long n1 = ((long long)p.stage_off - p.slot_off[1]) / head_stride;
+    const long long n2 = ((long long)p.bytes - p.attn_off) / head_stride;
+    p.head_reg[0] = p.slot_off[1];
+    p.head_reg[1] = p.attn_off;
+    p.head_n1 = (int)n1;
+    return n1 + n2 >= (long long)kMegaWarps * kHeadRing;
 }
 
 }  // namespace hyk

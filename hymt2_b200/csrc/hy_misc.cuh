@@ -75,40 +75,6 @@ __global__ void q80_relayout(const uint8_t *raw, int n, int nblk, uint8_t *dst, 
     row[(size_t)nblk * 32 + 2 * b + 1] = blk[1];
 }
 
-// Q6_K head (device relayout above) -> int8 rows for the persistent decode
-// kernel's LM head, laid out like the Q8_K activation stage: codes (q - 32)
-// as int8 in planes, w[l*(k/4) + u*16 + j] = element b*256 + c*64 + l*16 + j
-// for unit u = 4b + p and natural chunk c = piece_of_chunk(p); then the
-// sub-scales by unit, s[u*4 + l] (sub-block b*16 + c*4 + l); then each
-// block's d as fp32.  The per-block integer sums are exactly the Q6_K GEMV's
-// and a lane reads its unit's 16-byte pieces without bank conflicts.  One
-// thread per (row, 16-element group).
-__host__ __device__ inline long long head_i8_stride(int k) {
-    return (long long)((k + k / 16 + (k / 256) * 4 + 15) & ~15);
-}
-__global__ void q6k_to_i8(const __grid_constant__ WDesc w, uint8_t *dst, long long dstride) {
-    const int ng = w.k / 16;
-    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (long long)w.n * ng) return;
-    const int r = (int)(i / ng), g = (int)(i % ng), nb = w.k / 256, b = g >> 4;
-    const int c = (g & 15) >> 2, l = g & 3, u = b * 4 + piece_of_chunk(c);
-    const uint8_t *row = w.w + (size_t)r * w.stride;
-    uint8_t *out = dst + (size_t)r * dstride;
-    for (int j = 0; j < 16; j++) {
-        const int x = ((g & 15) << 4) + j;  // element within the block
-        const int half = x >> 7, q = (x & 127) >> 5, li = x & 31;
-        const uint8_t lb = row[(size_t)b * 128 + half * 64 + li + (q & 1) * 32];
-        const int lo = (q & 2) ? (lb >> 4) : (lb & 15);
-        const int hi = (row[(size_t)nb * 128 + (size_t)b * 64 + half * 32 + li] >> (2 * q)) & 3;
-        out[(size_t)l * (w.k / 4) + (size_t)u * 16 + j] = (uint8_t)(int8_t)((lo | (hi << 4)) - 32);
-    }
-    out[w.k + (size_t)u * 4 + l] = row[(size_t)nb * 192 + (size_t)g];  // sub-scale of elements g*16 ..
-    if ((g & 15) == 0) {
-        const float d = h2f((uint16_t)(row[(size_t)nb * 208 + 2 * b] | (row[(size_t)nb * 208 + 2 * b + 1] << 8)));
-        *(float *)(out + w.k + ng + (size_t)b * 4) = d;
-    }
-}
-
 // ---------------------------------------------------------------- dequantisation (embedding rows)
 
 // Element e of row r of a device weight, as fp32 (reference dequant_row,
