@@ -34,6 +34,7 @@ data path); the process group only carries the barrier and the max-time.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import datetime
 import json
 import os
@@ -294,7 +295,7 @@ def serve_requests(n: int) -> list[list[int]]:
     return out
 
 
-def bench_serving(dm, stream, torch, rank, world, nreq, max_over_ranks, barrier) -> dict:
+def bench_serving(dm, stream, torch, rank, world, nreq, max_over_ranks, barrier, tops=None, tops_kind="") -> dict:
     """Config 3 on this rank's shard (requests r, r + N, ...): continuous
     batching over 256 slots, 64 greedy tokens per request, device-timed
     around the whole serve call (host scheduling included)."""
@@ -312,7 +313,17 @@ def bench_serving(dm, stream, torch, rank, world, nreq, max_over_ranks, barrier)
     wall = time.perf_counter() - t0
     ms = max_over_ranks(e0.elapsed_time(e1))
     total_gen = SERVE_MAX_NEW * nreq
+    # useful int8 ops of this rank's run: every token (prefill or decode) through the layers, the head on each
+    # generated token; the pass runs on the tensor cores (tcgen05 int8, >= 32 tokens per GEMM)
+    ops = INT8_OPS_PER_TOKEN * (st["decode_tokens"] + st["prefill_tokens"]) + HEAD_OPS_PER_SEQ * st["decode_tokens"]
+    roof = None
+    if tops:
+        achieved = ops / (ms / 1e3) / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(tops, 1),
+                "unit": "TOPS (int8, useful ops, rank 0's share over the max-over-ranks time)",
+                "frac": round(achieved / tops, 4), "peak_kind": tops_kind, "ops_rank0": int(ops)}
     return {"value": round(total_gen / (ms / 1e3), 1), "unit": "generated tok/s", "n_gpus": world,
+            "roofline": roof,
             "requests": nreq, "requests_per_gpu": len(reqs), "max_new": SERVE_MAX_NEW, "slots_per_gpu": SERVE_SLOTS,
             "step_token_budget": SERVE_STEP_TOKENS, "ms": round(ms, 2), "wall_s_rank0": round(wall, 3),
             "steps_rank0": st["steps"], "prefill_tokens_rank0": st["prefill_tokens"],
@@ -501,13 +512,112 @@ def bench_c4(args, be, torch, peak) -> dict:
                "roofline_step": {"bytes_per_step": int(step_bytes),
                                  "achieved_gbs": round(step_bytes / step_ms / 1e6, 1),
                                  "frac": round(step_bytes / step_ms / 1e6 / peak, 4)},
-               "cpu_baseline": {"unavailable": "the reference's Q8_0 rows are scalar fp32 on the CPU; a 4096-token "
-                                               "prefill there is far beyond this bench's time budget"}}
+               }
         if path_why:
             out["decode_path"] = path_why
+        if not args.no_cpu_baseline:
+            out["cpu_baseline"] = c4_cpu_baseline(path)
         return out
     finally:
         dm.close()
+
+
+def c4_cpu_baseline(path: str) -> dict:
+    """The reference's CPU decode of the config-4 model (scalar fp32 Q8_0
+    rows, src/kernels.c:1097-1107) on all host cores.  Its prefill runs at
+    ~0.3 s per token on 8 cores, so a 4096-token prompt would take tens of
+    minutes: the sample is a 64-token prompt, then 4 decode tokens at KV
+    64..67.  Attention over 4096 keys adds ~0.5 G multiply-adds per token to
+    the ~1.9 G of the weights, so decode at KV 4096 is slower still."""
+    try:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        os.environ["HYMT2_DEVICE"] = "cpu"
+        ref = O.Reference()
+        cores = int(ref.lib.refh_physical_cores())
+        m = ref.load(path, threads=cores, ctx=128)
+        ids = np.random.default_rng(1).integers(0, VOCAB, 64).tolist()
+        _, _, pre_ms, dec_ms, _ = m.greedy(ids, 5)
+        thr = m.threads()
+        m.close()
+        return {"value": round(4 / (dec_ms / 1e3), 3), "unit": UNIT, "cores": thr, "kind": "reference",
+                "sample": f"reference CPU ({ref.isa()}, {thr} threads): 64-token prompt ({pre_ms:.0f} ms), then 4 "
+                          f"decode tokens at KV 64..67 (a 4096-token prefill is beyond the bench budget; KV 4096 "
+                          f"decode is slower than this)"}
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": str(e)}
+
+
+def bench_c4_tp(args, be, torch, dist, rank, world, max_over_ranks) -> dict:
+    """Config 4 as specified: the Q8_0 model split over the N GPUs
+    (tensor parallelism: heads and FFN columns per rank, o_proj / down
+    row-parallel with the partial products summed by the backend's one-shot
+    push over NVLink peer memory, vocabulary-split head).  Every rank prefills
+    the 4096-token seeded prompt, then 63 greedy decode steps are timed with
+    CUDA events on each rank's stream; the per-token latency is the max over
+    ranks.  For comparison, the latency of one NCCL all-reduce of the same
+    8 KB (2048 fp32, the exchange after o_proj and after down) is timed too."""
+    from hymt2_b200 import synth
+    from hymt2_b200.tp import TPDeviceModel
+    if rank == 0:
+        path = synth.ensure("c4_q8_0", args.model_dir)
+        dist.barrier()
+    else:
+        dist.barrier()
+        path = synth.ensure("c4_q8_0", args.model_dir)
+
+    def allgather(b):
+        out = [None] * world
+        dist.all_gather_object(out, b)
+        return out
+
+    tm = TPDeviceModel(path, be, rank, world, allgather, ctx=C4_PROMPT + C4_GEN + 64)
+    try:
+        lib, impl = be.lib, be.impl
+        ids = np.random.default_rng(1).integers(0, VOCAB, C4_PROMPT).astype(np.int32)
+        stream = torch.cuda.ExternalStream(be.stream())
+        ms = None
+        for _ in range(2):
+            if lib.hyc_decode_begin(impl, ids.ctypes.data, C4_PROMPT, 0, C4_GEN, None, 0, tm.vocab_out) != 0:
+                raise RuntimeError("decode_begin: " + be.error())
+            be.sync()
+            dist.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            if lib.hyc_decode_steps(impl, C4_GEN - 1) != 0:
+                raise RuntimeError("decode_steps: " + be.error())
+            e1.record(stream)
+            torch.cuda.synchronize()
+            be.sync()
+            ms = max_over_ranks(e0.elapsed_time(e1))
+        out_ids = np.zeros(C4_GEN, dtype=np.int32)
+        n = lib.hyc_decode_read(impl, out_ids.ctypes.data, C4_GEN)
+        if n != C4_GEN:
+            raise RuntimeError("decode_read: " + be.error())
+        dist.barrier()  # every rank done with its peers' memory before any unmaps
+    finally:
+        tm.close()
+    # the NCCL reference point: an all-reduce of 2048 fp32 (CUDA events, 200 iterations after warm-up)
+    x = torch.zeros(2048, dtype=torch.float32, device="cuda")
+    for _ in range(20):
+        dist.all_reduce(x)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(200):
+        dist.all_reduce(x)
+    b.record()
+    torch.cuda.synchronize()
+    nccl_us = max_over_ranks(a.elapsed_time(b) / 200 * 1e3)
+    step_ms = ms / (C4_GEN - 1)
+    per_rank_bytes = (C4_LAYER_BYTES + C4_HEAD_BYTES) / world + L * 2 * (C4_PROMPT + (C4_GEN - 1) / 2) * KVD * 2 / min(world, 4)
+    return {"value": round((C4_GEN - 1) / (ms / 1e3), 1), "unit": "tok/s", "ms_per_token": round(step_ms, 4),
+            "tp": world, "exchanges_per_token": 2 * L + 1, "nccl_allreduce_8kb_us": round(nccl_us, 2),
+            "workload": "c4_q8_0 tensor-parallel over the GPUs: bs1 greedy decode after a 4096-token seeded prompt, "
+                        "positions 4096..4159; per-token latency = max over ranks (CUDA events)",
+            "roofline_step": {"bytes_per_rank_per_step": int(per_rank_bytes),
+                              "achieved_gbs_per_rank": round(per_rank_bytes / step_ms / 1e6, 1)},
+            "ids_head": out_ids[:8].tolist()}
 
 
 def quant_gemv_entry(kernels, peak):
@@ -634,13 +744,28 @@ def main():
     clk = clocks.stop()
     ms = max_over_ranks(e0.elapsed_time(e1))
 
-    # ---- end to end: every step's token through pinned host memory, wall clock
-    host = lib.hyc_host_alloc(4 * (GEN_LEN + 1))
-    run_steps(max(3, args.warmup), host)
+    # ---- end to end with the host in the loop, as the reference's loop runs (src/model.c:943-954): every
+    # step the host's token goes in from pinned memory, one decode step runs, the new token comes back, and the
+    # host waits for it, reads it and checks it against the stop ids before it issues the next step
+    host = lib.hyc_host_alloc(4 * 2)
+    hp = ctypes.cast(host, ctypes.POINTER(ctypes.c_int))
+    stop_ids = {-1}  # no id stops the benchmark stream; the membership test is the host loop's own work
+
+    def host_loop(n):
+        s = 0
+        while s < n:
+            check(lib.hyc_decode_rewind(impl, PROMPT_LEN, tok0), "rewind")
+            for _ in range(min(GEN_LEN, n - s)):
+                check(lib.hyc_decode_steps_host(impl, 1, host), "steps_host")
+                check(lib.hyc_sync(impl), "sync")
+                if hp[1] in stop_ids:
+                    break
+                s += 1
+
+    host_loop(max(3, args.warmup))
     barrier()
     t0 = time.perf_counter()
-    run_steps(args.steps, host)
-    be.sync()
+    host_loop(args.steps)
     e2e_s = max_over_ranks(time.perf_counter() - t0)
     lib.hyc_host_free(host)
 
@@ -698,7 +823,9 @@ def main():
     # ---- config 3: continuous-batching serving on every GPU (bs256/GPU)
     serving = None
     if args.serve_requests > 0:
-        serving = bench_serving(dm, stream, torch, rank, world, args.serve_requests, max_over_ranks, barrier)
+        stops, stops_kind = int8_peak(torch)
+        serving = bench_serving(dm, stream, torch, rank, world, args.serve_requests, max_over_ranks, barrier,
+                                stops, stops_kind)
 
     if rank == 0:
         step_ms = ms / args.steps
@@ -713,8 +840,9 @@ def main():
                        "l2": "weights 613 MB per step > 126 MB L2 (no flush needed)"},
             "e2e": {"value": round(world * args.steps / e2e_s, 2), "unit": UNIT, "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": 4,
-                    "path": f"hyc_decode_steps_host: token in from pinned host, one decode step ({path_name}), "
-                            f"token out to pinned host"},
+                    "path": f"host loop through the C ABI: hyc_decode_steps_host(1) (token in from pinned host, one "
+                            f"decode step ({path_name}), token out), hyc_sync, the host reads the token and checks "
+                            f"the stop ids; wall clock, max over ranks"},
             "decode_path": path_name,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
                          "frac": round(dk["gbs"] / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
@@ -737,6 +865,13 @@ def main():
                                             "cpu_baseline above")
             out["serving"] = serving
     dm.close()
+    if world > 1 and not args.no_extra:
+        try:
+            c4tp = bench_c4_tp(args, be, torch, dist, rank, world, max_over_ranks)
+        except Exception as e:  # noqa: BLE001 - report, do not lose the headline
+            c4tp = {"unavailable": str(e)}
+        if rank == 0:
+            out["decode_c4_tp"] = c4tp
     if rank == 0 and world == 1 and not args.no_extra:
         tops, tops_kind = int8_peak(torch)
         for key, fn in (("prefill_c2", lambda: bench_prefill(args, be, torch, tops, tops_kind)),

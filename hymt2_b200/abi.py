@@ -96,6 +96,8 @@ SIGNATURES = {
     "hyc_quantize_q8k": (I, [P, P, I, I, P]),
     "hyc_block_ints": (I, [P, P, P, I, P]),
     "hyc_tc_block_ints": (I, [P, P, P, I, P]),
+    "hyc_tp_init": (I, [P, I, I, I, P]),
+    "hyc_tp_connect": (I, [P, P]),
     "hyc_dequant_row": (I, [P, P, I, P]),
     "hyc_matmul_f32": (I, [P, P, P, I, P]),
     "hyc_kv_read": (I, [P, I, I, P, P]),

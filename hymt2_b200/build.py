@@ -87,21 +87,22 @@ def build_synth(force: bool = False) -> None:
 
 
 def build_oracle(reference: str | None = None) -> None:
-    """Test-only checkers under oracle/ (see oracle/Makefile)."""
+    """Test-only checkers under oracle/ (see oracle/Makefile): always the C
+    restatement; the reference's own CPU library and the drop-in link only
+    when `reference` names a checkout of the reference (its src/)."""
     odir = os.path.join(_paths.ROOT, "oracle")
-    ref = reference or os.environ.get("HYMT2_REFERENCE", "/root/reference")
     env_cc = "CC=" + _cc()
     _run(["make", "-s", env_cc, "orc"], cwd=odir)
-    if os.path.isdir(os.path.join(ref, "src")):
-        _run(["make", "-s", env_cc, "REF=" + ref, "ref"], cwd=odir)
+    if reference and os.path.isdir(os.path.join(reference, "src")):
+        _run(["make", "-s", env_cc, "REF=" + reference, "ref"], cwd=odir)
         if os.path.exists(_paths.BACKEND_ARCHIVE):
-            _run(["make", "-s", env_cc, "REF=" + ref, "dropin"], cwd=odir)
+            _run(["make", "-s", env_cc, "REF=" + reference, "dropin"], cwd=odir)
 
 
-def build_all(force: bool = False) -> None:
+def build_all(force: bool = False, reference: str | None = None) -> None:
     build_synth(force)
     build_backend(force)
-    build_oracle()
+    build_oracle(reference)
 
 
 if __name__ == "__main__":
@@ -109,5 +110,5 @@ if __name__ == "__main__":
         build_backend(force="--force" in sys.argv, trace=True)
         print("built:", _paths.TRACE_LIB)
         sys.exit(0)
-    build_all(force="--force" in sys.argv)
+    build_all(force="--force" in sys.argv, reference=os.environ.get("HYMT2_REFERENCE"))
     print("built:", _paths.BACKEND_LIB, _paths.BACKEND_ARCHIVE, _paths.SYNTH_LIB)

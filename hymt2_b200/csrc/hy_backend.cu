@@ -584,6 +584,18 @@ bool tc_status(HyCtx *c) {
     return false;
 }
 
+// Tensor-parallel exchanges report a timed-out wait through their error word.
+bool tp_status(HyCtx *c) {
+    if (!c->d_tp_err) return true;
+    int err = 0;
+    CK(c, cudaMemcpyAsync(&err, c->d_tp_err, 4, cudaMemcpyDeviceToHost, c->st));
+    CK(c, cudaStreamSynchronize(c->st));
+    if (!err) return true;
+    c->broken = true;
+    snprintf(c->err, sizeof c->err, "tensor-parallel exchange: a wait for a peer timed out");
+    return false;
+}
+
 // ---------------------------------------------------------------- fused layer loop
 
 template <int HD, int G>
@@ -920,6 +932,7 @@ bool mega_check(HyCtx *c) {
         return false;
     };
     if (!c->fused || !c->outw || !c->embd) return no("model not prepared");
+    if (c->tp_world > 1) return no("tensor-parallel rank (the per-layer graph carries the exchanges)");
     const int G = c->heads / c->kvh;
     int CF = (c->F + 2047) / 2048;
     if (CF == 2) CF = 3;
@@ -1151,10 +1164,27 @@ void free_fused(HyCtx *c) {
     c->mega_state = -1;
 }
 
+void tp_free(HyCtx *c) {
+    for (int q = 0; q < c->tp_world && q < kTpMax; q++)
+        if (q != c->tp_rank && c->tp.area[q]) cudaIpcCloseMemHandle(c->tp.area[q]);
+    if (c->d_tp_area) cudaFree(c->d_tp_area);
+    if (c->d_tp_part) cudaFree(c->d_tp_part);
+    if (c->d_tp_err) cudaFree(c->d_tp_err);
+    c->d_tp_area = nullptr;
+    c->d_tp_part = nullptr;
+    c->d_tp_err = nullptr;
+    memset(&c->tp, 0, sizeof c->tp);
+    c->tp_on = false;
+    c->tp_world = 1;
+    c->tp_rank = 0;
+    c->tp_vocab0 = 0;
+}
+
 void destroy_impl(void *impl) {
     HyCtx *c = (HyCtx *)impl;
     if (!c) return;
     cudaSetDevice(c->dev);
+    tp_free(c);
     free_fused(c);
     if (c->d_xq) cudaFree(c->d_xq);
     if (c->d_x32) cudaFree(c->d_x32);
@@ -1453,6 +1483,7 @@ bool fused_forward(void *impl, hy_fused_args *a) {
     if (!c || c->broken || !c->fused || !a || !a->h || a->nt < 1 || a->nt > kMaxChunk) return false;
     if (a->pos0 < 0 || a->pos0 + a->nt > c->ctx) return false;
     if (a->want_logits && (!c->outw || !a->logits)) return false;
+    REQ(c, c->tp_world == 1, "fused_forward: a tensor-parallel rank holds only a slice of the logits");
     if (cudaSetDevice(c->dev) != cudaSuccess) return false;
     const int nt = a->nt;
     for (int i = 0; i < c->L; i++) {  // the host may pass a fresh layer array; handles must match
@@ -1603,7 +1634,7 @@ HYC_API int hyc_sync(void *impl) {
         fail(c, "cudaStreamSynchronize", e);
         return -1;
     }
-    return mega_status(c) && tc_status(c) ? 0 : -1;
+    return mega_status(c) && tc_status(c) && tp_status(c) ? 0 : -1;
 }
 
 HYC_API int hyc_set_embedding(void *impl, hy_dweight *embd) {
@@ -1707,7 +1738,7 @@ HYC_API int hyc_tc_block_ints(void *impl, hy_dweight *hw, const q8k_block *xq, i
 
 HYC_API int hyc_batch_prepare(void *impl, int slots, int slot_ctx, int max_tokens, int max_out) {
     HyCtx *c = (HyCtx *)impl;
-    if (!c || c->broken || cudaSetDevice(c->dev) != cudaSuccess) return -1;
+    if (!c || c->broken || c->tp_world > 1 || cudaSetDevice(c->dev) != cudaSuccess) return -1;
     return batch_prepare(c, slots, slot_ctx, max_tokens, max_out) ? 0 : -1;
 }
 
@@ -1831,7 +1862,9 @@ HYC_API int hyc_decode_begin(void *impl, const int *prompt, int n, int keep, int
     if (!c || c->broken || !c->fused || !c->embd || !c->outw || !prompt) return -1;
     if (n < 1 || keep < 0 || keep >= n || max_new < 1 || n + max_new > c->ctx || n_stop < 0 || n_stop > 16) return -1;
     if (cudaSetDevice(c->dev) != cudaSuccess) return -1;
-    c->vocab_out = (vocab_out > 0 && vocab_out <= c->outw->n) ? vocab_out : c->outw->n;
+    // rows below vocab_out (of the whole vocabulary: a tensor-parallel rank's head holds rows tp_vocab0 ..)
+    // compete for the argmax
+    c->vocab_out = vocab_out > 0 ? vocab_out : c->outw->n + c->tp_vocab0;
     DecodeState s;
     memset(&s, 0, sizeof s);
     s.pos = n - 1;
@@ -1889,7 +1922,7 @@ HYC_API int hyc_decode_steps_host(void *impl, int steps, int *tok_io) {
 HYC_API int hyc_decode_read(void *impl, int *out_ids, int cap) {
     HyCtx *c = (HyCtx *)impl;
     if (!c || c->broken || !c->fused) return -1;
-    if (!mega_status(c) || !tc_status(c)) return -1;
+    if (!mega_status(c) || !tc_status(c) || !tp_status(c)) return -1;
     DecodeState s;
     if (cudaMemcpyAsync(&s, c->d_state, sizeof s, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
         cudaStreamSynchronize(c->st) != cudaSuccess) {
@@ -2343,6 +2376,84 @@ HYC_API int hyc_mega_timeline(void *impl, unsigned long long *out, int cap) {
     (void)cap;
     return -1;  // this library was built without the timeline (HYK_TRACE)
 #endif
+}
+
+// ---------------------------------------------------------------- tensor parallelism
+
+// This handle holds rank `rank` of `world` of a tensor-parallel split (its
+// fused_prepare shape is the rank's share: heads, KV heads and FFN columns
+// per rank; o_proj and down with the rank's K columns; the head with
+// vocabulary rows vocab0 ..).  Allocates and zeroes the exchange area and
+// writes its CUDA IPC handle (64 bytes) to handle_out.
+HYC_API int hyc_tp_init(void *impl, int rank, int world, int vocab0, unsigned char *handle_out) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->fused || !handle_out || world < 1 || world > kTpMax || rank < 0 || rank >= world ||
+        vocab0 < 0)
+        return -1;
+    if (cudaSetDevice(c->dev) != cudaSuccess) return -1;
+    tp_free(c);
+    c->tp_cap = (long long)kMaxChunk * c->H;
+    const TpLayout L = tp_layout(c->tp_cap);
+    cudaIpcMemHandle_t hdl;
+    const bool ok = cudaMalloc(&c->d_tp_area, L.bytes) == cudaSuccess &&
+                    cudaMalloc(&c->d_tp_part, (size_t)c->tp_cap * 4) == cudaSuccess &&
+                    cudaMalloc(&c->d_tp_err, 4) == cudaSuccess &&
+                    cudaMemsetAsync(c->d_tp_area, 0, L.bytes, c->st) == cudaSuccess &&
+                    cudaMemsetAsync(c->d_tp_err, 0, 4, c->st) == cudaSuccess &&
+                    cudaStreamSynchronize(c->st) == cudaSuccess &&
+                    cudaIpcGetMemHandle(&hdl, c->d_tp_area) == cudaSuccess;
+    if (!ok) {
+        cudaGetLastError();
+        tp_free(c);
+        snprintf(c->err, sizeof c->err, "tensor-parallel exchange area: allocation or IPC export failed");
+        return -1;
+    }
+    memcpy(handle_out, &hdl, sizeof hdl);
+    c->tp_rank = rank;
+    c->tp_world = world;
+    c->tp_vocab0 = vocab0;
+    c->mega_state = -1;
+    return (int)sizeof hdl;
+}
+
+// Map the peers' exchange areas (handles[q * 64 ..] from every rank's
+// hyc_tp_init, the own one ignored) and switch the layer loop and the head
+// to the exchanges.  Every rank must have finished hyc_tp_init (its area
+// zeroed) before any rank connects: a host barrier between the two calls.
+HYC_API int hyc_tp_connect(void *impl, const unsigned char *handles) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->d_tp_area || !handles) return -1;
+    if (cudaSetDevice(c->dev) != cudaSuccess) return -1;
+    TpArgs t;
+    memset(&t, 0, sizeof t);
+    t.cap = c->tp_cap;
+    t.rank = c->tp_rank;
+    t.world = c->tp_world;
+    t.err = c->d_tp_err;
+    for (int q = 0; q < c->tp_world; q++) {
+        if (q == c->tp_rank) {
+            t.area[q] = c->d_tp_area;
+            continue;
+        }
+        cudaIpcMemHandle_t hdl;
+        memcpy(&hdl, handles + (size_t)q * sizeof hdl, sizeof hdl);
+        void *p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, hdl, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            for (int j = 0; j < q; j++)
+                if (j != c->tp_rank && t.area[j]) cudaIpcCloseMemHandle(t.area[j]);
+            snprintf(c->err, sizeof c->err, "tensor-parallel exchange: mapping rank %d's area failed", q);
+            return -1;
+        }
+        t.area[q] = (uint8_t *)p;
+    }
+    c->tp = t;
+    c->tp_on = c->tp_world > 1;
+    graph_reset(c->g_fwd1);
+    graph_reset(c->g_fwd1_logits);
+    graph_reset(c->g_dec);
+    c->g_dec_vocab = -1;
+    return 0;
 }
 
 // ---------------------------------------------------------------- allocation-free decode attention

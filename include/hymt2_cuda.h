@@ -227,6 +227,32 @@ HYC_API long long hyc_launch_count(void *impl);
  * 4 o_proj GEMV, 5 decode attention; layer weights rotate over all layers. */
 HYC_API int hyc_bench_op(void *impl, int op, int iters);
 
+/* ---- tensor parallelism (the optional split of config 4) -------------- */
+
+/* One process per GPU; each handle holds one rank's share of the model,
+ * uploaded and fused_prepare'd with the rank's shape: query heads
+ * [r*heads/world, (r+1)*heads/world) with the KV heads they use (a KV head
+ * is replicated when world > kv_heads), gate/up rows and down K-columns of
+ * FFN slice r, o_proj with the rank's K-columns, and the LM head's
+ * vocabulary rows [vocab0, vocab0 + n) (the embedding table whole).  The
+ * layer loop then adds the sum over ranks of the o_proj and down partial
+ * products to the residual (a one-shot push over NVLink peer memory, the
+ * sum in rank order: every rank holds bit-identical activations), and the
+ * greedy token is the largest (logit, first index) key over the ranks.
+ * Splits the reference's layer loop src/model.c:824-882 and its head and
+ * argmax :884-900, 945-948; no counterpart in its device interface.
+ * hyc_tp_init: allocate and zero the exchange area, write its CUDA IPC
+ * handle (64 bytes) to handle_out; returns the handle size or -1.
+ * hyc_tp_connect: map every peer's area (handles of all ranks, 64 bytes
+ * each, in rank order); call it on every rank only after every rank's
+ * hyc_tp_init has returned.  Returns 0 or -1.  Decode (hyc_decode_begin /
+ * steps / read, hyc_generate) then runs the split; the persistent kernel,
+ * fused_forward and the batch engine are refused on a rank.  A wait for a
+ * peer is bounded (2 s); a timeout marks the handle broken and hyc_sync /
+ * hyc_decode_read report it. */
+HYC_API int hyc_tp_init(void *impl, int rank, int world, int vocab0, unsigned char *handle_out);
+HYC_API int hyc_tp_connect(void *impl, const unsigned char *handles);
+
 /* ---- allocation-free decode attention -------------------------------- */
 
 /* No counterpart in the reference (its CUDA path allocates every buffer in

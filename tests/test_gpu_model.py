@@ -222,3 +222,38 @@ def test_reference_debug_device_matmul_cuda():
                                                    gpu.ctypes.data)
             assert rc == 0
             assert np.abs(gpu - cpu).max() / max(np.abs(cpu).max(), 1e-6) < 2e-4
+
+
+@pytest.mark.parametrize("cfg", ["t_stq", "t_q8_0"])
+def test_decode_stops_at_stop_id(backend, tiny_models, cfg):
+    """On-device stop ids of a single sequence (hyc_decode_begin's stop list,
+    the reference loop's break at src/model.c:947-949): with the k-th greedy
+    id of an unstopped run as a stop id, the run ends there, hyc_decode_read
+    returns the k ids before it, and later steps emit nothing.  t_stq runs the
+    persistent kernel, t_q8_0 the per-layer graph."""
+    from hymt2_b200.device import DeviceModel
+    dm = DeviceModel(tiny_models[cfg], backend, ctx=256)
+    lib, impl = backend.lib, backend.impl
+    try:
+        ids = np.random.default_rng(21).integers(0, dm.vocab_out, 20).astype(np.int32)
+
+        def run(stops):
+            st = np.asarray(stops or [0], dtype=np.int32)
+            assert lib.hyc_decode_begin(impl, ids.ctypes.data, len(ids), 0, 12, st.ctypes.data, len(stops),
+                                        dm.vocab_out) == 0, backend.error()
+            assert lib.hyc_decode_steps(impl, 11) == 0, backend.error()
+            out = np.zeros(12, dtype=np.int32)
+            n = lib.hyc_decode_read(impl, out.ctypes.data, 12)
+            assert n >= 0, backend.error()
+            return out[:n].tolist()
+
+        free = run([])
+        assert len(free) == 12
+        # the first id from position 2 on that has not appeared before it
+        k = next((i for i in range(2, 12) if free[i] not in free[:i]), None)
+        if k is None:
+            pytest.skip("greedy stream repeats one id")
+        stopped = run([free[k], dm.vocab_out + 5])
+        assert stopped == free[:k], (free, k, stopped)
+    finally:
+        dm.close()
