@@ -507,8 +507,8 @@ def bench_c4(args, be, torch, peak) -> dict:
         step_ms = ms / (C4_GEN - 1)
         out = {"value": round((C4_GEN - 1) / (ms / 1e3), 1), "unit": UNIT, "ms_per_step": round(step_ms, 4),
                "workload": "c4_q8_0 on one GPU: Q8_0 layers and tied Q8_0 head (fp32 activations); bs1 greedy "
-                           "decode, 4096-token seeded prompt, 64 tokens (positions 4096..4159); tensor "
-                           "parallelism of config 4 not built",
+                           "decode, 4096-token seeded prompt, 64 tokens (positions 4096..4159); the model whole on one "
+                           "GPU (its tensor-parallel split over N GPUs is the decode_c4_tp line at N >= 2)",
                "roofline_step": {"bytes_per_step": int(step_bytes),
                                  "achieved_gbs": round(step_bytes / step_ms / 1e6, 1),
                                  "frac": round(step_bytes / step_ms / 1e6 / peak, 4)},

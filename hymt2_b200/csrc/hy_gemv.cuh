@@ -158,19 +158,22 @@ __device__ inline void stage_fp32(const GemvArgs &a, int t, float *dst, float *r
     const float4 *y4 = a.act == ACT_NORM ? (const float4 *)a.norm_w
                                          : (a.act == ACT_SILU ? (const float4 *)(a.x2 + (size_t)t * a.ldx) : nullptr);
     const int n4 = K >> 2;
+    const bool norm = a.act == ACT_NORM;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     float4 *d4 = (float4 *)dst;
-    if (a.act == ACT_NORM) {
-        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-        float4 xv[SV], yv[SV];
+    // one set of loads for every mode (RMSNorm inputs in the block-wise layout of norm_f4)
+    float4 xv[SV], yv[SV];
 #pragma unroll
-        for (int j = 0; j < SV; j++) {
-            const int i = norm_f4(j, warp, lane, nw);
-            xv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (i < n4) {
-                xv[j] = x4[i];
-                yv[j] = pre ? (*pre)[j] : __ldg(y4 + i);
-            }
+    for (int j = 0; j < SV; j++) {
+        const int i = norm ? norm_f4(j, warp, lane, nw) : (int)threadIdx.x + j * (int)blockDim.x;
+        xv[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < n4) {
+            xv[j] = x4[i];
+            if (norm && pre) yv[j] = (*pre)[j];
+            else if (y4) yv[j] = __ldg(y4 + i);
         }
+    }
+    if (norm) {
         __syncthreads();  // red and dst may still be read by the previous token's quantiser
         const float ss = norm_ss<SV>(xv, K, red);
         const float scale = 1.0f / sqrtf(ss / (float)K + a.eps);
@@ -183,18 +186,7 @@ __device__ inline void stage_fp32(const GemvArgs &a, int t, float *dst, float *r
                                     __fmul_rn(__fmul_rn(xv[j].z, scale), yv[j].z),
                                     __fmul_rn(__fmul_rn(xv[j].w, scale), yv[j].w));
         }
-        return;
-    }
-    float4 xv[SV], yv[SV];
-#pragma unroll
-    for (int j = 0; j < SV; j++) {
-        const int i = threadIdx.x + j * blockDim.x;
-        if (i < n4) {
-            xv[j] = x4[i];
-            if (y4) yv[j] = __ldg(y4 + i);
-        }
-    }
-    if (a.act == ACT_SILU) {
+    } else if (a.act == ACT_SILU) {
 #pragma unroll
         for (int j = 0; j < SV; j++) {
             const int i = threadIdx.x + j * blockDim.x;

@@ -404,6 +404,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                             }
                         }
                     }
+                    if constexpr (C / CW == 1) {
+                        // every TMEM word of this block is in registers: hand the accumulator set
+                        // back to the MMA warp before the arithmetic (the scale slot, which the
+                        // arithmetic still reads, is released after it)
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) tc_mbar_arrive(&acce[buf]);
+                    }
 #pragma unroll
                     for (int j4 = 0; j4 < CW / 4; j4++) {
                         const float4 w1 = ws1[c * CW / 4 + j4];
@@ -426,11 +434,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                         }
                     }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    tc_mbar_arrive(&acce[buf]);
-                    tc_mbar_arrive(&sempty[sl]);
+                if constexpr (C / CW == 1) {
+                    __syncwarp();
+                    if (lane == 0) tc_mbar_arrive(&sempty[sl]);
+                } else {
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tc_mbar_arrive(&acce[buf]);
+                        tc_mbar_arrive(&sempty[sl]);
+                    }
                 }
             }
             if (ok && t < a.T) {
