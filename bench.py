@@ -11,8 +11,10 @@ flush is needed between steps.
 
   value        device-timed decode tok/s (CUDA events on the backend stream,
                max over ranks; whole job = ranks * steps / max time)
-  e2e          the same decode through the public C ABI with every step's
-               token copied in from / out to pinned host memory, wall-clock
+  e2e          the same decode through the public C ABI with the host in the
+               loop: every step's token goes in from and comes back to pinned
+               host memory, and the host waits for it and checks the stop ids
+               before the next step (wall clock)
   roofline     the dominant kernel: the persistent decode kernel (one launch
                runs up to 64 decode steps), each launch timed with CUDA
                events; algorithmic bytes = every weight byte of a step plus
@@ -23,8 +25,10 @@ flush is needed between steps.
   prefill_c2   config 2 (N = 1): 32 x 256-token Q4_K_M prefill on the tensor
                cores, with its int8 roofline and the reference CPU prefill
   decode_c1    config 1 (N = 1): Q2_0C bs1 decode after a 512-token prompt
-  decode_c4    config 4's model on ONE GPU (its tensor parallelism is not
-               built): Q8_0 bs1 decode at KV length 4096, graph path
+  decode_c4    config 4's model whole on ONE GPU (N = 1): Q8_0 bs1 decode at
+               KV length 4096, graph path
+  decode_c4_tp config 4 as specified (N >= 2): the model split over the N
+               GPUs (tensor parallelism), per-token latency (max over ranks)
 
 `--impl reference` times the reference's own CPU implementation of the path
 (oracle/_ref/libhymt2_ref.so, built from its sources) on the same config.
@@ -85,10 +89,11 @@ def parse():
                    help="also time each kernel of the per-layer graph path alone")
     p.add_argument("--serve-requests", type=int, default=4096, help="config-3 requests (all GPUs); 0 skips")
     p.add_argument("--no-extra", action="store_true", help="skip the config 1 / config 2 lines (N = 1 only)")
-    p.add_argument("--profile-pass", choices=["c2", "c3step", "c4step"],
-                   help="for ncu --profile-from-start off: warm up, then run one batch pass of config 2 "
-                        "(32 x 256 prefill), one config-3-shaped step (256 decode tokens at position 100) or two "
-                        "config-4 decode steps (Q8_0, KV 4096) between cuProfilerStart/Stop, and exit")
+    p.add_argument("--profile-pass", choices=["c0mega", "c2", "c3step", "c4step"],
+                   help="for ncu --profile-from-start off: warm up, then run one persistent-kernel launch of "
+                        "three config-0 decode steps, one batch pass of config 2 (32 x 256 prefill), one "
+                        "config-3-shaped step (256 decode tokens at position 100) or two config-4 decode steps "
+                        "(Q8_0, KV 4096) between cuProfilerStart/Stop, and exit")
     p.add_argument("--layers", type=int, default=32, help="model layers for --profile-pass")
     return p.parse_args()
 
@@ -99,6 +104,25 @@ def profile_pass(args):
     import ctypes
     from hymt2_b200 import synth
     from hymt2_b200.device import Backend, DeviceModel
+    if args.profile_pass == "c0mega":
+        be = Backend(0)
+        dm = DeviceModel(synth.ensure("c0_stq", args.model_dir), be, ctx=1024)
+        lib, impl = be.lib, be.impl
+        ids = prompt_ids()
+        if lib.hyc_decode_begin(impl, ids.ctypes.data, PROMPT_LEN, 0, GEN_LEN, None, 0, dm.vocab_out) != 0 or \
+                lib.hyc_decode_steps(impl, 3) != 0:
+            raise RuntimeError(be.error())
+        be.sync()
+        cu = ctypes.CDLL("libcuda.so.1")
+        cu.cuProfilerStart()
+        if lib.hyc_decode_steps(impl, 3) != 0:
+            raise RuntimeError(be.error())
+        be.sync()
+        cu.cuProfilerStop()
+        dm.close()
+        be.close()
+        print("profiled one persistent-kernel launch of three decode steps")
+        return
     if args.profile_pass == "c4step":
         be = Backend(0)
         dm = DeviceModel(synth.ensure("c4_q8_0", args.model_dir, layers=args.layers), be, ctx=C4_PROMPT + 128)
@@ -140,6 +164,18 @@ def profile_pass(args):
     dm.close()
     be.close()
     print("profiled one pass")
+
+
+def kernel_source_hash() -> str:
+    """sha256 (first 16 hex digits) of the CUDA sources the backend is built from."""
+    import hashlib
+    h = hashlib.sha256()
+    cdir = os.path.join(ROOT, "hymt2_b200", "csrc")
+    for name in sorted(os.listdir(cdir)):
+        if name.endswith((".cu", ".cuh")):
+            with open(os.path.join(cdir, name), "rb") as f:
+                h.update(name.encode() + b"\0" + f.read())
+    return h.hexdigest()[:16]
 
 
 def dist_env():
@@ -633,11 +669,34 @@ def quant_gemv_entry(kernels, peak):
             "ms_per_launch": k["ms_per_launch"]}
 
 
+def c0_config(world: int) -> dict:
+    """The `config` of the headline line, the same in both arms."""
+    return {"workload": "c0_stq: Hy-MT2-1.8B shape, 32 layers STQ1_0 (panel) + Q6_K tied head, reference bench GGUF; "
+                        "bs1 greedy decode after a 48-token prompt, positions 48..111",
+            "global_batch": world, "seq_len": PROMPT_LEN + GEN_LEN, "parallelism": f"dp{world} replicas",
+            "l2": "weights 613 MB per step > 126 MB L2 (no flush needed)"}
+
+
+def reference_bench_gguf(model_dir: str) -> str:
+    """The config-0 model written by the reference's own tool
+    (tools/make_bench_gguf.c, compiled into oracle/_ref by its Makefile);
+    the synthetic writer's byte-identical copy where the tool is not built."""
+    tool = os.path.join(ROOT, "oracle", "_ref", "make_bench_gguf")
+    if not os.path.exists(tool):
+        from hymt2_b200 import synth
+        return synth.ensure("c0_stq", model_dir)
+    os.makedirs(model_dir, exist_ok=True)
+    path = os.path.join(model_dir, "ref_make_bench_gguf_L32.gguf")
+    if not os.path.exists(path):
+        subprocess.run([tool, path + ".tmp"], check=True, stdout=subprocess.DEVNULL)
+        os.replace(path + ".tmp", path)
+    return path
+
+
 def run_reference_arm(args, rank, world):
     if rank != 0:
         return
-    from hymt2_b200 import synth
-    path = synth.ensure("c0_stq", args.model_dir)
+    path = reference_bench_gguf(args.model_dir)
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     os.environ["HYMT2_DEVICE"] = "cpu"
@@ -659,7 +718,7 @@ def run_reference_arm(args, rank, world):
         "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": round(dec_ms / steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic",
-        "config": {"workload": "c0_stq bs1 greedy decode, 48-token prompt, positions 48..111", "parallelism": "none"},
+        "config": c0_config(world),
         "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": threads, "kind": "reference",
                          "sample": f"reference CPU ({ref.isa()}, {threads} threads), {steps} decode steps after a "
                                    f"cached 48-token prompt"},
@@ -812,13 +871,19 @@ def main():
     else:
         dom = max(kernels, key=lambda k: kernels[k]["share_of_step_ms"])
         dk = kernels[dom]
-    traffic = None
+    # DRAM bytes per step of one ncu capture of this kernel, scaled to a launch; only from a capture of the
+    # same kernel sources (the file records their hash)
+    traffic, traffic_note = None, "no capture of the current kernel sources"
     tfile = os.path.join(ROOT, "profiles", "dram_traffic_c0_stq.json")
     if os.path.exists(tfile):
         with open(tfile) as f:
-            tj = json.load(f).get(dom)
-        if tj:  # per-step DRAM bytes of one ncu capture, scaled to a launch
-            traffic = int(tj["dram_bytes_per_step"] * dk.get("steps_per_launch", 1))
+            tj = json.load(f)
+        ent = tj.get(dom)
+        if ent and tj.get("source_sha16") == kernel_source_hash():
+            traffic = int(ent["dram_bytes_per_step"] * dk.get("steps_per_launch", 1))
+            traffic_note = f"ncu capture of {ent.get('kernel', dom)} ({tj.get('command', '')})"
+        elif ent:
+            traffic_note = "the committed capture is of other kernel sources: not used"
 
     # ---- config 3: continuous-batching serving on every GPU (bs256/GPU)
     serving = None
@@ -834,10 +899,7 @@ def main():
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8+fp32", "data": "synthetic",
-            "config": {"workload": "c0_stq: Hy-MT2-1.8B shape, 32 layers STQ1_0 (panel) + Q6_K tied head, reference "
-                                   "bench GGUF; bs1 greedy decode after a 48-token prompt, positions 48..111",
-                       "global_batch": world, "seq_len": PROMPT_LEN + GEN_LEN, "parallelism": f"dp{world} replicas",
-                       "l2": "weights 613 MB per step > 126 MB L2 (no flush needed)"},
+            "config": c0_config(world),
             "e2e": {"value": round(world * args.steps / e2e_s, 2), "unit": UNIT, "h2d_bytes_per_step": 4,
                     "d2h_bytes_per_step": 4,
                     "path": f"host loop through the C ABI: hyc_decode_steps_host(1) (token in from pinned host, one "
@@ -845,7 +907,8 @@ def main():
                             f"the stop ids; wall clock, max over ranks"},
             "decode_path": path_name,
             "roofline": {"bound": "hbm", "kernel": dom, "achieved": dk["gbs"], "peak": peak, "unit": "GB/s",
-                         "frac": round(dk["gbs"] / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
+                         "frac": round(dk["gbs"] / peak, 4), "traffic": traffic, "traffic_note": traffic_note,
+                         "peak_kind": peak_kind,
                          "bytes_per_launch": dk["bytes_per_launch"], "ms_per_launch": dk["ms_per_launch"]},
             "roofline_step": {"bytes_per_step": STEP_BYTES, "achieved_gbs": round(STEP_BYTES / step_ms / 1e6, 1),
                               "frac": round(STEP_BYTES / step_ms / 1e6 / peak, 4)},
