@@ -167,12 +167,12 @@ def profile_pass(args):
 
 
 def kernel_source_hash() -> str:
-    """sha256 (first 16 hex digits) of the CUDA sources the backend is built from."""
+    """sha256 (first 16 hex digits) of the device-code headers the kernels are built from (hy_*.cuh)."""
     import hashlib
     h = hashlib.sha256()
     cdir = os.path.join(ROOT, "hymt2_b200", "csrc")
     for name in sorted(os.listdir(cdir)):
-        if name.endswith((".cu", ".cuh")):
+        if name.endswith(".cuh"):
             with open(os.path.join(cdir, name), "rb") as f:
                 h.update(name.encode() + b"\0" + f.read())
     return h.hexdigest()[:16]
@@ -503,6 +503,82 @@ def bench_c1(args, be, torch, peak) -> dict:
         dm.close()
 
 
+NATIVE = 42 / 256  # native STQ1_0 bytes per weight (qs 32 + sign 8 + d 2 per 256)
+
+
+def _graph_decode_ms(be, dm, torch, ids, n) -> float:
+    """CUDA-event ms per step of n - 1 bs1 decode steps on the per-layer graph."""
+    lib, impl = be.lib, be.impl
+    stream = torch.cuda.ExternalStream(be.stream())
+    if lib.hyc_set_decode_mode(impl, 1) != 0:
+        raise RuntimeError("decode_mode: " + be.error())
+    try:
+        for _ in range(2):
+            if lib.hyc_decode_begin(impl, ids.ctypes.data, len(ids), 0, n, None, 0, dm.vocab_out) != 0:
+                raise RuntimeError("decode_begin: " + be.error())
+            be.sync()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            if lib.hyc_decode_steps(impl, n - 1) != 0:
+                raise RuntimeError("decode_steps: " + be.error())
+            e1.record(stream)
+            torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / (n - 1)
+    finally:
+        lib.hyc_set_decode_mode(impl, 0)
+
+
+def bench_c0_native(args, be, torch, peak, path) -> dict:
+    """The native STQ1_0 layout (the file's 42 B per 256 weights, the pattern
+    table decoded in registers) on the config-0 model: the four layer GEMVs at
+    one token, each cycling over the 32 layers' weights, bytes as stored; and
+    bs1 decode on the per-layer graph (the persistent kernel takes panels
+    only) beside the panel upload on the same graph."""
+    from hymt2_b200.device import DeviceModel
+    lib, impl = be.lib, be.impl
+    stream = torch.cuda.ExternalStream(be.stream())
+    ids = prompt_ids()
+    out = {}
+    for native in (True, False):
+        be.set_stq_layout(native)
+        try:
+            dm = DeviceModel(path, be, ctx=1024)
+        finally:
+            be.set_stq_layout(False)
+        try:
+            step_ms = _graph_decode_ms(be, dm, torch, ids, GEN_LEN)
+            key = "native" if native else "panel"
+            out[f"graph_decode_{key}"] = {"tok_s": round(1e3 / step_ms, 1), "ms_per_step": round(step_ms, 4)}
+            if native:
+                kern = {}
+                for op in (1, 2, 3, 4):
+                    name = OPS[op][0].replace("_panel", "_native")
+                    nbytes = int(OPS[op][2] / PANEL * NATIVE)
+                    if lib.hyc_bench_op(impl, op, 4) != 0:
+                        raise RuntimeError("bench_op: " + be.error())
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record(stream)
+                    if lib.hyc_bench_op(impl, op, 128) != 0:
+                        raise RuntimeError("bench_op: " + be.error())
+                    b.record(stream)
+                    be.sync()
+                    t = a.elapsed_time(b) / 128
+                    kern[name] = {"ms_per_launch": round(t, 5), "bytes_per_launch": nbytes,
+                                  "gbs": round(nbytes / (t / 1e3) / 1e9, 1),
+                                  "gweights_s": round(nbytes / NATIVE / (t / 1e3) / 1e9, 1)}
+                out["kernels"] = kern
+        finally:
+            dm.close()
+    gu = out["kernels"]["gate_up_gemv_native"]
+    out.update({"workload": "c0_stq with STQ1_0 layers uploaded native (hyc_set_stq_layout): gemv_panel_dec "
+                            "<CPL, FMT_STQN> (row slice staged in shared memory, patterns decoded there), bs1 decode "
+                            "positions 48..111 on the per-layer graph",
+                "quant_gemv": {"kernel": "gate_up_gemv_native (2 x 6144 x 2048 native STQ1_0, nt 1)",
+                               "gbs": gu["gbs"], "frac": round(gu["gbs"] / peak, 4),
+                               "bytes_per_launch": gu["bytes_per_launch"], "ms_per_launch": gu["ms_per_launch"]}})
+    return out
+
+
 C4_PROMPT, C4_GEN = 4096, 64
 # config 4 bytes per decode step: Q8_0 (34 B per 32 weights) layers and tied head as stored
 C4_LAYER_BYTES = L * ((QD + 2 * KVD) * H + H * QD + 3 * FFN * H) * 34 // 32
@@ -745,7 +821,16 @@ def main():
     from hymt2_b200.device import Backend, DeviceModel
     path = ensure_model(rank, local, world, args.model_dir, dist)
     be = Backend(local)
+    # GGUF -> device: every weight through the pinned staging ring, STQ1_0 panels and the Q6_K head relaid out
+    # on the device from the file's own bytes, then fused_prepare (the file is in the page cache: just written)
+    t_load = time.perf_counter()
     dm = DeviceModel(path, be, ctx=1024)
+    be.sync()
+    load_s = time.perf_counter() - t_load
+    load = {"s": round(load_s, 3), "file_bytes": os.path.getsize(path),
+            "gbs": round(os.path.getsize(path) / load_s / 1e9, 2),
+            "path": "mmap'd GGUF bytes through two 16 MB pinned staging slots (host copy of one chunk overlapping "
+                    "the DMA of the previous), device-side repack to panels / Q6_K planes; includes fused_prepare"}
     lib, impl = be.lib, be.impl
     stream = torch.cuda.ExternalStream(be.stream())
     ids = prompt_ids()
@@ -915,6 +1000,7 @@ def main():
             "kernels": kernels,
             "quant_gemv": quant_gemv_entry(kernels, peak),
             "gpu_launches": int(launches),
+            "load_c0": load,
             "clocks": clk,
             "device": be.info,
         }
@@ -938,6 +1024,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_extra:
         tops, tops_kind = int8_peak(torch)
         for key, fn in (("prefill_c2", lambda: bench_prefill(args, be, torch, tops, tops_kind)),
+                        ("decode_c0_native", lambda: bench_c0_native(args, be, torch, peak, path)),
                         ("decode_c1", lambda: bench_c1(args, be, torch, peak)),
                         ("decode_c4", lambda: bench_c4(args, be, torch, peak))):
             try:

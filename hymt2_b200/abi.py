@@ -84,6 +84,7 @@ SIGNATURES = {
     "hyc_host_free": (None, [P]),
     "hyc_set_decode_mode": (I, [P, I]),
     "hyc_set_tc": (I, [P, I]),
+    "hyc_set_stq_layout": (I, [P, I]),
     "hyc_tc_test": (I, [P, P, I, P, P, P, F, I, P]),
     "hyc_decode_path": (I, [P, C.c_char_p, I]),
     "hyc_wait_probe": (I, [P, C.c_ulonglong, P]),

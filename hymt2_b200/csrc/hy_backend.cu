@@ -116,6 +116,9 @@ struct HyCtx {
     unsigned long long *d_tl = nullptr;
     int tl_cap = 0;
     MegaPlan mega_plan_v{};
+    // STQ1_0 weights: panels (default) or the native 42 B / 256 layout
+    // (FMT_STQN), from HYMT2_STQ_LAYOUT=native or hyc_set_stq_layout
+    bool stq_native = false;
     // tensor-core path for multi-token chunks (hy_tc.cuh)
     bool tc_on = true;
     int max_tokens = kMaxChunk;     // tokens per forward pass (the batch engine raises it)
@@ -126,6 +129,13 @@ struct HyCtx {
     size_t l2_bytes = 0;
     void *mega_kernel = nullptr;
     Batch *bat = nullptr;           // ragged multi-sequence batches (hy_batch.cuh)
+    // weight upload: a pinned staging ring (the host's mmap'd GGUF bytes are copied through it, so
+    // every device copy is an asynchronous DMA from pinned memory) and a reusable buffer for the raw
+    // bytes the device repacks
+    uint8_t *h_stage[2] = {nullptr, nullptr};
+    cudaEvent_t stage_ev[2] = {nullptr, nullptr};
+    uint8_t *d_raw = nullptr;
+    size_t raw_cap = 0;
     // tensor parallelism: this handle holds one rank's share of a split model (hy_tp.cuh)
     int tp_rank = 0, tp_world = 1, tp_vocab0 = 0;
     bool tp_on = false;             // connected to its peers: o_proj / down / head exchange
@@ -165,6 +175,47 @@ cudaError_t h2d(HyCtx *c, void *dst, const void *src, size_t bytes) {
 cudaError_t d2h(HyCtx *c, void *dst, const void *src, size_t bytes) {
     cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, c->st);
     return e == cudaSuccess ? cudaStreamSynchronize(c->st) : e;
+}
+
+// Host bytes (pageable, e.g. the mmap'd GGUF) -> device, through two pinned
+// staging slots: the host copy of one chunk overlaps the DMA of the previous
+// one.  Returns when every copy is enqueued; stream order makes them visible.
+constexpr size_t kStageBytes = 16u << 20;
+cudaError_t h2d_staged(HyCtx *c, void *dst, const void *src, size_t bytes) {
+    if (!c->h_stage[0]) {
+        for (int i = 0; i < 2; i++) {
+            cudaError_t e = cudaHostAlloc((void **)&c->h_stage[i], kStageBytes, cudaHostAllocDefault);
+            if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->stage_ev[i], cudaEventDisableTiming);
+            if (e != cudaSuccess) return e;
+        }
+    }
+    size_t o = 0;
+    for (int i = 0; o < bytes; i++, o += kStageBytes) {
+        const int k = i & 1;
+        const size_t n = bytes - o < kStageBytes ? bytes - o : kStageBytes;
+        cudaError_t e = cudaEventSynchronize(c->stage_ev[k]);  // the slot's previous DMA is done
+        if (e != cudaSuccess) return e;
+        memcpy(c->h_stage[k], (const uint8_t *)src + o, n);
+        e = cudaMemcpyAsync((uint8_t *)dst + o, c->h_stage[k], n, cudaMemcpyHostToDevice, c->st);
+        if (e == cudaSuccess) e = cudaEventRecord(c->stage_ev[k], c->st);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+// The reusable device buffer for raw bytes the device repacks (grown as needed).
+uint8_t *raw_buf(HyCtx *c, size_t bytes) {
+    if (bytes > c->raw_cap) {
+        if (c->d_raw) {
+            cudaStreamSynchronize(c->st);
+            cudaFree(c->d_raw);
+        }
+        c->d_raw = nullptr;
+        c->raw_cap = 0;
+        if (cudaMalloc(&c->d_raw, bytes) != cudaSuccess) return nullptr;
+        c->raw_cap = bytes;
+    }
+    return c->d_raw;
 }
 
 template <typename... KArgs, typename... Args>
@@ -227,7 +278,7 @@ WDesc desc(const HyWeight *w, float *out, int ld) {
     return d;
 }
 
-bool is_q8_fmt(int fmt) { return fmt == FMT_PANEL || fmt == FMT_Q4K || fmt == FMT_Q6K; }
+bool is_q8_fmt(int fmt) { return fmt == FMT_PANEL || fmt == FMT_STQN || fmt == FMT_Q4K || fmt == FMT_Q6K; }
 
 // ---------------------------------------------------------------- GEMV dispatch
 
@@ -261,6 +312,16 @@ void init_kernel_attrs_current() {
     set_smem(gemv_panel_nt1<4>);
     set_smem(gemv_panel_nt<4>);
     set_smem(gemv_panel_nt<16>);
+    set_smem(gemv_panel_nt1<1, FMT_STQN>);
+    set_smem(gemv_panel_nt1<2, FMT_STQN>);
+    set_smem(gemv_panel_nt1<3, FMT_STQN>);
+    set_smem(gemv_panel_nt1<4, FMT_STQN>);
+    set_smem(gemv_panel_nt<4, FMT_STQN>);
+    set_smem(gemv_panel_nt<16, FMT_STQN>);
+    set_smem(gemv_panel_dec<1, FMT_STQN>);
+    set_smem(gemv_panel_dec<2, FMT_STQN>);
+    set_smem(gemv_panel_dec<3, FMT_STQN>);
+    set_smem(gemv_panel_dec<4, FMT_STQN>);
     set_smem(gemv_q6k<1>);
     set_smem(gemv_q6k<4>);
     set_smem(gemv_q6k<16>);
@@ -349,6 +410,7 @@ bool gemv_launch(HyCtx *c, const GemvArgs &a_in, bool pdl, int ctas_per_sm) {
                     }
                 }
             }
+            REQ(c, a.epi != EPI_SILU, "interleaved gate|up pair needs the staged decode GEMV");
             if (NT == 1 && cpl <= 4) {
                 switch (cpl) {
                 case 1: return launch(c, gemv_panel_nt1<1>, grid, blk, smem, pdl, a);
@@ -359,6 +421,32 @@ bool gemv_launch(HyCtx *c, const GemvArgs &a_in, bool pdl, int ctas_per_sm) {
             }
             if (NT <= 4) return launch(c, gemv_panel_nt<4>, grid, blk, q8_smem_bytes(4, a.k), pdl, a);
             return launch(c, gemv_panel_nt<16>, grid, blk, smem, pdl, a);
+        }
+        if (fmt == FMT_STQN) {
+            const int cpl = (a.k + 2047) / 2048;
+            if (NT == 1 && cpl <= 4 && a.epi != EPI_ARGMAX) {
+                const int rpc = ((a.rows_total + grid - 1) / grid + 3) & ~3;
+                const size_t sm = panel_dec_smem(rpc, a.k, FMT_STQN);
+                if (sm <= kMaxDynSmem) {
+                    switch (cpl) {
+                    case 1: return launch(c, gemv_panel_dec<1, FMT_STQN>, grid, blk, sm, pdl, a, rpc);
+                    case 2: return launch(c, gemv_panel_dec<2, FMT_STQN>, grid, blk, sm, pdl, a, rpc);
+                    case 3: return launch(c, gemv_panel_dec<3, FMT_STQN>, grid, blk, sm, pdl, a, rpc);
+                    default: return launch(c, gemv_panel_dec<4, FMT_STQN>, grid, blk, sm, pdl, a, rpc);
+                    }
+                }
+            }
+            REQ(c, a.epi != EPI_SILU, "interleaved gate|up pair needs the staged decode GEMV");
+            if (NT == 1 && cpl <= 4) {
+                switch (cpl) {
+                case 1: return launch(c, gemv_panel_nt1<1, FMT_STQN>, grid, blk, smem, pdl, a);
+                case 2: return launch(c, gemv_panel_nt1<2, FMT_STQN>, grid, blk, smem, pdl, a);
+                case 3: return launch(c, gemv_panel_nt1<3, FMT_STQN>, grid, blk, smem, pdl, a);
+                default: return launch(c, gemv_panel_nt1<4, FMT_STQN>, grid, blk, smem, pdl, a);
+                }
+            }
+            if (NT <= 4) return launch(c, gemv_panel_nt<4, FMT_STQN>, grid, blk, q8_smem_bytes(4, a.k), pdl, a);
+            return launch(c, gemv_panel_nt<16, FMT_STQN>, grid, blk, smem, pdl, a);
         }
         if (fmt == FMT_Q6K) {
             if (NT == 1) return launch(c, gemv_q6k<1>, grid, blk, smem, pdl, a);
@@ -639,7 +727,8 @@ bool attention(HyCtx *c, const AttnArgs &aa_in, int nt, bool pdl) {
 // quantises that vector.  Otherwise gate and up land in separate buffers and
 // down applies SiLU*up in its prologue.
 bool ffn_pair_ok(const Layer &L, int nt) {
-    return nt == 1 && L.g->fmt == FMT_PANEL && L.u->fmt == FMT_PANEL && L.g->n == L.u->n && L.g->k == L.u->k &&
+    return nt == 1 && (L.g->fmt == FMT_PANEL || L.g->fmt == FMT_STQN) && L.u->fmt == L.g->fmt && L.g->n == L.u->n &&
+           L.g->k == L.u->k &&
            L.g->shift == L.u->shift && L.g->off == L.u->off;
 }
 
@@ -1193,6 +1282,11 @@ void destroy_impl(void *impl) {
     if (c->d_tcad) cudaFree(c->d_tcad);
     if (c->d_tcerr) cudaFree(c->d_tcerr);
     if (c->h_pinned_int) cudaFreeHost(c->h_pinned_int);
+    for (int i = 0; i < 2; i++) {
+        if (c->h_stage[i]) cudaFreeHost(c->h_stage[i]);
+        if (c->stage_ev[i]) cudaEventDestroy(c->stage_ev[i]);
+    }
+    if (c->d_raw) cudaFree(c->d_raw);
     if (c->st) cudaStreamDestroy(c->st);
     delete c;
 }
@@ -1232,6 +1326,27 @@ hy_dweight *upload(void *impl, const weight_t *w) {
     };
     switch (w->type) {
     case GT_STQ1_0:
+        if (c->stq_native) {
+            // the file's 42-byte blocks, relaid per row into qs | sign | d planes
+            if (w->k % 256) return bail("inner dimension not a block multiple");
+            if (!w->data || w->row_bytes != (size_t)d->nb * 42) return bail("native STQ1_0 rows needed");
+            d->fmt = FMT_STQN;
+            d->shift = 0;
+            d->off = 1;
+            d->stride = (long long)align16((size_t)d->nb * 42);
+            const size_t rb = (size_t)d->n * w->row_bytes;
+            ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess;
+            uint8_t *raw = ok ? raw_buf(c, rb) : nullptr;
+            ok = raw && h2d_staged(c, raw, w->data, rb) == cudaSuccess;
+            if (ok) {
+                const long long tot = (long long)d->n * d->nb;
+                stqn_from_native<<<(unsigned)((tot + 255) / 256), 256, 0, c->st>>>(raw, (long long)w->row_bytes, d->n,
+                                                                                 d->nb, d->w, d->stride);
+                ok = cudaGetLastError() == cudaSuccess;
+            }
+            break;
+        }
+        [[fallthrough]];
     case GT_Q2_0C: {
         if (w->k % (w->type == GT_Q2_0C ? 512 : 256)) return bail("inner dimension not a block multiple");
         d->fmt = FMT_PANEL;
@@ -1246,19 +1361,19 @@ hy_dweight *upload(void *impl, const weight_t *w) {
         ok = cudaMalloc(&d->w, pk_bytes) == cudaSuccess && cudaMalloc(&d->s, ps_bytes) == cudaSuccess;
         if (!ok) return bail("out of device memory");
         if (w->pk) {
-            ok = h2d(c, d->w, w->pk, pk_bytes) == cudaSuccess &&
-                 h2d(c, d->s, w->ps, ps_bytes) == cudaSuccess;
+            ok = h2d_staged(c, d->w, w->pk, pk_bytes) == cudaSuccess &&
+                 h2d_staged(c, d->s, w->ps, ps_bytes) == cudaSuccess;
         } else {
-            uint8_t *raw = nullptr;
+            // the file's native rows, repacked to panels on the device
             const size_t rb = (size_t)d->n * w->row_bytes;
-            ok = cudaMalloc(&raw, rb) == cudaSuccess && h2d(c, raw, w->data, rb) == cudaSuccess;
+            uint8_t *raw = raw_buf(c, rb);
+            ok = raw && h2d_staged(c, raw, w->data, rb) == cudaSuccess;
             if (ok) {
                 const long long tot = (long long)d->n * d->nb;
                 panel_from_native<<<(unsigned)((tot + 255) / 256), 256, 0, c->st>>>(raw, (long long)w->row_bytes, w->type,
                                                                                   d->n, d->nb, d->w, d->s);
-                ok = cudaStreamSynchronize(c->st) == cudaSuccess && cudaGetLastError() == cudaSuccess;
+                ok = cudaGetLastError() == cudaSuccess;
             }
-            if (raw) cudaFree(raw);
         }
         break;
     }
@@ -1267,22 +1382,21 @@ hy_dweight *upload(void *impl, const weight_t *w) {
         d->fmt = FMT_Q4K;
         d->stride = (long long)d->nb * 144;
         ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess &&
-             h2d(c, d->w, w->data, (size_t)d->n * d->stride) == cudaSuccess;
+             h2d_staged(c, d->w, w->data, (size_t)d->n * d->stride) == cudaSuccess;
         break;
     case GT_Q6_K: {
         if (w->k % 256) return bail("inner dimension not a block multiple");
         d->fmt = FMT_Q6K;
         d->stride = (long long)align16((size_t)d->nb * 208 + (size_t)d->nb * 2);
-        uint8_t *raw = nullptr;
         const size_t rb = (size_t)d->n * d->nb * 210;
-        ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess && cudaMalloc(&raw, rb) == cudaSuccess &&
-             h2d(c, raw, w->data, rb) == cudaSuccess;
+        ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess;
+        uint8_t *raw = ok ? raw_buf(c, rb) : nullptr;
+        ok = raw && h2d_staged(c, raw, w->data, rb) == cudaSuccess;
         if (ok) {
             const long long tot = (long long)d->n * d->nb;
             q6k_relayout<<<(unsigned)((tot + 255) / 256), 256, 0, c->st>>>(raw, d->n, d->nb, d->w, d->stride);
-            ok = cudaStreamSynchronize(c->st) == cudaSuccess && cudaGetLastError() == cudaSuccess;
+            ok = cudaGetLastError() == cudaSuccess;
         }
-        if (raw) cudaFree(raw);
         break;
     }
     case GT_Q8_0: {
@@ -1290,16 +1404,15 @@ hy_dweight *upload(void *impl, const weight_t *w) {
         d->fmt = FMT_Q80;
         const int nblk = w->k / 32;
         d->stride = (long long)align16((size_t)w->k + (size_t)nblk * 2);
-        uint8_t *raw = nullptr;
         const size_t rb = (size_t)d->n * nblk * 34;
-        ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess && cudaMalloc(&raw, rb) == cudaSuccess &&
-             h2d(c, raw, w->data, rb) == cudaSuccess;
+        ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess;
+        uint8_t *raw = ok ? raw_buf(c, rb) : nullptr;
+        ok = raw && h2d_staged(c, raw, w->data, rb) == cudaSuccess;
         if (ok) {
             const long long tot = (long long)d->n * nblk;
             q80_relayout<<<(unsigned)((tot + 255) / 256), 256, 0, c->st>>>(raw, d->n, nblk, d->w, d->stride);
-            ok = cudaStreamSynchronize(c->st) == cudaSuccess && cudaGetLastError() == cudaSuccess;
+            ok = cudaGetLastError() == cudaSuccess;
         }
-        if (raw) cudaFree(raw);
         break;
     }
     case GT_F16:
@@ -1309,7 +1422,7 @@ hy_dweight *upload(void *impl, const weight_t *w) {
         d->fmt = w->type == GT_F16 ? FMT_F16 : FMT_F32;
         d->stride = (long long)w->k * es;
         ok = cudaMalloc(&d->w, (size_t)d->n * d->stride) == cudaSuccess &&
-             h2d(c, d->w, w->data, (size_t)d->n * d->stride) == cudaSuccess;
+             h2d_staged(c, d->w, w->data, (size_t)d->n * d->stride) == cudaSuccess;
         break;
     }
     default:
@@ -1582,6 +1695,8 @@ HYC_API void *hyc_create(int device, char *info, size_t cap) {
     }
     HyCtx *c = new HyCtx();
     c->dev = device;
+    const char *lay = getenv("HYMT2_STQ_LAYOUT");
+    c->stq_native = lay && strcmp(lay, "native") == 0;
     c->nsm = p.multiProcessorCount;
     c->l2_bytes = (size_t)p.l2CacheSize;
     if (!init_kernel_attrs(device)) {
@@ -1644,6 +1759,13 @@ HYC_API int hyc_set_embedding(void *impl, hy_dweight *embd) {
     graph_reset(c->g_dec);
     c->g_dec_vocab = -1;
     c->mega_state = -1;
+    return 0;
+}
+
+HYC_API int hyc_set_stq_layout(void *impl, int native) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c) return -1;
+    c->stq_native = native != 0;
     return 0;
 }
 

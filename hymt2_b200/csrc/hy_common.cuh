@@ -11,11 +11,13 @@ namespace hyk {
 
 // Device weight layouts (chosen at upload; see hy_backend.cu):
 //   PANEL  n x nb x 64 B of 2-bit codes (host panel order) + float scale [n*nb]
+//   STQN   native STQ1_0, 42 B per 256 weights, per row: qs[nb*32] | sign[nb*8] |
+//          d f16[nb] padded to 16 B (chunk order and sign bits: stq_decode_unit)
 //   Q4K    native 144-byte blocks, rows of nb*144 B
 //   Q6K    per row: ql[nb*128] | qh[nb*64] | scales[nb*16] | d f16[nb] padded to 16 B
 //   Q80    per row: qs[k] int8 | d f16[k/32] padded to 16 B
 //   F16    native half rows;  F32 native float rows
-enum Fmt { FMT_PANEL = 0, FMT_Q4K = 1, FMT_Q6K = 2, FMT_Q80 = 3, FMT_F16 = 4, FMT_F32 = 5 };
+enum Fmt { FMT_PANEL = 0, FMT_Q4K = 1, FMT_Q6K = 2, FMT_Q80 = 3, FMT_F16 = 4, FMT_F32 = 5, FMT_STQN = 6 };
 
 // How a GEMV launch builds its activation in shared memory.
 enum ActMode {
@@ -77,12 +79,85 @@ __device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
 
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
 
+// ---------------------------------------------------------------- STQ1_0 patterns
+
+// The STQ1_0 pattern table, a constant of the file format (reference
+// src/kernels.c:178-181): entry (sign << 4) | slot holds four 2-bit codes,
+// code - 1 in {-1, 0, +1}, lane l at bits 2l .. 2l+1, exactly one zero.
+struct StqPatterns { uint8_t v[32]; };
+constexpr StqPatterns kStqPatterns = {{
+    0xA9, 0x89, 0x29, 0x09, 0xA6, 0x86, 0x26, 0x06, 0x9A, 0x92, 0x1A, 0x12, 0x6A, 0x62, 0x4A, 0x42,
+    0x01, 0x21, 0x81, 0xA1, 0x04, 0x24, 0x84, 0xA4, 0x10, 0x18, 0x90, 0x98, 0x40, 0x48, 0x60, 0x68,
+}};
+// Entries 4m .. 4m+3 as one little-endian word.
+__host__ __device__ constexpr uint32_t stq_word(int m) {
+    return (uint32_t)kStqPatterns.v[4 * m] | ((uint32_t)kStqPatterns.v[4 * m + 1] << 8) |
+           ((uint32_t)kStqPatterns.v[4 * m + 2] << 16) | ((uint32_t)kStqPatterns.v[4 * m + 3] << 24);
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+// Patterns of four groups at once, from registers (no table memory): nibble i
+// of `slots` (bits 0..15; higher bits ignored) is group i's 4-bit slot, and
+// bit 2 of nibble i of `sel_sign` its sign, the other bits of sel_sign being
+// 0x3210.  Byte permutes over the table words: the slot's low 3 bits pick a
+// byte of each 8-entry quarter, its bit 3 picks the quarter within a sign
+// half, the sign picks the half.  Byte i of the result = group i's pattern.
+__device__ __forceinline__ uint32_t stq_decode_quad(uint32_t slots, uint32_t sel_sign) {
+    const uint32_t s1 = slots & 0x7777u;
+    const uint32_t q0 = prmt(stq_word(0), stq_word(1), s1), q1 = prmt(stq_word(2), stq_word(3), s1);
+    const uint32_t q2 = prmt(stq_word(4), stq_word(5), s1), q3 = prmt(stq_word(6), stq_word(7), s1);
+    const uint32_t s2 = ((slots >> 1) & 0x4444u) | 0x3210u;
+    return prmt(prmt(q0, q1, s2), prmt(q2, q3, s2), sel_sign);
+}
+
+// One pattern: (sign << 4) | slot -> its byte.
+__device__ __forceinline__ uint32_t stq_pattern(int idx) {
+    return stq_decode_quad((uint32_t)(idx & 15), 0x3210u | (uint32_t)((idx >> 4) & 1) << 2) & 0xffu;
+}
+
+// One 64-weight unit of a native row (see FMT_STQN): the 16 slots of one
+// 16-group chunk of a block (8 qs bytes, group m at nibble m) and its 16 sign
+// bits stored bit-sliced (bit 4i + j = sign of group 4j + i).  Returns the
+// unit's patterns as a 16-byte panel chunk: word j, byte i = group 4j + i.
+__device__ __forceinline__ uint4 stq_decode_unit(uint2 qs, uint32_t sg) {
+    uint4 w;
+    w.x = stq_decode_quad(qs.x, ((sg << 2) & 0x4444u) | 0x3210u);
+    w.y = stq_decode_quad(qs.x >> 16, ((sg << 1) & 0x4444u) | 0x3210u);
+    w.z = stq_decode_quad(qs.y, (sg & 0x4444u) | 0x3210u);
+    w.w = stq_decode_quad(qs.y >> 16, ((sg >> 1) & 0x4444u) | 0x3210u);
+    return w;
+}
+
+// Bit-sliced form of a chunk's 16 natural sign bits (bit m = group m):
+// bit 4i + j <- bit 4j + i (a 4 x 4 bit transpose).
+__host__ __device__ inline uint32_t stq_slice_signs(uint32_t s) {
+    uint32_t o = 0;
+    for (int i = 0; i < 4; i++)
+        for (int j = 0; j < 4; j++) o |= ((s >> (4 * j + i)) & 1u) << (4 * i + j);
+    return o;
+}
+
 // 16-byte streaming load of weights (read-only, not kept in L1).
 __device__ __forceinline__ uint4 ldg_stream(const void *p) {
     uint4 r;
     asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
                  : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint2 ldg_stream8(const void *p) {
+    uint2 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint32_t ldg_stream16(const void *p) {
+    unsigned short r;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(r) : "l"(p));
     return r;
 }
 

@@ -390,9 +390,42 @@ __device__ __forceinline__ int panel_chunk_dot4(const uint4 wv, const int4 *act4
 }
 __device__ __forceinline__ int panel_chunk_dot(const uint4 wv, const int4 *act4) { return panel_chunk_dot4(wv, act4); }
 
+// One lane's 64-weight unit u of a row (u = 4 b + p: panel chunk u), as
+// loaded from HBM, for the two 2-bit layouts.  PANEL: the 16-byte chunk of
+// pre-decoded codes and the block's fp32 scale.  STQN (native STQ1_0, 42 B /
+// 256): 8 bytes of slots, 16 sign bits and the f16 scale, decoded in
+// registers (stq_decode_unit) into the identical chunk.
+template <int FMT>
+struct PUnit;
+template <>
+struct PUnit<FMT_PANEL> {
+    uint4 w;
+    float s;
+    __device__ __forceinline__ void load(const WDesc &d, int r, int u, int nb) {
+        w = ldg_stream(d.w + (size_t)r * d.stride + (size_t)u * 16);
+        s = __ldg(d.s + (size_t)r * nb + (u >> 2));
+    }
+    __device__ __forceinline__ uint4 codes() const { return w; }
+};
+template <>
+struct PUnit<FMT_STQN> {
+    uint2 q;
+    uint32_t sg, dh;
+    __device__ __forceinline__ void load(const WDesc &d, int r, int u, int nb) {
+        const uint8_t *row = d.w + (size_t)r * d.stride;
+        q = ldg_stream8(row + (size_t)u * 8);
+        sg = ldg_stream16(row + (size_t)nb * 32 + (size_t)u * 2);
+        dh = ldg_stream16(row + (size_t)nb * 40 + (size_t)(u >> 2) * 2);
+    }
+    __device__ __forceinline__ uint4 codes() const { return stq_decode_unit(q, sg); }
+    __device__ __forceinline__ float scale() const { return h2f((uint16_t)dh); }
+};
+__device__ __forceinline__ float punit_scale(const PUnit<FMT_PANEL> &u) { return u.s; }
+__device__ __forceinline__ float punit_scale(const PUnit<FMT_STQN> &u) { return u.scale(); }
+
 // Decode (nt == 1): the lane's activation chunks live in registers for the
 // whole launch.  CPL = 16-byte chunks per lane per row (K <= 2048*CPL).
-template <int CPL>
+template <int CPL, int FMT = FMT_PANEL>
 __global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt1(const __grid_constant__ GemvArgs a) {
     trace_mark(a.trace, 0);
     pdl_trigger();
@@ -402,8 +435,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt1(const __grid_cons
     const int gw = blockIdx.x * kGemvWarps + (threadIdx.x >> 5), nw = gridDim.x * kGemvWarps;
 
     // prefetch the first row's weights before waiting on the producer
-    uint4 wcur[CPL];
-    float scur[CPL];
+    PUnit<FMT> wcur[CPL];
     int r = gw, wi = 0, lr = 0;
     if (r < a.rows_total) {
         map_row(a, r, wi, lr);
@@ -411,10 +443,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt1(const __grid_cons
 #pragma unroll
         for (int i = 0; i < CPL; i++) {
             const int c = lane + 32 * i;
-            if (c < nchunk) {
-                wcur[i] = ldg_stream(w.w + (size_t)lr * w.stride + (size_t)c * 16);
-                scur[i] = __ldg(w.s + (size_t)lr * nb + (c >> 2));
-            }
+            if (c < nchunk) wcur[i].load(w, lr, c, nb);
         }
     }
     pdl_wait();
@@ -447,18 +476,14 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt1(const __grid_cons
         // issue the next row's loads before computing this one
         const int rn = r + nw;
         int wn = 0, ln = 0;
-        uint4 wnext[CPL];
-        float snext[CPL];
+        PUnit<FMT> wnext[CPL];
         if (rn < a.rows_total) {
             map_row(a, rn, wn, ln);
             const WDesc &w2 = wsel(a, wn);
 #pragma unroll
             for (int i = 0; i < CPL; i++) {
                 const int c = lane + 32 * i;
-                if (c < nchunk) {
-                    wnext[i] = ldg_stream(w2.w + (size_t)ln * w2.stride + (size_t)c * 16);
-                    snext[i] = __ldg(w2.s + (size_t)ln * nb + (c >> 2));
-                }
+                if (c < nchunk) wnext[i].load(w2, ln, c, nb);
             }
         }
         const WDesc &w = wsel(a, wi);
@@ -466,22 +491,19 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt1(const __grid_cons
 #pragma unroll
         for (int i = 0; i < CPL; i++) {
             const int c = lane + 32 * i;
-            int e = c < nchunk ? panel_chunk_dot(wcur[i], act[i]) : 0;
+            int e = c < nchunk ? panel_chunk_dot(wcur[i].codes(), act[i]) : 0;
             e += __shfl_xor_sync(0xffffffffu, e, 1);
             e += __shfl_xor_sync(0xffffffffu, e, 2);
             if (c < nchunk && (lane & 3) == 0) {
                 const int v = e * (1 << w.shift) - w.off * sblk[i];
                 if (a.ints) a.ints[(size_t)r * nb + (c >> 2)] = v;
-                acc += scur[i] * dblk[i] * (float)v;
+                acc += punit_scale(wcur[i]) * dblk[i] * (float)v;
             }
         }
         acc = warp_sum(acc);
         row_epilogue<1>(a, w, lr, r, &acc, best);
 #pragma unroll
-        for (int i = 0; i < CPL; i++) {
-            wcur[i] = wnext[i];
-            scur[i] = snext[i];
-        }
+        for (int i = 0; i < CPL; i++) wcur[i] = wnext[i];
         wi = wn;
         lr = ln;
     }
@@ -494,8 +516,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt1(const __grid_cons
 // blocks and scales (weights never depend on the previous kernel), so the
 // HBM stream overlaps the producer kernel; after the wait it only builds the
 // activation and computes from shared memory.
-__host__ __device__ inline size_t panel_dec_smem(int rows_per_cta, int K) {
+__host__ __device__ inline size_t panel_dec_smem(int rows_per_cta, int K, int fmt = FMT_PANEL) {
     const int nb = K / 256;
+    if (fmt == FMT_STQN) return align16((size_t)rows_per_cta * align16((size_t)nb * 42)) + q8_smem_bytes(1, K);
     return align16((size_t)rows_per_cta * nb * 64) + align16((size_t)rows_per_cta * nb * 4) + q8_smem_bytes(1, K);
 }
 
@@ -505,33 +528,40 @@ __device__ __forceinline__ void cp_async4(void *dst, const void *src) {
 }
 
 
-template <int CPL>
+// FMT_STQN stages each row's native bytes whole (qs | sign | d, the row
+// stride) and decodes the patterns from shared memory (stq_decode_unit).
+template <int CPL, int FMT = FMT_PANEL>
 __global__ void __launch_bounds__(kGemvThreads) gemv_panel_dec(const __grid_constant__ GemvArgs a, int rows_per_cta) {
     constexpr int RG = CPL == 1 ? 4 : 2;  // rows per warp iteration (independent chains)
+    constexpr bool NATIVE = FMT == FMT_STQN;
     extern __shared__ __align__(16) uint8_t smem[];
     trace_mark(a.trace, 0);
     pdl_trigger();
-    const int K = a.k, nb = K / 256, nchunk = nb * 4, row_b = nb * 64;
+    const int K = a.k, nb = K / 256, nchunk = nb * 4;
+    const int row_b = NATIVE ? (int)a.w[0].stride : nb * 64;  // merged weights share K, so the stride
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int r0 = blockIdx.x * rows_per_cta;
     const int r1 = min(r0 + rows_per_cta, a.rows_total);
     uint8_t *sw = smem;
     float *ss = (float *)(smem + align16((size_t)rows_per_cta * row_b));
-    uint8_t *sact = smem + align16((size_t)rows_per_cta * row_b) + align16((size_t)rows_per_cta * nb * 4);
+    uint8_t *sact = smem + align16((size_t)rows_per_cta * row_b) + (NATIVE ? 0 : align16((size_t)rows_per_cta * nb * 4));
     // stage the weight slice (16-byte chunks) and scales (4-byte) asynchronously
-    for (int idx = threadIdx.x; idx < (r1 - r0) * nchunk; idx += blockDim.x) {
-        const int rr = idx / nchunk, c = idx - rr * nchunk;
+    const int units = row_b / 16;
+    for (int idx = threadIdx.x; idx < (r1 - r0) * units; idx += blockDim.x) {
+        const int rr = idx / units, c = idx - rr * units;
         int wi, lr;
         map_row(a, r0 + rr, wi, lr);
         const WDesc &w = wsel(a, wi);
         cp_async16(sw + (size_t)rr * row_b + c * 16, w.w + (size_t)lr * w.stride + (size_t)c * 16);
     }
-    for (int idx = threadIdx.x; idx < (r1 - r0) * nb; idx += blockDim.x) {
-        const int rr = idx / nb, b = idx - rr * nb;
-        int wi, lr;
-        map_row(a, r0 + rr, wi, lr);
-        const WDesc &w = wsel(a, wi);
-        cp_async4(ss + (size_t)rr * nb + b, w.s + (size_t)lr * nb + b);
+    if constexpr (!NATIVE) {
+        for (int idx = threadIdx.x; idx < (r1 - r0) * nb; idx += blockDim.x) {
+            const int rr = idx / nb, b = idx - rr * nb;
+            int wi, lr;
+            map_row(a, r0 + rr, wi, lr);
+            const WDesc &w = wsel(a, wi);
+            cp_async4(ss + (size_t)rr * nb + b, w.s + (size_t)lr * nb + b);
+        }
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
     constexpr int SV = 2 * CPL;  // K <= 2048*CPL: 2*CPL float4 per thread at 256 threads
@@ -576,8 +606,16 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_panel_dec(const __grid_cons
 #pragma unroll
             for (int g = 0; g < RG; g++) {
                 e[g] = 0;
-                if (c < nchunk && rb + g < r1)
-                    e[g] = panel_chunk_dot4(*(const uint4 *)(sw + (size_t)(rb + g - r0) * row_b + c * 16), act[i]);
+                if (c < nchunk && rb + g < r1) {
+                    const uint8_t *srow = sw + (size_t)(rb + g - r0) * row_b;
+                    uint4 wv;
+                    if constexpr (NATIVE)
+                        wv = stq_decode_unit(*(const uint2 *)(srow + c * 8),
+                                             *(const uint16_t *)(srow + nb * 32 + c * 2));
+                    else
+                        wv = *(const uint4 *)(srow + c * 16);
+                    e[g] = panel_chunk_dot4(wv, act[i]);
+                }
             }
 #pragma unroll
             for (int g = 0; g < RG; g++) e[g] += __shfl_xor_sync(0xffffffffu, e[g], 1);
@@ -589,7 +627,12 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_panel_dec(const __grid_cons
                     if (rb + g >= r1) break;
                     const int v = e[g] * (1 << shift) - off * sblk[i];
                     if (a.ints) a.ints[(size_t)(rb + g) * nb + (c >> 2)] = v;
-                    acc[g] += ss[(size_t)(rb + g - r0) * nb + (c >> 2)] * dblk[i] * (float)v;
+                    float sc;
+                    if constexpr (NATIVE)
+                        sc = h2f(*(const uint16_t *)(sw + (size_t)(rb + g - r0) * row_b + nb * 40 + (c >> 2) * 2));
+                    else
+                        sc = ss[(size_t)(rb + g - r0) * nb + (c >> 2)];
+                    acc[g] += sc * dblk[i] * (float)v;
                 }
             }
         }
@@ -623,7 +666,7 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_panel_dec(const __grid_cons
 }
 
 // Small batches (1 < nt <= NT): activations read from plane-major smem.
-template <int NT>
+template <int NT, int FMT = FMT_PANEL>
 __global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt(const __grid_constant__ GemvArgs a) {
     trace_mark(a.trace, 0);
     pdl_trigger();
@@ -650,8 +693,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_panel_nt(const __grid_const
             uint4 wv = make_uint4(0, 0, 0, 0);
             float sc = 0.f;
             if (ok) {
-                wv = ldg_stream(w.w + (size_t)lr * w.stride + (size_t)c * 16);
-                sc = __ldg(w.s + (size_t)lr * nb + (c >> 2));
+                PUnit<FMT> pu;
+                pu.load(w, lr, c, nb);
+                wv = pu.codes();
+                sc = punit_scale(pu);
             }
             const uint32_t wd[4] = {wv.x, wv.y, wv.z, wv.w};
             uint32_t code[4][4];

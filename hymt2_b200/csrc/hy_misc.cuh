@@ -7,12 +7,6 @@ namespace hyk {
 
 // ---------------------------------------------------------------- upload relayouts
 
-// STQ1_0 pattern table (format constant; reference src/kernels.c:178-181).
-__constant__ uint8_t c_stq_patterns[32] = {
-    0xA9, 0x89, 0x29, 0x09, 0xA6, 0x86, 0x26, 0x06, 0x9A, 0x92, 0x1A, 0x12, 0x6A, 0x62, 0x4A, 0x42,
-    0x01, 0x21, 0x81, 0xA1, 0x04, 0x24, 0x84, 0xA4, 0x10, 0x18, 0x90, 0x98, 0x40, 0x48, 0x60, 0x68,
-};
-
 // Native STQ1_0 / Q2_0C rows -> panel blocks (same bytes the host's
 // panel_repack_rows produces, reference src/kernels.c:535-561).  One thread
 // per (row, 256-block).
@@ -29,7 +23,7 @@ __global__ void panel_from_native(const uint8_t *raw, long long row_bytes, int t
         for (int g = 0; g < 64; g++) {
             const int slot = (blk[g >> 1] >> ((g & 1) * 4)) & 0x0f;
             const int sign = (blk[32 + (g >> 3)] >> (g & 7)) & 1;
-            out[piece_of_chunk(g >> 4) * 16 + (g & 15)] = c_stq_patterns[(sign << 4) | slot];
+            out[piece_of_chunk(g >> 4) * 16 + (g & 15)] = (uint8_t)stq_pattern((sign << 4) | slot);
         }
     } else {
         const uint8_t *blk = row + (size_t)(b >> 1) * 130;
@@ -47,6 +41,29 @@ __global__ void panel_from_native(const uint8_t *raw, long long row_bytes, int t
     }
     uint4 *dst = (uint4 *)(pk + (size_t)i * 64);
     for (int j = 0; j < 4; j++) dst[j] = ((const uint4 *)out)[j];
+}
+
+// Native STQ1_0 rows (42-byte blocks qs[32] | sign[8] | d) -> the FMT_STQN
+// planes: per row qs[nb*32] | sign[nb*8] | d[nb*2], the 8-byte qs chunks and
+// 2-byte sign chunks of block b in panel piece order (unit 4b + p holds chunk
+// piece_of_chunk(p)), the sign bits bit-sliced (stq_slice_signs).  The same
+// 42 bytes per 256 weights.  One thread per (row, block).
+__global__ void stqn_from_native(const uint8_t *raw, long long row_bytes, int n, int nb, uint8_t *dst,
+                                 long long stride) {
+    const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (long long)n * nb) return;
+    const int r = (int)(i / nb), b = (int)(i % nb);
+    const uint8_t *blk = raw + (size_t)r * row_bytes + (size_t)b * 42;
+    uint8_t *row = dst + (size_t)r * stride;
+    for (int p = 0; p < 4; p++) {
+        const int ch = piece_of_chunk(p);
+        for (int j = 0; j < 8; j++) row[(size_t)b * 32 + p * 8 + j] = blk[ch * 8 + j];
+        const uint32_t sg = stq_slice_signs((uint32_t)blk[32 + 2 * ch] | ((uint32_t)blk[33 + 2 * ch] << 8));
+        row[(size_t)nb * 32 + (size_t)b * 8 + p * 2] = (uint8_t)sg;
+        row[(size_t)nb * 32 + (size_t)b * 8 + p * 2 + 1] = (uint8_t)(sg >> 8);
+    }
+    row[(size_t)nb * 40 + (size_t)b * 2] = blk[40];
+    row[(size_t)nb * 40 + (size_t)b * 2 + 1] = blk[41];
 }
 
 // Q6_K 210-byte blocks -> per-row planes ql | qh | scales | d.
@@ -88,6 +105,14 @@ __device__ inline float dequant_elem(const WDesc &w, int r, int e) {
         const uint8_t byte = row[(size_t)b * 64 + piece_of_chunk(ch) * 16 + i];
         const int code = (byte >> (2 * l)) & 3;
         return (float)(code * (1 << w.shift) - w.off) * w.s[(size_t)r * nb + b];
+    }
+    case FMT_STQN: {
+        const int ch = x >> 6, l = (x >> 4) & 3, g = x & 15, u = b * 4 + piece_of_chunk(ch);
+        const int slot = (row[(size_t)u * 8 + (g >> 1)] >> ((g & 1) * 4)) & 15;
+        const uint32_t sg = row[(size_t)nb * 32 + u * 2] | ((uint32_t)row[(size_t)nb * 32 + u * 2 + 1] << 8);
+        const int sign = (sg >> (4 * (g & 3) + (g >> 2))) & 1;
+        const int code = (stq_pattern((sign << 4) | slot) >> (2 * l)) & 3;
+        return (float)(code - 1) * h2f((uint16_t)(row[(size_t)nb * 40 + 2 * b] | (row[(size_t)nb * 40 + 2 * b + 1] << 8)));
     }
     case FMT_Q6K: {
         const int half = x >> 7, q = (x & 127) >> 5, l = x & 31;

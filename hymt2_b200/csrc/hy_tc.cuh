@@ -80,7 +80,7 @@ __host__ __device__ inline size_t tc_smem_bytes(int P, int NM) {
 static_assert(tc_stages(1, 256) >= 4 && tc_stages(3, 64) >= 4, "tc pipeline too shallow");
 // Planes of a device weight format (0: not on the tensor-core path).
 __host__ __device__ constexpr int tc_planes(int fmt) {
-    return fmt == FMT_PANEL ? 1 : (fmt == FMT_Q6K ? 2 : (fmt == FMT_Q4K ? 3 : 0));
+    return (fmt == FMT_PANEL || fmt == FMT_STQN) ? 1 : (fmt == FMT_Q6K ? 2 : (fmt == FMT_Q4K ? 3 : 0));
 }
 
 // Byte offset of (row r, k) inside a canonical tile of R rows (any K).
@@ -217,7 +217,20 @@ __device__ __forceinline__ void tc_ld(uint32_t taddr, uint32_t (&r)[W]) {
     if constexpr (W == 16) tc_ld16(taddr, r);
     else tc_ld8(taddr, r);
 }
-__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Wait for this thread's tcgen05.ld results.  The loads write their
+// registers asynchronously, but the compiler sees those registers as defined
+// by the tcgen05.ld statement itself and may move arithmetic on them above a
+// wait that names no register.  So every destination register also passes
+// through an empty statement after the wait (asm volatile statements keep
+// their order), and each use depends on that statement's output.
+template <int P, int W>
+__device__ __forceinline__ void tc_wait_ld(uint32_t (&r)[P][W]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int p = 0; p < P; p++)
+#pragma unroll
+        for (int j = 0; j < W; j++) asm volatile("" : "+r"(r[p][j]));
+}
 
 // int32 -> fp32 for |v| < 2^22 without the conversion unit: the bits of
 // 1.5 * 2^23 + v.  Exact, so fmaf(tc_magic(v), s, -1.5 * 2^23 * s) rounds
@@ -387,7 +400,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                     uint32_t r[P][CW];
 #pragma unroll
                     for (int p = 0; p < P; p++) tc_ld<CW>(tbase + (uint32_t)(p * NM + c * CW), r[p]);
-                    tc_wait_ld();
+                    tc_wait_ld(r);
                     if constexpr (INTS) {
                         const int nmax = a.N[wi];
                         for (int j = 0; j < CW; j++) {
@@ -403,14 +416,6 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                                 a.ints[(o * nb + kb) * 2 + 1] = (int)r[2][j];
                             }
                         }
-                    }
-                    if constexpr (C / CW == 1) {
-                        // every TMEM word of this block is in registers: hand the accumulator set
-                        // back to the MMA warp before the arithmetic (the scale slot, which the
-                        // arithmetic still reads, is released after it)
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) tc_mbar_arrive(&acce[buf]);
                     }
 #pragma unroll
                     for (int j4 = 0; j4 < CW / 4; j4++) {
@@ -434,16 +439,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) tc_gemm(const __grid_constant__
                         }
                     }
                 }
-                if constexpr (C / CW == 1) {
-                    __syncwarp();
-                    if (lane == 0) tc_mbar_arrive(&sempty[sl]);
-                } else {
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) {
-                        tc_mbar_arrive(&acce[buf]);
-                        tc_mbar_arrive(&sempty[sl]);
-                    }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    tc_mbar_arrive(&acce[buf]);
+                    tc_mbar_arrive(&sempty[sl]);
                 }
             }
             if (ok && t < a.T) {
@@ -491,8 +491,16 @@ __device__ inline void tc_elem(const WDesc &w, int r, int b, int x, int (&v)[P])
     const int nb = w.k / 256;
     if constexpr (P == 1) {
         const int ch = x >> 6, l = (x >> 4) & 3, i = x & 15;
-        const uint8_t byte = row[(size_t)b * 64 + piece_of_chunk(ch) * 16 + i];
-        v[0] = ((byte >> (2 * l)) & 3) * (1 << w.shift) - w.off;
+        uint32_t byte;
+        if (w.fmt == FMT_STQN) {
+            const int u = b * 4 + piece_of_chunk(ch);
+            const int slot = (row[(size_t)u * 8 + (i >> 1)] >> ((i & 1) * 4)) & 15;
+            const uint32_t sg = row[(size_t)nb * 32 + u * 2] | ((uint32_t)row[(size_t)nb * 32 + u * 2 + 1] << 8);
+            byte = stq_pattern((int)(((sg >> (4 * (i & 3) + (i >> 2))) & 1) << 4) | slot);
+        } else {
+            byte = row[(size_t)b * 64 + piece_of_chunk(ch) * 16 + i];
+        }
+        v[0] = (int)((byte >> (2 * l)) & 3) * (1 << w.shift) - w.off;
     } else if constexpr (P == 2) {
         const int half = x >> 7, q = (x & 127) >> 5, l = x & 31;
         const uint8_t lb = row[(size_t)b * 128 + half * 64 + l + (q & 1) * 32];
@@ -522,7 +530,8 @@ __device__ inline void tc_block_scales(const WDesc &w, int r, int b, float &s1, 
     const uint8_t *row = w.w + (size_t)r * w.stride;
     const int nb = w.k / 256;
     if constexpr (P == 1) {
-        s1 = w.s[(size_t)r * nb + b];
+        s1 = w.fmt == FMT_STQN ? h2f((uint16_t)(row[(size_t)nb * 40 + 2 * b] | (row[(size_t)nb * 40 + 2 * b + 1] << 8)))
+                               : w.s[(size_t)r * nb + b];
         s2 = -kTcMagic * s1;  // exact: s1 is an f16 value
     } else if constexpr (P == 2) {
         s1 = h2f((uint16_t)(row[(size_t)nb * 208 + 2 * b] | (row[(size_t)nb * 208 + 2 * b + 1] << 8)));

@@ -60,6 +60,12 @@ class Backend:
         self.lib.hyc_last_error(self.impl, buf, 512)
         return buf.value.decode()
 
+    def set_stq_layout(self, native: bool) -> None:
+        """STQ1_0 weights uploaded from now on: panels (False) or the native
+        42 B / 256 blocks decoded in registers (True)."""
+        if self.lib.hyc_set_stq_layout(self.impl, 1 if native else 0) != 0:
+            raise BackendError("hyc_set_stq_layout failed")
+
     def upload(self, w: abi.WeightT) -> int:
         h = self.ops.upload(self.impl, C.byref(w))
         if not h:

@@ -111,6 +111,17 @@ HYC_API int hyc_set_decode_mode(void *impl, int mode);
  * GEMM on host inputs (act as hyc_gemv_test: 1 plain, 2 RMSNorm*w,
  * 3 SiLU(x)*x2; nt 1..256) and writes out[t*n + r]. */
 HYC_API int hyc_set_tc(void *impl, int on);
+/* STQ1_0 weight layout for later uploads (replaces the panel decision of
+ * reference src/model.c:385-388, which always uploads the host-built panel):
+ * native == 0 (the default) stores the panel (64 B of 2-bit codes + an fp32
+ * scale per 256 weights, 68 B); native != 0 stores the file's own 42-byte
+ * blocks (weight_t.data, row_bytes = 42 * k / 256), split per row into
+ * qs | sign | d planes and decoded in registers by the GEMV kernels, with the
+ * same per-block integers (reference stq1_0_dot_scalar, src/kernels.c:202-215).
+ * The environment variable HYMT2_STQ_LAYOUT=native sets it at hyc_create.
+ * The persistent decode kernel takes panels only; native layers decode
+ * through the per-layer graph. */
+HYC_API int hyc_set_stq_layout(void *impl, int native);
 HYC_API int hyc_tc_test(void *impl, hy_dweight *w, int act, const float *x, const float *x2, const float *norm_w,
                         float eps, int nt, float *out);
 HYC_API int hyc_decode_path(void *impl, char *why, int cap);
