@@ -364,6 +364,8 @@ def bench_serving(dm, stream, torch, rank, world, nreq, max_over_ranks, barrier,
             "step_token_budget": SERVE_STEP_TOKENS, "ms": round(ms, 2), "wall_s_rank0": round(wall, 3),
             "steps_rank0": st["steps"], "prefill_tokens_rank0": st["prefill_tokens"],
             "prefix_hits_rank0": st["prefix_hits"], "prefix_tokens_rank0": st["prefix_tokens"],
+            "kv_pages_shared_rank0": st["shared_pages"], "kv_rows_copied_rank0": st["copied_rows"],
+            "kv_pages_evicted_rank0": st["evictions"],
             "tokens_per_s_incl_prefill": round((st["decode_tokens"] + st["prefill_tokens"]) * world / (ms / 1e3), 1),
             "workload": "c3: c0_stq model, 4096 requests (prompt U[16,128] ids with a shared 24-token prefix), "
                         "64 greedy tokens each, continuous batching <= 256 sequences per GPU, requests sharded "

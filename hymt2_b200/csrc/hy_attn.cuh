@@ -9,6 +9,7 @@
 // contexts with a last-CTA log-sum-exp merge.
 #pragma once
 #include "hy_common.cuh"
+#include "hy_pages.h"
 
 namespace hyk {
 
@@ -29,10 +30,14 @@ struct AttnArgs {
     int max_chunks, units;  // attn_max_chunks(ctx); units available (SMs)
     int trace;              // timeline slot (< 0: off)
     // ragged batch of several sequences (prefill kernels only): token t sits
-    // at position tok_pos[t] of sequence slot tok_slot[t], whose cache starts
-    // slot_stride elements after the previous slot's (kc/vc: slot 0)
+    // at position tok_pos[t] of sequence slot tok_slot[t], whose cache is
+    // paged: row pos of a slot is row pos % kPageRows of page
+    // pages[slot * page_max + pos / kPageRows], page_stride elements per page
+    // (kc / vc: page 0's K / V rows of this layer)
     const int *tok_pos, *tok_slot;
-    long long slot_stride;
+    const int *pages;
+    int page_max;
+    long long page_stride;
     // query blocks of the tensor-core prefill kernel: (first token, count)
     // pairs of <= kFaQ consecutive positions of one slot; null: tokens
     // 16b .. 16b+15 of one sequence
@@ -40,10 +45,15 @@ struct AttnArgs {
     int nqb;
 };
 
-// Position of token t and the element offset of its sequence's cache.
+// Position and sequence slot of token t, and the element offset (from kc /
+// vc) of row pos of slot's cache: contiguous rows for the single-sequence
+// cache, page-table rows for a batch.
 __device__ __forceinline__ int attn_tok_pos(const AttnArgs &a, int t) { return a.tok_pos ? a.tok_pos[t] : *a.pos_ptr + t; }
-__device__ __forceinline__ long long attn_tok_kv(const AttnArgs &a, int t) {
-    return a.tok_slot ? (long long)a.tok_slot[t] * a.slot_stride : 0;
+__device__ __forceinline__ int attn_tok_slot(const AttnArgs &a, int t) { return a.tok_slot ? a.tok_slot[t] : 0; }
+__device__ __forceinline__ long long attn_kv_row(const AttnArgs &a, int slot, int pos) {
+    if (!a.pages) return (long long)pos * a.kvdim;
+    return (long long)__ldg(a.pages + slot * a.page_max + (pos >> kPageShift)) * a.page_stride +
+           (long long)(pos & (kPageRows - 1)) * a.kvdim;
 }
 
 // NeoX rotation + per-head RMSNorm of one head held as v[i] = x[lane + 32 i].
@@ -80,7 +90,7 @@ __global__ void rope_norm_store(const __grid_constant__ AttnArgs a) {
     // the grid strides over the tokens (a few CTAs per SM, not one per token)
     for (int t = blockIdx.x; t < a.nt; t += gridDim.x) {
     const int pos = attn_tok_pos(a, t);
-    const long long kvo = attn_tok_kv(a, t);
+    const long long kvr = attn_kv_row(a, attn_tok_slot(a, t), pos);
     const float *cs = a.rope_cos + (size_t)pos * a.half, *sn = a.rope_sin + (size_t)pos * a.half;
     float *row = a.qkv + (size_t)t * a.qkv_ld;
     for (int hh = w; hh < a.heads + a.kv_heads; hh += blockDim.x >> 5) {
@@ -96,8 +106,7 @@ __global__ void rope_norm_store(const __grid_constant__ AttnArgs a) {
         } else {
             const int kvh = hh - a.heads;
             const float *vs = row + a.qdim + a.kvdim + kvh * HD;
-            uint16_t *kd = a.kc + kvo + (size_t)pos * a.kvdim + kvh * HD,
-                     *vd = a.vc + kvo + (size_t)pos * a.kvdim + kvh * HD;
+            uint16_t *kd = a.kc + kvr + kvh * HD, *vd = a.vc + kvr + kvh * HD;
 #pragma unroll
             for (int i = 0; i < HD / 32; i++) {
                 kd[lane + 32 * i] = f32_to_bf16_bits(v[i]);
@@ -851,8 +860,8 @@ __host__ __device__ constexpr size_t prefill_stage_bytes() {
 // rows go to this warp's shared buffer sv (cp.async) before the scores, and
 // each lane loads its key's whole K row into registers.
 template <int HD, int G>
-__device__ __forceinline__ void attend_range_staged(const AttnArgs &a, const uint16_t *kc, const uint16_t *vc, int kvh,
-                                                    int j1, const float (*sq)[HD], uint16_t *sv, float (&m)[G],
+__device__ __forceinline__ void attend_range_staged(const AttnArgs &a, int slot, int kvh, int j1,
+                                                    const float (*sq)[HD], uint16_t *sv, float (&m)[G],
                                                     float (&l)[G], float (&o)[G][HD / 32]) {
     constexpr int CH = HD / 8;  // 16-byte chunks per row
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -863,12 +872,12 @@ __device__ __forceinline__ void attend_range_staged(const AttnArgs &a, const uin
 #pragma unroll
         for (int i = 0; i < HD / 32; i++) o[h][i] = 0.f;
     }
-    const uint16_t *Kb = kc + kvh * HD, *Vb = vc + kvh * HD;
+    const uint16_t *Kb = a.kc + kvh * HD, *Vb = a.vc + kvh * HD;
     for (int tile = w * 32; tile < j1; tile += G * 32) {
         const int nk = min(32, j1 - tile);
         for (int i = lane; i < nk * CH; i += 32) {
             const int r = i / CH, c = i - r * CH;
-            cp_async16(sv + r * HD + c * 8, Vb + (size_t)(tile + r) * a.kvdim + c * 8);
+            cp_async16(sv + r * HD + c * 8, Vb + attn_kv_row(a, slot, tile + r) + c * 8);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
         const int j = tile + lane;
@@ -877,7 +886,7 @@ __device__ __forceinline__ void attend_range_staged(const AttnArgs &a, const uin
 #pragma unroll
         for (int h = 0; h < G; h++) s[h] = 0.f;
         if (valid) {
-            const uint16_t *kr = Kb + (size_t)j * a.kvdim;
+            const uint16_t *kr = Kb + attn_kv_row(a, slot, j);
             uint4 kk[CH];
 #pragma unroll
             for (int c = 0; c < CH; c++) kk[c] = *(const uint4 *)(kr + c * 8);
@@ -938,13 +947,12 @@ __global__ void __launch_bounds__(G * 32) attn_prefill(const __grid_constant__ A
     const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_wait();
     const int pos = attn_tok_pos(a, t);
-    const long long kvo = attn_tok_kv(a, t);
     const float *qr = a.qkv + (size_t)t * a.qkv_ld + (kvh * G + w) * HD;
 #pragma unroll
     for (int i = 0; i < HD / 32; i++) S.sq[w][lane + 32 * i] = qr[lane + 32 * i];
     __syncthreads();
     float m[G], l[G], o[G][HD / 32];
-    attend_range_staged<HD, G>(a, a.kc + kvo, a.vc + kvo, kvh, pos + 1, S.sq, (uint16_t *)dsm + w * 32 * HD, m, l, o);
+    attend_range_staged<HD, G>(a, attn_tok_slot(a, t), kvh, pos + 1, S.sq, (uint16_t *)dsm + w * 32 * HD, m, l, o);
 #pragma unroll
     for (int h = 0; h < G; h++) {
         if (lane == 0) {
@@ -1022,18 +1030,19 @@ __device__ __forceinline__ void fa_ldm4t(uint32_t (&r)[4], const void *p) {
 
 // Stage keys [k0, k0 + kFaK) (rows past kend zero-filled) of K and V.
 template <int HD, int G>
-__device__ __forceinline__ void fa_stage(const uint16_t *Kg, const uint16_t *Vg, int kvdim, int k0, int kend,
-                                         uint16_t *sk, uint16_t *sv) {
+__device__ __forceinline__ void fa_stage(const AttnArgs &a, const uint16_t *Kg, const uint16_t *Vg, int slot, int k0,
+                                         int kend, uint16_t *sk, uint16_t *sv) {
     constexpr int CH = HD / 8;  // 16-byte chunks per row
     for (int i = threadIdx.x; i < kFaK * CH; i += G * 32) {
         const int r = i / CH, c = i % CH, key = k0 + r;
         uint16_t *dk = sk + r * fa_row<HD>() + c * 8, *dv = sv + r * fa_row<HD>() + c * 8;
         if (key < kend) {
+            const long long ro = attn_kv_row(a, slot, key);
             asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dk)),
-                         "l"(Kg + (size_t)key * kvdim + c * 8)
+                         "l"(Kg + ro + c * 8)
                          : "memory");
             asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dv)),
-                         "l"(Vg + (size_t)key * kvdim + c * 8)
+                         "l"(Vg + ro + c * 8)
                          : "memory");
         } else {
             *(uint4 *)dk = make_uint4(0, 0, 0, 0);
@@ -1062,7 +1071,7 @@ __global__ void __launch_bounds__(G * 32) attn_fa(const __grid_constant__ AttnAr
         nq = min(kFaQ, a.nt - t0);
     }
     const int pos0 = attn_tok_pos(a, t0);  // the block's positions are pos0 .. pos0 + nq - 1
-    const long long kvo = attn_tok_kv(a, t0);
+    const int slot = attn_tok_slot(a, t0);
     const int kend = pos0 + nq;
     const int head = kvh * G + w;
     // q rows of this warp's head -> bf16 terms (rows past nq repeat the last token)
@@ -1075,9 +1084,9 @@ __global__ void __launch_bounds__(G * 32) attn_fa(const __grid_constant__ AttnAr
 #pragma unroll
         for (int x = 0; x < kFaTerms; x++) *(uint32_t *)(qs + ((size_t)(x * G + w) * kFaQ + r) * R + d) = tt[x];
     }
-    const uint16_t *Kg = a.kc + kvo + kvh * HD, *Vg = a.vc + kvo + kvh * HD;
+    const uint16_t *Kg = a.kc + kvh * HD, *Vg = a.vc + kvh * HD;
     const int ntiles = (kend + kFaK - 1) / kFaK;
-    fa_stage<HD, G>(Kg, Vg, a.kvdim, 0, kend, sk0, sk0 + kFaK * R);
+    fa_stage<HD, G>(a, Kg, Vg, slot, 0, kend, sk0, sk0 + kFaK * R);
     const int qp0 = pos0 + min(g, nq - 1), qp1 = pos0 + min(g + 8, nq - 1);  // positions of rows g, g + 8
     float o[NT][4];
 #pragma unroll
@@ -1088,7 +1097,7 @@ __global__ void __launch_bounds__(G * 32) attn_fa(const __grid_constant__ AttnAr
         uint16_t *sk = sk0 + (size_t)(kt & 1) * 2 * kFaK * R, *sv = sk + kFaK * R;
         if (kt + 1 < ntiles) {
             uint16_t *nk = sk0 + (size_t)((kt + 1) & 1) * 2 * kFaK * R;
-            fa_stage<HD, G>(Kg, Vg, a.kvdim, (kt + 1) * kFaK, kend, nk, nk + kFaK * R);
+            fa_stage<HD, G>(a, Kg, Vg, slot, (kt + 1) * kFaK, kend, nk, nk + kFaK * R);
             asm volatile("cp.async.wait_group 1;" ::: "memory");
         } else {
             asm volatile("cp.async.wait_group 0;" ::: "memory");

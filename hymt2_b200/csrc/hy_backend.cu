@@ -737,10 +737,12 @@ bool ffn_pair_ok(const Layer &L, int nt) {
 // a ragged batch (token t at tok_pos[t] of sequence slot tok_slot[t]).
 struct Fwd {
     float *h, *qkv, *ao, *g, *u;  // [tokens][H | qd + 2 kvd | qd | F | F]
-    uint16_t *kv;                 // layer li's K cache at kv + li * layer_stride, V kv_ctx rows later
+    uint16_t *kv;                 // layer li's K cache at kv + li * layer_stride, V v_rows rows later
     size_t layer_stride;
-    long long slot_stride;        // elements between two slots' caches (batch)
-    int kv_ctx;
+    const int *pages;             // batch: page table [slot][page_max] (hy_pages.h), page_stride elements a page
+    int page_max;
+    long long page_stride;
+    int kv_ctx, v_rows;
     const int *pos_ptr;
     const int *tok_pos, *tok_slot;
     const int *qblk;              // batch: attention query blocks (first token, count)
@@ -758,6 +760,7 @@ Fwd fwd_single(HyCtx *c, const int *pos_ptr) {
     f.kv = c->d_kv;
     f.layer_stride = (size_t)2 * c->ctx * c->kvd;
     f.kv_ctx = c->ctx;
+    f.v_rows = c->ctx;
     f.pos_ptr = pos_ptr;
     return f;
 }
@@ -856,7 +859,7 @@ bool layer_forward(HyCtx *c, const Fwd &f, int li, int nt, bool pdl) {
         aa.qkv = f.qkv;
         aa.qkv_ld = qkv_ld;
         aa.kc = f.kv + (size_t)li * f.layer_stride;
-        aa.vc = aa.kc + (size_t)f.kv_ctx * c->kvd;
+        aa.vc = aa.kc + (size_t)f.v_rows * c->kvd;
         aa.q_norm = L.q_norm;
         aa.k_norm = L.k_norm;
         aa.rope_cos = c->d_cos;
@@ -864,7 +867,9 @@ bool layer_forward(HyCtx *c, const Fwd &f, int li, int nt, bool pdl) {
         aa.pos_ptr = f.pos_ptr;
         aa.tok_pos = f.tok_pos;
         aa.tok_slot = f.tok_slot;
-        aa.slot_stride = f.slot_stride;
+        aa.pages = f.pages;
+        aa.page_max = f.page_max;
+        aa.page_stride = f.page_stride;
         aa.qblk = f.qblk;
         aa.nqb = f.nqb;
         aa.nt = nt;
@@ -1901,7 +1906,7 @@ HYC_API int hyc_batch_kv_copy(void *impl, int src_slot, int dst_slot, int npos) 
     HyCtx *c = (HyCtx *)impl;
     if (!c || c->broken || !c->bat || cudaSetDevice(c->dev) != cudaSuccess) return -1;
     const Batch &b = *c->bat;
-    if (src_slot < 0 || src_slot > b.slots || dst_slot < 0 || dst_slot > b.slots || npos < 0 || npos > b.slot_ctx)
+    if (src_slot < 0 || src_slot >= b.slots || dst_slot < 0 || dst_slot >= b.slots || npos < 0 || npos > b.slot_ctx)
         return -1;
     return kv_copy(c, src_slot, dst_slot, npos) && cudaStreamSynchronize(c->st) == cudaSuccess ? 0 : -1;
 }
@@ -1910,14 +1915,19 @@ HYC_API int hyc_batch_kv_read(void *impl, int slot, int layer, int npos, uint16_
     HyCtx *c = (HyCtx *)impl;
     if (!c || c->broken || !c->bat || !k || !v || cudaSetDevice(c->dev) != cudaSuccess) return -1;
     const Batch &b = *c->bat;
-    if (slot < 0 || slot > b.slots || layer < 0 || layer >= c->L || npos < 1 || npos > b.slot_ctx) return -1;
-    const uint16_t *kc = b.kv + (size_t)layer * b.layer_stride(c) + (size_t)slot * b.slot_stride(c);
-    const uint16_t *vc = kc + (size_t)b.slot_ctx * c->kvd;
-    if (cudaMemcpyAsync(k, kc, (size_t)npos * c->kvd * 2, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
-        cudaMemcpyAsync(v, vc, (size_t)npos * c->kvd * 2, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
-        cudaStreamSynchronize(c->st) != cudaSuccess)
-        return -1;
-    return 0;
+    if (slot < 0 || slot >= b.slots || layer < 0 || layer >= c->L || npos < 1 || npos > b.slot_ctx) return -1;
+    // page by page through the slot's row of the page table
+    for (int j = 0; j * kPageRows < npos; j++) {
+        const int n = npos - j * kPageRows < kPageRows ? npos - j * kPageRows : kPageRows;
+        const uint16_t *kc = b.kv + (size_t)layer * b.layer_stride(c) +
+                             (size_t)b.h_pages[slot * b.page_max + j] * b.page_stride(c);
+        const uint16_t *vc = kc + (size_t)kPageRows * c->kvd;
+        const size_t o = (size_t)j * kPageRows * c->kvd, bytes = (size_t)n * c->kvd * 2;
+        if (cudaMemcpyAsync(k + o, kc, bytes, cudaMemcpyDeviceToHost, c->st) != cudaSuccess ||
+            cudaMemcpyAsync(v + o, vc, bytes, cudaMemcpyDeviceToHost, c->st) != cudaSuccess)
+            return -1;
+    }
+    return cudaStreamSynchronize(c->st) == cudaSuccess ? 0 : -1;
 }
 
 HYC_API int hyc_serve(void *impl, const int *prompts, const int *prompt_off, int nreq, int max_new,

@@ -3,28 +3,35 @@
 // HyCtx, the layer loop and the tensor-core linear defined there).
 //
 // A batch is a list of tokens, token t at position tok_pos[t] of sequence
-// slot tok_slot[t].  Every slot owns a bf16 KV cache of slot_ctx rows per
-// layer, laid out [L][slots + 1][K | V][slot_ctx][kvdim]; slot `slots` holds
-// the server's shared-prefix cache.  One forward pass embeds every token,
-// runs all layers over the whole batch (tensor-core GEMMs from kTcMinTokens
-// tokens up, so a step of 256 decode tokens or a 32 x 256 prefill is one
-// GEMM per projection), then the LM head over the selected rows with one
-// argmax per row (reference semantics: first maximum wins, src/model.c:945-948).
+// slot tok_slot[t].  The bf16 KV cache is paged: pages of kPageRows
+// positions, laid out [L][npages][K | V][kPageRows][kvdim], and a page table
+// [slots][page_max] maps (slot, pos / kPageRows) to a page.  The direct
+// batch API gives slot s the pages s * page_max + j; the server allocates
+// pages as its sequences grow and shares cached prompt pages between
+// requests (hy_pages.h).  One forward pass embeds every token, runs all
+// layers over the whole batch (tensor-core GEMMs from kTcMinTokens tokens
+// up, so a step of 256 decode tokens or a 32 x 256 prefill is one GEMM per
+// projection), then the LM head over the selected rows with one argmax per
+// row (reference semantics: first maximum wins, src/model.c:945-948).
 //
 // The server (reference gen_ids, src/model.c:914-958, for many requests at
 // once; a request ends at max_new ids or at its first stop id, which then
-// frees its slot): every step feeds one token of each decoding sequence plus prompt
-// chunks of newly admitted ones, up to a token budget; a request whose
-// prompt shares at least kServeMinPrefix leading tokens with the cached
-// prefix starts from a device copy of those KV rows (the reference's
-// longest-common-prefix reuse, src/model.c:931-936, across requests), and
-// the last prompt token is always recomputed for its logits.
-
-constexpr int kServeMinPrefix = 8;  // shortest shared prefix worth a cache copy
+// frees its slot and its pages): every step feeds one token of each decoding
+// sequence plus prompt chunks of newly admitted ones, up to a token budget.
+// An admitted prompt first takes the longest chain of cached full pages
+// matching its leading tokens by reference, then copies the matching first
+// rows of one cached page that continues the chain (the reference's
+// longest-common-prefix reuse, src/model.c:931-936, against every cached
+// prompt instead of the previous one); the last prompt token is always
+// recomputed for its logits.  When a prompt has been fed, its full pages are
+// sealed into the cache.
 
 struct Batch {
     int slots = 0, slot_ctx = 0, max_tokens = 0, max_out = 0;
+    int page_max = 0;  // pages per slot: ceil(slot_ctx / kPageRows)
+    int npages = 0;    // device pages: slots * page_max for the slots, the rest for cached prompt pages
     uint16_t *kv = nullptr;
+    int *d_pages = nullptr, *h_pages = nullptr;  // page table [slots][page_max] (h: pinned copy)
     float *h = nullptr, *qkv = nullptr, *ao = nullptr, *g = nullptr, *u = nullptr;
     // tok [max_tokens] | slot [max_tokens] | pos [max_tokens] | rows [max_out] | qblk [2 max_tokens]
     int *d_in = nullptr;
@@ -33,9 +40,14 @@ struct Batch {
     float *sel = nullptr;  // [max_out][H] residual rows for the head
     float *logits = nullptr;  // [max_out][vocab]
     int *d_ids = nullptr, *h_ids = nullptr;
-    size_t kv_elems(const HyCtx *c) const { return (size_t)c->L * (slots + 1) * 2 * slot_ctx * c->kvd; }
-    long long slot_stride(const HyCtx *c) const { return (long long)2 * slot_ctx * c->kvd; }
-    size_t layer_stride(const HyCtx *c) const { return (size_t)(slots + 1) * 2 * slot_ctx * c->kvd; }
+    long long page_stride(const HyCtx *c) const { return (long long)2 * kPageRows * c->kvd; }
+    size_t layer_stride(const HyCtx *c) const { return (size_t)npages * page_stride(c); }
+    size_t kv_elems(const HyCtx *c) const { return (size_t)c->L * layer_stride(c); }
+    // the direct batch API's table: slot s owns pages s * page_max + j
+    void identity_pages() {
+        for (int sl = 0; sl < slots; sl++)
+            for (int j = 0; j < page_max; j++) h_pages[sl * page_max + j] = sl * page_max + j;
+    }
     int *tok() const { return d_in; }
     int *slot() const { return d_in + max_tokens; }
     int *pos() const { return d_in + 2 * max_tokens; }
@@ -81,14 +93,15 @@ __global__ void __launch_bounds__(1024) rows_argmax(const float *logits, long lo
     }
 }
 
-// Rows [0, npos) of every layer's K and V cache: slot src -> slot dst.
-// grid (layers, 2); 16-byte words.
-__global__ void kv_copy_rows(uint16_t *kv, size_t layer_stride, long long slot_stride, long long v_off, int src, int dst,
-                             long long words) {
-    const size_t base = (size_t)blockIdx.x * layer_stride + (blockIdx.y ? (size_t)v_off : 0);
-    const uint4 *s = (const uint4 *)(kv + base + (size_t)src * slot_stride);
-    uint4 *d = (uint4 *)(kv + base + (size_t)dst * slot_stride);
-    for (long long i = threadIdx.x; i < words; i += blockDim.x) d[i] = s[i];
+// Rows [0, nrows) of page src -> page dst, K and V of every layer; grid
+// (layers, 2); 16-byte words.
+__global__ void kv_copy_page(uint16_t *kv, size_t layer_stride, long long page_stride, int kvd, int src, int dst,
+                             int nrows) {
+    const size_t base = (size_t)blockIdx.x * layer_stride + (blockIdx.y ? (size_t)kPageRows * kvd : 0);
+    const uint4 *s = (const uint4 *)(kv + base + (size_t)src * page_stride);
+    uint4 *d = (uint4 *)(kv + base + (size_t)dst * page_stride);
+    const int words = nrows * kvd / 8;
+    for (int i = threadIdx.x; i < words; i += blockDim.x) d[i] = s[i];
 }
 
 // ---------------------------------------------------------------- host side
@@ -106,6 +119,8 @@ void batch_free(HyCtx *c) {
     cudaFree(b->sel);
     cudaFree(b->logits);
     cudaFree(b->d_ids);
+    cudaFree(b->d_pages);
+    if (b->h_pages) cudaFreeHost(b->h_pages);
     if (b->h_in) cudaFreeHost(b->h_in);
     if (b->h_ids) cudaFreeHost(b->h_ids);
     delete b;
@@ -128,9 +143,17 @@ bool batch_prepare(HyCtx *c, int slots, int slot_ctx, int max_tokens, int max_ou
     b->slot_ctx = slot_ctx;
     b->max_tokens = max_tokens;
     b->max_out = max_out;
+    b->page_max = (slot_ctx + kPageRows - 1) / kPageRows;
+    // the slots' own pages, plus a quarter more (at least one slot's worth)
+    // that keeps finished prompts' pages cached for later requests
+    b->npages = slots * b->page_max + (slots * b->page_max / 4 > b->page_max ? slots * b->page_max / 4 : b->page_max);
     const size_t T = (size_t)max_tokens;
     CK(c, cudaMalloc(&b->kv, b->kv_elems(c) * 2));
     CK(c, cudaMemsetAsync(b->kv, 0, b->kv_elems(c) * 2, c->st));
+    CK(c, cudaMalloc(&b->d_pages, (size_t)slots * b->page_max * 4));
+    CK(c, cudaMallocHost(&b->h_pages, (size_t)slots * b->page_max * 4));
+    b->identity_pages();
+    CK(c, cudaMemcpyAsync(b->d_pages, b->h_pages, (size_t)slots * b->page_max * 4, cudaMemcpyHostToDevice, c->st));
     CK(c, cudaMalloc(&b->h, T * c->H * 4));
     CK(c, cudaMalloc(&b->qkv, T * (c->qd + 2 * c->kvd) * 4));
     CK(c, cudaMalloc(&b->ao, T * c->qd * 4));
@@ -158,8 +181,11 @@ Fwd fwd_batch(HyCtx *c) {
     f.u = b.u;
     f.kv = b.kv;
     f.layer_stride = b.layer_stride(c);
-    f.slot_stride = b.slot_stride(c);
+    f.pages = b.d_pages;
+    f.page_max = b.page_max;
+    f.page_stride = b.page_stride(c);
     f.kv_ctx = b.slot_ctx;
+    f.v_rows = kPageRows;
     f.tok_pos = b.pos();
     f.tok_slot = b.slot();
     f.qblk = b.d_in + b.qblk_off();
@@ -234,35 +260,60 @@ bool batch_run(HyCtx *c, int nt, int nout, int vocab_out) {
                   vocab_out, b.d_ids);
 }
 
+bool kv_copy_rows(HyCtx *c, int src_page, int dst_page, int nrows) {
+    Batch &b = *c->bat;
+    if (nrows < 1) return true;
+    return launch(c, kv_copy_page, dim3(c->L, 2), dim3(256), 0, false, b.kv, b.layer_stride(c), b.page_stride(c),
+                  c->kvd, src_page, dst_page, nrows);
+}
+
+// Rows 0 .. npos - 1 of slot src -> slot dst through the current page table.
 bool kv_copy(HyCtx *c, int src, int dst, int npos) {
     Batch &b = *c->bat;
-    const long long words = (long long)npos * c->kvd * 2 / 16;
-    if (words < 1) return true;
-    return launch(c, kv_copy_rows, dim3(c->L, 2), dim3(256), 0, false, b.kv, b.layer_stride(c), b.slot_stride(c),
-                  (long long)b.slot_ctx * c->kvd, src, dst, words);
+    for (int j = 0; j * kPageRows < npos; j++) {
+        const int n = npos - j * kPageRows < kPageRows ? npos - j * kPageRows : kPageRows;
+        if (!kv_copy_rows(c, b.h_pages[src * b.page_max + j], b.h_pages[dst * b.page_max + j], n)) return false;
+    }
+    return true;
 }
 
 // ---------------------------------------------------------------- server
 
 struct ServeSeq {
     int req, slot, n, fed, gen, last;
-    bool stopped;  // emitted a stop id
+    bool stopped;            // emitted a stop id
+    bool sealed;             // its prompt pages went into the cache
+    std::vector<int> pages;  // its page table row
 };
 
 bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_new, const int *stop_ids, int n_stop,
                int vocab_out, int step_tokens, int *out, int *out_len, hyc_serve_stats *st) {
     Batch &b = *c->bat;
-    const int S = b.slots, T = b.max_tokens;
+    const int S = b.slots, T = b.max_tokens, PM = b.page_max;
     REQ(c, step_tokens >= 1 && step_tokens <= T, "step token budget exceeds the batch capacity");
     REQ(c, max_new >= 1 && b.max_out >= S, "batch head rows must cover every slot");
     for (int r = 0; r < nreq; r++) {
         const int n = off[r + 1] - off[r];
         REQ(c, n >= 1 && n + max_new - 1 <= b.slot_ctx, "request does not fit a slot's context");
     }
+    PagePool pool;
+    pool.reset(b.npages);
+    for (int i = 0; i < S * PM; i++) b.h_pages[i] = 0;  // rows of idle slots are never read
+    bool table_dirty = true;
+    // the page holding position pos of q, allocated (with any before it) on first use
+    auto need_page = [&](ServeSeq &q, int pos) -> bool {
+        while ((int)q.pages.size() <= (pos >> kPageShift)) {
+            const int pg = pool.alloc();
+            REQ(c, pg >= 0, "KV page pool exhausted");
+            b.h_pages[q.slot * PM + (int)q.pages.size()] = pg;
+            q.pages.push_back(pg);
+            table_dirty = true;
+        }
+        return true;
+    };
     std::vector<int> free_slots;
     for (int s = S - 1; s >= 0; s--) free_slots.push_back(s);
     std::vector<ServeSeq> act;
-    std::vector<int> ptoks;  // tokens whose KV rows the prefix slot holds
     int next = 0, done = 0;
     std::vector<int> row_seq;
     memset(st, 0, sizeof *st);
@@ -280,15 +331,27 @@ bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_n
             q.gen = 0;
             q.last = -1;
             q.stopped = false;
+            q.sealed = false;
             const int *p = prompts + off[q.req];
-            int l = 0;
-            const int lmax = (int)ptoks.size() < q.n - 1 ? (int)ptoks.size() : q.n - 1;
-            while (l < lmax && p[l] == ptoks[l]) l++;
-            if (l >= kServeMinPrefix) {
-                if (!kv_copy(c, S, q.slot, l)) return false;
-                q.fed = l;
+            // cached prefix: whole pages by reference, then a copy of the first rows of one more
+            PagePool::Match m = pool.match(p, q.n - 1);
+            for (size_t j = 0; j < m.full.size(); j++) {
+                b.h_pages[q.slot * PM + (int)j] = m.full[j];
+                q.pages.push_back(m.full[j]);
+            }
+            table_dirty = table_dirty || !m.full.empty();
+            if (m.src >= 0 && m.src_rows > 0) {
+                pool.ref(m.src);  // not evictable while this request takes its own page
+                const bool ok = need_page(q, m.rows - 1) && kv_copy_rows(c, m.src, q.pages.back(), m.src_rows);
+                pool.unref(m.src);
+                if (!ok) return false;
+                st->copied_rows += m.src_rows;
+            }
+            q.fed = m.rows;
+            if (m.rows > 0) {
                 st->prefix_hits++;
-                st->prefix_tokens += l;
+                st->prefix_tokens += m.rows;
+                st->shared_pages += (long long)m.full.size();
             }
             act.push_back(q);
         }
@@ -298,6 +361,7 @@ bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_n
         for (size_t i = 0; i < act.size(); i++) {
             ServeSeq &q = act[i];
             if (q.fed < q.n || nt >= step_tokens) continue;
+            if (!need_page(q, q.n + q.gen - 1)) return false;
             h_tok[nt] = q.last;
             h_slot[nt] = q.slot;
             h_pos[nt] = q.n + q.gen - 1;
@@ -310,6 +374,7 @@ bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_n
             if (q.fed >= q.n) continue;
             const int *p = prompts + off[q.req];
             const int take = (q.n - q.fed) < (step_tokens - nt) ? (q.n - q.fed) : (step_tokens - nt);
+            if (!need_page(q, q.fed + take - 1)) return false;
             for (int j = 0; j < take; j++) {
                 h_tok[nt] = p[q.fed + j];
                 h_slot[nt] = q.slot;
@@ -324,20 +389,26 @@ bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_n
             }
         }
         REQ(c, nt > 0, "server made no progress");
+        if (table_dirty) {
+            CK(c, cudaMemcpyAsync(b.d_pages, b.h_pages, (size_t)S * PM * 4, cudaMemcpyHostToDevice, c->st));
+            table_dirty = false;
+        }
         if (!batch_upload(c, nt, nout) || !batch_run(c, nt, nout, vocab_out)) return false;
-        // the first finished prompt becomes the shared-prefix cache
-        if (ptoks.empty())
-            for (size_t i = 0; i < act.size(); i++) {
-                const ServeSeq &q = act[i];
-                if (q.fed == q.n && q.gen == 0 && q.n > kServeMinPrefix) {
-                    if (!kv_copy(c, q.slot, S, q.n - 1)) return false;
-                    ptoks.assign(prompts + off[q.req], prompts + off[q.req] + q.n - 1);
-                    break;
-                }
-            }
         CK(c, cudaMemcpyAsync(b.h_ids, b.d_ids, (size_t)nout * 4, cudaMemcpyDeviceToHost, c->st));
         CK(c, cudaStreamSynchronize(c->st));
         st->steps++;
+        // prompts fed in full: their full pages become shareable (each one's
+        // parent must be cached, so the chain stops at a page another
+        // request cached first)
+        for (size_t i = 0; i < act.size(); i++) {
+            ServeSeq &q = act[i];
+            if (q.sealed || q.fed < q.n) continue;
+            q.sealed = true;
+            const int *p = prompts + off[q.req];
+            for (int j = 0; (j + 1) * kPageRows <= q.n; j++)
+                if (!pool.cached(q.pages[j]) && !pool.seal(q.pages[j], j ? q.pages[j - 1] : -1, p + j * kPageRows))
+                    break;
+        }
         for (int i = 0; i < nout; i++) {
             ServeSeq &q = act[row_seq[i]];
             const int id = b.h_ids[i];
@@ -347,19 +418,27 @@ bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_n
             for (int k = 0; k < n_stop; k++)
                 if (id == stop_ids[k]) q.stopped = true;
         }
-        // retire finished sequences
+        // retire finished sequences: their slots and page references
         size_t w = 0;
         for (size_t i = 0; i < act.size(); i++) {
-            if (act[i].stopped || (act[i].fed == act[i].n && act[i].gen >= max_new)) {
-                free_slots.push_back(act[i].slot);
+            ServeSeq &q = act[i];
+            if (q.stopped || (q.fed == q.n && q.gen >= max_new)) {
+                free_slots.push_back(q.slot);
+                for (int pg : q.pages) pool.unref(pg);
                 done++;
-                st->generated += act[i].gen;
-                out_len[act[i].req] = act[i].stopped ? act[i].gen - 1 : act[i].gen;  // the stop id is not output
+                st->generated += q.gen;
+                out_len[q.req] = q.stopped ? q.gen - 1 : q.gen;  // the stop id is not output
             } else {
-                act[w++] = act[i];
+                if (w != i) act[w] = std::move(act[i]);
+                w++;
             }
         }
         act.resize(w);
     }
+    st->evictions = pool.evictions();
+    // the direct batch API's table again
+    b.identity_pages();
+    CK(c, cudaMemcpyAsync(b.d_pages, b.h_pages, (size_t)S * PM * 4, cudaMemcpyHostToDevice, c->st));
+    CK(c, cudaStreamSynchronize(c->st));
     return tc_status(c);
 }

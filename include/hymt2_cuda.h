@@ -139,10 +139,11 @@ HYC_API int hyc_wait_probe(void *impl, unsigned long long limit_ns, int *out);
  * (additive extension, no reference counterpart: the reference serves one
  * sequence per handle, src/model.c:914-958; these run many of them through
  * one forward pass).  After fused_prepare and hyc_set_embedding:
- * hyc_batch_prepare allocates `slots` sequence caches of slot_ctx rows
- * (slot_ctx <= the prepared ctx) plus one shared-prefix cache, and
- * activations for up to max_tokens tokens per pass with up to max_out head
- * rows.  hyc_batch_forward runs one pass over host arrays: token t is
+ * hyc_batch_prepare allocates a paged KV cache (pages of 16 positions in
+ * every layer; each of the `slots` sequences holds up to slot_ctx rows,
+ * slot_ctx <= the prepared ctx, plus a quarter more pages for the server's
+ * prompt cache), and activations for up to max_tokens tokens per pass with
+ * up to max_out head rows.  hyc_batch_forward runs one pass over host arrays: token t is
  * tokens[t] at position tok_pos[t] of slot tok_slot[t] (its K/V row is
  * written there; it attends to rows 0..tok_pos[t] of that slot, which must
  * be filled by this or earlier passes; no (slot, position) twice in one
@@ -150,22 +151,27 @@ HYC_API int hyc_wait_probe(void *impl, unsigned long long limit_ns, int *out);
  * vocab_out logits (all when <= 0) of token out_rows[i], after the output
  * RMSNorm and LM head; `logits` (optional) receives them as [nout][n_vocab].
  * hyc_batch_kv_copy copies rows 0..npos-1 of every layer from one slot to
- * another (slot `slots` is the prefix cache); hyc_batch_kv_read reads one
- * slot's layer like hyc_kv_read.
+ * another; hyc_batch_kv_read reads one slot's layer like hyc_kv_read.
  * hyc_serve generates max_new greedy tokens for each of nreq requests
  * (request r = prompts[prompt_off[r] .. prompt_off[r+1])), as the
  * reference's gen_ids would one request at a time, with continuous batching
  * over the prepared slots: each pass feeds one token of every decoding
  * request plus prompt chunks of newly admitted ones, at most step_tokens in
- * all (<= max_tokens; max_out must be >= slots), and a prompt that shares
- * >= 8 leading tokens with the first completed prompt starts from a copy of
- * those cached rows (always recomputing its last prompt token).  A request
+ * all (<= max_tokens; max_out must be >= slots).  Pages are allocated as
+ * sequences grow and freed when they end; a fed prompt's full pages stay
+ * cached (least recently used evicted first), and a new prompt shares the
+ * longest chain of cached pages its leading tokens match, by reference,
+ * then copies the matching first rows of one more cached page (the
+ * reference's longest-common-prefix reuse, src/model.c:931-936, against
+ * every cached prompt; the last prompt token is always recomputed).  A request
  * also ends at its first id in stop_ids (n_stop <= 16), as the reference's
  * loop breaks there.  out_ids is [nreq][max_new]: the ids before the stop
  * id, then the stop id, then -1; out_len[r] counts the ids before the stop
  * id (max_new when none came).  All return 0 or -1 (hyc_last_error). */
 typedef struct hyc_serve_stats {
     long long steps, decode_tokens, prefill_tokens, prefix_hits, prefix_tokens, generated;
+    long long shared_pages, copied_rows, evictions;  /* paged KV: pages shared by reference, rows copied, cached
+                                                        pages evicted */
 } hyc_serve_stats;
 HYC_API int hyc_batch_prepare(void *impl, int slots, int slot_ctx, int max_tokens, int max_out);
 HYC_API int hyc_batch_forward(void *impl, const int *tokens, const int *tok_slot, const int *tok_pos, int nt,

@@ -219,3 +219,46 @@ def test_serve_edge_cases(backend, synth, model_dir):
         assert out1.tolist() == out2.tolist() == out3.tolist()
     finally:
         dm.close()
+
+
+def test_serve_paged_prefix_cache(backend, oracle, synth, model_dir):
+    """Paged KV (pages of 16 positions): 40 requests through 3 slots with a
+    pool of 24 pages, so cached prompt pages are evicted.  Prompts share
+    prefixes of 8..48 tokens with earlier requests (not only the first one),
+    one repeats an earlier prompt whole; every request still gets the
+    oracle's greedy stream, shared pages are taken by reference and partial
+    pages copied, and every prompt token is either fed or reused."""
+    dm, om, path = _models(backend, oracle, synth, model_dir, "t_stq")
+    try:
+        rng = np.random.default_rng(29)
+        stems = [rng.integers(0, dm.vocab_out, 48).tolist() for _ in range(4)]
+        prompts = []
+        for i in range(40):
+            if i % 5 == 4:
+                prompts.append(list(prompts[i - 3]))                      # a repeat
+            else:
+                s = stems[int(rng.integers(0, 4))][:int(rng.integers(8, 49))]
+                prompts.append(s + rng.integers(0, dm.vocab_out, int(rng.integers(1, 24))).tolist())
+        max_new = 5
+        dm.batch_prepare(slots=3, slot_ctx=96, max_tokens=96)
+        out, st = dm.serve(prompts, max_new, step_tokens=64)
+        assert st["generated"] == 40 * max_new
+        assert st["prefill_tokens"] + st["prefix_tokens"] == sum(len(p) for p in prompts)
+        assert st["shared_pages"] >= 10 and st["copied_rows"] > 0 and st["evictions"] > 0, st
+        for r, p in enumerate(prompts):
+            tol = _bar(oracle, path, p)
+            om.reset()
+            _, lo = om.forward(p, 0)
+            for k in range(max_new):
+                lo = lo[:dm.vocab_out]
+                _check_id(out[r, k], lo, tol, ("paged", r, k))
+                _, lo = om.forward([int(out[r, k])], len(p) + k)
+        # the direct batch API gets its own page table back
+        p0 = prompts[0]
+        ids, _ = dm.batch_forward(p0, [1] * len(p0), np.arange(len(p0)), [len(p0) - 1])
+        om.reset()
+        _, lo = om.forward(p0, 0)
+        _check_id(int(ids[0]), lo[:dm.vocab_out], _bar(oracle, path, p0), "direct after serve")
+    finally:
+        dm.close()
+        om.close()
