@@ -117,33 +117,6 @@ __global__ void rope_norm_store(const __grid_constant__ AttnArgs a) {
     }
 }
 
-template <int HD, int G>
-struct AttnSmem {
-    float sq[G][HD];
-    float pm[G][G], pl[G][G];
-    float po[G][G][HD];
-    int last;
-};
-
-// Merge the G warps' partial (m, l, o) for head h = warp into (M, L, O).
-template <int HD, int G>
-__device__ __forceinline__ void merge_warps(AttnSmem<HD, G> &S, float &M, float &L, float (&O)[HD / 32]) {
-    const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < G; w++) M = fmaxf(M, S.pm[w][h]);
-    L = 0.f;
-#pragma unroll
-    for (int i = 0; i < HD / 32; i++) O[i] = 0.f;
-#pragma unroll
-    for (int w = 0; w < G; w++) {
-        const float f = S.pl[w][h] > 0.f ? expf(S.pm[w][h] - M) : 0.f;
-        L = fmaf(S.pl[w][h], f, L);
-#pragma unroll
-        for (int i = 0; i < HD / 32; i++) O[i] = fmaf(S.po[w][h][lane + 32 * i], f, O[i]);
-    }
-}
-
 // Decode attention, one query token at position pos: grid (kv_heads, splits
 // of kDecSplit keys).  Warps 0..G-1 are the query heads kvh*G + w, warp G
 // rotates/normalises this KV head's k and stores k and v.  The split's cached
@@ -847,128 +820,185 @@ __global__ void __launch_bounds__(32) attn_merge_kernel(const __grid_constant__ 
     attn_merge_head<HD>(a.cpart, a.max_chunks, (pos + cs) / cs, blockIdx.x, a.ao + (size_t)blockIdx.x * HD);
 }
 
-// attn_prefill's dynamic shared memory: per warp the V rows of one 32-key tile.
-template <int HD, int G>
-__host__ __device__ constexpr size_t prefill_stage_bytes() {
-    return (size_t)G * 32 * HD * 2;
-}
+// ---------------------------------------------------------------- batched decode attention
+//
+// A pass whose every token is the next token of its own sequence (the
+// continuous-batching server's decode steps): token t attends to rows
+// 0 .. pos of its slot, all already in the (paged) cache.  CTA = (KV head,
+// token), kDbWarps warps taking groups of KG = 32 / G consecutive keys round
+// robin.  Lane l owns head dims l * HD/32 .. of every head: the query of the
+// G heads stays in registers, a key's K and V rows are read once and
+// coalesced (HD * 2 bytes per warp per row), and the G x KG dot products of a
+// group finish in one 31-step reduce-scatter that leaves lane l with the score
+// of (key l / G, head l % G).  Online softmax per head (reference attn_task,
+// src/model.c:768-795: q.k / sqrt(hd), max-subtracted expf, p.v over the sum
+// of p), then the warps' (m, l, o) merge in shared memory.
+constexpr int kDbWarps = 4;
 
-// Keys [0, j1) of KV head kvh (all in the cache) for the G query heads in
-// sq[G][HD]: warp w takes the 32-key tiles w*32 + k*G*32, one key per lane
-// (scores over d in order, a warp softmax per tile, then p.V over the tile's
-// keys in order).  Every global load of a tile is in flight at once: the V
-// rows go to this warp's shared buffer sv (cp.async) before the scores, and
-// each lane loads its key's whole K row into registers.
-template <int HD, int G>
-__device__ __forceinline__ void attend_range_staged(const AttnArgs &a, int slot, int kvh, int j1,
-                                                    const float (*sq)[HD], uint16_t *sv, float (&m)[G],
-                                                    float (&l)[G], float (&o)[G][HD / 32]) {
-    constexpr int CH = HD / 8;  // 16-byte chunks per row
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-    for (int h = 0; h < G; h++) {
-        m[h] = -INFINITY;
-        l[h] = 0.f;
-#pragma unroll
-        for (int i = 0; i < HD / 32; i++) o[h][i] = 0.f;
+template <int D>
+struct BfRow;  // D consecutive bf16 of a row, as loaded by one lane
+template <>
+struct BfRow<4> {
+    uint2 v;
+    __device__ __forceinline__ void load(const uint16_t *p) { v = __ldg((const uint2 *)p); }
+    __device__ __forceinline__ void zero() { v = make_uint2(0u, 0u); }
+    __device__ __forceinline__ void get(float (&f)[4]) const {
+        f[0] = __uint_as_float(v.x << 16);
+        f[1] = __uint_as_float(v.x & 0xffff0000u);
+        f[2] = __uint_as_float(v.y << 16);
+        f[3] = __uint_as_float(v.y & 0xffff0000u);
     }
-    const uint16_t *Kb = a.kc + kvh * HD, *Vb = a.vc + kvh * HD;
-    for (int tile = w * 32; tile < j1; tile += G * 32) {
-        const int nk = min(32, j1 - tile);
-        for (int i = lane; i < nk * CH; i += 32) {
-            const int r = i / CH, c = i - r * CH;
-            cp_async16(sv + r * HD + c * 8, Vb + attn_kv_row(a, slot, tile + r) + c * 8);
-        }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-        const int j = tile + lane;
-        const bool valid = j < j1;
-        float s[G];
+};
+template <>
+struct BfRow<2> {
+    uint32_t v;
+    __device__ __forceinline__ void load(const uint16_t *p) { v = __ldg((const uint32_t *)p); }
+    __device__ __forceinline__ void zero() { v = 0u; }
+    __device__ __forceinline__ void get(float (&f)[2]) const {
+        f[0] = __uint_as_float(v << 16);
+        f[1] = __uint_as_float(v & 0xffff0000u);
+    }
+};
+
+template <int HD, int G>
+__global__ void __launch_bounds__(kDbWarps * 32) attn_batch_dec(const __grid_constant__ AttnArgs a) {
+    constexpr int D = HD / 32, KG = 32 / G;
+    __shared__ float s_m[kDbWarps][G], s_l[kDbWarps][G], s_o[kDbWarps][G][HD];
+    pdl_trigger();
+    const int kvh = blockIdx.x, t = blockIdx.y, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    pdl_wait();
+    const int pos = attn_tok_pos(a, t), slot = attn_tok_slot(a, t), nkeys = pos + 1;
+    float q[G][D];
+    const float *qr = a.qkv + (size_t)t * a.qkv_ld + (size_t)kvh * G * HD + lane * D;
 #pragma unroll
-        for (int h = 0; h < G; h++) s[h] = 0.f;
-        if (valid) {
-            const uint16_t *kr = Kb + attn_kv_row(a, slot, j);
-            uint4 kk[CH];
+    for (int h = 0; h < G; h++)
 #pragma unroll
-            for (int c = 0; c < CH; c++) kk[c] = *(const uint4 *)(kr + c * 8);
+        for (int d = 0; d < D; d++) q[h][d] = qr[h * HD + d];
+    // the slot's page numbers, lane j holding page j (tables of up to 32 pages)
+    const bool reg_tab = a.pages && a.page_max <= 32;
+    const int pg = reg_tab && lane < a.page_max ? __ldg(a.pages + slot * a.page_max + lane) : 0;
+    const uint16_t *Kb = a.kc + kvh * HD + lane * D, *Vb = a.vc + kvh * HD + lane * D;
+    float o[G][D];
 #pragma unroll
-            for (int c = 0; c < CH; c++) {
-                const uint32_t kw[4] = {kk[c].x, kk[c].y, kk[c].z, kk[c].w};
+    for (int h = 0; h < G; h++)
 #pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const float k0 = bf16_bits_to_f32(kw[q] & 0xffffu), k1 = bf16_bits_to_f32(kw[q] >> 16);
+        for (int d = 0; d < D; d++) o[h][d] = 0.f;
+    float mh = -INFINITY, lh = 0.f;  // running max and sum of head lane % G
+    const int ngroups = (nkeys + KG - 1) / KG;
+    // K and V rows of group g into registers (keys past pos read as zeros)
+    auto load_group = [&](int g, BfRow<D> (&kr)[KG], BfRow<D> (&vr)[KG]) {
 #pragma unroll
-                    for (int h = 0; h < G; h++) {
-                        s[h] = fmaf(sq[h][c * 8 + 2 * q], k0, s[h]);
-                        s[h] = fmaf(sq[h][c * 8 + 2 * q + 1], k1, s[h]);
-                    }
-                }
+        for (int k = 0; k < KG; k++) {
+            const int j = g * KG + k;
+            if (j < nkeys) {
+                const long long off = reg_tab ? (long long)__shfl_sync(0xffffffffu, pg, j >> kPageShift) * a.page_stride +
+                                                    (long long)(j & (kPageRows - 1)) * a.kvdim
+                                              : attn_kv_row(a, slot, j);
+                kr[k].load(Kb + off);
+                vr[k].load(Vb + off);
+            } else {
+                kr[k].zero();
+                vr[k].zero();
             }
         }
-        float p[G];
+    };
+    BfRow<D> nkr[KG], nvr[KG];  // the next group's rows, in flight while this group computes
+    if (w < ngroups) load_group(w, nkr, nvr);
+    for (int g = w; g < ngroups; g += kDbWarps) {
+        const int k0 = g * KG;
+        BfRow<D> kr[KG], vr[KG];
 #pragma unroll
-        for (int h = 0; h < G; h++) {
-            const float sc = valid ? s[h] * a.scale : -INFINITY;
-            const float mt = warp_max(sc);
-            const float mn = fmaxf(m[h], mt);
-            const float corr = expf(m[h] - mn);
-            p[h] = valid ? expf(sc - mn) : 0.f;
-            l[h] = l[h] * corr + warp_sum(p[h]);
-            m[h] = mn;
-#pragma unroll
-            for (int i = 0; i < HD / 32; i++) o[h][i] *= corr;
+        for (int k = 0; k < KG; k++) {
+            kr[k] = nkr[k];
+            vr[k] = nvr[k];
         }
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
-        __syncwarp();
-        for (int jj = 0; jj < nk; jj++) {
-            float vv[HD / 32];
+        if (g + kDbWarps < ngroups) load_group(g + kDbWarps, nkr, nvr);
+        // partial dots over this lane's dims: v[k * G + h]
+        float v[32];
 #pragma unroll
-            for (int i = 0; i < HD / 32; i++) vv[i] = bf16_bits_to_f32(sv[jj * HD + lane + 32 * i]);
+        for (int k = 0; k < KG; k++) {
+            float kf[D];
+            kr[k].get(kf);
 #pragma unroll
             for (int h = 0; h < G; h++) {
-                const float pj = __shfl_sync(0xffffffffu, p[h], jj);
+                float acc = 0.f;
 #pragma unroll
-                for (int i = 0; i < HD / 32; i++) o[h][i] = fmaf(pj, vv[i], o[h][i]);
+                for (int d = 0; d < D; d++) acc = fmaf(q[h][d], kf[d], acc);
+                v[k * G + h] = acc;
             }
         }
-        __syncwarp();  // the buffer is free for the next tile
-    }
-}
-
-// Prefill: token t (position *pos_ptr + t) attends to 0..pos inclusive; q
-// already rotated/normalised and k/v already in the cache (rope_norm_store).
-// grid (kv_heads, nt), G warps, prefill_stage_bytes<HD, G>() of dynamic
-// shared memory.
-template <int HD, int G>
-__global__ void __launch_bounds__(G * 32) attn_prefill(const __grid_constant__ AttnArgs a) {
-    pdl_trigger();
-    __shared__ AttnSmem<HD, G> S;
-    extern __shared__ __align__(16) uint8_t dsm[];
-    const int kvh = blockIdx.x, t = blockIdx.y;
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    pdl_wait();
-    const int pos = attn_tok_pos(a, t);
-    const float *qr = a.qkv + (size_t)t * a.qkv_ld + (kvh * G + w) * HD;
+        // reduce-scatter: after the stage of width sw, v[i] (i < sw) is the sum of
+        // value i + (lane & -sw) over the lanes that differ from this one only in
+        // bits >= sw; after sw = 1, v[0] is the warp's sum of value `lane`
 #pragma unroll
-    for (int i = 0; i < HD / 32; i++) S.sq[w][lane + 32 * i] = qr[lane + 32 * i];
-    __syncthreads();
-    float m[G], l[G], o[G][HD / 32];
-    attend_range_staged<HD, G>(a, attn_tok_slot(a, t), kvh, pos + 1, S.sq, (uint16_t *)dsm + w * 32 * HD, m, l, o);
+        for (int sw = 16; sw >= 1; sw >>= 1) {
+            const bool up = (lane & sw) != 0;
 #pragma unroll
-    for (int h = 0; h < G; h++) {
-        if (lane == 0) {
-            S.pm[w][h] = m[h];
-            S.pl[w][h] = l[h];
+            for (int i = 0; i < sw; i++) {
+                const float send = up ? v[i] : v[i + sw];
+                const float keep = up ? v[i + sw] : v[i];
+                v[i] = keep + __shfl_xor_sync(0xffffffffu, send, sw);
+            }
+        }
+        const int mk = k0 + lane / G;
+        const float sc = mk < nkeys ? v[0] * a.scale : -INFINITY;
+        float gm = sc;
+#pragma unroll
+        for (int x = G; x < 32; x <<= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, x));
+        const float mn = fmaxf(mh, gm);
+        const float corr = expf(mh - mn);
+        const float p = mk < nkeys ? expf(sc - mn) : 0.f;
+        float ps = p;
+#pragma unroll
+        for (int x = G; x < 32; x <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, x);
+        lh = lh * corr + ps;
+        mh = mn;
+#pragma unroll
+        for (int h = 0; h < G; h++) {
+            const float ch = __shfl_sync(0xffffffffu, corr, h);  // lane h: head h
+#pragma unroll
+            for (int d = 0; d < D; d++) o[h][d] *= ch;
         }
 #pragma unroll
-        for (int i = 0; i < HD / 32; i++) S.po[w][h][lane + 32 * i] = o[h][i];
-    }
-    __syncthreads();
-    float M, L, O[HD / 32];
-    merge_warps<HD, G>(S, M, L, O);
-    const float inv = 1.0f / L;
-    float *dst = a.ao + (size_t)t * a.qdim + (kvh * G + w) * HD;
+        for (int k = 0; k < KG; k++) {
+            float vf[D];
+            vr[k].get(vf);
 #pragma unroll
-    for (int i = 0; i < HD / 32; i++) dst[lane + 32 * i] = O[i] * inv;
+            for (int h = 0; h < G; h++) {
+                const float pk = __shfl_sync(0xffffffffu, p, k * G + h);
+#pragma unroll
+                for (int d = 0; d < D; d++) o[h][d] = fmaf(pk, vf[d], o[h][d]);
+            }
+        }
+    }
+    if (lane < G) {
+        s_m[w][lane] = mh;
+        s_l[w][lane] = lh;
+    }
+#pragma unroll
+    for (int h = 0; h < G; h++)
+#pragma unroll
+        for (int d = 0; d < D; d++) s_o[w][h][lane * D + d] = o[h][d];
+    __syncthreads();
+    for (int h = w; h < G; h += kDbWarps) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int x = 0; x < kDbWarps; x++) M = fmaxf(M, s_m[x][h]);
+        float L = 0.f, O[D];
+#pragma unroll
+        for (int d = 0; d < D; d++) O[d] = 0.f;
+#pragma unroll
+        for (int x = 0; x < kDbWarps; x++) {
+            const float f = s_l[x][h] > 0.f ? expf(s_m[x][h] - M) : 0.f;
+            L = fmaf(s_l[x][h], f, L);
+#pragma unroll
+            for (int d = 0; d < D; d++) O[d] = fmaf(s_o[x][h][lane * D + d], f, O[d]);
+        }
+        const float inv = 1.0f / L;
+        float *dst = a.ao + (size_t)t * a.qdim + (size_t)(kvh * G + h) * HD + lane * D;
+#pragma unroll
+        for (int d = 0; d < D; d++) dst[d] = O[d] * inv;
+    }
 }
 
 // ---------------------------------------------------------------- prefill attention on tensor cores

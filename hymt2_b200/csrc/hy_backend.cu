@@ -354,14 +354,6 @@ void init_kernel_attrs_current() {
     set_smem(attn_chunk_kernel<64, 2>);
     set_smem(attn_chunk_kernel<64, 4>);
     set_smem(attn_chunk_kernel<64, 8>);
-    set_smem(attn_prefill<128, 1>, prefill_stage_bytes<128, 1>());
-    set_smem(attn_prefill<128, 2>, prefill_stage_bytes<128, 2>());
-    set_smem(attn_prefill<128, 4>, prefill_stage_bytes<128, 4>());
-    set_smem(attn_prefill<128, 8>, prefill_stage_bytes<128, 8>());
-    set_smem(attn_prefill<64, 1>, prefill_stage_bytes<64, 1>());
-    set_smem(attn_prefill<64, 2>, prefill_stage_bytes<64, 2>());
-    set_smem(attn_prefill<64, 4>, prefill_stage_bytes<64, 4>());
-    set_smem(attn_prefill<64, 8>, prefill_stage_bytes<64, 8>());
     set_smem(attn_fa<128, 1>, fa_smem<128, 1>());
     set_smem(attn_fa<128, 2>, fa_smem<128, 2>());
     set_smem(attn_fa<128, 4>, fa_smem<128, 4>());
@@ -703,9 +695,8 @@ bool attn_launch(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
     const int rgrid = nt < 16 * c->nsm ? nt : 16 * c->nsm;
     if (!launch(c, rope_norm_store<HD>, dim3(rgrid), dim3(warps * 32), 0, pdl, aa)) return false;
     const int nqb = aa.qblk ? aa.nqb : (nt + kFaQ - 1) / kFaQ;
-    if (nqb == nt)  // one token per sequence (a batch of decode steps): the per-token kernel is faster
-        return launch(c, attn_prefill<HD, G>, dim3(aa.kv_heads, nt), dim3(G * 32), prefill_stage_bytes<HD, G>(), pdl,
-                      aa);
+    if (nqb == nt && aa.tok_slot)  // one token per sequence (a batch of decode steps)
+        return launch(c, attn_batch_dec<HD, G>, dim3(aa.kv_heads, nt), dim3(kDbWarps * 32), 0, pdl, aa);
     return launch(c, attn_fa<HD, G>, dim3(nqb, aa.kv_heads), dim3(G * 32), fa_smem<HD, G>(), pdl, aa);
 }
 
