@@ -298,6 +298,7 @@ def cpu_baseline(path: str, ntok: int) -> dict:
 
 
 SERVE_PREFIX, SERVE_MAX_NEW, SERVE_SLOTS, SERVE_STEP_TOKENS = 24, 64, 256, 512
+SERVE_MAX_TOKENS = 4096  # pass capacity: prompt chunks may fill it while fewer than half the slots decode
 
 
 def shard(items: list, rank: int, world: int) -> list:
@@ -336,7 +337,7 @@ def bench_serving(dm, stream, torch, rank, world, nreq, max_over_ranks, barrier,
     batching over 256 slots, 64 greedy tokens per request, device-timed
     around the whole serve call (host scheduling included)."""
     reqs = shard(serve_requests(nreq), rank, world)
-    dm.batch_prepare(slots=SERVE_SLOTS, slot_ctx=128 + SERVE_MAX_NEW, max_tokens=SERVE_STEP_TOKENS,
+    dm.batch_prepare(slots=SERVE_SLOTS, slot_ctx=128 + SERVE_MAX_NEW, max_tokens=SERVE_MAX_TOKENS,
                      max_out=SERVE_SLOTS)
     dm.serve(reqs[:min(len(reqs), 300)], 4, SERVE_STEP_TOKENS)  # warm-up: tensor-core weight tiles, clocks
     barrier()
@@ -361,7 +362,9 @@ def bench_serving(dm, stream, torch, rank, world, nreq, max_over_ranks, barrier,
     return {"value": round(total_gen / (ms / 1e3), 1), "unit": "generated tok/s", "n_gpus": world,
             "roofline": roof,
             "requests": nreq, "requests_per_gpu": len(reqs), "max_new": SERVE_MAX_NEW, "slots_per_gpu": SERVE_SLOTS,
-            "step_token_budget": SERVE_STEP_TOKENS, "ms": round(ms, 2), "wall_s_rank0": round(wall, 3),
+            "step_token_budget": SERVE_STEP_TOKENS, "pass_capacity": SERVE_MAX_TOKENS,
+            "mean_slot_occupancy_rank0": round(st["active_seq_steps"] / max(1, st["steps"] * SERVE_SLOTS), 3),
+            "ms": round(ms, 2), "wall_s_rank0": round(wall, 3),
             "steps_rank0": st["steps"], "prefill_tokens_rank0": st["prefill_tokens"],
             "prefix_hits_rank0": st["prefix_hits"], "prefix_tokens_rank0": st["prefix_tokens"],
             "kv_pages_shared_rank0": st["shared_pages"], "kv_rows_copied_rank0": st["copied_rows"],

@@ -61,7 +61,8 @@ class DeviceOps(C.Structure):
 class ServeStats(C.Structure):
     _fields_ = [("steps", C.c_longlong), ("decode_tokens", C.c_longlong), ("prefill_tokens", C.c_longlong),
                 ("prefix_hits", C.c_longlong), ("prefix_tokens", C.c_longlong), ("generated", C.c_longlong),
-                ("shared_pages", C.c_longlong), ("copied_rows", C.c_longlong), ("evictions", C.c_longlong)]
+                ("shared_pages", C.c_longlong), ("copied_rows", C.c_longlong), ("evictions", C.c_longlong),
+                ("active_seq_steps", C.c_longlong)]
 
 
 # Every symbol include/hymt2_cuda.h declares, with its ctypes signature.

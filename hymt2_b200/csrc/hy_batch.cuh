@@ -314,6 +314,12 @@ bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_n
     std::vector<int> free_slots;
     for (int s = S - 1; s >= 0; s--) free_slots.push_back(s);
     std::vector<ServeSeq> act;
+    // admission order: longest prompts first (ties in request order), so the
+    // last wave is not held up by a long prompt admitted late
+    std::vector<int> order((size_t)nreq);
+    for (int r = 0; r < nreq; r++) order[(size_t)r] = r;
+    std::stable_sort(order.begin(), order.end(),
+                     [&](int x, int y) { return off[x + 1] - off[x] > off[y + 1] - off[y]; });
     int next = 0, done = 0;
     std::vector<int> row_seq;
     memset(st, 0, sizeof *st);
@@ -323,7 +329,7 @@ bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_n
         // admit while there are free slots
         while (!free_slots.empty() && next < nreq) {
             ServeSeq q;
-            q.req = next++;
+            q.req = order[(size_t)next++];
             q.slot = free_slots.back();
             free_slots.pop_back();
             q.n = off[q.req + 1] - off[q.req];
@@ -355,12 +361,18 @@ bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_n
             }
             act.push_back(q);
         }
-        // one step: a token of every decoding sequence, then prompt chunks
+        // one step: a token of every decoding sequence, then prompt chunks; while
+        // fewer than half the slots decode (waves of admissions, the drain), the
+        // prompt chunks may fill the whole pass capacity
+        int ndec = 0;
+        for (const ServeSeq &q : act) ndec += q.fed >= q.n;
+        const int budget = ndec < S / 2 ? T : step_tokens;
+        st->active_seq_steps += (long long)act.size();
         int nt = 0, nout = 0;
         row_seq.clear();
         for (size_t i = 0; i < act.size(); i++) {
             ServeSeq &q = act[i];
-            if (q.fed < q.n || nt >= step_tokens) continue;
+            if (q.fed < q.n || nt >= budget) continue;
             if (!need_page(q, q.n + q.gen - 1)) return false;
             h_tok[nt] = q.last;
             h_slot[nt] = q.slot;
@@ -369,11 +381,11 @@ bool serve_run(HyCtx *c, const int *prompts, const int *off, int nreq, int max_n
             row_seq.push_back((int)i);
             st->decode_tokens++;
         }
-        for (size_t i = 0; i < act.size() && nt < step_tokens; i++) {
+        for (size_t i = 0; i < act.size() && nt < budget; i++) {
             ServeSeq &q = act[i];
             if (q.fed >= q.n) continue;
             const int *p = prompts + off[q.req];
-            const int take = (q.n - q.fed) < (step_tokens - nt) ? (q.n - q.fed) : (step_tokens - nt);
+            const int take = (q.n - q.fed) < (budget - nt) ? (q.n - q.fed) : (budget - nt);
             if (!need_page(q, q.fed + take - 1)) return false;
             for (int j = 0; j < take; j++) {
                 h_tok[nt] = p[q.fed + j];

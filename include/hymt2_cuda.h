@@ -157,7 +157,9 @@ HYC_API int hyc_wait_probe(void *impl, unsigned long long limit_ns, int *out);
  * reference's gen_ids would one request at a time, with continuous batching
  * over the prepared slots: each pass feeds one token of every decoding
  * request plus prompt chunks of newly admitted ones, at most step_tokens in
- * all (<= max_tokens; max_out must be >= slots).  Pages are allocated as
+ * all (<= max_tokens; max_out must be >= slots), or up to max_tokens while
+ * fewer than half the slots are decoding; requests are admitted longest
+ * prompt first.  Pages are allocated as
  * sequences grow and freed when they end; a fed prompt's full pages stay
  * cached (least recently used evicted first), and a new prompt shares the
  * longest chain of cached pages its leading tokens match, by reference,
@@ -172,6 +174,7 @@ typedef struct hyc_serve_stats {
     long long steps, decode_tokens, prefill_tokens, prefix_hits, prefix_tokens, generated;
     long long shared_pages, copied_rows, evictions;  /* paged KV: pages shared by reference, rows copied, cached
                                                         pages evicted */
+    long long active_seq_steps;                      /* sum over passes of the requests holding a slot */
 } hyc_serve_stats;
 HYC_API int hyc_batch_prepare(void *impl, int slots, int slot_ctx, int max_tokens, int max_out);
 HYC_API int hyc_batch_forward(void *impl, const int *tokens, const int *tok_slot, const int *tok_pos, int nt,

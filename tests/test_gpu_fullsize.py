@@ -155,7 +155,7 @@ def test_c3_serving_full_size(backend, oracle, reference, synth, model_dir):
     max_new = 16
     dm = DeviceModel(path, backend, ctx=256)
     try:
-        dm.batch_prepare(slots=bench.SERVE_SLOTS, slot_ctx=128 + max_new, max_tokens=bench.SERVE_STEP_TOKENS,
+        dm.batch_prepare(slots=bench.SERVE_SLOTS, slot_ctx=128 + max_new, max_tokens=bench.SERVE_MAX_TOKENS,
                          max_out=bench.SERVE_SLOTS)
         out, _ = dm.serve(reqs, max_new, bench.SERVE_STEP_TOKENS)
     finally:
