@@ -199,3 +199,43 @@ def test_c4_q8_0_decode_full_size(backend, oracle, reference, synth, model_dir):
     assert rel <= tol and (tol > 1e-3 or rel <= 1e-3), (rel, tol)
     d = _first_div(got, want)
     assert d is None or _near_tie(steps[d], tol), (got, want)
+
+
+def test_c0_reference_loop_through_backend(backend, oracle, synth, model_dir):
+    """The drop-in at full size: the reference's own model.c (oracle/_ref/
+    libhymt2_dropin.so: its host C from its sources, linked with this backend
+    in place of src/cuda.c) runs config 0 with HYMT2_DEVICE=cuda through the
+    vtable (upload of host-built panels, fused_prepare, fused_forward per
+    token with host h and logits, the host's own argmax, src/model.c:904-954).
+    Its ids must be this backend's own on-device decode ids up to a near tie;
+    the rate of that loop is printed (the path a reference user gets without
+    the additive hyc_decode_* entry points)."""
+    import oracle as O
+    from hymt2_b200.device import DeviceModel
+    if not os.path.exists(O.DROPIN_LIB):
+        pytest.skip("drop-in not built")
+    path = synth.ensure("c0_stq", model_dir)
+    ids = np.random.default_rng(1).integers(0, VOCAB, 48).tolist()
+    n = 33
+    dm = DeviceModel(path, backend, ctx=256)
+    try:
+        own = dm.generate(ids, n)
+    finally:
+        dm.close()
+    os.environ["HYMT2_DEVICE"] = "cuda"
+    try:
+        ref = O.Reference(O.DROPIN_LIB).load(path, threads=4, ctx=256)
+        try:
+            assert ref.uses_device(), ref.info()
+            got, steps, *_ = ref.greedy(ids, n, step_logits=True)
+            ref.reset_cache()
+            _, _, pre_ms, dec_ms, _ = ref.greedy(ids, n)  # timed without the harness's logits copies
+        finally:
+            ref.close()
+    finally:
+        os.environ["HYMT2_DEVICE"] = "cpu"
+    spread, tol = _spread_tol(oracle, path, ids)
+    print(f"c0 reference loop through the backend: prompt {pre_ms:.1f} ms, {(n - 1) / (dec_ms / 1e3):.1f} decode "
+          f"tok/s (fused_forward per token, host logits and argmax); ids {got[:8]}")
+    d = _first_div(got, own)
+    assert d is None or _near_tie(steps[d], tol), (got, own)
