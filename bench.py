@@ -167,12 +167,12 @@ def profile_pass(args):
 
 
 def kernel_source_hash() -> str:
-    """sha256 (first 16 hex digits) of the device-code headers the kernels are built from (hy_*.cuh)."""
+    """sha256 (first 16 hex digits) of the headers the kernels are built from (hy_*.cuh, hy_*.h)."""
     import hashlib
     h = hashlib.sha256()
     cdir = os.path.join(ROOT, "hymt2_b200", "csrc")
     for name in sorted(os.listdir(cdir)):
-        if name.endswith(".cuh"):
+        if name.endswith((".cuh", ".h")):
             with open(os.path.join(cdir, name), "rb") as f:
                 h.update(name.encode() + b"\0" + f.read())
     return h.hexdigest()[:16]
