@@ -10,6 +10,7 @@
 #pragma once
 #include "hy_common.cuh"
 #include "hy_pages.h"
+#include "hy_tc.cuh"
 
 namespace hyk {
 
@@ -28,6 +29,12 @@ struct AttnArgs {
     int split_len, max_splits;
     float *cpart;           // wide decode partials [heads][max_chunks][HD+kPartPad]
     int max_chunks, units;  // attn_max_chunks(ctx); units available (SMs)
+    // all-decode passes whose o_proj runs on the tensor cores: attn_batch_dec
+    // writes its Q8_K blocks straight into the GEMM's tiled activation (tca,
+    // scales tcad, tc_nb blocks per token) instead of ao
+    int8_t *tca;
+    float *tcad;
+    int tc_nb;
     int trace;              // timeline slot (< 0: off)
     // ragged batch of several sequences (prefill kernels only): token t sits
     // at position tok_pos[t] of sequence slot tok_slot[t], whose cache is
@@ -864,6 +871,7 @@ template <int HD, int G>
 __global__ void __launch_bounds__(kDbWarps * 32) attn_batch_dec(const __grid_constant__ AttnArgs a) {
     constexpr int D = HD / 32, KG = 32 / G;
     __shared__ float s_m[kDbWarps][G], s_l[kDbWarps][G], s_o[kDbWarps][G][HD];
+    __shared__ __align__(16) float s_out[G * HD];  // the finished heads, for the fused quantiser
     pdl_trigger();
     const int kvh = blockIdx.x, t = blockIdx.y, w = threadIdx.x >> 5, lane = threadIdx.x & 31;
     pdl_wait();
@@ -995,9 +1003,21 @@ __global__ void __launch_bounds__(kDbWarps * 32) attn_batch_dec(const __grid_con
             for (int d = 0; d < D; d++) O[d] = fmaf(s_o[x][h][lane * D + d], f, O[d]);
         }
         const float inv = 1.0f / L;
-        float *dst = a.ao + (size_t)t * a.qdim + (size_t)(kvh * G + h) * HD + lane * D;
+        float *dst = a.tca ? s_out + h * HD + lane * D : a.ao + (size_t)t * a.qdim + (size_t)(kvh * G + h) * HD + lane * D;
 #pragma unroll
         for (int d = 0; d < D; d++) dst[d] = O[d] * inv;
+    }
+    if (a.tca) {
+        // the G heads are G * HD / 256 whole Q8_K blocks of the o_proj input:
+        // warp j quantises block j exactly as tc_quantize_blocks would
+        __syncthreads();
+        constexpr int NBC = G * HD / 256;
+        static_assert(NBC <= kDbWarps, "one warp per block");
+        if (w < NBC) {
+            const float4 v0 = *(const float4 *)&s_out[w * 256 + lane * 8], v1 = *(const float4 *)&s_out[w * 256 + lane * 8 + 4];
+            const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+            tc_quant_store(v, a.tca, a.tcad, t / kTcM, a.tc_nb, (kvh * G * HD) / 256 + w, t % kTcM);
+        }
     }
 }
 

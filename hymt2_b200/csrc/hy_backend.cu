@@ -604,13 +604,15 @@ bool tc_gemm_launch(HyCtx *c, TcArgs &ta, int P, HyWeight *const *ws, int cnt, b
 // prologue (pro.act / x / x2 / norm_w / eps, pro.k = K): one quantise launch
 // writing tiled Q8_K codes, then one tensor-core GEMM per weight format; outs[i] is
 // [nt][lds[i]], stored (epi 0) or accumulated (epi 1).
+// act_ready: the tiled Q8_K activation of the nt tokens is in place already
+// (written by the kernel before, e.g. attn_batch_dec), so no quantiser runs.
 bool tc_linear(HyCtx *c, const GemvArgs &pro, int nt, HyWeight *const *ws, float *const *outs, const int *lds,
-               int cnt, int epi, bool pdl) {
+               int cnt, int epi, bool pdl, bool act_ready = false) {
     const int K = pro.k, nb = K / 256, tpad = (nt + kTcM - 1) / kTcM * kTcM;
     if (!tc_scratch(c, K)) return false;
     for (int i = 0; i < cnt; i++)
         if (!tc_weight(c, ws[i])) return false;
-    {
+    if (!act_ready) {
         const dim3 g(tpad), b(kGemvThreads);
         const size_t sm = (size_t)(K + 64) * 4;
         const int sv = (K / 4 + kGemvThreads - 1) / kGemvThreads;
@@ -828,6 +830,12 @@ bool ffn_forward(HyCtx *c, const Fwd &f, const Layer &L, int nt, bool pdl) {
 bool layer_forward(HyCtx *c, const Fwd &f, int li, int nt, bool pdl) {
     const Layer &L = c->layers[li];
     const int qkv_ld = c->qd + 2 * c->kvd;
+    // an all-decode batch pass (one token per query block: attn_batch_dec)
+    // whose o_proj runs on the tensor cores: the attention kernel writes the
+    // GEMM's tiled Q8_K input itself (whole blocks: G * hd a multiple of 256)
+    HyWeight *wo[1] = {L.o};
+    const bool fuse_oq = f.tok_slot && f.qblk && f.nqb == nt && L.o->k == c->qd &&
+                         ((c->heads / c->kvh) * c->hd) % 256 == 0 && tc_usable(c, nt, wo, 1);
     {
         HyWeight *ws[3] = {L.q, L.k, L.v};
         float *outs[3] = {f.qkv, f.qkv + c->qd, f.qkv + c->qd + c->kvd};
@@ -882,6 +890,12 @@ bool layer_forward(HyCtx *c, const Fwd &f, int li, int nt, bool pdl) {
         aa.tickets = c->d_tickets;
         aa.split_len = kSplitLen;
         aa.max_splits = c->max_splits;
+        if (fuse_oq) {
+            if (!tc_scratch(c, c->qd)) return false;
+            aa.tca = c->d_tca;
+            aa.tcad = c->d_tcad;
+            aa.tc_nb = c->qd / 256;
+        }
         if (!attention(c, aa, nt, pdl)) return false;
     }
     {
@@ -896,7 +910,7 @@ bool layer_forward(HyCtx *c, const Fwd &f, int li, int nt, bool pdl) {
         float *outs[1] = {dst};
         const int lds[1] = {c->H};
         if (tc_usable(c, nt, ws, 1)) {
-            if (!tc_linear(c, a, nt, ws, outs, lds, 1, epi, pdl)) return false;
+            if (!tc_linear(c, a, nt, ws, outs, lds, 1, epi, pdl, fuse_oq)) return false;
         } else {
             a.epi = epi ? EPI_ADD : EPI_STORE;
             a.nw = 1;
