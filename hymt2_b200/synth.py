@@ -64,7 +64,10 @@ FULL = dict(n_layer=32, hidden=2048, heads=16, kv_heads=4, hdim=128, ffn=6144, v
 TINY = dict(n_layer=2, hidden=256, heads=4, kv_heads=2, hdim=64, ffn=512, vocab=1000)
 TINY512 = dict(n_layer=2, hidden=512, heads=8, kv_heads=2, hdim=64, ffn=1024, vocab=1000)
 # splits over 2 / 4 / 8 ranks (heads, KV heads, FFN columns and vocabulary divide)
-TINY_TP = dict(n_layer=2, hidden=512, heads=8, kv_heads=4, hdim=64, ffn=1024, vocab=1000)
+# tensor-parallel test model: 2-, 4- and 8-way splits keep whole 256-element
+# blocks per rank (query dims 16 x 128 / 8, FFN 2048 / 8), and at 8 ranks every
+# KV head sits on two ranks, as in the 1.8B shape
+TINY_TP = dict(n_layer=2, hidden=512, heads=16, kv_heads=4, hdim=128, ffn=2048, vocab=1000)
 
 
 def make_spec(mix: str, shape: dict, reftool: bool = False, seed: int = 0, embd: str = "Q6_K",
@@ -95,7 +98,7 @@ CONFIGS = {
     "t_q4km": lambda layers=2: make_spec("q4km", dict(TINY, n_layer=layers), seed=7, alpha=3.0, norm_jitter=0.2),
     "t_q8_0": lambda layers=2: make_spec("q8_0", dict(TINY, n_layer=layers), seed=7, embd="Q8_0", alpha=3.0,
                                          norm_jitter=0.2),
-    "t_q8_0_tp": lambda layers=2: make_spec("q8_0", dict(TINY_TP, n_layer=layers), seed=11, embd="Q8_0", alpha=3.0,
+    "t_q8_0_tp16": lambda layers=2: make_spec("q8_0", dict(TINY_TP, n_layer=layers), seed=11, embd="Q8_0", alpha=3.0,
                                             norm_jitter=0.2),
     "t_f16head": lambda layers=2: make_spec("stq", dict(TINY, n_layer=layers), seed=7, embd="F16", alpha=3.0,
                                             norm_jitter=0.2),

@@ -20,7 +20,7 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
-CFG, PROMPT, GEN = "t_q8_0_tp", 40, 12
+CFG, PROMPT, GEN = "t_q8_0_tp16", 40, 12
 
 
 def _free_port() -> int:
