@@ -80,6 +80,9 @@ SIGNATURES = {
     "hyc_decode_begin": (I, [P, P, I, I, I, P, I, I]),
     "hyc_decode_steps": (I, [P, I]),
     "hyc_decode_steps_host": (I, [P, I, P]),
+    "hyc_decode_resident": (I, [P, I, P, C.c_ulonglong]),
+    "hyc_resident_go": (I, [P, I, I]),
+    "hyc_resident_wait": (I, [P, I, P, C.c_ulonglong]),
     "hyc_decode_read": (I, [P, P, I]),
     "hyc_decode_rewind": (I, [P, I, I]),
     "hyc_host_alloc": (P, [Z]),

@@ -16,6 +16,8 @@
 #include <cstdio>
 #include <cstdlib>
 #include <algorithm>
+#include <atomic>
+#include <chrono>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -110,6 +112,8 @@ struct HyCtx {
     int trace_next = 0;
     // persistent decode kernel
     int decode_mode = 0;            // 0: persistent kernel when supported, 1: graph of per-layer launches
+    int *host_io = nullptr;         // device view of the resident host loop's words (hyc_decode_resident)
+    unsigned long long host_limit_ns = 0;
     int mega_state = -1;            // -1 unchecked, 0 unsupported, 1 ready
     char mega_why[128] = {0};       // why unsupported
     MegaLayer *d_mega_layers = nullptr;
@@ -1162,6 +1166,8 @@ bool mega_launch(HyCtx *c, int steps) {
     a.tl = c->trace_on ? c->d_tl : nullptr;
     a.tl_cap = c->tl_cap;
     a.steps = steps;
+    a.host_io = c->host_io;
+    a.host_limit_ns = c->host_limit_ns;
     CK(c, cudaMemsetAsync(c->d_mega_sync, 0, sizeof(MegaSync), c->st));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(c->nsm);
@@ -1186,6 +1192,12 @@ bool mega_status(HyCtx *c) {
     CK(c, cudaMemcpyAsync(&err, &c->d_mega_sync->err, 4, cudaMemcpyDeviceToHost, c->st));
     CK(c, cudaStreamSynchronize(c->st));
     if (err == MEGA_OK) return true;
+    if (err == MEGA_ERR_HOST) {
+        // the resident loop ended cleanly (state written, copies drained): the handle stays usable
+        snprintf(c->err, sizeof c->err, "persistent decode kernel: the host did not answer within the limit");
+        CK(c, cudaMemsetAsync(&c->d_mega_sync->err, 0, 4, c->st));
+        return false;
+    }
     static const char *what[] = {"", "grid barrier timed out", "position outside the context",
                                  "weight slice copy timed out", "K/V row copy timed out"};
     c->broken = true;
@@ -2054,6 +2066,57 @@ HYC_API int hyc_decode_steps_host(void *impl, int steps, int *tok_io) {
         if (!decode_run(c, 1)) return -1;
         if (cudaMemcpyAsync(&tok_io[i + 1], &c->d_state->tok, 4, cudaMemcpyDeviceToHost, c->st) != cudaSuccess) return -1;
     }
+    return 0;
+}
+
+HYC_API int hyc_decode_resident(void *impl, int max_steps, int *io, unsigned long long limit_ns) {
+    HyCtx *c = (HyCtx *)impl;
+    if (!c || c->broken || !c->fused || !io || max_steps < 1) return -1;
+    if (cudaSetDevice(c->dev) != cudaSuccess) return -1;
+    if (!use_mega(c)) {
+        snprintf(c->err, sizeof c->err, "resident decode needs the persistent kernel: %s",
+                 c->decode_mode == 1 ? "graph requested" : c->mega_why);
+        return -1;
+    }
+    int *dio = nullptr;
+    if (cudaHostGetDevicePointer((void **)&dio, io, 0) != cudaSuccess || !dio) {
+        cudaGetLastError();
+        snprintf(c->err, sizeof c->err, "resident decode: io is not pinned host memory (hyc_host_alloc)");
+        return -1;
+    }
+    ((volatile int *)io)[2] = 0;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+    c->host_io = dio;
+    c->host_limit_ns = limit_ns == 0 ? kMegaWaitNs : (limit_ns < 10000000000ull ? limit_ns : 10000000000ull);
+    const bool ok = mega_launch(c, max_steps);
+    c->host_io = nullptr;
+    return ok ? 0 : -1;
+}
+
+HYC_API int hyc_resident_go(int *io, int step, int tok) {
+    if (!io) return -1;
+    volatile int *v = io;
+    v[1] = tok;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+    v[0] = step < 0 ? -1 : step + 1;
+    return 0;
+}
+
+HYC_API int hyc_resident_wait(const int *io, int step, int *tok, unsigned long long limit_ns) {
+    if (!io || !tok || step < 0) return -1;
+    const volatile int *v = io;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (unsigned it = 0;; it++) {
+        const int d = v[2];
+        if (d < 0) return -1;
+        if (d >= step + 1) break;
+        if ((it & 1023) == 1023 &&
+            (unsigned long long)std::chrono::duration_cast<std::chrono::nanoseconds>(
+                std::chrono::steady_clock::now() - t0).count() > limit_ns)
+            return -2;
+    }
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+    *tok = v[3];
     return 0;
 }
 

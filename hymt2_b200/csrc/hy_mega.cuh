@@ -34,7 +34,7 @@ constexpr int kMegaRowAlign = 8;                           // row slices in mult
 constexpr unsigned long long kMegaWaitNs = 2000000000ull;  // 2 s bound on any wait
 constexpr int kMegaKPad = kChunkKPad;                      // K rows padded in smem (bank spread)
 
-enum MegaErr { MEGA_OK = 0, MEGA_ERR_BARRIER = 1, MEGA_ERR_POS = 2, MEGA_ERR_WEIGHTS = 3, MEGA_ERR_KV = 4 };
+enum MegaErr { MEGA_OK = 0, MEGA_ERR_BARRIER = 1, MEGA_ERR_POS = 2, MEGA_ERR_WEIGHTS = 3, MEGA_ERR_KV = 4, MEGA_ERR_HOST = 5 };
 
 // Device-resident per-layer table.
 struct MegaLayer {
@@ -50,6 +50,7 @@ struct MegaSync {
     unsigned bar;                // grid barrier arrivals (monotonic within a launch)
     int err;                     // MegaErr of the first failure
     int tickets[64];             // attention split merge tickets per KV head
+    int go, go_tok;              // resident host loop: the host's go for the next step (-1: stop), its token
 };
 
 struct MegaArgs {
@@ -73,6 +74,11 @@ struct MegaArgs {
     unsigned long long *tl;   // optional timeline (block 0): globaltimer per phase edge
     int tl_cap;
     int steps;
+    // resident host loop (null: off): mapped pinned ints [go, token in, done, token out].  Step s
+    // starts once the host has set go >= s + 1 (go < 0: stop) and takes its input token from
+    // token in; after it, token out holds its argmax and done = s + 1 (-1 after an error)
+    int *host_io;
+    unsigned long long host_limit_ns;  // bound on each wait for the host
 };
 
 // ---------------------------------------------------------------- primitives
@@ -139,6 +145,73 @@ __device__ __forceinline__ int ld_relaxed_s32(const int *p) {
     return v;
 }
 __device__ __forceinline__ void raise_err(const MegaArgs &a, int code) { atomicCAS(&a.sync->err, 0, code); }
+// System-scope accesses of the mapped host words of the resident loop.
+__device__ __forceinline__ int ld_acquire_sys_s32(const int *p) {
+    int v;
+    asm volatile("ld.acquire.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ int ld_relaxed_sys_s32(const int *p) {
+    int v;
+    asm volatile("ld.relaxed.sys.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys_s32(int *p, int v) {
+    asm volatile("st.release.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys_s32(int *p, int v) {
+    asm volatile("st.relaxed.sys.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_gpu_s32(int *p, int v) {
+    asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu_s32(const int *p) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Resident host loop, before step `step` (all threads): block 0's thread 0
+// waits (bounded by host_limit_ns) for the host's go and reads its token,
+// then publishes both in device memory, where every CTA's thread 0 waits for
+// them (bounded).  Returns the token, or -1 when the host stopped the loop,
+// did not answer (MEGA_ERR_HOST) or another CTA failed.
+__device__ __forceinline__ int host_step_begin(const MegaArgs &a, int step, int *s_word) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        int v = ld_acquire_sys_s32(&a.host_io[0]);
+        const unsigned long long t0 = gtimer();
+        unsigned it = 0;
+        while (v >= 0 && v < step + 1) {
+            if ((++it & 63) == 0 && gtimer() - t0 > a.host_limit_ns) {
+                raise_err(a, MEGA_ERR_HOST);
+                v = -1;
+                break;
+            }
+            v = ld_acquire_sys_s32(&a.host_io[0]);
+        }
+        const int t = v >= 0 ? ld_relaxed_sys_s32(&a.host_io[1]) : 0;
+        a.sync->go_tok = t;
+        st_release_gpu_s32(&a.sync->go, v >= 0 ? step + 1 : -1);
+    }
+    if (threadIdx.x == 0) {
+        int g = ld_acquire_gpu_s32(&a.sync->go);
+        const unsigned long long t0 = gtimer();
+        unsigned it = 0;
+        while (g >= 0 && g < step + 1) {
+            if ((++it & 63) == 0) {
+                if (ld_relaxed_s32(&a.sync->err)) { g = -1; break; }
+                if (gtimer() - t0 > a.host_limit_ns + kMegaWaitNs) { raise_err(a, MEGA_ERR_BARRIER); g = -1; break; }
+            }
+            g = ld_acquire_gpu_s32(&a.sync->go);
+        }
+        *s_word = g < 0 ? -1 : *(volatile int *)&a.sync->go_tok;
+    }
+    __syncthreads();
+    const int r = *s_word;
+    __syncthreads();  // s_word is reused
+    return r;
+}
+
 
 // Grid-wide barrier in two halves.  bar_arrive: once every thread's writes
 // of the phase are done (__syncthreads), thread 0 adds 1 to the arrival
@@ -547,7 +620,7 @@ template <int HD, int G, int CF>
 __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_constant__ MegaArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ __align__(8) uint64_t mbar[4];  // weight slots
-    __shared__ int s_flag;
+    __shared__ int s_flag, s_hostw;
     __shared__ unsigned long long s_best[kMegaWarps];
     __shared__ __align__(16) float sq[G][HD];
     __shared__ __align__(16) float skc[HD], svc[HD];
@@ -591,7 +664,16 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
     if (a.steps > 0 && attn_cta(pos)) mega_kv_fill<HD>(a, tab[0], sK, sV, akvh, j0_of(pos), ncache_of(pos));
     NormPre npre;
     norm_preload(tab[0].attn_norm, a.H, npre);
+    bool host_early = false;  // the resident host loop ended before a.steps
     for (int step = 0; step < a.steps && ok; step++) {
+        if (a.host_io) {
+            const int t = host_step_begin(a, step, &s_hostw);
+            if (t < 0) {
+                host_early = true;
+                break;
+            }
+            tok = t;
+        }
         if (pos < 0 || pos >= a.ctx) {
             if (tid == 0) raise_err(a, MEGA_ERR_POS);
             ok = false;
@@ -903,12 +985,18 @@ __global__ void __launch_bounds__(kMegaThreads, 1) decode_mega(const __grid_cons
             }
             tok = idx;
             pos += 1;
+            if (a.host_io && blockIdx.x == 0 && tid == 0) {
+                st_relaxed_sys_s32(&a.host_io[3], idx);
+                __threadfence_system();
+                st_release_sys_s32(&a.host_io[2], step + 1);
+            }
         }
     }
     if (blockIdx.x == 0 && tid == 0) {
         a.st->tok = tok;
         a.st->pos = pos;
         a.st->amax = 0ull;
+        if (a.host_io && (!ok || host_early)) st_release_sys_s32(&a.host_io[2], -1);
     }
     // copies still in flight into this CTA's shared memory (error exits)
     if (tid == 0)

@@ -92,6 +92,25 @@ HYC_API int hyc_decode_begin(void *impl, const int *prompt, int n, int keep, int
                              int n_stop, int vocab_out);
 HYC_API int hyc_decode_steps(void *impl, int steps);
 HYC_API int hyc_decode_steps_host(void *impl, int steps, int *tok_io);
+/* Resident host loop (the reference's gen_ids loop, src/model.c:943-954, with
+ * the host reading every token and choosing the next input, without a launch
+ * per token): hyc_decode_resident starts ONE persistent-kernel launch of up to
+ * max_steps steps after hyc_decode_begin and returns at once.  io is 4 ints of
+ * pinned host memory (hyc_host_alloc): [go, token in, done, token out].  Step
+ * s runs once go >= s + 1 and takes its input token from io[1]; when it has
+ * finished, io[3] holds its argmax and done = s + 1.  hyc_resident_go(io, s,
+ * tok) releases step s with input tok (s < 0: stop the loop); call it for step
+ * 0 before or after hyc_decode_resident.  hyc_resident_wait(io, s, &tok,
+ * limit_ns) spins until step s is done and returns its token (0), -1 when the
+ * loop ended with an error (done < 0) or -2 after limit_ns.  The kernel waits
+ * for each go at most limit_ns (0: 2 s); a host that does not answer ends the
+ * loop, hyc_sync then reports it once and the handle stays usable, with the
+ * decode state after the last finished step.  Needs the persistent kernel
+ * (hyc_decode_path() == 1); stop ids still end the emitted-id count as in
+ * hyc_decode_read. */
+HYC_API int hyc_decode_resident(void *impl, int max_steps, int *io, unsigned long long limit_ns);
+HYC_API int hyc_resident_go(int *io, int step, int tok);
+HYC_API int hyc_resident_wait(const int *io, int step, int *tok, unsigned long long limit_ns);
 HYC_API int hyc_decode_read(void *impl, int *out_ids, int cap);
 HYC_API int hyc_decode_rewind(void *impl, int pos, int tok);
 HYC_API void *hyc_host_alloc(size_t bytes);

@@ -131,3 +131,92 @@ def test_bounded_waits_report_and_leave_the_handle_usable(backend, synth, model_
         assert len(dm.generate([1, 2, 3, 4], 4)) == 4
     finally:
         dm.close()
+
+
+def _resident_begin(lib, impl, dm, ids, max_new):
+    pr = np.asarray(ids, dtype=np.int32)
+    assert lib.hyc_decode_begin(impl, pr.ctypes.data, len(pr), 0, max_new, None, 0, dm.vocab_out) == 0
+    first = np.zeros(1, dtype=np.int32)
+    assert lib.hyc_decode_read(impl, first.ctypes.data, 1) == 1
+    return int(first[0])
+
+
+def test_resident_host_loop(backend, synth, model_dir):
+    """The resident host loop (hyc_decode_resident): one persistent launch in
+    which the host reads every step's token through mapped pinned memory and
+    releases the next step with it, as the reference's loop does
+    (src/model.c:943-954).  Its ids are the device-resident loop's; a host
+    stop after five steps leaves the decode state after step five, and plain
+    decode steps continue from there to the same stream."""
+    from hymt2_b200.device import DeviceModel
+    lib, impl = backend.lib, backend.impl
+    dm = DeviceModel(synth.ensure("t_stq", model_dir), backend, ctx=256)
+    io = lib.hyc_host_alloc(16)
+    try:
+        assert lib.hyc_set_decode_mode(impl, 0) == 0
+        ids = np.arange(3, 19).tolist()
+        want = dm.generate(ids, 12)
+        t = C.c_int()
+        # the whole stream
+        tok = _resident_begin(lib, impl, dm, ids, 12)
+        assert lib.hyc_resident_go(io, 0, tok) == 0
+        assert lib.hyc_decode_resident(impl, 11, io, 0) == 0, backend.error()
+        got = [tok]
+        for s in range(11):
+            assert lib.hyc_resident_wait(io, s, C.byref(t), 5_000_000_000) == 0
+            got.append(t.value)
+            if s + 1 < 11:
+                lib.hyc_resident_go(io, s + 1, t.value)
+        assert lib.hyc_sync(impl) == 0, backend.error()
+        out = np.zeros(12, dtype=np.int32)
+        assert lib.hyc_decode_read(impl, out.ctypes.data, 12) == 12
+        assert got == want and out.tolist() == want
+        # the host stops after five steps, then plain steps continue
+        tok = _resident_begin(lib, impl, dm, ids, 12)
+        lib.hyc_resident_go(io, 0, tok)
+        assert lib.hyc_decode_resident(impl, 11, io, 0) == 0, backend.error()
+        for s in range(5):
+            assert lib.hyc_resident_wait(io, s, C.byref(t), 5_000_000_000) == 0
+            lib.hyc_resident_go(io, s + 1 if s < 4 else -1, t.value)
+        assert lib.hyc_sync(impl) == 0, backend.error()
+        assert lib.hyc_decode_read(impl, out.ctypes.data, 12) == 6
+        assert out[:6].tolist() == want[:6]
+        assert lib.hyc_decode_steps(impl, 6) == 0
+        assert lib.hyc_decode_read(impl, out.ctypes.data, 12) == 12
+        assert out.tolist() == want
+    finally:
+        lib.hyc_host_free(io)
+        dm.close()
+
+
+def test_resident_host_timeout_reports_and_leaves_the_handle_usable(backend, synth, model_dir):
+    """A host that never releases step 2 (limit 5 ms): the kernel gives up
+    waiting, ends the loop cleanly and reports it once through hyc_sync; the
+    waiting host sees the loop end (done < 0); the same handle decodes
+    normally afterwards.  No trap, no fault, no hang."""
+    from hymt2_b200.device import DeviceModel
+    lib, impl = backend.lib, backend.impl
+    dm = DeviceModel(synth.ensure("t_stq", model_dir), backend, ctx=256)
+    io = lib.hyc_host_alloc(16)
+    try:
+        assert lib.hyc_set_decode_mode(impl, 0) == 0
+        ids = np.arange(5, 21).tolist()
+        want = dm.generate(ids, 8)
+        t = C.c_int()
+        tok = _resident_begin(lib, impl, dm, ids, 8)
+        lib.hyc_resident_go(io, 0, tok)
+        assert lib.hyc_decode_resident(impl, 7, io, 5_000_000) == 0, backend.error()
+        for s in range(2):
+            assert lib.hyc_resident_wait(io, s, C.byref(t), 5_000_000_000) == 0
+            if s == 0:
+                lib.hyc_resident_go(io, 1, t.value)
+        assert lib.hyc_resident_wait(io, 2, C.byref(t), 5_000_000_000) == -1
+        assert lib.hyc_sync(impl) == -1 and "host" in backend.error()
+        assert lib.hyc_sync(impl) == 0                      # reported once; the handle is not broken
+        out = np.zeros(8, dtype=np.int32)
+        assert lib.hyc_decode_read(impl, out.ctypes.data, 8) == 3   # the prefill token and steps 0, 1
+        assert out[:3].tolist() == want[:3]
+        assert dm.generate(ids, 8) == want
+    finally:
+        lib.hyc_host_free(io)
+        dm.close()
