@@ -57,6 +57,34 @@ def test_standalone_create_is_not_a_drop_in():
     assert info.value
 
 
+def test_resident_loop_host_words():
+    """The host half of the resident decode loop (hyc_resident_go / wait)
+    touches only the four host words [go, token in, done, token out], so it
+    runs here: go writes the token before the go word (a negative step
+    writes the stop value), wait returns the token once done reaches the
+    step, -1 when the loop ended with an error (done < 0) and -2 after its
+    limit."""
+    import ctypes as C
+
+    import numpy as np
+
+    from hymt2_b200 import device
+    lib = device.load_library()
+    io = np.zeros(4, dtype=np.int32)
+    p = io.ctypes.data
+    assert lib.hyc_resident_go(p, 0, 77) == 0 and io.tolist() == [1, 77, 0, 0]
+    assert lib.hyc_resident_go(p, 4, 5) == 0 and io[:2].tolist() == [5, 5]
+    assert lib.hyc_resident_go(p, -1, 0) == 0 and io[0] == -1
+    t = C.c_int(-9)
+    assert lib.hyc_resident_wait(p, 0, C.byref(t), 2_000_000) == -2     # done = 0: nothing finished
+    io[2], io[3] = 3, 1234
+    assert lib.hyc_resident_wait(p, 2, C.byref(t), 2_000_000) == 0 and t.value == 1234
+    assert lib.hyc_resident_wait(p, 3, C.byref(t), 2_000_000) == -2     # step 3 not done yet
+    io[2] = -1
+    assert lib.hyc_resident_wait(p, 3, C.byref(t), 2_000_000) == -1     # the loop ended with an error
+    assert lib.hyc_resident_go(None, 0, 0) == -1 and lib.hyc_resident_wait(None, 0, C.byref(t), 1) == -1
+
+
 def test_rope_tables_match_loader_formula():
     import numpy as np
     lib = abi.bind(ctypes.CDLL(_paths.BACKEND_LIB))
