@@ -473,6 +473,22 @@ __host__ __device__ inline int attn_chunk_len(int pos, int kv_heads, int units) 
         if (kv_heads * ((pos + cs) / cs) <= units) return cs;
     return 0;
 }
+
+// The per-layer kernels' rule: attn_chunk_len where it has an answer (so the
+// per-layer and persistent paths split a position identically), else the
+// same search with up to kMaxUnitsWide units (long contexts: 4 KV heads x 37
+// chunks of 128 keys on 148 SMs).  The per-layer merge holds kWideNR chunk
+// weights per lane.
+constexpr int kMaxUnitsWide = 160;
+constexpr int kWideNR = kMaxUnitsWide / 32;
+__host__ __device__ inline int attn_chunk_len_wide(int pos, int kv_heads, int units) {
+    const int cs = attn_chunk_len(pos, kv_heads, units);
+    if (cs || units <= kMaxUnits) return cs;
+    if (units > kMaxUnitsWide) units = kMaxUnitsWide;
+    for (int c = kChunkMin; c <= kChunkMax; c += kChunkMin)
+        if (kv_heads * ((pos + c) / c) <= units) return c;
+    return 0;
+}
 __host__ __device__ inline int attn_max_chunks(int ctx) { return (ctx + kChunkMin - 1) / kChunkMin; }
 
 template <int HD>
@@ -694,12 +710,15 @@ struct PlainPartLoader {
 // One warp: output of a head from its nchunks partials.  Lane c holds chunk
 // c's (m, l); M by warp max, L by warp sum of l_c e^(m_c - M) (lane order), O
 // over chunks in chunk order with the chunk weights broadcast from their
-// lanes; the first four chunks' rows are loaded before any arithmetic.
-template <int HD, typename Loader>
+// lanes; the first four chunks' rows are loaded before any arithmetic.  NR
+// chunk weights per lane (nchunks <= 32 * NR); lanes past nchunks add exact
+// zeros, so the result does not depend on NR.  Chunks past the fourth are
+// loaded B at a time before their FMAs (B = 1: one load per FMA group, the
+// persistent kernel's form); the FMA order, and so the result, is the same.
+template <int HD, typename Loader, int NR = (kMaxUnits + 31) / 32, int B = 1>
 __device__ __forceinline__ void attn_merge_head_with(const Loader &ld, int nchunks, float *out) {
     constexpr int DPL = HD / 32;
     const int lane = threadIdx.x & 31;
-    constexpr int NR = (kMaxUnits + 31) / 32;  // nchunks <= kMaxUnits (attn_chunk_len)
     float mc[NR], lc[NR];
 #pragma unroll
     for (int r = 0; r < NR; r++) {
@@ -747,12 +766,29 @@ __device__ __forceinline__ void attn_merge_head_with(const Loader &ld, int nchun
             for (int q = 0; q < DPL; q++) O[q] = fmaf(ov0[u][q], fw, O[q]);
         }
     }
-    for (int c = 4; c < nchunks; c++) {
-        const float fw = f_of(c);
-        float vv[DPL];
-        ld.template o<DPL>(c, lane, vv);
+    if constexpr (B == 1) {
+        for (int c = 4; c < nchunks; c++) {
+            const float fw = f_of(c);
+            float vv[DPL];
+            ld.template o<DPL>(c, lane, vv);
 #pragma unroll
-        for (int q = 0; q < DPL; q++) O[q] = fmaf(vv[q], fw, O[q]);
+            for (int q = 0; q < DPL; q++) O[q] = fmaf(vv[q], fw, O[q]);
+        }
+    } else {
+        for (int c0 = 4; c0 < nchunks; c0 += B) {
+            float vv[B][DPL];
+#pragma unroll
+            for (int u = 0; u < B; u++)
+                if (c0 + u < nchunks) ld.template o<DPL>(c0 + u, lane, vv[u]);
+#pragma unroll
+            for (int u = 0; u < B; u++) {
+                if (c0 + u < nchunks) {
+                    const float fw = f_of(c0 + u);
+#pragma unroll
+                    for (int q = 0; q < DPL; q++) O[q] = fmaf(vv[u][q], fw, O[q]);
+                }
+            }
+        }
     }
     const float inv = 1.0f / L;
 #pragma unroll
@@ -765,9 +801,10 @@ __device__ __forceinline__ void attn_merge_head(const float *part, int max_chunk
     attn_merge_head_with<HD>(ld, nchunks, out);
 }
 
-// Per-layer form: grid (kv_heads, attn_max_chunks(ctx)); units past the
-// position's chunk count return.  Rows staged with cp.async (K rows padded
-// by 16 bytes so the 8 key groups of a warp read different banks).
+// Per-layer form: grid (kv_heads, attn_max_chunks(ctx)), chunk length by
+// attn_chunk_len_wide; units past the position's chunk count return.  Rows
+// staged with cp.async (K rows padded by 64 bytes so the 8 key groups of a
+// warp read different banks).
 template <int HD, int G>
 __global__ void __launch_bounds__(kDecWarps * 32) attn_chunk_kernel(const __grid_constant__ AttnArgs a) {
     constexpr int KROW = HD * 2 + kChunkKPad, CH = HD / 8;
@@ -782,7 +819,7 @@ __global__ void __launch_bounds__(kDecWarps * 32) attn_chunk_kernel(const __grid
     const int kvh = blockIdx.x, chunk = blockIdx.y, w = threadIdx.x >> 5;
     const int pos = *a.pos_ptr;  // written before this graph / >= 2 kernels back
     if (blockDim.x != kDecWarps * 32 || pos < 0 || pos >= a.ctx) return;
-    const int cs = attn_chunk_len(pos, a.kv_heads, a.units);
+    const int cs = attn_chunk_len_wide(pos, a.kv_heads, a.units);
     if (cs == 0 || chunk * cs > pos) return;
     const int j0 = chunk * cs, ncache = max(0, min(pos, j0 + cs) - j0);
     const uint16_t *Kg = a.kc + kvh * HD, *Vg = a.vc + kvh * HD;
@@ -822,9 +859,10 @@ __global__ void __launch_bounds__(32) attn_merge_kernel(const __grid_constant__ 
     pdl_wait();
     const int pos = *a.pos_ptr;
     if (pos < 0 || pos >= a.ctx) return;
-    const int cs = attn_chunk_len(pos, a.kv_heads, a.units);
+    const int cs = attn_chunk_len_wide(pos, a.kv_heads, a.units);
     if (cs == 0) return;
-    attn_merge_head<HD>(a.cpart, a.max_chunks, (pos + cs) / cs, blockIdx.x, a.ao + (size_t)blockIdx.x * HD);
+    const PlainPartLoader<HD> ld{a.cpart + (size_t)blockIdx.x * a.max_chunks * (HD + kPartPad)};
+    attn_merge_head_with<HD, PlainPartLoader<HD>, kWideNR, 16>(ld, (pos + cs) / cs, a.ao + (size_t)blockIdx.x * HD);
 }
 
 // ---------------------------------------------------------------- batched decode attention

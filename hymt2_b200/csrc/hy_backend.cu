@@ -687,7 +687,7 @@ bool tp_status(HyCtx *c) {
 
 template <int HD, int G>
 bool attn_launch(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
-    if (nt == 1 && !aa.tok_pos && aa.cpart && attn_chunk_len(aa.ctx - 1, aa.kv_heads, aa.units) > 0) {
+    if (nt == 1 && !aa.tok_pos && aa.cpart && attn_chunk_len_wide(aa.ctx - 1, aa.kv_heads, aa.units) > 0) {
         // wide decode attention: units of (KV head, key chunk), then the per-head merge
         if (!launch(c, attn_chunk_kernel<HD, G>, dim3(aa.kv_heads, aa.max_chunks), dim3(kDecWarps * 32),
                     attn_chunk_smem<HD>(), pdl, aa))

@@ -62,7 +62,24 @@ def test_gemv_prologue(backend, oracle, name, act, k, nt):
 @pytest.mark.parametrize("heads,kvh", [(4, 4), (4, 2), (16, 4), (16, 2)])
 @pytest.mark.parametrize("pos0,nt", [(0, 1), (7, 1), (111, 1), (300, 1), (600, 1), (0, 5), (40, 17)])
 def test_attention(backend, oracle, hd, heads, kvh, pos0, nt):
-    ctx = 1024
+    _check_attention(backend, oracle, hd, heads, kvh, 1024, pos0, nt)
+
+
+# Single-token decode past the persistent kernel's 64 units.  The kernel
+# pair is fixed per context by the last position: with 4 KV heads up to
+# ctx 4736 (37 chunks of 128 keys, 148 units) the per-layer chunk kernel,
+# past it the split-KV kernel (ctx 8192).  Covered: chunk lengths 64, 96 and
+# 128, merges of up to 141 chunks (kvh 1), a chunk holding only the current
+# key (pos 4096), exactly 148 units (pos 4700).  Config 4's attention is
+# (128, 16, 4) at KV 4096 in a 4224-row cache.
+@pytest.mark.parametrize("hd,heads,kvh,ctx,pos0", [(128, 16, 4, 4736, 2100), (128, 16, 4, 4736, 4096),
+                                                  (128, 16, 4, 4736, 4700), (128, 16, 4, 8192, 6000),
+                                                  (64, 4, 2, 9472, 5000), (64, 8, 1, 10240, 9000)])
+def test_attention_long_context(backend, oracle, hd, heads, kvh, ctx, pos0):
+    _check_attention(backend, oracle, hd, heads, kvh, ctx, pos0, 1)
+
+
+def _check_attention(backend, oracle, hd, heads, kvh, ctx, pos0, nt):
     rng = np.random.default_rng(hd + heads * 3 + kvh + pos0 + nt)
     qd, kvd = heads * hd, kvh * hd
     cos, sin = _rope(ctx, hd)
