@@ -688,8 +688,11 @@ bool tp_status(HyCtx *c) {
 template <int HD, int G>
 bool attn_launch(HyCtx *c, const AttnArgs &aa, int nt, bool pdl) {
     if (nt == 1 && !aa.tok_pos && aa.cpart && attn_chunk_len_wide(aa.ctx - 1, aa.kv_heads, aa.units) > 0) {
-        // wide decode attention: units of (KV head, key chunk), then the per-head merge
-        if (!launch(c, attn_chunk_kernel<HD, G>, dim3(aa.kv_heads, aa.max_chunks), dim3(kDecWarps * 32),
+        // wide decode attention: units of (KV head, key chunk), then the per-head merge.  The chunk
+        // rule keeps kv_heads * chunks <= min(units, kMaxUnitsWide) at every position, so no more
+        // chunk rows are launched than that (one wave of CTAs).
+        const int ych = std::min(aa.max_chunks, std::min(aa.units, kMaxUnitsWide) / aa.kv_heads);
+        if (!launch(c, attn_chunk_kernel<HD, G>, dim3(aa.kv_heads, ych), dim3(kDecWarps * 32),
                     attn_chunk_smem<HD>(), pdl, aa))
             return false;
         return launch(c, attn_merge_kernel<HD>, dim3(aa.heads), dim3(32), 0, pdl, aa);
